@@ -1,0 +1,179 @@
+"""Seeded synthetic models and prompts for the benchmark configurations.
+
+There is no network and no released checkpoint, so every benchmark and parity
+case runs a random-initialised model of the named architecture:
+
+* matrices ~ N(0, 0.02) (router matrices ~ N(0, 0.01)), every 1-D tensor
+  (norm gains, gates, router biases) = 1.0, as in the reference's own test
+  fixture (tests/test_inference.py:15-22);
+* the small FP32 configuration (``nano15``) draws its matrices from
+  ``numpy.random.default_rng(seed).normal`` in ``expected_shapes`` order;
+* the BF16 configurations use a counter-based generator (``hash_normal``):
+  SplitMix64 of (seed, tensor index, element index) gives twelve 16-bit
+  uniforms whose centred sum (Irwin-Hall, variance 1) is scaled by the std in
+  float32 and rounded to BF16.  It is integer arithmetic plus one exact int->
+  float conversion and one float32 multiply, so the CUDA fill kernel
+  (``mr_model_fill_synthetic``) and this NumPy version give the same bits,
+  which lets the GPU build 76 GB models in HBM without a host copy while the
+  CPU oracle reproduces any tensor of them;
+* prompts are ``default_rng(1).integers(3, vocab)``.
+
+Architecture fields the benchmark description leaves open are fixed here and
+listed in ``UNPINNED_CHOICES``.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from .config import ModelConfig
+from .weights import BF16Array, expected_shapes, float32_to_bf16_bits
+
+# Values chosen where the benchmark description does not pin the architecture.
+UNPINNED_CHOICES = {
+    "lighting": {"kv_heads": 24, "window": 2048, "memory_slots": 0,
+                 "note": "24 KV heads = the literal '24 heads'; memory_slots 0 is the family default "
+                         "(drop path); RoPE rotates the full head_dim as in the reference"},
+    "heavy": {"query_heads": 32, "kv_heads": 8, "head_dim": 128, "latent_dim": 512,
+              "router_top_k_min": 2, "note": "36.5B-class layout: 66 experts x 3 x 4096 x 1408 x 32 layers"},
+    "nano17": {"kv_heads": 4, "global_kv_heads": 8,
+               "note": "'alternating 4/8' expressed as local 4 / global 8 (the reference's only per-layer form)"},
+}
+
+
+def config_for(name: str) -> ModelConfig:
+    """ModelConfig for one of the benchmark configurations."""
+    if name == "nano15":
+        return ModelConfig(family="flashnano-1.5", vocab_size=512, hidden_size=256, layers=4,
+                           query_heads=8, kv_heads=2, head_dim=32, ffn_dim=688, max_positions=256,
+                           window=64, global_layers=(2, 4), rope_theta=1e4, norm_eps=1e-6)
+    if name == "nano17":
+        return ModelConfig(family="flashnano-1.7", vocab_size=32000, hidden_size=1024, layers=19,
+                           query_heads=16, kv_heads=4, global_kv_heads=8, head_dim=64, ffn_dim=2816,
+                           max_positions=2048, window=512, global_layers=(4, 8, 12, 16),
+                           rope_theta=1e4)
+    if name == "lite":
+        return ModelConfig(family="flashlite-2.0", vocab_size=64000, hidden_size=2048, layers=24,
+                           query_heads=16, kv_heads=4, head_dim=128, ffn_dim=5632, max_positions=8192,
+                           window=None, rope_theta=5e5, residual_scale=(2 * 24) ** -0.5)
+    if name == "lighting":
+        choice = UNPINNED_CHOICES["lighting"]
+        return ModelConfig(family="flashlighting-2.0", vocab_size=64000, hidden_size=3072, layers=28,
+                           query_heads=24, kv_heads=choice["kv_heads"], head_dim=128, ffn_dim=8192,
+                           max_positions=16384, window=choice["window"], latent_dim=512,
+                           memory_slots=choice["memory_slots"], residual_scale=(2 * 28) ** -0.5,
+                           source={"rope_scaling_type": "yarn", "rope_scaling_factor": 4.0,
+                                   "max_position_embeddings": 4096})
+    if name == "heavy":
+        choice = UNPINNED_CHOICES["heavy"]
+        return ModelConfig(family="heavy-medium-2.0", vocab_size=64000, hidden_size=4096, layers=32,
+                           query_heads=choice["query_heads"], kv_heads=choice["kv_heads"],
+                           head_dim=choice["head_dim"], ffn_dim=1408, max_positions=32768, window=1024,
+                           latent_dim=choice["latent_dim"], inner_loop_steps=2,
+                           source={"routed_experts": 64, "router_groups": 8, "router_top_k_max": 8,
+                                   "router_top_k_min": choice["router_top_k_min"], "shared_experts": 2,
+                                   "long_context": {"local_window": 1024, "global_block_size": 64,
+                                                    "global_slots": 16, "target_context": 32768}})
+    raise ValueError(f"unknown configuration {name!r}")
+
+
+# (context, prompt tokens, decode tokens) per configuration
+WORKLOADS = {"nano15": (256, 32, 64), "nano17": (2048, 512, 512), "lite": (8192, 2048, 1024),
+             "lighting": (16384, 4096, 512), "heavy": (32768, 4096, 256)}
+STORED_DTYPE = {"nano15": "F32", "nano17": "BF16", "lite": "BF16", "lighting": "BF16", "heavy": "BF16"}
+
+
+def prompt_ids(vocab_size: int, count: int, seed: int = 1) -> np.ndarray:
+    return np.random.default_rng(seed).integers(3, vocab_size, count).astype(np.int64)
+
+
+def tensor_std(name: str) -> float:
+    return 0.01 if ".router." in name else 0.02
+
+
+# counter-based BF16 generator --------------------------------------------------------
+_GOLDEN = np.uint64(0x9E3779B97F4A7C15)
+_M1, _M2 = np.uint64(0xBF58476D1CE4E5B9), np.uint64(0x94D049BB133111EB)
+_LANES = np.uint64(0x0000FFFF0000FFFF)
+
+
+def _splitmix(z):
+    z = (z ^ (z >> np.uint64(30))) * _M1
+    z = (z ^ (z >> np.uint64(27))) * _M2
+    return z ^ (z >> np.uint64(31))
+
+
+def hash_normal_f32(seed: int, tensor_index: int, start: int, count: int, std: float) -> np.ndarray:
+    """float32 values of elements [start, start+count) of one tensor (see module doc).
+
+    Element i of tensor t: key = splitmix(seed*G + t + 1); for word w in 0..2,
+    z_w = splitmix(key ^ ((3i + w) * G)); the twelve 16-bit fields of z_0..z_2
+    are summed (two 32-bit SWAR lanes, folded at the end), centred by 6*2^16
+    and scaled by std/2^16 in float32.
+    """
+    with np.errstate(over="ignore"):
+        key = _splitmix(np.uint64(seed) * _GOLDEN + np.uint64(tensor_index + 1))
+        index3 = np.arange(start, start + count, dtype=np.uint64) * np.uint64(3)
+        acc = np.zeros(count, dtype=np.uint64)
+        for word in range(3):
+            z = index3 + np.uint64(word)
+            z *= _GOLDEN
+            z ^= key
+            z ^= z >> np.uint64(30)
+            z *= _M1
+            z ^= z >> np.uint64(27)
+            z *= _M2
+            z ^= z >> np.uint64(31)
+            acc += z & _LANES
+            z >>= np.uint64(16)
+            z &= _LANES
+            acc += z
+        total = (acc & np.uint64(0xFFFFFFFF)) + (acc >> np.uint64(32))
+    centred = (total.astype(np.int64) - 6 * 65536).astype(np.float32)
+    return centred * np.float32(std / 65536.0)
+
+
+def hash_normal_bf16(seed, tensor_index, shape, std, chunk=1 << 20) -> np.ndarray:
+    from concurrent.futures import ThreadPoolExecutor
+    n = math.prod(shape)
+    out = np.empty(n, dtype=np.uint16)
+
+    def fill(start):
+        count = min(chunk, n - start)
+        out[start:start + count] = float32_to_bf16_bits(hash_normal_f32(seed, tensor_index, start, count, std))
+
+    if n <= chunk:
+        fill(0)
+    else:
+        with ThreadPoolExecutor() as pool:
+            list(pool.map(fill, range(0, n, chunk)))
+    return out.reshape(shape)
+
+
+def tensor_plan(config: ModelConfig):
+    """[(tensor index, canonical name, shape, std or None for 1-D ones)] in a fixed order."""
+    plan = []
+    for index, (name, shape) in enumerate(expected_shapes(config).items()):
+        plan.append((index, name, shape, tensor_std(name) if len(shape) == 2 else None))
+    return plan
+
+
+def synthetic_weights(config: ModelConfig, stored: str = "BF16", seed: int = 0, names=None):
+    """Host weights dict (canonical names).  ``names`` limits generation to a subset."""
+    weights = {}
+    rng = np.random.default_rng(seed) if stored == "F32" else None
+    for index, name, shape, std in tensor_plan(config):
+        if std is None:
+            weights[name] = np.ones(shape, np.float32)
+            continue
+        if stored == "F32":
+            # always draw, so a subset sees the same stream as the full model
+            value = rng.normal(0.0, std, shape).astype(np.float32)
+            if names is None or name in names:
+                weights[name] = value
+            continue
+        if names is not None and name not in names:
+            continue
+        weights[name] = BF16Array(hash_normal_bf16(seed, index, shape, std))
+    return weights
