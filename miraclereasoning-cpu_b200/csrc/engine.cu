@@ -1,0 +1,749 @@
+// Whole-model engine, host side: tensor registry (the canonical names and
+// shapes of weights.py expected_shapes, weights.py:211-245), HBM residency of
+// the stored bytes, the per-step phase plan, and the launch loop behind
+// mr_model_step / prefill / generate.
+//
+// Replaces the reference's per-op Python dispatch (model.py:257-312), its
+// per-op clCreateBuffer/clEnqueueNDRangeKernel traffic (opencl.py:326-387)
+// and its LRU weight cache (weights.py:258-297).
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "engine.cuh"
+
+namespace mr {
+
+__global__ void decode_step_kernel(const Phase *__restrict__ phases, int nphases, StepState *st, StepControl ctl);
+size_t decode_step_smem_bytes();
+
+namespace {
+
+struct TensorSlot {
+    std::vector<int64_t> shape;
+    int dtype = -1;
+    void *ptr = nullptr;
+    size_t bytes = 0;
+};
+
+bool is_gqa_family(int f) {
+    return f == MR_FAMILY_FLASHNANO_15 || f == MR_FAMILY_FLASHNANO_17 || f == MR_FAMILY_FLASHLITE_20;
+}
+
+size_t dtype_size(int dtype) { return dtype == MR_DTYPE_F32 ? 4 : 2; }
+
+// ---- synthetic weights (counter hash, bit-identical to synthetic.py) -------------
+__device__ __forceinline__ uint64_t splitmix(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__global__ void k_fill_hash_bf16(uint16_t *out, size_t n, uint64_t key, float scale) {
+    const uint64_t golden = 0x9E3779B97F4A7C15ull, lanes = 0x0000FFFF0000FFFFull;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        uint64_t acc = 0;
+        for (uint64_t w = 0; w < 3; ++w) {
+            const uint64_t z = splitmix(((3ull * i + w) * golden) ^ key);
+            acc += z & lanes;
+            acc += (z >> 16) & lanes;
+        }
+        const uint64_t total = (acc & 0xFFFFFFFFull) + (acc >> 32);
+        const float centred = static_cast<float>(static_cast<int64_t>(total) - 6 * 65536);
+        const uint32_t bits = __float_as_uint(__fmul_rn(centred, scale));
+        out[i] = static_cast<uint16_t>((bits + 0x7FFFu + ((bits >> 16) & 1u)) >> 16);
+    }
+}
+
+__global__ void k_fill_value(void *out, int dtype, size_t n, float value) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        if (dtype == MR_DTYPE_F32) {
+            static_cast<float *>(out)[i] = value;
+        } else if (dtype == MR_DTYPE_BF16) {
+            const uint32_t bits = __float_as_uint(value);
+            static_cast<uint16_t *>(out)[i] = static_cast<uint16_t>((bits + 0x7FFFu + ((bits >> 16) & 1u)) >> 16);
+        } else {
+            static_cast<__half *>(out)[i] = __float2half_rn(value);
+        }
+    }
+}
+
+uint64_t host_splitmix(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+}  // namespace
+}  // namespace mr
+
+using namespace mr;
+
+struct mr_model {
+    mr_context *ctx = nullptr;
+    mr_model_config cfg{};
+    std::vector<int> layer_kvh, layer_window;
+    std::vector<float> inv_freq;
+    std::map<std::string, TensorSlot> tensors;
+    std::vector<void *> allocations;
+    bool finalized = false;
+    bool failed = false;
+    int position = 0;
+    int grid = 0;
+    // device buffers
+    float *d_inv_freq = nullptr;
+    float *x = nullptr, *q_raw = nullptr, *k_raw = nullptr, *v_raw = nullptr, *attn = nullptr, *ffn = nullptr;
+    float *logits = nullptr;
+    int logits_rows = 0;
+    float *partial = nullptr;
+    unsigned int *arrivals = nullptr;
+    int max_chunks = 0;
+    std::vector<float *> k_cache, v_cache;
+    std::vector<int> cache_capacity;
+    StepState *state = nullptr;
+    int *feed = nullptr;
+    int feed_capacity = 0;
+    int *gen_out = nullptr;
+    int gen_capacity = 0;
+    Phase *d_phases = nullptr;
+    std::vector<Phase> phases;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+};
+
+namespace {
+
+void *device_alloc(mr_model *m, size_t bytes, int *rc) {
+    void *p = nullptr;
+    bytes = (bytes + 255) & ~size_t(255);
+    cudaError_t err = cudaMalloc(&p, bytes ? bytes : 256);
+    if (err != cudaSuccess) {
+        *rc = cuda_error(err, "cudaMalloc");
+        return nullptr;
+    }
+    m->allocations.push_back(p);
+    return p;
+}
+
+// Canonical tensor names and shapes (weights.py expected_shapes).
+void expected_tensors(mr_model *m) {
+    const mr_model_config &c = m->cfg;
+    const int64_t h = c.hidden_size, d = c.head_dim, q = (int64_t)c.query_heads * c.head_dim, f = c.ffn_dim;
+    auto add = [&](const std::string &name, std::vector<int64_t> shape) { m->tensors[name].shape = shape; };
+    add("embed", {c.vocab_size, h});
+    add("norm", {h});
+    if (!c.tie_embeddings) add("output", {c.vocab_size, h});
+    const bool heavy = c.family == MR_FAMILY_HEAVY_MEDIUM_20, lighting = c.family == MR_FAMILY_FLASHLIGHTING_20;
+    for (int i = 0; i < c.layers; ++i) {
+        const std::string p = "layers." + std::to_string(i) + ".";
+        const int64_t kv = (int64_t)m->layer_kvh[i] * d;
+        add(p + "a_norm", {h});
+        add(p + "q", {q, h});
+        add(p + "o", {h, q});
+        if (!lighting) add(p + "f_norm", {h});
+        if (c.latent_dim) add(p + "latent", {c.latent_dim, h});
+        if (heavy) {
+            add(p + "kv_up", {2 * kv, c.latent_dim});
+            add(p + "router.coarse.weight", {c.router_groups, h});
+            add(p + "router.coarse.bias", {c.router_groups});
+            add(p + "router.fine.weight", {c.routed_experts, h});
+            add(p + "router.fine.bias", {c.routed_experts});
+            add(p + "router.group_bias", {c.router_groups});
+            add(p + "router.expert_bias", {c.routed_experts});
+        } else {
+            const int64_t inner = c.latent_dim ? c.latent_dim : h;
+            add(p + "k", {kv, inner});
+            add(p + "v", {kv, inner});
+            if (c.qk_norm) {
+                add(p + "q_norm", {d});
+                add(p + "k_norm", {d});
+            }
+        }
+        if (lighting) {
+            add(p + "latent_norm", {c.latent_dim});
+            add(p + "attention_gate", {1});
+            add(p + "ffn_gate", {1});
+        }
+        if (c.family == MR_FAMILY_FLASHNANO_16) add(p + "cbr", {c.cbr_slots, h});
+        std::vector<std::string> roots;
+        if (heavy) {
+            for (int e = 0; e < c.routed_experts; ++e) roots.push_back(p + "experts." + std::to_string(e) + ".");
+            for (int e = 0; e < c.shared_experts; ++e) roots.push_back(p + "shared." + std::to_string(e) + ".");
+        } else {
+            roots.push_back(p + "ffn.");
+        }
+        for (auto &r : roots) {
+            add(r + "gate", {f, h});
+            add(r + "up", {f, h});
+            add(r + "down", {h, f});
+        }
+    }
+}
+
+int check_tensor(mr_model *m, const char *name, int dtype, int ndim, const int64_t *shape, TensorSlot **out) {
+    MR_REQUIRE(m && name, "NULL argument");
+    MR_REQUIRE(!m->finalized, "model is finalized; tensors are immutable");
+    auto it = m->tensors.find(name);
+    MR_REQUIRE(it != m->tensors.end(), "unexpected tensor %s", name);
+    MR_REQUIRE(dtype == MR_DTYPE_F32 || dtype == MR_DTYPE_F16 || dtype == MR_DTYPE_BF16, "%s: unsupported dtype %d",
+               name, dtype);
+    TensorSlot &t = it->second;
+    bool same = ndim == (int)t.shape.size() && shape;
+    for (int i = 0; same && i < ndim; ++i) same = shape[i] == t.shape[i];
+    if (!same) {
+        std::string want;
+        for (auto v : t.shape) want += std::to_string(v) + ",";
+        return set_error(MR_ERR_ARGUMENT, "%s: expected shape (%s)", name, want.c_str());
+    }
+    size_t n = 1;
+    for (auto v : t.shape) n *= (size_t)v;
+    const size_t bytes = n * dtype_size(dtype);
+    if (!t.ptr || t.bytes != bytes) {
+        int rc = MR_OK;
+        t.ptr = device_alloc(m, bytes, &rc);
+        if (rc) return rc;
+    }
+    t.bytes = bytes;
+    t.dtype = dtype;
+    *out = &t;
+    return MR_OK;
+}
+
+const TensorSlot *tensor(mr_model *m, const std::string &name) {
+    auto it = m->tensors.find(name);
+    return it == m->tensors.end() ? nullptr : &it->second;
+}
+
+Segment segment(const TensorSlot *t, float *out = nullptr) {
+    Segment s{};
+    s.w = t->ptr;
+    s.dtype = t->dtype;
+    s.rows = (int)t->shape[0];
+    s.cols = (int)t->shape[1];
+    s.out = out;
+    return s;
+}
+
+Phase gemv_phase(int layer, const float *in, const TensorSlot *norm_gain, float eps) {
+    Phase ph{};
+    ph.kind = PH_GEMV;
+    ph.layer = layer;
+    ph.gemv.input_kind = IN_VECTOR;
+    ph.gemv.in = in;
+    if (norm_gain) {
+        ph.gemv.norm = 1;
+        ph.gemv.norm_gain = norm_gain->ptr;
+        ph.gemv.norm_gain_dtype = norm_gain->dtype;
+        ph.gemv.norm_eps = eps;
+    }
+    return ph;
+}
+
+int build_plan(mr_model *m) {
+    const mr_model_config &c = m->cfg;
+    if (!is_gqa_family(c.family))
+        return set_error(MR_ERR_ARGUMENT, "family %d is not supported by this engine build yet", c.family);
+    m->phases.clear();
+    const TensorSlot *embed = tensor(m, "embed");
+    for (int l = 0; l < c.layers; ++l) {
+        const std::string p = "layers." + std::to_string(l) + ".";
+        // 1. RMSNorm(x) -> q, k, v (layer 0 reads the embedding row directly)
+        Phase qkv = gemv_phase(l, m->x, tensor(m, p + "a_norm"), c.norm_eps);
+        if (l == 0) {
+            qkv.gemv.input_kind = IN_EMBED_ROW;
+            qkv.gemv.embed = embed->ptr;
+            qkv.gemv.embed_dtype = embed->dtype;
+            qkv.gemv.embed_copy = m->x;
+        }
+        qkv.gemv.nseg = 3;
+        qkv.gemv.seg[0] = segment(tensor(m, p + "q"), m->q_raw);
+        qkv.gemv.seg[1] = segment(tensor(m, p + "k"), m->k_raw);
+        qkv.gemv.seg[2] = segment(tensor(m, p + "v"), m->v_raw);
+        qkv.gemv.epilogue = EPI_STORE;
+        m->phases.push_back(qkv);
+        // 2. attention
+        Phase at{};
+        at.kind = PH_ATTN_GQA;
+        at.layer = l;
+        AttnPhase &a = at.attn;
+        a.q_raw = m->q_raw;
+        a.k_raw = m->k_raw;
+        a.v_raw = m->v_raw;
+        a.qk_norm = c.qk_norm;
+        if (c.qk_norm) {
+            const TensorSlot *qn = tensor(m, p + "q_norm"), *kn = tensor(m, p + "k_norm");
+            if (qn->dtype != kn->dtype) return set_error(MR_ERR_ARGUMENT, "q_norm/k_norm dtypes differ");
+            a.q_gain = qn->ptr;
+            a.k_gain = kn->ptr;
+            a.gain_dtype = qn->dtype;
+        }
+        a.norm_eps = c.norm_eps;
+        a.heads = c.query_heads;
+        a.kv_heads = m->layer_kvh[l];
+        a.dim = c.head_dim;
+        a.split_half = c.split_half_rope;
+        a.inv_freq = m->d_inv_freq;
+        a.k_cache = m->k_cache[l];
+        a.v_cache = m->v_cache[l];
+        a.capacity = m->cache_capacity[l];
+        a.partial = m->partial;
+        a.arrivals = m->arrivals;
+        a.max_chunks = m->max_chunks;
+        a.out = m->attn;
+        m->phases.push_back(at);
+        // 3. o projection + residual (model.py:282)
+        Phase o = gemv_phase(l, m->attn, nullptr, 0.f);
+        o.gemv.nseg = 1;
+        o.gemv.seg[0] = segment(tensor(m, p + "o"));
+        o.gemv.epilogue = EPI_RESIDUAL;
+        o.gemv.scale = c.residual_scale;
+        o.gemv.x = m->x;
+        m->phases.push_back(o);
+        // 4. RMSNorm(x) -> gate, up -> SwiGLU (model.py:87-89)
+        Phase gu = gemv_phase(l, m->x, tensor(m, p + "f_norm"), c.norm_eps);
+        gu.gemv.nseg = 2;
+        gu.gemv.seg[0] = segment(tensor(m, p + "ffn.gate"));
+        gu.gemv.seg[1] = segment(tensor(m, p + "ffn.up"));
+        gu.gemv.epilogue = EPI_SWIGLU;
+        gu.gemv.out = m->ffn;
+        m->phases.push_back(gu);
+        // 5. down projection + residual (model.py:283)
+        Phase dn = gemv_phase(l, m->ffn, nullptr, 0.f);
+        dn.gemv.nseg = 1;
+        dn.gemv.seg[0] = segment(tensor(m, p + "ffn.down"));
+        dn.gemv.epilogue = EPI_RESIDUAL;
+        dn.gemv.scale = c.residual_scale;
+        dn.gemv.x = m->x;
+        m->phases.push_back(dn);
+    }
+    // final RMSNorm + head (model.py:285, 307)
+    Phase head = gemv_phase(-1, m->x, tensor(m, "norm"), c.norm_eps);
+    head.gemv.nseg = 1;
+    head.gemv.seg[0] = segment(tensor(m, c.tie_embeddings ? "embed" : "output"));
+    head.gemv.epilogue = EPI_LOGITS;
+    head.gemv.out = m->logits;
+    m->phases.push_back(head);
+    Phase end{};
+    end.kind = PH_STEP_END;
+    end.layer = -2;
+    m->phases.push_back(end);
+    return MR_OK;
+}
+
+int sync_and_check(mr_model *m, const char *what) {
+    MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    int error = 0;
+    MR_CUDA_TRY(cudaMemcpy(&error, &m->state->error, sizeof(int), cudaMemcpyDeviceToHost));
+    if (error) {
+        m->failed = true;
+        if (error == 3) return set_error(MR_ERR_STATE, "%s: context_length exceeded on the device", what);
+        return set_error(MR_ERR_TIMEOUT, "%s: device wait timed out (code %d); call reset()", what, error);
+    }
+    return MR_OK;
+}
+
+int ensure_feed(mr_model *m, int n) {
+    if (n <= m->feed_capacity) return MR_OK;
+    int rc = MR_OK;
+    const int cap = std::max(n, 256);
+    m->feed = static_cast<int *>(device_alloc(m, sizeof(int) * cap, &rc));
+    if (rc) return rc;
+    m->feed_capacity = cap;
+    return MR_OK;
+}
+
+int ensure_gen(mr_model *m, int n) {
+    if (n <= m->gen_capacity) return MR_OK;
+    int rc = MR_OK;
+    const int cap = std::max(n, 256);
+    m->gen_out = static_cast<int *>(device_alloc(m, sizeof(int) * cap, &rc));
+    if (rc) return rc;
+    m->gen_capacity = cap;
+    return MR_OK;
+}
+
+int launch_step(mr_model *m, const StepControl &ctl) {
+    int nphases = (int)m->phases.size();
+    StepControl control = ctl;
+    void *args[] = {&m->d_phases, &nphases, &m->state, &control};
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(m->grid);
+    cfg.blockDim = dim3(kEngineThreads);
+    cfg.dynamicSmemBytes = decode_step_smem_bytes();
+    cfg.stream = m->ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MR_CUDA_TRY(cudaLaunchKernelExC(&cfg, reinterpret_cast<const void *>(decode_step_kernel), args));
+    return MR_OK;
+}
+
+StepControl base_control(mr_model *m) {
+    StepControl ctl{};
+    ctl.feed = m->feed;
+    ctl.feed_base = m->position;
+    ctl.logits_rows = m->logits_rows;
+    ctl.eos = -1;
+    ctl.context_length = m->cfg.context_length;
+    return ctl;
+}
+
+int ready(mr_model *m) {
+    MR_REQUIRE(m, "model is NULL");
+    if (!m->finalized) return set_error(MR_ERR_STATE, "model is not finalized");
+    if (m->failed)
+        return set_error(MR_ERR_STATE, "A previous device operation failed; call reset() before reusing this model");
+    MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
+    return MR_OK;
+}
+
+// Runs n fed tokens starting at the current position; logits of the selected
+// rows are copied to `out` (return_all: n rows, else the last row only).
+int run_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
+    const int V = m->cfg.vocab_size;
+    for (int i = 0; i < n; ++i) MR_REQUIRE(ids[i] >= 0 && ids[i] < V, "input token is outside the vocabulary");
+    MR_REQUIRE(m->position + n <= m->cfg.context_length,
+               "input would exceed context_length; reset or allocate a larger context");
+    int rc = ensure_feed(m, n);
+    if (rc) return rc;
+    MR_CUDA_TRY(cudaMemcpyAsync(m->feed, ids, sizeof(int) * n, cudaMemcpyHostToDevice, m->ctx->stream));
+    StepControl ctl = base_control(m);
+    ctl.feed_len = n;
+    ctl.return_all = return_all;
+    int done = 0;
+    while (done < n) {
+        const int batch = return_all ? std::min(m->logits_rows, n - done) : n - done;
+        for (int i = 0; i < batch; ++i) {
+            rc = launch_step(m, ctl);
+            if (rc) {
+                m->failed = true;
+                return rc;
+            }
+        }
+        if (return_all && out) {
+            for (int i = 0; i < batch; ++i) {
+                const int row = (done + i) % m->logits_rows;
+                MR_CUDA_TRY(cudaMemcpyAsync(out + (size_t)(done + i) * V, m->logits + (size_t)row * V,
+                                            sizeof(float) * V, cudaMemcpyDeviceToHost, m->ctx->stream));
+            }
+        }
+        rc = sync_and_check(m, "prefill");
+        if (rc) return rc;
+        done += batch;
+    }
+    if (!return_all && out) MR_CUDA_TRY(cudaMemcpy(out, m->logits, sizeof(float) * V, cudaMemcpyDeviceToHost));
+    m->position += n;
+    return MR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mr_model_create(mr_context *ctx, const mr_model_config *config, const int *layer_kv_heads,
+                    const int *layer_window, const float *inv_freq, mr_model **out) {
+    MR_REQUIRE(ctx && config && layer_kv_heads && layer_window && inv_freq && out, "NULL argument");
+    const mr_model_config &c = *config;
+    MR_REQUIRE(c.family >= 0 && c.family <= MR_FAMILY_HEAVY_MEDIUM_20, "unknown family %d", c.family);
+    MR_REQUIRE(c.vocab_size > 0 && c.hidden_size > 0 && c.layers > 0 && c.query_heads > 0 && c.kv_heads > 0 &&
+                   c.head_dim > 0 && c.head_dim % 2 == 0 && c.ffn_dim > 0 && c.context_length > 0,
+               "invalid model geometry");
+    MR_REQUIRE(c.head_dim <= 256, "head_dim %d too large for the engine", c.head_dim);
+    for (int l = 0; l < c.layers; ++l)
+        MR_REQUIRE(layer_kv_heads[l] > 0 && c.query_heads % layer_kv_heads[l] == 0, "layer %d: invalid KV head count",
+                   l);
+    MR_CUDA_TRY(cudaSetDevice(ctx->device));
+    auto *m = new mr_model();
+    m->ctx = ctx;
+    m->cfg = c;
+    m->layer_kvh.assign(layer_kv_heads, layer_kv_heads + c.layers);
+    m->layer_window.assign(layer_window, layer_window + c.layers);
+    m->inv_freq.assign(inv_freq, inv_freq + c.head_dim / 2);
+    expected_tensors(m);
+    m->grid = ctx->sm_count;
+    *out = m;
+    return MR_OK;
+}
+
+int mr_model_destroy(mr_model *m) {
+    if (!m) return MR_OK;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    for (void *p : m->allocations) cudaFree(p);
+    if (m->ev0) cudaEventDestroy(m->ev0);
+    if (m->ev1) cudaEventDestroy(m->ev1);
+    delete m;
+    return MR_OK;
+}
+
+int mr_model_load_tensor(mr_model *m, const char *name, int dtype, int ndim, const int64_t *shape,
+                         const void *host) {
+    MR_REQUIRE(m && host, "NULL argument");
+    MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
+    TensorSlot *t = nullptr;
+    int rc = check_tensor(m, name, dtype, ndim, shape, &t);
+    if (rc) return rc;
+    MR_CUDA_TRY(cudaMemcpyAsync(t->ptr, host, t->bytes, cudaMemcpyHostToDevice, m->ctx->stream));
+    MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    return MR_OK;
+}
+
+int mr_model_fill_synthetic(mr_model *m, const char *name, int dtype, int ndim, const int64_t *shape,
+                            uint64_t seed, int tensor_index, float scale, float fill) {
+    MR_REQUIRE(m, "NULL argument");
+    MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
+    TensorSlot *t = nullptr;
+    int rc = check_tensor(m, name, dtype, ndim, shape, &t);
+    if (rc) return rc;
+    const size_t n = t->bytes / dtype_size(dtype);
+    const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 64);
+    if (scale != 0.0f) {
+        MR_REQUIRE(dtype == MR_DTYPE_BF16, "%s: the hash generator produces BF16 only", name);
+        const uint64_t key = host_splitmix(seed * 0x9E3779B97F4A7C15ull + (uint64_t)(tensor_index + 1));
+        k_fill_hash_bf16<<<blocks, 256, 0, m->ctx->stream>>>(static_cast<uint16_t *>(t->ptr), n, key, scale);
+    } else {
+        k_fill_value<<<blocks, 256, 0, m->ctx->stream>>>(t->ptr, dtype, n, fill);
+    }
+    MR_CUDA_TRY(cudaGetLastError());
+    MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    return MR_OK;
+}
+
+int mr_model_finalize(mr_model *m) {
+    MR_REQUIRE(m, "model is NULL");
+    MR_REQUIRE(!m->finalized, "model already finalized");
+    MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
+    for (auto &kv : m->tensors)
+        if (!kv.second.ptr || kv.second.dtype < 0)
+            return set_error(MR_ERR_ARGUMENT, "Missing tensor %s", kv.first.c_str());
+    if (!is_gqa_family(m->cfg.family))
+        return set_error(MR_ERR_ARGUMENT, "family %d is not supported by this engine build yet", m->cfg.family);
+    for (auto &kv : m->tensors)
+        if (kv.second.shape.size() == 2 && kv.second.shape[1] > kMaxInput)
+            return set_error(MR_ERR_ARGUMENT, "%s: input width %lld above the engine limit %d", kv.first.c_str(),
+                             (long long)kv.second.shape[1], kMaxInput);
+    const mr_model_config &c = m->cfg;
+    int rc = MR_OK;
+    const int H = c.query_heads, d = c.head_dim;
+    const int max_kvh = *std::max_element(m->layer_kvh.begin(), m->layer_kvh.end());
+    const int gq_max = H / *std::min_element(m->layer_kvh.begin(), m->layer_kvh.end());
+    // attention scratch must fit the shared input area (see attn_gqa_phase)
+    const int attn_floats = 2 * gq_max * d + 32 * (d + 1) + 32 * d + gq_max * 32 + 3 * gq_max + d;
+    MR_REQUIRE(attn_floats <= kMaxInput, "attention group too large for shared memory");
+    auto falloc = [&](size_t n) { return static_cast<float *>(device_alloc(m, n * sizeof(float), &rc)); };
+    m->d_inv_freq = falloc(d / 2);
+    m->x = falloc(c.hidden_size);
+    m->q_raw = falloc((size_t)H * d);
+    m->k_raw = falloc((size_t)max_kvh * d);
+    m->v_raw = falloc((size_t)max_kvh * d);
+    m->attn = falloc((size_t)H * d);
+    m->ffn = falloc(c.ffn_dim);
+    m->logits_rows = 64;
+    m->logits = falloc((size_t)m->logits_rows * c.vocab_size);
+    m->max_chunks = m->grid;
+    m->partial = falloc((size_t)H * m->max_chunks * (d + 2));
+    m->arrivals = static_cast<unsigned int *>(device_alloc(m, sizeof(unsigned) * max_kvh, &rc));
+    m->state = static_cast<StepState *>(device_alloc(m, sizeof(StepState), &rc));
+    if (rc) return rc;
+    m->k_cache.resize(c.layers);
+    m->v_cache.resize(c.layers);
+    m->cache_capacity.resize(c.layers);
+    for (int l = 0; l < c.layers; ++l) {
+        // model.py:105: capacity = min(window or context, context)
+        const int w = m->layer_window[l];
+        const int cap = std::min(w > 0 ? w : c.context_length, c.context_length);
+        m->cache_capacity[l] = cap;
+        const size_t n = (size_t)m->layer_kvh[l] * cap * d;
+        m->k_cache[l] = falloc(n);
+        m->v_cache[l] = falloc(n);
+        if (rc) return rc;
+    }
+    MR_CUDA_TRY(cudaMemcpy(m->d_inv_freq, m->inv_freq.data(), sizeof(float) * (d / 2), cudaMemcpyHostToDevice));
+    MR_CUDA_TRY(cudaMemset(m->arrivals, 0, sizeof(unsigned) * max_kvh));
+    rc = build_plan(m);
+    if (rc) return rc;
+    m->d_phases = static_cast<Phase *>(device_alloc(m, sizeof(Phase) * m->phases.size(), &rc));
+    if (rc) return rc;
+    MR_CUDA_TRY(cudaMemcpy(m->d_phases, m->phases.data(), sizeof(Phase) * m->phases.size(), cudaMemcpyHostToDevice));
+    MR_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void *>(decode_step_kernel),
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_step_smem_bytes()));
+    int per_sm = 0;
+    MR_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reinterpret_cast<const void *>(decode_step_kernel),
+                                                              kEngineThreads, decode_step_smem_bytes()));
+    MR_REQUIRE(per_sm >= 1, "decode kernel cannot be resident (occupancy 0)");
+    MR_CUDA_TRY(cudaEventCreate(&m->ev0));
+    MR_CUDA_TRY(cudaEventCreate(&m->ev1));
+    m->finalized = true;
+    return mr_model_reset(m);
+}
+
+int mr_model_reset(mr_model *m) {
+    MR_REQUIRE(m, "model is NULL");
+    MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
+    if (!m->finalized) return set_error(MR_ERR_STATE, "model is not finalized");
+    MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    MR_CUDA_TRY(cudaMemset(m->state, 0, sizeof(StepState)));
+    m->position = 0;
+    m->failed = false;
+    return MR_OK;
+}
+
+int mr_model_position(const mr_model *m, int *position) {
+    MR_REQUIRE(m && position, "NULL argument");
+    *position = m->position;
+    return MR_OK;
+}
+
+int mr_model_weight_bytes(const mr_model *m, uint64_t *bytes) {
+    MR_REQUIRE(m && bytes, "NULL argument");
+    uint64_t total = 0;
+    for (auto &kv : m->tensors) total += kv.second.bytes;
+    *bytes = total;
+    return MR_OK;
+}
+
+int mr_model_step(mr_model *m, int token, float *logits_out, int *argmax_out) {
+    int rc = ready(m);
+    if (rc) return rc;
+    rc = run_feed(m, &token, 1, 0, logits_out);
+    if (rc) return rc;
+    if (argmax_out) {
+        StepState s;
+        MR_CUDA_TRY(cudaMemcpy(&s, m->state, sizeof(s), cudaMemcpyDeviceToHost));
+        *argmax_out = s.last_argmax;
+    }
+    return MR_OK;
+}
+
+int mr_model_prefill(mr_model *m, const int *ids, int n, int return_all, float *out) {
+    int rc = ready(m);
+    if (rc) return rc;
+    MR_REQUIRE(ids && n > 0, "input_ids must be a non-empty 1D integer sequence");
+    return run_feed(m, ids, n, return_all, out);
+}
+
+int mr_model_generate_greedy(mr_model *m, const int *ids, int n, int max_new, int eos, int *out_tokens,
+                             int *out_count, int *out_nonfinite) {
+    int rc = ready(m);
+    if (rc) return rc;
+    MR_REQUIRE(ids && n > 0 && out_tokens && out_count && out_nonfinite, "NULL argument");
+    MR_REQUIRE(max_new > 0, "max_new must be positive");
+    const int V = m->cfg.vocab_size;
+    for (int i = 0; i < n; ++i) MR_REQUIRE(ids[i] >= 0 && ids[i] < V, "input token is outside the vocabulary");
+    MR_REQUIRE(m->position + n + max_new - 1 <= m->cfg.context_length,
+               "prompt plus requested generation exceeds context_length");
+    rc = ensure_feed(m, n);
+    if (!rc) rc = ensure_gen(m, max_new);
+    if (rc) return rc;
+    MR_CUDA_TRY(cudaMemcpyAsync(m->feed, ids, sizeof(int) * n, cudaMemcpyHostToDevice, m->ctx->stream));
+    StepControl ctl = base_control(m);
+    ctl.feed_len = n;
+    ctl.gen_max = max_new;
+    ctl.eos = eos;
+    ctl.gen_out = m->gen_out;
+    for (int i = 0; i < n + max_new - 1; ++i) {
+        rc = launch_step(m, ctl);
+        if (rc) {
+            m->failed = true;
+            return rc;
+        }
+    }
+    rc = sync_and_check(m, "generate");
+    if (rc) return rc;
+    StepState s;
+    MR_CUDA_TRY(cudaMemcpy(&s, m->state, sizeof(s), cudaMemcpyDeviceToHost));
+    *out_count = s.gen_count;
+    *out_nonfinite = s.nonfinite;
+    if (s.gen_count) MR_CUDA_TRY(cudaMemcpy(out_tokens, m->gen_out, sizeof(int) * s.gen_count, cudaMemcpyDeviceToHost));
+    m->position = s.position;
+    // leave the state ready for further decode calls
+    MR_CUDA_TRY(cudaMemset(&m->state->stopped, 0, sizeof(int)));
+    MR_CUDA_TRY(cudaMemset(&m->state->gen_count, 0, sizeof(int)));
+    return MR_OK;
+}
+
+int mr_model_layer_state(const mr_model *m, int layer, int loop, mr_layer_state *out) {
+    MR_REQUIRE(m && out, "NULL argument");
+    MR_REQUIRE(layer >= 0 && layer < m->cfg.layers, "layer out of range");
+    MR_REQUIRE(loop >= 0 && loop < std::max(1, m->cfg.inner_loop_steps), "loop out of range");
+    memset(out, 0, sizeof(*out));
+    out->present = m->position > 0;
+    if (!out->present || !m->finalized) return MR_OK;
+    const int cap = m->cache_capacity[layer];
+    out->ring_count = m->position;
+    out->ring_capacity = cap;
+    out->ring_length = std::min(m->position, cap);
+    out->ring_start = (m->position - out->ring_length) % cap;
+    return MR_OK;
+}
+
+int mr_model_latent_positions(const mr_model *m, int layer, int *out, int capacity, int *rows) {
+    MR_REQUIRE(m && rows, "NULL argument");
+    (void)layer;
+    (void)out;
+    (void)capacity;
+    *rows = 0;
+    return set_error(MR_ERR_ARGUMENT, "model has no latent cache");
+}
+
+int mr_model_last_topk(const mr_model *m, int layer, int loop, int *blocks, int capacity) {
+    (void)layer;
+    (void)loop;
+    (void)blocks;
+    (void)capacity;
+    MR_REQUIRE(m, "NULL argument");
+    return set_error(MR_ERR_ARGUMENT, "model has no sparse block attention");
+}
+
+int mr_model_last_experts(const mr_model *m, int layer, int loop, int *experts, float *weights, int capacity) {
+    (void)layer;
+    (void)loop;
+    (void)experts;
+    (void)weights;
+    (void)capacity;
+    MR_REQUIRE(m, "NULL argument");
+    return set_error(MR_ERR_ARGUMENT, "model has no experts");
+}
+
+int mr_model_bench_decode(mr_model *m, int first_token, int steps, float *device_ms) {
+    int rc = ready(m);
+    if (rc) return rc;
+    MR_REQUIRE(device_ms && steps > 0, "bad arguments");
+    MR_REQUIRE(first_token >= 0 && first_token < m->cfg.vocab_size, "token outside the vocabulary");
+    MR_REQUIRE(m->position + steps <= m->cfg.context_length, "decode steps exceed context_length");
+    rc = ensure_feed(m, 1);
+    if (!rc) rc = ensure_gen(m, steps);
+    if (rc) return rc;
+    MR_CUDA_TRY(cudaMemcpyAsync(m->feed, &first_token, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
+    StepControl ctl = base_control(m);
+    ctl.feed_len = 1;
+    ctl.gen_max = steps + 1;
+    ctl.gen_out = m->gen_out;
+    MR_CUDA_TRY(cudaEventRecord(m->ev0, m->ctx->stream));
+    for (int i = 0; i < steps; ++i) {
+        rc = launch_step(m, ctl);
+        if (rc) {
+            m->failed = true;
+            return rc;
+        }
+    }
+    MR_CUDA_TRY(cudaEventRecord(m->ev1, m->ctx->stream));
+    rc = sync_and_check(m, "bench");
+    if (rc) return rc;
+    MR_CUDA_TRY(cudaEventElapsedTime(device_ms, m->ev0, m->ev1));
+    StepState s;
+    MR_CUDA_TRY(cudaMemcpy(&s, m->state, sizeof(s), cudaMemcpyDeviceToHost));
+    m->position = s.position;
+    MR_CUDA_TRY(cudaMemset(&m->state->stopped, 0, sizeof(int)));
+    MR_CUDA_TRY(cudaMemset(&m->state->gen_count, 0, sizeof(int)));
+    return MR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,312 @@
+"""``MiracleModel``: the reference token-loop API on the CUDA engine.
+
+Same public surface as the reference (miracle_reasoning/model.py:36-357):
+``MiracleModel(config, weights, *, backend, context_length,
+weight_cache_bytes)``, ``from_pretrained``, ``prefill(ids, return_all)``,
+``decode(id)``, ``generate(...)``, ``reset()``, and the attributes
+``position``, ``states`` and ``weight_cache``, with the same validation order
+and error types.
+
+What runs underneath is different: the checkpoint's stored bytes are copied
+once into HBM (no LRU, no host widening), and each token is one launch of the
+persistent decode kernel (csrc/engine_kernel.cu).  Greedy ``generate`` runs
+entirely on the device (argmax feeds the next step); sampled ``generate``
+reads the logits each step and samples on the host with the reference's exact
+NumPy procedure.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+import math
+from pathlib import Path
+
+import numpy as np
+
+from . import _native
+from .backend import CUDABackend
+from .config import ModelConfig
+from .weights import DTYPE_BF16, DTYPE_F32, SafeTensors, ShardedSafeTensors, adapt_weights, expected_shapes, \
+    stored_tensor
+
+_I32 = C.POINTER(C.c_int)
+_F32 = C.POINTER(C.c_float)
+
+
+def engine_config(config: ModelConfig, context_length: int) -> _native.ModelConfigC:
+    """Flatten a ModelConfig into the C struct mr_model_config."""
+    s = config.source
+    c = _native.ModelConfigC()
+    c.family = _native.FAMILY_CODES[config.family]
+    for name in ("vocab_size", "hidden_size", "layers", "query_heads", "kv_heads", "head_dim", "ffn_dim",
+                 "latent_dim", "memory_slots", "cbr_chunk_size", "cbr_slots", "inner_loop_steps"):
+        setattr(c, name, getattr(config, name))
+    c.context_length = context_length
+    c.window = config.window or 0
+    c.tie_embeddings = int(config.tie_embeddings)
+    c.qk_norm = int(config.qk_norm)
+    c.split_half_rope = int(config.split_half_rope)
+    c.norm_eps, c.residual_scale, c.cbr_norm_eps = config.norm_eps, config.residual_scale, config.cbr_norm_eps
+    if config.family == "heavy-medium-2.0":
+        geometry = s["long_context"]
+        c.routed_experts, c.router_groups = s["routed_experts"], s["router_groups"]
+        c.router_top_k_min, c.router_top_k_max = s["router_top_k_min"], s["router_top_k_max"]
+        c.shared_experts = s["shared_experts"]
+        c.block_size, c.global_slots = geometry["global_block_size"], geometry["global_slots"]
+        c.router_temperature = float(np.float32(max(s.get("router_temperature", 1.0), 1e-4)))
+        c.alibi_slope = float(np.float32(geometry.get("alibi_slope_scale", 0.015) / math.sqrt(config.head_dim)))
+    return c
+
+
+class ResidentWeights:
+    """Stands where the reference's WeightCache was: the whole model is resident."""
+
+    def __init__(self, used, budget):
+        self.used, self.budget = used, budget
+
+
+class RingView:
+    def __init__(self, count, capacity, length, start, width):
+        self.count, self.capacity, self.width = count, capacity, width
+        self.length, self.start = length, start
+
+
+class RelayView:
+    def __init__(self, count):
+        self.count = count
+
+
+class LatentView:
+    def __init__(self, rows, width):
+        self.shape = (rows, width)
+
+
+class MiracleModel:
+    """FP32 next-token engine for six Miracle architectures on one B200.
+
+    Each instance owns one sequence; call reset() for a new request.
+    """
+
+    def __init__(self, config, weights=None, *, backend=None, context_length=None,
+                 weight_cache_bytes=256 * 1024 * 1024, _synthetic=None):
+        self.config = config
+        if context_length is None:
+            context_length = min(2048, config.max_positions)
+        if type(context_length) is not int or not 0 < context_length <= config.max_positions:
+            raise ValueError(f"context_length must be in [1, {config.max_positions}]")
+        if type(weight_cache_bytes) is not int or weight_cache_bytes < 4096:
+            raise ValueError("weight_cache_bytes must be an integer >= 4096")
+        # Validate the full checkpoint before creating any device allocations.
+        self.weights = adapt_weights(config, weights) if _synthetic is None else None
+        backend = backend if backend is not None else CUDABackend()
+        if not isinstance(backend, CUDABackend):
+            raise TypeError("MiracleModel runs on a CUDABackend (there is no CPU path)")
+        self.backend = backend
+        self.context_length = context_length
+        self._handle = None
+        kv = (C.c_int * config.layers)(*[config.layer_kv_heads(i) for i in range(config.layers)])
+        windows = (C.c_int * config.layers)(*[config.layer_window(i) or 0 for i in range(config.layers)])
+        inv = np.ascontiguousarray(config.inverse_frequencies(), dtype=np.float32)
+        handle = C.c_void_p()
+        cfg = engine_config(config, context_length)
+        _native.call("mr_model_create", backend.context, C.byref(cfg), kv, windows,
+                     inv.ctypes.data_as(_F32), C.byref(handle))
+        self._handle = handle
+        if _synthetic is None:
+            self._load(self.weights)
+        else:
+            self._fill_synthetic(*_synthetic)
+        _native.call("mr_model_finalize", self._handle)
+        used = C.c_uint64()
+        _native.call("mr_model_weight_bytes", self._handle, C.byref(used))
+        self.weight_cache = ResidentWeights(int(used.value), weight_cache_bytes)
+        self.frequencies = backend.upload(inv)
+        self.reset()
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle and _native._lib is not None:
+            _native._lib.mr_model_destroy(handle)
+            self._handle = None
+
+    def _load(self, weights):
+        for name, shape in expected_shapes(self.config).items():
+            dtype, array = stored_tensor(weights, name)
+            dims = (C.c_int64 * len(shape))(*shape)
+            _native.call("mr_model_load_tensor", self._handle, name.encode(), dtype, len(shape), dims,
+                         array.ctypes.data)
+
+    def _fill_synthetic(self, stored, seed):
+        from . import synthetic
+        host = synthetic.synthetic_weights(self.config, "F32", seed) if stored == "F32" else None
+        for index, name, shape, std in synthetic.tensor_plan(self.config):
+            dims = (C.c_int64 * len(shape))(*shape)
+            if host is not None:
+                array = np.ascontiguousarray(host[name], dtype=np.float32)
+                _native.call("mr_model_load_tensor", self._handle, name.encode(), DTYPE_F32, len(shape), dims,
+                             array.ctypes.data)
+            elif std is None:
+                _native.call("mr_model_fill_synthetic", self._handle, name.encode(), DTYPE_F32, len(shape), dims,
+                             0, index, 0.0, 1.0)
+            else:
+                scale = float(np.float32(std / 65536.0))
+                _native.call("mr_model_fill_synthetic", self._handle, name.encode(), DTYPE_BF16, len(shape), dims,
+                             seed, index, scale, 0.0)
+
+    @classmethod
+    def synthetic(cls, config, *, stored="BF16", seed=0, **kwargs):
+        """Random-initialised model built directly in HBM (see synthetic.py)."""
+        return cls(config, None, _synthetic=(stored, seed), **kwargs)
+
+    @classmethod
+    def from_pretrained(cls, directory, *, family=None, **kwargs):
+        directory = Path(directory)
+        config = ModelConfig.from_dict(json.loads((directory / "config.json").read_text(encoding="utf-8")), family)
+        if (directory / "model.safetensors").is_file():
+            weights = SafeTensors(directory / "model.safetensors")
+        elif (directory / "model.npz").is_file():
+            weights = np.load(directory / "model.npz", allow_pickle=False)
+        elif (directory / "model.safetensors.index.json").is_file():
+            weights = ShardedSafeTensors(directory / "model.safetensors.index.json")
+        else:
+            raise ValueError("Expected model.safetensors, a safetensors index, or model.npz; "
+                             "use the export command for PyTorch checkpoints")
+        return cls(config, weights, **kwargs)
+
+    # sequence state -------------------------------------------------------------
+    def reset(self):
+        """Release sequence caches while retaining weights."""
+        _native.call("mr_model_reset", self._handle)
+        self._failed = False
+
+    @property
+    def position(self):
+        value = C.c_int()
+        _native.call("mr_model_position", self._handle, C.byref(value))
+        return value.value
+
+    @property
+    def states(self):
+        """Per-layer cache views with the attributes the reference exposes."""
+        c = self.config
+        views = []
+        for layer in range(c.layers):
+            entry = {}
+            loops = c.inner_loop_steps if c.family == "heavy-medium-2.0" else 1
+            per_loop = []
+            for loop in range(loops):
+                st = _native.LayerState()
+                _native.call("mr_model_layer_state", self._handle, layer, loop, C.byref(st))
+                per_loop.append(st)
+            st = per_loop[0]
+            if st.present:
+                width = c.layer_kv_heads(layer) * c.head_dim
+                if c.family == "heavy-medium-2.0":
+                    entry["loops"] = [{"ring": RingView(s.ring_count, s.ring_capacity, s.ring_length,
+                                                        s.ring_start, c.kv_heads * c.head_dim)} for s in per_loop]
+                elif c.family == "flashlighting-2.0":
+                    entry["latent"] = LatentView(st.latent_rows, c.latent_dim)
+                    entry["memory_size"] = st.memory_size
+                    entry["positions"] = self._latent_positions(layer, st.latent_rows)
+                else:
+                    entry["ring"] = RingView(st.ring_count, st.ring_capacity, st.ring_length, st.ring_start, width)
+                    if c.family == "flashnano-1.6" and st.relay_count:
+                        entry["relay"] = RelayView(st.relay_count)
+            views.append(entry)
+        return views
+
+    def _latent_positions(self, layer, rows):
+        out = (C.c_int * max(rows, 1))()
+        n = C.c_int()
+        _native.call("mr_model_latent_positions", self._handle, layer, out, max(rows, 1), C.byref(n))
+        return list(out[:n.value])
+
+    # token loop -------------------------------------------------------------------
+    def _tokens(self, ids):
+        array = np.asarray(ids)
+        if array.ndim != 1 or array.size == 0 or array.dtype.kind not in "iu":
+            raise ValueError("input_ids must be a non-empty 1D integer sequence")
+        if np.any(array < 0) or np.any(array >= self.config.vocab_size):
+            raise ValueError("input token is outside the vocabulary")
+        return array
+
+    def prefill(self, input_ids, *, return_all=False):
+        """Append a prompt, returning [vocab] or, if requested, [tokens, vocab]."""
+        tokens = self._tokens(input_ids)
+        if self._failed:
+            raise RuntimeError("A previous device operation failed; call reset() before reusing this model")
+        if self.position + len(tokens) > self.context_length:
+            raise ValueError("input would exceed context_length; reset or allocate a larger context")
+        ids = np.ascontiguousarray(tokens, dtype=np.int32)
+        V = self.config.vocab_size
+        out = np.empty((len(ids), V) if return_all else (V,), dtype=np.float32)
+        try:
+            _native.call("mr_model_prefill", self._handle, ids.ctypes.data_as(_I32), len(ids), int(return_all),
+                         out.ctypes.data_as(_F32))
+        except Exception:
+            self._failed = True
+            raise
+        return out
+
+    def decode(self, token_id):
+        """Append one token to the current sequence and return next-token logits."""
+        return self.prefill([token_id])
+
+    def generate(self, input_ids, *, max_new_tokens=32, temperature=0.0, top_k=0, top_p=1.0, seed=17,
+                 eos_token_id=None):
+        """Return generated token IDs, excluding the prompt and including EOS."""
+        tokens = self._tokens(input_ids)
+        if type(max_new_tokens) is not int or max_new_tokens < 0:
+            raise ValueError("max_new_tokens must be a non-negative integer")
+        if not math.isfinite(temperature) or temperature < 0:
+            raise ValueError("temperature must be finite and non-negative")
+        if type(top_k) is not int or top_k < 0 or not math.isfinite(top_p) or not 0 < top_p <= 1:
+            raise ValueError("top_k must be non-negative and top_p must be in (0,1]")
+        eos = self.config.eos_token_id if eos_token_id is None else eos_token_id
+        if type(eos) is not int or not 0 <= eos < self.config.vocab_size:
+            raise ValueError("eos_token_id is outside vocabulary")
+        if len(tokens) + max(0, max_new_tokens - 1) > self.context_length:
+            raise ValueError("prompt plus requested generation exceeds context_length")
+        self.reset()
+        if max_new_tokens == 0:
+            return []
+        if temperature == 0:
+            return self._generate_greedy(tokens, max_new_tokens, eos)
+        rng, generated = np.random.default_rng(seed), []
+        logits = self.prefill(tokens)
+        for i in range(max_new_tokens):
+            if not np.all(np.isfinite(logits)):
+                raise FloatingPointError("non-finite output logits")
+            token = sample_next(logits, temperature, top_k, top_p, rng)
+            generated.append(token)
+            if token == eos or i + 1 == max_new_tokens:
+                break
+            logits = self.decode(token)
+        return generated
+
+    def _generate_greedy(self, tokens, max_new_tokens, eos):
+        ids = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros(max_new_tokens, dtype=np.int32)
+        count, nonfinite = C.c_int(), C.c_int()
+        try:
+            _native.call("mr_model_generate_greedy", self._handle, ids.ctypes.data_as(_I32), len(ids),
+                         max_new_tokens, eos, out.ctypes.data_as(_I32), C.byref(count), C.byref(nonfinite))
+        except Exception:
+            self._failed = True
+            raise
+        if nonfinite.value:
+            raise FloatingPointError("non-finite output logits")
+        return [int(t) for t in out[:count.value]]
+
+
+def sample_next(logits, temperature, top_k, top_p, rng):
+    """Seeded top-k/top-p sampling, the reference's exact procedure (model.py:343-352)."""
+    order = np.argsort(-logits, kind="stable")
+    if top_k:
+        order = order[:top_k]
+    scores = logits[order].astype(np.float64) / temperature
+    probs = np.exp(scores - scores.max())
+    probs /= probs.sum()
+    cutoff = min(len(order), int(np.searchsorted(np.cumsum(probs), top_p)) + 1)
+    order, probs = order[:cutoff], probs[:cutoff]
+    return int(rng.choice(order, p=probs / probs.sum()))
