@@ -342,6 +342,7 @@ int sync_and_check(mr_model *m, const char *what) {
     if (error) {
         m->failed = true;
         if (error == 3) return set_error(MR_ERR_STATE, "%s: context_length exceeded on the device", what);
+        if (error == 4) return set_error(MR_ERR_STATE, "%s: a token outside the vocabulary reached the device", what);
         return set_error(MR_ERR_TIMEOUT, "%s: device wait timed out (code %d); call reset()", what, error);
     }
     return MR_OK;
@@ -392,6 +393,7 @@ StepControl base_control(mr_model *m) {
     ctl.logits_rows = m->logits_rows;
     ctl.eos = -1;
     ctl.context_length = m->cfg.context_length;
+    ctl.vocab_size = m->cfg.vocab_size;
     return ctl;
 }
 

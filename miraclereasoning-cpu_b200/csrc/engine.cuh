@@ -105,7 +105,7 @@ struct StepState {
     int stopped;                      // generation finished: further launches do nothing
     int nonfinite;                    // a non-finite logit was produced
     int last_argmax;
-    int error;                        // nonzero: a bounded wait gave up (1000 + phase), 3 = context full
+    int error;                        // nonzero: 1000 + phase = a bounded wait gave up, 3 = context full, 4 = bad token
 };
 
 // Per-launch control, passed by value.
@@ -117,6 +117,7 @@ struct StepControl {
     int gen_max, eos;                 // device greedy generation (gen_max 0 = off)
     int *gen_out;
     int context_length;
+    int vocab_size;                   // tokens outside [0, vocab) stop the step with error 4
 };
 
 }  // namespace mr

@@ -556,6 +556,10 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
             if (blockIdx.x == 0) atomicCAS(&st->error, 0, 3);
             skip = 1;
         }
+        if (!skip && (info.token < 0 || info.token >= ctl.vocab_size)) {
+            if (blockIdx.x == 0) atomicCAS(&st->error, 0, 4);
+            skip = 1;
+        }
     }
     __syncthreads();
     if (skip) return;
