@@ -163,7 +163,7 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
                 "reasons": reasons, "samples": len(rows)}
@@ -293,6 +293,46 @@ def run_profile_case(args):
     return 0
 
 
+def run_trace(args, steps=8):
+    """Per-phase timing of decode steps from the kernel's globaltimer stamps."""
+    import ctypes as C
+    syn = _pkg("synthetic")
+    native = _pkg("_native")
+    config = syn.config_for(args.config)
+    context, prompt_len, _ = syn.WORKLOADS[args.config]
+    backend = _pkg("backend").CUDABackend(device_index=int(os.environ.get("LOCAL_RANK", "0")))
+    model = _pkg("model").MiracleModel.synthetic(config, stored=syn.STORED_DTYPE[args.config], backend=backend,
+                                                 context_length=context)
+    token = int(np.argmax(model.prefill(syn.prompt_ids(config.vocab_size, prompt_len, seed=1))))
+    kinds = ["qkv", "attn", "o", "gate_up", "down"] * config.layers + ["head"]
+    capacity = 1 + len(kinds) * 200
+    stamps = (C.c_uint64 * capacity)()
+    phases, grid = C.c_int(), C.c_int()
+    per_kind = {}
+    totals = []
+    for _ in range(steps):
+        native.call("mr_model_trace_decode", model._handle, token, stamps, capacity, C.byref(phases), C.byref(grid))
+        g = grid.value
+        t = np.frombuffer(stamps, dtype=np.uint64, count=1 + phases.value * (g + 1)).astype(np.int64)
+        start = t[0]
+        for k in range(phases.value):
+            row = t[1 + k * (g + 1): 1 + (k + 1) * (g + 1)]
+            done, exit_ = row[:g], row[g]
+            entry = per_kind.setdefault(kinds[k], {"compute_max": [], "compute_median": [], "barrier": []})
+            entry["compute_max"].append(done.max() - start)
+            entry["compute_median"].append(np.median(done) - start)
+            entry["barrier"].append(exit_ - done.max())
+            start = exit_
+        totals.append(start - t[0])
+    report = {"config": args.config, "position": model.position, "steps": steps,
+              "step_us": round(float(np.median(totals)) / 1e3, 2), "phases": {}}
+    for kind, entry in per_kind.items():
+        report["phases"][kind] = {k: round(float(np.median(v)) / 1e3, 3) for k, v in entry.items()}
+        report["phases"][kind]["count_per_step"] = len(entry["barrier"]) // steps
+    print(json.dumps(report, indent=1))
+    return 0
+
+
 def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
@@ -302,6 +342,8 @@ def main(argv=None):
     parser.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     parser.add_argument("--cpu-tokens", type=int, default=12, help="decode tokens of the CPU baseline sample")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--trace", action="store_true",
+                        help="print per-phase device timings of decode steps (phase tracing) and exit")
     parser.add_argument("--profile-steps", type=int, default=0,
                         help="profiling workload for ncu: build the model, prefill the prompt, run this many "
                              "decode steps, print no measurement")
@@ -334,6 +376,8 @@ def main(argv=None):
 
     if args.profile_steps:
         return run_profile_case(args)
+    if args.trace:
+        return run_trace(args)
     ranks = Ranks(args.gpus)
     result, config, context, prompt = run_cuda(args, ranks)
     if ranks.rank == 0 and not args.no_cpu_baseline:

@@ -226,6 +226,15 @@ MR_API int mr_model_last_experts(const mr_model *model, int layer, int loop, int
  * stream.  No reference counterpart. */
 MR_API int mr_model_bench_decode(mr_model *model, int first_token, int steps, float *device_ms);
 
+/* Tracing: run one decode step (feeding `token`) with per-phase device
+ * timestamps (globaltimer, ns).  Layout: stamps[0] = launch start; for the
+ * k-th executed phase, stamps[1 + k*(grid+1) + b] = CTA b finished computing
+ * and stamps[1 + k*(grid+1) + grid] = CTA 0 left the phase's grid barrier.
+ * *phases receives the number of executed phases, *grid the CTA count.  No
+ * reference counterpart (the reference has no tracing). */
+MR_API int mr_model_trace_decode(mr_model *model, int token, uint64_t *stamps, int capacity, int *phases,
+                                 int *grid);
+
 #ifdef __cplusplus
 }
 #endif

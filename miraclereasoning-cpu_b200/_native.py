@@ -93,6 +93,7 @@ SIGNATURES = {
     "mr_model_last_topk": (_I, [_P, _I, _I, _IP, _I]),
     "mr_model_last_experts": (_I, [_P, _I, _I, _IP, _FP, _I]),
     "mr_model_bench_decode": (_I, [_P, _I, _I, _FP]),
+    "mr_model_trace_decode": (_I, [_P, _I, C.POINTER(C.c_uint64), _I, _IP, _IP]),
 }
 
 _lib = None

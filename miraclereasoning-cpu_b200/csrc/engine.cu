@@ -714,6 +714,38 @@ int mr_model_last_experts(const mr_model *m, int layer, int loop, int *experts, 
     return set_error(MR_ERR_ARGUMENT, "model has no experts");
 }
 
+int mr_model_trace_decode(mr_model *m, int token, uint64_t *stamps, int capacity, int *phases, int *grid) {
+    int rc = ready(m);
+    if (rc) return rc;
+    MR_REQUIRE(stamps && phases && grid, "NULL argument");
+    MR_REQUIRE(token >= 0 && token < m->cfg.vocab_size, "token outside the vocabulary");
+    MR_REQUIRE(m->position + 1 <= m->cfg.context_length, "context_length exceeded");
+    const int executed = (int)m->phases.size() - 1;  // every phase but the step end
+    const size_t need = 1 + (size_t)executed * (m->grid + 1);
+    MR_REQUIRE((size_t)capacity >= need, "trace needs %zu stamps", need);
+    rc = ensure_feed(m, 1);
+    if (rc) return rc;
+    unsigned long long *d_trace = nullptr;
+    MR_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void **>(&d_trace), need * sizeof(unsigned long long),
+                                m->ctx->stream));
+    MR_CUDA_TRY(cudaMemcpyAsync(m->feed, &token, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
+    StepControl ctl = base_control(m);
+    ctl.feed_len = 1;
+    ctl.trace = d_trace;
+    rc = launch_step(m, ctl);
+    if (!rc) rc = sync_and_check(m, "trace");
+    if (!rc) {
+        cudaError_t err = cudaMemcpy(stamps, d_trace, need * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+        if (err != cudaSuccess) rc = cuda_error(err, "trace copy");
+    }
+    cudaFreeAsync(d_trace, m->ctx->stream);
+    if (rc) return rc;
+    m->position += 1;
+    *phases = executed;
+    *grid = m->grid;
+    return MR_OK;
+}
+
 int mr_model_bench_decode(mr_model *m, int first_token, int steps, float *device_ms) {
     int rc = ready(m);
     if (rc) return rc;

@@ -21,6 +21,7 @@ constexpr int kEngineWarps = kEngineThreads / 32;
 constexpr int kMaxSegments = 3;
 constexpr int kMaxInput = 16384;     // floats of one GEMV input vector held in shared memory
 constexpr int kRowBatch = 256;       // local rows per GEMV epilogue batch
+constexpr int kMergeSlots = 2048;    // (query head, chunk) softmax weights staged for a merge
 
 enum PhaseKind : int {
     PH_GEMV = 1,        // y = W x for up to 3 weight segments, then an epilogue
@@ -118,6 +119,10 @@ struct StepControl {
     int *gen_out;
     int context_length;
     int vocab_size;                   // tokens outside [0, vocab) stop the step with error 4
+    // Optional phase trace (globaltimer ns): [0] = launch start (CTA 0); then per
+    // executed phase k, slots 1 + k*(grid+1) + b = CTA b done computing, and
+    // slot 1 + k*(grid+1) + grid = CTA 0 leaving the barrier.  NULL = off.
+    unsigned long long *trace;
 };
 
 }  // namespace mr

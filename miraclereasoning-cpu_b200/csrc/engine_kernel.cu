@@ -29,6 +29,7 @@ struct Shared {
     float partial[kEngineWarps * kEngineWarps];
     float y[kMaxSegments][kRowBatch];
     float red[kEngineWarps];
+    float merge_w[kMergeSlots];
     unsigned long long best[kEngineWarps];
     int flag;
     int ok;
@@ -382,7 +383,8 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, Shared 
     const int extra = a.relay_count ? __ldcg(a.relay_count) : 0;
     const int total = length + extra;
     int chunks = max(1, min(a.max_chunks, G / a.kv_heads));
-    chunks = min(chunks, max(1, (total + 15) / 16));
+    chunks = min(chunks, max(1, (total + kKeyTile - 1) / kKeyTile));
+    chunks = min(chunks, kMergeSlots / gq);
     const int chunk_len = (total + chunks - 1) / chunks;
     chunks = (total + chunk_len - 1) / chunk_len;
     const float pos_f = static_cast<float>(info.position);
@@ -514,19 +516,39 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, Shared 
         }
         __syncthreads();
         if (sm.flag) {
-            for (int e = threadIdx.x; e < gq * d; e += blockDim.x) {
-                const int i = e / d, j = e % d;
+            // one warp per query head: all chunk maxima / sums loaded in parallel,
+            // softmax-merge weights staged in shared memory
+            for (int i = warp; i < gq; i += kEngineWarps) {
                 const float *base = a.partial + static_cast<size_t>(g * gq + i) * a.max_chunks * stride;
                 float m = -INFINITY;
-                for (int cc = 0; cc < chunks; ++cc) m = fmaxf(m, __ldcg(base + cc * stride + d));
-                float num = 0.f, den = 0.f;
-                for (int cc = 0; cc < chunks; ++cc) {
+                for (int cc = lane; cc < chunks; cc += 32) m = fmaxf(m, __ldcg(base + cc * stride + d));
+                m = warp_max(m);
+                float den = 0.f;
+                for (int cc = lane; cc < chunks; cc += 32) {
                     const float mc = __ldcg(base + cc * stride + d);
                     const float w = (mc == -INFINITY) ? 0.f : expf(mc - m);
-                    num = fmaf(w, __ldcg(base + cc * stride + j), num);
+                    sm.merge_w[i * chunks + cc] = w;
                     den = fmaf(w, __ldcg(base + cc * stride + d + 1), den);
                 }
-                a.out[static_cast<size_t>(g * gq + i) * d + j] = num / den;
+                den = warp_sum(den);
+                __syncwarp();
+                for (int cc = lane; cc < chunks; cc += 32) sm.merge_w[i * chunks + cc] /= den;
+            }
+            __syncthreads();
+            for (int e = threadIdx.x; e < gq * d; e += blockDim.x) {
+                const int i = e / d, j = e % d;
+                const float *base = a.partial + static_cast<size_t>(g * gq + i) * a.max_chunks * stride + j;
+                const float *w = sm.merge_w + i * chunks;
+                float num0 = 0.f, num1 = 0.f, num2 = 0.f, num3 = 0.f;
+                int cc = 0;
+                for (; cc + 3 < chunks; cc += 4) {
+                    num0 = fmaf(w[cc], __ldcg(base + cc * stride), num0);
+                    num1 = fmaf(w[cc + 1], __ldcg(base + (cc + 1) * stride), num1);
+                    num2 = fmaf(w[cc + 2], __ldcg(base + (cc + 2) * stride), num2);
+                    num3 = fmaf(w[cc + 3], __ldcg(base + (cc + 3) * stride), num3);
+                }
+                for (; cc < chunks; ++cc) num0 = fmaf(w[cc], __ldcg(base + cc * stride), num0);
+                a.out[static_cast<size_t>(g * gq + i) * d + j] = (num0 + num1) + (num2 + num3);
             }
         }
         __syncthreads();
@@ -563,6 +585,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
     }
     __syncthreads();
     if (skip) return;
+    if (ctl.trace && blockIdx.x == 0 && threadIdx.x == 0) ctl.trace[0] = global_ns();
     int barriers = 0;
     // warm the first weight-streaming phase
     for (int p = 0; p < nphases; ++p)
@@ -583,8 +606,14 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
         }
         if (ph.kind == PH_GEMV) gemv_phase(ph.gemv, st, info, sm);
         else if (ph.kind == PH_ATTN_GQA) attn_gqa_phase(ph.attn, info, sm);
+        unsigned long long *stamp = ctl.trace ? ctl.trace + 1 + static_cast<size_t>(barriers) * (gridDim.x + 1) : nullptr;
+        if (stamp) {
+            __syncthreads();
+            if (threadIdx.x == 0) stamp[blockIdx.x] = global_ns();
+        }
         ++barriers;
         if (!grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, p, sm)) return;
+        if (stamp && blockIdx.x == 0 && threadIdx.x == 0) stamp[gridDim.x] = global_ns();
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         volatile StepState *s = st;
