@@ -235,6 +235,25 @@ MR_API int mr_model_bench_decode(mr_model *model, int first_token, int steps, fl
 MR_API int mr_model_trace_decode(mr_model *model, int token, uint64_t *stamps, int capacity, int *phases,
                                  int *grid);
 
+/* Attention that allocates nothing on the device.  No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc while they run
+ * (a framework that owns all device memory through its own pool, or code in a
+ * section where an allocation could synchronise the device or fail).  Same
+ * result as CUDABackend.attention / mr_op_scores + mr_op_softmax + mr_op_mix
+ * (opencl.py:432-448), but the [heads x (length + extra_length)] score matrix
+ * lives in a 4 MiB file-scope device array that every GPU loading this library
+ * keeps until the process exits.  All pointers are device pointers the caller
+ * owns; keys/values are ring buffers [capacity, kv_heads*dim] read in logical
+ * order [start, start+length), then extra rows [extra_length, kv_heads*dim].
+ * heads * (length + extra_length) above 1048576 fails with MR_ERR_ARGUMENT.
+ * The first call on a device looks up the array's address (do it before any
+ * stream capture); every call shares the array, so calls that overlap on the
+ * GPU race and must be serialised by the caller.  Runs on ctx's stream. */
+MR_API int mr_attention_static_scratch(mr_context *ctx, const float *q, const float *keys, const float *values,
+                                       const float *extra_keys, const float *extra_values, float *out, int heads,
+                                       int kv_heads, int dim, int capacity, int start, int length,
+                                       int extra_length);
+
 #ifdef __cplusplus
 }
 #endif
