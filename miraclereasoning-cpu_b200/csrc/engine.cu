@@ -19,7 +19,7 @@
 namespace mr {
 
 __global__ void decode_step_kernel(const Phase *__restrict__ phases, int nphases, StepState *st, StepControl ctl);
-size_t decode_step_smem_bytes();
+size_t decode_control_bytes();
 
 namespace {
 
@@ -102,8 +102,8 @@ struct mr_model {
     float *logits = nullptr;
     int logits_rows = 0;
     float *partial = nullptr;
-    unsigned int *arrivals = nullptr;
-    int max_chunks = 0;
+    int scratch_floats = 0, ring_bytes = 0;
+    size_t smem_bytes = 0;
     std::vector<float *> k_cache, v_cache;
     std::vector<int> cache_capacity;
     StepState *state = nullptr;
@@ -292,12 +292,16 @@ int build_plan(mr_model *m) {
         a.v_cache = m->v_cache[l];
         a.capacity = m->cache_capacity[l];
         a.partial = m->partial;
-        a.arrivals = m->arrivals;
-        a.max_chunks = m->max_chunks;
-        a.out = m->attn;
         m->phases.push_back(at);
-        // 3. o projection + residual (model.py:282)
-        Phase o = gemv_phase(l, m->attn, nullptr, 0.f);
+        // 3. merge the attention chunks, o projection + residual (model.py:282)
+        Phase o = gemv_phase(l, nullptr, nullptr, 0.f);
+        o.gemv.input_kind = IN_ATTN_MERGE;
+        o.gemv.merge.partial = m->partial;
+        o.gemv.merge.heads = c.query_heads;
+        o.gemv.merge.kv_heads = m->layer_kvh[l];
+        o.gemv.merge.dim = c.head_dim;
+        o.gemv.merge.capacity = m->cache_capacity[l];
+        o.gemv.merge.relay_count = nullptr;
         o.gemv.nseg = 1;
         o.gemv.seg[0] = segment(tensor(m, p + "o"));
         o.gemv.epilogue = EPI_RESIDUAL;
@@ -332,6 +336,23 @@ int build_plan(mr_model *m) {
     end.kind = PH_STEP_END;
     end.layer = -2;
     m->phases.push_back(end);
+    // Weight streaming through the shared-memory ring: pieces of at most a
+    // quarter of the ring, whole 16-byte rows (cp.async.bulk granularity).
+    const int piece_cap = m->ring_bytes / 4;
+    for (Phase &ph : m->phases) {
+        if (ph.kind != PH_GEMV) continue;
+        GemvPhase &g = ph.gemv;
+        bool bulk = true;
+        for (int i = 0; i < g.nseg; ++i) {
+            const int row_bytes = g.seg[i].cols * (int)dtype_size(g.seg[i].dtype);
+            if (row_bytes % 16 || row_bytes > piece_cap) bulk = false;
+            else g.seg[i].rows_per_piece = std::max(1, std::min(kRowBatch, piece_cap / row_bytes));
+        }
+        if (g.epilogue == EPI_SWIGLU && g.seg[0].rows_per_piece != g.seg[1].rows_per_piece) bulk = false;
+        g.bulk = bulk;
+        const int gain_bytes = (g.seg[0].cols * (int)dtype_size(g.norm_gain_dtype) + 15) & ~15;
+        g.gain_piece = bulk && g.norm && g.norm_gain && gain_bytes <= piece_cap;
+    }
     return MR_OK;
 }
 
@@ -375,7 +396,7 @@ int launch_step(mr_model *m, const StepControl &ctl) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(m->grid);
     cfg.blockDim = dim3(kEngineThreads);
-    cfg.dynamicSmemBytes = decode_step_smem_bytes();
+    cfg.dynamicSmemBytes = m->smem_bytes;
     cfg.stream = m->ctx->stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
@@ -394,6 +415,8 @@ StepControl base_control(mr_model *m) {
     ctl.eos = -1;
     ctl.context_length = m->cfg.context_length;
     ctl.vocab_size = m->cfg.vocab_size;
+    ctl.scratch_floats = m->scratch_floats;
+    ctl.ring_bytes = m->ring_bytes;
     return ctl;
 }
 
@@ -527,18 +550,23 @@ int mr_model_finalize(mr_model *m) {
             return set_error(MR_ERR_ARGUMENT, "Missing tensor %s", kv.first.c_str());
     if (!is_gqa_family(m->cfg.family))
         return set_error(MR_ERR_ARGUMENT, "family %d is not supported by this engine build yet", m->cfg.family);
-    for (auto &kv : m->tensors)
-        if (kv.second.shape.size() == 2 && kv.second.shape[1] > kMaxInput)
-            return set_error(MR_ERR_ARGUMENT, "%s: input width %lld above the engine limit %d", kv.first.c_str(),
-                             (long long)kv.second.shape[1], kMaxInput);
     const mr_model_config &c = m->cfg;
     int rc = MR_OK;
     const int H = c.query_heads, d = c.head_dim;
+    MR_REQUIRE(H <= 64, "query_heads %d above the engine limit 64", H);
     const int max_kvh = *std::max_element(m->layer_kvh.begin(), m->layer_kvh.end());
     const int gq_max = H / *std::min_element(m->layer_kvh.begin(), m->layer_kvh.end());
-    // attention scratch must fit the shared input area (see attn_gqa_phase)
-    const int attn_floats = 2 * gq_max * d + 32 * (d + 1) + 32 * d + gq_max * 32 + 3 * gq_max + d;
-    MR_REQUIRE(attn_floats <= kMaxInput, "attention group too large for shared memory");
+    // shared memory: control block, scratch (GEMV input vector / attention tiles), weight ring
+    int max_cols = 0;
+    for (auto &kv : m->tensors)
+        if (kv.second.shape.size() == 2) max_cols = std::max(max_cols, (int)kv.second.shape[1]);
+    m->scratch_floats = std::max(max_cols, attn_scratch_floats(gq_max, d));
+    const size_t control = decode_control_bytes();
+    const size_t scratch = ((size_t)m->scratch_floats * 4 + 127) & ~size_t(127);
+    const long long ring = (long long)kSmemLimit - 1024 - (long long)control - (long long)scratch;
+    MR_REQUIRE(ring >= 16 * 1024, "model too wide for the decode kernel's shared memory (input width %d)", max_cols);
+    m->ring_bytes = (int)(ring & ~127ll);
+    m->smem_bytes = control + scratch + (size_t)m->ring_bytes;
     auto falloc = [&](size_t n) { return static_cast<float *>(device_alloc(m, n * sizeof(float), &rc)); };
     m->d_inv_freq = falloc(d / 2);
     m->x = falloc(c.hidden_size);
@@ -549,9 +577,7 @@ int mr_model_finalize(mr_model *m) {
     m->ffn = falloc(c.ffn_dim);
     m->logits_rows = 64;
     m->logits = falloc((size_t)m->logits_rows * c.vocab_size);
-    m->max_chunks = m->grid;
-    m->partial = falloc((size_t)H * m->max_chunks * (d + 2));
-    m->arrivals = static_cast<unsigned int *>(device_alloc(m, sizeof(unsigned) * max_kvh, &rc));
+    m->partial = falloc((size_t)H * kMaxAttnChunks * (d + 2));
     m->state = static_cast<StepState *>(device_alloc(m, sizeof(StepState), &rc));
     if (rc) return rc;
     m->k_cache.resize(c.layers);
@@ -568,17 +594,16 @@ int mr_model_finalize(mr_model *m) {
         if (rc) return rc;
     }
     MR_CUDA_TRY(cudaMemcpy(m->d_inv_freq, m->inv_freq.data(), sizeof(float) * (d / 2), cudaMemcpyHostToDevice));
-    MR_CUDA_TRY(cudaMemset(m->arrivals, 0, sizeof(unsigned) * max_kvh));
     rc = build_plan(m);
     if (rc) return rc;
     m->d_phases = static_cast<Phase *>(device_alloc(m, sizeof(Phase) * m->phases.size(), &rc));
     if (rc) return rc;
     MR_CUDA_TRY(cudaMemcpy(m->d_phases, m->phases.data(), sizeof(Phase) * m->phases.size(), cudaMemcpyHostToDevice));
     MR_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void *>(decode_step_kernel),
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_step_smem_bytes()));
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem_bytes));
     int per_sm = 0;
     MR_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reinterpret_cast<const void *>(decode_step_kernel),
-                                                              kEngineThreads, decode_step_smem_bytes()));
+                                                              kEngineThreads, m->smem_bytes));
     MR_REQUIRE(per_sm >= 1, "decode kernel cannot be resident (occupancy 0)");
     MR_CUDA_TRY(cudaEventCreate(&m->ev0));
     MR_CUDA_TRY(cudaEventCreate(&m->ev1));

@@ -7,9 +7,17 @@
 // previous phase (a GEMV needs the whole input vector; attention needs all of
 // this token's q/k/v).  The decode kernel is launched cooperatively with one
 // CTA per SM and runs every phase of a step, separated by grid-wide barriers;
-// inside a phase each CTA takes its share of the work.  Before a phase starts
-// computing, its CTA issues L2 bulk prefetches for its share of the NEXT
-// weight-streaming phase, so HBM keeps streaming through the barriers.
+// inside a phase each CTA takes its share of the work.
+//
+// Weight streaming: every CTA owns a fixed row range of each weight segment.
+// Thread 0 of each CTA walks the CTA's slices of all weight-streaming phases
+// of the step, in order, as "pieces" (whole rows of one segment, or a norm
+// gain vector) and copies them with TMA bulk copies (cp.async.bulk + one
+// mbarrier per piece) into a shared-memory byte ring, as far ahead as the ring
+// has room -- across phase boundaries and grid barriers.  The compute of a
+// phase then reads its weights from shared memory, so the only global round
+// trips left on the critical path are the phase's input vector and the
+// barrier.
 #pragma once
 
 #include "common.cuh"
@@ -19,9 +27,12 @@ namespace mr {
 constexpr int kEngineThreads = 512;  // 16 warps per CTA, one CTA per SM
 constexpr int kEngineWarps = kEngineThreads / 32;
 constexpr int kMaxSegments = 3;
-constexpr int kMaxInput = 16384;     // floats of one GEMV input vector held in shared memory
-constexpr int kRowBatch = 256;       // local rows per GEMV epilogue batch
-constexpr int kMergeSlots = 2048;    // (query head, chunk) softmax weights staged for a merge
+constexpr int kRowBatch = 256;       // rows of one piece (and of one direct-load batch)
+constexpr int kQueue = 32;           // pieces in flight per CTA (one mbarrier each)
+constexpr int kMaxAttnChunks = 16;   // key chunks per KV head (merged by the consumer)
+constexpr int kKeysPerChunk = 64;    // target keys per attention work unit
+constexpr int kKeyTile = 32;         // keys per attention tile
+constexpr int kSmemLimit = 227 * 1024;
 
 enum PhaseKind : int {
     PH_GEMV = 1,        // y = W x for up to 3 weight segments, then an epilogue
@@ -39,13 +50,23 @@ enum Epilogue : int {
 enum InputKind : int {
     IN_VECTOR = 0,      // a float vector in global memory
     IN_EMBED_ROW = 1,   // row `token` of the embedding, widened
+    IN_ATTN_MERGE = 2,  // softmax-merge of the attention chunk partials
 };
 
 struct Segment {
     const void *w;      // [rows, cols] row-major, stored dtype
     int dtype;
     int rows, cols;
+    int rows_per_piece; // rows per bulk piece (bulk phases)
     float *out;         // EPI_STORE destination (rows floats)
+};
+
+// Chunk partials written by an attention phase, merged by the next GEMV phase.
+struct AttnMerge {
+    const float *partial;           // [heads][kMaxAttnChunks][dim + 2]: acc[dim], max, sum
+    int heads, kv_heads, dim;
+    int capacity;                   // of the layer's ring, to recompute the chunk count
+    const int *relay_count;
 };
 
 struct GemvPhase {
@@ -54,12 +75,15 @@ struct GemvPhase {
     const void *embed;          // IN_EMBED_ROW source [vocab, cols]
     int embed_dtype;
     float *embed_copy;          // when set, CTA 0 also stores the widened row here
+    AttnMerge merge;            // IN_ATTN_MERGE source
     int norm;                   // apply RMSNorm to the input
     const void *norm_gain;      // NULL -> non-affine
     int norm_gain_dtype;
     float norm_eps;
+    int gain_piece;             // the gain vector travels through the ring as the phase's first piece
     int nseg;
     Segment seg[kMaxSegments];
+    int bulk;                   // weights stream through the shared-memory ring
     int epilogue;
     float scale;                // EPI_RESIDUAL scale
     float *x;                   // EPI_RESIDUAL vector
@@ -80,10 +104,7 @@ struct AttnPhase {
     const float *relay_k, *relay_v; // [kv_heads][relay_capacity][dim] (flashnano-1.6) or NULL
     const int *relay_count;
     int relay_capacity;
-    float *partial;                 // [heads][max_chunks][dim + 2]
-    unsigned int *arrivals;         // [kv_heads]
-    int max_chunks;
-    float *out;                     // [heads * dim]
+    float *partial;                 // [heads][kMaxAttnChunks][dim + 2]
 };
 
 struct Phase {
@@ -92,6 +113,22 @@ struct Phase {
     GemvPhase gemv;
     AttnPhase attn;
 };
+
+// Attention work split: chunks of keys per KV head (same formula in the
+// attention phase and in the merge that consumes its partials).
+__host__ __device__ inline int attn_chunks(int total_keys, int kv_heads, int grid) {
+    int chunks = grid / kv_heads;
+    const int by_keys = (total_keys + kKeysPerChunk - 1) / kKeysPerChunk;
+    if (by_keys < chunks) chunks = by_keys;
+    if (kMaxAttnChunks < chunks) chunks = kMaxAttnChunks;
+    return chunks < 1 ? 1 : chunks;
+}
+
+// Shared-memory scratch (floats) the attention phase needs for one KV group.
+__host__ __device__ inline int attn_scratch_floats(int group_heads, int dim) {
+    return 2 * group_heads * dim + kKeyTile * (dim + 1) + kKeyTile * dim + group_heads * kKeyTile +
+           3 * group_heads + dim;
+}
 
 // Device-resident state of the running sequence, advanced by the decode
 // kernel itself (CTA 0, after the step's final barrier) so that steps can be
@@ -106,7 +143,7 @@ struct StepState {
     int stopped;                      // generation finished: further launches do nothing
     int nonfinite;                    // a non-finite logit was produced
     int last_argmax;
-    int error;                        // nonzero: 1000 + phase = a bounded wait gave up, 3 = context full, 4 = bad token
+    int error;                        // 1000 + phase: a bounded wait gave up; 3: context full; 4: bad token
 };
 
 // Per-launch control, passed by value.
@@ -119,6 +156,8 @@ struct StepControl {
     int *gen_out;
     int context_length;
     int vocab_size;                   // tokens outside [0, vocab) stop the step with error 4
+    int scratch_floats;               // shared-memory scratch (input vector / attention tiles)
+    int ring_bytes;                   // shared-memory weight ring
     // Optional phase trace (globaltimer ns): [0] = launch start (CTA 0); then per
     // executed phase k, slots 1 + k*(grid+1) + b = CTA b done computing, and
     // slot 1 + k*(grid+1) + grid = CTA 0 leaving the barrier.  NULL = off.

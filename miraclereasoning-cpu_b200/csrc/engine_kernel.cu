@@ -7,7 +7,16 @@
 //   ATTN_GQA  model._gqa (model.py:95-116): per-head Q/K RMSNorm, RoPE
 //             (kernels.cl:30-44), ring append (model.py:21-25), scores /
 //             softmax / mix over the ring in logical order plus relay rows
-//             (kernels.cl:58-107)
+//             (kernels.cl:58-107), split over key chunks; the chunks are
+//             merged (softmax-rescaled) by the next GEMV phase as it loads
+//             its input.
+//
+// Weight streaming (see engine.cuh): thread 0 is the producer of a
+// shared-memory byte ring fed by TMA bulk copies (cp.async.bulk, completion
+// on one mbarrier per piece); every thread consumes pieces in the same order.
+// All waits are bounded (2 s): a wait that gives up records an error code in
+// StepState, every CTA drains its in-flight copies (bounded) and returns, and
+// the host raises.
 //
 // Numerics: weights are widened from their stored dtype exactly as the
 // reference widens them; all arithmetic is float32.  Dot products and the
@@ -21,22 +30,32 @@ namespace mr {
 namespace {
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
-constexpr int kKeyTile = 32;
-constexpr size_t kPrefetchCap = 512 * 1024;  // bytes of next-phase weights per CTA
+constexpr int kMaxMergeHeads = 64;
 
-struct Shared {
-    float in[kMaxInput];
+// Fixed part of the dynamic shared memory; the scratch floats and the weight
+// ring follow it.
+struct Control {
+    unsigned long long mbar[kQueue];
+    int offset[kQueue];
     float partial[kEngineWarps * kEngineWarps];
-    float y[kMaxSegments][kRowBatch];
+    float y[2][kRowBatch];   // y[0]: rows of the current piece; y[1]: gate rows (SwiGLU)
     float red[kEngineWarps];
-    float merge_w[kMergeSlots];
+    float merge_w[kMaxMergeHeads * kMaxAttnChunks];
     unsigned long long best[kEngineWarps];
-    int flag;
-    int ok;
+    int flag, ok;
+    // producer state (written by thread 0 only)
+    int issued, consumed, head_offset, cur_phase, cur_piece;
 };
 
 struct StepInfo {
     int position, token, logits_row;
+};
+
+struct Smem {
+    Control *c;
+    float *scratch;
+    unsigned char *ring;
+    int ring_bytes;
 };
 
 __device__ __forceinline__ void row_range(int rows, int b, int g, int &r0, int &r1) {
@@ -45,17 +64,179 @@ __device__ __forceinline__ void row_range(int rows, int b, int g, int &r0, int &
 }
 
 __device__ __forceinline__ int esize(int dtype) { return dtype == MR_DTYPE_F32 ? 4 : 2; }
+__device__ __forceinline__ int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier / bulk copy primitives --------------------------------------------------
+__device__ __forceinline__ void mbar_init(unsigned long long *bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, int parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, unsigned long long *bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// ---- piece schedule (identical in producer and consumers) ----------------------------
+struct Piece {
+    int seg;     // -1: the norm gain vector
+    int row0, nrows;
+};
+
+__device__ int phase_pieces(const GemvPhase &g, int b, int G) {
+    if (!g.bulk) return 0;
+    int n = g.gain_piece ? 1 : 0;
+    if (g.epilogue == EPI_SWIGLU) {
+        int r0, r1;
+        row_range(g.seg[0].rows, b, G, r0, r1);
+        return n + 2 * ceil_div(r1 - r0, g.seg[0].rows_per_piece);
+    }
+    for (int s = 0; s < g.nseg; ++s) {
+        int r0, r1;
+        row_range(g.seg[s].rows, b, G, r0, r1);
+        n += ceil_div(r1 - r0, g.seg[s].rows_per_piece);
+    }
+    return n;
+}
+
+__device__ Piece phase_piece(const GemvPhase &g, int b, int G, int k) {
+    if (g.gain_piece) {
+        if (k == 0) return {-1, 0, 0};
+        --k;
+    }
+    if (g.epilogue == EPI_SWIGLU) {
+        int r0, r1;
+        row_range(g.seg[0].rows, b, G, r0, r1);
+        const int rpp = g.seg[0].rows_per_piece, row0 = r0 + (k >> 1) * rpp;
+        return {k & 1, row0, min(rpp, r1 - row0)};
+    }
+    for (int s = 0; s < g.nseg; ++s) {
+        int r0, r1;
+        row_range(g.seg[s].rows, b, G, r0, r1);
+        const int rpp = g.seg[s].rows_per_piece, np = ceil_div(r1 - r0, rpp);
+        if (k < np) {
+            const int row0 = r0 + k * rpp;
+            return {s, row0, min(rpp, r1 - row0)};
+        }
+        k -= np;
+    }
+    return {0, 0, 0};
+}
+
+__device__ uint32_t piece_bytes(const GemvPhase &g, const Piece &p) {
+    if (p.seg < 0) return static_cast<uint32_t>((g.seg[0].cols * esize(g.norm_gain_dtype) + 15) & ~15);
+    const Segment &s = g.seg[p.seg];
+    return static_cast<uint32_t>(p.nrows) * s.cols * esize(s.dtype);
+}
+
+__device__ const void *piece_src(const GemvPhase &g, const Piece &p) {
+    if (p.seg < 0) return g.norm_gain;
+    const Segment &s = g.seg[p.seg];
+    return static_cast<const char *>(s.w) + static_cast<size_t>(p.row0) * s.cols * esize(s.dtype);
+}
+
+// Producer (thread 0): issue the next pieces of this step while the ring and
+// the mbarrier queue have room.
+__device__ void refill(const Phase *phases, int nphases, bool need_head, const Smem &sm) {
+    Control &c = *sm.c;
+    const int b = blockIdx.x, G = gridDim.x;
+    bool fenced = false;
+    while (c.cur_phase < nphases) {
+        const Phase &ph = phases[c.cur_phase];
+        if (ph.kind != PH_GEMV || !ph.gemv.bulk || (ph.layer < 0 && !need_head) ||
+            c.cur_piece >= phase_pieces(ph.gemv, b, G)) {
+            ++c.cur_phase;
+            c.cur_piece = 0;
+            continue;
+        }
+        if (c.issued - c.consumed >= kQueue) return;
+        const Piece p = phase_piece(ph.gemv, b, G, c.cur_piece);
+        const int bytes = static_cast<int>(piece_bytes(ph.gemv, p));
+        int off;
+        if (c.issued == c.consumed) {
+            off = 0;
+        } else {
+            const int head = c.head_offset, tail = c.offset[c.consumed % kQueue];
+            if (head == tail) return;  // full
+            if (head > tail) {
+                if (head + bytes <= sm.ring_bytes) off = head;
+                else if (bytes <= tail) off = 0;
+                else return;
+            } else {
+                if (head + bytes <= tail) off = head;
+                else return;
+            }
+        }
+        if (!fenced) {
+            // the region may have been read through the generic proxy
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            fenced = true;
+        }
+        const int slot = c.issued % kQueue;
+        c.offset[slot] = off;
+        bulk_load(sm.ring + off, piece_src(ph.gemv, p), static_cast<uint32_t>(bytes), &c.mbar[slot]);
+        c.head_offset = off + bytes;
+        ++c.issued;
+        ++c.cur_piece;
+    }
+}
+
+// Bounded wait for piece `idx` (all threads).
+__device__ bool wait_piece(const Smem &sm, int idx, StepState *st, int phase) {
+    unsigned long long *bar = &sm.c->mbar[idx % kQueue];
+    const int parity = (idx / kQueue) & 1;
+    uint64_t start = 0;
+    for (unsigned spin = 0;; ++spin) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((spin & 255u) == 255u) {
+            if (*reinterpret_cast<volatile int *>(&st->error)) return false;
+            const uint64_t now = global_ns();
+            if (!start) {
+                start = now;
+            } else if (now - start > kWaitLimitNs) {
+                atomicCAS(&st->error, 0, 1000 + phase);
+                return false;
+            }
+        }
+    }
+}
+
+// Thread 0, on exit: wait (bounded) for every issued copy so that no bulk copy
+// writes into shared memory after the CTA has left.
+__device__ void drain(const Smem &sm) {
+    Control &c = *sm.c;
+    const uint64_t start = global_ns();
+    for (int idx = c.consumed; idx < c.issued; ++idx) {
+        while (!mbar_try_wait(&c.mbar[idx % kQueue], (idx / kQueue) & 1)) {
+            if (global_ns() - start > kWaitLimitNs) return;
+        }
+    }
+}
 
 // ---- grid barrier ------------------------------------------------------------------
-// Arrive, then wait (thread 0 of each CTA) until every CTA has arrived.  The
-// wait is bounded: after kWaitLimitNs it records 1000+phase in st->error and
-// every CTA returns, leaving the context usable.
-__device__ bool grid_barrier(StepState *st, unsigned long long target, int phase, Shared &sm) {
+// Release-add arrival (cumulative over the CTA's writes ordered by bar.sync),
+// acquire polling by thread 0, bounded by kWaitLimitNs.
+__device__ bool grid_barrier(StepState *st, unsigned long long target, int phase, const Smem &sm) {
     __syncthreads();
     if (threadIdx.x == 0) {
         int ok = 1;
-        __threadfence();
-        atomicAdd(&st->barrier, 1ull);
+        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(&st->barrier) : "memory");
         uint64_t start = 0;
         for (unsigned spin = 0;; ++spin) {
             if (ld_acquire_u64(&st->barrier) >= target) break;
@@ -74,33 +255,31 @@ __device__ bool grid_barrier(StepState *st, unsigned long long target, int phase
                 }
             }
         }
-        __threadfence();
-        sm.ok = ok;
+        sm.c->ok = ok;
     }
     __syncthreads();
-    return sm.ok != 0;
+    return sm.c->ok != 0;
 }
 
 // Deterministic block sum (same order in every CTA -> identical bits).
-__device__ float block_sum(float v, Shared &sm) {
+__device__ float block_sum(float v, Control &c) {
     v = warp_sum(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __syncthreads();
-    if (lane == 0) sm.red[warp] = v;
+    if (lane == 0) c.red[warp] = v;
     __syncthreads();
     if (warp == 0) {
-        float total = lane < kEngineWarps ? sm.red[lane] : 0.f;
+        float total = lane < kEngineWarps ? c.red[lane] : 0.f;
         total = warp_sum(total);
-        if (lane == 0) sm.red[0] = total;
+        if (lane == 0) c.red[0] = total;
     }
     __syncthreads();
-    const float total = sm.red[0];
+    const float total = c.red[0];
     __syncthreads();
     return total;
 }
 
-// ---- GEMV --------------------------------------------------------------------------
-// One 16-byte chunk of a weight row times the matching shared-memory inputs.
+// ---- dot products -------------------------------------------------------------------
 template <int DT>
 struct RowDot;
 
@@ -154,7 +333,7 @@ struct RowDot<MR_DTYPE_F32> {
     }
 };
 
-// Weights are read once per step: bypass L1 (they were prefetched into L2).
+// Weights read straight from global memory (non-bulk phases): bypass L1.
 __device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
     uint4 v;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -162,175 +341,276 @@ __device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
                  : "l"(p));
     return v;
 }
+__device__ __forceinline__ uint4 ld_smem(const uint4 *p) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(smem_addr(p)));
+    return v;
+}
 
-// Partial dot product of weight `row` with the input: 16-byte chunks
-// first, first+stride, ...; elements past the last whole chunk are taken by
-// lane `tail_lane` (-1: none).  Rows whose byte length is not a multiple of 16
-// (tiny shapes only) fall back to scalar loads by the tail lane's warp.
-template <int DT>
-__device__ float row_partial(const void *wbase, int cols, int row, int first, int stride, int tail_lane,
-                             const float *x) {
+// Partial dot product of one row (16-byte chunks first, first+stride, ...).
+// FROM_SMEM rows are in the weight ring (always whole 16-byte chunks); global
+// rows may have a scalar tail, taken by `tail_lane` (-1: none), and rows whose
+// byte length is not a multiple of 16 use scalar loads only.
+template <int DT, bool FROM_SMEM>
+__device__ float row_partial(const char *rp, int cols, int first, int stride, int tail_lane, const float *x) {
     using D = RowDot<DT>;
     const int nv = cols / D::VEC;
     const size_t row_bytes = static_cast<size_t>(cols) * esize(DT);
-    const char *rp = static_cast<const char *>(wbase) + static_cast<size_t>(row) * row_bytes;
     float acc = 0.f;
-    if ((row_bytes & 15) == 0) {
+    if (FROM_SMEM || (row_bytes & 15) == 0) {
         const uint4 *v = reinterpret_cast<const uint4 *>(rp);
         int c = first;
         for (; c + 3 * stride < nv; c += 4 * stride) {
-            const uint4 w0 = ld_stream(v + c), w1 = ld_stream(v + c + stride), w2 = ld_stream(v + c + 2 * stride),
-                        w3 = ld_stream(v + c + 3 * stride);
+            uint4 w0, w1, w2, w3;
+            if (FROM_SMEM) {
+                w0 = ld_smem(v + c), w1 = ld_smem(v + c + stride), w2 = ld_smem(v + c + 2 * stride),
+                w3 = ld_smem(v + c + 3 * stride);
+            } else {
+                w0 = ld_stream(v + c), w1 = ld_stream(v + c + stride), w2 = ld_stream(v + c + 2 * stride),
+                w3 = ld_stream(v + c + 3 * stride);
+            }
             acc += D::chunk(w0, x + c * D::VEC);
             acc += D::chunk(w1, x + (c + stride) * D::VEC);
             acc += D::chunk(w2, x + (c + 2 * stride) * D::VEC);
             acc += D::chunk(w3, x + (c + 3 * stride) * D::VEC);
         }
-        for (; c < nv; c += stride) acc += D::chunk(ld_stream(v + c), x + c * D::VEC);
-        if (tail_lane >= 0) {
+        for (; c < nv; c += stride) acc += D::chunk(FROM_SMEM ? ld_smem(v + c) : ld_stream(v + c), x + c * D::VEC);
+        if (!FROM_SMEM && tail_lane >= 0)
             for (int j = nv * D::VEC + tail_lane; j < cols; j += 32) acc = fmaf(load_weight(rp, DT, j), x[j], acc);
-        }
     } else if (tail_lane >= 0) {
         for (int j = tail_lane; j < cols; j += 32) acc = fmaf(load_weight(rp, DT, j), x[j], acc);
     }
     return acc;
 }
 
-__device__ float row_partial_any(const Segment &s, int row, int first, int stride, int tail_lane, const float *x) {
-    switch (s.dtype) {
-        case MR_DTYPE_BF16: return row_partial<MR_DTYPE_BF16>(s.w, s.cols, row, first, stride, tail_lane, x);
-        case MR_DTYPE_F16: return row_partial<MR_DTYPE_F16>(s.w, s.cols, row, first, stride, tail_lane, x);
-        default: return row_partial<MR_DTYPE_F32>(s.w, s.cols, row, first, stride, tail_lane, x);
+template <bool FROM_SMEM>
+__device__ float row_partial_any(int dtype, const char *rp, int cols, int first, int stride, int tail_lane,
+                                 const float *x) {
+    switch (dtype) {
+        case MR_DTYPE_BF16: return row_partial<MR_DTYPE_BF16, FROM_SMEM>(rp, cols, first, stride, tail_lane, x);
+        case MR_DTYPE_F16: return row_partial<MR_DTYPE_F16, FROM_SMEM>(rp, cols, first, stride, tail_lane, x);
+        default: return row_partial<MR_DTYPE_F32, FROM_SMEM>(rp, cols, first, stride, tail_lane, x);
     }
 }
 
-// y[i] = W[r0+i] . in for i < n (n <= kRowBatch), results in sm.y[slot].
-// Many rows: one warp per row.  Few rows: several warps split each row.
-__device__ void gemv_rows(const Segment &s, int r0, int n, int slot, Shared &sm) {
+// y[i] = row_i . x for i < n (n <= kRowBatch) into c.y[0]; rows start at `base`
+// with stride row_bytes.  Many rows: one warp per row.  Few rows: several
+// warps split each row and their partials are summed in a fixed order.
+template <bool FROM_SMEM>
+__device__ void rows_dot(const char *base, int dtype, int cols, int n, const float *x, Control &c) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t row_bytes = static_cast<size_t>(cols) * esize(dtype);
     if (n >= kEngineWarps) {
         for (int i = warp; i < n; i += kEngineWarps) {
-            float acc = row_partial_any(s, r0 + i, lane, 32, lane, sm.in);
+            float acc = row_partial_any<FROM_SMEM>(dtype, base + i * row_bytes, cols, lane, 32, lane, x);
             acc = warp_sum(acc);
-            if (lane == 0) sm.y[slot][i] = acc;
+            if (lane == 0) c.y[0][i] = acc;
         }
         __syncthreads();
         return;
     }
-    const int wpr = kEngineWarps / n;  // warps per row
+    const int wpr = kEngineWarps / n;
     const int i = warp / wpr, part = warp % wpr;
     if (i < n) {
-        float acc = row_partial_any(s, r0 + i, part * 32 + lane, 32 * wpr, part == 0 ? lane : -1, sm.in);
+        float acc = row_partial_any<FROM_SMEM>(dtype, base + i * row_bytes, cols, part * 32 + lane, 32 * wpr,
+                                               part == 0 ? lane : -1, x);
         acc = warp_sum(acc);
-        if (lane == 0) sm.partial[i * wpr + part] = acc;
+        if (lane == 0) c.partial[i * wpr + part] = acc;
     }
     __syncthreads();
     if (threadIdx.x < n) {
         float total = 0.f;
-        for (int p = 0; p < wpr; ++p) total += sm.partial[threadIdx.x * wpr + p];
-        sm.y[slot][threadIdx.x] = total;
+        for (int p = 0; p < wpr; ++p) total += c.partial[threadIdx.x * wpr + p];
+        c.y[0][threadIdx.x] = total;
     }
     __syncthreads();
 }
 
-__device__ void load_input(const GemvPhase &g, int cols, int token, Shared &sm) {
-    if (g.input_kind == IN_EMBED_ROW) {
-        for (int j = threadIdx.x; j < cols; j += blockDim.x) {
-            const float v = load_weight(g.embed, g.embed_dtype, static_cast<size_t>(token) * cols + j);
-            sm.in[j] = v;
-            if (g.embed_copy && blockIdx.x == 0) g.embed_copy[j] = v;
-        }
-    } else {
-        for (int j = threadIdx.x; j < cols; j += blockDim.x) sm.in[j] = __ldcg(g.in + j);
+// ---- GEMV phases ----------------------------------------------------------------------
+__device__ void merge_attention(const AttnMerge &m, int position, float *in, Control &c) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int total = min(position + 1, m.capacity) + (m.relay_count ? __ldcg(m.relay_count) : 0);
+    const int chunks = attn_chunks(total, m.kv_heads, gridDim.x);
+    const int stride = m.dim + 2;
+    for (int h = warp; h < m.heads; h += kEngineWarps) {
+        const float *base = m.partial + static_cast<size_t>(h) * kMaxAttnChunks * stride;
+        const float mc = lane < chunks ? __ldcg(base + lane * stride + m.dim) : -INFINITY;
+        const float lc = lane < chunks ? __ldcg(base + lane * stride + m.dim + 1) : 0.f;
+        const float mx = warp_max(mc);
+        const float w = (mc == -INFINITY) ? 0.f : expf(mc - mx);
+        const float den = warp_sum(w * lc);
+        if (lane < kMaxAttnChunks) c.merge_w[h * kMaxAttnChunks + lane] = lane < chunks ? w / den : 0.f;
     }
     __syncthreads();
+    for (int e = threadIdx.x; e < m.heads * m.dim; e += blockDim.x) {
+        const int h = e / m.dim, j = e % m.dim;
+        const float *base = m.partial + static_cast<size_t>(h) * kMaxAttnChunks * stride + j;
+        const float *w = c.merge_w + h * kMaxAttnChunks;
+        float a0 = 0.f, a1 = 0.f;
+        int cc = 0;
+        for (; cc + 1 < chunks; cc += 2) {
+            a0 = fmaf(w[cc], __ldcg(base + cc * stride), a0);
+            a1 = fmaf(w[cc + 1], __ldcg(base + (cc + 1) * stride), a1);
+        }
+        if (cc < chunks) a0 = fmaf(w[cc], __ldcg(base + cc * stride), a0);
+        in[e] = a0 + a1;
+    }
+    __syncthreads();
+}
+
+__device__ void load_input(const GemvPhase &g, int cols, const StepInfo &info, float *in, Control &c) {
+    if (g.input_kind == IN_EMBED_ROW) {
+        for (int j = threadIdx.x; j < cols; j += blockDim.x) {
+            const float v = load_weight(g.embed, g.embed_dtype, static_cast<size_t>(info.token) * cols + j);
+            in[j] = v;
+            if (g.embed_copy && blockIdx.x == 0) g.embed_copy[j] = v;
+        }
+        __syncthreads();
+    } else if (g.input_kind == IN_ATTN_MERGE) {
+        merge_attention(g.merge, info.position, in, c);
+    } else {
+        for (int j = threadIdx.x; j < cols; j += blockDim.x) in[j] = __ldcg(g.in + j);
+        __syncthreads();
+    }
+}
+
+struct Epi {
+    unsigned long long best = 0;
+    int nonfinite = 0;
+};
+
+// Epilogue of rows [row0, row0+n) of segment `s` whose dot products are in c.y[0].
+__device__ void epilogue(const GemvPhase &g, int s, int row0, int n, const StepInfo &info, Control &c, Epi &e) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int r = row0 + i;
+        const float y = c.y[0][i];
+        switch (g.epilogue) {
+            case EPI_STORE: g.seg[s].out[r] = y; break;
+            case EPI_RESIDUAL: g.x[r] = __fadd_rn(__ldcg(g.x + r), __fmul_rn(g.scale, y)); break;
+            case EPI_SWIGLU:
+                if (s == 0) {
+                    c.y[1][i] = y;
+                } else {
+                    const float gt = c.y[1][i];
+                    g.out[r] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), y);
+                }
+                break;
+            case EPI_LOGITS:
+                g.out[static_cast<size_t>(info.logits_row) * g.seg[0].rows + r] = y;
+                if (!isfinite(y)) e.nonfinite = 1;
+                else e.best = max(e.best, argmax_key(y, r));
+                break;
+        }
+    }
+}
+
+__device__ void finish_logits(StepState *st, Control &c, Epi &e) {
+    unsigned long long best = e.best;
+    for (int offset = 16; offset > 0; offset >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, offset));
+    const int nonfinite = __any_sync(0xffffffffu, e.nonfinite);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        c.best[warp] = best;
+        if (nonfinite) atomicExch(&st->nonfinite, 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long m = 0;
+        for (int w = 0; w < kEngineWarps; ++w) m = max(m, c.best[w]);
+        if (m) atomicMax(&st->best, m);
+    }
+    __syncthreads();
+}
+
+// GEMV whose weights stream through the shared-memory ring.  `cidx` is the
+// index of the next piece to consume (the same in every thread).
+__device__ bool gemv_bulk(const Phase *phases, int nphases, bool need_head, int p, StepState *st,
+                          const StepInfo &info, const Smem &sm, int &cidx) {
+    const GemvPhase &g = phases[p].gemv;
+    Control &c = *sm.c;
+    const int b = blockIdx.x, G = gridDim.x, cols = g.seg[0].cols;
+    float *in = sm.scratch;
+    auto consumed = [&]() {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            ++c.consumed;
+            refill(phases, nphases, need_head, sm);
+        }
+        ++cidx;
+    };
+    load_input(g, cols, info, in, c);
     if (g.norm) {
         float ss = 0.f;
-        for (int j = threadIdx.x; j < cols; j += blockDim.x) ss = fmaf(sm.in[j], sm.in[j], ss);
-        ss = block_sum(ss, sm);
+        for (int j = threadIdx.x; j < cols; j += blockDim.x) ss = fmaf(in[j], in[j], ss);
+        ss = block_sum(ss, c);
         // kernels.cl:25-27: scale = 1/sqrt(mean + eps); y = (x * scale) * gain
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), g.norm_eps)));
+        const unsigned char *gain_smem = nullptr;
+        if (g.gain_piece) {
+            // every thread agrees on the outcome before any of them moves on
+            if (!__syncthreads_and(wait_piece(sm, cidx, st, p))) return false;
+            gain_smem = sm.ring + c.offset[cidx % kQueue];
+        }
+        for (int j = threadIdx.x; j < cols; j += blockDim.x) {
+            float gain = 1.0f;
+            if (gain_smem) gain = load_weight(gain_smem, g.norm_gain_dtype, j);
+            else if (g.norm_gain) gain = load_weight(g.norm_gain, g.norm_gain_dtype, j);
+            in[j] = __fmul_rn(__fmul_rn(in[j], scale), gain);
+        }
+        if (g.gain_piece) consumed();
+        else __syncthreads();
+    }
+    Epi e;
+    const int pieces = phase_pieces(g, b, G) - (g.gain_piece ? 1 : 0);
+    for (int k = 0; k < pieces; ++k) {
+        const Piece pc = phase_piece(g, b, G, k + (g.gain_piece ? 1 : 0));
+        if (!__syncthreads_and(wait_piece(sm, cidx, st, p))) return false;
+        const Segment &s = g.seg[pc.seg];
+        const char *rows = reinterpret_cast<const char *>(sm.ring + c.offset[cidx % kQueue]);
+        rows_dot<true>(rows, s.dtype, cols, pc.nrows, in, c);
+        epilogue(g, pc.seg, pc.row0, pc.nrows, info, c, e);
+        consumed();
+    }
+    if (g.epilogue == EPI_LOGITS) finish_logits(st, c, e);
+    return true;
+}
+
+// GEMV reading weights straight from global memory (shapes the ring cannot take).
+__device__ void gemv_direct(const GemvPhase &g, StepState *st, const StepInfo &info, const Smem &sm) {
+    Control &c = *sm.c;
+    const int G = gridDim.x, b = blockIdx.x, cols = g.seg[0].cols;
+    float *in = sm.scratch;
+    load_input(g, cols, info, in, c);
+    if (g.norm) {
+        float ss = 0.f;
+        for (int j = threadIdx.x; j < cols; j += blockDim.x) ss = fmaf(in[j], in[j], ss);
+        ss = block_sum(ss, c);
         const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), g.norm_eps)));
         for (int j = threadIdx.x; j < cols; j += blockDim.x) {
             const float gain = g.norm_gain ? load_weight(g.norm_gain, g.norm_gain_dtype, j) : 1.0f;
-            sm.in[j] = __fmul_rn(__fmul_rn(sm.in[j], scale), gain);
+            in[j] = __fmul_rn(__fmul_rn(in[j], scale), gain);
         }
         __syncthreads();
     }
-}
-
-__device__ void gemv_phase(const GemvPhase &g, StepState *st, const StepInfo &info, Shared &sm) {
-    const int G = gridDim.x, b = blockIdx.x;
-    const int cols = g.seg[0].cols;
-    load_input(g, cols, info.token, sm);
+    Epi e;
     const bool paired = g.epilogue == EPI_SWIGLU;
-    const int passes = paired ? 1 : g.nseg;
-    unsigned long long best = 0;
-    int nonfinite = 0;
-    for (int s = 0; s < passes; ++s) {
-        const Segment &seg = g.seg[s];
+    for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
         int r0, r1;
-        row_range(seg.rows, b, G, r0, r1);
+        row_range(g.seg[s].rows, b, G, r0, r1);
         for (int rb = r0; rb < r1; rb += kRowBatch) {
             const int n = min(kRowBatch, r1 - rb);
-            gemv_rows(seg, rb, n, 0, sm);
-            if (paired) gemv_rows(g.seg[1], rb, n, 1, sm);
-            for (int i = threadIdx.x; i < n; i += blockDim.x) {
-                const int r = rb + i;
-                const float y = sm.y[0][i];
-                switch (g.epilogue) {
-                    case EPI_STORE: seg.out[r] = y; break;
-                    case EPI_RESIDUAL: g.x[r] = __fadd_rn(__ldcg(g.x + r), __fmul_rn(g.scale, y)); break;
-                    case EPI_SWIGLU: {
-                        const float u = sm.y[1][i];
-                        g.out[r] = __fmul_rn(__fdiv_rn(y, __fadd_rn(1.0f, expf(-y))), u);
-                        break;
-                    }
-                    case EPI_LOGITS: {
-                        g.out[static_cast<size_t>(info.logits_row) * seg.rows + r] = y;
-                        if (!isfinite(y)) nonfinite = 1;
-                        else best = max(best, argmax_key(y, r));
-                        break;
-                    }
-                }
+            for (int part = 0; part < (paired ? 2 : 1); ++part) {
+                const Segment &seg = g.seg[s + part];
+                const char *base = static_cast<const char *>(seg.w) + static_cast<size_t>(rb) * cols * esize(seg.dtype);
+                rows_dot<false>(base, seg.dtype, cols, n, in, c);
+                epilogue(g, s + part, rb, n, info, c, e);
+                __syncthreads();
             }
-            __syncthreads();
         }
     }
-    if (g.epilogue == EPI_LOGITS) {
-        // CTA argmax -> one atomic per CTA
-        for (int offset = 16; offset > 0; offset >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, offset));
-        nonfinite = __any_sync(0xffffffffu, nonfinite);
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        if (lane == 0) {
-            sm.best[warp] = best;
-            if (nonfinite) atomicExch(&st->nonfinite, 1);
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            unsigned long long m = 0;
-            for (int w = 0; w < kEngineWarps; ++w) m = max(m, sm.best[w]);
-            if (m) atomicMax(&st->best, m);
-        }
-        __syncthreads();
-    }
-}
-
-__device__ void prefetch_gemv(const GemvPhase &g) {
-    if (threadIdx.x != 0) return;
-    const int G = gridDim.x, b = blockIdx.x;
-    size_t budget = kPrefetchCap;
-    const int nseg = g.epilogue == EPI_SWIGLU ? 2 : g.nseg;
-    for (int s = 0; s < nseg && budget; ++s) {
-        const Segment &seg = g.seg[s];
-        int r0, r1;
-        row_range(seg.rows, b, G, r0, r1);
-        if (r1 <= r0) continue;
-        const size_t row_bytes = static_cast<size_t>(seg.cols) * esize(seg.dtype);
-        size_t bytes = static_cast<size_t>(r1 - r0) * row_bytes;
-        if (bytes > budget) bytes = budget;
-        budget -= bytes;
-        prefetch_l2(static_cast<const char *>(seg.w) + static_cast<size_t>(r0) * row_bytes, bytes);
-    }
+    if (g.epilogue == EPI_LOGITS) finish_logits(st, c, e);
 }
 
 // ---- grouped-query attention ------------------------------------------------------
@@ -369,10 +649,10 @@ __device__ void norm_rope_warp(float *v, int dim, const void *gain, int gain_dty
     __syncwarp();
 }
 
-// Work unit = (KV head g, chunk c of the attended rows).  Each unit does an
-// online-softmax pass over its rows for the group's query heads; a chunked
-// head's partials are merged by the unit that arrives last.
-__device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, Shared &sm) {
+// Work unit = (KV head g, chunk c of the attended rows): an online-softmax
+// pass over the chunk's keys for the group's query heads; writes the chunk's
+// (acc, max, sum) for the consumer to merge.
+__device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const Smem &sm) {
     const int G = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = a.dim, gq = a.heads / a.kv_heads;
@@ -382,16 +662,13 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, Shared 
     const int start = (count - length) % cap;
     const int extra = a.relay_count ? __ldcg(a.relay_count) : 0;
     const int total = length + extra;
-    int chunks = max(1, min(a.max_chunks, G / a.kv_heads));
-    chunks = min(chunks, max(1, (total + kKeyTile - 1) / kKeyTile));
-    chunks = min(chunks, kMergeSlots / gq);
+    const int chunks = attn_chunks(total, a.kv_heads, G);
     const int chunk_len = (total + chunks - 1) / chunks;
-    chunks = (total + chunk_len - 1) / chunk_len;
     const float pos_f = static_cast<float>(info.position);
     const float sqrt_d = __fsqrt_rn(static_cast<float>(d));  // divisor, kernels.cl:72
+    const int stride = d + 2;
 
-    // shared-memory carve-up (reuses the GEMV input area)
-    float *q = sm.in;                                  // [gq][d]
+    float *q = sm.scratch;                             // [gq][d]
     float *kt = q + gq * d;                            // [kKeyTile][d+1]
     float *vt = kt + kKeyTile * (d + 1);               // [kKeyTile][d]
     float *p = vt + kKeyTile * d;                      // [gq][kKeyTile]
@@ -485,71 +762,15 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, Shared 
             }
             __syncthreads();
         }
-        // 4. publish (single chunk: final; else partial + last-arriver merge)
-        if (chunks == 1) {
-            for (int e = threadIdx.x; e < gq * d; e += blockDim.x) {
-                const int i = e / d, j = e % d;
-                a.out[static_cast<size_t>(g * gq + i) * d + j] = acc[e] / lrow[i];
-            }
-            __syncthreads();
-            continue;
-        }
-        const int stride = d + 2;
+        // 4. publish the chunk partial: acc[d], running max, running sum
         for (int e = threadIdx.x; e < gq * d; e += blockDim.x) {
             const int i = e / d, j = e % d;
-            a.partial[(static_cast<size_t>(g * gq + i) * a.max_chunks + c) * stride + j] = acc[e];
+            a.partial[(static_cast<size_t>(g * gq + i) * kMaxAttnChunks + c) * stride + j] = acc[e];
         }
         if (threadIdx.x < gq) {
-            float *rec = a.partial + (static_cast<size_t>(g * gq + threadIdx.x) * a.max_chunks + c) * stride;
+            float *rec = a.partial + (static_cast<size_t>(g * gq + threadIdx.x) * kMaxAttnChunks + c) * stride;
             rec[d] = mrow[threadIdx.x];
             rec[d + 1] = lrow[threadIdx.x];
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            const unsigned old = atomicAdd(a.arrivals + g, 1u);
-            sm.flag = (old == static_cast<unsigned>(chunks - 1));
-            if (sm.flag) {
-                a.arrivals[g] = 0u;
-                __threadfence();
-            }
-        }
-        __syncthreads();
-        if (sm.flag) {
-            // one warp per query head: all chunk maxima / sums loaded in parallel,
-            // softmax-merge weights staged in shared memory
-            for (int i = warp; i < gq; i += kEngineWarps) {
-                const float *base = a.partial + static_cast<size_t>(g * gq + i) * a.max_chunks * stride;
-                float m = -INFINITY;
-                for (int cc = lane; cc < chunks; cc += 32) m = fmaxf(m, __ldcg(base + cc * stride + d));
-                m = warp_max(m);
-                float den = 0.f;
-                for (int cc = lane; cc < chunks; cc += 32) {
-                    const float mc = __ldcg(base + cc * stride + d);
-                    const float w = (mc == -INFINITY) ? 0.f : expf(mc - m);
-                    sm.merge_w[i * chunks + cc] = w;
-                    den = fmaf(w, __ldcg(base + cc * stride + d + 1), den);
-                }
-                den = warp_sum(den);
-                __syncwarp();
-                for (int cc = lane; cc < chunks; cc += 32) sm.merge_w[i * chunks + cc] /= den;
-            }
-            __syncthreads();
-            for (int e = threadIdx.x; e < gq * d; e += blockDim.x) {
-                const int i = e / d, j = e % d;
-                const float *base = a.partial + static_cast<size_t>(g * gq + i) * a.max_chunks * stride + j;
-                const float *w = sm.merge_w + i * chunks;
-                float num0 = 0.f, num1 = 0.f, num2 = 0.f, num3 = 0.f;
-                int cc = 0;
-                for (; cc + 3 < chunks; cc += 4) {
-                    num0 = fmaf(w[cc], __ldcg(base + cc * stride), num0);
-                    num1 = fmaf(w[cc + 1], __ldcg(base + (cc + 1) * stride), num1);
-                    num2 = fmaf(w[cc + 2], __ldcg(base + (cc + 2) * stride), num2);
-                    num3 = fmaf(w[cc + 3], __ldcg(base + (cc + 3) * stride), num3);
-                }
-                for (; cc < chunks; ++cc) num0 = fmaf(w[cc], __ldcg(base + cc * stride), num0);
-                a.out[static_cast<size_t>(g * gq + i) * d + j] = (num0 + num1) + (num2 + num3);
-            }
         }
         __syncthreads();
     }
@@ -559,8 +780,14 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, Shared 
 
 __global__ void __launch_bounds__(kEngineThreads, 1)
     decode_step_kernel(const Phase *__restrict__ phases, int nphases, StepState *st, StepControl ctl) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    Shared &sm = *reinterpret_cast<Shared *>(smem_raw);
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    Smem sm;
+    sm.c = reinterpret_cast<Control *>(smem_raw);
+    sm.scratch = reinterpret_cast<float *>(smem_raw + ((sizeof(Control) + 127) & ~size_t(127)));
+    sm.ring = reinterpret_cast<unsigned char *>(sm.scratch) +
+              ((static_cast<size_t>(ctl.scratch_floats) * 4 + 127) & ~size_t(127));
+    sm.ring_bytes = ctl.ring_bytes;
+    Control &c = *sm.c;
     __shared__ StepInfo info;
     __shared__ unsigned long long base;
     __shared__ int skip, need_head;
@@ -582,39 +809,45 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
             if (blockIdx.x == 0) atomicCAS(&st->error, 0, 4);
             skip = 1;
         }
+        if (!skip) {
+            for (int i = 0; i < kQueue; ++i) mbar_init(&c.mbar[i], 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            c.issued = c.consumed = c.head_offset = c.cur_phase = c.cur_piece = 0;
+        }
     }
     __syncthreads();
     if (skip) return;
-    if (ctl.trace && blockIdx.x == 0 && threadIdx.x == 0) ctl.trace[0] = global_ns();
-    int barriers = 0;
-    // warm the first weight-streaming phase
-    for (int p = 0; p < nphases; ++p)
-        if (phases[p].kind == PH_GEMV) {
-            prefetch_gemv(phases[p].gemv);
-            break;
-        }
-    for (int p = 0; p < nphases; ++p) {
+    if (threadIdx.x == 0) {
+        if (ctl.trace && blockIdx.x == 0) ctl.trace[0] = global_ns();
+        refill(phases, nphases, need_head != 0, sm);
+    }
+    __syncthreads();
+    int barriers = 0, cidx = 0;
+    bool ok = true;
+    for (int p = 0; p < nphases && ok; ++p) {
         const Phase &ph = phases[p];
         if (ph.kind == PH_STEP_END) break;
         if (ph.layer < 0 && !need_head) continue;
-        // prefetch this CTA's share of the next weight-streaming phase
-        for (int q = p + 1; q < nphases; ++q) {
-            if (phases[q].kind == PH_GEMV) {
-                if (!(phases[q].layer < 0 && !need_head)) prefetch_gemv(phases[q].gemv);
-                break;
-            }
+        if (ph.kind == PH_GEMV) {
+            if (ph.gemv.bulk) ok = gemv_bulk(phases, nphases, need_head != 0, p, st, info, sm, cidx);
+            else gemv_direct(ph.gemv, st, info, sm);
+        } else if (ph.kind == PH_ATTN_GQA) {
+            attn_gqa_phase(ph.attn, info, sm);
         }
-        if (ph.kind == PH_GEMV) gemv_phase(ph.gemv, st, info, sm);
-        else if (ph.kind == PH_ATTN_GQA) attn_gqa_phase(ph.attn, info, sm);
-        unsigned long long *stamp = ctl.trace ? ctl.trace + 1 + static_cast<size_t>(barriers) * (gridDim.x + 1) : nullptr;
+        if (!ok) break;
+        unsigned long long *stamp =
+            ctl.trace ? ctl.trace + 1 + static_cast<size_t>(barriers) * (gridDim.x + 1) : nullptr;
         if (stamp) {
             __syncthreads();
             if (threadIdx.x == 0) stamp[blockIdx.x] = global_ns();
         }
         ++barriers;
-        if (!grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, p, sm)) return;
-        if (stamp && blockIdx.x == 0 && threadIdx.x == 0) stamp[gridDim.x] = global_ns();
+        ok = grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, p, sm);
+        if (ok && stamp && blockIdx.x == 0 && threadIdx.x == 0) stamp[gridDim.x] = global_ns();
     }
+    __syncthreads();
+    if (threadIdx.x == 0) drain(sm);  // nothing is in flight on the normal path; bounded either way
+    if (!ok) return;
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         volatile StepState *s = st;
         const int pos = info.position;
@@ -642,6 +875,6 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
     }
 }
 
-size_t decode_step_smem_bytes() { return sizeof(Shared); }
+size_t decode_control_bytes() { return (sizeof(Control) + 127) & ~size_t(127); }
 
 }  // namespace mr
