@@ -104,6 +104,9 @@ struct mr_model {
     float *partial = nullptr;
     int scratch_floats = 0, ring_bytes = 0;
     size_t smem_bytes = 0;
+    PieceDesc *d_pieces = nullptr;
+    int *d_piece_count = nullptr;
+    int piece_stride = 0;
     std::vector<float *> k_cache, v_cache;
     std::vector<int> cache_capacity;
     StepState *state = nullptr;
@@ -356,6 +359,69 @@ int build_plan(mr_model *m) {
     return MR_OK;
 }
 
+// The weight stream of every CTA: its pieces of every bulk phase, in the
+// order the kernel consumes them (gain vector first, then the rows; SwiGLU
+// phases alternate gate and up pieces of the same rows).
+int build_pieces(mr_model *m) {
+    const int G = m->grid;
+    std::vector<std::vector<PieceDesc>> per(G);
+    for (size_t p = 0; p < m->phases.size(); ++p) {
+        const Phase &ph = m->phases[p];
+        if (ph.kind != PH_GEMV || !ph.gemv.bulk) continue;
+        const GemvPhase &g = ph.gemv;
+        const uint32_t gain_bytes = (uint32_t)((g.seg[0].cols * (int)dtype_size(g.norm_gain_dtype) + 15) & ~15);
+        auto add = [&](std::vector<PieceDesc> &v, int s, int row0, int n) {
+            const Segment &seg = g.seg[s];
+            const size_t row_bytes = (size_t)seg.cols * dtype_size(seg.dtype);
+            PieceDesc d{};
+            d.src = static_cast<const char *>(seg.w) + row_bytes * row0;
+            d.bytes = (uint32_t)(row_bytes * n);
+            d.row0 = row0;
+            d.seg = (short)s;
+            d.nrows = (short)n;
+            d.phase = (short)p;
+            v.push_back(d);
+        };
+        for (int b = 0; b < G; ++b) {
+            std::vector<PieceDesc> &v = per[b];
+            if (g.gain_piece) {
+                PieceDesc d{};
+                d.src = g.norm_gain;
+                d.bytes = gain_bytes;
+                d.seg = -1;
+                d.phase = (short)p;
+                v.push_back(d);
+            }
+            const bool paired = g.epilogue == EPI_SWIGLU;
+            for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
+                const int rows = g.seg[s].rows, rpp = g.seg[s].rows_per_piece;
+                const int r0 = (int)((long long)rows * b / G), r1 = (int)((long long)rows * (b + 1) / G);
+                for (int row0 = r0; row0 < r1; row0 += rpp) {
+                    const int n = std::min(rpp, r1 - row0);
+                    add(v, s, row0, n);
+                    if (paired) add(v, 1, row0, n);
+                }
+            }
+        }
+    }
+    size_t stride = 1;
+    for (auto &v : per) stride = std::max(stride, v.size());
+    std::vector<PieceDesc> flat(stride * G);
+    std::vector<int> counts(G);
+    for (int b = 0; b < G; ++b) {
+        std::copy(per[b].begin(), per[b].end(), flat.begin() + (size_t)b * stride);
+        counts[b] = (int)per[b].size();
+    }
+    int rc = MR_OK;
+    m->d_pieces = static_cast<PieceDesc *>(device_alloc(m, sizeof(PieceDesc) * flat.size(), &rc));
+    m->d_piece_count = static_cast<int *>(device_alloc(m, sizeof(int) * G, &rc));
+    if (rc) return rc;
+    MR_CUDA_TRY(cudaMemcpy(m->d_pieces, flat.data(), sizeof(PieceDesc) * flat.size(), cudaMemcpyHostToDevice));
+    MR_CUDA_TRY(cudaMemcpy(m->d_piece_count, counts.data(), sizeof(int) * G, cudaMemcpyHostToDevice));
+    m->piece_stride = (int)stride;
+    return MR_OK;
+}
+
 int sync_and_check(mr_model *m, const char *what) {
     MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
     int error = 0;
@@ -417,6 +483,9 @@ StepControl base_control(mr_model *m) {
     ctl.vocab_size = m->cfg.vocab_size;
     ctl.scratch_floats = m->scratch_floats;
     ctl.ring_bytes = m->ring_bytes;
+    ctl.pieces = m->d_pieces;
+    ctl.piece_count = m->d_piece_count;
+    ctl.piece_stride = m->piece_stride;
     return ctl;
 }
 
@@ -554,6 +623,7 @@ int mr_model_finalize(mr_model *m) {
     int rc = MR_OK;
     const int H = c.query_heads, d = c.head_dim;
     MR_REQUIRE(H <= 64, "query_heads %d above the engine limit 64", H);
+    MR_REQUIRE(d <= 128, "head_dim %d above the engine limit 128", d);
     const int max_kvh = *std::max_element(m->layer_kvh.begin(), m->layer_kvh.end());
     const int gq_max = H / *std::min_element(m->layer_kvh.begin(), m->layer_kvh.end());
     // shared memory: control block, scratch (GEMV input vector / attention tiles), weight ring
@@ -595,6 +665,7 @@ int mr_model_finalize(mr_model *m) {
     }
     MR_CUDA_TRY(cudaMemcpy(m->d_inv_freq, m->inv_freq.data(), sizeof(float) * (d / 2), cudaMemcpyHostToDevice));
     rc = build_plan(m);
+    if (!rc) rc = build_pieces(m);
     if (rc) return rc;
     m->d_phases = static_cast<Phase *>(device_alloc(m, sizeof(Phase) * m->phases.size(), &rc));
     if (rc) return rc;

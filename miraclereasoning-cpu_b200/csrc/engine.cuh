@@ -31,7 +31,7 @@ constexpr int kRowBatch = 256;       // rows of one piece (and of one direct-loa
 constexpr int kQueue = 32;           // pieces in flight per CTA (one mbarrier each)
 constexpr int kMaxAttnChunks = 16;   // key chunks per KV head (merged by the consumer)
 constexpr int kKeysPerChunk = 64;    // target keys per attention work unit
-constexpr int kKeyTile = 32;         // keys per attention tile
+constexpr int kKeyTile = 64;         // keys per attention tile
 constexpr int kSmemLimit = 227 * 1024;
 
 enum PhaseKind : int {
@@ -107,6 +107,18 @@ struct AttnPhase {
     float *partial;                 // [heads][kMaxAttnChunks][dim + 2]
 };
 
+// One bulk copy of a CTA's weight stream, precomputed on the host: the CTA's
+// pieces of every weight-streaming phase of a step, in consumption order.
+struct PieceDesc {
+    const void *src;    // global source (16-byte aligned)
+    uint32_t bytes;     // multiple of 16
+    int row0;           // first row (weight pieces)
+    short seg;          // segment index, -1 = the phase's norm gain vector
+    short nrows;
+    short phase;        // index in the phase list
+    short pad;
+};
+
 struct Phase {
     int kind;
     int layer;                      // -1: the output head (skipped when no logits are needed)
@@ -158,6 +170,9 @@ struct StepControl {
     int vocab_size;                   // tokens outside [0, vocab) stop the step with error 4
     int scratch_floats;               // shared-memory scratch (input vector / attention tiles)
     int ring_bytes;                   // shared-memory weight ring
+    const PieceDesc *pieces;          // [grid][piece_stride] weight stream of each CTA
+    const int *piece_count;           // [grid]
+    int piece_stride;
     // Optional phase trace (globaltimer ns): [0] = launch start (CTA 0); then per
     // executed phase k, slots 1 + k*(grid+1) + b = CTA b done computing, and
     // slot 1 + k*(grid+1) + grid = CTA 0 leaving the barrier.  NULL = off.

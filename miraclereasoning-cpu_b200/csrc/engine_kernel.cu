@@ -44,7 +44,7 @@ struct Control {
     unsigned long long best[kEngineWarps];
     int flag, ok;
     // producer state (written by thread 0 only)
-    int issued, consumed, head_offset, cur_phase, cur_piece;
+    int issued, consumed, head_offset;
 };
 
 struct StepInfo {
@@ -93,81 +93,23 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         : "memory");
 }
 
-// ---- piece schedule (identical in producer and consumers) ----------------------------
-struct Piece {
-    int seg;     // -1: the norm gain vector
-    int row0, nrows;
-};
-
-__device__ int phase_pieces(const GemvPhase &g, int b, int G) {
-    if (!g.bulk) return 0;
-    int n = g.gain_piece ? 1 : 0;
-    if (g.epilogue == EPI_SWIGLU) {
-        int r0, r1;
-        row_range(g.seg[0].rows, b, G, r0, r1);
-        return n + 2 * ceil_div(r1 - r0, g.seg[0].rows_per_piece);
-    }
-    for (int s = 0; s < g.nseg; ++s) {
-        int r0, r1;
-        row_range(g.seg[s].rows, b, G, r0, r1);
-        n += ceil_div(r1 - r0, g.seg[s].rows_per_piece);
-    }
-    return n;
+// ---- piece stream (host-precomputed table, see PieceDesc) ---------------------------
+__device__ __forceinline__ const PieceDesc *cta_pieces(const StepControl &ctl) {
+    return ctl.pieces + static_cast<size_t>(blockIdx.x) * ctl.piece_stride;
 }
 
-__device__ Piece phase_piece(const GemvPhase &g, int b, int G, int k) {
-    if (g.gain_piece) {
-        if (k == 0) return {-1, 0, 0};
-        --k;
-    }
-    if (g.epilogue == EPI_SWIGLU) {
-        int r0, r1;
-        row_range(g.seg[0].rows, b, G, r0, r1);
-        const int rpp = g.seg[0].rows_per_piece, row0 = r0 + (k >> 1) * rpp;
-        return {k & 1, row0, min(rpp, r1 - row0)};
-    }
-    for (int s = 0; s < g.nseg; ++s) {
-        int r0, r1;
-        row_range(g.seg[s].rows, b, G, r0, r1);
-        const int rpp = g.seg[s].rows_per_piece, np = ceil_div(r1 - r0, rpp);
-        if (k < np) {
-            const int row0 = r0 + k * rpp;
-            return {s, row0, min(rpp, r1 - row0)};
-        }
-        k -= np;
-    }
-    return {0, 0, 0};
-}
-
-__device__ uint32_t piece_bytes(const GemvPhase &g, const Piece &p) {
-    if (p.seg < 0) return static_cast<uint32_t>((g.seg[0].cols * esize(g.norm_gain_dtype) + 15) & ~15);
-    const Segment &s = g.seg[p.seg];
-    return static_cast<uint32_t>(p.nrows) * s.cols * esize(s.dtype);
-}
-
-__device__ const void *piece_src(const GemvPhase &g, const Piece &p) {
-    if (p.seg < 0) return g.norm_gain;
-    const Segment &s = g.seg[p.seg];
-    return static_cast<const char *>(s.w) + static_cast<size_t>(p.row0) * s.cols * esize(s.dtype);
-}
-
-// Producer (thread 0): issue the next pieces of this step while the ring and
-// the mbarrier queue have room.
-__device__ void refill(const Phase *phases, int nphases, bool need_head, const Smem &sm) {
+// Producer (thread 0): issue the next pieces of this CTA's stream while the
+// ring and the mbarrier queue have room.  Pieces of the head phase are only
+// streamed when this step computes logits.
+__device__ void refill(const StepControl &ctl, bool need_head, int head_phase, const Smem &sm) {
     Control &c = *sm.c;
-    const int b = blockIdx.x, G = gridDim.x;
+    const PieceDesc *table = cta_pieces(ctl);
+    const int count = ctl.piece_count[blockIdx.x];
     bool fenced = false;
-    while (c.cur_phase < nphases) {
-        const Phase &ph = phases[c.cur_phase];
-        if (ph.kind != PH_GEMV || !ph.gemv.bulk || (ph.layer < 0 && !need_head) ||
-            c.cur_piece >= phase_pieces(ph.gemv, b, G)) {
-            ++c.cur_phase;
-            c.cur_piece = 0;
-            continue;
-        }
-        if (c.issued - c.consumed >= kQueue) return;
-        const Piece p = phase_piece(ph.gemv, b, G, c.cur_piece);
-        const int bytes = static_cast<int>(piece_bytes(ph.gemv, p));
+    while (c.issued < count && c.issued - c.consumed < kQueue) {
+        const PieceDesc d = table[c.issued];
+        if (!need_head && d.phase == head_phase) return;
+        const int bytes = static_cast<int>(d.bytes);
         int off;
         if (c.issued == c.consumed) {
             off = 0;
@@ -190,10 +132,9 @@ __device__ void refill(const Phase *phases, int nphases, bool need_head, const S
         }
         const int slot = c.issued % kQueue;
         c.offset[slot] = off;
-        bulk_load(sm.ring + off, piece_src(ph.gemv, p), static_cast<uint32_t>(bytes), &c.mbar[slot]);
+        bulk_load(sm.ring + off, d.src, d.bytes, &c.mbar[slot]);
         c.head_offset = off + bytes;
         ++c.issued;
-        ++c.cur_piece;
     }
 }
 
@@ -525,18 +466,19 @@ __device__ void finish_logits(StepState *st, Control &c, Epi &e) {
 }
 
 // GEMV whose weights stream through the shared-memory ring.  `cidx` is the
-// index of the next piece to consume (the same in every thread).
-__device__ bool gemv_bulk(const Phase *phases, int nphases, bool need_head, int p, StepState *st,
-                          const StepInfo &info, const Smem &sm, int &cidx) {
-    const GemvPhase &g = phases[p].gemv;
+// index of the next piece of this CTA's stream (the same in every thread).
+__device__ bool gemv_bulk(const GemvPhase &g, int p, const StepControl &ctl, bool need_head, int head_phase,
+                          StepState *st, const StepInfo &info, const Smem &sm, int &cidx) {
     Control &c = *sm.c;
-    const int b = blockIdx.x, G = gridDim.x, cols = g.seg[0].cols;
+    const int cols = g.seg[0].cols;
+    const PieceDesc *table = cta_pieces(ctl);
+    const int count = ctl.piece_count[blockIdx.x];
     float *in = sm.scratch;
     auto consumed = [&]() {
         __syncthreads();
         if (threadIdx.x == 0) {
             ++c.consumed;
-            refill(phases, nphases, need_head, sm);
+            refill(ctl, need_head, head_phase, sm);
         }
         ++cidx;
     };
@@ -563,14 +505,14 @@ __device__ bool gemv_bulk(const Phase *phases, int nphases, bool need_head, int 
         else __syncthreads();
     }
     Epi e;
-    const int pieces = phase_pieces(g, b, G) - (g.gain_piece ? 1 : 0);
-    for (int k = 0; k < pieces; ++k) {
-        const Piece pc = phase_piece(g, b, G, k + (g.gain_piece ? 1 : 0));
+    while (cidx < count) {
+        const PieceDesc d = table[cidx];
+        if (d.phase != p) break;
         if (!__syncthreads_and(wait_piece(sm, cidx, st, p))) return false;
-        const Segment &s = g.seg[pc.seg];
+        const Segment &s = g.seg[d.seg];
         const char *rows = reinterpret_cast<const char *>(sm.ring + c.offset[cidx % kQueue]);
-        rows_dot<true>(rows, s.dtype, cols, pc.nrows, in, c);
-        epilogue(g, pc.seg, pc.row0, pc.nrows, info, c, e);
+        rows_dot<true>(rows, s.dtype, cols, d.nrows, in, c);
+        epilogue(g, d.seg, d.row0, d.nrows, info, c, e);
         consumed();
     }
     if (g.epilogue == EPI_LOGITS) finish_logits(st, c, e);
@@ -614,6 +556,13 @@ __device__ void gemv_direct(const GemvPhase &g, StepState *st, const StepInfo &i
 }
 
 // ---- grouped-query attention ------------------------------------------------------
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+}
+
 __device__ __forceinline__ void rope_pair(float &u, float &v, float angle) {
     const float c = cosf(angle), s = sinf(angle);
     const float a = __fsub_rn(__fmul_rn(u, c), __fmul_rn(v, s));
@@ -623,8 +572,9 @@ __device__ __forceinline__ void rope_pair(float &u, float &v, float angle) {
 }
 
 // In-place per-head RMSNorm (optional) + RoPE of a [dim] vector held by one warp
-// in shared memory (kernels.cl rms 19-28 then rope 30-44).
-__device__ void norm_rope_warp(float *v, int dim, const void *gain, int gain_dtype, float eps, bool do_norm,
+// in shared memory (kernels.cl rms 19-28 then rope 30-44).  `gain` is in
+// shared memory (float) or NULL.
+__device__ void norm_rope_warp(float *v, int dim, const float *gain, float eps, bool do_norm,
                                const float *inv_freq, float position, int split_half) {
     const int lane = threadIdx.x & 31;
     if (do_norm) {
@@ -632,10 +582,7 @@ __device__ void norm_rope_warp(float *v, int dim, const void *gain, int gain_dty
         for (int j = lane; j < dim; j += 32) ss = fmaf(v[j], v[j], ss);
         ss = warp_sum(ss);
         const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
-        for (int j = lane; j < dim; j += 32) {
-            const float gn = gain ? load_weight(gain, gain_dtype, j) : 1.0f;
-            v[j] = __fmul_rn(__fmul_rn(v[j], scale), gn);
-        }
+        for (int j = lane; j < dim; j += 32) v[j] = __fmul_rn(__fmul_rn(v[j], scale), gain ? gain[j] : 1.0f);
         __syncwarp();
     }
     const int half = dim / 2;
@@ -649,9 +596,12 @@ __device__ void norm_rope_warp(float *v, int dim, const void *gain, int gain_dty
     __syncwarp();
 }
 
-// Work unit = (KV head g, chunk c of the attended rows): an online-softmax
-// pass over the chunk's keys for the group's query heads; writes the chunk's
-// (acc, max, sum) for the consumer to merge.
+// Work unit = (KV head g, chunk c of the attended rows): one pass over the
+// chunk's keys (in tiles of kKeyTile) for the group's query heads; writes the
+// chunk's (acc, max, sum) for the consumer to merge.  All of a tile's global
+// reads are issued at once with cp.async; the newest row (this token's key and
+// value, appended to the ring by the unit that owns it) is patched into the
+// tile in shared memory.
 __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const Smem &sm) {
     const int G = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -677,42 +627,26 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
     float *lrow = mrow + gq;                           // [gq]
     float *corr = lrow + gq;                           // [gq]
     float *knew = corr + gq;                           // [d]
+    float *gains = sm.c->y[1];                         // q gain [d], k gain [d] (kRowBatch >= 2 * 128)
 
     for (int unit = blockIdx.x; unit < a.kv_heads * chunks; unit += G) {
         const int g = unit / chunks, c = unit % chunks;
         const int t0 = c * chunk_len, t1 = min(total, t0 + chunk_len);
-        // 1. this group's query heads: RMSNorm + RoPE
-        for (int i = warp; i < gq; i += kEngineWarps) {
-            float *qi = q + i * d;
-            const float *src = a.q_raw + static_cast<size_t>(g * gq + i) * d;
-            for (int j = lane; j < d; j += 32) qi[j] = __ldcg(src + j);
-            __syncwarp();
-            norm_rope_warp(qi, d, a.q_gain, a.gain_dtype, a.norm_eps, a.qk_norm != 0, a.inv_freq, pos_f,
-                           a.split_half);
-        }
-        // 2. the unit owning the newest ring row appends this token's key/value
         const int newest = length - 1;
-        if (newest >= t0 && newest < t1) {
-            const size_t slot = static_cast<size_t>(g) * cap + (count - 1) % cap;
-            if (warp == 0) {
-                const float *src = a.k_raw + static_cast<size_t>(g) * d;
-                for (int j = lane; j < d; j += 32) knew[j] = __ldcg(src + j);
-                __syncwarp();
-                norm_rope_warp(knew, d, a.k_gain, a.gain_dtype, a.norm_eps, a.qk_norm != 0, a.inv_freq, pos_f,
-                               a.split_half);
-                for (int j = lane; j < d; j += 32) a.k_cache[slot * d + j] = knew[j];
-            } else if (warp == 1) {
-                const float *src = a.v_raw + static_cast<size_t>(g) * d;
-                for (int j = lane; j < d; j += 32) a.v_cache[slot * d + j] = __ldcg(src + j);
-            }
-        }
+        const bool owner = newest >= t0 && newest < t1;
+        // 1. issue: the group's raw q rows, the first key/value tile, and (owner) the raw k/v row
+        for (int e = threadIdx.x; e < gq * d; e += blockDim.x) cp_async4(q + e, a.q_raw + static_cast<size_t>(g) * gq * d + e);
+        if (owner)
+            for (int e = threadIdx.x; e < d; e += blockDim.x) cp_async4(knew + e, a.k_raw + static_cast<size_t>(g) * d + e);
+        if (a.qk_norm && a.q_gain)
+            for (int e = threadIdx.x; e < 2 * d; e += blockDim.x)
+                gains[e] = load_weight(e < d ? a.q_gain : a.k_gain, a.gain_dtype, e < d ? e : e - d);
         for (int e = threadIdx.x; e < gq * d; e += blockDim.x) acc[e] = 0.f;
         if (threadIdx.x < gq) {
             mrow[threadIdx.x] = -INFINITY;
             lrow[threadIdx.x] = 0.f;
         }
-        __syncthreads();
-        // 3. key tiles: scores, online softmax, value mix
+        bool first = true;
         for (int tb = t0; tb < t1; tb += kKeyTile) {
             const int nt = min(kKeyTile, t1 - tb);
             for (int e = threadIdx.x; e < nt * d; e += blockDim.x) {
@@ -727,42 +661,93 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
                     kr = a.relay_k + row * d;
                     vr = a.relay_v + row * d;
                 }
-                kt[t * (d + 1) + j] = __ldcg(kr + j);
-                vt[t * d + j] = __ldcg(vr + j);
+                cp_async4(kt + t * (d + 1) + j, kr + j);
+                cp_async4(vt + t * d + j, vr + j);
+            }
+            cp_async_wait_all();
+            __syncthreads();
+            if (first) {
+                // 2. query heads: RMSNorm + RoPE; the owner also finishes this token's key/value
+                const float *qg = (a.qk_norm && a.q_gain) ? gains : nullptr;
+                const float *kg = (a.qk_norm && a.k_gain) ? gains + d : nullptr;
+                for (int i = warp; i < gq; i += kEngineWarps)
+                    norm_rope_warp(q + i * d, d, qg, a.norm_eps, a.qk_norm != 0, a.inv_freq, pos_f, a.split_half);
+                if (owner && warp == kEngineWarps - 1) {
+                    norm_rope_warp(knew, d, kg, a.norm_eps, a.qk_norm != 0, a.inv_freq, pos_f, a.split_half);
+                    const size_t slot = static_cast<size_t>(g) * cap + (count - 1) % cap;
+                    for (int j = lane; j < d; j += 32) a.k_cache[slot * d + j] = knew[j];
+                }
+                if (owner && warp == kEngineWarps - 2) {
+                    const size_t slot = static_cast<size_t>(g) * cap + (count - 1) % cap;
+                    for (int j = lane; j < d; j += 32) a.v_cache[slot * d + j] = __ldcg(a.v_raw + static_cast<size_t>(g) * d + j);
+                }
+                __syncthreads();
+                first = false;
+            }
+            if (owner && newest >= tb && newest < tb + nt) {
+                // the tile holds the ring's previous occupant of the newest slot: patch it
+                const int t = newest - tb;
+                for (int j = threadIdx.x; j < d; j += blockDim.x) {
+                    kt[t * (d + 1) + j] = knew[j];
+                    vt[t * d + j] = __ldcg(a.v_raw + static_cast<size_t>(g) * d + j);
+                }
+                __syncthreads();
+            }
+            // 3. scores (4 independent partial sums per dot product)
+            for (int e = threadIdx.x; e < gq * nt; e += blockDim.x) {
+                const int i = e / nt, t = e % nt;
+                const float *qi = q + i * d, *kr = kt + t * (d + 1);
+                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+                int j = 0;
+                for (; j + 3 < d; j += 4) {
+                    s0 = fmaf(qi[j], kr[j], s0);
+                    s1 = fmaf(qi[j + 1], kr[j + 1], s1);
+                    s2 = fmaf(qi[j + 2], kr[j + 2], s2);
+                    s3 = fmaf(qi[j + 3], kr[j + 3], s3);
+                }
+                for (; j < d; ++j) s0 = fmaf(qi[j], kr[j], s0);
+                p[i * kKeyTile + t] = __fdiv_rn((s0 + s1) + (s2 + s3), sqrt_d);
             }
             __syncthreads();
+            // 4. online softmax per query head
             for (int i = warp; i < gq; i += kEngineWarps) {
-                float s = -INFINITY;
-                if (lane < nt) {
-                    const float *qi = q + i * d, *kr = kt + lane * (d + 1);
-                    float dot = 0.f;
-                    for (int j = 0; j < d; ++j) dot = fmaf(qi[j], kr[j], dot);
-                    s = __fdiv_rn(dot, sqrt_d);
+                float mt = -INFINITY;
+                for (int t = lane; t < nt; t += 32) mt = fmaxf(mt, p[i * kKeyTile + t]);
+                mt = warp_max(mt);
+                const float m_old = mrow[i], m_new = fmaxf(m_old, mt);
+                float sum = 0.f;
+                for (int t = lane; t < nt; t += 32) {
+                    const float e = (m_new == -INFINITY) ? 0.f : expf(p[i * kKeyTile + t] - m_new);
+                    p[i * kKeyTile + t] = e;
+                    sum += e;
                 }
-                const float tile_max = warp_max(s);
-                const float m_old = mrow[i];
-                const float m_new = fmaxf(m_old, tile_max);
-                const float e = (m_new == -INFINITY) ? 0.f : expf(s - m_new);
-                const float tile_sum = warp_sum(e);
-                p[i * kKeyTile + lane] = e;
+                sum = warp_sum(sum);
                 if (lane == 0) {
                     const float cf = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
                     corr[i] = cf;
-                    lrow[i] = lrow[i] * cf + tile_sum;
+                    lrow[i] = lrow[i] * cf + sum;
                     mrow[i] = m_new;
                 }
             }
             __syncthreads();
+            // 5. value mix (4 independent partial sums)
             for (int e = threadIdx.x; e < gq * d; e += blockDim.x) {
                 const int i = e / d, j = e % d;
-                float v = acc[e] * corr[i];
                 const float *pi = p + i * kKeyTile;
-                for (int t = 0; t < nt; ++t) v = fmaf(pi[t], vt[t * d + j], v);
-                acc[e] = v;
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                int t = 0;
+                for (; t + 3 < nt; t += 4) {
+                    a0 = fmaf(pi[t], vt[t * d + j], a0);
+                    a1 = fmaf(pi[t + 1], vt[(t + 1) * d + j], a1);
+                    a2 = fmaf(pi[t + 2], vt[(t + 2) * d + j], a2);
+                    a3 = fmaf(pi[t + 3], vt[(t + 3) * d + j], a3);
+                }
+                for (; t < nt; ++t) a0 = fmaf(pi[t], vt[t * d + j], a0);
+                acc[e] = fmaf(acc[e], corr[i], (a0 + a1) + (a2 + a3));
             }
             __syncthreads();
         }
-        // 4. publish the chunk partial: acc[d], running max, running sum
+        // 6. publish the chunk partial: acc[d], running max, running sum
         for (int e = threadIdx.x; e < gq * d; e += blockDim.x) {
             const int i = e / d, j = e % d;
             a.partial[(static_cast<size_t>(g * gq + i) * kMaxAttnChunks + c) * stride + j] = acc[e];
@@ -788,6 +773,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
               ((static_cast<size_t>(ctl.scratch_floats) * 4 + 127) & ~size_t(127));
     sm.ring_bytes = ctl.ring_bytes;
     Control &c = *sm.c;
+    const int head_phase = nphases - 2;  // the phase list ends with the head, then the step end
     __shared__ StepInfo info;
     __shared__ unsigned long long base;
     __shared__ int skip, need_head;
@@ -812,14 +798,14 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
         if (!skip) {
             for (int i = 0; i < kQueue; ++i) mbar_init(&c.mbar[i], 1);
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-            c.issued = c.consumed = c.head_offset = c.cur_phase = c.cur_piece = 0;
+            c.issued = c.consumed = c.head_offset = 0;
         }
     }
     __syncthreads();
     if (skip) return;
     if (threadIdx.x == 0) {
         if (ctl.trace && blockIdx.x == 0) ctl.trace[0] = global_ns();
-        refill(phases, nphases, need_head != 0, sm);
+        refill(ctl, need_head != 0, head_phase, sm);
     }
     __syncthreads();
     int barriers = 0, cidx = 0;
@@ -829,7 +815,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
         if (ph.kind == PH_STEP_END) break;
         if (ph.layer < 0 && !need_head) continue;
         if (ph.kind == PH_GEMV) {
-            if (ph.gemv.bulk) ok = gemv_bulk(phases, nphases, need_head != 0, p, st, info, sm, cidx);
+            if (ph.gemv.bulk) ok = gemv_bulk(ph.gemv, p, ctl, need_head != 0, head_phase, st, info, sm, cidx);
             else gemv_direct(ph.gemv, st, info, sm);
         } else if (ph.kind == PH_ATTN_GQA) {
             attn_gqa_phase(ph.attn, info, sm);
