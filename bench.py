@@ -305,27 +305,36 @@ def run_trace(args, steps=8):
                                                  context_length=context)
     token = int(np.argmax(model.prefill(syn.prompt_ids(config.vocab_size, prompt_len, seed=1))))
     kinds = ["qkv", "attn", "o", "gate_up", "down"] * config.layers + ["head"]
-    capacity = 1 + len(kinds) * 200
+    stamps_per_cta = 4
+    capacity = 1 + len(kinds) * (200 * stamps_per_cta + 1)
     stamps = (C.c_uint64 * capacity)()
     phases, grid = C.c_int(), C.c_int()
-    per_kind = {}
-    totals = []
+    per_kind, totals = {}, []
     for _ in range(steps):
         native.call("mr_model_trace_decode", model._handle, token, stamps, capacity, C.byref(phases), C.byref(grid))
         g = grid.value
-        t = np.frombuffer(stamps, dtype=np.uint64, count=1 + phases.value * (g + 1)).astype(np.int64)
+        rec = g * stamps_per_cta + 1
+        t = np.frombuffer(stamps, dtype=np.uint64, count=1 + phases.value * rec).astype(np.int64)
         start = t[0]
         for k in range(phases.value):
-            row = t[1 + k * (g + 1): 1 + (k + 1) * (g + 1)]
-            done, exit_ = row[:g], row[g]
-            entry = per_kind.setdefault(kinds[k], {"compute_max": [], "compute_median": [], "barrier": []})
-            entry["compute_max"].append(done.max() - start)
-            entry["compute_median"].append(np.median(done) - start)
-            entry["barrier"].append(exit_ - done.max())
+            row = t[1 + k * rec: 1 + (k + 1) * rec]
+            cta = row[:g * stamps_per_cta].reshape(g, stamps_per_cta) - start
+            exit_ = row[-1]
+            entry = per_kind.setdefault(kinds[k], {"cp0": [], "cp1": [], "cp2": [], "done_median": [],
+                                                   "done_max": [], "barrier": []})
+            for i in range(3):
+                vals = cta[:, i]
+                vals = vals[vals > 0]
+                entry[f"cp{i}"].append(np.median(vals) if len(vals) else 0)
+            entry["done_median"].append(np.median(cta[:, 3]))
+            entry["done_max"].append(cta[:, 3].max())
+            entry["barrier"].append(exit_ - (start + cta[:, 3].max()))
             start = exit_
         totals.append(start - t[0])
     report = {"config": args.config, "position": model.position, "steps": steps,
-              "step_us": round(float(np.median(totals)) / 1e3, 2), "phases": {}}
+              "step_us": round(float(np.median(totals)) / 1e3, 2),
+              "legend": "us from the previous barrier exit, median over CTAs (cp*: GEMV input, norm, weights; "
+                        "attention first tile, q/k, compute)", "phases": {}}
     for kind, entry in per_kind.items():
         report["phases"][kind] = {k: round(float(np.median(v)) / 1e3, 3) for k, v in entry.items()}
         report["phases"][kind]["count_per_step"] = len(entry["barrier"]) // steps

@@ -227,9 +227,12 @@ MR_API int mr_model_last_experts(const mr_model *model, int layer, int loop, int
 MR_API int mr_model_bench_decode(mr_model *model, int first_token, int steps, float *device_ms);
 
 /* Tracing: run one decode step (feeding `token`) with per-phase device
- * timestamps (globaltimer, ns).  Layout: stamps[0] = launch start; for the
- * k-th executed phase, stamps[1 + k*(grid+1) + b] = CTA b finished computing
- * and stamps[1 + k*(grid+1) + grid] = CTA 0 left the phase's grid barrier.
+ * timestamps (globaltimer, ns).  Layout: stamps[0] = launch start; the k-th
+ * executed phase has a record of grid*4 + 1 stamps at 1 + k*(grid*4 + 1):
+ * CTA b's checkpoints at offset b*4 + i (i = 0..2 phase-specific, 3 = done
+ * computing) and CTA 0 leaving the phase's grid barrier at offset grid*4.
+ * GEMV checkpoints: input loaded, input normalised, weights consumed;
+ * attention: first tile loaded, q/k prepared, scores/mix done.
  * *phases receives the number of executed phases, *grid the CTA count.  No
  * reference counterpart (the reference has no tracing). */
 MR_API int mr_model_trace_decode(mr_model *model, int token, uint64_t *stamps, int capacity, int *phases,

@@ -817,7 +817,7 @@ int mr_model_trace_decode(mr_model *m, int token, uint64_t *stamps, int capacity
     MR_REQUIRE(token >= 0 && token < m->cfg.vocab_size, "token outside the vocabulary");
     MR_REQUIRE(m->position + 1 <= m->cfg.context_length, "context_length exceeded");
     const int executed = (int)m->phases.size() - 1;  // every phase but the step end
-    const size_t need = 1 + (size_t)executed * (m->grid + 1);
+    const size_t need = 1 + (size_t)executed * ((size_t)m->grid * kTraceStamps + 1);
     MR_REQUIRE((size_t)capacity >= need, "trace needs %zu stamps", need);
     rc = ensure_feed(m, 1);
     if (rc) return rc;

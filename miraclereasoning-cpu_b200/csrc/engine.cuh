@@ -33,6 +33,7 @@ constexpr int kMaxAttnChunks = 16;   // key chunks per KV head (merged by the co
 constexpr int kKeysPerChunk = 64;    // target keys per attention work unit
 constexpr int kKeyTile = 64;         // keys per attention tile
 constexpr int kSmemLimit = 227 * 1024;
+constexpr int kTraceStamps = 4;
 
 enum PhaseKind : int {
     PH_GEMV = 1,        // y = W x for up to 3 weight segments, then an epilogue
@@ -174,8 +175,9 @@ struct StepControl {
     const int *piece_count;           // [grid]
     int piece_stride;
     // Optional phase trace (globaltimer ns): [0] = launch start (CTA 0); then per
-    // executed phase k, slots 1 + k*(grid+1) + b = CTA b done computing, and
-    // slot 1 + k*(grid+1) + grid = CTA 0 leaving the barrier.  NULL = off.
+    // executed phase k a record of grid*kTraceStamps + 1 slots: CTA b's stamps
+    // at 1 + k*rec + b*kTraceStamps + i (i = 0..2 phase-specific checkpoints,
+    // 3 = done computing) and CTA 0 leaving the barrier at 1 + k*rec + grid*kTraceStamps.
     unsigned long long *trace;
 };
 

@@ -51,6 +51,16 @@ struct StepInfo {
     int position, token, logits_row;
 };
 
+// Phase trace checkpoints (no-ops unless the launch carries a trace buffer).
+struct Tracer {
+    unsigned long long *rec;  // this phase's record, or NULL
+    __device__ void mark(int i) const {
+        if (!rec) return;
+        __syncthreads();
+        if (threadIdx.x == 0) rec[blockIdx.x * kTraceStamps + i] = global_ns();
+    }
+};
+
 struct Smem {
     Control *c;
     float *scratch;
@@ -68,6 +78,43 @@ __device__ __forceinline__ int ceil_div(int a, int b) { return (a + b - 1) / b; 
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- asynchronous copies into shared memory ----------------------------------------------
+// Data written earlier in the same launch by other CTAs is read through L2
+// only (.cg, 16-byte granules); .ca (4-byte) is used only for data written by
+// earlier launches.
+__device__ __forceinline__ void cp_async16_cg(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+}
+// Copy n floats produced in this launch into shared memory: 16-byte .cg
+// granules when both ends are 16-byte aligned and n % 4 == 0, else loads
+// batched in registers (no store-to-load ordering between iterations).
+__device__ void copy_fresh(float *dst, const float *src, int n) {
+    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0 && (n & 3) == 0) {
+        for (int e = threadIdx.x * 4; e < n; e += blockDim.x * 4) cp_async16_cg(dst + e, src + e);
+        cp_async_wait_all();
+        return;
+    }
+    for (int base = 0; base < n; base += 4 * blockDim.x) {
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = base + u * blockDim.x + threadIdx.x;
+            v[u] = e < n ? __ldcg(src + e) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = base + u * blockDim.x + threadIdx.x;
+            if (e < n) dst[e] = v[u];
+        }
+    }
 }
 
 // ---- mbarrier / bulk copy primitives --------------------------------------------------
@@ -388,14 +435,16 @@ __device__ void merge_attention(const AttnMerge &m, int position, float *in, Con
     for (int e = threadIdx.x; e < m.heads * m.dim; e += blockDim.x) {
         const int h = e / m.dim, j = e % m.dim;
         const float *base = m.partial + static_cast<size_t>(h) * kMaxAttnChunks * stride + j;
+        float v[kMaxAttnChunks];
+#pragma unroll
+        for (int cc = 0; cc < kMaxAttnChunks; ++cc) v[cc] = cc < chunks ? __ldcg(base + cc * stride) : 0.f;
         const float *w = c.merge_w + h * kMaxAttnChunks;
         float a0 = 0.f, a1 = 0.f;
-        int cc = 0;
-        for (; cc + 1 < chunks; cc += 2) {
-            a0 = fmaf(w[cc], __ldcg(base + cc * stride), a0);
-            a1 = fmaf(w[cc + 1], __ldcg(base + (cc + 1) * stride), a1);
+#pragma unroll
+        for (int cc = 0; cc < kMaxAttnChunks; cc += 2) {
+            a0 = fmaf(w[cc], v[cc], a0);
+            a1 = fmaf(w[cc + 1], v[cc + 1], a1);
         }
-        if (cc < chunks) a0 = fmaf(w[cc], __ldcg(base + cc * stride), a0);
         in[e] = a0 + a1;
     }
     __syncthreads();
@@ -412,7 +461,7 @@ __device__ void load_input(const GemvPhase &g, int cols, const StepInfo &info, f
     } else if (g.input_kind == IN_ATTN_MERGE) {
         merge_attention(g.merge, info.position, in, c);
     } else {
-        for (int j = threadIdx.x; j < cols; j += blockDim.x) in[j] = __ldcg(g.in + j);
+        copy_fresh(in, g.in, cols);
         __syncthreads();
     }
 }
@@ -468,7 +517,7 @@ __device__ void finish_logits(StepState *st, Control &c, Epi &e) {
 // GEMV whose weights stream through the shared-memory ring.  `cidx` is the
 // index of the next piece of this CTA's stream (the same in every thread).
 __device__ bool gemv_bulk(const GemvPhase &g, int p, const StepControl &ctl, bool need_head, int head_phase,
-                          StepState *st, const StepInfo &info, const Smem &sm, int &cidx) {
+                          StepState *st, const StepInfo &info, const Smem &sm, int &cidx, const Tracer &tr) {
     Control &c = *sm.c;
     const int cols = g.seg[0].cols;
     const PieceDesc *table = cta_pieces(ctl);
@@ -483,6 +532,7 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, const StepControl &ctl, boo
         ++cidx;
     };
     load_input(g, cols, info, in, c);
+    tr.mark(0);
     if (g.norm) {
         float ss = 0.f;
         for (int j = threadIdx.x; j < cols; j += blockDim.x) ss = fmaf(in[j], in[j], ss);
@@ -504,6 +554,7 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, const StepControl &ctl, boo
         if (g.gain_piece) consumed();
         else __syncthreads();
     }
+    tr.mark(1);
     Epi e;
     while (cidx < count) {
         const PieceDesc d = table[cidx];
@@ -515,6 +566,7 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, const StepControl &ctl, boo
         epilogue(g, d.seg, d.row0, d.nrows, info, c, e);
         consumed();
     }
+    tr.mark(2);
     if (g.epilogue == EPI_LOGITS) finish_logits(st, c, e);
     return true;
 }
@@ -556,13 +608,6 @@ __device__ void gemv_direct(const GemvPhase &g, StepState *st, const StepInfo &i
 }
 
 // ---- grouped-query attention ------------------------------------------------------
-__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
-}
-
 __device__ __forceinline__ void rope_pair(float &u, float &v, float angle) {
     const float c = cosf(angle), s = sinf(angle);
     const float a = __fsub_rn(__fmul_rn(u, c), __fmul_rn(v, s));
@@ -602,7 +647,7 @@ __device__ void norm_rope_warp(float *v, int dim, const float *gain, float eps, 
 // reads are issued at once with cp.async; the newest row (this token's key and
 // value, appended to the ring by the unit that owns it) is patched into the
 // tile in shared memory.
-__device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const Smem &sm) {
+__device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const Smem &sm, const Tracer &tr) {
     const int G = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = a.dim, gq = a.heads / a.kv_heads;
@@ -635,9 +680,17 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
         const int newest = length - 1;
         const bool owner = newest >= t0 && newest < t1;
         // 1. issue: the group's raw q rows, the first key/value tile, and (owner) the raw k/v row
-        for (int e = threadIdx.x; e < gq * d; e += blockDim.x) cp_async4(q + e, a.q_raw + static_cast<size_t>(g) * gq * d + e);
-        if (owner)
-            for (int e = threadIdx.x; e < d; e += blockDim.x) cp_async4(knew + e, a.k_raw + static_cast<size_t>(g) * d + e);
+        if ((d & 3) == 0) {
+            for (int e = threadIdx.x * 4; e < gq * d; e += blockDim.x * 4)
+                cp_async16_cg(q + e, a.q_raw + static_cast<size_t>(g) * gq * d + e);
+            if (owner)
+                for (int e = threadIdx.x * 4; e < d; e += blockDim.x * 4)
+                    cp_async16_cg(knew + e, a.k_raw + static_cast<size_t>(g) * d + e);
+        } else {
+            for (int e = threadIdx.x; e < gq * d; e += blockDim.x) q[e] = __ldcg(a.q_raw + static_cast<size_t>(g) * gq * d + e);
+            if (owner)
+                for (int e = threadIdx.x; e < d; e += blockDim.x) knew[e] = __ldcg(a.k_raw + static_cast<size_t>(g) * d + e);
+        }
         if (a.qk_norm && a.q_gain)
             for (int e = threadIdx.x; e < 2 * d; e += blockDim.x)
                 gains[e] = load_weight(e < d ? a.q_gain : a.k_gain, a.gain_dtype, e < d ? e : e - d);
@@ -666,6 +719,7 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
             }
             cp_async_wait_all();
             __syncthreads();
+            if (first) tr.mark(0);
             if (first) {
                 // 2. query heads: RMSNorm + RoPE; the owner also finishes this token's key/value
                 const float *qg = (a.qk_norm && a.q_gain) ? gains : nullptr;
@@ -683,6 +737,7 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
                 }
                 __syncthreads();
                 first = false;
+                tr.mark(1);
             }
             if (owner && newest >= tb && newest < tb + nt) {
                 // the tile holds the ring's previous occupant of the newest slot: patch it
@@ -747,6 +802,7 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
             }
             __syncthreads();
         }
+        tr.mark(2);
         // 6. publish the chunk partial: acc[d], running max, running sum
         for (int e = threadIdx.x; e < gq * d; e += blockDim.x) {
             const int i = e / d, j = e % d;
@@ -814,22 +870,19 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
         const Phase &ph = phases[p];
         if (ph.kind == PH_STEP_END) break;
         if (ph.layer < 0 && !need_head) continue;
+        const Tracer tr{ctl.trace ? ctl.trace + 1 + static_cast<size_t>(barriers) * (gridDim.x * kTraceStamps + 1)
+                                  : nullptr};
         if (ph.kind == PH_GEMV) {
-            if (ph.gemv.bulk) ok = gemv_bulk(ph.gemv, p, ctl, need_head != 0, head_phase, st, info, sm, cidx);
+            if (ph.gemv.bulk) ok = gemv_bulk(ph.gemv, p, ctl, need_head != 0, head_phase, st, info, sm, cidx, tr);
             else gemv_direct(ph.gemv, st, info, sm);
         } else if (ph.kind == PH_ATTN_GQA) {
-            attn_gqa_phase(ph.attn, info, sm);
+            attn_gqa_phase(ph.attn, info, sm, tr);
         }
         if (!ok) break;
-        unsigned long long *stamp =
-            ctl.trace ? ctl.trace + 1 + static_cast<size_t>(barriers) * (gridDim.x + 1) : nullptr;
-        if (stamp) {
-            __syncthreads();
-            if (threadIdx.x == 0) stamp[blockIdx.x] = global_ns();
-        }
+        tr.mark(3);
         ++barriers;
         ok = grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, p, sm);
-        if (ok && stamp && blockIdx.x == 0 && threadIdx.x == 0) stamp[gridDim.x] = global_ns();
+        if (ok && tr.rec && blockIdx.x == 0 && threadIdx.x == 0) tr.rec[gridDim.x * kTraceStamps] = global_ns();
     }
     __syncthreads();
     if (threadIdx.x == 0) drain(sm);  // nothing is in flight on the normal path; bounded either way
