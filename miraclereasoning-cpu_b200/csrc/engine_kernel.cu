@@ -663,15 +663,17 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
     const float sqrt_d = __fsqrt_rn(static_cast<float>(d));  // divisor, kernels.cl:72
     const int stride = d + 2;
 
+    // q and knew first: 16-byte cp.async targets (scratch is 128-byte aligned,
+    // gq*d is a multiple of 4 whenever d is)
     float *q = sm.scratch;                             // [gq][d]
-    float *kt = q + gq * d;                            // [kKeyTile][d+1]
+    float *knew = q + gq * d;                          // [d]
+    float *kt = knew + d;                              // [kKeyTile][d+1]
     float *vt = kt + kKeyTile * (d + 1);               // [kKeyTile][d]
     float *p = vt + kKeyTile * d;                      // [gq][kKeyTile]
     float *acc = p + gq * kKeyTile;                    // [gq][d]
     float *mrow = acc + gq * d;                        // [gq]
     float *lrow = mrow + gq;                           // [gq]
     float *corr = lrow + gq;                           // [gq]
-    float *knew = corr + gq;                           // [d]
     float *gains = sm.c->y[1];                         // q gain [d], k gain [d] (kRowBatch >= 2 * 128)
 
     for (int unit = blockIdx.x; unit < a.kv_heads * chunks; unit += G) {
