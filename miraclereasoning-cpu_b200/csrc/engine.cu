@@ -376,10 +376,7 @@ int build_pieces(mr_model *m) {
             PieceDesc d{};
             d.src = static_cast<const char *>(seg.w) + row_bytes * row0;
             d.bytes = (uint32_t)(row_bytes * n);
-            d.row0 = row0;
-            d.seg = (short)s;
-            d.nrows = (short)n;
-            d.phase = (short)p;
+            d.phase = (int)p;
             v.push_back(d);
         };
         for (int b = 0; b < G; ++b) {
@@ -388,8 +385,7 @@ int build_pieces(mr_model *m) {
                 PieceDesc d{};
                 d.src = g.norm_gain;
                 d.bytes = gain_bytes;
-                d.seg = -1;
-                d.phase = (short)p;
+                d.phase = (int)p;
                 v.push_back(d);
             }
             const bool paired = g.epilogue == EPI_SWIGLU;
@@ -461,7 +457,7 @@ int launch_step(mr_model *m, const StepControl &ctl) {
     void *args[] = {&m->d_phases, &nphases, &m->state, &control};
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(m->grid);
-    cfg.blockDim = dim3(kEngineThreads);
+    cfg.blockDim = dim3(kBlockThreads);
     cfg.dynamicSmemBytes = m->smem_bytes;
     cfg.stream = m->ctx->stream;
     cudaLaunchAttribute attr[1];
@@ -630,7 +626,7 @@ int mr_model_finalize(mr_model *m) {
     int max_cols = 0;
     for (auto &kv : m->tensors)
         if (kv.second.shape.size() == 2) max_cols = std::max(max_cols, (int)kv.second.shape[1]);
-    m->scratch_floats = std::max(max_cols, attn_scratch_floats(gq_max, d));
+    m->scratch_floats = std::max(max_cols, attn_layout(gq_max, d).total);
     const size_t control = decode_control_bytes();
     const size_t scratch = ((size_t)m->scratch_floats * 4 + 127) & ~size_t(127);
     const long long ring = (long long)kSmemLimit - 1024 - (long long)control - (long long)scratch;
@@ -674,7 +670,7 @@ int mr_model_finalize(mr_model *m) {
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem_bytes));
     int per_sm = 0;
     MR_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reinterpret_cast<const void *>(decode_step_kernel),
-                                                              kEngineThreads, m->smem_bytes));
+                                                              kBlockThreads, m->smem_bytes));
     MR_REQUIRE(per_sm >= 1, "decode kernel cannot be resident (occupancy 0)");
     MR_CUDA_TRY(cudaEventCreate(&m->ev0));
     MR_CUDA_TRY(cudaEventCreate(&m->ev1));

@@ -10,22 +10,24 @@
 // inside a phase each CTA takes its share of the work.
 //
 // Weight streaming: every CTA owns a fixed row range of each weight segment.
-// Thread 0 of each CTA walks the CTA's slices of all weight-streaming phases
-// of the step, in order, as "pieces" (whole rows of one segment, or a norm
-// gain vector) and copies them with TMA bulk copies (cp.async.bulk + one
-// mbarrier per piece) into a shared-memory byte ring, as far ahead as the ring
-// has room -- across phase boundaries and grid barriers.  The compute of a
-// phase then reads its weights from shared memory, so the only global round
-// trips left on the critical path are the phase's input vector and the
-// barrier.
+// A dedicated producer warp walks the CTA's slices of all weight-streaming
+// phases of the step, in order, as "pieces" (whole rows of one segment, or a
+// norm gain vector) and copies them with TMA bulk copies (cp.async.bulk, one
+// "full" mbarrier per piece) into a shared-memory byte ring, as far ahead as
+// the ring has room -- across phase boundaries and grid barriers.  The 16
+// compute warps consume the pieces in the same order and hand each slot back
+// through an "empty" mbarrier.  The compute of a phase reads its weights from
+// shared memory, so the only global round trips left on its critical path are
+// the phase's input vector and the barrier.
 #pragma once
 
 #include "common.cuh"
 
 namespace mr {
 
-constexpr int kEngineThreads = 512;  // 16 warps per CTA, one CTA per SM
+constexpr int kEngineThreads = 512;  // compute warps per CTA (16), one CTA per SM
 constexpr int kEngineWarps = kEngineThreads / 32;
+constexpr int kBlockThreads = kEngineThreads + 32;  // + the weight-stream producer warp
 constexpr int kMaxSegments = 3;
 constexpr int kRowBatch = 256;       // rows of one piece (and of one direct-load batch)
 constexpr int kQueue = 32;           // pieces in flight per CTA (one mbarrier each)
@@ -110,22 +112,23 @@ struct AttnPhase {
 
 // One bulk copy of a CTA's weight stream, precomputed on the host: the CTA's
 // pieces of every weight-streaming phase of a step, in consumption order.
-struct PieceDesc {
+// 16 bytes, so the producer fetches each with one vector load.
+struct alignas(16) PieceDesc {
     const void *src;    // global source (16-byte aligned)
     uint32_t bytes;     // multiple of 16
-    int row0;           // first row (weight pieces)
-    short seg;          // segment index, -1 = the phase's norm gain vector
-    short nrows;
-    short phase;        // index in the phase list
-    short pad;
+    int phase;          // index in the phase list
 };
+static_assert(sizeof(PieceDesc) == 16, "PieceDesc is one 16-byte load");
 
-struct Phase {
+// 16-byte aligned and sized: the kernel prefetches the next phase into shared
+// memory with 16-byte asynchronous copies.
+struct alignas(16) Phase {
     int kind;
     int layer;                      // -1: the output head (skipped when no logits are needed)
     GemvPhase gemv;
     AttnPhase attn;
 };
+static_assert(sizeof(Phase) % 16 == 0, "Phase must be a whole number of 16-byte granules");
 
 // Attention work split: chunks of keys per KV head (same formula in the
 // attention phase and in the merge that consumes its partials).
@@ -137,10 +140,32 @@ __host__ __device__ inline int attn_chunks(int total_keys, int kv_heads, int gri
     return chunks < 1 ? 1 : chunks;
 }
 
-// Shared-memory scratch (floats) the attention phase needs for one KV group.
-__host__ __device__ inline int attn_scratch_floats(int group_heads, int dim) {
-    return 2 * group_heads * dim + kKeyTile * (dim + 1) + kKeyTile * dim + group_heads * kKeyTile +
-           3 * group_heads + dim;
+// Shared-memory scratch carve-up (float offsets) of the attention phase for
+// one KV group.  Every array starts on a 16-byte boundary; key rows are
+// padded to dim + 4 floats so that float4 reads of 8 consecutive keys hit 32
+// distinct banks.
+struct AttnLayout {
+    int q, knew, vnew, kt, vt, p, acc, m, l, corr, total;
+    int kstride, vstride;
+};
+__host__ __device__ inline int round4(int x) { return (x + 3) & ~3; }
+__host__ __device__ inline AttnLayout attn_layout(int group_heads, int dim) {
+    AttnLayout L;
+    L.kstride = round4(dim) + 4;
+    L.vstride = round4(dim);
+    int o = 0;
+    L.q = o;    o += round4(group_heads * dim);   // [gq][dim]
+    L.knew = o; o += round4(dim);                 // this token's key
+    L.vnew = o; o += round4(dim);                 // this token's value
+    L.kt = o;   o += kKeyTile * L.kstride;        // key tile
+    L.vt = o;   o += kKeyTile * L.vstride;        // value tile
+    L.p = o;    o += round4(group_heads * kKeyTile);
+    L.acc = o;  o += round4(group_heads * dim);
+    L.m = o;    o += round4(group_heads);
+    L.l = o;    o += round4(group_heads);
+    L.corr = o; o += round4(group_heads);
+    L.total = o;
+    return L;
 }
 
 // Device-resident state of the running sequence, advanced by the decode

@@ -11,12 +11,20 @@
 //             merged (softmax-rescaled) by the next GEMV phase as it loads
 //             its input.
 //
-// Weight streaming (see engine.cuh): thread 0 is the producer of a
-// shared-memory byte ring fed by TMA bulk copies (cp.async.bulk, completion
-// on one mbarrier per piece); every thread consumes pieces in the same order.
+// CTA layout: warps 0-15 compute (they synchronise among themselves with
+// named barrier 1, never with __syncthreads), warp 16 is the weight-stream
+// producer.  The producer walks the CTA's piece table (engine.cuh) and issues
+// TMA bulk copies (cp.async.bulk) into a shared-memory byte ring, each piece
+// completing a "full" mbarrier; the compute warps consume the pieces in the
+// same order -- they derive the order from the phase list, so only the ring
+// offset passes between the two sides -- and return each slot through an
+// "empty" mbarrier.  The producer runs ahead across phases and grid barriers
+// as far as the ring has room, so a phase normally finds its weights already
+// in shared memory.
+//
 // All waits are bounded (2 s): a wait that gives up records an error code in
-// StepState, every CTA drains its in-flight copies (bounded) and returns, and
-// the host raises.
+// StepState, the compute warps stop, the producer waits (bounded) for its
+// copies in flight, and the host raises.
 //
 // Numerics: weights are widened from their stored dtype exactly as the
 // reference widens them; all arithmetic is float32.  Dot products and the
@@ -30,33 +38,49 @@ namespace mr {
 namespace {
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
-constexpr int kMaxMergeHeads = 64;
+constexpr int kMaxHeadDim = 128;
 
 // Fixed part of the dynamic shared memory; the scratch floats and the weight
 // ring follow it.
 struct Control {
-    unsigned long long mbar[kQueue];
-    int offset[kQueue];
+    unsigned long long full[kQueue];   // piece landed (producer expect_tx + bulk-copy bytes)
+    unsigned long long empty[kQueue];  // piece consumed (compute thread 0 arrives)
+    Phase phase[2];                    // current and next phase descriptor
+    int offset[kQueue];                // ring offset of each piece in flight (producer writes)
     float partial[kEngineWarps * kEngineWarps];
-    float y[2][kRowBatch];   // y[0]: rows of the current piece; y[1]: gate rows (SwiGLU)
+    float y[2][kRowBatch];             // dot products of alternate pieces
+    float gate[kRowBatch];             // SwiGLU gate rows of the current row batch
+    float xres[kRowBatch];             // this CTA's residual rows, fetched with the phase input
+    float gains[2 * kMaxHeadDim];      // attention q / k norm gains
     float red[kEngineWarps];
-    float merge_w[kMaxMergeHeads * kMaxAttnChunks];
     unsigned long long best[kEngineWarps];
-    int flag, ok;
-    // producer state (written by thread 0 only)
-    int issued, consumed, head_offset;
+    int ok;
+    int abort;                         // the compute warps stopped: the producer stops too
 };
 
 struct StepInfo {
     int position, token, logits_row;
 };
 
+// ---- compute-warp synchronisation (named barrier 1, the 512 compute threads) ----------
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kEngineThreads) : "memory"); }
+// Barrier that also ANDs a predicate over the compute threads.
+__device__ __forceinline__ bool csync_and(bool v) {
+    int r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.and.pred q, 1, %2, p;\n selp.s32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"(static_cast<int>(v)), "n"(kEngineThreads)
+        : "memory");
+    return r != 0;
+}
+
 // Phase trace checkpoints (no-ops unless the launch carries a trace buffer).
 struct Tracer {
     unsigned long long *rec;  // this phase's record, or NULL
     __device__ void mark(int i) const {
         if (!rec) return;
-        __syncthreads();
+        csync();
         if (threadIdx.x == 0) rec[blockIdx.x * kTraceStamps + i] = global_ns();
     }
 };
@@ -74,7 +98,6 @@ __device__ __forceinline__ void row_range(int rows, int b, int g, int &r0, int &
 }
 
 __device__ __forceinline__ int esize(int dtype) { return dtype == MR_DTYPE_F32 ? 4 : 2; }
-__device__ __forceinline__ int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -90,31 +113,18 @@ __device__ __forceinline__ void cp_async16_cg(void *dst, const void *src) {
 __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
 }
-// Copy n floats produced in this launch into shared memory: 16-byte .cg
-// granules when both ends are 16-byte aligned and n % 4 == 0, else loads
-// batched in registers (no store-to-load ordering between iterations).
-__device__ void copy_fresh(float *dst, const float *src, int n) {
-    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0 && (n & 3) == 0) {
-        for (int e = threadIdx.x * 4; e < n; e += blockDim.x * 4) cp_async16_cg(dst + e, src + e);
-        cp_async_wait_all();
-        return;
-    }
-    for (int base = 0; base < n; base += 4 * blockDim.x) {
-        float v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int e = base + u * blockDim.x + threadIdx.x;
-            v[u] = e < n ? __ldcg(src + e) : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int e = base + u * blockDim.x + threadIdx.x;
-            if (e < n) dst[e] = v[u];
-        }
-    }
+
+// Prefetch a phase descriptor into shared memory (completed by the next
+// cp_async_wait_all of each thread plus a compute barrier).
+__device__ void fetch_phase(Phase *dst, const Phase *src) {
+    constexpr int kGranules = static_cast<int>(sizeof(Phase) / 16);
+    for (int i = threadIdx.x; i < kGranules; i += kEngineThreads)
+        cp_async16_cg(reinterpret_cast<char *>(dst) + 16 * i, reinterpret_cast<const char *>(src) + 16 * i);
+    cp_async_commit();
 }
 
 // ---- mbarrier / bulk copy primitives --------------------------------------------------
@@ -130,6 +140,9 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, int parit
         : "memory");
     return ok != 0;
 }
+__device__ __forceinline__ void mbar_arrive(unsigned long long *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, unsigned long long *bar) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                  : "memory");
@@ -140,60 +153,17 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         : "memory");
 }
 
-// ---- piece stream (host-precomputed table, see PieceDesc) ---------------------------
-__device__ __forceinline__ const PieceDesc *cta_pieces(const StepControl &ctl) {
-    return ctl.pieces + static_cast<size_t>(blockIdx.x) * ctl.piece_stride;
-}
-
-// Producer (thread 0): issue the next pieces of this CTA's stream while the
-// ring and the mbarrier queue have room.  Pieces of the head phase are only
-// streamed when this step computes logits.
-__device__ void refill(const StepControl &ctl, bool need_head, int head_phase, const Smem &sm) {
-    Control &c = *sm.c;
-    const PieceDesc *table = cta_pieces(ctl);
-    const int count = ctl.piece_count[blockIdx.x];
-    bool fenced = false;
-    while (c.issued < count && c.issued - c.consumed < kQueue) {
-        const PieceDesc d = table[c.issued];
-        if (!need_head && d.phase == head_phase) return;
-        const int bytes = static_cast<int>(d.bytes);
-        int off;
-        if (c.issued == c.consumed) {
-            off = 0;
-        } else {
-            const int head = c.head_offset, tail = c.offset[c.consumed % kQueue];
-            if (head == tail) return;  // full
-            if (head > tail) {
-                if (head + bytes <= sm.ring_bytes) off = head;
-                else if (bytes <= tail) off = 0;
-                else return;
-            } else {
-                if (head + bytes <= tail) off = head;
-                else return;
-            }
-        }
-        if (!fenced) {
-            // the region may have been read through the generic proxy
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            fenced = true;
-        }
-        const int slot = c.issued % kQueue;
-        c.offset[slot] = off;
-        bulk_load(sm.ring + off, d.src, d.bytes, &c.mbar[slot]);
-        c.head_offset = off + bytes;
-        ++c.issued;
-    }
-}
-
-// Bounded wait for piece `idx` (all threads).
-__device__ bool wait_piece(const Smem &sm, int idx, StepState *st, int phase) {
-    unsigned long long *bar = &sm.c->mbar[idx % kQueue];
-    const int parity = (idx / kQueue) & 1;
+// Bounded wait on one phase of an mbarrier.  Gives up when another wait has
+// already recorded an error, when the compute warps stopped (`watch_abort`),
+// or after kWaitLimitNs (recording 1000 + phase).
+__device__ bool wait_bar(unsigned long long *bar, int parity, StepState *st, const Control &c, int phase,
+                         bool watch_abort) {
     uint64_t start = 0;
     for (unsigned spin = 0;; ++spin) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((spin & 255u) == 255u) {
-            if (*reinterpret_cast<volatile int *>(&st->error)) return false;
+            if (*reinterpret_cast<volatile const int *>(&st->error)) return false;
+            if (watch_abort && *reinterpret_cast<volatile const int *>(&c.abort)) return false;
             const uint64_t now = global_ns();
             if (!start) {
                 start = now;
@@ -205,23 +175,99 @@ __device__ bool wait_piece(const Smem &sm, int idx, StepState *st, int phase) {
     }
 }
 
-// Thread 0, on exit: wait (bounded) for every issued copy so that no bulk copy
-// writes into shared memory after the CTA has left.
-__device__ void drain(const Smem &sm) {
+// ---- the weight-stream producer (lane 0 of warp 16) -----------------------------------
+__device__ __forceinline__ uint4 ld_desc(const PieceDesc *table, int i, int count) {
+    if (i >= count) return make_uint4(0u, 0u, 0u, 0u);
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(table + i));
+    return v;
+}
+
+// Issues every piece of this CTA's stream (up to the head phase when no
+// logits are needed) into the ring, allocating ring bytes first-fit in
+// stream order: a piece goes after the newest one, or wraps to offset 0, once
+// the pieces it would overwrite have been consumed.  Descriptors are loaded
+// four pieces ahead.  Before returning, waits (bounded) until every issued
+// copy has landed, so that no copy writes shared memory after the CTA exits.
+__device__ void produce(const StepControl &ctl, bool need_head, int head_phase, StepState *st, const Smem &sm) {
     Control &c = *sm.c;
-    const uint64_t start = global_ns();
-    for (int idx = c.consumed; idx < c.issued; ++idx) {
-        while (!mbar_try_wait(&c.mbar[idx % kQueue], (idx / kQueue) & 1)) {
-            if (global_ns() - start > kWaitLimitNs) return;
+    const PieceDesc *table = ctl.pieces + static_cast<size_t>(blockIdx.x) * ctl.piece_stride;
+    const int count = ctl.piece_count[blockIdx.x];
+    uint4 q0 = ld_desc(table, 0, count), q1 = ld_desc(table, 1, count), q2 = ld_desc(table, 2, count),
+          q3 = ld_desc(table, 3, count);
+    int tail = 0, head_off = 0, issued = 0;
+    bool ok = true;
+    while (ok && issued < count) {
+        const uint4 d = q0;
+        q0 = q1;
+        q1 = q2;
+        q2 = q3;
+        q3 = ld_desc(table, issued + 4, count);
+        const void *src = reinterpret_cast<const void *>((static_cast<unsigned long long>(d.y) << 32) | d.x);
+        const int bytes = static_cast<int>(d.z), phase = static_cast<int>(d.w);
+        if (!need_head && phase == head_phase) break;
+        // a free mbarrier slot: piece issued - kQueue must have been consumed
+        while (ok && tail <= issued - kQueue) {
+            ok = wait_bar(&c.empty[tail % kQueue], (tail / kQueue) & 1, st, c, phase, true);
+            ++tail;
         }
+        int off = 0;
+        while (ok) {
+            if (tail == issued) {  // nothing in flight: the ring is empty
+                off = 0;
+                break;
+            }
+            const int tail_off = c.offset[tail % kQueue];
+            if (head_off > tail_off) {
+                if (head_off + bytes <= sm.ring_bytes) {
+                    off = head_off;
+                    break;
+                }
+                if (bytes <= tail_off) {
+                    off = 0;
+                    break;
+                }
+            } else if (head_off < tail_off && head_off + bytes <= tail_off) {
+                off = head_off;
+                break;
+            }
+            ok = wait_bar(&c.empty[tail % kQueue], (tail / kQueue) & 1, st, c, phase, true);
+            ++tail;
+        }
+        if (!ok) break;
+        const int slot = issued % kQueue;
+        c.offset[slot] = off;
+        // the region was last read through the generic proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        bulk_load(sm.ring + off, src, static_cast<uint32_t>(bytes), &c.full[slot]);
+        head_off = off + bytes;
+        ++issued;
+    }
+    const uint64_t start = global_ns();
+    for (int j = max(tail, issued - kQueue); j < issued; ++j) {
+        while (!mbar_try_wait(&c.full[j % kQueue], (j / kQueue) & 1))
+            if (global_ns() - start > kWaitLimitNs) return;
     }
 }
 
+// Consumer side: bounded wait for piece `idx`, agreed by every compute thread.
+__device__ bool take_piece(Control &c, int idx, StepState *st, int phase) {
+    const bool ok = csync_and(wait_bar(&c.full[idx % kQueue], (idx / kQueue) & 1, st, c, phase, false));
+    if (!ok && threadIdx.x == 0) c.abort = 1;
+    return ok;
+}
+// Every compute thread has passed a compute barrier since its last read of the piece.
+__device__ __forceinline__ void release_piece(Control &c, int idx) {
+    if (threadIdx.x == 0) mbar_arrive(&c.empty[idx % kQueue]);
+}
+
 // ---- grid barrier ------------------------------------------------------------------
-// Release-add arrival (cumulative over the CTA's writes ordered by bar.sync),
-// acquire polling by thread 0, bounded by kWaitLimitNs.
-__device__ bool grid_barrier(StepState *st, unsigned long long target, int phase, const Smem &sm) {
-    __syncthreads();
+// Release-add arrival (cumulative over the CTA's writes ordered by the compute
+// barrier), acquire polling by thread 0, bounded by kWaitLimitNs.
+__device__ bool grid_barrier(StepState *st, unsigned long long target, int phase, Control &c) {
+    csync();
     if (threadIdx.x == 0) {
         int ok = 1;
         asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(&st->barrier) : "memory");
@@ -243,27 +289,23 @@ __device__ bool grid_barrier(StepState *st, unsigned long long target, int phase
                 }
             }
         }
-        sm.c->ok = ok;
+        c.ok = ok;
+        if (!ok) c.abort = 1;
     }
-    __syncthreads();
-    return sm.c->ok != 0;
+    csync();
+    return c.ok != 0;
 }
 
-// Deterministic block sum (same order in every CTA -> identical bits).
+// Block sum in a fixed order (identical bits in every thread and CTA).  The
+// caller separates two calls by at least one compute barrier.
 __device__ float block_sum(float v, Control &c) {
     v = warp_sum(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();
     if (lane == 0) c.red[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-        float total = lane < kEngineWarps ? c.red[lane] : 0.f;
-        total = warp_sum(total);
-        if (lane == 0) c.red[0] = total;
-    }
-    __syncthreads();
-    const float total = c.red[0];
-    __syncthreads();
+    csync();
+    float total = 0.f;
+#pragma unroll
+    for (int w = 0; w < kEngineWarps; ++w) total += c.red[w];
     return total;
 }
 
@@ -383,20 +425,21 @@ __device__ float row_partial_any(int dtype, const char *rp, int cols, int first,
     }
 }
 
-// y[i] = row_i . x for i < n (n <= kRowBatch) into c.y[0]; rows start at `base`
-// with stride row_bytes.  Many rows: one warp per row.  Few rows: several
-// warps split each row and their partials are summed in a fixed order.
+// y[i] = row_i . x for i < n (n <= kRowBatch); rows start at `base` with
+// stride row_bytes.  Many rows: one warp per row.  Few rows: several warps
+// split each row and their partials are summed in a fixed order.  Ends with a
+// compute barrier, after which every read of `base` has completed.
 template <bool FROM_SMEM>
-__device__ void rows_dot(const char *base, int dtype, int cols, int n, const float *x, Control &c) {
+__device__ void rows_dot(const char *base, int dtype, int cols, int n, const float *x, float *y, Control &c) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t row_bytes = static_cast<size_t>(cols) * esize(dtype);
     if (n >= kEngineWarps) {
         for (int i = warp; i < n; i += kEngineWarps) {
             float acc = row_partial_any<FROM_SMEM>(dtype, base + i * row_bytes, cols, lane, 32, lane, x);
             acc = warp_sum(acc);
-            if (lane == 0) c.y[0][i] = acc;
+            if (lane == 0) y[i] = acc;
         }
-        __syncthreads();
+        csync();
         return;
     }
     const int wpr = kEngineWarps / n;
@@ -407,63 +450,104 @@ __device__ void rows_dot(const char *base, int dtype, int cols, int n, const flo
         acc = warp_sum(acc);
         if (lane == 0) c.partial[i * wpr + part] = acc;
     }
-    __syncthreads();
+    csync();
     if (threadIdx.x < n) {
         float total = 0.f;
         for (int p = 0; p < wpr; ++p) total += c.partial[threadIdx.x * wpr + p];
-        c.y[0][threadIdx.x] = total;
+        y[threadIdx.x] = total;
     }
-    __syncthreads();
+    csync();
 }
 
 // ---- GEMV phases ----------------------------------------------------------------------
-__device__ void merge_attention(const AttnMerge &m, int position, float *in, Control &c) {
+// Softmax-merge of the attention chunk partials into the attention output
+// (the O projection's input).  One warp per head; every load of a head (each
+// chunk's running max and sum, and up to 64 lanes' worth of accumulators) is
+// issued before the first use, so a head costs one L2 round trip for dim <= 64.
+__device__ void merge_attention(const AttnMerge &m, int position, float *in) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int total = min(position + 1, m.capacity) + (m.relay_count ? __ldcg(m.relay_count) : 0);
     const int chunks = attn_chunks(total, m.kv_heads, gridDim.x);
-    const int stride = m.dim + 2;
+    const int d = m.dim, stride = d + 2;
     for (int h = warp; h < m.heads; h += kEngineWarps) {
         const float *base = m.partial + static_cast<size_t>(h) * kMaxAttnChunks * stride;
-        const float mc = lane < chunks ? __ldcg(base + lane * stride + m.dim) : -INFINITY;
-        const float lc = lane < chunks ? __ldcg(base + lane * stride + m.dim + 1) : 0.f;
-        const float mx = warp_max(mc);
-        const float w = (mc == -INFINITY) ? 0.f : expf(mc - mx);
-        const float den = warp_sum(w * lc);
-        if (lane < kMaxAttnChunks) c.merge_w[h * kMaxAttnChunks + lane] = lane < chunks ? w / den : 0.f;
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < m.heads * m.dim; e += blockDim.x) {
-        const int h = e / m.dim, j = e % m.dim;
-        const float *base = m.partial + static_cast<size_t>(h) * kMaxAttnChunks * stride + j;
-        float v[kMaxAttnChunks];
+        for (int j0 = 0; j0 < d; j0 += 64) {
+            const int ja = j0 + lane, jb = j0 + 32 + lane;
+            const float mc = lane < chunks ? __ldcg(base + lane * stride + d) : -INFINITY;
+            const float lc = lane < chunks ? __ldcg(base + lane * stride + d + 1) : 0.f;
+            float va[kMaxAttnChunks], vb[kMaxAttnChunks];
 #pragma unroll
-        for (int cc = 0; cc < kMaxAttnChunks; ++cc) v[cc] = cc < chunks ? __ldcg(base + cc * stride) : 0.f;
-        const float *w = c.merge_w + h * kMaxAttnChunks;
-        float a0 = 0.f, a1 = 0.f;
+            for (int cc = 0; cc < kMaxAttnChunks; ++cc) {
+                va[cc] = (cc < chunks && ja < d) ? __ldcg(base + cc * stride + ja) : 0.f;
+                vb[cc] = (cc < chunks && jb < d) ? __ldcg(base + cc * stride + jb) : 0.f;
+            }
+            const float mx = warp_max(mc);
+            float w = (mc == -INFINITY) ? 0.f : expf(mc - mx);
+            const float den = warp_sum(w * lc);
+            w = w / den;
+            float a = 0.f, b = 0.f;
 #pragma unroll
-        for (int cc = 0; cc < kMaxAttnChunks; cc += 2) {
-            a0 = fmaf(w[cc], v[cc], a0);
-            a1 = fmaf(w[cc + 1], v[cc + 1], a1);
+            for (int cc = 0; cc < kMaxAttnChunks; ++cc) {
+                const float wc = __shfl_sync(0xffffffffu, w, cc);
+                a = fmaf(wc, va[cc], a);
+                b = fmaf(wc, vb[cc], b);
+            }
+            if (ja < d) in[h * d + ja] = a;
+            if (jb < d) in[h * d + jb] = b;
         }
-        in[e] = a0 + a1;
     }
-    __syncthreads();
 }
 
-__device__ void load_input(const GemvPhase &g, int cols, const StepInfo &info, float *in, Control &c) {
+// Loads a GEMV phase's input vector into `in`; ends with a compute barrier.
+// `pre` runs between issuing the asynchronous loads and waiting for them.
+template <typename Pre>
+__device__ void load_input(const GemvPhase &g, int cols, const StepInfo &info, float *in, Pre pre) {
     if (g.input_kind == IN_EMBED_ROW) {
-        for (int j = threadIdx.x; j < cols; j += blockDim.x) {
+        pre();
+        for (int j = threadIdx.x; j < cols; j += kEngineThreads) {
             const float v = load_weight(g.embed, g.embed_dtype, static_cast<size_t>(info.token) * cols + j);
             in[j] = v;
             if (g.embed_copy && blockIdx.x == 0) g.embed_copy[j] = v;
         }
-        __syncthreads();
     } else if (g.input_kind == IN_ATTN_MERGE) {
-        merge_attention(g.merge, info.position, in, c);
+        pre();
+        merge_attention(g.merge, info.position, in);
+    } else if (((reinterpret_cast<uintptr_t>(g.in) | reinterpret_cast<uintptr_t>(in)) & 15) == 0 && (cols & 3) == 0) {
+        for (int e = threadIdx.x * 4; e < cols; e += kEngineThreads * 4) cp_async16_cg(in + e, g.in + e);
+        pre();
     } else {
-        copy_fresh(in, g.in, cols);
-        __syncthreads();
+        pre();
+        for (int base = 0; base < cols; base += 4 * kEngineThreads) {
+            float v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = base + u * kEngineThreads + threadIdx.x;
+                v[u] = e < cols ? __ldcg(g.in + e) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = base + u * kEngineThreads + threadIdx.x;
+                if (e < cols) in[e] = v[u];
+            }
+        }
     }
+    cp_async_wait_all();
+    csync();
+}
+
+// In-place RMSNorm of the input (kernels.cl:25-27: scale = 1/sqrt(mean + eps);
+// y = (x * scale) * gain).  `gain` is in shared memory or global memory (or
+// NULL: non-affine).  Ends with a compute barrier.
+__device__ void norm_input(float *in, int cols, float eps, const void *gain, int gain_dtype, Control &c) {
+    float ss = 0.f;
+    for (int j = threadIdx.x; j < cols; j += kEngineThreads) ss = fmaf(in[j], in[j], ss);
+    ss = block_sum(ss, c);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
+    for (int j = threadIdx.x; j < cols; j += kEngineThreads) {
+        const float gn = gain ? load_weight(gain, gain_dtype, j) : 1.0f;
+        in[j] = __fmul_rn(__fmul_rn(in[j], scale), gn);
+    }
+    csync();
 }
 
 struct Epi {
@@ -471,26 +555,33 @@ struct Epi {
     int nonfinite = 0;
 };
 
-// Epilogue of rows [row0, row0+n) of segment `s` whose dot products are in c.y[0].
-__device__ void epilogue(const GemvPhase &g, int s, int row0, int n, const StepInfo &info, Control &c, Epi &e) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+// Epilogue of rows [row0, row0+n) of segment `s` whose dot products are in y.
+// `xres` (or NULL) holds the residual rows row0.. of this CTA.
+__device__ void epilogue(const GemvPhase &g, int s, int row0, int n, const float *y, const float *xres,
+                         const StepInfo &info, Control &c, Epi &e) {
+    for (int i = threadIdx.x; i < n; i += kEngineThreads) {
         const int r = row0 + i;
-        const float y = c.y[0][i];
+        const float v = y[i];
         switch (g.epilogue) {
-            case EPI_STORE: g.seg[s].out[r] = y; break;
-            case EPI_RESIDUAL: g.x[r] = __fadd_rn(__ldcg(g.x + r), __fmul_rn(g.scale, y)); break;
+            case EPI_STORE: g.seg[s].out[r] = v; break;
+            case EPI_RESIDUAL: {
+                const float xv = xres ? xres[i] : __ldcg(g.x + r);
+                g.x[r] = __fadd_rn(xv, __fmul_rn(g.scale, v));
+                break;
+            }
             case EPI_SWIGLU:
+                // the gate and up rows of index i are handled by the same thread
                 if (s == 0) {
-                    c.y[1][i] = y;
+                    c.gate[i] = v;
                 } else {
-                    const float gt = c.y[1][i];
-                    g.out[r] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), y);
+                    const float gt = c.gate[i];
+                    g.out[r] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), v);
                 }
                 break;
             case EPI_LOGITS:
-                g.out[static_cast<size_t>(info.logits_row) * g.seg[0].rows + r] = y;
-                if (!isfinite(y)) e.nonfinite = 1;
-                else e.best = max(e.best, argmax_key(y, r));
+                g.out[static_cast<size_t>(info.logits_row) * g.seg[0].rows + r] = v;
+                if (!isfinite(v)) e.nonfinite = 1;
+                else e.best = max(e.best, argmax_key(v, r));
                 break;
         }
     }
@@ -505,66 +596,77 @@ __device__ void finish_logits(StepState *st, Control &c, Epi &e) {
         c.best[warp] = best;
         if (nonfinite) atomicExch(&st->nonfinite, 1);
     }
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) {
         unsigned long long m = 0;
         for (int w = 0; w < kEngineWarps; ++w) m = max(m, c.best[w]);
         if (m) atomicMax(&st->best, m);
     }
-    __syncthreads();
 }
 
+// Residual rows of this CTA, fetched while the phase input is in flight.
+struct ResidualRows {
+    int r0 = 0, r1 = 0;
+    bool in_smem = false;
+    float v = 0.f;
+    bool mine = false;
+    __device__ void start(const GemvPhase &g) {
+        if (g.epilogue != EPI_RESIDUAL) return;
+        row_range(g.seg[0].rows, blockIdx.x, gridDim.x, r0, r1);
+        in_smem = r1 - r0 <= kRowBatch;
+        mine = in_smem && static_cast<int>(threadIdx.x) < r1 - r0;
+        if (mine) v = __ldcg(g.x + r0 + threadIdx.x);
+    }
+    // After the input's compute barrier; the next compute barrier publishes it.
+    __device__ void store(Control &c) const {
+        if (mine) c.xres[threadIdx.x] = v;
+    }
+    __device__ const float *rows(const Control &c, int row0) const { return in_smem ? c.xres + (row0 - r0) : nullptr; }
+};
+
 // GEMV whose weights stream through the shared-memory ring.  `cidx` is the
-// index of the next piece of this CTA's stream (the same in every thread).
-__device__ bool gemv_bulk(const GemvPhase &g, int p, const StepControl &ctl, bool need_head, int head_phase,
-                          StepState *st, const StepInfo &info, const Smem &sm, int &cidx, const Tracer &tr) {
+// index of the next piece of this CTA's stream (the same in every thread);
+// the pieces come in the order the host's piece table lists them: the gain
+// vector, then per segment the CTA's rows in batches of rows_per_piece
+// (SwiGLU: gate and up batches alternate).
+__device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepInfo &info, const Smem &sm, int &cidx,
+                          const Tracer &tr) {
     Control &c = *sm.c;
     const int cols = g.seg[0].cols;
-    const PieceDesc *table = cta_pieces(ctl);
-    const int count = ctl.piece_count[blockIdx.x];
     float *in = sm.scratch;
-    auto consumed = [&]() {
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            ++c.consumed;
-            refill(ctl, need_head, head_phase, sm);
-        }
-        ++cidx;
-    };
-    load_input(g, cols, info, in, c);
+    ResidualRows res;
+    load_input(g, cols, info, in, [&] { res.start(g); });
+    res.store(c);
     tr.mark(0);
     if (g.norm) {
-        float ss = 0.f;
-        for (int j = threadIdx.x; j < cols; j += blockDim.x) ss = fmaf(in[j], in[j], ss);
-        ss = block_sum(ss, c);
-        // kernels.cl:25-27: scale = 1/sqrt(mean + eps); y = (x * scale) * gain
-        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), g.norm_eps)));
-        const unsigned char *gain_smem = nullptr;
+        const void *gain = g.norm_gain;
         if (g.gain_piece) {
-            // every thread agrees on the outcome before any of them moves on
-            if (!__syncthreads_and(wait_piece(sm, cidx, st, p))) return false;
-            gain_smem = sm.ring + c.offset[cidx % kQueue];
+            if (!take_piece(c, cidx, st, p)) return false;
+            gain = sm.ring + c.offset[cidx % kQueue];
         }
-        for (int j = threadIdx.x; j < cols; j += blockDim.x) {
-            float gain = 1.0f;
-            if (gain_smem) gain = load_weight(gain_smem, g.norm_gain_dtype, j);
-            else if (g.norm_gain) gain = load_weight(g.norm_gain, g.norm_gain_dtype, j);
-            in[j] = __fmul_rn(__fmul_rn(in[j], scale), gain);
-        }
-        if (g.gain_piece) consumed();
-        else __syncthreads();
+        norm_input(in, cols, g.norm_eps, gain, g.norm_gain_dtype, c);
+        if (g.gain_piece) release_piece(c, cidx++);
     }
     tr.mark(1);
     Epi e;
-    while (cidx < count) {
-        const PieceDesc d = table[cidx];
-        if (d.phase != p) break;
-        if (!__syncthreads_and(wait_piece(sm, cidx, st, p))) return false;
-        const Segment &s = g.seg[d.seg];
-        const char *rows = reinterpret_cast<const char *>(sm.ring + c.offset[cidx % kQueue]);
-        rows_dot<true>(rows, s.dtype, cols, d.nrows, in, c);
-        epilogue(g, d.seg, d.row0, d.nrows, info, c, e);
-        consumed();
+    int buf = 0;
+    const bool paired = g.epilogue == EPI_SWIGLU;
+    for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
+        int r0, r1;
+        row_range(g.seg[s].rows, blockIdx.x, gridDim.x, r0, r1);
+        const int rpp = g.seg[s].rows_per_piece;
+        for (int row0 = r0; row0 < r1; row0 += rpp) {
+            const int n = min(rpp, r1 - row0);
+            for (int part = 0; part < (paired ? 2 : 1); ++part) {
+                const Segment &seg = g.seg[s + part];
+                if (!take_piece(c, cidx, st, p)) return false;
+                const char *rows = reinterpret_cast<const char *>(sm.ring + c.offset[cidx % kQueue]);
+                rows_dot<true>(rows, seg.dtype, cols, n, in, c.y[buf], c);
+                release_piece(c, cidx++);
+                epilogue(g, s + part, row0, n, c.y[buf], res.rows(c, row0), info, c, e);
+                buf ^= 1;
+            }
+        }
     }
     tr.mark(2);
     if (g.epilogue == EPI_LOGITS) finish_logits(st, c, e);
@@ -576,19 +678,12 @@ __device__ void gemv_direct(const GemvPhase &g, StepState *st, const StepInfo &i
     Control &c = *sm.c;
     const int G = gridDim.x, b = blockIdx.x, cols = g.seg[0].cols;
     float *in = sm.scratch;
-    load_input(g, cols, info, in, c);
-    if (g.norm) {
-        float ss = 0.f;
-        for (int j = threadIdx.x; j < cols; j += blockDim.x) ss = fmaf(in[j], in[j], ss);
-        ss = block_sum(ss, c);
-        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), g.norm_eps)));
-        for (int j = threadIdx.x; j < cols; j += blockDim.x) {
-            const float gain = g.norm_gain ? load_weight(g.norm_gain, g.norm_gain_dtype, j) : 1.0f;
-            in[j] = __fmul_rn(__fmul_rn(in[j], scale), gain);
-        }
-        __syncthreads();
-    }
+    ResidualRows res;
+    load_input(g, cols, info, in, [&] { res.start(g); });
+    res.store(c);
+    if (g.norm) norm_input(in, cols, g.norm_eps, g.norm_gain, g.norm_gain_dtype, c);
     Epi e;
+    int buf = 0;
     const bool paired = g.epilogue == EPI_SWIGLU;
     for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
         int r0, r1;
@@ -598,9 +693,9 @@ __device__ void gemv_direct(const GemvPhase &g, StepState *st, const StepInfo &i
             for (int part = 0; part < (paired ? 2 : 1); ++part) {
                 const Segment &seg = g.seg[s + part];
                 const char *base = static_cast<const char *>(seg.w) + static_cast<size_t>(rb) * cols * esize(seg.dtype);
-                rows_dot<false>(base, seg.dtype, cols, n, in, c);
-                epilogue(g, s + part, rb, n, info, c, e);
-                __syncthreads();
+                rows_dot<false>(base, seg.dtype, cols, n, in, c.y[buf], c);
+                epilogue(g, s + part, rb, n, c.y[buf], res.rows(c, rb), info, c, e);
+                buf ^= 1;
             }
         }
     }
@@ -641,12 +736,52 @@ __device__ void norm_rope_warp(float *v, int dim, const float *gain, float eps, 
     __syncwarp();
 }
 
+// Issues the asynchronous loads of one key/value tile (logical keys tb ..
+// tb+nt-1 of KV head g) into kt / vt.  Ring rows were written by earlier
+// launches (the newest row, written in this launch, is patched from shared
+// memory by its owner), relay rows by the host.
+__device__ void issue_tile(const AttnPhase &a, int g, int tb, int nt, int start, int length, const AttnLayout &L,
+                           float *kt, float *vt) {
+    const int d = a.dim, cap = a.capacity;
+    auto row_src = [&](int lt, const float *&kr, const float *&vr) {
+        if (lt < length) {
+            const size_t row = static_cast<size_t>(g) * cap + (start + lt) % cap;
+            kr = a.k_cache + row * d;
+            vr = a.v_cache + row * d;
+        } else {
+            const size_t row = static_cast<size_t>(g) * a.relay_capacity + (lt - length);
+            kr = a.relay_k + row * d;
+            vr = a.relay_v + row * d;
+        }
+    };
+    if ((d & 3) == 0) {
+        const int per_row = d / 4;
+        for (int e = threadIdx.x; e < nt * per_row; e += kEngineThreads) {
+            const int t = e / per_row, j = (e - t * per_row) * 4;
+            const float *kr, *vr;
+            row_src(tb + t, kr, vr);
+            cp_async16_cg(kt + t * L.kstride + j, kr + j);
+            cp_async16_cg(vt + t * L.vstride + j, vr + j);
+        }
+    } else {
+        for (int e = threadIdx.x; e < nt * d; e += kEngineThreads) {
+            const int t = e / d, j = e - t * d;
+            const float *kr, *vr;
+            row_src(tb + t, kr, vr);
+            cp_async4(kt + t * L.kstride + j, kr + j);
+            cp_async4(vt + t * L.vstride + j, vr + j);
+        }
+    }
+    cp_async_commit();
+}
+
 // Work unit = (KV head g, chunk c of the attended rows): one pass over the
 // chunk's keys (in tiles of kKeyTile) for the group's query heads; writes the
-// chunk's (acc, max, sum) for the consumer to merge.  All of a tile's global
-// reads are issued at once with cp.async; the newest row (this token's key and
-// value, appended to the ring by the unit that owns it) is patched into the
-// tile in shared memory.
+// chunk's (acc, max, sum) for the consumer to merge.  The group's raw q rows,
+// this token's raw k/v rows (owner) and the first tile are all requested
+// before the first wait; the newest row (this token's key and value, appended
+// to the ring by the unit that owns it) is patched into its tile in shared
+// memory.
 __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const Smem &sm, const Tracer &tr) {
     const int G = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -662,41 +797,39 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
     const float pos_f = static_cast<float>(info.position);
     const float sqrt_d = __fsqrt_rn(static_cast<float>(d));  // divisor, kernels.cl:72
     const int stride = d + 2;
+    const bool vec = (d & 3) == 0;
 
-    // q and knew first: 16-byte cp.async targets (scratch is 128-byte aligned,
-    // gq*d is a multiple of 4 whenever d is)
-    float *q = sm.scratch;                             // [gq][d]
-    float *knew = q + gq * d;                          // [d]
-    float *kt = knew + d;                              // [kKeyTile][d+1]
-    float *vt = kt + kKeyTile * (d + 1);               // [kKeyTile][d]
-    float *p = vt + kKeyTile * d;                      // [gq][kKeyTile]
-    float *acc = p + gq * kKeyTile;                    // [gq][d]
-    float *mrow = acc + gq * d;                        // [gq]
-    float *lrow = mrow + gq;                           // [gq]
-    float *corr = lrow + gq;                           // [gq]
-    float *gains = sm.c->y[1];                         // q gain [d], k gain [d] (kRowBatch >= 2 * 128)
+    const AttnLayout L = attn_layout(gq, d);
+    float *q = sm.scratch + L.q, *knew = sm.scratch + L.knew, *vnew = sm.scratch + L.vnew;
+    float *kt = sm.scratch + L.kt, *vt = sm.scratch + L.vt, *p = sm.scratch + L.p, *acc = sm.scratch + L.acc;
+    float *mrow = sm.scratch + L.m, *lrow = sm.scratch + L.l, *corr = sm.scratch + L.corr;
+    float *gains = sm.c->gains;
 
     for (int unit = blockIdx.x; unit < a.kv_heads * chunks; unit += G) {
         const int g = unit / chunks, c = unit % chunks;
         const int t0 = c * chunk_len, t1 = min(total, t0 + chunk_len);
         const int newest = length - 1;
         const bool owner = newest >= t0 && newest < t1;
-        // 1. issue: the group's raw q rows, the first key/value tile, and (owner) the raw k/v row
-        if ((d & 3) == 0) {
-            for (int e = threadIdx.x * 4; e < gq * d; e += blockDim.x * 4)
-                cp_async16_cg(q + e, a.q_raw + static_cast<size_t>(g) * gq * d + e);
+        const float *qsrc = a.q_raw + static_cast<size_t>(g) * gq * d;
+        const float *ksrc = a.k_raw + static_cast<size_t>(g) * d, *vsrc = a.v_raw + static_cast<size_t>(g) * d;
+        // 1. issue: the group's raw q rows, (owner) the raw k/v row, the first tile
+        if (vec) {
+            for (int e = threadIdx.x * 4; e < gq * d; e += kEngineThreads * 4) cp_async16_cg(q + e, qsrc + e);
             if (owner)
-                for (int e = threadIdx.x * 4; e < d; e += blockDim.x * 4)
-                    cp_async16_cg(knew + e, a.k_raw + static_cast<size_t>(g) * d + e);
-        } else {
-            for (int e = threadIdx.x; e < gq * d; e += blockDim.x) q[e] = __ldcg(a.q_raw + static_cast<size_t>(g) * gq * d + e);
+                for (int e = threadIdx.x * 4; e < 2 * d; e += kEngineThreads * 4)
+                    cp_async16_cg(e < d ? knew + e : vnew + (e - d), e < d ? ksrc + e : vsrc + (e - d));
+        }
+        if (t0 < t1) issue_tile(a, g, t0, min(kKeyTile, t1 - t0), start, length, L, kt, vt);
+        if (!vec) {
+            for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) q[e] = __ldcg(qsrc + e);
             if (owner)
-                for (int e = threadIdx.x; e < d; e += blockDim.x) knew[e] = __ldcg(a.k_raw + static_cast<size_t>(g) * d + e);
+                for (int e = threadIdx.x; e < 2 * d; e += kEngineThreads)
+                    (e < d ? knew[e] : vnew[e - d]) = __ldcg(e < d ? ksrc + e : vsrc + (e - d));
         }
         if (a.qk_norm && a.q_gain)
-            for (int e = threadIdx.x; e < 2 * d; e += blockDim.x)
+            for (int e = threadIdx.x; e < 2 * d; e += kEngineThreads)
                 gains[e] = load_weight(e < d ? a.q_gain : a.k_gain, a.gain_dtype, e < d ? e : e - d);
-        for (int e = threadIdx.x; e < gq * d; e += blockDim.x) acc[e] = 0.f;
+        for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) acc[e] = 0.f;
         if (threadIdx.x < gq) {
             mrow[threadIdx.x] = -INFINITY;
             lrow[threadIdx.x] = 0.f;
@@ -704,25 +837,10 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
         bool first = true;
         for (int tb = t0; tb < t1; tb += kKeyTile) {
             const int nt = min(kKeyTile, t1 - tb);
-            for (int e = threadIdx.x; e < nt * d; e += blockDim.x) {
-                const int t = e / d, j = e % d, lt = tb + t;
-                const float *kr, *vr;
-                if (lt < length) {
-                    const size_t row = static_cast<size_t>(g) * cap + (start + lt) % cap;
-                    kr = a.k_cache + row * d;
-                    vr = a.v_cache + row * d;
-                } else {
-                    const size_t row = static_cast<size_t>(g) * a.relay_capacity + (lt - length);
-                    kr = a.relay_k + row * d;
-                    vr = a.relay_v + row * d;
-                }
-                cp_async4(kt + t * (d + 1) + j, kr + j);
-                cp_async4(vt + t * d + j, vr + j);
-            }
             cp_async_wait_all();
-            __syncthreads();
-            if (first) tr.mark(0);
+            csync();
             if (first) {
+                tr.mark(0);
                 // 2. query heads: RMSNorm + RoPE; the owner also finishes this token's key/value
                 const float *qg = (a.qk_norm && a.q_gain) ? gains : nullptr;
                 const float *kg = (a.qk_norm && a.k_gain) ? gains + d : nullptr;
@@ -735,37 +853,41 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
                 }
                 if (owner && warp == kEngineWarps - 2) {
                     const size_t slot = static_cast<size_t>(g) * cap + (count - 1) % cap;
-                    for (int j = lane; j < d; j += 32) a.v_cache[slot * d + j] = __ldcg(a.v_raw + static_cast<size_t>(g) * d + j);
+                    for (int j = lane; j < d; j += 32) a.v_cache[slot * d + j] = vnew[j];
                 }
-                __syncthreads();
+                csync();
                 first = false;
                 tr.mark(1);
             }
             if (owner && newest >= tb && newest < tb + nt) {
                 // the tile holds the ring's previous occupant of the newest slot: patch it
                 const int t = newest - tb;
-                for (int j = threadIdx.x; j < d; j += blockDim.x) {
-                    kt[t * (d + 1) + j] = knew[j];
-                    vt[t * d + j] = __ldcg(a.v_raw + static_cast<size_t>(g) * d + j);
+                for (int j = threadIdx.x; j < d; j += kEngineThreads) {
+                    kt[t * L.kstride + j] = knew[j];
+                    vt[t * L.vstride + j] = vnew[j];
                 }
-                __syncthreads();
+                csync();
             }
             // 3. scores (4 independent partial sums per dot product)
-            for (int e = threadIdx.x; e < gq * nt; e += blockDim.x) {
-                const int i = e / nt, t = e % nt;
-                const float *qi = q + i * d, *kr = kt + t * (d + 1);
+            for (int e = threadIdx.x; e < gq * nt; e += kEngineThreads) {
+                const int i = e / nt, t = e - i * nt;
+                const float *qi = q + i * d, *kr = kt + t * L.kstride;
                 float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-                int j = 0;
-                for (; j + 3 < d; j += 4) {
-                    s0 = fmaf(qi[j], kr[j], s0);
-                    s1 = fmaf(qi[j + 1], kr[j + 1], s1);
-                    s2 = fmaf(qi[j + 2], kr[j + 2], s2);
-                    s3 = fmaf(qi[j + 3], kr[j + 3], s3);
+                if (vec) {
+                    for (int j = 0; j < d; j += 4) {
+                        const float4 qa = *reinterpret_cast<const float4 *>(qi + j);
+                        const float4 ka = *reinterpret_cast<const float4 *>(kr + j);
+                        s0 = fmaf(qa.x, ka.x, s0);
+                        s1 = fmaf(qa.y, ka.y, s1);
+                        s2 = fmaf(qa.z, ka.z, s2);
+                        s3 = fmaf(qa.w, ka.w, s3);
+                    }
+                } else {
+                    for (int j = 0; j < d; ++j) s0 = fmaf(qi[j], kr[j], s0);
                 }
-                for (; j < d; ++j) s0 = fmaf(qi[j], kr[j], s0);
                 p[i * kKeyTile + t] = __fdiv_rn((s0 + s1) + (s2 + s3), sqrt_d);
             }
-            __syncthreads();
+            csync();
             // 4. online softmax per query head
             for (int i = warp; i < gq; i += kEngineWarps) {
                 float mt = -INFINITY;
@@ -786,28 +908,29 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
                     mrow[i] = m_new;
                 }
             }
-            __syncthreads();
+            csync();
             // 5. value mix (4 independent partial sums)
-            for (int e = threadIdx.x; e < gq * d; e += blockDim.x) {
-                const int i = e / d, j = e % d;
+            for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
+                const int i = e / d, j = e - i * d;
                 const float *pi = p + i * kKeyTile;
                 float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
                 int t = 0;
                 for (; t + 3 < nt; t += 4) {
-                    a0 = fmaf(pi[t], vt[t * d + j], a0);
-                    a1 = fmaf(pi[t + 1], vt[(t + 1) * d + j], a1);
-                    a2 = fmaf(pi[t + 2], vt[(t + 2) * d + j], a2);
-                    a3 = fmaf(pi[t + 3], vt[(t + 3) * d + j], a3);
+                    a0 = fmaf(pi[t], vt[t * L.vstride + j], a0);
+                    a1 = fmaf(pi[t + 1], vt[(t + 1) * L.vstride + j], a1);
+                    a2 = fmaf(pi[t + 2], vt[(t + 2) * L.vstride + j], a2);
+                    a3 = fmaf(pi[t + 3], vt[(t + 3) * L.vstride + j], a3);
                 }
-                for (; t < nt; ++t) a0 = fmaf(pi[t], vt[t * d + j], a0);
+                for (; t < nt; ++t) a0 = fmaf(pi[t], vt[t * L.vstride + j], a0);
                 acc[e] = fmaf(acc[e], corr[i], (a0 + a1) + (a2 + a3));
             }
-            __syncthreads();
+            csync();
+            if (tb + kKeyTile < t1) issue_tile(a, g, tb + kKeyTile, min(kKeyTile, t1 - tb - kKeyTile), start, length, L, kt, vt);
         }
         tr.mark(2);
         // 6. publish the chunk partial: acc[d], running max, running sum
-        for (int e = threadIdx.x; e < gq * d; e += blockDim.x) {
-            const int i = e / d, j = e % d;
+        for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
+            const int i = e / d, j = e - i * d;
             a.partial[(static_cast<size_t>(g * gq + i) * kMaxAttnChunks + c) * stride + j] = acc[e];
         }
         if (threadIdx.x < gq) {
@@ -815,13 +938,13 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
             rec[d] = mrow[threadIdx.x];
             rec[d + 1] = lrow[threadIdx.x];
         }
-        __syncthreads();
+        csync();
     }
 }
 
 }  // namespace
 
-__global__ void __launch_bounds__(kEngineThreads, 1)
+__global__ void __launch_bounds__(kBlockThreads, 1)
     decode_step_kernel(const Phase *__restrict__ phases, int nphases, StepState *st, StepControl ctl) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     Smem sm;
@@ -854,41 +977,50 @@ __global__ void __launch_bounds__(kEngineThreads, 1)
             skip = 1;
         }
         if (!skip) {
-            for (int i = 0; i < kQueue; ++i) mbar_init(&c.mbar[i], 1);
+            for (int i = 0; i < kQueue; ++i) {
+                mbar_init(&c.full[i], 1);
+                mbar_init(&c.empty[i], 1);
+            }
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-            c.issued = c.consumed = c.head_offset = 0;
+            c.abort = 0;
         }
+        if (!skip && ctl.trace && blockIdx.x == 0) ctl.trace[0] = global_ns();
     }
-    __syncthreads();
+    __syncthreads();  // the last block-wide barrier: warp 16 leaves below
     if (skip) return;
-    if (threadIdx.x == 0) {
-        if (ctl.trace && blockIdx.x == 0) ctl.trace[0] = global_ns();
-        refill(ctl, need_head != 0, head_phase, sm);
+    if (threadIdx.x >= kEngineThreads) {
+        if (threadIdx.x == kEngineThreads) produce(ctl, need_head != 0, head_phase, st, sm);
+        return;
     }
-    __syncthreads();
+    fetch_phase(&c.phase[0], &phases[0]);
+    cp_async_wait_all();
+    csync();
     int barriers = 0, cidx = 0;
     bool ok = true;
-    for (int p = 0; p < nphases && ok; ++p) {
-        const Phase &ph = phases[p];
-        if (ph.kind == PH_STEP_END) break;
-        if (ph.layer < 0 && !need_head) continue;
+    for (int p = 0; p < nphases - 1 && ok; ++p) {
+        const Phase &ph = c.phase[p & 1];
+        if (ph.layer < 0 && !need_head) break;  // the head is the last phase before the step end
+        if (p + 1 < nphases - 1) fetch_phase(&c.phase[(p + 1) & 1], &phases[p + 1]);
         const Tracer tr{ctl.trace ? ctl.trace + 1 + static_cast<size_t>(barriers) * (gridDim.x * kTraceStamps + 1)
                                   : nullptr};
         if (ph.kind == PH_GEMV) {
-            if (ph.gemv.bulk) ok = gemv_bulk(ph.gemv, p, ctl, need_head != 0, head_phase, st, info, sm, cidx, tr);
+            if (ph.gemv.bulk) ok = gemv_bulk(ph.gemv, p, st, info, sm, cidx, tr);
             else gemv_direct(ph.gemv, st, info, sm);
         } else if (ph.kind == PH_ATTN_GQA) {
             attn_gqa_phase(ph.attn, info, sm, tr);
         }
         if (!ok) break;
+        cp_async_wait_all();  // the next phase's descriptor (published by the barrier)
         tr.mark(3);
         ++barriers;
-        ok = grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, p, sm);
+        ok = grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, p, c);
         if (ok && tr.rec && blockIdx.x == 0 && threadIdx.x == 0) tr.rec[gridDim.x * kTraceStamps] = global_ns();
     }
-    __syncthreads();
-    if (threadIdx.x == 0) drain(sm);  // nothing is in flight on the normal path; bounded either way
-    if (!ok) return;
+    cp_async_wait_all();
+    if (!ok) {
+        if (threadIdx.x == 0) c.abort = 1;
+        return;
+    }
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         volatile StepState *s = st;
         const int pos = info.position;
