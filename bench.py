@@ -305,7 +305,7 @@ def run_trace(args, steps=8):
                                                  context_length=context)
     token = int(np.argmax(model.prefill(syn.prompt_ids(config.vocab_size, prompt_len, seed=1))))
     kinds = ["qkv", "attn", "o", "gate_up", "down"] * config.layers + ["head"]
-    stamps_per_cta = 4
+    stamps_per_cta = 6
     capacity = 1 + len(kinds) * (200 * stamps_per_cta + 1)
     stamps = (C.c_uint64 * capacity)()
     phases, grid = C.c_int(), C.c_int()
@@ -321,12 +321,16 @@ def run_trace(args, steps=8):
             cta = row[:g * stamps_per_cta].reshape(g, stamps_per_cta) - start
             exit_ = row[-1]
             entry = per_kind.setdefault(kinds[k], {"cp0": [], "cp1": [], "cp2": [], "done_median": [],
-                                                   "done_max": [], "barrier": []})
+                                                   "done_max": [], "barrier": [], "piece_wait": [],
+                                                   "late_pieces": []})
             for i in range(3):
                 vals = cta[:, i]
                 vals = vals[vals > 0]
                 entry[f"cp{i}"].append(np.median(vals) if len(vals) else 0)
             entry["done_median"].append(np.median(cta[:, 3]))
+            raw = row[:g * stamps_per_cta].reshape(g, stamps_per_cta)
+            entry["piece_wait"].append(np.median(raw[:, 4]))
+            entry["late_pieces"].append(1e3 * np.median(raw[:, 5]))  # reported /1e3 below
             entry["done_max"].append(cta[:, 3].max())
             entry["barrier"].append(exit_ - (start + cta[:, 3].max()))
             start = exit_
@@ -334,7 +338,9 @@ def run_trace(args, steps=8):
     report = {"config": args.config, "position": model.position, "steps": steps,
               "step_us": round(float(np.median(totals)) / 1e3, 2),
               "legend": "us from the previous barrier exit, median over CTAs (cp*: GEMV input, norm, weights; "
-                        "attention first tile, q/k, compute)", "phases": {}}
+                        "attention first tile, q/k, compute); piece_wait: us waiting for weight pieces, "
+                        "late_pieces: pieces not yet in shared memory when first needed (median CTA)",
+              "phases": {}}
     for kind, entry in per_kind.items():
         report["phases"][kind] = {k: round(float(np.median(v)) / 1e3, 3) for k, v in entry.items()}
         report["phases"][kind]["count_per_step"] = len(entry["barrier"]) // steps

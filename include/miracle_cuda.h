@@ -85,6 +85,9 @@ MR_API int mr_device_query(int ordinal, mr_device_info *info);
 
 /* ---- context: one device + one stream (OpenCLBackend.__init__, opencl.py:284-314) */
 MR_API int mr_context_create(int device_ordinal, mr_context **out);
+/* Releases the caller's reference.  Buffers and models made on the context
+ * hold their own references, so handles may be released in any order; the
+ * stream is destroyed with the last one. */
 MR_API int mr_context_destroy(mr_context *ctx);
 /* OpenCLBackend.finish (opencl.py:450-451) */
 MR_API int mr_context_finish(mr_context *ctx);
@@ -228,11 +231,13 @@ MR_API int mr_model_bench_decode(mr_model *model, int first_token, int steps, fl
 
 /* Tracing: run one decode step (feeding `token`) with per-phase device
  * timestamps (globaltimer, ns).  Layout: stamps[0] = launch start; the k-th
- * executed phase has a record of grid*4 + 1 stamps at 1 + k*(grid*4 + 1):
- * CTA b's checkpoints at offset b*4 + i (i = 0..2 phase-specific, 3 = done
- * computing) and CTA 0 leaving the phase's grid barrier at offset grid*4.
- * GEMV checkpoints: input loaded, input normalised, weights consumed;
- * attention: first tile loaded, q/k prepared, scores/mix done.
+ * executed phase has a record of grid*6 + 1 stamps at 1 + k*(grid*6 + 1):
+ * CTA b's slots at offset b*6 + i (i = 0..2 phase-specific checkpoints, 3 =
+ * done computing, 4 = ns spent waiting for weight pieces, 5 = pieces not yet
+ * in shared memory when first needed) and CTA 0 leaving the phase's grid
+ * barrier at offset grid*6.  GEMV checkpoints: input loaded, input
+ * normalised, weights consumed; attention: first tile loaded, q/k prepared,
+ * scores/mix done.
  * *phases receives the number of executed phases, *grid the CTA count.  No
  * reference counterpart (the reference has no tracing). */
 MR_API int mr_model_trace_decode(mr_model *model, int token, uint64_t *stamps, int capacity, int *phases,

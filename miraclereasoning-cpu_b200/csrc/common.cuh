@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/miracle_cuda.h"
 
 // ---- host-side error reporting ------------------------------------------------
@@ -27,12 +29,28 @@ int cuda_error(cudaError_t err, const char *what);
         if (!(cond)) return mr::set_error(MR_ERR_ARGUMENT, __VA_ARGS__);        \
     } while (0)
 
+// A context is shared by its creator and by every buffer and model made on
+// it; each holds one reference and the last release destroys the stream.  So
+// the handles can be released in any order (a garbage-collected host
+// language finalises them in no fixed order at exit).
 struct mr_context {
     int device = 0;
     int sm_count = 0;
     cudaStream_t stream = nullptr;
     size_t max_allocation = 0;
+    std::atomic<int> refs{1};
 };
+
+namespace mr {
+inline void context_retain(mr_context *ctx) { ctx->refs.fetch_add(1, std::memory_order_relaxed); }
+inline void context_release(mr_context *ctx) {
+    if (ctx->refs.fetch_sub(1, std::memory_order_acq_rel) != 1) return;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+}  // namespace mr
 
 struct mr_buffer {
     mr_context *ctx = nullptr;

@@ -551,6 +551,7 @@ int mr_model_create(mr_context *ctx, const mr_model_config *config, const int *l
                    l);
     MR_CUDA_TRY(cudaSetDevice(ctx->device));
     auto *m = new mr_model();
+    mr::context_retain(ctx);
     m->ctx = ctx;
     m->cfg = c;
     m->layer_kvh.assign(layer_kv_heads, layer_kv_heads + c.layers);
@@ -569,7 +570,9 @@ int mr_model_destroy(mr_model *m) {
     for (void *p : m->allocations) cudaFree(p);
     if (m->ev0) cudaEventDestroy(m->ev0);
     if (m->ev1) cudaEventDestroy(m->ev1);
+    mr_context *ctx = m->ctx;
     delete m;
+    mr::context_release(ctx);
     return MR_OK;
 }
 

@@ -35,7 +35,7 @@ constexpr int kMaxAttnChunks = 16;   // key chunks per KV head (merged by the co
 constexpr int kKeysPerChunk = 64;    // target keys per attention work unit
 constexpr int kKeyTile = 64;         // keys per attention tile
 constexpr int kSmemLimit = 227 * 1024;
-constexpr int kTraceStamps = 4;
+constexpr int kTraceStamps = 6;
 
 enum PhaseKind : int {
     PH_GEMV = 1,        // y = W x for up to 3 weight segments, then an epilogue
@@ -200,9 +200,11 @@ struct StepControl {
     const int *piece_count;           // [grid]
     int piece_stride;
     // Optional phase trace (globaltimer ns): [0] = launch start (CTA 0); then per
-    // executed phase k a record of grid*kTraceStamps + 1 slots: CTA b's stamps
+    // executed phase k a record of grid*kTraceStamps + 1 slots: CTA b's slots
     // at 1 + k*rec + b*kTraceStamps + i (i = 0..2 phase-specific checkpoints,
-    // 3 = done computing) and CTA 0 leaving the barrier at 1 + k*rec + grid*kTraceStamps.
+    // 3 = done computing, 4 = ns waiting for weight pieces, 5 = pieces not
+    // resident when first needed) and CTA 0 leaving the barrier at
+    // 1 + k*rec + grid*kTraceStamps.
     unsigned long long *trace;
 };
 

@@ -56,6 +56,8 @@ struct Control {
     unsigned long long best[kEngineWarps];
     int ok;
     int abort;                         // the compute warps stopped: the producer stops too
+    unsigned long long wait_ns;        // tracing: time thread 0 spent in take_piece this phase
+    int late;                          // tracing: pieces not resident at their first probe
 };
 
 struct StepInfo {
@@ -82,6 +84,14 @@ struct Tracer {
         if (!rec) return;
         csync();
         if (threadIdx.x == 0) rec[blockIdx.x * kTraceStamps + i] = global_ns();
+    }
+    // Slots 4 and 5: weight-piece waiting of the phase (thread 0's accounting).
+    __device__ void waits(unsigned long long &wait_ns, int &late) const {
+        if (!rec || threadIdx.x != 0) return;
+        rec[blockIdx.x * kTraceStamps + 4] = wait_ns;
+        rec[blockIdx.x * kTraceStamps + 5] = static_cast<unsigned long long>(late);
+        wait_ns = 0;
+        late = 0;
     }
 };
 
@@ -253,9 +263,18 @@ __device__ void produce(const StepControl &ctl, bool need_head, int head_phase, 
 }
 
 // Consumer side: bounded wait for piece `idx`, agreed by every compute thread.
-__device__ bool take_piece(Control &c, int idx, StepState *st, int phase) {
-    const bool ok = csync_and(wait_bar(&c.full[idx % kQueue], (idx / kQueue) & 1, st, c, phase, false));
+// With `tracing`, thread 0 accounts the time to agreement and late pieces.
+__device__ bool take_piece(Control &c, int idx, StepState *st, int phase, bool tracing) {
+    unsigned long long *bar = &c.full[idx % kQueue];
+    const int parity = (idx / kQueue) & 1;
+    uint64_t t0 = 0;
+    if (tracing && threadIdx.x == 0) {
+        t0 = global_ns();
+        if (!mbar_try_wait(bar, parity)) ++c.late;
+    }
+    const bool ok = csync_and(wait_bar(bar, parity, st, c, phase, false));
     if (!ok && threadIdx.x == 0) c.abort = 1;
+    if (tracing && threadIdx.x == 0) c.wait_ns += global_ns() - t0;
     return ok;
 }
 // Every compute thread has passed a compute barrier since its last read of the piece.
@@ -641,7 +660,7 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
     if (g.norm) {
         const void *gain = g.norm_gain;
         if (g.gain_piece) {
-            if (!take_piece(c, cidx, st, p)) return false;
+            if (!take_piece(c, cidx, st, p, tr.rec != nullptr)) return false;
             gain = sm.ring + c.offset[cidx % kQueue];
         }
         norm_input(in, cols, g.norm_eps, gain, g.norm_gain_dtype, c);
@@ -659,7 +678,7 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
             const int n = min(rpp, r1 - row0);
             for (int part = 0; part < (paired ? 2 : 1); ++part) {
                 const Segment &seg = g.seg[s + part];
-                if (!take_piece(c, cidx, st, p)) return false;
+                if (!take_piece(c, cidx, st, p, tr.rec != nullptr)) return false;
                 const char *rows = reinterpret_cast<const char *>(sm.ring + c.offset[cidx % kQueue]);
                 rows_dot<true>(rows, seg.dtype, cols, n, in, c.y[buf], c);
                 release_piece(c, cidx++);
@@ -669,6 +688,7 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
         }
     }
     tr.mark(2);
+    tr.waits(c.wait_ns, c.late);
     if (g.epilogue == EPI_LOGITS) finish_logits(st, c, e);
     return true;
 }
@@ -983,6 +1003,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             }
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
             c.abort = 0;
+            c.wait_ns = 0;
+            c.late = 0;
         }
         if (!skip && ctl.trace && blockIdx.x == 0) ctl.trace[0] = global_ns();
     }

@@ -89,11 +89,7 @@ int mr_context_create(int device_ordinal, mr_context **out) {
 }
 
 int mr_context_destroy(mr_context *ctx) {
-    if (!ctx) return MR_OK;
-    cudaSetDevice(ctx->device);
-    cudaStreamSynchronize(ctx->stream);
-    cudaStreamDestroy(ctx->stream);
-    delete ctx;
+    if (ctx) mr::context_release(ctx);
     return MR_OK;
 }
 
@@ -112,6 +108,7 @@ int mr_buffer_alloc(mr_context *ctx, size_t count, mr_buffer **out) {
     float *ptr = nullptr;
     MR_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void **>(&ptr), count * sizeof(float), ctx->stream));
     auto *buf = new mr_buffer();
+    mr::context_retain(ctx);
     buf->ctx = ctx;
     buf->ptr = ptr;
     buf->count = count;
@@ -123,6 +120,7 @@ int mr_buffer_free(mr_buffer *buf) {
     if (!buf) return MR_OK;
     cudaSetDevice(buf->ctx->device);
     cudaFreeAsync(buf->ptr, buf->ctx->stream);
+    mr::context_release(buf->ctx);
     delete buf;
     return MR_OK;
 }

@@ -175,3 +175,34 @@ def test_bench_nano17_full_model(backend):
     np.testing.assert_allclose(logits[:, :cases.LOGIT_SUBSET], golden["lead"], atol=ATOL, rtol=RTOL)
     np.testing.assert_allclose(np.take_along_axis(logits, golden["top_ids"], axis=1), golden["top_values"],
                                atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.gpu
+def test_handles_release_in_any_order(tmp_path):
+    """The backend (context) may be finalised before the model and buffers made on it."""
+    import subprocess
+    import sys
+    import textwrap
+    from conftest import REPO
+    script = tmp_path / "release_order.py"
+    script.write_text(textwrap.dedent(f"""
+        import gc, importlib, sys
+        sys.path[:0] = [{str(REPO)!r}, {str(REPO / "tests" / "golden")!r}]
+        import cases
+        mr = importlib.import_module("miraclereasoning-cpu_b200")
+        backend = mr.CUDABackend()
+        model = mr.MiracleModel.synthetic(cases.micro_config("nano15"), backend=backend, context_length=16)
+        buf = backend.upload([1.0, 2.0, 3.0])
+        model.prefill([1, 2, 3])
+        backend.__del__()           # the caller's context reference goes first
+        del backend
+        gc.collect()
+        model.decode(4)             # the model's own reference keeps the context alive
+        del model
+        gc.collect()
+        del buf
+        print("ok")
+    """))
+    out = subprocess.run([sys.executable, str(script)], capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert out.stdout.strip().endswith("ok")
