@@ -105,6 +105,7 @@ struct mr_model {
     int scratch_floats = 0, ring_bytes = 0;
     size_t smem_bytes = 0;
     PieceDesc *d_pieces = nullptr;
+    GroupTable *d_groups = nullptr;
     int *d_piece_count = nullptr;
     int piece_stride = 0;
     std::vector<float *> k_cache, v_cache;
@@ -349,7 +350,9 @@ int build_plan(mr_model *m) {
         for (int i = 0; i < g.nseg; ++i) {
             const int row_bytes = g.seg[i].cols * (int)dtype_size(g.seg[i].dtype);
             if (row_bytes % 16 || row_bytes > piece_cap) bulk = false;
-            else g.seg[i].rows_per_piece = std::max(1, std::min(kRowBatch, piece_cap / row_bytes));
+            // a SwiGLU gate/up pair shares one group of at most kRowBatch rows
+            else g.seg[i].rows_per_piece = std::max(1, std::min(g.epilogue == EPI_SWIGLU ? kRowBatch / 2 : kRowBatch,
+                                                                piece_cap / row_bytes));
         }
         if (g.epilogue == EPI_SWIGLU && g.seg[0].rows_per_piece != g.seg[1].rows_per_piece) bulk = false;
         g.bulk = bulk;
@@ -418,6 +421,78 @@ int build_pieces(mr_model *m) {
     return MR_OK;
 }
 
+// Piece groups of every (bulk phase, CTA), in the stream order of
+// build_pieces: greedy, a group closes before the piece (or gate/up pair) that
+// would take it past half the ring, kRowBatch rows or kGroupPieces pieces.
+int build_groups(mr_model *m) {
+    const int G = m->grid, cap = m->ring_bytes / 2;
+    std::vector<GroupTable> flat;
+    for (Phase &ph : m->phases) {
+        if (ph.kind != PH_GEMV || !ph.gemv.bulk) continue;
+        GemvPhase &g = ph.gemv;
+        const bool paired = g.epilogue == EPI_SWIGLU;
+        const int cols = g.seg[0].cols, per = paired ? 2 : 1;
+        std::vector<std::vector<GroupTable>> per_cta(G);
+        size_t stride = 1;
+        for (int b = 0; b < G; ++b) {
+            std::vector<GroupTable> &out = per_cta[b];
+            GroupTable t{};
+            int bytes = 0;
+            auto close = [&]() {
+                out.push_back(t);
+                t = GroupTable{};
+                bytes = 0;
+            };
+            if (g.gain_piece) {
+                t.p[0] = GroupPiece{-1, 0, 0, 0};
+                t.count = 1;
+                bytes = (int)((cols * dtype_size(g.norm_gain_dtype) + 15) & ~size_t(15));
+            }
+            for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
+                const int rows = g.seg[s].rows, rpp = g.seg[s].rows_per_piece;
+                const int r0 = (int)((long long)rows * b / G), r1 = (int)((long long)rows * (b + 1) / G);
+                for (int row0 = r0; row0 < r1; row0 += rpp) {
+                    const int n = std::min(rpp, r1 - row0);
+                    int ubytes = n * cols * (int)dtype_size(g.seg[s].dtype);
+                    if (paired) ubytes += n * cols * (int)dtype_size(g.seg[s + 1].dtype);
+                    if (t.count > 0 &&
+                        (bytes + ubytes > cap || t.rows + per * n > kRowBatch || t.count + per > kGroupPieces))
+                        close();
+                    t.p[t.count++] = GroupPiece{s, row0, n, t.rows};
+                    t.rows += n;
+                    if (paired) {
+                        t.p[t.count++] = GroupPiece{s + 1, row0, n, t.rows};
+                        t.rows += n;
+                    }
+                    bytes += ubytes;
+                }
+            }
+            out.push_back(t);
+            for (size_t k = 0; k + 1 < out.size(); ++k) out[k].more = 1;
+            stride = std::max(stride, out.size());
+        }
+        g.group_offset = (int)flat.size();
+        g.group_stride = (int)stride;
+        for (int b = 0; b < G; ++b)
+            for (size_t k = 0; k < stride; ++k) flat.push_back(k < per_cta[b].size() ? per_cta[b][k] : GroupTable{});
+    }
+    for (size_t p = 0; p < m->phases.size(); ++p) {
+        Phase &ph = m->phases[p];
+        ph.next_groups = -1;
+        ph.next_group_stride = 0;
+        if (p + 1 < m->phases.size() && m->phases[p + 1].kind == PH_GEMV && m->phases[p + 1].gemv.bulk) {
+            ph.next_groups = m->phases[p + 1].gemv.group_offset;
+            ph.next_group_stride = m->phases[p + 1].gemv.group_stride;
+        }
+    }
+    if (flat.empty()) flat.push_back(GroupTable{});
+    int rc = MR_OK;
+    m->d_groups = static_cast<GroupTable *>(device_alloc(m, sizeof(GroupTable) * flat.size(), &rc));
+    if (rc) return rc;
+    MR_CUDA_TRY(cudaMemcpy(m->d_groups, flat.data(), sizeof(GroupTable) * flat.size(), cudaMemcpyHostToDevice));
+    return MR_OK;
+}
+
 int sync_and_check(mr_model *m, const char *what) {
     MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
     int error = 0;
@@ -480,6 +555,7 @@ StepControl base_control(mr_model *m) {
     ctl.scratch_floats = m->scratch_floats;
     ctl.ring_bytes = m->ring_bytes;
     ctl.pieces = m->d_pieces;
+    ctl.groups = m->d_groups;
     ctl.piece_count = m->d_piece_count;
     ctl.piece_stride = m->piece_stride;
     return ctl;
@@ -665,6 +741,7 @@ int mr_model_finalize(mr_model *m) {
     MR_CUDA_TRY(cudaMemcpy(m->d_inv_freq, m->inv_freq.data(), sizeof(float) * (d / 2), cudaMemcpyHostToDevice));
     rc = build_plan(m);
     if (!rc) rc = build_pieces(m);
+    if (!rc) rc = build_groups(m);
     if (rc) return rc;
     m->d_phases = static_cast<Phase *>(device_alloc(m, sizeof(Phase) * m->phases.size(), &rc));
     if (rc) return rc;

@@ -25,7 +25,9 @@
 
 namespace mr {
 
-constexpr int kEngineThreads = 512;  // compute warps per CTA (16), one CTA per SM
+// 15 compute warps + 1 producer warp: 16 warps, 4 per SM sub-partition, so
+// each thread may hold 128 registers (a 17th warp would cap it at 96).
+constexpr int kEngineThreads = 480;  // compute threads per CTA, one CTA per SM
 constexpr int kEngineWarps = kEngineThreads / 32;
 constexpr int kBlockThreads = kEngineThreads + 32;  // + the weight-stream producer warp
 constexpr int kMaxSegments = 3;
@@ -91,6 +93,8 @@ struct GemvPhase {
     float scale;                // EPI_RESIDUAL scale
     float *x;                   // EPI_RESIDUAL vector
     float *out;                 // EPI_SWIGLU / EPI_LOGITS destination
+    int group_offset;           // bulk: this phase's group tables in StepControl::groups,
+    int group_stride;           //   CTA b's g-th at group_offset + b * group_stride + g
 };
 
 struct AttnPhase {
@@ -110,6 +114,29 @@ struct AttnPhase {
     float *partial;                 // [heads][kMaxAttnChunks][dim + 2]
 };
 
+// The compute warps take a bulk phase's pieces in groups, precomputed on the
+// host per (phase, CTA): consecutive pieces (a SwiGLU gate/up pair is never
+// split) of at most half the ring, kRowBatch rows and kGroupPieces pieces,
+// awaited together and computed in one pass.  Every older piece has been
+// released when a group is awaited and no piece exceeds a quarter of the
+// ring, so a whole group always fits in the ring at once.
+constexpr int kGroupPieces = kQueue / 2;
+
+struct GroupPiece {
+    int seg;     // segment, -1: the phase's norm gain vector
+    int row0;    // first output row
+    int n;       // rows
+    int vbase;   // index of its first row among the group's rows
+};
+struct alignas(16) GroupTable {
+    GroupPiece p[kGroupPieces];
+    int count;   // pieces
+    int rows;    // dot products
+    int more;    // another group of the phase follows
+    int pad;
+};
+static_assert(sizeof(GroupTable) % 16 == 0, "GroupTable travels in 16-byte granules");
+
 // One bulk copy of a CTA's weight stream, precomputed on the host: the CTA's
 // pieces of every weight-streaming phase of a step, in consumption order.
 // 16 bytes, so the producer fetches each with one vector load.
@@ -125,6 +152,8 @@ static_assert(sizeof(PieceDesc) == 16, "PieceDesc is one 16-byte load");
 struct alignas(16) Phase {
     int kind;
     int layer;                      // -1: the output head (skipped when no logits are needed)
+    int next_groups;                // the next phase's group tables (its gemv.group_offset) or -1
+    int next_group_stride;          //   and its gemv.group_stride: prefetched with its descriptor
     GemvPhase gemv;
     AttnPhase attn;
 };
@@ -197,6 +226,7 @@ struct StepControl {
     int scratch_floats;               // shared-memory scratch (input vector / attention tiles)
     int ring_bytes;                   // shared-memory weight ring
     const PieceDesc *pieces;          // [grid][piece_stride] weight stream of each CTA
+    const GroupTable *groups;         // piece groups of every (bulk phase, CTA)
     const int *piece_count;           // [grid]
     int piece_stride;
     // Optional phase trace (globaltimer ns): [0] = launch start (CTA 0); then per

@@ -11,8 +11,8 @@
 //             merged (softmax-rescaled) by the next GEMV phase as it loads
 //             its input.
 //
-// CTA layout: warps 0-15 compute (they synchronise among themselves with
-// named barrier 1, never with __syncthreads), warp 16 is the weight-stream
+// CTA layout: warps 0-14 compute (they synchronise among themselves with
+// named barrier 1, never with __syncthreads), warp 15 is the weight-stream
 // producer.  The producer walks the CTA's piece table (engine.cuh) and issues
 // TMA bulk copies (cp.async.bulk) into a shared-memory byte ring, each piece
 // completing a "full" mbarrier; the compute warps consume the pieces in the
@@ -39,6 +39,7 @@ namespace {
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
 constexpr int kMaxHeadDim = 128;
+constexpr int kMaxMergeHeads = 64;  // query heads (the host enforces the limit)
 
 // Fixed part of the dynamic shared memory; the scratch floats and the weight
 // ring follow it.
@@ -52,7 +53,11 @@ struct Control {
     float gate[kRowBatch];             // SwiGLU gate rows of the current row batch
     float xres[kRowBatch];             // this CTA's residual rows, fetched with the phase input
     float gains[2 * kMaxHeadDim];      // attention q / k norm gains
+    GroupTable group[2][2];            // piece-group tables: [phase parity][group parity]
+    unsigned long long rbar;           // the next phase's records landed (descriptor + first group table)
+    unsigned long long gbar;           // a later group table of the current phase landed
     float red[kEngineWarps];
+    float merge_w[kMaxMergeHeads * kMaxAttnChunks];  // attention merge weights [head][chunk]
     unsigned long long best[kEngineWarps];
     int ok;
     int abort;                         // the compute warps stopped: the producer stops too
@@ -64,7 +69,7 @@ struct StepInfo {
     int position, token, logits_row;
 };
 
-// ---- compute-warp synchronisation (named barrier 1, the 512 compute threads) ----------
+// ---- compute-warp synchronisation (named barrier 1, the compute threads) --------------
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kEngineThreads) : "memory"); }
 // Barrier that also ANDs a predicate over the compute threads.
 __device__ __forceinline__ bool csync_and(bool v) {
@@ -128,13 +133,18 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
 }
 
-// Prefetch a phase descriptor into shared memory (completed by the next
-// cp_async_wait_all of each thread plus a compute barrier).
-__device__ void fetch_phase(Phase *dst, const Phase *src) {
-    constexpr int kGranules = static_cast<int>(sizeof(Phase) / 16);
-    for (int i = threadIdx.x; i < kGranules; i += kEngineThreads)
-        cp_async16_cg(reinterpret_cast<char *>(dst) + 16 * i, reinterpret_cast<const char *>(src) + 16 * i);
-    cp_async_commit();
+// Bulk copy of a record without an arrival (the caller arrives once with the
+// transaction bytes of all copies that complete on `bar`).
+__device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t bytes, unsigned long long *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+__device__ __forceinline__ void mbar_expect(unsigned long long *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
 }
 
 // ---- mbarrier / bulk copy primitives --------------------------------------------------
@@ -147,6 +157,18 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, int parit
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
         : "=r"(ok)
         : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// try_wait with a suspend-time hint: a waiting thread sleeps until the phase
+// completes (or the hint elapses) instead of re-polling and taking issue
+// slots from the compute warps of its sub-partition.
+__device__ __forceinline__ bool mbar_wait_sleep(unsigned long long *bar, int parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(20000u)
         : "memory");
     return ok != 0;
 }
@@ -168,10 +190,11 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 // or after kWaitLimitNs (recording 1000 + phase).
 __device__ bool wait_bar(unsigned long long *bar, int parity, StepState *st, const Control &c, int phase,
                          bool watch_abort) {
+    if (mbar_try_wait(bar, parity)) return true;
     uint64_t start = 0;
     for (unsigned spin = 0;; ++spin) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((spin & 255u) == 255u) {
+        if (mbar_wait_sleep(bar, parity)) return true;
+        if ((spin & 7u) == 7u) {
             if (*reinterpret_cast<volatile const int *>(&st->error)) return false;
             if (watch_abort && *reinterpret_cast<volatile const int *>(&c.abort)) return false;
             const uint64_t now = global_ns();
@@ -257,29 +280,35 @@ __device__ void produce(const StepControl &ctl, bool need_head, int head_phase, 
     }
     const uint64_t start = global_ns();
     for (int j = max(tail, issued - kQueue); j < issued; ++j) {
-        while (!mbar_try_wait(&c.full[j % kQueue], (j / kQueue) & 1))
+        while (!mbar_wait_sleep(&c.full[j % kQueue], (j / kQueue) & 1))
             if (global_ns() - start > kWaitLimitNs) return;
     }
 }
 
-// Consumer side: bounded wait for piece `idx`, agreed by every compute thread.
-// With `tracing`, thread 0 accounts the time to agreement and late pieces.
-__device__ bool take_piece(Control &c, int idx, StepState *st, int phase, bool tracing) {
-    unsigned long long *bar = &c.full[idx % kQueue];
-    const int parity = (idx / kQueue) & 1;
-    uint64_t t0 = 0;
-    if (tracing && threadIdx.x == 0) {
-        t0 = global_ns();
-        if (!mbar_try_wait(bar, parity)) ++c.late;
+// Warp 0: bounded wait until pieces [first, first + count) are in the ring,
+// lane k watching piece k (count <= kGroupPieces), so the checks overlap.
+// The compute barrier that follows orders the bulk-copy writes, observed
+// here, before every thread's reads of the ring.  With `tracing`, thread 0
+// accounts the waiting time and the pieces not yet landed.
+__device__ bool wait_group(Control &c, int first, int count, StepState *st, int phase, bool tracing) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t t0 = tracing && lane == 0 ? global_ns() : 0;
+    bool ok = true, late = false;
+    if (lane < count) {
+        unsigned long long *bar = &c.full[(first + lane) % kQueue];
+        const int parity = ((first + lane) / kQueue) & 1;
+        if (tracing) late = !mbar_try_wait(bar, parity);
+        ok = wait_bar(bar, parity, st, c, phase, false);
     }
-    const bool ok = csync_and(wait_bar(bar, parity, st, c, phase, false));
-    if (!ok && threadIdx.x == 0) c.abort = 1;
-    if (tracing && threadIdx.x == 0) c.wait_ns += global_ns() - t0;
+    ok = __all_sync(0xffffffffu, ok);
+    if (tracing) {
+        const int n_late = __popc(__ballot_sync(0xffffffffu, late));
+        if (lane == 0) {
+            c.late += n_late;
+            c.wait_ns += global_ns() - t0;
+        }
+    }
     return ok;
-}
-// Every compute thread has passed a compute barrier since its last read of the piece.
-__device__ __forceinline__ void release_piece(Control &c, int idx) {
-    if (threadIdx.x == 0) mbar_arrive(&c.empty[idx % kQueue]);
 }
 
 // ---- grid barrier ------------------------------------------------------------------
@@ -480,47 +509,75 @@ __device__ void rows_dot(const char *base, int dtype, int cols, int n, const flo
 
 // ---- GEMV phases ----------------------------------------------------------------------
 // Softmax-merge of the attention chunk partials into the attention output
-// (the O projection's input).  One warp per head; every load of a head (each
-// chunk's running max and sum, and up to 64 lanes' worth of accumulators) is
-// issued before the first use, so a head costs one L2 round trip for dim <= 64.
-__device__ void merge_attention(const AttnMerge &m, int position, float *in) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int total = min(position + 1, m.capacity) + (m.relay_count ? __ldcg(m.relay_count) : 0);
-    const int chunks = attn_chunks(total, m.kv_heads, gridDim.x);
-    const int d = m.dim, stride = d + 2;
-    for (int h = warp; h < m.heads; h += kEngineWarps) {
-        const float *base = m.partial + static_cast<size_t>(h) * kMaxAttnChunks * stride;
-        for (int j0 = 0; j0 < d; j0 += 64) {
-            const int ja = j0 + lane, jb = j0 + 32 + lane;
-            const float mc = lane < chunks ? __ldcg(base + lane * stride + d) : -INFINITY;
-            const float lc = lane < chunks ? __ldcg(base + lane * stride + d + 1) : 0.f;
-            float va[kMaxAttnChunks], vb[kMaxAttnChunks];
+// (the O projection's input).  Each thread requests its output columns'
+// accumulators of every chunk (kPer columns at a time) and, for the weights,
+// one (head, chunk) pair's running max and sum, all before the first use; the
+// weights w[h][c] = exp(m_c - max) / sum_c'(exp(m_c' - max) l_c') are reduced
+// over the 16 chunk lanes of a head and shared through shared memory.  One L2
+// round trip for up to kPer x (compute threads) columns.  DIM > 0 fixes the
+// head size at compile time, so that a column's chunk loads address off one
+// base register.
+template <int DIM>
+__device__ void merge_heads(const AttnMerge &m, int chunks, float *in, Control &c) {
+    constexpr int kPer = 3;
+    const int d = DIM > 0 ? DIM : m.dim, stride = d + 2;
+    const int total = m.heads * d, pairs = m.heads * kMaxAttnChunks;
+    for (int e0 = 0; e0 < total; e0 += kPer * kEngineThreads) {
+        float v[kPer][kMaxAttnChunks];
 #pragma unroll
-            for (int cc = 0; cc < kMaxAttnChunks; ++cc) {
-                va[cc] = (cc < chunks && ja < d) ? __ldcg(base + cc * stride + ja) : 0.f;
-                vb[cc] = (cc < chunks && jb < d) ? __ldcg(base + cc * stride + jb) : 0.f;
-            }
-            const float mx = warp_max(mc);
-            float w = (mc == -INFINITY) ? 0.f : expf(mc - mx);
-            const float den = warp_sum(w * lc);
-            w = w / den;
-            float a = 0.f, b = 0.f;
+        for (int q = 0; q < kPer; ++q) {
+            const int e = e0 + q * kEngineThreads + threadIdx.x;
+            const int h = e < total ? e / d : 0, j = e < total ? e - h * d : 0;
+            const float *pj = m.partial + static_cast<size_t>(h) * kMaxAttnChunks * stride + j;
 #pragma unroll
-            for (int cc = 0; cc < kMaxAttnChunks; ++cc) {
-                const float wc = __shfl_sync(0xffffffffu, w, cc);
-                a = fmaf(wc, va[cc], a);
-                b = fmaf(wc, vb[cc], b);
+            for (int cc = 0; cc < kMaxAttnChunks; ++cc) v[q][cc] = (e < total && cc < chunks) ? __ldcg(pj + cc * stride) : 0.f;
+        }
+        if (e0 == 0) {
+            for (int t0 = 0; t0 < pairs; t0 += kEngineThreads) {  // 16-lane groups = one head each
+                const int t = t0 + threadIdx.x, cc = t % kMaxAttnChunks;
+                const bool live = t < pairs && cc < chunks;
+                const float *rec = m.partial + (static_cast<size_t>(t / kMaxAttnChunks) * kMaxAttnChunks + cc) * stride + d;
+                const float mc = live ? __ldcg(rec) : -INFINITY, lc = live ? __ldcg(rec + 1) : 0.f;
+                float mx = mc;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                const float w = (mc == -INFINITY) ? 0.f : expf(mc - mx);
+                float den = w * lc;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+                if (t < pairs) c.merge_w[t] = live ? w / den : 0.f;
             }
-            if (ja < d) in[h * d + ja] = a;
-            if (jb < d) in[h * d + jb] = b;
+            csync();
+        }
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) {
+            const int e = e0 + q * kEngineThreads + threadIdx.x;
+            if (e >= total) continue;
+            const float *w = c.merge_w + (e / d) * kMaxAttnChunks;
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int cc = 0; cc < kMaxAttnChunks; cc += 2) {
+                a0 = fmaf(w[cc], v[q][cc], a0);
+                a1 = fmaf(w[cc + 1], v[q][cc + 1], a1);
+            }
+            in[e] = a0 + a1;
         }
     }
 }
 
-// Loads a GEMV phase's input vector into `in`; ends with a compute barrier.
-// `pre` runs between issuing the asynchronous loads and waiting for them.
+__device__ void merge_attention(const AttnMerge &m, int position, float *in, Control &c) {
+    const int total = min(position + 1, m.capacity) + (m.relay_count ? __ldcg(m.relay_count) : 0);
+    const int chunks = attn_chunks(total, m.kv_heads, gridDim.x);
+    if (m.dim == 64) merge_heads<64>(m, chunks, in, c);
+    else if (m.dim == 128) merge_heads<128>(m, chunks, in, c);
+    else merge_heads<0>(m, chunks, in, c);
+}
+
+// Requests a GEMV phase's input vector into `in` (complete after the
+// caller's cp_async_wait_all and a compute barrier).  `pre` runs between
+// issuing the asynchronous loads and waiting for them.
 template <typename Pre>
-__device__ void load_input(const GemvPhase &g, int cols, const StepInfo &info, float *in, Pre pre) {
+__device__ void issue_input(const GemvPhase &g, int cols, const StepInfo &info, float *in, Control &c, Pre pre) {
     if (g.input_kind == IN_EMBED_ROW) {
         pre();
         for (int j = threadIdx.x; j < cols; j += kEngineThreads) {
@@ -530,7 +587,7 @@ __device__ void load_input(const GemvPhase &g, int cols, const StepInfo &info, f
         }
     } else if (g.input_kind == IN_ATTN_MERGE) {
         pre();
-        merge_attention(g.merge, info.position, in);
+        merge_attention(g.merge, info.position, in, c);
     } else if (((reinterpret_cast<uintptr_t>(g.in) | reinterpret_cast<uintptr_t>(in)) & 15) == 0 && (cols & 3) == 0) {
         for (int e = threadIdx.x * 4; e < cols; e += kEngineThreads * 4) cp_async16_cg(in + e, g.in + e);
         pre();
@@ -550,6 +607,12 @@ __device__ void load_input(const GemvPhase &g, int cols, const StepInfo &info, f
             }
         }
     }
+}
+
+// Loads a GEMV phase's input vector into `in`; ends with a compute barrier.
+template <typename Pre>
+__device__ void load_input(const GemvPhase &g, int cols, const StepInfo &info, float *in, Control &c, Pre pre) {
+    issue_input(g, cols, info, in, c, pre);
     cp_async_wait_all();
     csync();
 }
@@ -643,48 +706,194 @@ struct ResidualRows {
     __device__ const float *rows(const Control &c, int row0) const { return in_smem ? c.xres + (row0 - r0) : nullptr; }
 };
 
+// ---- piece groups ----------------------------------------------------------------
+// Piece of the group holding dot product v (v < t.rows).
+__device__ __forceinline__ int find_piece(const GroupTable &t, int v) {
+    int k = 0;
+    while (t.p[k].seg < 0 || v >= t.p[k].vbase + t.p[k].n) ++k;
+    return k;
+}
+__device__ __forceinline__ const char *group_row(const GemvPhase &g, const GroupTable &t, int cbase, const Smem &sm,
+                                                 int v, int &dtype) {
+    const int k = find_piece(t, v);
+    const Segment &seg = g.seg[t.p[k].seg];
+    dtype = seg.dtype;
+    return reinterpret_cast<const char *>(sm.ring) + sm.c->offset[(cbase + k) % kQueue] +
+           static_cast<size_t>(v - t.p[k].vbase) * seg.cols * esize(seg.dtype);
+}
+
+// y[v] = row_v . x for the group's rows.  Many rows: each warp takes two rows
+// at a time (their reductions overlap); few rows: several warps split each
+// row and their partials are summed in a fixed order.  Ends with a compute
+// barrier (none when the group has no rows).
+__device__ void group_dots(const GemvPhase &g, const GroupTable &t, int cbase, const Smem &sm, const float *x,
+                           float *y) {
+    Control &c = *sm.c;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int R = t.rows, cols = g.seg[0].cols;
+    if (R >= kEngineWarps) {
+        for (int v = warp; v < R; v += 2 * kEngineWarps) {
+            const int v2 = v + kEngineWarps;
+            int dt;
+            const char *row = group_row(g, t, cbase, sm, v, dt);
+            float a = row_partial_any<true>(dt, row, cols, lane, 32, lane, x);
+            float b = 0.f;
+            if (v2 < R) {
+                row = group_row(g, t, cbase, sm, v2, dt);
+                b = row_partial_any<true>(dt, row, cols, lane, 32, lane, x);
+            }
+            a = warp_sum(a);
+            b = warp_sum(b);
+            if (lane == 0) {
+                y[v] = a;
+                if (v2 < R) y[v2] = b;
+            }
+        }
+        csync();
+    } else if (R > 0) {
+        const int P = kEngineWarps / R;
+        const int v = warp / P, part = warp % P;
+        if (v < R) {
+            int dt;
+            const char *row = group_row(g, t, cbase, sm, v, dt);
+            float acc = row_partial_any<true>(dt, row, cols, part * 32 + lane, 32 * P, part == 0 ? lane : -1, x);
+            acc = warp_sum(acc);
+            if (lane == 0) c.partial[v * P + part] = acc;
+        }
+        csync();
+        if (threadIdx.x < R) {
+            float total = 0.f;
+            for (int q = 0; q < P; ++q) total += c.partial[threadIdx.x * P + q];
+            y[threadIdx.x] = total;
+        }
+        csync();
+    }
+}
+
+// Epilogue of the group: thread v finishes dot product v.  `scale` is the
+// input's RMSNorm factor (applied here: scale * (W . (x * gain)) equals the
+// reference's W . ((x * scale) * gain) up to float32 rounding).
+__device__ void group_epilogue(const GemvPhase &g, const GroupTable &t, const float *y, float scale,
+                               const ResidualRows &res, const StepInfo &info, Control &c, Epi &e) {
+    const int v = threadIdx.x;
+    if (v >= t.rows) return;
+    const int k = find_piece(t, v);
+    const int s = t.p[k].seg, r = t.p[k].row0 + (v - t.p[k].vbase);
+    const float val = g.norm ? __fmul_rn(y[v], scale) : y[v];
+    switch (g.epilogue) {
+        case EPI_STORE: g.seg[s].out[r] = val; break;
+        case EPI_RESIDUAL: {
+            const float xv = res.in_smem ? c.xres[r - res.r0] : __ldcg(g.x + r);
+            g.x[r] = __fadd_rn(xv, __fmul_rn(g.scale, val));
+            break;
+        }
+        case EPI_SWIGLU:
+            if (s == 1) {  // the gate row of the same index is the previous piece's
+                const float gy = y[v - t.p[k].n];
+                const float gt = g.norm ? __fmul_rn(gy, scale) : gy;
+                g.out[r] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), val);
+            }
+            break;
+        case EPI_LOGITS:
+            g.out[static_cast<size_t>(info.logits_row) * g.seg[0].rows + r] = val;
+            if (!isfinite(val)) e.nonfinite = 1;
+            else e.best = max(e.best, argmax_key(val, r));
+            break;
+    }
+}
+
 // GEMV whose weights stream through the shared-memory ring.  `cidx` is the
-// index of the next piece of this CTA's stream (the same in every thread);
-// the pieces come in the order the host's piece table lists them: the gain
-// vector, then per segment the CTA's rows in batches of rows_per_piece
-// (SwiGLU: gate and up batches alternate).
-__device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepInfo &info, const Smem &sm, int &cidx,
-                          const Tracer &tr) {
+// index of the next piece of this CTA's stream (the same in every thread).
+// The first group's table is already in shared memory; its pieces are awaited
+// together with the input vector.  The RMSNorm's sum of squares is taken while
+// the input is scaled by the gain, and its factor is applied in the
+// epilogue, so the norm adds one compute barrier.
+// Record copies on an mbarrier: issued and awaited counts (thread 0), so that
+// an early exit can wait for a copy still in flight.
+struct RecordCopies {
+    int issued = 0, waited = 0;
+    __device__ int next_parity() { return waited++ & 1; }
+    __device__ void drain(unsigned long long *bar) {
+        const uint64_t start = global_ns();
+        for (; waited < issued; ++waited)
+            while (!mbar_wait_sleep(bar, waited & 1))
+                if (global_ns() - start > kWaitLimitNs) return;
+    }
+};
+
+__device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepInfo &info, const StepControl &ctl,
+                          const Smem &sm, int &cidx, RecordCopies &gcopies, const Tracer &tr) {
     Control &c = *sm.c;
     const int cols = g.seg[0].cols;
+    const bool tracing = tr.rec != nullptr;
+    GroupTable *tables = c.group[p & 1];
+    const GroupTable *src = ctl.groups + g.group_offset + static_cast<size_t>(blockIdx.x) * g.group_stride;
     float *in = sm.scratch;
     ResidualRows res;
-    load_input(g, cols, info, in, [&] { res.start(g); });
+    issue_input(g, cols, info, in, c, [&] { res.start(g); });
+    bool ok = true;
+    if (threadIdx.x == 0 && tables[0].more) {  // later group tables arrive one group ahead
+        mbar_expect(&c.gbar, sizeof(GroupTable));
+        bulk_copy(&tables[1], src + 1, sizeof(GroupTable), &c.gbar);
+        ++gcopies.issued;
+    }
+    if (threadIdx.x < 32) ok = wait_group(c, cidx, tables[0].count, st, p, tracing);
+    cp_async_wait_all();
     res.store(c);
+    if (!csync_and(ok)) {
+        if (threadIdx.x == 0) c.abort = 1;
+        return false;
+    }
     tr.mark(0);
+    float scale = 1.0f;
     if (g.norm) {
+        const GroupTable &t = tables[0];
         const void *gain = g.norm_gain;
-        if (g.gain_piece) {
-            if (!take_piece(c, cidx, st, p, tr.rec != nullptr)) return false;
-            gain = sm.ring + c.offset[cidx % kQueue];
+        if (t.count > 0 && t.p[0].seg < 0) gain = sm.ring + c.offset[cidx % kQueue];
+        float ss = 0.f;
+        for (int j = threadIdx.x; j < cols; j += kEngineThreads) {
+            const float xv = in[j];
+            ss = fmaf(xv, xv, ss);
+            if (gain) in[j] = __fmul_rn(xv, load_weight(gain, g.norm_gain_dtype, j));
         }
-        norm_input(in, cols, g.norm_eps, gain, g.norm_gain_dtype, c);
-        if (g.gain_piece) release_piece(c, cidx++);
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) c.red[threadIdx.x >> 5] = ss;
+        csync();
+        float total = 0.f;
+#pragma unroll
+        for (int w = 0; w < kEngineWarps; ++w) total += c.red[w];
+        // kernels.cl:25-27: scale = 1/sqrt(mean + eps)
+        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)cols), g.norm_eps)));
     }
     tr.mark(1);
     Epi e;
-    int buf = 0;
-    const bool paired = g.epilogue == EPI_SWIGLU;
-    for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
-        int r0, r1;
-        row_range(g.seg[s].rows, blockIdx.x, gridDim.x, r0, r1);
-        const int rpp = g.seg[s].rows_per_piece;
-        for (int row0 = r0; row0 < r1; row0 += rpp) {
-            const int n = min(rpp, r1 - row0);
-            for (int part = 0; part < (paired ? 2 : 1); ++part) {
-                const Segment &seg = g.seg[s + part];
-                if (!take_piece(c, cidx, st, p, tr.rec != nullptr)) return false;
-                const char *rows = reinterpret_cast<const char *>(sm.ring + c.offset[cidx % kQueue]);
-                rows_dot<true>(rows, seg.dtype, cols, n, in, c.y[buf], c);
-                release_piece(c, cidx++);
-                epilogue(g, s + part, row0, n, c.y[buf], res.rows(c, row0), info, c, e);
-                buf ^= 1;
-            }
+    for (int gi = 0;; ++gi) {
+        const GroupTable &t = tables[gi & 1];
+        float *y = c.y[gi & 1];
+        group_dots(g, t, cidx, sm, in, y);
+        const int count = t.count;
+        const bool more = t.more != 0;
+        if (threadIdx.x == 0)
+            for (int k = 0; k < count; ++k) mbar_arrive(&c.empty[(cidx + k) % kQueue]);
+        group_epilogue(g, t, y, scale, res, info, c, e);
+        cidx += count;
+        if (!more) break;
+        ok = true;
+        if (threadIdx.x < 32) {
+            if (threadIdx.x == 0) ok = wait_bar(&c.gbar, gcopies.next_parity(), st, c, p, false);  // table gi + 1
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (ok) ok = wait_group(c, cidx, tables[(gi + 1) & 1].count, st, p, tracing);
+        }
+        if (!csync_and(ok)) {
+            if (threadIdx.x == 0) c.abort = 1;
+            return false;
+        }
+        // every thread has finished group gi's epilogue: its table buffer takes group gi + 2
+        if (threadIdx.x == 0 && tables[(gi + 1) & 1].more) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_expect(&c.gbar, sizeof(GroupTable));
+            bulk_copy(&tables[gi & 1], src + gi + 2, sizeof(GroupTable), &c.gbar);
+            ++gcopies.issued;
         }
     }
     tr.mark(2);
@@ -699,7 +908,7 @@ __device__ void gemv_direct(const GemvPhase &g, StepState *st, const StepInfo &i
     const int G = gridDim.x, b = blockIdx.x, cols = g.seg[0].cols;
     float *in = sm.scratch;
     ResidualRows res;
-    load_input(g, cols, info, in, [&] { res.start(g); });
+    load_input(g, cols, info, in, c, [&] { res.start(g); });
     res.store(c);
     if (g.norm) norm_input(in, cols, g.norm_eps, g.norm_gain, g.norm_gain_dtype, c);
     Epi e;
@@ -1001,6 +1210,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
                 mbar_init(&c.full[i], 1);
                 mbar_init(&c.empty[i], 1);
             }
+            mbar_init(&c.rbar, 1);
+            mbar_init(&c.gbar, 1);
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
             c.abort = 0;
             c.wait_ns = 0;
@@ -1008,31 +1219,62 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         }
         if (!skip && ctl.trace && blockIdx.x == 0) ctl.trace[0] = global_ns();
     }
-    __syncthreads();  // the last block-wide barrier: warp 16 leaves below
+    __syncthreads();  // the last block-wide barrier: the producer warp leaves below
     if (skip) return;
-    if (threadIdx.x >= kEngineThreads) {
+    if (threadIdx.x >= kEngineThreads) {  // the producer warp
         if (threadIdx.x == kEngineThreads) produce(ctl, need_head != 0, head_phase, st, sm);
         return;
     }
-    fetch_phase(&c.phase[0], &phases[0]);
-    cp_async_wait_all();
-    csync();
-    int barriers = 0, cidx = 0;
+    // the first phase's records: descriptor, then its first group table (two round trips, once per launch)
+    RecordCopies rcopies, gcopies;
     bool ok = true;
+    if (threadIdx.x == 0) {
+        mbar_expect(&c.rbar, sizeof(Phase));
+        bulk_copy(&c.phase[0], &phases[0], sizeof(Phase), &c.rbar);
+        ++rcopies.issued;
+        ok = wait_bar(&c.rbar, rcopies.next_parity(), st, c, 0, false);
+        if (ok && c.phase[0].kind == PH_GEMV && c.phase[0].gemv.bulk) {
+            mbar_expect(&c.rbar, sizeof(GroupTable));
+            bulk_copy(&c.group[0][0],
+                      ctl.groups + c.phase[0].gemv.group_offset +
+                          static_cast<size_t>(blockIdx.x) * c.phase[0].gemv.group_stride,
+                      sizeof(GroupTable), &c.rbar);
+            ++rcopies.issued;
+            ok = wait_bar(&c.rbar, rcopies.next_parity(), st, c, 0, false);
+        }
+    }
+    ok = csync_and(ok);
+    int barriers = 0, cidx = 0;
     for (int p = 0; p < nphases - 1 && ok; ++p) {
         const Phase &ph = c.phase[p & 1];
         if (ph.layer < 0 && !need_head) break;  // the head is the last phase before the step end
-        if (p + 1 < nphases - 1) fetch_phase(&c.phase[(p + 1) & 1], &phases[p + 1]);
+        const bool prefetch = p + 1 < nphases - 1;
+        if (threadIdx.x == 0 && prefetch) {
+            // the next phase's descriptor and first group table: two bulk copies on one barrier
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const bool table = ph.next_groups >= 0;
+            mbar_expect(&c.rbar, sizeof(Phase) + (table ? sizeof(GroupTable) : 0));
+            bulk_copy(&c.phase[(p + 1) & 1], &phases[p + 1], sizeof(Phase), &c.rbar);
+            if (table)
+                bulk_copy(&c.group[(p + 1) & 1][0],
+                          ctl.groups + ph.next_groups + static_cast<size_t>(blockIdx.x) * ph.next_group_stride,
+                          sizeof(GroupTable), &c.rbar);
+            ++rcopies.issued;
+        }
         const Tracer tr{ctl.trace ? ctl.trace + 1 + static_cast<size_t>(barriers) * (gridDim.x * kTraceStamps + 1)
                                   : nullptr};
         if (ph.kind == PH_GEMV) {
-            if (ph.gemv.bulk) ok = gemv_bulk(ph.gemv, p, st, info, sm, cidx, tr);
+            if (ph.gemv.bulk) ok = gemv_bulk(ph.gemv, p, st, info, ctl, sm, cidx, gcopies, tr);
             else gemv_direct(ph.gemv, st, info, sm);
         } else if (ph.kind == PH_ATTN_GQA) {
             attn_gqa_phase(ph.attn, info, sm, tr);
         }
         if (!ok) break;
-        cp_async_wait_all();  // the next phase's descriptor (published by the barrier)
+        cp_async_wait_all();
+        // the next phase's records have landed (normally long since); the barrier publishes them
+        if (threadIdx.x == 0 && prefetch) ok = wait_bar(&c.rbar, rcopies.next_parity(), st, c, p, false);
+        ok = csync_and(ok);
+        if (!ok) break;
         tr.mark(3);
         ++barriers;
         ok = grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, p, c);
@@ -1040,7 +1282,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     }
     cp_async_wait_all();
     if (!ok) {
-        if (threadIdx.x == 0) c.abort = 1;
+        if (threadIdx.x == 0) {
+            c.abort = 1;
+            rcopies.drain(&c.rbar);  // no record copy may land after the CTA has left
+            gcopies.drain(&c.gbar);
+        }
         return;
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) {
