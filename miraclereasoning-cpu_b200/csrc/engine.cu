@@ -102,7 +102,7 @@ struct mr_model {
     float *logits = nullptr;
     int logits_rows = 0;
     float *partial = nullptr;
-    int scratch_floats = 0, ring_bytes = 0;
+    int scratch_floats = 0, attn_base = 0, ring_bytes = 0;
     size_t smem_bytes = 0;
     PieceDesc *d_pieces = nullptr;
     GroupTable *d_groups = nullptr;
@@ -553,6 +553,9 @@ StepControl base_control(mr_model *m) {
     ctl.context_length = m->cfg.context_length;
     ctl.vocab_size = m->cfg.vocab_size;
     ctl.scratch_floats = m->scratch_floats;
+    ctl.attn_base = m->attn_base;
+    ctl.inv_freq = m->d_inv_freq;
+    ctl.rope_pairs = m->cfg.head_dim / 2;
     ctl.ring_bytes = m->ring_bytes;
     ctl.pieces = m->d_pieces;
     ctl.groups = m->d_groups;
@@ -705,7 +708,10 @@ int mr_model_finalize(mr_model *m) {
     int max_cols = 0;
     for (auto &kv : m->tensors)
         if (kv.second.shape.size() == 2) max_cols = std::max(max_cols, (int)kv.second.shape[1]);
-    m->scratch_floats = std::max(max_cols, attn_layout(gq_max, d).total);
+    // the attention region follows the GEMV input vector, so that an attention
+    // tile can be requested while the preceding GEMV phase still uses its input
+    m->attn_base = (max_cols + 31) & ~31;
+    m->scratch_floats = m->attn_base + attn_layout(gq_max, d).total;
     const size_t control = decode_control_bytes();
     const size_t scratch = ((size_t)m->scratch_floats * 4 + 127) & ~size_t(127);
     const long long ring = (long long)kSmemLimit - 1024 - (long long)control - (long long)scratch;

@@ -223,7 +223,10 @@ struct StepControl {
     int *gen_out;
     int context_length;
     int vocab_size;                   // tokens outside [0, vocab) stop the step with error 4
-    int scratch_floats;               // shared-memory scratch (input vector / attention tiles)
+    int scratch_floats;               // shared-memory scratch: GEMV input vector, then the attention region
+    int attn_base;                    // float offset of the attention region (16-byte aligned)
+    const float *inv_freq;            // RoPE inverse frequencies [rope_pairs], shared by every layer
+    int rope_pairs;
     int ring_bytes;                   // shared-memory weight ring
     const PieceDesc *pieces;          // [grid][piece_stride] weight stream of each CTA
     const GroupTable *groups;         // piece groups of every (bulk phase, CTA)

@@ -53,6 +53,8 @@ struct Control {
     float gate[kRowBatch];             // SwiGLU gate rows of the current row batch
     float xres[kRowBatch];             // this CTA's residual rows, fetched with the phase input
     float gains[2 * kMaxHeadDim];      // attention q / k norm gains
+    float rope_cos[kMaxHeadDim / 2];   // RoPE cos / sin of this launch's position, per frequency
+    float rope_sin[kMaxHeadDim / 2];
     GroupTable group[2][2];            // piece-group tables: [phase parity][group parity]
     unsigned long long rbar;           // the next phase's records landed (descriptor + first group table)
     unsigned long long gbar;           // a later group table of the current phase landed
@@ -103,6 +105,7 @@ struct Tracer {
 struct Smem {
     Control *c;
     float *scratch;
+    float *attn;        // attention region of the scratch
     unsigned char *ring;
     int ring_bytes;
 };
@@ -313,12 +316,15 @@ __device__ bool wait_group(Control &c, int first, int count, StepState *st, int 
 
 // ---- grid barrier ------------------------------------------------------------------
 // Release-add arrival (cumulative over the CTA's writes ordered by the compute
-// barrier), acquire polling by thread 0, bounded by kWaitLimitNs.
-__device__ bool grid_barrier(StepState *st, unsigned long long target, int phase, Control &c) {
+// barrier), acquire polling by thread 0, bounded by kWaitLimitNs.  `during`
+// runs in every compute thread after the arrival, overlapping the wait.
+template <typename During>
+__device__ bool grid_barrier(StepState *st, unsigned long long target, int phase, Control &c, During during) {
     csync();
+    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(&st->barrier) : "memory");
+    during();
     if (threadIdx.x == 0) {
         int ok = 1;
-        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(&st->barrier) : "memory");
         uint64_t start = 0;
         for (unsigned spin = 0;; ++spin) {
             if (ld_acquire_u64(&st->barrier) >= target) break;
@@ -932,19 +938,12 @@ __device__ void gemv_direct(const GemvPhase &g, StepState *st, const StepInfo &i
 }
 
 // ---- grouped-query attention ------------------------------------------------------
-__device__ __forceinline__ void rope_pair(float &u, float &v, float angle) {
-    const float c = cosf(angle), s = sinf(angle);
-    const float a = __fsub_rn(__fmul_rn(u, c), __fmul_rn(v, s));
-    const float b = __fadd_rn(__fmul_rn(u, s), __fmul_rn(v, c));
-    u = a;
-    v = b;
-}
-
 // In-place per-head RMSNorm (optional) + RoPE of a [dim] vector held by one warp
 // in shared memory (kernels.cl rms 19-28 then rope 30-44).  `gain` is in
-// shared memory (float) or NULL.
+// shared memory (float) or NULL; cos / sin of position * inv_freq[p] come
+// from the launch's table (the same float32 values the reference computes).
 __device__ void norm_rope_warp(float *v, int dim, const float *gain, float eps, bool do_norm,
-                               const float *inv_freq, float position, int split_half) {
+                               const float *rope_cos, const float *rope_sin, int split_half) {
     const int lane = threadIdx.x & 31;
     if (do_norm) {
         float ss = 0.f;
@@ -957,10 +956,9 @@ __device__ void norm_rope_warp(float *v, int dim, const float *gain, float eps, 
     const int half = dim / 2;
     for (int p = lane; p < half; p += 32) {
         const int j = split_half ? p : 2 * p, k = split_half ? p + half : 2 * p + 1;
-        float u = v[j], w = v[k];
-        rope_pair(u, w, __fmul_rn(position, inv_freq[p]));
-        v[j] = u;
-        v[k] = w;
+        const float u = v[j], w = v[k], cs = rope_cos[p], sn = rope_sin[p];
+        v[j] = __fsub_rn(__fmul_rn(u, cs), __fmul_rn(w, sn));
+        v[k] = __fadd_rn(__fmul_rn(u, sn), __fmul_rn(w, cs));
     }
     __syncwarp();
 }
@@ -1011,27 +1009,52 @@ __device__ void issue_tile(const AttnPhase &a, int g, int tb, int nt, int start,
 // before the first wait; the newest row (this token's key and value, appended
 // to the ring by the unit that owns it) is patched into its tile in shared
 // memory.
-__device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const Smem &sm, const Tracer &tr) {
+// Attention work geometry of this step for one layer.
+struct AttnGeometry {
+    int count, length, start, total, chunks, chunk_len;
+    __device__ AttnGeometry(const AttnPhase &a, const StepInfo &info) {
+        count = info.position + 1;
+        length = min(count, a.capacity);
+        start = (count - length) % a.capacity;
+        total = length + (a.relay_count ? __ldcg(a.relay_count) : 0);
+        chunks = attn_chunks(total, a.kv_heads, gridDim.x);
+        chunk_len = (total + chunks - 1) / chunks;
+    }
+};
+
+// Requests the first key/value tile of this CTA's first attention unit (all
+// compute threads; completed by the attention phase's first wait).  Called at
+// the end of the preceding phase, so that the load overlaps the grid barrier:
+// ring rows come from earlier launches (the newest row, written in this
+// launch, is patched from shared memory by its owner), relay rows from the host.
+__device__ bool attn_first_tile(const AttnPhase &a, const StepInfo &info, const Smem &sm) {
+    const AttnGeometry geo(a, info);
+    const int unit = blockIdx.x;
+    if (unit >= a.kv_heads * geo.chunks) return false;
+    const int g = unit / geo.chunks, c = unit % geo.chunks;
+    const int t0 = c * geo.chunk_len, t1 = min(geo.total, t0 + geo.chunk_len);
+    if (t0 >= t1) return false;
+    const AttnLayout L = attn_layout(a.heads / a.kv_heads, a.dim);
+    issue_tile(a, g, t0, min(kKeyTile, t1 - t0), geo.start, geo.length, L, sm.attn + L.kt, sm.attn + L.vt);
+    return true;
+}
+
+__device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const Smem &sm, bool first_tile_issued,
+                               const Tracer &tr) {
     const int G = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = a.dim, gq = a.heads / a.kv_heads;
-    const int count = info.position + 1;
-    const int cap = a.capacity;
-    const int length = min(count, cap);
-    const int start = (count - length) % cap;
-    const int extra = a.relay_count ? __ldcg(a.relay_count) : 0;
-    const int total = length + extra;
-    const int chunks = attn_chunks(total, a.kv_heads, G);
-    const int chunk_len = (total + chunks - 1) / chunks;
-    const float pos_f = static_cast<float>(info.position);
+    const AttnGeometry geo(a, info);
+    const int count = geo.count, cap = a.capacity, length = geo.length, start = geo.start, total = geo.total;
+    const int chunks = geo.chunks, chunk_len = geo.chunk_len;
     const float sqrt_d = __fsqrt_rn(static_cast<float>(d));  // divisor, kernels.cl:72
     const int stride = d + 2;
     const bool vec = (d & 3) == 0;
 
     const AttnLayout L = attn_layout(gq, d);
-    float *q = sm.scratch + L.q, *knew = sm.scratch + L.knew, *vnew = sm.scratch + L.vnew;
-    float *kt = sm.scratch + L.kt, *vt = sm.scratch + L.vt, *p = sm.scratch + L.p, *acc = sm.scratch + L.acc;
-    float *mrow = sm.scratch + L.m, *lrow = sm.scratch + L.l, *corr = sm.scratch + L.corr;
+    float *q = sm.attn + L.q, *knew = sm.attn + L.knew, *vnew = sm.attn + L.vnew;
+    float *kt = sm.attn + L.kt, *vt = sm.attn + L.vt, *p = sm.attn + L.p, *acc = sm.attn + L.acc;
+    float *mrow = sm.attn + L.m, *lrow = sm.attn + L.l, *corr = sm.attn + L.corr;
     float *gains = sm.c->gains;
 
     for (int unit = blockIdx.x; unit < a.kv_heads * chunks; unit += G) {
@@ -1048,7 +1071,8 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
                 for (int e = threadIdx.x * 4; e < 2 * d; e += kEngineThreads * 4)
                     cp_async16_cg(e < d ? knew + e : vnew + (e - d), e < d ? ksrc + e : vsrc + (e - d));
         }
-        if (t0 < t1) issue_tile(a, g, t0, min(kKeyTile, t1 - t0), start, length, L, kt, vt);
+        if (t0 < t1 && !(first_tile_issued && unit == static_cast<int>(blockIdx.x)))
+            issue_tile(a, g, t0, min(kKeyTile, t1 - t0), start, length, L, kt, vt);
         if (!vec) {
             for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) q[e] = __ldcg(qsrc + e);
             if (owner)
@@ -1073,10 +1097,11 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
                 // 2. query heads: RMSNorm + RoPE; the owner also finishes this token's key/value
                 const float *qg = (a.qk_norm && a.q_gain) ? gains : nullptr;
                 const float *kg = (a.qk_norm && a.k_gain) ? gains + d : nullptr;
+                const float *rc = sm.c->rope_cos, *rs = sm.c->rope_sin;
                 for (int i = warp; i < gq; i += kEngineWarps)
-                    norm_rope_warp(q + i * d, d, qg, a.norm_eps, a.qk_norm != 0, a.inv_freq, pos_f, a.split_half);
+                    norm_rope_warp(q + i * d, d, qg, a.norm_eps, a.qk_norm != 0, rc, rs, a.split_half);
                 if (owner && warp == kEngineWarps - 1) {
-                    norm_rope_warp(knew, d, kg, a.norm_eps, a.qk_norm != 0, a.inv_freq, pos_f, a.split_half);
+                    norm_rope_warp(knew, d, kg, a.norm_eps, a.qk_norm != 0, rc, rs, a.split_half);
                     const size_t slot = static_cast<size_t>(g) * cap + (count - 1) % cap;
                     for (int j = lane; j < d; j += 32) a.k_cache[slot * d + j] = knew[j];
                 }
@@ -1182,6 +1207,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     sm.ring = reinterpret_cast<unsigned char *>(sm.scratch) +
               ((static_cast<size_t>(ctl.scratch_floats) * 4 + 127) & ~size_t(127));
     sm.ring_bytes = ctl.ring_bytes;
+    sm.attn = sm.scratch + ctl.attn_base;
     Control &c = *sm.c;
     const int head_phase = nphases - 2;  // the phase list ends with the head, then the step end
     __shared__ StepInfo info;
@@ -1225,6 +1251,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         if (threadIdx.x == kEngineThreads) produce(ctl, need_head != 0, head_phase, st, sm);
         return;
     }
+    // RoPE cos / sin of this launch's position (kernels.cl:30-44 computes them per element)
+    for (int i = threadIdx.x; i < ctl.rope_pairs; i += kEngineThreads) {
+        const float angle = __fmul_rn(static_cast<float>(info.position), ctl.inv_freq[i]);
+        c.rope_cos[i] = cosf(angle);
+        c.rope_sin[i] = sinf(angle);
+    }
     // the first phase's records: descriptor, then its first group table (two round trips, once per launch)
     RecordCopies rcopies, gcopies;
     bool ok = true;
@@ -1245,6 +1277,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     }
     ok = csync_and(ok);
     int barriers = 0, cidx = 0;
+    bool tile_issued = false;  // the next attention phase's first tile is in flight
     for (int p = 0; p < nphases - 1 && ok; ++p) {
         const Phase &ph = c.phase[p & 1];
         if (ph.layer < 0 && !need_head) break;  // the head is the last phase before the step end
@@ -1267,7 +1300,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             if (ph.gemv.bulk) ok = gemv_bulk(ph.gemv, p, st, info, ctl, sm, cidx, gcopies, tr);
             else gemv_direct(ph.gemv, st, info, sm);
         } else if (ph.kind == PH_ATTN_GQA) {
-            attn_gqa_phase(ph.attn, info, sm, tr);
+            attn_gqa_phase(ph.attn, info, sm, tile_issued, tr);
+            tile_issued = false;
         }
         if (!ok) break;
         cp_async_wait_all();
@@ -1277,7 +1311,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         if (!ok) break;
         tr.mark(3);
         ++barriers;
-        ok = grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, p, c);
+        // an attention phase next: its first key/value tile loads while the grid synchronises
+        const bool attn_next = prefetch && c.phase[(p + 1) & 1].kind == PH_ATTN_GQA;
+        ok = grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, p, c, [&] {
+            if (attn_next) tile_issued = attn_first_tile(c.phase[(p + 1) & 1].attn, info, sm);
+        });
         if (ok && tr.rec && blockIdx.x == 0 && threadIdx.x == 0) tr.rec[gridDim.x * kTraceStamps] = global_ns();
     }
     cp_async_wait_all();
