@@ -294,7 +294,15 @@ def run_profile_case(args):
 
 
 def run_trace(args, steps=8):
-    """Per-phase timing of decode steps from the kernel's globaltimer stamps."""
+    """Per-phase timing of decode steps from the kernel's globaltimer stamps.
+
+    Phases are not separated by grid barriers: every CTA starts a phase when it
+    has finished the previous one and its input words carry the expected tag.
+    Per phase kind (median over CTAs and steps, us): `input` = wait for the
+    input words (plus the group's weight pieces) after the CTA finished the
+    previous phase, `norm`, `compute`, `tail` (epilogue, record waits), and
+    `critical` = how far the phase moves the slowest CTA's finish time.
+    """
     import ctypes as C
     syn = _pkg("synthetic")
     native = _pkg("_native")
@@ -315,35 +323,37 @@ def run_trace(args, steps=8):
         g = grid.value
         rec = g * stamps_per_cta + 1
         t = np.frombuffer(stamps, dtype=np.uint64, count=1 + phases.value * rec).astype(np.int64)
-        start = t[0]
+        launch = t[0]
+        prev_done = np.full(g, launch)
+        prev_max = launch
         for k in range(phases.value):
-            row = t[1 + k * rec: 1 + (k + 1) * rec]
-            cta = row[:g * stamps_per_cta].reshape(g, stamps_per_cta) - start
-            exit_ = row[-1]
-            entry = per_kind.setdefault(kinds[k], {"cp0": [], "cp1": [], "cp2": [], "done_median": [],
-                                                   "done_max": [], "barrier": [], "piece_wait": [],
-                                                   "late_pieces": []})
-            for i in range(3):
-                vals = cta[:, i]
-                vals = vals[vals > 0]
-                entry[f"cp{i}"].append(np.median(vals) if len(vals) else 0)
-            entry["done_median"].append(np.median(cta[:, 3]))
-            raw = row[:g * stamps_per_cta].reshape(g, stamps_per_cta)
-            entry["piece_wait"].append(np.median(raw[:, 4]))
-            entry["late_pieces"].append(1e3 * np.median(raw[:, 5]))  # reported /1e3 below
-            entry["done_max"].append(cta[:, 3].max())
-            entry["barrier"].append(exit_ - (start + cta[:, 3].max()))
-            start = exit_
-        totals.append(start - t[0])
+            raw = t[1 + k * rec: 1 + (k + 1) * rec][:g * stamps_per_cta].reshape(g, stamps_per_cta)
+            done = raw[:, 3]
+            live = raw[:, 0] > 0  # CTAs that worked in this phase
+            entry = per_kind.setdefault(kinds[k], {"input": [], "norm": [], "compute": [], "tail": [],
+                                                   "critical": [], "piece_wait": [], "late_pieces": []})
+            if live.any():
+                r = raw[live]
+                entry["input"].append(np.median(r[:, 0] - prev_done[live]))
+                entry["norm"].append(np.median(r[:, 1] - r[:, 0]))
+                entry["compute"].append(np.median(r[:, 2] - r[:, 1]))
+                entry["tail"].append(np.median(r[:, 3] - r[:, 2]))
+                entry["piece_wait"].append(np.median(r[:, 4]))
+                entry["late_pieces"].append(1e3 * np.median(r[:, 5]))  # reported /1e3 below
+            entry["critical"].append(done.max() - prev_max)
+            prev_max = done.max()
+            prev_done = done
+        totals.append(prev_max - launch)
     report = {"config": args.config, "position": model.position, "steps": steps,
               "step_us": round(float(np.median(totals)) / 1e3, 2),
-              "legend": "us from the previous barrier exit, median over CTAs (cp*: GEMV input, norm, weights; "
-                        "attention first tile, q/k, compute); piece_wait: us waiting for weight pieces, "
-                        "late_pieces: pieces not yet in shared memory when first needed (median CTA)",
+              "legend": "us, median over working CTAs: input = wait for the phase's input words after finishing the "
+                        "previous phase; norm; compute (dot products / attention); tail (epilogue, record waits); "
+                        "critical = advance of the slowest CTA's finish; piece_wait = thread 0 waiting for weight "
+                        "pieces; late_pieces = pieces not yet in shared memory when first needed",
               "phases": {}}
     for kind, entry in per_kind.items():
-        report["phases"][kind] = {k: round(float(np.median(v)) / 1e3, 3) for k, v in entry.items()}
-        report["phases"][kind]["count_per_step"] = len(entry["barrier"]) // steps
+        report["phases"][kind] = {k: round(float(np.median(v)) / 1e3, 3) if v else 0.0 for k, v in entry.items()}
+        report["phases"][kind]["count_per_step"] = len(entry["critical"]) // steps
     print(json.dumps(report, indent=1))
     return 0
 

@@ -234,10 +234,12 @@ MR_API int mr_model_bench_decode(mr_model *model, int first_token, int steps, fl
  * executed phase has a record of grid*6 + 1 stamps at 1 + k*(grid*6 + 1):
  * CTA b's slots at offset b*6 + i (i = 0..2 phase-specific checkpoints, 3 =
  * done computing, 4 = ns spent waiting for weight pieces, 5 = pieces not yet
- * in shared memory when first needed) and CTA 0 leaving the phase's grid
- * barrier at offset grid*6.  GEMV checkpoints: input loaded, input
- * normalised, weights consumed; attention: first tile loaded, q/k prepared,
- * scores/mix done.
+ * in shared memory when first needed) and CTA 0 finishing the phase at
+ * offset grid*6 (phases are not separated by grid barriers; each CTA moves
+ * on when its own inputs have arrived).  GEMV checkpoints: input loaded,
+ * input normalised, weights consumed; attention: first tile and q/k/v
+ * loaded, q/k prepared, scores/mix done; slot 3: phase done.  A CTA with no
+ * work in a phase leaves slots 0-2 zero.
  * *phases receives the number of executed phases, *grid the CTA count.  No
  * reference counterpart (the reference has no tracing). */
 MR_API int mr_model_trace_decode(mr_model *model, int token, uint64_t *stamps, int capacity, int *phases,

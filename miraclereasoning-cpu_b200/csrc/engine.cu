@@ -98,10 +98,12 @@ struct mr_model {
     int grid = 0;
     // device buffers
     float *d_inv_freq = nullptr;
-    float *x = nullptr, *q_raw = nullptr, *k_raw = nullptr, *v_raw = nullptr, *attn = nullptr, *ffn = nullptr;
+    Word *x = nullptr, *q_raw = nullptr, *k_raw = nullptr, *v_raw = nullptr, *ffn = nullptr;  // exchange words
+    Word *attn_out = nullptr;
+    unsigned long long launches = 0;  // launches so far: each gets its own exchange tags
     float *logits = nullptr;
     int logits_rows = 0;
-    float *partial = nullptr;
+    Word *partial = nullptr;
     int scratch_floats = 0, attn_base = 0, ring_bytes = 0;
     size_t smem_bytes = 0;
     PieceDesc *d_pieces = nullptr;
@@ -223,7 +225,7 @@ const TensorSlot *tensor(mr_model *m, const std::string &name) {
     return it == m->tensors.end() ? nullptr : &it->second;
 }
 
-Segment segment(const TensorSlot *t, float *out = nullptr) {
+Segment segment(const TensorSlot *t, Word *out = nullptr) {
     Segment s{};
     s.w = t->ptr;
     s.dtype = t->dtype;
@@ -233,7 +235,7 @@ Segment segment(const TensorSlot *t, float *out = nullptr) {
     return s;
 }
 
-Phase gemv_phase(int layer, const float *in, const TensorSlot *norm_gain, float eps) {
+Phase gemv_phase(int layer, const Word *in, const TensorSlot *norm_gain, float eps) {
     Phase ph{};
     ph.kind = PH_GEMV;
     ph.layer = layer;
@@ -262,7 +264,6 @@ int build_plan(mr_model *m) {
             qkv.gemv.input_kind = IN_EMBED_ROW;
             qkv.gemv.embed = embed->ptr;
             qkv.gemv.embed_dtype = embed->dtype;
-            qkv.gemv.embed_copy = m->x;
         }
         qkv.gemv.nseg = 3;
         qkv.gemv.seg[0] = segment(tensor(m, p + "q"), m->q_raw);
@@ -296,16 +297,10 @@ int build_plan(mr_model *m) {
         a.v_cache = m->v_cache[l];
         a.capacity = m->cache_capacity[l];
         a.partial = m->partial;
+        a.out = m->attn_out;
         m->phases.push_back(at);
-        // 3. merge the attention chunks, o projection + residual (model.py:282)
-        Phase o = gemv_phase(l, nullptr, nullptr, 0.f);
-        o.gemv.input_kind = IN_ATTN_MERGE;
-        o.gemv.merge.partial = m->partial;
-        o.gemv.merge.heads = c.query_heads;
-        o.gemv.merge.kv_heads = m->layer_kvh[l];
-        o.gemv.merge.dim = c.head_dim;
-        o.gemv.merge.capacity = m->cache_capacity[l];
-        o.gemv.merge.relay_count = nullptr;
+        // 3. o projection of the attention output + residual (model.py:282)
+        Phase o = gemv_phase(l, m->attn_out, nullptr, 0.f);
         o.gemv.nseg = 1;
         o.gemv.seg[0] = segment(tensor(m, p + "o"));
         o.gemv.epilogue = EPI_RESIDUAL;
@@ -334,7 +329,7 @@ int build_plan(mr_model *m) {
     head.gemv.nseg = 1;
     head.gemv.seg[0] = segment(tensor(m, c.tie_embeddings ? "embed" : "output"));
     head.gemv.epilogue = EPI_LOGITS;
-    head.gemv.out = m->logits;
+    head.gemv.logits = m->logits;
     m->phases.push_back(head);
     Phase end{};
     end.kind = PH_STEP_END;
@@ -362,6 +357,15 @@ int build_plan(mr_model *m) {
     return MR_OK;
 }
 
+// Whether CTA b owns any rows of the phase (a CTA with none skips the phase).
+bool cta_has_rows(const GemvPhase &g, int b, int G) {
+    for (int s = 0; s < g.nseg; ++s) {
+        const long long rows = g.seg[s].rows;
+        if (rows * (b + 1) / G > rows * b / G) return true;
+    }
+    return false;
+}
+
 // The weight stream of every CTA: its pieces of every bulk phase, in the
 // order the kernel consumes them (gain vector first, then the rows; SwiGLU
 // phases alternate gate and up pieces of the same rows).
@@ -384,7 +388,7 @@ int build_pieces(mr_model *m) {
         };
         for (int b = 0; b < G; ++b) {
             std::vector<PieceDesc> &v = per[b];
-            if (g.gain_piece) {
+            if (g.gain_piece && cta_has_rows(g, b, G)) {
                 PieceDesc d{};
                 d.src = g.norm_gain;
                 d.bytes = gain_bytes;
@@ -443,7 +447,7 @@ int build_groups(mr_model *m) {
                 t = GroupTable{};
                 bytes = 0;
             };
-            if (g.gain_piece) {
+            if (g.gain_piece && cta_has_rows(g, b, G)) {
                 t.p[0] = GroupPiece{-1, 0, 0, 0};
                 t.count = 1;
                 bytes = (int)((cols * dtype_size(g.norm_gain_dtype) + 15) & ~size_t(15));
@@ -529,6 +533,8 @@ int ensure_gen(mr_model *m, int n) {
 int launch_step(mr_model *m, const StepControl &ctl) {
     int nphases = (int)m->phases.size();
     StepControl control = ctl;
+    // distinct exchange tags per launch (tags repeat only after 2^32 / nphases launches)
+    control.tag_base = static_cast<unsigned int>(++m->launches * static_cast<unsigned long long>(nphases));
     void *args[] = {&m->d_phases, &nphases, &m->state, &control};
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(m->grid);
@@ -556,6 +562,10 @@ StepControl base_control(mr_model *m) {
     ctl.attn_base = m->attn_base;
     ctl.inv_freq = m->d_inv_freq;
     ctl.rope_pairs = m->cfg.head_dim / 2;
+    const TensorSlot *embed = tensor(m, "embed");
+    ctl.embed = embed->ptr;
+    ctl.embed_dtype = embed->dtype;
+    ctl.hidden = m->cfg.hidden_size;
     ctl.ring_bytes = m->ring_bytes;
     ctl.pieces = m->d_pieces;
     ctl.groups = m->d_groups;
@@ -701,6 +711,8 @@ int mr_model_finalize(mr_model *m) {
     int rc = MR_OK;
     const int H = c.query_heads, d = c.head_dim;
     MR_REQUIRE(H <= 64, "query_heads %d above the engine limit 64", H);
+    MR_REQUIRE(c.hidden_size <= kRowBatch * m->grid, "hidden size %d above the engine limit %d (rows per CTA)",
+               c.hidden_size, kRowBatch * m->grid);
     MR_REQUIRE(d <= 128, "head_dim %d above the engine limit 128", d);
     const int max_kvh = *std::max_element(m->layer_kvh.begin(), m->layer_kvh.end());
     const int gq_max = H / *std::min_element(m->layer_kvh.begin(), m->layer_kvh.end());
@@ -719,16 +731,17 @@ int mr_model_finalize(mr_model *m) {
     m->ring_bytes = (int)(ring & ~127ll);
     m->smem_bytes = control + scratch + (size_t)m->ring_bytes;
     auto falloc = [&](size_t n) { return static_cast<float *>(device_alloc(m, n * sizeof(float), &rc)); };
+    auto walloc = [&](size_t n) { return static_cast<Word *>(device_alloc(m, n * sizeof(Word), &rc)); };
     m->d_inv_freq = falloc(d / 2);
-    m->x = falloc(c.hidden_size);
-    m->q_raw = falloc((size_t)H * d);
-    m->k_raw = falloc((size_t)max_kvh * d);
-    m->v_raw = falloc((size_t)max_kvh * d);
-    m->attn = falloc((size_t)H * d);
-    m->ffn = falloc(c.ffn_dim);
+    m->x = walloc(c.hidden_size);
+    m->q_raw = walloc((size_t)H * d);
+    m->k_raw = walloc((size_t)max_kvh * d);
+    m->v_raw = walloc((size_t)max_kvh * d);
+    m->ffn = walloc(c.ffn_dim);
+    m->attn_out = walloc((size_t)H * d);
     m->logits_rows = 64;
     m->logits = falloc((size_t)m->logits_rows * c.vocab_size);
-    m->partial = falloc((size_t)H * kMaxAttnChunks * (d + 2));
+    m->partial = walloc((size_t)H * kMaxAttnChunks * (d + 2));
     m->state = static_cast<StepState *>(device_alloc(m, sizeof(StepState), &rc));
     if (rc) return rc;
     m->k_cache.resize(c.layers);

@@ -9,6 +9,19 @@
 // CTA per SM and runs every phase of a step, separated by grid-wide barriers;
 // inside a phase each CTA takes its share of the work.
 //
+// Data exchange between phases: every vector one phase hands to the next (the
+// residual stream x, q/k/v rows, attention chunk partials, the SwiGLU
+// activation) is stored as 64-bit words {float value (low half), tag (high
+// half)}, written and read with single-copy-atomic 64-bit accesses.  The tag
+// names the launch and the producing phase, so a reader polls its words until
+// they carry the expected tag: no grid barrier between phases, one L2 round
+// trip from the last write to the reader.  Every phase reads what the phase
+// before it wrote (expected tag = tag_base + p - 1).  A buffer is rewritten
+// only after every reader of its previous contents has finished, because each
+// writer's own inputs depend, through the phase chain, on every such reader
+// having produced its output -- which is why a CTA that has no output in a
+// phase reads none of its input either.
+//
 // Weight streaming: every CTA owns a fixed row range of each weight segment.
 // A dedicated producer warp walks the CTA's slices of all weight-streaming
 // phases of the step, in order, as "pieces" (whole rows of one segment, or a
@@ -55,32 +68,23 @@ enum Epilogue : int {
 enum InputKind : int {
     IN_VECTOR = 0,      // a float vector in global memory
     IN_EMBED_ROW = 1,   // row `token` of the embedding, widened
-    IN_ATTN_MERGE = 2,  // softmax-merge of the attention chunk partials
 };
+
+typedef unsigned long long Word;  // exchanged value: float bits | tag << 32
 
 struct Segment {
     const void *w;      // [rows, cols] row-major, stored dtype
     int dtype;
     int rows, cols;
     int rows_per_piece; // rows per bulk piece (bulk phases)
-    float *out;         // EPI_STORE destination (rows floats)
-};
-
-// Chunk partials written by an attention phase, merged by the next GEMV phase.
-struct AttnMerge {
-    const float *partial;           // [heads][kMaxAttnChunks][dim + 2]: acc[dim], max, sum
-    int heads, kv_heads, dim;
-    int capacity;                   // of the layer's ring, to recompute the chunk count
-    const int *relay_count;
+    Word *out;          // EPI_STORE destination (rows words)
 };
 
 struct GemvPhase {
     int input_kind;
-    const float *in;            // IN_VECTOR source (cols floats)
+    const Word *in;             // IN_VECTOR source (cols words)
     const void *embed;          // IN_EMBED_ROW source [vocab, cols]
     int embed_dtype;
-    float *embed_copy;          // when set, CTA 0 also stores the widened row here
-    AttnMerge merge;            // IN_ATTN_MERGE source
     int norm;                   // apply RMSNorm to the input
     const void *norm_gain;      // NULL -> non-affine
     int norm_gain_dtype;
@@ -91,14 +95,15 @@ struct GemvPhase {
     int bulk;                   // weights stream through the shared-memory ring
     int epilogue;
     float scale;                // EPI_RESIDUAL scale
-    float *x;                   // EPI_RESIDUAL vector
-    float *out;                 // EPI_SWIGLU / EPI_LOGITS destination
+    Word *x;                    // EPI_RESIDUAL: the residual stream (this CTA keeps its rows in shared memory)
+    Word *out;                  // EPI_SWIGLU destination
+    float *logits;              // EPI_LOGITS destination
     int group_offset;           // bulk: this phase's group tables in StepControl::groups,
     int group_stride;           //   CTA b's g-th at group_offset + b * group_stride + g
 };
 
 struct AttnPhase {
-    const float *q_raw, *k_raw, *v_raw;
+    const Word *q_raw, *k_raw, *v_raw;
     int qk_norm;                    // per-head RMSNorm of q and k before RoPE
     const void *q_gain, *k_gain;    // its gains (NULL: non-affine)
     int gain_dtype;
@@ -111,7 +116,8 @@ struct AttnPhase {
     const float *relay_k, *relay_v; // [kv_heads][relay_capacity][dim] (flashnano-1.6) or NULL
     const int *relay_count;
     int relay_capacity;
-    float *partial;                 // [heads][kMaxAttnChunks][dim + 2]
+    Word *partial;                  // [heads][kMaxAttnChunks][dim + 2]: chunks 1.. (acc[dim], max, sum)
+    Word *out;                      // [heads * dim] attention output (the o projection's input)
 };
 
 // The compute warps take a bulk phase's pieces in groups, precomputed on the
@@ -223,10 +229,13 @@ struct StepControl {
     int *gen_out;
     int context_length;
     int vocab_size;                   // tokens outside [0, vocab) stop the step with error 4
+    unsigned int tag_base;            // exchange tags of this launch: tag_base + producing phase
     int scratch_floats;               // shared-memory scratch: GEMV input vector, then the attention region
     int attn_base;                    // float offset of the attention region (16-byte aligned)
     const float *inv_freq;            // RoPE inverse frequencies [rope_pairs], shared by every layer
     int rope_pairs;
+    const void *embed;                // embedding [vocab, hidden]: this CTA's rows of the residual stream
+    int embed_dtype, hidden;          //   start as the token's embedding
     int ring_bytes;                   // shared-memory weight ring
     const PieceDesc *pieces;          // [grid][piece_stride] weight stream of each CTA
     const GroupTable *groups;         // piece groups of every (bulk phase, CTA)
@@ -236,7 +245,7 @@ struct StepControl {
     // executed phase k a record of grid*kTraceStamps + 1 slots: CTA b's slots
     // at 1 + k*rec + b*kTraceStamps + i (i = 0..2 phase-specific checkpoints,
     // 3 = done computing, 4 = ns waiting for weight pieces, 5 = pieces not
-    // resident when first needed) and CTA 0 leaving the barrier at
+    // resident when first needed) and CTA 0 finishing the phase at
     // 1 + k*rec + grid*kTraceStamps.
     unsigned long long *trace;
 };

@@ -51,7 +51,7 @@ struct Control {
     float partial[kEngineWarps * kEngineWarps];
     float y[2][kRowBatch];             // dot products of alternate pieces
     float gate[kRowBatch];             // SwiGLU gate rows of the current row batch
-    float xres[kRowBatch];             // this CTA's residual rows, fetched with the phase input
+    float xres[kRowBatch];             // this CTA's rows of the residual stream, for the whole launch
     float gains[2 * kMaxHeadDim];      // attention q / k norm gains
     float rope_cos[kMaxHeadDim / 2];   // RoPE cos / sin of this launch's position, per frequency
     float rope_sin[kMaxHeadDim / 2];
@@ -59,7 +59,6 @@ struct Control {
     unsigned long long rbar;           // the next phase's records landed (descriptor + first group table)
     unsigned long long gbar;           // a later group table of the current phase landed
     float red[kEngineWarps];
-    float merge_w[kMaxMergeHeads * kMaxAttnChunks];  // attention merge weights [head][chunk]
     unsigned long long best[kEngineWarps];
     int ok;
     int abort;                         // the compute warps stopped: the producer stops too
@@ -69,6 +68,8 @@ struct Control {
 
 struct StepInfo {
     int position, token, logits_row;
+    unsigned tag_base;  // exchange tag of phase p: tag_base + p
+    int xr0, xr1;       // this CTA's rows of the residual stream (kept in Control::xres)
 };
 
 // ---- compute-warp synchronisation (named barrier 1, the compute threads) --------------
@@ -135,6 +136,19 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
 }
+
+// ---- exchange words (see engine.cuh) --------------------------------------------------
+__device__ __forceinline__ Word ld_word(const Word *p) {
+    Word v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_word(Word *p, float v, unsigned tag) {
+    const Word w = (static_cast<Word>(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ bool word_ok(Word w, unsigned tag) { return static_cast<unsigned>(w >> 32) == tag; }
+__device__ __forceinline__ float word_value(Word w) { return __uint_as_float(static_cast<unsigned>(w)); }
 
 // Bulk copy of a record without an arrival (the caller arrives once with the
 // transaction bytes of all copies that complete on `bar`).
@@ -209,6 +223,62 @@ __device__ bool wait_bar(unsigned long long *bar, int parity, StepState *st, con
             }
         }
     }
+}
+
+// Reads N exchange words (NULL pointer: none), polling each until it carries
+// `tag`; bounded like every wait (gives up early when another wait recorded
+// an error).  Every load is issued before the first check.
+template <int N>
+__device__ bool read_words(const Word *const (&src)[N], unsigned tag, float (&out)[N], StepState *st, int phase) {
+    Word w[N];
+#pragma unroll
+    for (int u = 0; u < N; ++u) w[u] = src[u] ? ld_word(src[u]) : (static_cast<Word>(tag) << 32);
+    uint64_t start = 0;
+    for (unsigned spin = 0;; ++spin) {
+        bool all = true;
+#pragma unroll
+        for (int u = 0; u < N; ++u)
+            if (!word_ok(w[u], tag)) {
+                all = false;
+                w[u] = ld_word(src[u]);
+            }
+        if (all) break;
+        if ((spin & 15u) == 15u) {
+            if (*reinterpret_cast<volatile const int *>(&st->error)) return false;
+            const uint64_t now = global_ns();
+            if (!start) {
+                start = now;
+            } else if (now - start > kWaitLimitNs) {
+                atomicCAS(&st->error, 0, 1000 + phase);
+                return false;
+            }
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < N; ++u) out[u] = word_value(w[u]);
+    return true;
+}
+
+// Reads n exchange words src[0..n) carrying `tag` into dst (shared memory),
+// four per thread per pass; every compute thread takes part (no barrier).
+__device__ bool read_vector(const Word *src, int n, unsigned tag, float *dst, StepState *st, int phase) {
+    bool ok = true;
+    for (int base = 0; base < n && ok; base += 4 * kEngineThreads) {
+        const Word *ptr[4];
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = base + u * kEngineThreads + threadIdx.x;
+            ptr[u] = e < n ? src + e : nullptr;
+        }
+        ok = read_words(ptr, tag, v, st, phase);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = base + u * kEngineThreads + threadIdx.x;
+            if (ok && e < n) dst[e] = v[u];
+        }
+    }
+    return ok;
 }
 
 // ---- the weight-stream producer (lane 0 of warp 16) -----------------------------------
@@ -514,113 +584,20 @@ __device__ void rows_dot(const char *base, int dtype, int cols, int n, const flo
 }
 
 // ---- GEMV phases ----------------------------------------------------------------------
-// Softmax-merge of the attention chunk partials into the attention output
-// (the O projection's input).  Each thread requests its output columns'
-// accumulators of every chunk (kPer columns at a time) and, for the weights,
-// one (head, chunk) pair's running max and sum, all before the first use; the
-// weights w[h][c] = exp(m_c - max) / sum_c'(exp(m_c' - max) l_c') are reduced
-// over the 16 chunk lanes of a head and shared through shared memory.  One L2
-// round trip for up to kPer x (compute threads) columns.  DIM > 0 fixes the
-// head size at compile time, so that a column's chunk loads address off one
-// base register.
-template <int DIM>
-__device__ void merge_heads(const AttnMerge &m, int chunks, float *in, Control &c) {
-    constexpr int kPer = 3;
-    const int d = DIM > 0 ? DIM : m.dim, stride = d + 2;
-    const int total = m.heads * d, pairs = m.heads * kMaxAttnChunks;
-    for (int e0 = 0; e0 < total; e0 += kPer * kEngineThreads) {
-        float v[kPer][kMaxAttnChunks];
-#pragma unroll
-        for (int q = 0; q < kPer; ++q) {
-            const int e = e0 + q * kEngineThreads + threadIdx.x;
-            const int h = e < total ? e / d : 0, j = e < total ? e - h * d : 0;
-            const float *pj = m.partial + static_cast<size_t>(h) * kMaxAttnChunks * stride + j;
-#pragma unroll
-            for (int cc = 0; cc < kMaxAttnChunks; ++cc) v[q][cc] = (e < total && cc < chunks) ? __ldcg(pj + cc * stride) : 0.f;
-        }
-        if (e0 == 0) {
-            for (int t0 = 0; t0 < pairs; t0 += kEngineThreads) {  // 16-lane groups = one head each
-                const int t = t0 + threadIdx.x, cc = t % kMaxAttnChunks;
-                const bool live = t < pairs && cc < chunks;
-                const float *rec = m.partial + (static_cast<size_t>(t / kMaxAttnChunks) * kMaxAttnChunks + cc) * stride + d;
-                const float mc = live ? __ldcg(rec) : -INFINITY, lc = live ? __ldcg(rec + 1) : 0.f;
-                float mx = mc;
-#pragma unroll
-                for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                const float w = (mc == -INFINITY) ? 0.f : expf(mc - mx);
-                float den = w * lc;
-#pragma unroll
-                for (int o = 8; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-                if (t < pairs) c.merge_w[t] = live ? w / den : 0.f;
-            }
-            csync();
-        }
-#pragma unroll
-        for (int q = 0; q < kPer; ++q) {
-            const int e = e0 + q * kEngineThreads + threadIdx.x;
-            if (e >= total) continue;
-            const float *w = c.merge_w + (e / d) * kMaxAttnChunks;
-            float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-            for (int cc = 0; cc < kMaxAttnChunks; cc += 2) {
-                a0 = fmaf(w[cc], v[q][cc], a0);
-                a1 = fmaf(w[cc + 1], v[q][cc + 1], a1);
-            }
-            in[e] = a0 + a1;
-        }
-    }
-}
+struct Epi {
+    unsigned long long best = 0;
+    int nonfinite = 0;
+};
 
-__device__ void merge_attention(const AttnMerge &m, int position, float *in, Control &c) {
-    const int total = min(position + 1, m.capacity) + (m.relay_count ? __ldcg(m.relay_count) : 0);
-    const int chunks = attn_chunks(total, m.kv_heads, gridDim.x);
-    if (m.dim == 64) merge_heads<64>(m, chunks, in, c);
-    else if (m.dim == 128) merge_heads<128>(m, chunks, in, c);
-    else merge_heads<0>(m, chunks, in, c);
-}
-
-// Requests a GEMV phase's input vector into `in` (complete after the
-// caller's cp_async_wait_all and a compute barrier).  `pre` runs between
-// issuing the asynchronous loads and waiting for them.
-template <typename Pre>
-__device__ void issue_input(const GemvPhase &g, int cols, const StepInfo &info, float *in, Control &c, Pre pre) {
+// Loads a GEMV phase's input vector into `in` (no barrier): the token's
+// embedding row (layer 0), else the previous phase's exchange words.
+__device__ bool read_input(const GemvPhase &g, int cols, const StepInfo &info, int p, float *in, StepState *st) {
     if (g.input_kind == IN_EMBED_ROW) {
-        pre();
-        for (int j = threadIdx.x; j < cols; j += kEngineThreads) {
-            const float v = load_weight(g.embed, g.embed_dtype, static_cast<size_t>(info.token) * cols + j);
-            in[j] = v;
-            if (g.embed_copy && blockIdx.x == 0) g.embed_copy[j] = v;
-        }
-    } else if (g.input_kind == IN_ATTN_MERGE) {
-        pre();
-        merge_attention(g.merge, info.position, in, c);
-    } else if (((reinterpret_cast<uintptr_t>(g.in) | reinterpret_cast<uintptr_t>(in)) & 15) == 0 && (cols & 3) == 0) {
-        for (int e = threadIdx.x * 4; e < cols; e += kEngineThreads * 4) cp_async16_cg(in + e, g.in + e);
-        pre();
-    } else {
-        pre();
-        for (int base = 0; base < cols; base += 4 * kEngineThreads) {
-            float v[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int e = base + u * kEngineThreads + threadIdx.x;
-                v[u] = e < cols ? __ldcg(g.in + e) : 0.f;
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int e = base + u * kEngineThreads + threadIdx.x;
-                if (e < cols) in[e] = v[u];
-            }
-        }
+        for (int j = threadIdx.x; j < cols; j += kEngineThreads)
+            in[j] = load_weight(g.embed, g.embed_dtype, static_cast<size_t>(info.token) * cols + j);
+        return true;
     }
-}
-
-// Loads a GEMV phase's input vector into `in`; ends with a compute barrier.
-template <typename Pre>
-__device__ void load_input(const GemvPhase &g, int cols, const StepInfo &info, float *in, Control &c, Pre pre) {
-    issue_input(g, cols, info, in, c, pre);
-    cp_async_wait_all();
-    csync();
+    return read_vector(g.in, cols, info.tag_base + p - 1, in, st, p);
 }
 
 // In-place RMSNorm of the input (kernels.cl:25-27: scale = 1/sqrt(mean + eps);
@@ -638,41 +615,31 @@ __device__ void norm_input(float *in, int cols, float eps, const void *gain, int
     csync();
 }
 
-struct Epi {
-    unsigned long long best = 0;
-    int nonfinite = 0;
-};
 
-// Epilogue of rows [row0, row0+n) of segment `s` whose dot products are in y.
-// `xres` (or NULL) holds the residual rows row0.. of this CTA.
-__device__ void epilogue(const GemvPhase &g, int s, int row0, int n, const float *y, const float *xres,
-                         const StepInfo &info, Control &c, Epi &e) {
-    for (int i = threadIdx.x; i < n; i += kEngineThreads) {
-        const int r = row0 + i;
-        const float v = y[i];
-        switch (g.epilogue) {
-            case EPI_STORE: g.seg[s].out[r] = v; break;
-            case EPI_RESIDUAL: {
-                const float xv = xres ? xres[i] : __ldcg(g.x + r);
-                g.x[r] = __fadd_rn(xv, __fmul_rn(g.scale, v));
-                break;
-            }
-            case EPI_SWIGLU:
-                // the gate and up rows of index i are handled by the same thread
-                if (s == 0) {
-                    c.gate[i] = v;
-                } else {
-                    const float gt = c.gate[i];
-                    g.out[r] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), v);
-                }
-                break;
-            case EPI_LOGITS:
-                g.out[static_cast<size_t>(info.logits_row) * g.seg[0].rows + r] = v;
-                if (!isfinite(v)) e.nonfinite = 1;
-                else e.best = max(e.best, argmax_key(v, r));
-                break;
+// Finishes output row r of segment s (dot product `val`, RMSNorm factor
+// already applied): exchange word, residual update, or logit.
+__device__ __forceinline__ void finish_row(const GemvPhase &g, int s, int r, float val, const StepInfo &info, int p,
+                                           Control &c, Epi &e) {
+    const unsigned tag = info.tag_base + p;
+    switch (g.epilogue) {
+        case EPI_STORE: st_word(g.seg[s].out + r, val, tag); break;
+        case EPI_RESIDUAL: {  // model.py:282-283; x rows of this CTA live in shared memory
+            const float xn = __fadd_rn(c.xres[r - info.xr0], __fmul_rn(g.scale, val));
+            c.xres[r - info.xr0] = xn;
+            st_word(g.x + r, xn, tag);
+            break;
         }
+        case EPI_LOGITS:
+            g.logits[static_cast<size_t>(info.logits_row) * g.seg[0].rows + r] = val;
+            if (!isfinite(val)) e.nonfinite = 1;
+            else e.best = max(e.best, argmax_key(val, r));
+            break;
+        default: break;  // EPI_SWIGLU: see swiglu_row
     }
+}
+// kernels.cl:46-50: out = (g / (1 + exp(-g))) * u
+__device__ __forceinline__ void swiglu_row(const GemvPhase &g, int r, float gt, float up, const StepInfo &info, int p) {
+    st_word(g.out + r, __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up), info.tag_base + p);
 }
 
 __device__ void finish_logits(StepState *st, Control &c, Epi &e) {
@@ -691,26 +658,6 @@ __device__ void finish_logits(StepState *st, Control &c, Epi &e) {
         if (m) atomicMax(&st->best, m);
     }
 }
-
-// Residual rows of this CTA, fetched while the phase input is in flight.
-struct ResidualRows {
-    int r0 = 0, r1 = 0;
-    bool in_smem = false;
-    float v = 0.f;
-    bool mine = false;
-    __device__ void start(const GemvPhase &g) {
-        if (g.epilogue != EPI_RESIDUAL) return;
-        row_range(g.seg[0].rows, blockIdx.x, gridDim.x, r0, r1);
-        in_smem = r1 - r0 <= kRowBatch;
-        mine = in_smem && static_cast<int>(threadIdx.x) < r1 - r0;
-        if (mine) v = __ldcg(g.x + r0 + threadIdx.x);
-    }
-    // After the input's compute barrier; the next compute barrier publishes it.
-    __device__ void store(Control &c) const {
-        if (mine) c.xres[threadIdx.x] = v;
-    }
-    __device__ const float *rows(const Control &c, int row0) const { return in_smem ? c.xres + (row0 - r0) : nullptr; }
-};
 
 // ---- piece groups ----------------------------------------------------------------
 // Piece of the group holding dot product v (v < t.rows).
@@ -780,40 +727,20 @@ __device__ void group_dots(const GemvPhase &g, const GroupTable &t, int cbase, c
 // input's RMSNorm factor (applied here: scale * (W . (x * gain)) equals the
 // reference's W . ((x * scale) * gain) up to float32 rounding).
 __device__ void group_epilogue(const GemvPhase &g, const GroupTable &t, const float *y, float scale,
-                               const ResidualRows &res, const StepInfo &info, Control &c, Epi &e) {
+                               const StepInfo &info, int p, Control &c, Epi &e) {
     const int v = threadIdx.x;
     if (v >= t.rows) return;
     const int k = find_piece(t, v);
     const int s = t.p[k].seg, r = t.p[k].row0 + (v - t.p[k].vbase);
     const float val = g.norm ? __fmul_rn(y[v], scale) : y[v];
-    switch (g.epilogue) {
-        case EPI_STORE: g.seg[s].out[r] = val; break;
-        case EPI_RESIDUAL: {
-            const float xv = res.in_smem ? c.xres[r - res.r0] : __ldcg(g.x + r);
-            g.x[r] = __fadd_rn(xv, __fmul_rn(g.scale, val));
-            break;
-        }
-        case EPI_SWIGLU:
-            if (s == 1) {  // the gate row of the same index is the previous piece's
-                const float gy = y[v - t.p[k].n];
-                const float gt = g.norm ? __fmul_rn(gy, scale) : gy;
-                g.out[r] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), val);
-            }
-            break;
-        case EPI_LOGITS:
-            g.out[static_cast<size_t>(info.logits_row) * g.seg[0].rows + r] = val;
-            if (!isfinite(val)) e.nonfinite = 1;
-            else e.best = max(e.best, argmax_key(val, r));
-            break;
+    if (g.epilogue != EPI_SWIGLU) {
+        finish_row(g, s, r, val, info, p, c, e);
+    } else if (s == 1) {  // the gate row of the same index is in the previous piece
+        const float gy = y[v - t.p[k].n];
+        swiglu_row(g, r, g.norm ? __fmul_rn(gy, scale) : gy, val, info, p);
     }
 }
 
-// GEMV whose weights stream through the shared-memory ring.  `cidx` is the
-// index of the next piece of this CTA's stream (the same in every thread).
-// The first group's table is already in shared memory; its pieces are awaited
-// together with the input vector.  The RMSNorm's sum of squares is taken while
-// the input is scaled by the gain, and its factor is applied in the
-// epilogue, so the norm adds one compute barrier.
 // Record copies on an mbarrier: issued and awaited counts (thread 0), so that
 // an early exit can wait for a copy still in flight.
 struct RecordCopies {
@@ -827,16 +754,22 @@ struct RecordCopies {
     }
 };
 
+// GEMV whose weights stream through the shared-memory ring.  `cidx` is the
+// index of the next piece of this CTA's stream (the same in every thread).
+// The first group's table is already in shared memory.  A CTA without rows
+// in the phase skips it (and reads none of its input).  The first group's
+// pieces are awaited (warp 0) while the input words are polled; the RMSNorm's
+// sum of squares is taken while the input is scaled by the gain, and its
+// factor is applied in the epilogue.
 __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepInfo &info, const StepControl &ctl,
                           const Smem &sm, int &cidx, RecordCopies &gcopies, const Tracer &tr) {
     Control &c = *sm.c;
+    GroupTable *tables = c.group[p & 1];
+    if (tables[0].count == 0 && !tables[0].more) return true;  // no rows here
     const int cols = g.seg[0].cols;
     const bool tracing = tr.rec != nullptr;
-    GroupTable *tables = c.group[p & 1];
     const GroupTable *src = ctl.groups + g.group_offset + static_cast<size_t>(blockIdx.x) * g.group_stride;
     float *in = sm.scratch;
-    ResidualRows res;
-    issue_input(g, cols, info, in, c, [&] { res.start(g); });
     bool ok = true;
     if (threadIdx.x == 0 && tables[0].more) {  // later group tables arrive one group ahead
         mbar_expect(&c.gbar, sizeof(GroupTable));
@@ -844,8 +777,7 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
         ++gcopies.issued;
     }
     if (threadIdx.x < 32) ok = wait_group(c, cidx, tables[0].count, st, p, tracing);
-    cp_async_wait_all();
-    res.store(c);
+    ok = read_input(g, cols, info, p, in, st) && ok;
     if (!csync_and(ok)) {
         if (threadIdx.x == 0) c.abort = 1;
         return false;
@@ -881,7 +813,7 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
         const bool more = t.more != 0;
         if (threadIdx.x == 0)
             for (int k = 0; k < count; ++k) mbar_arrive(&c.empty[(cidx + k) % kQueue]);
-        group_epilogue(g, t, y, scale, res, info, c, e);
+        group_epilogue(g, t, y, scale, info, p, c, e);
         cidx += count;
         if (!more) break;
         ok = true;
@@ -908,14 +840,24 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
     return true;
 }
 
-// GEMV reading weights straight from global memory (shapes the ring cannot take).
-__device__ void gemv_direct(const GemvPhase &g, StepState *st, const StepInfo &info, const Smem &sm) {
+// GEMV reading weights straight from global memory (shapes the ring cannot
+// take).  A CTA without rows in the phase skips it.
+__device__ bool gemv_direct(const GemvPhase &g, int p, StepState *st, const StepInfo &info, const Smem &sm) {
     Control &c = *sm.c;
     const int G = gridDim.x, b = blockIdx.x, cols = g.seg[0].cols;
+    bool mine = false;
+    for (int s = 0; s < g.nseg; ++s) {
+        int r0, r1;
+        row_range(g.seg[s].rows, b, G, r0, r1);
+        mine = mine || r1 > r0;
+    }
+    if (!mine) return true;
     float *in = sm.scratch;
-    ResidualRows res;
-    load_input(g, cols, info, in, c, [&] { res.start(g); });
-    res.store(c);
+    const bool ok = read_input(g, cols, info, p, in, st);
+    if (!csync_and(ok)) {
+        if (threadIdx.x == 0) c.abort = 1;
+        return false;
+    }
     if (g.norm) norm_input(in, cols, g.norm_eps, g.norm_gain, g.norm_gain_dtype, c);
     Epi e;
     int buf = 0;
@@ -929,12 +871,18 @@ __device__ void gemv_direct(const GemvPhase &g, StepState *st, const StepInfo &i
                 const Segment &seg = g.seg[s + part];
                 const char *base = static_cast<const char *>(seg.w) + static_cast<size_t>(rb) * cols * esize(seg.dtype);
                 rows_dot<false>(base, seg.dtype, cols, n, in, c.y[buf], c);
-                epilogue(g, s + part, rb, n, c.y[buf], res.rows(c, rb), info, c, e);
+                // the gate and up rows of index i are finished by the same thread
+                for (int i = threadIdx.x; i < n; i += kEngineThreads) {
+                    if (!paired) finish_row(g, s, rb + i, c.y[buf][i], info, p, c, e);
+                    else if (part == 0) c.gate[i] = c.y[buf][i];
+                    else swiglu_row(g, rb + i, c.gate[i], c.y[buf][i], info, p);
+                }
                 buf ^= 1;
             }
         }
     }
     if (g.epilogue == EPI_LOGITS) finish_logits(st, c, e);
+    return true;
 }
 
 // ---- grouped-query attention ------------------------------------------------------
@@ -1002,13 +950,6 @@ __device__ void issue_tile(const AttnPhase &a, int g, int tb, int nt, int start,
     cp_async_commit();
 }
 
-// Work unit = (KV head g, chunk c of the attended rows): one pass over the
-// chunk's keys (in tiles of kKeyTile) for the group's query heads; writes the
-// chunk's (acc, max, sum) for the consumer to merge.  The group's raw q rows,
-// this token's raw k/v rows (owner) and the first tile are all requested
-// before the first wait; the newest row (this token's key and value, appended
-// to the ring by the unit that owns it) is patched into its tile in shared
-// memory.
 // Attention work geometry of this step for one layer.
 struct AttnGeometry {
     int count, length, start, total, chunks, chunk_len;
@@ -1024,9 +965,9 @@ struct AttnGeometry {
 
 // Requests the first key/value tile of this CTA's first attention unit (all
 // compute threads; completed by the attention phase's first wait).  Called at
-// the end of the preceding phase, so that the load overlaps the grid barrier:
-// ring rows come from earlier launches (the newest row, written in this
-// launch, is patched from shared memory by its owner), relay rows from the host.
+// the end of the preceding phase: ring rows come from earlier launches (the
+// newest row, written in this launch, is patched from shared memory by its
+// owner), relay rows from the host.
 __device__ bool attn_first_tile(const AttnPhase &a, const StepInfo &info, const Smem &sm) {
     const AttnGeometry geo(a, info);
     const int unit = blockIdx.x;
@@ -1039,8 +980,80 @@ __device__ bool attn_first_tile(const AttnPhase &a, const StepInfo &info, const 
     return true;
 }
 
-__device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const Smem &sm, bool first_tile_issued,
-                               const Tracer &tr) {
+// Unit (g, 0) of each KV head merges its group's chunks into the attention
+// output: the reference's softmax over all keys (model.py:95-116) equals
+// sum_c w_c acc_c with w_c = exp(m_c - M) / sum_c' exp(m_c' - M) l_c', M the
+// largest chunk maximum.  Its own chunk is in shared memory; the others are
+// polled as exchange words.  Output rows go out as exchange words for the o
+// projection.  `scratch` holds 3 * gq * kMaxAttnChunks floats.
+__device__ bool merge_chunks(const AttnPhase &a, int g, int gq, int chunks, const float *acc, const float *mrow,
+                             const float *lrow, float *scratch, unsigned tag, StepState *st, int phase) {
+    const int d = a.dim, stride = d + 2, others = chunks - 1;
+    float *mm = scratch, *ll = scratch + gq * kMaxAttnChunks, *ww = scratch + 2 * gq * kMaxAttnChunks;
+    auto rec = [&](int i, int cc) {
+        return a.partial + (static_cast<size_t>(g * gq + i) * kMaxAttnChunks + cc) * stride;
+    };
+    bool ok = true;
+    for (int e0 = 0; e0 < gq * d; e0 += kEngineThreads) {
+        const int e = e0 + threadIdx.x, i = e / d, j = e - i * d;
+        const bool live = e < gq * d;
+        // this element's accumulator in chunks 1.., and (first pass) one chunk's running max / sum
+        const Word *ptr[kMaxAttnChunks + 1];
+        float v[kMaxAttnChunks + 1];
+#pragma unroll
+        for (int cc = 1; cc < kMaxAttnChunks; ++cc) ptr[cc - 1] = (live && cc < chunks) ? rec(i, cc) + j : nullptr;
+        const int t = threadIdx.x, pi = t / max(others, 1), pc = 1 + t % max(others, 1);
+        const bool pair = e0 == 0 && t < gq * others;
+        ptr[kMaxAttnChunks - 1] = pair ? rec(pi, pc) + d : nullptr;
+        ptr[kMaxAttnChunks] = pair ? rec(pi, pc) + d + 1 : nullptr;
+        ok = read_words(ptr, tag, v, st, phase) && ok;
+        if (e0 == 0) {
+            if (pair) {
+                mm[pi * kMaxAttnChunks + pc] = v[kMaxAttnChunks - 1];
+                ll[pi * kMaxAttnChunks + pc] = v[kMaxAttnChunks];
+            }
+            if (t < gq) {
+                mm[t * kMaxAttnChunks] = mrow[t];
+                ll[t * kMaxAttnChunks] = lrow[t];
+            }
+            csync();
+            if (t < gq) {
+                float mx = -INFINITY;
+                for (int cc = 0; cc < chunks; ++cc) mx = fmaxf(mx, mm[t * kMaxAttnChunks + cc]);
+                float den = 0.f;
+                for (int cc = 0; cc < chunks; ++cc) {
+                    const float m = mm[t * kMaxAttnChunks + cc];
+                    const float w = (m == -INFINITY) ? 0.f : expf(m - mx);
+                    ww[t * kMaxAttnChunks + cc] = w;
+                    den += w * ll[t * kMaxAttnChunks + cc];
+                }
+                for (int cc = 0; cc < chunks; ++cc) ww[t * kMaxAttnChunks + cc] /= den;
+            }
+            csync();
+        }
+        if (live) {
+            const float *w = ww + i * kMaxAttnChunks;
+            float sum = w[0] * acc[e];
+#pragma unroll
+            for (int cc = 1; cc < kMaxAttnChunks; ++cc)
+                if (cc < chunks) sum = fmaf(w[cc], v[cc - 1], sum);
+            st_word(a.out + static_cast<size_t>(g * gq + i) * d + j, sum, tag);
+        }
+    }
+    return ok;
+}
+
+// Work unit = (KV head g, chunk c of the attended rows): one pass over the
+// chunk's keys (in tiles of kKeyTile) for the group's query heads.  The
+// group's raw q rows and (owner) this token's raw k/v rows come from the qkv
+// phase as exchange words; the newest row (this token's key and value,
+// appended to the ring by the unit that owns it) is patched into its tile in
+// shared memory.  Units c > 0 publish their chunk (acc, max, sum) as exchange
+// words; unit c = 0 merges (merge_chunks).  With chunks >= 2 there are never
+// more units than CTAs, so a merging unit never waits for work queued behind
+// it on its own CTA.
+__device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph, const Smem &sm,
+                               bool first_tile_issued, StepState *st, const Tracer &tr) {
     const int G = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = a.dim, gq = a.heads / a.kv_heads;
@@ -1050,6 +1063,7 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
     const float sqrt_d = __fsqrt_rn(static_cast<float>(d));  // divisor, kernels.cl:72
     const int stride = d + 2;
     const bool vec = (d & 3) == 0;
+    const unsigned in_tag = info.tag_base + ph - 1, out_tag = info.tag_base + ph;
 
     const AttnLayout L = attn_layout(gq, d);
     float *q = sm.attn + L.q, *knew = sm.attn + L.knew, *vnew = sm.attn + L.vnew;
@@ -1062,23 +1076,9 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
         const int t0 = c * chunk_len, t1 = min(total, t0 + chunk_len);
         const int newest = length - 1;
         const bool owner = newest >= t0 && newest < t1;
-        const float *qsrc = a.q_raw + static_cast<size_t>(g) * gq * d;
-        const float *ksrc = a.k_raw + static_cast<size_t>(g) * d, *vsrc = a.v_raw + static_cast<size_t>(g) * d;
-        // 1. issue: the group's raw q rows, (owner) the raw k/v row, the first tile
-        if (vec) {
-            for (int e = threadIdx.x * 4; e < gq * d; e += kEngineThreads * 4) cp_async16_cg(q + e, qsrc + e);
-            if (owner)
-                for (int e = threadIdx.x * 4; e < 2 * d; e += kEngineThreads * 4)
-                    cp_async16_cg(e < d ? knew + e : vnew + (e - d), e < d ? ksrc + e : vsrc + (e - d));
-        }
+        // 1. the first tile (unless requested at the end of the previous phase), norm gains
         if (t0 < t1 && !(first_tile_issued && unit == static_cast<int>(blockIdx.x)))
             issue_tile(a, g, t0, min(kKeyTile, t1 - t0), start, length, L, kt, vt);
-        if (!vec) {
-            for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) q[e] = __ldcg(qsrc + e);
-            if (owner)
-                for (int e = threadIdx.x; e < 2 * d; e += kEngineThreads)
-                    (e < d ? knew[e] : vnew[e - d]) = __ldcg(e < d ? ksrc + e : vsrc + (e - d));
-        }
         if (a.qk_norm && a.q_gain)
             for (int e = threadIdx.x; e < 2 * d; e += kEngineThreads)
                 gains[e] = load_weight(e < d ? a.q_gain : a.k_gain, a.gain_dtype, e < d ? e : e - d);
@@ -1087,14 +1087,38 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
             mrow[threadIdx.x] = -INFINITY;
             lrow[threadIdx.x] = 0.f;
         }
+        // 2. the group's q rows and (owner) this token's k / v rows
+        bool ok = true;
+        const int nq = gq * d, nread = nq + (owner ? 2 * d : 0);
+        for (int base = 0; base < nread && ok; base += 4 * kEngineThreads) {
+            const Word *ptr[4];
+            float v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = base + u * kEngineThreads + threadIdx.x;
+                ptr[u] = e >= nread ? nullptr
+                         : e < nq   ? a.q_raw + static_cast<size_t>(g) * nq + e
+                         : e < nq + d ? a.k_raw + static_cast<size_t>(g) * d + (e - nq)
+                                      : a.v_raw + static_cast<size_t>(g) * d + (e - nq - d);
+            }
+            ok = read_words(ptr, in_tag, v, st, ph);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = base + u * kEngineThreads + threadIdx.x;
+                if (!ok || e >= nread) continue;
+                if (e < nq) q[e] = v[u];
+                else if (e < nq + d) knew[e - nq] = v[u];
+                else vnew[e - nq - d] = v[u];
+            }
+        }
         bool first = true;
         for (int tb = t0; tb < t1; tb += kKeyTile) {
             const int nt = min(kKeyTile, t1 - tb);
             cp_async_wait_all();
-            csync();
+            if (!csync_and(ok)) return false;
             if (first) {
                 tr.mark(0);
-                // 2. query heads: RMSNorm + RoPE; the owner also finishes this token's key/value
+                // 3. query heads: RMSNorm + RoPE; the owner also finishes this token's key/value
                 const float *qg = (a.qk_norm && a.q_gain) ? gains : nullptr;
                 const float *kg = (a.qk_norm && a.k_gain) ? gains + d : nullptr;
                 const float *rc = sm.c->rope_cos, *rs = sm.c->rope_sin;
@@ -1122,7 +1146,7 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
                 }
                 csync();
             }
-            // 3. scores (4 independent partial sums per dot product)
+            // 4. scores (4 independent partial sums per dot product)
             for (int e = threadIdx.x; e < gq * nt; e += kEngineThreads) {
                 const int i = e / nt, t = e - i * nt;
                 const float *qi = q + i * d, *kr = kt + t * L.kstride;
@@ -1142,7 +1166,7 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
                 p[i * kKeyTile + t] = __fdiv_rn((s0 + s1) + (s2 + s3), sqrt_d);
             }
             csync();
-            // 4. online softmax per query head
+            // 5. online softmax per query head
             for (int i = warp; i < gq; i += kEngineWarps) {
                 float mt = -INFINITY;
                 for (int t = lane; t < nt; t += 32) mt = fmaxf(mt, p[i * kKeyTile + t]);
@@ -1163,7 +1187,7 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
                 }
             }
             csync();
-            // 5. value mix (4 independent partial sums)
+            // 6. value mix (4 independent partial sums)
             for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
                 const int i = e / d, j = e - i * d;
                 const float *pi = p + i * kKeyTile;
@@ -1182,18 +1206,28 @@ __device__ void attn_gqa_phase(const AttnPhase &a, const StepInfo &info, const S
             if (tb + kKeyTile < t1) issue_tile(a, g, tb + kKeyTile, min(kKeyTile, t1 - tb - kKeyTile), start, length, L, kt, vt);
         }
         tr.mark(2);
-        // 6. publish the chunk partial: acc[d], running max, running sum
-        for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
-            const int i = e / d, j = e - i * d;
-            a.partial[(static_cast<size_t>(g * gq + i) * kMaxAttnChunks + c) * stride + j] = acc[e];
-        }
-        if (threadIdx.x < gq) {
-            float *rec = a.partial + (static_cast<size_t>(g * gq + threadIdx.x) * kMaxAttnChunks + c) * stride;
-            rec[d] = mrow[threadIdx.x];
-            rec[d + 1] = lrow[threadIdx.x];
+        // 7. the chunk's result: output rows (single chunk), a published partial, or the merge
+        if (chunks == 1) {
+            for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
+                const int i = e / d, j = e - i * d;
+                st_word(a.out + static_cast<size_t>(g * gq + i) * d + j, __fdiv_rn(acc[e], lrow[i]), out_tag);
+            }
+        } else if (c > 0) {
+            for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
+                const int i = e / d, j = e - i * d;
+                st_word(a.partial + (static_cast<size_t>(g * gq + i) * kMaxAttnChunks + c) * stride + j, acc[e], out_tag);
+            }
+            if (threadIdx.x < gq) {
+                Word *rec = a.partial + (static_cast<size_t>(g * gq + threadIdx.x) * kMaxAttnChunks + c) * stride;
+                st_word(rec + d, mrow[threadIdx.x], out_tag);
+                st_word(rec + d + 1, lrow[threadIdx.x], out_tag);
+            }
+        } else if (!csync_and(merge_chunks(a, g, gq, chunks, acc, mrow, lrow, p, out_tag, st, ph))) {
+            return false;
         }
         csync();
     }
+    return true;
 }
 
 }  // namespace
@@ -1222,6 +1256,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         info.token = (rel >= 0 && rel < ctl.feed_len) ? ctl.feed[rel] : vs->token;
         need_head = ctl.return_all || rel >= ctl.feed_len - 1;
         info.logits_row = ctl.return_all ? rel % ctl.logits_rows : 0;
+        info.tag_base = ctl.tag_base;
+        row_range(ctl.hidden, blockIdx.x, gridDim.x, info.xr0, info.xr1);
         base = vs->barrier_base;
         if (!skip && pos >= ctl.context_length) {
             if (blockIdx.x == 0) atomicCAS(&st->error, 0, 3);
@@ -1257,6 +1293,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         c.rope_cos[i] = cosf(angle);
         c.rope_sin[i] = sinf(angle);
     }
+    // this CTA's rows of the residual stream start as the token's embedding
+    for (int i = threadIdx.x; i < info.xr1 - info.xr0; i += kEngineThreads)
+        c.xres[i] = load_weight(ctl.embed, ctl.embed_dtype, static_cast<size_t>(info.token) * ctl.hidden + info.xr0 + i);
     // the first phase's records: descriptor, then its first group table (two round trips, once per launch)
     RecordCopies rcopies, gcopies;
     bool ok = true;
@@ -1276,7 +1315,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         }
     }
     ok = csync_and(ok);
-    int barriers = 0, cidx = 0;
+    int cidx = 0, executed = 0;
     bool tile_issued = false;  // the next attention phase's first tile is in flight
     for (int p = 0; p < nphases - 1 && ok; ++p) {
         const Phase &ph = c.phase[p & 1];
@@ -1294,13 +1333,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
                           sizeof(GroupTable), &c.rbar);
             ++rcopies.issued;
         }
-        const Tracer tr{ctl.trace ? ctl.trace + 1 + static_cast<size_t>(barriers) * (gridDim.x * kTraceStamps + 1)
+        const Tracer tr{ctl.trace ? ctl.trace + 1 + static_cast<size_t>(executed) * (gridDim.x * kTraceStamps + 1)
                                   : nullptr};
         if (ph.kind == PH_GEMV) {
             if (ph.gemv.bulk) ok = gemv_bulk(ph.gemv, p, st, info, ctl, sm, cidx, gcopies, tr);
-            else gemv_direct(ph.gemv, st, info, sm);
+            else ok = gemv_direct(ph.gemv, p, st, info, sm);
         } else if (ph.kind == PH_ATTN_GQA) {
-            attn_gqa_phase(ph.attn, info, sm, tile_issued, tr);
+            ok = attn_gqa_phase(ph.attn, info, p, sm, tile_issued, st, tr);
             tile_issued = false;
         }
         if (!ok) break;
@@ -1309,16 +1348,20 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         if (threadIdx.x == 0 && prefetch) ok = wait_bar(&c.rbar, rcopies.next_parity(), st, c, p, false);
         ok = csync_and(ok);
         if (!ok) break;
+        // an attention phase next: its first key/value tile loads while the q/k/v words are awaited
+        if (prefetch && c.phase[(p + 1) & 1].kind == PH_ATTN_GQA)
+            tile_issued = attn_first_tile(c.phase[(p + 1) & 1].attn, info, sm);
         tr.mark(3);
-        ++barriers;
-        // an attention phase next: its first key/value tile loads while the grid synchronises
-        const bool attn_next = prefetch && c.phase[(p + 1) & 1].kind == PH_ATTN_GQA;
-        ok = grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, p, c, [&] {
-            if (attn_next) tile_issued = attn_first_tile(c.phase[(p + 1) & 1].attn, info, sm);
-        });
-        if (ok && tr.rec && blockIdx.x == 0 && threadIdx.x == 0) tr.rec[gridDim.x * kTraceStamps] = global_ns();
+        if (tr.rec && blockIdx.x == 0 && threadIdx.x == 0) tr.rec[gridDim.x * kTraceStamps] = global_ns();
+        ++executed;
     }
     cp_async_wait_all();
+    // one grid barrier per step: every CTA's logits and argmax are in before the step ends
+    int barriers = 0;
+    if (ok && need_head) {
+        ++barriers;
+        ok = grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, nphases - 2, c, [] {});
+    }
     if (!ok) {
         if (threadIdx.x == 0) {
             c.abort = 1;
