@@ -512,7 +512,8 @@ __device__ float row_partial(const char *rp, int cols, int first, int stride, in
     using D = RowDot<DT>;
     const int nv = cols / D::VEC;
     const size_t row_bytes = static_cast<size_t>(cols) * esize(DT);
-    float acc = 0.f;
+    // four independent accumulators: the chunks' FMA chains overlap
+    float acc = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
     if (FROM_SMEM || (row_bytes & 15) == 0) {
         const uint4 *v = reinterpret_cast<const uint4 *>(rp);
         int c = first;
@@ -526,11 +527,19 @@ __device__ float row_partial(const char *rp, int cols, int first, int stride, in
                 w3 = ld_stream(v + c + 3 * stride);
             }
             acc += D::chunk(w0, x + c * D::VEC);
-            acc += D::chunk(w1, x + (c + stride) * D::VEC);
-            acc += D::chunk(w2, x + (c + 2 * stride) * D::VEC);
-            acc += D::chunk(w3, x + (c + 3 * stride) * D::VEC);
+            acc1 += D::chunk(w1, x + (c + stride) * D::VEC);
+            acc2 += D::chunk(w2, x + (c + 2 * stride) * D::VEC);
+            acc3 += D::chunk(w3, x + (c + 3 * stride) * D::VEC);
         }
-        for (; c < nv; c += stride) acc += D::chunk(FROM_SMEM ? ld_smem(v + c) : ld_stream(v + c), x + c * D::VEC);
+        if (c + stride < nv) {
+            const uint4 w0 = FROM_SMEM ? ld_smem(v + c) : ld_stream(v + c);
+            const uint4 w1 = FROM_SMEM ? ld_smem(v + c + stride) : ld_stream(v + c + stride);
+            acc1 += D::chunk(w0, x + c * D::VEC);
+            acc2 += D::chunk(w1, x + (c + stride) * D::VEC);
+            c += 2 * stride;
+        }
+        for (; c < nv; c += stride) acc3 += D::chunk(FROM_SMEM ? ld_smem(v + c) : ld_stream(v + c), x + c * D::VEC);
+        acc = (acc + acc1) + (acc2 + acc3);
         if (!FROM_SMEM && tail_lane >= 0)
             for (int j = nv * D::VEC + tail_lane; j < cols; j += 32) acc = fmaf(load_weight(rp, DT, j), x[j], acc);
     } else if (tail_lane >= 0) {
@@ -590,14 +599,44 @@ struct Epi {
 };
 
 // Loads a GEMV phase's input vector into `in` (no barrier): the token's
-// embedding row (layer 0), else the previous phase's exchange words.
-__device__ bool read_input(const GemvPhase &g, int cols, const StepInfo &info, int p, float *in, StepState *st) {
+// embedding row (layer 0), else the previous phase's exchange words.  With
+// `gain` (an RMSNorm input; NULL gain pointer = non-affine), stores x * gain
+// instead and returns this thread's part of sum(x^2) in `ss`: the norm's
+// factor is then applied to the dot products (kernels.cl:19-28 computes
+// (x * scale) * gain; scale * (W . (x * gain)) differs by float32 rounding).
+__device__ bool read_input(const GemvPhase &g, int cols, const StepInfo &info, int p, float *in, StepState *st,
+                           bool norm, const void *gain, float &ss) {
+    ss = 0.f;
+    auto put = [&](int j, float v) {
+        if (norm) {
+            ss = fmaf(v, v, ss);
+            if (gain) v = __fmul_rn(v, load_weight(gain, g.norm_gain_dtype, j));
+        }
+        in[j] = v;
+    };
     if (g.input_kind == IN_EMBED_ROW) {
         for (int j = threadIdx.x; j < cols; j += kEngineThreads)
-            in[j] = load_weight(g.embed, g.embed_dtype, static_cast<size_t>(info.token) * cols + j);
+            put(j, load_weight(g.embed, g.embed_dtype, static_cast<size_t>(info.token) * cols + j));
         return true;
     }
-    return read_vector(g.in, cols, info.tag_base + p - 1, in, st, p);
+    const unsigned tag = info.tag_base + p - 1;
+    bool ok = true;
+    for (int base = 0; base < cols && ok; base += 4 * kEngineThreads) {
+        const Word *ptr[4];
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = base + u * kEngineThreads + threadIdx.x;
+            ptr[u] = e < cols ? g.in + e : nullptr;
+        }
+        ok = read_words(ptr, tag, v, st, p);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = base + u * kEngineThreads + threadIdx.x;
+            if (ok && e < cols) put(e, v[u]);
+        }
+    }
+    return ok;
 }
 
 // In-place RMSNorm of the input (kernels.cl:25-27: scale = 1/sqrt(mean + eps);
@@ -777,7 +816,19 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
         ++gcopies.issued;
     }
     if (threadIdx.x < 32) ok = wait_group(c, cidx, tables[0].count, st, p, tracing);
-    ok = read_input(g, cols, info, p, in, st) && ok;
+    // the norm gain travels as the first group's first piece: every thread
+    // observes its landing (long since, normally) before reading it
+    const void *gain = g.norm_gain;
+    if (g.norm && tables[0].count > 0 && tables[0].p[0].seg < 0) {
+        ok = wait_bar(&c.full[cidx % kQueue], (cidx / kQueue) & 1, st, c, p, false) && ok;
+        gain = sm.ring + c.offset[cidx % kQueue];
+    }
+    float ss = 0.f;
+    ok = ok && read_input(g, cols, info, p, in, st, g.norm != 0, gain, ss);
+    if (g.norm) {
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) c.red[threadIdx.x >> 5] = ss;
+    }
     if (!csync_and(ok)) {
         if (threadIdx.x == 0) c.abort = 1;
         return false;
@@ -785,18 +836,6 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
     tr.mark(0);
     float scale = 1.0f;
     if (g.norm) {
-        const GroupTable &t = tables[0];
-        const void *gain = g.norm_gain;
-        if (t.count > 0 && t.p[0].seg < 0) gain = sm.ring + c.offset[cidx % kQueue];
-        float ss = 0.f;
-        for (int j = threadIdx.x; j < cols; j += kEngineThreads) {
-            const float xv = in[j];
-            ss = fmaf(xv, xv, ss);
-            if (gain) in[j] = __fmul_rn(xv, load_weight(gain, g.norm_gain_dtype, j));
-        }
-        ss = warp_sum(ss);
-        if ((threadIdx.x & 31) == 0) c.red[threadIdx.x >> 5] = ss;
-        csync();
         float total = 0.f;
 #pragma unroll
         for (int w = 0; w < kEngineWarps; ++w) total += c.red[w];
@@ -853,7 +892,8 @@ __device__ bool gemv_direct(const GemvPhase &g, int p, StepState *st, const Step
     }
     if (!mine) return true;
     float *in = sm.scratch;
-    const bool ok = read_input(g, cols, info, p, in, st);
+    float ss;
+    const bool ok = read_input(g, cols, info, p, in, st, false, nullptr, ss);
     if (!csync_and(ok)) {
         if (threadIdx.x == 0) c.abort = 1;
         return false;
