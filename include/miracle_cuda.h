@@ -229,6 +229,21 @@ MR_API int mr_model_last_experts(const mr_model *model, int layer, int loop, int
  * stream.  No reference counterpart. */
 MR_API int mr_model_bench_decode(mr_model *model, int first_token, int steps, float *device_ms);
 
+/* Resident tensors of a finalized model, for the families whose token step
+ * runs on the host over the op kernels (flashnano-1.6, FlashLighting, Heavy
+ * Medium; the decode engine covers the grouped-query families).  They replace
+ * the reference's WeightCache (weights.py:258-297): the weights stay in HBM in
+ * their stored dtype.
+ *   mr_model_linear: y[rows, out] = x[rows, in] . W^T, W = the named tensor;
+ *     the reference's linear arithmetic (kernels.cl:5-17) over the exactly
+ *     widened weights, so bit-identical to it.
+ *   mr_model_tensor_rows: rows [row0, row0 + nrows) widened to float32 into
+ *     `out` (a 1-D tensor is one row).
+ *   mr_model_tensor_download: the whole tensor widened to float32 on the host. */
+MR_API int mr_model_linear(mr_model *model, const char *name, const mr_buffer *x, int rows, mr_buffer *y);
+MR_API int mr_model_tensor_rows(mr_model *model, const char *name, int64_t row0, int64_t nrows, mr_buffer *out);
+MR_API int mr_model_tensor_download(mr_model *model, const char *name, float *host, size_t count);
+
 /* Tracing: run one decode step (feeding `token`) with per-phase device
  * timestamps (globaltimer, ns).  Layout: stamps[0] = launch start; the k-th
  * executed phase has a record of grid*6 + 1 stamps at 1 + k*(grid*6 + 1):

@@ -94,6 +94,7 @@ struct mr_model {
     std::vector<void *> allocations;
     bool finalized = false;
     bool failed = false;
+    bool op_path = false;  // no decode plan: the token step runs on the host over the op kernels
     int position = 0;
     int grid = 0;
     // device buffers
@@ -577,6 +578,9 @@ StepControl base_control(mr_model *m) {
 int ready(mr_model *m) {
     MR_REQUIRE(m, "model is NULL");
     if (!m->finalized) return set_error(MR_ERR_STATE, "model is not finalized");
+    if (m->op_path)
+        return set_error(MR_ERR_STATE, "family %d has no decode-engine plan: its token step runs on the host over "
+                         "the op kernels (mr_model_linear and mr_op_*)", m->cfg.family);
     if (m->failed)
         return set_error(MR_ERR_STATE, "A previous device operation failed; call reset() before reusing this model");
     MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
@@ -623,6 +627,29 @@ int run_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
 }
 
 }  // namespace
+
+namespace mr {
+// A finalized model's resident tensor (tensor_ops.cu): device pointer, stored
+// dtype, and its shape as rows x cols (1-D tensors: 1 x n).
+int model_tensor(mr_model *m, const char *name, const void **ptr, int *dtype, int64_t *rows, int64_t *cols) {
+    MR_REQUIRE(m && name, "NULL argument");
+    if (!m->finalized) return set_error(MR_ERR_STATE, "model is not finalized");
+    auto it = m->tensors.find(name);
+    MR_REQUIRE(it != m->tensors.end(), "unknown tensor %s", name);
+    const TensorSlot &t = it->second;
+    *ptr = t.ptr;
+    *dtype = t.dtype;
+    *rows = t.shape.size() == 2 ? t.shape[0] : 1;
+    *cols = t.shape.size() == 2 ? t.shape[1] : t.shape[0];
+    return MR_OK;
+}
+int model_stream(mr_model *m, cudaStream_t *stream, int *device) {
+    MR_REQUIRE(m, "model is NULL");
+    *stream = m->ctx->stream;
+    *device = m->ctx->device;
+    return MR_OK;
+}
+}  // namespace mr
 
 extern "C" {
 
@@ -705,8 +732,12 @@ int mr_model_finalize(mr_model *m) {
     for (auto &kv : m->tensors)
         if (!kv.second.ptr || kv.second.dtype < 0)
             return set_error(MR_ERR_ARGUMENT, "Missing tensor %s", kv.first.c_str());
-    if (!is_gqa_family(m->cfg.family))
-        return set_error(MR_ERR_ARGUMENT, "family %d is not supported by this engine build yet", m->cfg.family);
+    if (!is_gqa_family(m->cfg.family)) {
+        // resident weights only; the host drives the op kernels (tensor_ops.cu)
+        m->op_path = true;
+        m->finalized = true;
+        return MR_OK;
+    }
     const mr_model_config &c = m->cfg;
     int rc = MR_OK;
     const int H = c.query_heads, d = c.head_dim;
@@ -782,7 +813,7 @@ int mr_model_reset(mr_model *m) {
     MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
     if (!m->finalized) return set_error(MR_ERR_STATE, "model is not finalized");
     MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
-    MR_CUDA_TRY(cudaMemset(m->state, 0, sizeof(StepState)));
+    if (!m->op_path) MR_CUDA_TRY(cudaMemset(m->state, 0, sizeof(StepState)));
     m->position = 0;
     m->failed = false;
     return MR_OK;

@@ -8,11 +8,13 @@ weight_cache_bytes)``, ``from_pretrained``, ``prefill(ids, return_all)``,
 and error types.
 
 What runs underneath is different: the checkpoint's stored bytes are copied
-once into HBM (no LRU, no host widening), and each token is one launch of the
-persistent decode kernel (csrc/engine_kernel.cu).  Greedy ``generate`` runs
-entirely on the device (argmax feeds the next step); sampled ``generate``
-reads the logits each step and samples on the host with the reference's exact
-NumPy procedure.
+once into HBM (no LRU, no host widening).  For the grouped-query families
+(flashnano-1.5/1.7, FlashLite) each token is one launch of the persistent
+decode kernel (csrc/engine_kernel.cu) and greedy ``generate`` runs entirely on
+the device (argmax feeds the next step).  flashnano-1.6, FlashLighting and
+Heavy Medium step on the host over the op kernels against the resident
+weights (stepper.py).  Sampled ``generate`` reads the logits each step and
+samples on the host with the reference's exact NumPy procedure.
 """
 from __future__ import annotations
 
@@ -26,6 +28,7 @@ import numpy as np
 from . import _native
 from .backend import CUDABackend
 from .config import ModelConfig
+from .stepper import FAMILIES as HOST_STEPPED, OpStepper
 from .weights import DTYPE_BF16, DTYPE_F32, SafeTensors, ShardedSafeTensors, adapt_weights, expected_shapes, \
     stored_tensor
 
@@ -121,6 +124,7 @@ class MiracleModel:
         _native.call("mr_model_weight_bytes", self._handle, C.byref(used))
         self.weight_cache = ResidentWeights(int(used.value), weight_cache_bytes)
         self.frequencies = backend.upload(inv)
+        self._stepper = OpStepper(self) if config.family in HOST_STEPPED else None
         self.reset()
 
     def __del__(self):
@@ -177,17 +181,29 @@ class MiracleModel:
     def reset(self):
         """Release sequence caches while retaining weights."""
         _native.call("mr_model_reset", self._handle)
+        if self._stepper is not None:
+            self._stepper.reset()
         self._failed = False
 
     @property
     def position(self):
+        if self._stepper is not None:
+            return self._stepper.position
         value = C.c_int()
         _native.call("mr_model_position", self._handle, C.byref(value))
         return value.value
 
     @property
+    def decisions(self):
+        """Per token and layer, the discrete choices of the host-stepped families
+        (heavy top-k blocks, MoE experts and weights, latent positions)."""
+        return self._stepper.decisions if self._stepper is not None else []
+
+    @property
     def states(self):
         """Per-layer cache views with the attributes the reference exposes."""
+        if self._stepper is not None:
+            return self._stepper.states
         c = self.config
         views = []
         for layer in range(c.layers):
@@ -241,8 +257,16 @@ class MiracleModel:
         V = self.config.vocab_size
         out = np.empty((len(ids), V) if return_all else (V,), dtype=np.float32)
         try:
-            _native.call("mr_model_prefill", self._handle, ids.ctypes.data_as(_I32), len(ids), int(return_all),
-                         out.ctypes.data_as(_F32))
+            if self._stepper is not None:
+                for i, token in enumerate(ids):
+                    hidden = self._stepper.step(int(token))
+                    if return_all:
+                        out[i] = self._stepper.logits(hidden)
+                    elif i == len(ids) - 1:
+                        out[:] = self._stepper.logits(hidden)
+            else:
+                _native.call("mr_model_prefill", self._handle, ids.ctypes.data_as(_I32), len(ids), int(return_all),
+                             out.ctypes.data_as(_F32))
         except Exception:
             self._failed = True
             raise
@@ -270,14 +294,14 @@ class MiracleModel:
         self.reset()
         if max_new_tokens == 0:
             return []
-        if temperature == 0:
+        if temperature == 0 and self._stepper is None:
             return self._generate_greedy(tokens, max_new_tokens, eos)
         rng, generated = np.random.default_rng(seed), []
         logits = self.prefill(tokens)
         for i in range(max_new_tokens):
             if not np.all(np.isfinite(logits)):
                 raise FloatingPointError("non-finite output logits")
-            token = sample_next(logits, temperature, top_k, top_p, rng)
+            token = int(np.argmax(logits)) if temperature == 0 else sample_next(logits, temperature, top_k, top_p, rng)
             generated.append(token)
             if token == eos or i + 1 == max_new_tokens:
                 break

@@ -82,6 +82,89 @@ def test_generate_greedy_and_sampled(backend, name):
     assert tokens == golden["greedy"].tolist()
 
 
+# ---- families stepped on the host over the op kernels (stepper.py) -----------------
+OP_CASES = ("nano16", "lighting", "lighting_drop", "heavy", "heavy_mid")
+
+
+def _state_summary(model):
+    """The reference's cache state in the fixtures' format (make_golden.py state_summary)."""
+    out = []
+    for st in model.states:
+        entry = {}
+        if "ring" in st:
+            r = st["ring"]
+            entry["ring"] = [r.count, r.length, r.start, r.capacity]
+        if "relay" in st:
+            entry["relay"] = st["relay"].count
+        if "latent" in st:
+            entry["latent_rows"] = st["latent"].shape[0]
+            entry["positions"] = list(st["positions"])
+            entry["counts"] = list(st["counts"])
+            entry["memory_size"] = st["memory_size"]
+        if "loops" in st:
+            entry["loops"] = [[s["ring"].count, s["ring"].capacity] for s in st["loops"]]
+        out.append(entry)
+    return out
+
+
+def _decisions(model):
+    """Per token: per-layer choices flattened across layers, as the fixtures hold them."""
+    out = []
+    for token in model.decisions:
+        entry = {"topk": [], "experts": [], "expert_weights": [], "latent_positions": [], "memory_size": []}
+        for layer in token:
+            for key in entry:
+                entry[key].extend(layer.get(key, []))
+        out.append(entry)
+    return out
+
+
+@pytest.mark.parametrize("name", OP_CASES)
+def test_op_path_prefill_state_and_decisions(backend, name):
+    golden = np.load(cases.GOLDEN_DIR / f"micro_{name}.npz")
+    meta = json.loads(str(golden["meta"]))
+    model = _model(backend, name)
+    prompt = cases.micro_prompt(name)
+    logits = model.prefill(prompt, return_all=True)
+    np.testing.assert_allclose(logits, golden["logits"], atol=ATOL, rtol=RTOL)
+    assert model.position == len(prompt)
+    assert _state_summary(model) == meta["state"]
+    got, want = _decisions(model), meta["decisions"]
+    assert len(got) == len(want)
+    for g, w in zip(got, want):
+        for key in ("topk", "experts", "latent_positions", "memory_size"):
+            assert g[key] == w[key], key
+        # the weights come from the device softmax (CUDA expf; the fixtures used glibc's expf)
+        for gw, ww in zip(g["expert_weights"], w["expert_weights"]):
+            np.testing.assert_allclose(gw, ww, rtol=1e-5, atol=1e-7)
+    model.reset()
+    np.testing.assert_array_equal(model.prefill(prompt), logits[-1])
+
+
+@pytest.mark.parametrize("name", OP_CASES)
+def test_op_path_chunked_and_stepped(backend, name):
+    golden = np.load(cases.GOLDEN_DIR / f"micro_{name}.npz")
+    model = _model(backend, name)
+    prompt = cases.micro_prompt(name)
+    whole = model.prefill(prompt, return_all=True)
+    model.reset()
+    chunked = np.concatenate([model.prefill(prompt[:5], return_all=True), model.prefill(prompt[5:], return_all=True)])
+    np.testing.assert_allclose(chunked, golden["chunked"], atol=ATOL, rtol=RTOL)
+    np.testing.assert_array_equal(chunked, whole)
+    model.reset()
+    np.testing.assert_array_equal(np.stack([model.decode(t) for t in prompt]), whole)
+
+
+@pytest.mark.parametrize("name", OP_CASES)
+def test_op_path_generate(backend, name):
+    golden = np.load(cases.GOLDEN_DIR / f"micro_{name}.npz")
+    model = _model(backend, name)
+    prompt = cases.micro_prompt(name)
+    assert model.generate(prompt[:3], max_new_tokens=6) == golden["greedy"].tolist()
+    assert model.generate(prompt[:2], max_new_tokens=5, temperature=0.8, top_k=5, top_p=0.9,
+                          seed=7) == golden["sampled"].tolist()
+
+
 def test_cache_bounds_and_validation(backend):
     # tests/test_inference.py:52-69 on the engine
     config = cases.micro_config("nano15")
