@@ -1020,65 +1020,57 @@ __device__ bool attn_first_tile(const AttnPhase &a, const StepInfo &info, const 
     return true;
 }
 
-// Unit (g, 0) of each KV head merges its group's chunks into the attention
-// output: the reference's softmax over all keys (model.py:95-116) equals
-// sum_c w_c acc_c with w_c = exp(m_c - M) / sum_c' exp(m_c' - M) l_c', M the
-// largest chunk maximum.  Its own chunk is in shared memory; the others are
-// polled as exchange words.  Output rows go out as exchange words for the o
-// projection.  `scratch` holds 3 * gq * kMaxAttnChunks floats.
-__device__ bool merge_chunks(const AttnPhase &a, int g, int gq, int chunks, const float *acc, const float *mrow,
-                             const float *lrow, float *scratch, unsigned tag, StepState *st, int phase) {
-    const int d = a.dim, stride = d + 2, others = chunks - 1;
-    float *mm = scratch, *ll = scratch + gq * kMaxAttnChunks, *ww = scratch + 2 * gq * kMaxAttnChunks;
+// After publishing its own chunk, every unit of a KV head merges one slice
+// (1/chunks) of the head group's attention output: the reference's softmax
+// over all keys (model.py:95-116) equals sum_c w_c acc_c with
+// w_c = exp(m_c - M) / sum_c' exp(m_c' - M) l_c', M the largest chunk maximum.
+// One polling call per thread brings in its slice element's accumulators of
+// every chunk and one (head, chunk) running max / sum; the weights are reduced
+// over 16-lane groups (one per head).  Output rows go out as exchange words
+// for the o projection.  `scratch` holds gq * kMaxAttnChunks floats.
+__device__ bool merge_slice(const AttnPhase &a, int g, int gq, int chunks, int c, float *scratch, unsigned tag,
+                            StepState *st, int phase) {
+    const int d = a.dim, stride = d + 2, n = gq * d;
+    const int per = (n + chunks - 1) / chunks, e0 = c * per, e1 = min(n, e0 + per);
     auto rec = [&](int i, int cc) {
         return a.partial + (static_cast<size_t>(g * gq + i) * kMaxAttnChunks + cc) * stride;
     };
     bool ok = true;
-    for (int e0 = 0; e0 < gq * d; e0 += kEngineThreads) {
-        const int e = e0 + threadIdx.x, i = e / d, j = e - i * d;
-        const bool live = e < gq * d;
-        // this element's accumulator in chunks 1.., and (first pass) one chunk's running max / sum
-        const Word *ptr[kMaxAttnChunks + 1];
-        float v[kMaxAttnChunks + 1];
+    for (int base = e0; base < e1 || base == e0; base += kEngineThreads) {
+        const int e = base + threadIdx.x, i = e / d, j = e - i * d;
+        const bool live = e < e1;
+        const int t = threadIdx.x, pi = t / kMaxAttnChunks, pc = t % kMaxAttnChunks;
+        const bool pair = base == e0 && pi < gq && pc < chunks;
+        const Word *ptr[kMaxAttnChunks + 2];
+        float v[kMaxAttnChunks + 2];
 #pragma unroll
-        for (int cc = 1; cc < kMaxAttnChunks; ++cc) ptr[cc - 1] = (live && cc < chunks) ? rec(i, cc) + j : nullptr;
-        const int t = threadIdx.x, pi = t / max(others, 1), pc = 1 + t % max(others, 1);
-        const bool pair = e0 == 0 && t < gq * others;
-        ptr[kMaxAttnChunks - 1] = pair ? rec(pi, pc) + d : nullptr;
-        ptr[kMaxAttnChunks] = pair ? rec(pi, pc) + d + 1 : nullptr;
+        for (int cc = 0; cc < kMaxAttnChunks; ++cc) ptr[cc] = (live && cc < chunks) ? rec(i, cc) + j : nullptr;
+        ptr[kMaxAttnChunks] = pair ? rec(pi, pc) + d : nullptr;
+        ptr[kMaxAttnChunks + 1] = pair ? rec(pi, pc) + d + 1 : nullptr;
         ok = read_words(ptr, tag, v, st, phase) && ok;
-        if (e0 == 0) {
-            if (pair) {
-                mm[pi * kMaxAttnChunks + pc] = v[kMaxAttnChunks - 1];
-                ll[pi * kMaxAttnChunks + pc] = v[kMaxAttnChunks];
-            }
-            if (t < gq) {
-                mm[t * kMaxAttnChunks] = mrow[t];
-                ll[t * kMaxAttnChunks] = lrow[t];
-            }
-            csync();
-            if (t < gq) {
-                float mx = -INFINITY;
-                for (int cc = 0; cc < chunks; ++cc) mx = fmaxf(mx, mm[t * kMaxAttnChunks + cc]);
-                float den = 0.f;
-                for (int cc = 0; cc < chunks; ++cc) {
-                    const float m = mm[t * kMaxAttnChunks + cc];
-                    const float w = (m == -INFINITY) ? 0.f : expf(m - mx);
-                    ww[t * kMaxAttnChunks + cc] = w;
-                    den += w * ll[t * kMaxAttnChunks + cc];
-                }
-                for (int cc = 0; cc < chunks; ++cc) ww[t * kMaxAttnChunks + cc] /= den;
+        if (base == e0) {
+            if (t < 32 * ((gq * kMaxAttnChunks + 31) / 32)) {  // whole warps: 16-lane groups = one head each
+                const float m = pair ? v[kMaxAttnChunks] : -INFINITY, l = pair ? v[kMaxAttnChunks + 1] : 0.f;
+                float mx = m;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                const float w = (m == -INFINITY) ? 0.f : expf(m - mx);
+                float den = w * l;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+                if (pi < gq) scratch[t] = pair ? w / den : 0.f;
             }
             csync();
         }
         if (live) {
-            const float *w = ww + i * kMaxAttnChunks;
-            float sum = w[0] * acc[e];
+            const float *w = scratch + i * kMaxAttnChunks;
+            float sum = 0.f;
 #pragma unroll
-            for (int cc = 1; cc < kMaxAttnChunks; ++cc)
-                if (cc < chunks) sum = fmaf(w[cc], v[cc - 1], sum);
-            st_word(a.out + static_cast<size_t>(g * gq + i) * d + j, sum, tag);
+            for (int cc = 0; cc < kMaxAttnChunks; ++cc)
+                if (cc < chunks) sum = fmaf(w[cc], v[cc], sum);
+            st_word(a.out + static_cast<size_t>(g * gq) * d + e, sum, tag);
         }
+        if (base + kEngineThreads >= e1) break;
     }
     return ok;
 }
@@ -1088,10 +1080,10 @@ __device__ bool merge_chunks(const AttnPhase &a, int g, int gq, int chunks, cons
 // group's raw q rows and (owner) this token's raw k/v rows come from the qkv
 // phase as exchange words; the newest row (this token's key and value,
 // appended to the ring by the unit that owns it) is patched into its tile in
-// shared memory.  Units c > 0 publish their chunk (acc, max, sum) as exchange
-// words; unit c = 0 merges (merge_chunks).  With chunks >= 2 there are never
-// more units than CTAs, so a merging unit never waits for work queued behind
-// it on its own CTA.
+// shared memory.  Every unit publishes its chunk (acc, max, sum) as exchange
+// words and then merges one slice of the group's output (merge_slice).  With
+// chunks >= 2 there are never more units than CTAs, so a merging unit never
+// waits for work queued behind it on its own CTA.
 __device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph, const Smem &sm,
                                bool first_tile_issued, StepState *st, const Tracer &tr) {
     const int G = gridDim.x;
@@ -1246,13 +1238,13 @@ __device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph,
             if (tb + kKeyTile < t1) issue_tile(a, g, tb + kKeyTile, min(kKeyTile, t1 - tb - kKeyTile), start, length, L, kt, vt);
         }
         tr.mark(2);
-        // 7. the chunk's result: output rows (single chunk), a published partial, or the merge
+        // 7. the chunk's result: output rows (single chunk), else publish the chunk and merge a slice
         if (chunks == 1) {
             for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
                 const int i = e / d, j = e - i * d;
                 st_word(a.out + static_cast<size_t>(g * gq + i) * d + j, __fdiv_rn(acc[e], lrow[i]), out_tag);
             }
-        } else if (c > 0) {
+        } else {
             for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
                 const int i = e / d, j = e - i * d;
                 st_word(a.partial + (static_cast<size_t>(g * gq + i) * kMaxAttnChunks + c) * stride + j, acc[e], out_tag);
@@ -1262,8 +1254,7 @@ __device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph,
                 st_word(rec + d, mrow[threadIdx.x], out_tag);
                 st_word(rec + d + 1, lrow[threadIdx.x], out_tag);
             }
-        } else if (!csync_and(merge_chunks(a, g, gq, chunks, acc, mrow, lrow, p, out_tag, st, ph))) {
-            return false;
+            if (!csync_and(merge_slice(a, g, gq, chunks, c, p, out_tag, st, ph))) return false;
         }
         csync();
     }
