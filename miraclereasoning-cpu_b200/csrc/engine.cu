@@ -352,6 +352,11 @@ int build_plan(mr_model *m) {
         }
         if (g.epilogue == EPI_SWIGLU && g.seg[0].rows_per_piece != g.seg[1].rows_per_piece) bulk = false;
         g.bulk = bulk;
+        g.wdtype = g.seg[0].dtype;
+        for (int i = 1; i < g.nseg; ++i)
+            if (g.seg[i].dtype != g.wdtype) g.wdtype = -1;
+        // the input vector is staged split only where the ring feeds 16-bit rows of one dtype
+        g.xsplit = bulk && (g.wdtype == MR_DTYPE_BF16 || g.wdtype == MR_DTYPE_F16);
         const int gain_bytes = (g.seg[0].cols * (int)dtype_size(g.norm_gain_dtype) + 15) & ~15;
         g.gain_piece = bulk && g.norm && g.norm_gain && gain_bytes <= piece_cap;
     }

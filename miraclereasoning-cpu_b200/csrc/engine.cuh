@@ -98,6 +98,8 @@ struct GemvPhase {
     Word *x;                    // EPI_RESIDUAL: the residual stream (this CTA keeps its rows in shared memory)
     Word *out;                  // EPI_SWIGLU destination
     float *logits;              // EPI_LOGITS destination
+    int wdtype;                 // bulk: the segments' common dtype, -1 when they differ
+    int xsplit;                 // the input vector is staged split for 16-bit weights (see XView)
     int group_offset;           // bulk: this phase's group tables in StepControl::groups,
     int group_stride;           //   CTA b's g-th at group_offset + b * group_stride + g
 };

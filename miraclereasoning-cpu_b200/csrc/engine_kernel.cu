@@ -434,14 +434,32 @@ __device__ float block_sum(float v, Control &c) {
 }
 
 // ---- dot products -------------------------------------------------------------------
+// The input vector x of a GEMV phase, as staged in shared memory.  Weights are
+// read in 16-byte chunks (8 BF16/F16 or 4 F32 columns).  For 16-bit weights in
+// the ring, x is stored split ("lo" plane: columns 8c..8c+3 of chunk c at
+// lo + 4c; "hi" plane: 8c+4..8c+7 at hi + 4c), so that a warp reading the
+// chunks lane, lane + 32, ... loads consecutive 16-byte blocks (no bank
+// conflict); otherwise x is plain (lo = x, hi = x + 4, stride 8 or 4).
+struct XView {
+    const float *lo, *hi, *plain;
+    int stride;
+    __device__ __forceinline__ float4 L(int c) const { return *reinterpret_cast<const float4 *>(lo + c * stride); }
+    __device__ __forceinline__ float4 H(int c) const { return *reinterpret_cast<const float4 *>(hi + c * stride); }
+};
+__device__ __forceinline__ XView x_split(const float *in, int cols) { return XView{in, in + cols / 2, nullptr, 4}; }
+__device__ __forceinline__ XView x_plain(const float *in, int dtype) {
+    return dtype == MR_DTYPE_F32 ? XView{in, in, in, 4} : XView{in, in + 4, in, 8};
+}
+// Position of column j of x in the split layout.
+__device__ __forceinline__ int split_index(int j, int cols) { return (j >> 3) * 4 + (j & 3) + ((j & 4) ? cols / 2 : 0); }
+
 template <int DT>
 struct RowDot;
 
 template <>
 struct RowDot<MR_DTYPE_BF16> {
     static constexpr int VEC = 8;
-    __device__ static float chunk(const uint4 &w, const float *x) {
-        const float4 a = *reinterpret_cast<const float4 *>(x), b = *reinterpret_cast<const float4 *>(x + 4);
+    __device__ static float chunk(const uint4 &w, const float4 a, const float4 b) {
         float acc = __uint_as_float(w.x << 16) * a.x;
         acc = fmaf(__uint_as_float(w.x & 0xffff0000u), a.y, acc);
         acc = fmaf(__uint_as_float(w.y << 16), a.z, acc);
@@ -457,8 +475,7 @@ struct RowDot<MR_DTYPE_BF16> {
 template <>
 struct RowDot<MR_DTYPE_F16> {
     static constexpr int VEC = 8;
-    __device__ static float chunk(const uint4 &w, const float *x) {
-        const float4 a = *reinterpret_cast<const float4 *>(x), b = *reinterpret_cast<const float4 *>(x + 4);
+    __device__ static float chunk(const uint4 &w, const float4 a, const float4 b) {
         const __half2 *h = reinterpret_cast<const __half2 *>(&w);
         const float2 p0 = __half22float2(h[0]), p1 = __half22float2(h[1]), p2 = __half22float2(h[2]),
                      p3 = __half22float2(h[3]);
@@ -477,8 +494,7 @@ struct RowDot<MR_DTYPE_F16> {
 template <>
 struct RowDot<MR_DTYPE_F32> {
     static constexpr int VEC = 4;
-    __device__ static float chunk(const uint4 &w, const float *x) {
-        const float4 a = *reinterpret_cast<const float4 *>(x);
+    __device__ static float chunk(const uint4 &w, const float4 a, const float4) {
         float acc = __uint_as_float(w.x) * a.x;
         acc = fmaf(__uint_as_float(w.y), a.y, acc);
         acc = fmaf(__uint_as_float(w.z), a.z, acc);
@@ -486,6 +502,11 @@ struct RowDot<MR_DTYPE_F32> {
         return acc;
     }
 };
+
+template <int DT>
+__device__ __forceinline__ float xchunk(const uint4 &w, const XView &x, int c) {
+    return RowDot<DT>::chunk(w, x.L(c), DT == MR_DTYPE_F32 ? float4{} : x.H(c));
+}
 
 // Weights read straight from global memory (non-bulk phases): bypass L1.
 __device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
@@ -506,9 +527,9 @@ __device__ __forceinline__ uint4 ld_smem(const uint4 *p) {
 // Partial dot product of one row (16-byte chunks first, first+stride, ...).
 // FROM_SMEM rows are in the weight ring (always whole 16-byte chunks); global
 // rows may have a scalar tail, taken by `tail_lane` (-1: none), and rows whose
-// byte length is not a multiple of 16 use scalar loads only.
+// byte length is not a multiple of 16 use scalar loads only (plain x).
 template <int DT, bool FROM_SMEM>
-__device__ float row_partial(const char *rp, int cols, int first, int stride, int tail_lane, const float *x) {
+__device__ float row_partial(const char *rp, int cols, int first, int stride, int tail_lane, const XView &x) {
     using D = RowDot<DT>;
     const int nv = cols / D::VEC;
     const size_t row_bytes = static_cast<size_t>(cols) * esize(DT);
@@ -526,31 +547,31 @@ __device__ float row_partial(const char *rp, int cols, int first, int stride, in
                 w0 = ld_stream(v + c), w1 = ld_stream(v + c + stride), w2 = ld_stream(v + c + 2 * stride),
                 w3 = ld_stream(v + c + 3 * stride);
             }
-            acc += D::chunk(w0, x + c * D::VEC);
-            acc1 += D::chunk(w1, x + (c + stride) * D::VEC);
-            acc2 += D::chunk(w2, x + (c + 2 * stride) * D::VEC);
-            acc3 += D::chunk(w3, x + (c + 3 * stride) * D::VEC);
+            acc += xchunk<DT>(w0, x, c);
+            acc1 += xchunk<DT>(w1, x, c + stride);
+            acc2 += xchunk<DT>(w2, x, c + 2 * stride);
+            acc3 += xchunk<DT>(w3, x, c + 3 * stride);
         }
         if (c + stride < nv) {
             const uint4 w0 = FROM_SMEM ? ld_smem(v + c) : ld_stream(v + c);
             const uint4 w1 = FROM_SMEM ? ld_smem(v + c + stride) : ld_stream(v + c + stride);
-            acc1 += D::chunk(w0, x + c * D::VEC);
-            acc2 += D::chunk(w1, x + (c + stride) * D::VEC);
+            acc1 += xchunk<DT>(w0, x, c);
+            acc2 += xchunk<DT>(w1, x, c + stride);
             c += 2 * stride;
         }
-        for (; c < nv; c += stride) acc3 += D::chunk(FROM_SMEM ? ld_smem(v + c) : ld_stream(v + c), x + c * D::VEC);
+        for (; c < nv; c += stride) acc3 += xchunk<DT>(FROM_SMEM ? ld_smem(v + c) : ld_stream(v + c), x, c);
         acc = (acc + acc1) + (acc2 + acc3);
         if (!FROM_SMEM && tail_lane >= 0)
-            for (int j = nv * D::VEC + tail_lane; j < cols; j += 32) acc = fmaf(load_weight(rp, DT, j), x[j], acc);
+            for (int j = nv * D::VEC + tail_lane; j < cols; j += 32) acc = fmaf(load_weight(rp, DT, j), x.plain[j], acc);
     } else if (tail_lane >= 0) {
-        for (int j = tail_lane; j < cols; j += 32) acc = fmaf(load_weight(rp, DT, j), x[j], acc);
+        for (int j = tail_lane; j < cols; j += 32) acc = fmaf(load_weight(rp, DT, j), x.plain[j], acc);
     }
     return acc;
 }
 
 template <bool FROM_SMEM>
 __device__ float row_partial_any(int dtype, const char *rp, int cols, int first, int stride, int tail_lane,
-                                 const float *x) {
+                                 const XView &x) {
     switch (dtype) {
         case MR_DTYPE_BF16: return row_partial<MR_DTYPE_BF16, FROM_SMEM>(rp, cols, first, stride, tail_lane, x);
         case MR_DTYPE_F16: return row_partial<MR_DTYPE_F16, FROM_SMEM>(rp, cols, first, stride, tail_lane, x);
@@ -558,12 +579,41 @@ __device__ float row_partial_any(int dtype, const char *rp, int cols, int first,
     }
 }
 
+// Dot products of up to 4 ring rows with x, lanes over chunks lane, lane + 32,
+// ...: each x chunk is read once for all the rows.  nr is warp-uniform.
+template <int DT>
+__device__ __forceinline__ void rows4(const char *const (&rp)[4], int nr, int nv, int lane, const XView &x,
+                                      float (&out)[4]) {
+    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
+    int c = lane;
+    for (; c + 32 < nv; c += 64) {
+        const float4 x0 = x.L(c), x1 = x.L(c + 32);
+        const float4 y0 = DT == MR_DTYPE_F32 ? float4{} : x.H(c), y1 = DT == MR_DTYPE_F32 ? float4{} : x.H(c + 32);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            if (r < nr) {
+                const uint4 *v = reinterpret_cast<const uint4 *>(rp[r]);
+                a[r] += RowDot<DT>::chunk(ld_smem(v + c), x0, y0);
+                b[r] += RowDot<DT>::chunk(ld_smem(v + c + 32), x1, y1);
+            }
+        }
+    }
+    if (c < nv) {
+        const float4 x0 = x.L(c), y0 = DT == MR_DTYPE_F32 ? float4{} : x.H(c);
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            if (r < nr) a[r] += RowDot<DT>::chunk(ld_smem(reinterpret_cast<const uint4 *>(rp[r]) + c), x0, y0);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) out[r] = a[r] + b[r];
+}
+
 // y[i] = row_i . x for i < n (n <= kRowBatch); rows start at `base` with
 // stride row_bytes.  Many rows: one warp per row.  Few rows: several warps
 // split each row and their partials are summed in a fixed order.  Ends with a
 // compute barrier, after which every read of `base` has completed.
 template <bool FROM_SMEM>
-__device__ void rows_dot(const char *base, int dtype, int cols, int n, const float *x, float *y, Control &c) {
+__device__ void rows_dot(const char *base, int dtype, int cols, int n, const XView &x, float *y, Control &c) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t row_bytes = static_cast<size_t>(cols) * esize(dtype);
     if (n >= kEngineWarps) {
@@ -612,7 +662,7 @@ __device__ bool read_input(const GemvPhase &g, int cols, const StepInfo &info, i
             ss = fmaf(v, v, ss);
             if (gain) v = __fmul_rn(v, load_weight(gain, g.norm_gain_dtype, j));
         }
-        in[j] = v;
+        in[g.xsplit ? split_index(j, cols) : j] = v;
     };
     if (g.input_kind == IN_EMBED_ROW) {
         for (int j = threadIdx.x; j < cols; j += kEngineThreads)
@@ -714,31 +764,37 @@ __device__ __forceinline__ const char *group_row(const GemvPhase &g, const Group
            static_cast<size_t>(v - t.p[k].vbase) * seg.cols * esize(seg.dtype);
 }
 
-// y[v] = row_v . x for the group's rows.  Many rows: each warp takes two rows
-// at a time (their reductions overlap); few rows: several warps split each
-// row and their partials are summed in a fixed order.  Ends with a compute
-// barrier (none when the group has no rows).
-__device__ void group_dots(const GemvPhase &g, const GroupTable &t, int cbase, const Smem &sm, const float *x,
-                           float *y) {
+// y[v] = row_v . x for the group's rows, all of dtype DT.  Many rows: each
+// warp takes its rows (v = warp + 15k) four at a time, reading each x chunk
+// once for the four (shared memory bandwidth, not arithmetic, bounds this
+// loop: x read per row would cost twice the weight bytes); few rows: several
+// warps split each row and their partials are summed in a fixed order.  Ends with a compute barrier (none when the group has no rows).
+template <int DT>
+__device__ void group_dots_t(const GemvPhase &g, const GroupTable &t, int cbase, const Smem &sm, const XView &x,
+                             float *y) {
     Control &c = *sm.c;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int R = t.rows, cols = g.seg[0].cols;
+    const int R = t.rows, cols = g.seg[0].cols, nv = cols / RowDot<DT>::VEC;
     if (R >= kEngineWarps) {
-        for (int v = warp; v < R; v += 2 * kEngineWarps) {
-            const int v2 = v + kEngineWarps;
+        for (int j0 = 0;; j0 += 4) {
+            int nr = 0;
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+                if (warp + kEngineWarps * (j0 + r) < R) nr = r + 1;
+            if (nr == 0) break;  // warp-uniform
+            const char *rp[4];
             int dt;
-            const char *row = group_row(g, t, cbase, sm, v, dt);
-            float a = row_partial_any<true>(dt, row, cols, lane, 32, lane, x);
-            float b = 0.f;
-            if (v2 < R) {
-                row = group_row(g, t, cbase, sm, v2, dt);
-                b = row_partial_any<true>(dt, row, cols, lane, 32, lane, x);
-            }
-            a = warp_sum(a);
-            b = warp_sum(b);
-            if (lane == 0) {
-                y[v] = a;
-                if (v2 < R) y[v2] = b;
+            rp[0] = group_row(g, t, cbase, sm, warp + kEngineWarps * j0, dt);
+#pragma unroll
+            for (int r = 1; r < 4; ++r) rp[r] = r < nr ? group_row(g, t, cbase, sm, warp + kEngineWarps * (j0 + r), dt) : rp[0];
+            float out[4];
+            rows4<DT>(rp, nr, nv, lane, x, out);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                if (r < nr) {
+                    const float sum = warp_sum(out[r]);
+                    if (lane == 0) y[warp + kEngineWarps * (j0 + r)] = sum;
+                }
             }
         }
         csync();
@@ -748,7 +804,7 @@ __device__ void group_dots(const GemvPhase &g, const GroupTable &t, int cbase, c
         if (v < R) {
             int dt;
             const char *row = group_row(g, t, cbase, sm, v, dt);
-            float acc = row_partial_any<true>(dt, row, cols, part * 32 + lane, 32 * P, part == 0 ? lane : -1, x);
+            float acc = row_partial<DT, true>(row, cols, part * 32 + lane, 32 * P, part == 0 ? lane : -1, x);
             acc = warp_sum(acc);
             if (lane == 0) c.partial[v * P + part] = acc;
         }
@@ -759,6 +815,52 @@ __device__ void group_dots(const GemvPhase &g, const GroupTable &t, int cbase, c
             y[threadIdx.x] = total;
         }
         csync();
+    }
+}
+
+// Segments of different dtypes in one phase (plain x): one row at a time.
+__device__ void group_dots_mixed(const GemvPhase &g, const GroupTable &t, int cbase, const Smem &sm, const float *in,
+                                 float *y) {
+    Control &c = *sm.c;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int R = t.rows, cols = g.seg[0].cols;
+    if (R >= kEngineWarps) {
+        for (int v = warp; v < R; v += kEngineWarps) {
+            int dt;
+            const char *row = group_row(g, t, cbase, sm, v, dt);
+            const float a = warp_sum(row_partial_any<true>(dt, row, cols, lane, 32, lane, x_plain(in, dt)));
+            if (lane == 0) y[v] = a;
+        }
+        csync();
+    } else if (R > 0) {
+        const int P = kEngineWarps / R;
+        const int v = warp / P, part = warp % P;
+        if (v < R) {
+            int dt;
+            const char *row = group_row(g, t, cbase, sm, v, dt);
+            float acc = row_partial_any<true>(dt, row, cols, part * 32 + lane, 32 * P, part == 0 ? lane : -1,
+                                              x_plain(in, dt));
+            acc = warp_sum(acc);
+            if (lane == 0) c.partial[v * P + part] = acc;
+        }
+        csync();
+        if (threadIdx.x < R) {
+            float total = 0.f;
+            for (int q = 0; q < P; ++q) total += c.partial[threadIdx.x * P + q];
+            y[threadIdx.x] = total;
+        }
+        csync();
+    }
+}
+
+__device__ void group_dots(const GemvPhase &g, const GroupTable &t, int cbase, const Smem &sm, const float *in,
+                           float *y) {
+    const int cols = g.seg[0].cols;
+    switch (g.wdtype) {
+        case MR_DTYPE_BF16: group_dots_t<MR_DTYPE_BF16>(g, t, cbase, sm, x_split(in, cols), y); break;
+        case MR_DTYPE_F16: group_dots_t<MR_DTYPE_F16>(g, t, cbase, sm, x_split(in, cols), y); break;
+        case MR_DTYPE_F32: group_dots_t<MR_DTYPE_F32>(g, t, cbase, sm, x_plain(in, MR_DTYPE_F32), y); break;
+        default: group_dots_mixed(g, t, cbase, sm, in, y); break;
     }
 }
 
@@ -910,7 +1012,7 @@ __device__ bool gemv_direct(const GemvPhase &g, int p, StepState *st, const Step
             for (int part = 0; part < (paired ? 2 : 1); ++part) {
                 const Segment &seg = g.seg[s + part];
                 const char *base = static_cast<const char *>(seg.w) + static_cast<size_t>(rb) * cols * esize(seg.dtype);
-                rows_dot<false>(base, seg.dtype, cols, n, in, c.y[buf], c);
+                rows_dot<false>(base, seg.dtype, cols, n, x_plain(in, seg.dtype), c.y[buf], c);
                 // the gate and up rows of index i are finished by the same thread
                 for (int i = threadIdx.x; i < n; i += kEngineThreads) {
                     if (!paired) finish_row(g, s, rb + i, c.y[buf][i], info, p, c, e);
