@@ -106,6 +106,7 @@ struct mr_model {
     int logits_rows = 0;
     Word *partial = nullptr;
     int scratch_floats = 0, attn_base = 0, ring_bytes = 0;
+    int xres_skip = 0;              // CTAs owning no rows of the q/k/v, o and down phases
     size_t smem_bytes = 0;
     PieceDesc *d_pieces = nullptr;
     GroupTable *d_groups = nullptr;
@@ -271,6 +272,7 @@ int build_plan(mr_model *m) {
         qkv.gemv.seg[1] = segment(tensor(m, p + "k"), m->k_raw);
         qkv.gemv.seg[2] = segment(tensor(m, p + "v"), m->v_raw);
         qkv.gemv.epilogue = EPI_STORE;
+        qkv.gemv.skip = m->xres_skip;
         m->phases.push_back(qkv);
         // 2. attention
         Phase at{};
@@ -307,6 +309,7 @@ int build_plan(mr_model *m) {
         o.gemv.epilogue = EPI_RESIDUAL;
         o.gemv.scale = c.residual_scale;
         o.gemv.x = m->x;
+        o.gemv.skip = m->xres_skip;
         m->phases.push_back(o);
         // 4. RMSNorm(x) -> gate, up -> SwiGLU (model.py:87-89)
         Phase gu = gemv_phase(l, m->x, tensor(m, p + "f_norm"), c.norm_eps);
@@ -323,6 +326,7 @@ int build_plan(mr_model *m) {
         dn.gemv.epilogue = EPI_RESIDUAL;
         dn.gemv.scale = c.residual_scale;
         dn.gemv.x = m->x;
+        dn.gemv.skip = m->xres_skip;
         m->phases.push_back(dn);
     }
     // final RMSNorm + head (model.py:285, 307)
@@ -366,8 +370,9 @@ int build_plan(mr_model *m) {
 // Whether CTA b owns any rows of the phase (a CTA with none skips the phase).
 bool cta_has_rows(const GemvPhase &g, int b, int G) {
     for (int s = 0; s < g.nseg; ++s) {
-        const long long rows = g.seg[s].rows;
-        if (rows * (b + 1) / G > rows * b / G) return true;
+        int r0, r1;
+        cta_row_range(g.seg[s].rows, b, G, g.skip, r0, r1);
+        if (r1 > r0) return true;
     }
     return false;
 }
@@ -403,8 +408,9 @@ int build_pieces(mr_model *m) {
             }
             const bool paired = g.epilogue == EPI_SWIGLU;
             for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
-                const int rows = g.seg[s].rows, rpp = g.seg[s].rows_per_piece;
-                const int r0 = (int)((long long)rows * b / G), r1 = (int)((long long)rows * (b + 1) / G);
+                const int rpp = g.seg[s].rows_per_piece;
+                int r0, r1;
+                cta_row_range(g.seg[s].rows, b, G, g.skip, r0, r1);
                 for (int row0 = r0; row0 < r1; row0 += rpp) {
                     const int n = std::min(rpp, r1 - row0);
                     add(v, s, row0, n);
@@ -459,8 +465,9 @@ int build_groups(mr_model *m) {
                 bytes = (int)((cols * dtype_size(g.norm_gain_dtype) + 15) & ~size_t(15));
             }
             for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
-                const int rows = g.seg[s].rows, rpp = g.seg[s].rows_per_piece;
-                const int r0 = (int)((long long)rows * b / G), r1 = (int)((long long)rows * (b + 1) / G);
+                const int rpp = g.seg[s].rows_per_piece;
+                int r0, r1;
+                cta_row_range(g.seg[s].rows, b, G, g.skip, r0, r1);
                 for (int row0 = r0; row0 < r1; row0 += rpp) {
                     const int n = std::min(rpp, r1 - row0);
                     int ubytes = n * cols * (int)dtype_size(g.seg[s].dtype);
@@ -572,6 +579,7 @@ StepControl base_control(mr_model *m) {
     ctl.embed = embed->ptr;
     ctl.embed_dtype = embed->dtype;
     ctl.hidden = m->cfg.hidden_size;
+    ctl.xres_skip = m->xres_skip;
     ctl.ring_bytes = m->ring_bytes;
     ctl.pieces = m->d_pieces;
     ctl.groups = m->d_groups;
@@ -794,6 +802,18 @@ int mr_model_finalize(mr_model *m) {
         if (rc) return rc;
     }
     MR_CUDA_TRY(cudaMemcpy(m->d_inv_freq, m->inv_freq.data(), sizeof(float) * (d / 2), cudaMemcpyHostToDevice));
+    // Attention unit u runs on CTA u.  Those CTAs own no rows of the q/k/v,
+    // o and down phases (nor residual rows), so that they go from one
+    // attention phase's neighbours to the next without a GEMV of their own:
+    // the fewest units any layer has at full context, unless that is more
+    // than a quarter of the grid.
+    int skip = m->grid;
+    for (int l = 0; l < c.layers; ++l)
+        skip = std::min(skip, m->layer_kvh[l] * attn_chunks(m->cache_capacity[l], m->layer_kvh[l], m->grid));
+    if (skip > m->grid / 4) skip = 0;  // too many units to spare their CTAs: no CTA is set aside
+    m->xres_skip = skip;
+    MR_REQUIRE((c.hidden_size + m->grid - skip - 1) / (m->grid - skip) <= kRowBatch,
+               "hidden size %d above the engine limit (rows per CTA)", c.hidden_size);
     rc = build_plan(m);
     if (!rc) rc = build_pieces(m);
     if (!rc) rc = build_groups(m);

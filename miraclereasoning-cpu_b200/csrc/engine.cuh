@@ -102,6 +102,7 @@ struct GemvPhase {
     int xsplit;                 // the input vector is staged split for 16-bit weights (see XView)
     int group_offset;           // bulk: this phase's group tables in StepControl::groups,
     int group_stride;           //   CTA b's g-th at group_offset + b * group_stride + g
+    int skip;                   // CTAs 0 .. skip-1 own no rows of the phase (see cta_row_range)
 };
 
 struct AttnPhase {
@@ -169,6 +170,18 @@ static_assert(sizeof(Phase) % 16 == 0, "Phase must be a whole number of 16-byte 
 
 // Attention work split: chunks of keys per KV head (same formula in the
 // attention phase and in the merge that consumes its partials).
+// Rows [r0, r1) of a `rows`-row matrix owned by CTA b of G when the first
+// `skip` CTAs own none (they run the attention units, which would otherwise
+// make them the last to finish the phases next to attention).
+__host__ __device__ inline void cta_row_range(int rows, int b, int G, int skip, int &r0, int &r1) {
+    if (b < skip) {
+        r0 = r1 = 0;
+        return;
+    }
+    r0 = static_cast<int>(static_cast<long long>(rows) * (b - skip) / (G - skip));
+    r1 = static_cast<int>(static_cast<long long>(rows) * (b + 1 - skip) / (G - skip));
+}
+
 __host__ __device__ inline int attn_chunks(int total_keys, int kv_heads, int grid) {
     int chunks = grid / kv_heads;
     const int by_keys = (total_keys + kKeysPerChunk - 1) / kKeysPerChunk;
@@ -180,9 +193,10 @@ __host__ __device__ inline int attn_chunks(int total_keys, int kv_heads, int gri
 // Shared-memory scratch carve-up (float offsets) of the attention phase for
 // one KV group.  Every array starts on a 16-byte boundary; key rows are
 // padded to dim + 4 floats so that float4 reads of 8 consecutive keys hit 32
-// distinct banks.
+// distinct banks.  After the chunk's last tile the key/value region (`tiles`
+// floats from kt) takes the chunk records that merge_slice gathers.
 struct AttnLayout {
-    int q, knew, vnew, kt, vt, p, acc, m, l, corr, total;
+    int q, knew, vnew, kt, vt, tiles, p, acc, m, l, corr, total;
     int kstride, vstride;
 };
 __host__ __device__ inline int round4(int x) { return (x + 3) & ~3; }
@@ -194,8 +208,13 @@ __host__ __device__ inline AttnLayout attn_layout(int group_heads, int dim) {
     L.q = o;    o += round4(group_heads * dim);   // [gq][dim]
     L.knew = o; o += round4(dim);                 // this token's key
     L.vnew = o; o += round4(dim);                 // this token's value
-    L.kt = o;   o += kKeyTile * L.kstride;        // key tile
-    L.vt = o;   o += kKeyTile * L.vstride;        // value tile
+    L.kt = o;                                     // key tile
+    L.vt = o + kKeyTile * L.kstride;              // value tile
+    int tiles = kKeyTile * (L.kstride + L.vstride);
+    const int records = group_heads * dim + kMaxAttnChunks + 3 * group_heads * kMaxAttnChunks;
+    if (tiles < records) tiles = records;
+    L.tiles = round4(tiles);
+    o += L.tiles;
     L.p = o;    o += round4(group_heads * kKeyTile);
     L.acc = o;  o += round4(group_heads * dim);
     L.m = o;    o += round4(group_heads);
@@ -238,6 +257,7 @@ struct StepControl {
     int rope_pairs;
     const void *embed;                // embedding [vocab, hidden]: this CTA's rows of the residual stream
     int embed_dtype, hidden;          //   start as the token's embedding
+    int xres_skip;                    // CTAs owning no residual rows (cta_row_range)
     int ring_bytes;                   // shared-memory weight ring
     const PieceDesc *pieces;          // [grid][piece_stride] weight stream of each CTA
     const GroupTable *groups;         // piece groups of every (bulk phase, CTA)

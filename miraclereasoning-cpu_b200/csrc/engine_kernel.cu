@@ -39,7 +39,6 @@ namespace {
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
 constexpr int kMaxHeadDim = 128;
-constexpr int kMaxMergeHeads = 64;  // query heads (the host enforces the limit)
 
 // Fixed part of the dynamic shared memory; the scratch floats and the weight
 // ring follow it.
@@ -111,10 +110,6 @@ struct Smem {
     int ring_bytes;
 };
 
-__device__ __forceinline__ void row_range(int rows, int b, int g, int &r0, int &r1) {
-    r0 = static_cast<int>(static_cast<long long>(rows) * b / g);
-    r1 = static_cast<int>(static_cast<long long>(rows) * (b + 1) / g);
-}
 
 __device__ __forceinline__ int esize(int dtype) { return dtype == MR_DTYPE_F32 ? 4 : 2; }
 
@@ -225,14 +220,18 @@ __device__ bool wait_bar(unsigned long long *bar, int parity, StepState *st, con
     }
 }
 
-// Reads N exchange words (NULL pointer: none), polling each until it carries
-// `tag`; bounded like every wait (gives up early when another wait recorded
-// an error).  Every load is issued before the first check.
-template <int N>
-__device__ bool read_words(const Word *const (&src)[N], unsigned tag, float (&out)[N], StepState *st, int phase) {
+// Reads N exchange words at addr(0) .. addr(N - 1) (NULL: none), polling each
+// until it carries `tag`; bounded like every wait (gives up early when
+// another wait recorded an error).  Every load is issued before the first
+// check; addresses are recomputed rather than held, to spare registers.
+template <int N, typename Addr>
+__device__ __forceinline__ bool read_words(Addr addr, unsigned tag, float (&out)[N], StepState *st, int phase) {
     Word w[N];
 #pragma unroll
-    for (int u = 0; u < N; ++u) w[u] = src[u] ? ld_word(src[u]) : (static_cast<Word>(tag) << 32);
+    for (int u = 0; u < N; ++u) {
+        const Word *src = addr(u);
+        w[u] = src ? ld_word(src) : (static_cast<Word>(tag) << 32);
+    }
     uint64_t start = 0;
     for (unsigned spin = 0;; ++spin) {
         bool all = true;
@@ -240,7 +239,7 @@ __device__ bool read_words(const Word *const (&src)[N], unsigned tag, float (&ou
         for (int u = 0; u < N; ++u)
             if (!word_ok(w[u], tag)) {
                 all = false;
-                w[u] = ld_word(src[u]);
+                w[u] = ld_word(addr(u));
             }
         if (all) break;
         if ((spin & 15u) == 15u) {
@@ -257,28 +256,6 @@ __device__ bool read_words(const Word *const (&src)[N], unsigned tag, float (&ou
 #pragma unroll
     for (int u = 0; u < N; ++u) out[u] = word_value(w[u]);
     return true;
-}
-
-// Reads n exchange words src[0..n) carrying `tag` into dst (shared memory),
-// four per thread per pass; every compute thread takes part (no barrier).
-__device__ bool read_vector(const Word *src, int n, unsigned tag, float *dst, StepState *st, int phase) {
-    bool ok = true;
-    for (int base = 0; base < n && ok; base += 4 * kEngineThreads) {
-        const Word *ptr[4];
-        float v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int e = base + u * kEngineThreads + threadIdx.x;
-            ptr[u] = e < n ? src + e : nullptr;
-        }
-        ok = read_words(ptr, tag, v, st, phase);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int e = base + u * kEngineThreads + threadIdx.x;
-            if (ok && e < n) dst[e] = v[u];
-        }
-    }
-    return ok;
 }
 
 // ---- the weight-stream producer (lane 0 of warp 16) -----------------------------------
@@ -672,14 +649,13 @@ __device__ bool read_input(const GemvPhase &g, int cols, const StepInfo &info, i
     const unsigned tag = info.tag_base + p - 1;
     bool ok = true;
     for (int base = 0; base < cols && ok; base += 4 * kEngineThreads) {
-        const Word *ptr[4];
         float v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int e = base + u * kEngineThreads + threadIdx.x;
-            ptr[u] = e < cols ? g.in + e : nullptr;
-        }
-        ok = read_words(ptr, tag, v, st, p);
+        ok = read_words(
+            [&](int u) -> const Word * {
+                const int e = base + u * kEngineThreads + threadIdx.x;
+                return e < cols ? g.in + e : nullptr;
+            },
+            tag, v, st, p);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int e = base + u * kEngineThreads + threadIdx.x;
@@ -989,7 +965,7 @@ __device__ bool gemv_direct(const GemvPhase &g, int p, StepState *st, const Step
     bool mine = false;
     for (int s = 0; s < g.nseg; ++s) {
         int r0, r1;
-        row_range(g.seg[s].rows, b, G, r0, r1);
+        cta_row_range(g.seg[s].rows, b, G, g.skip, r0, r1);
         mine = mine || r1 > r0;
     }
     if (!mine) return true;
@@ -1006,7 +982,7 @@ __device__ bool gemv_direct(const GemvPhase &g, int p, StepState *st, const Step
     const bool paired = g.epilogue == EPI_SWIGLU;
     for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
         int r0, r1;
-        row_range(g.seg[s].rows, b, G, r0, r1);
+        cta_row_range(g.seg[s].rows, b, G, g.skip, r0, r1);
         for (int rb = r0; rb < r1; rb += kRowBatch) {
             const int n = min(kRowBatch, r1 - rb);
             for (int part = 0; part < (paired ? 2 : 1); ++part) {
@@ -1122,59 +1098,80 @@ __device__ bool attn_first_tile(const AttnPhase &a, const StepInfo &info, const 
     return true;
 }
 
+// Reads n exchange words carrying `tag`, word q at addr(q), into dst[q]
+// (shared memory), four per thread per pass; every compute thread takes part
+// (no barrier).
+template <typename Addr>
+__device__ bool read_to_smem(int n, Addr addr, unsigned tag, float *dst, StepState *st, int phase) {
+    bool ok = true;
+    for (int base = 0; base < n && ok; base += 4 * kEngineThreads) {
+        float v[4];
+        ok = read_words(
+            [&](int u) -> const Word * {
+                const int q = base + u * kEngineThreads + threadIdx.x;
+                return q < n ? addr(q) : nullptr;
+            },
+            tag, v, st, phase);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int q = base + u * kEngineThreads + threadIdx.x;
+            if (ok && q < n) dst[q] = v[u];
+        }
+    }
+    return ok;
+}
+
 // After publishing its own chunk, every unit of a KV head merges one slice
 // (1/chunks) of the head group's attention output: the reference's softmax
 // over all keys (model.py:95-116) equals sum_c w_c acc_c with
 // w_c = exp(m_c - M) / sum_c' exp(m_c' - M) l_c', M the largest chunk maximum.
-// One polling call per thread brings in its slice element's accumulators of
-// every chunk and one (head, chunk) running max / sum; the weights are reduced
-// over 16-lane groups (one per head).  Output rows go out as exchange words
-// for the o projection.  `scratch` holds gq * kMaxAttnChunks floats.
+// The slice's accumulators of every chunk and every (head, chunk) maximum and
+// sum are brought into shared memory (`scratch`, spread over all threads:
+// one polling round), the weights are formed per (head, chunk), and the
+// output rows go out as exchange words for the o projection.
 __device__ bool merge_slice(const AttnPhase &a, int g, int gq, int chunks, int c, float *scratch, unsigned tag,
                             StepState *st, int phase) {
     const int d = a.dim, stride = d + 2, n = gq * d;
     const int per = (n + chunks - 1) / chunks, e0 = c * per, e1 = min(n, e0 + per);
+    const int nacc = max(0, e1 - e0) * chunks, npair = gq * chunks;
     auto rec = [&](int i, int cc) {
         return a.partial + (static_cast<size_t>(g * gq + i) * kMaxAttnChunks + cc) * stride;
     };
-    bool ok = true;
-    for (int base = e0; base < e1 || base == e0; base += kEngineThreads) {
-        const int e = base + threadIdx.x, i = e / d, j = e - i * d;
-        const bool live = e < e1;
-        const int t = threadIdx.x, pi = t / kMaxAttnChunks, pc = t % kMaxAttnChunks;
-        const bool pair = base == e0 && pi < gq && pc < chunks;
-        const Word *ptr[kMaxAttnChunks + 2];
-        float v[kMaxAttnChunks + 2];
-#pragma unroll
-        for (int cc = 0; cc < kMaxAttnChunks; ++cc) ptr[cc] = (live && cc < chunks) ? rec(i, cc) + j : nullptr;
-        ptr[kMaxAttnChunks] = pair ? rec(pi, pc) + d : nullptr;
-        ptr[kMaxAttnChunks + 1] = pair ? rec(pi, pc) + d + 1 : nullptr;
-        ok = read_words(ptr, tag, v, st, phase) && ok;
-        if (base == e0) {
-            if (t < 32 * ((gq * kMaxAttnChunks + 31) / 32)) {  // whole warps: 16-lane groups = one head each
-                const float m = pair ? v[kMaxAttnChunks] : -INFINITY, l = pair ? v[kMaxAttnChunks + 1] : 0.f;
-                float mx = m;
-#pragma unroll
-                for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                const float w = (m == -INFINITY) ? 0.f : expf(m - mx);
-                float den = w * l;
-#pragma unroll
-                for (int o = 8; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-                if (pi < gq) scratch[t] = pair ? w / den : 0.f;
+    float *vals = scratch, *ml = scratch + nacc, *wgt = ml + 2 * npair;
+    // vals[k * chunks + cc] = acc of element e0 + k in chunk cc; ml[2 * (i * chunks + cc) + {0, 1}] = max, sum
+    const bool ok = read_to_smem(
+        nacc + 2 * npair,
+        [&](int q) -> const Word * {
+            if (q < nacc) {
+                const int k = q / chunks, cc = q - k * chunks, e = e0 + k;
+                return rec(e / d, cc) + (e % d);
             }
-            csync();
+            const int r = (q - nacc) >> 1, i = r / chunks, cc = r - i * chunks;
+            return rec(i, cc) + d + ((q - nacc) & 1);
+        },
+        tag, vals, st, phase);
+    if (!csync_and(ok)) return false;
+    if (threadIdx.x < npair) {
+        const int i = threadIdx.x / chunks, cc = threadIdx.x - i * chunks;
+        const float *mi = ml + 2 * i * chunks;
+        float mx = -INFINITY;
+        for (int u = 0; u < chunks; ++u) mx = fmaxf(mx, mi[2 * u]);
+        float den = 0.f;
+        for (int u = 0; u < chunks; ++u) {
+            const float mu = mi[2 * u];
+            den += (mu == -INFINITY) ? 0.f : expf(mu - mx) * mi[2 * u + 1];
         }
-        if (live) {
-            const float *w = scratch + i * kMaxAttnChunks;
-            float sum = 0.f;
-#pragma unroll
-            for (int cc = 0; cc < kMaxAttnChunks; ++cc)
-                if (cc < chunks) sum = fmaf(w[cc], v[cc], sum);
-            st_word(a.out + static_cast<size_t>(g * gq) * d + e, sum, tag);
-        }
-        if (base + kEngineThreads >= e1) break;
+        const float m = mi[2 * cc];
+        wgt[threadIdx.x] = (m == -INFINITY) ? 0.f : expf(m - mx) / den;
     }
-    return ok;
+    csync();
+    for (int k = threadIdx.x; k < e1 - e0; k += kEngineThreads) {
+        const int e = e0 + k, i = e / d;
+        float sum = 0.f;
+        for (int cc = 0; cc < chunks; ++cc) sum = fmaf(wgt[i * chunks + cc], vals[k * chunks + cc], sum);
+        st_word(a.out + static_cast<size_t>(g * gq) * d + e, sum, tag);
+    }
+    return true;
 }
 
 // Work unit = (KV head g, chunk c of the attended rows): one pass over the
@@ -1225,17 +1222,16 @@ __device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph,
         bool ok = true;
         const int nq = gq * d, nread = nq + (owner ? 2 * d : 0);
         for (int base = 0; base < nread && ok; base += 4 * kEngineThreads) {
-            const Word *ptr[4];
             float v[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int e = base + u * kEngineThreads + threadIdx.x;
-                ptr[u] = e >= nread ? nullptr
-                         : e < nq   ? a.q_raw + static_cast<size_t>(g) * nq + e
-                         : e < nq + d ? a.k_raw + static_cast<size_t>(g) * d + (e - nq)
-                                      : a.v_raw + static_cast<size_t>(g) * d + (e - nq - d);
-            }
-            ok = read_words(ptr, in_tag, v, st, ph);
+            ok = read_words(
+                [&](int u) -> const Word * {
+                    const int e = base + u * kEngineThreads + threadIdx.x;
+                    return e >= nread ? nullptr
+                           : e < nq   ? a.q_raw + static_cast<size_t>(g) * nq + e
+                           : e < nq + d ? a.k_raw + static_cast<size_t>(g) * d + (e - nq)
+                                        : a.v_raw + static_cast<size_t>(g) * d + (e - nq - d);
+                },
+                in_tag, v, st, ph);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int e = base + u * kEngineThreads + threadIdx.x;
@@ -1356,7 +1352,7 @@ __device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph,
                 st_word(rec + d, mrow[threadIdx.x], out_tag);
                 st_word(rec + d + 1, lrow[threadIdx.x], out_tag);
             }
-            if (!csync_and(merge_slice(a, g, gq, chunks, c, p, out_tag, st, ph))) return false;
+            if (!merge_slice(a, g, gq, chunks, c, kt, out_tag, st, ph)) return false;  // the tiles are free
         }
         csync();
     }
@@ -1390,7 +1386,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         need_head = ctl.return_all || rel >= ctl.feed_len - 1;
         info.logits_row = ctl.return_all ? rel % ctl.logits_rows : 0;
         info.tag_base = ctl.tag_base;
-        row_range(ctl.hidden, blockIdx.x, gridDim.x, info.xr0, info.xr1);
+        cta_row_range(ctl.hidden, blockIdx.x, gridDim.x, ctl.xres_skip, info.xr0, info.xr1);
         base = vs->barrier_base;
         if (!skip && pos >= ctl.context_length) {
             if (blockIdx.x == 0) atomicCAS(&st->error, 0, 3);
