@@ -439,7 +439,7 @@ int build_pieces(mr_model *m) {
 
 // Piece groups of every (bulk phase, CTA), in the stream order of
 // build_pieces: greedy, a group closes before the piece (or gate/up pair) that
-// would take it past half the ring, kRowBatch rows or kGroupPieces pieces.
+// would take its rows past half the ring, kRowBatch rows or kGroupPieces pieces.
 int build_groups(mr_model *m) {
     const int G = m->grid, cap = m->ring_bytes / 2;
     std::vector<GroupTable> flat;
@@ -459,10 +459,15 @@ int build_groups(mr_model *m) {
                 t = GroupTable{};
                 bytes = 0;
             };
+            // The gain vector (at most a quarter of the ring) rides in the first
+            // group without counting against the half-ring cap: a group still
+            // spans at most three quarters of the ring, which it always finds
+            // once the older pieces are released (a wrap wastes less than one
+            // piece, at most a quarter).  Counting it split the first group
+            // of CTAs whose rows just fill half the ring.
             if (g.gain_piece && cta_has_rows(g, b, G)) {
                 t.p[0] = GroupPiece{-1, 0, 0, 0};
                 t.count = 1;
-                bytes = (int)((cols * dtype_size(g.norm_gain_dtype) + 15) & ~size_t(15));
             }
             for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
                 const int rpp = g.seg[s].rows_per_piece;

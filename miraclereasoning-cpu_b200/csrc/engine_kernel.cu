@@ -55,6 +55,7 @@ struct Control {
     float rope_cos[kMaxHeadDim / 2];   // RoPE cos / sin of this launch's position, per frequency
     float rope_sin[kMaxHeadDim / 2];
     GroupTable group[2][2];            // piece-group tables: [phase parity][group parity]
+    int2 rowinfo[2][kRowBatch];        // row tables of alternate groups (build_rows)
     unsigned long long rbar;           // the next phase's records landed (descriptor + first group table)
     unsigned long long gbar;           // a later group table of the current phase landed
     float red[kEngineWarps];
@@ -731,14 +732,27 @@ __device__ __forceinline__ int find_piece(const GroupTable &t, int v) {
     while (t.p[k].seg < 0 || v >= t.p[k].vbase + t.p[k].n) ++k;
     return k;
 }
-__device__ __forceinline__ const char *group_row(const GemvPhase &g, const GroupTable &t, int cbase, const Smem &sm,
-                                                 int v, int &dtype) {
-    const int k = find_piece(t, v);
-    const Segment &seg = g.seg[t.p[k].seg];
-    dtype = seg.dtype;
-    return reinterpret_cast<const char *>(sm.ring) + sm.c->offset[(cbase + k) % kQueue] +
-           static_cast<size_t>(v - t.p[k].vbase) * seg.cols * esize(seg.dtype);
+// Row table of piece group t (pieces from stream index cbase), entries
+// first, first + step, ...: .x = ring byte offset of dot product v's row,
+// .y = segment << 30 | SwiGLU gate partner << 22 | output row (the partner of
+// an up row is the index of the gate row of the same output, one piece back).
+// Looked up once per group, off the path from the input to the dot products.
+__device__ __forceinline__ void build_rows(const GemvPhase &g, const GroupTable &t, int cbase, const Control &c,
+                                           int2 *rows, int first, int step) {
+    for (int v = first; v < t.rows; v += step) {
+        const int k = find_piece(t, v);
+        const GroupPiece &pc = t.p[k];
+        const int sgi = pc.seg, i = v - pc.vbase;
+        const Segment &seg = g.seg[sgi];
+        const int partner = (g.epilogue == EPI_SWIGLU && sgi == 1) ? v - pc.n : 0;
+        rows[v] = make_int2(c.offset[(cbase + k) % kQueue] + i * seg.cols * esize(seg.dtype),
+                            static_cast<int>((static_cast<unsigned>(sgi) << 30) | (static_cast<unsigned>(partner) << 22) |
+                                             static_cast<unsigned>(pc.row0 + i)));
+    }
 }
+__device__ __forceinline__ int row_seg(int2 r) { return static_cast<int>(static_cast<unsigned>(r.y) >> 30); }
+__device__ __forceinline__ int row_partner(int2 r) { return static_cast<int>((static_cast<unsigned>(r.y) >> 22) & 255u); }
+__device__ __forceinline__ int row_out(int2 r) { return static_cast<int>(static_cast<unsigned>(r.y) & 0x3FFFFFu); }
 
 // y[v] = row_v . x for the group's rows, all of dtype DT.  Many rows: each
 // warp takes its rows (v = warp + 15k) four at a time, reading each x chunk
@@ -746,7 +760,7 @@ __device__ __forceinline__ const char *group_row(const GemvPhase &g, const Group
 // loop: x read per row would cost twice the weight bytes); few rows: several
 // warps split each row and their partials are summed in a fixed order.  Ends with a compute barrier (none when the group has no rows).
 template <int DT>
-__device__ void group_dots_t(const GemvPhase &g, const GroupTable &t, int cbase, const Smem &sm, const XView &x,
+__device__ void group_dots_t(const GemvPhase &g, const GroupTable &t, const int2 *rows, const Smem &sm, const XView &x,
                              float *y) {
     Control &c = *sm.c;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -758,11 +772,10 @@ __device__ void group_dots_t(const GemvPhase &g, const GroupTable &t, int cbase,
             for (int r = 0; r < 4; ++r)
                 if (warp + kEngineWarps * (j0 + r) < R) nr = r + 1;
             if (nr == 0) break;  // warp-uniform
+            const char *ring = reinterpret_cast<const char *>(sm.ring);
             const char *rp[4];
-            int dt;
-            rp[0] = group_row(g, t, cbase, sm, warp + kEngineWarps * j0, dt);
 #pragma unroll
-            for (int r = 1; r < 4; ++r) rp[r] = r < nr ? group_row(g, t, cbase, sm, warp + kEngineWarps * (j0 + r), dt) : rp[0];
+            for (int r = 0; r < 4; ++r) rp[r] = ring + rows[warp + kEngineWarps * (r < nr ? j0 + r : j0)].x;
             float out[4];
             rows4<DT>(rp, nr, nv, lane, x, out);
 #pragma unroll
@@ -778,32 +791,36 @@ __device__ void group_dots_t(const GemvPhase &g, const GroupTable &t, int cbase,
         const int P = kEngineWarps / R;
         const int v = warp / P, part = warp % P;
         if (v < R) {
-            int dt;
-            const char *row = group_row(g, t, cbase, sm, v, dt);
+            const char *row = reinterpret_cast<const char *>(sm.ring) + rows[v].x;
             float acc = row_partial<DT, true>(row, cols, part * 32 + lane, 32 * P, part == 0 ? lane : -1, x);
             acc = warp_sum(acc);
-            if (lane == 0) c.partial[v * P + part] = acc;
+            if (lane == 0) {
+                if (P == 1) y[v] = acc;  // one warp per row: its sum is the dot product
+                else c.partial[v * P + part] = acc;
+            }
         }
         csync();
-        if (threadIdx.x < R) {
-            float total = 0.f;
-            for (int q = 0; q < P; ++q) total += c.partial[threadIdx.x * P + q];
-            y[threadIdx.x] = total;
+        if (P > 1) {
+            if (threadIdx.x < R) {
+                float total = 0.f;
+                for (int q = 0; q < P; ++q) total += c.partial[threadIdx.x * P + q];
+                y[threadIdx.x] = total;
+            }
+            csync();
         }
-        csync();
     }
 }
 
 // Segments of different dtypes in one phase (plain x): one row at a time.
-__device__ void group_dots_mixed(const GemvPhase &g, const GroupTable &t, int cbase, const Smem &sm, const float *in,
-                                 float *y) {
+__device__ void group_dots_mixed(const GemvPhase &g, const GroupTable &t, const int2 *rows, const Smem &sm,
+                                 const float *in, float *y) {
     Control &c = *sm.c;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int R = t.rows, cols = g.seg[0].cols;
     if (R >= kEngineWarps) {
         for (int v = warp; v < R; v += kEngineWarps) {
-            int dt;
-            const char *row = group_row(g, t, cbase, sm, v, dt);
+            const int dt = g.seg[row_seg(rows[v])].dtype;
+            const char *row = reinterpret_cast<const char *>(sm.ring) + rows[v].x;
             const float a = warp_sum(row_partial_any<true>(dt, row, cols, lane, 32, lane, x_plain(in, dt)));
             if (lane == 0) y[v] = a;
         }
@@ -812,8 +829,8 @@ __device__ void group_dots_mixed(const GemvPhase &g, const GroupTable &t, int cb
         const int P = kEngineWarps / R;
         const int v = warp / P, part = warp % P;
         if (v < R) {
-            int dt;
-            const char *row = group_row(g, t, cbase, sm, v, dt);
+            const int dt = g.seg[row_seg(rows[v])].dtype;
+            const char *row = reinterpret_cast<const char *>(sm.ring) + rows[v].x;
             float acc = row_partial_any<true>(dt, row, cols, part * 32 + lane, 32 * P, part == 0 ? lane : -1,
                                               x_plain(in, dt));
             acc = warp_sum(acc);
@@ -829,31 +846,31 @@ __device__ void group_dots_mixed(const GemvPhase &g, const GroupTable &t, int cb
     }
 }
 
-__device__ void group_dots(const GemvPhase &g, const GroupTable &t, int cbase, const Smem &sm, const float *in,
+__device__ void group_dots(const GemvPhase &g, const GroupTable &t, const int2 *rows, const Smem &sm, const float *in,
                            float *y) {
     const int cols = g.seg[0].cols;
     switch (g.wdtype) {
-        case MR_DTYPE_BF16: group_dots_t<MR_DTYPE_BF16>(g, t, cbase, sm, x_split(in, cols), y); break;
-        case MR_DTYPE_F16: group_dots_t<MR_DTYPE_F16>(g, t, cbase, sm, x_split(in, cols), y); break;
-        case MR_DTYPE_F32: group_dots_t<MR_DTYPE_F32>(g, t, cbase, sm, x_plain(in, MR_DTYPE_F32), y); break;
-        default: group_dots_mixed(g, t, cbase, sm, in, y); break;
+        case MR_DTYPE_BF16: group_dots_t<MR_DTYPE_BF16>(g, t, rows, sm, x_split(in, cols), y); break;
+        case MR_DTYPE_F16: group_dots_t<MR_DTYPE_F16>(g, t, rows, sm, x_split(in, cols), y); break;
+        case MR_DTYPE_F32: group_dots_t<MR_DTYPE_F32>(g, t, rows, sm, x_plain(in, MR_DTYPE_F32), y); break;
+        default: group_dots_mixed(g, t, rows, sm, in, y); break;
     }
 }
 
 // Epilogue of the group: thread v finishes dot product v.  `scale` is the
 // input's RMSNorm factor (applied here: scale * (W . (x * gain)) equals the
 // reference's W . ((x * scale) * gain) up to float32 rounding).
-__device__ void group_epilogue(const GemvPhase &g, const GroupTable &t, const float *y, float scale,
+__device__ void group_epilogue(const GemvPhase &g, const GroupTable &t, const int2 *rows, const float *y, float scale,
                                const StepInfo &info, int p, Control &c, Epi &e) {
     const int v = threadIdx.x;
     if (v >= t.rows) return;
-    const int k = find_piece(t, v);
-    const int s = t.p[k].seg, r = t.p[k].row0 + (v - t.p[k].vbase);
+    const int2 ri = rows[v];
+    const int s = row_seg(ri), r = row_out(ri);
     const float val = g.norm ? __fmul_rn(y[v], scale) : y[v];
     if (g.epilogue != EPI_SWIGLU) {
         finish_row(g, s, r, val, info, p, c, e);
-    } else if (s == 1) {  // the gate row of the same index is in the previous piece
-        const float gy = y[v - t.p[k].n];
+    } else if (s == 1) {  // the gate row of the same output is in the previous piece
+        const float gy = y[row_partner(ri)];
         swiglu_row(g, r, g.norm ? __fmul_rn(gy, scale) : gy, val, info, p);
     }
 }
@@ -893,7 +910,10 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
         bulk_copy(&tables[1], src + 1, sizeof(GroupTable), &c.gbar);
         ++gcopies.issued;
     }
-    if (threadIdx.x < 32) ok = wait_group(c, cidx, tables[0].count, st, p, tracing);
+    if (threadIdx.x < 32) {  // the first group's pieces, then its row table (while the input words arrive)
+        ok = wait_group(c, cidx, tables[0].count, st, p, tracing);
+        if (ok) build_rows(g, tables[0], cidx, c, c.rowinfo[0], threadIdx.x, 32);
+    }
     // the norm gain travels as the first group's first piece: every thread
     // observes its landing (long since, normally) before reading it
     const void *gain = g.norm_gain;
@@ -924,13 +944,15 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
     Epi e;
     for (int gi = 0;; ++gi) {
         const GroupTable &t = tables[gi & 1];
+        const int2 *rows = c.rowinfo[gi & 1];
         float *y = c.y[gi & 1];
-        group_dots(g, t, cidx, sm, in, y);
+        group_dots(g, t, rows, sm, in, y);
         const int count = t.count;
         const bool more = t.more != 0;
-        if (threadIdx.x == 0)
-            for (int k = 0; k < count; ++k) mbar_arrive(&c.empty[(cidx + k) % kQueue]);
-        group_epilogue(g, t, y, scale, info, p, c, e);
+        // the group's pieces are consumed: released by threads that finish no row (count <= 16, rows <= 256)
+        const int rel = kEngineThreads - 1 - threadIdx.x;
+        if (rel < count) mbar_arrive(&c.empty[(cidx + rel) % kQueue]);
+        group_epilogue(g, t, rows, y, scale, info, p, c, e);
         cidx += count;
         if (!more) break;
         ok = true;
@@ -938,6 +960,7 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
             if (threadIdx.x == 0) ok = wait_bar(&c.gbar, gcopies.next_parity(), st, c, p, false);  // table gi + 1
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (ok) ok = wait_group(c, cidx, tables[(gi + 1) & 1].count, st, p, tracing);
+            if (ok) build_rows(g, tables[(gi + 1) & 1], cidx, c, c.rowinfo[(gi + 1) & 1], threadIdx.x, 32);
         }
         if (!csync_and(ok)) {
             if (threadIdx.x == 0) c.abort = 1;
