@@ -632,8 +632,10 @@ struct Epi {
 // instead and returns this thread's part of sum(x^2) in `ss`: the norm's
 // factor is then applied to the dot products (kernels.cl:19-28 computes
 // (x * scale) * gain; scale * (W . (x * gain)) differs by float32 rounding).
+// Threads first .. first + count - 1 of the compute warps take part.
 __device__ bool read_input(const GemvPhase &g, int cols, const StepInfo &info, int p, float *in, StepState *st,
-                           bool norm, const void *gain, float &ss) {
+                           bool norm, const void *gain, float &ss, int first, int count) {
+    const int t = threadIdx.x - first;
     ss = 0.f;
     auto put = [&](int j, float v) {
         if (norm) {
@@ -642,24 +644,25 @@ __device__ bool read_input(const GemvPhase &g, int cols, const StepInfo &info, i
         }
         in[g.xsplit ? split_index(j, cols) : j] = v;
     };
+    if (t < 0 || t >= count) return true;
     if (g.input_kind == IN_EMBED_ROW) {
-        for (int j = threadIdx.x; j < cols; j += kEngineThreads)
+        for (int j = t; j < cols; j += count)
             put(j, load_weight(g.embed, g.embed_dtype, static_cast<size_t>(info.token) * cols + j));
         return true;
     }
     const unsigned tag = info.tag_base + p - 1;
     bool ok = true;
-    for (int base = 0; base < cols && ok; base += 4 * kEngineThreads) {
+    for (int base = 0; base < cols && ok; base += 4 * count) {
         float v[4];
         ok = read_words(
             [&](int u) -> const Word * {
-                const int e = base + u * kEngineThreads + threadIdx.x;
+                const int e = base + u * count + t;
                 return e < cols ? g.in + e : nullptr;
             },
             tag, v, st, p);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const int e = base + u * kEngineThreads + threadIdx.x;
+            const int e = base + u * count + t;
             if (ok && e < cols) put(e, v[u]);
         }
     }
@@ -910,19 +913,21 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
         bulk_copy(&tables[1], src + 1, sizeof(GroupTable), &c.gbar);
         ++gcopies.issued;
     }
-    if (threadIdx.x < 32) {  // the first group's pieces, then its row table (while the input words arrive)
+    float ss = 0.f;
+    if (threadIdx.x < 32) {
+        // warp 0: the first group's pieces, then its row table, while warps 1.. bring in the input
         ok = wait_group(c, cidx, tables[0].count, st, p, tracing);
         if (ok) build_rows(g, tables[0], cidx, c, c.rowinfo[0], threadIdx.x, 32);
+    } else {
+        // the norm gain travels as the first group's first piece: every reading
+        // thread observes its landing (long since, normally) before using it
+        const void *gain = g.norm_gain;
+        if (g.norm && tables[0].count > 0 && tables[0].p[0].seg < 0) {
+            ok = wait_bar(&c.full[cidx % kQueue], (cidx / kQueue) & 1, st, c, p, false);
+            gain = sm.ring + c.offset[cidx % kQueue];
+        }
+        ok = ok && read_input(g, cols, info, p, in, st, g.norm != 0, gain, ss, 32, kEngineThreads - 32);
     }
-    // the norm gain travels as the first group's first piece: every thread
-    // observes its landing (long since, normally) before reading it
-    const void *gain = g.norm_gain;
-    if (g.norm && tables[0].count > 0 && tables[0].p[0].seg < 0) {
-        ok = wait_bar(&c.full[cidx % kQueue], (cidx / kQueue) & 1, st, c, p, false) && ok;
-        gain = sm.ring + c.offset[cidx % kQueue];
-    }
-    float ss = 0.f;
-    ok = ok && read_input(g, cols, info, p, in, st, g.norm != 0, gain, ss);
     if (g.norm) {
         ss = warp_sum(ss);
         if ((threadIdx.x & 31) == 0) c.red[threadIdx.x >> 5] = ss;
@@ -994,7 +999,7 @@ __device__ bool gemv_direct(const GemvPhase &g, int p, StepState *st, const Step
     if (!mine) return true;
     float *in = sm.scratch;
     float ss;
-    const bool ok = read_input(g, cols, info, p, in, st, false, nullptr, ss);
+    const bool ok = read_input(g, cols, info, p, in, st, false, nullptr, ss, 0, kEngineThreads);
     if (!csync_and(ok)) {
         if (threadIdx.x == 0) c.abort = 1;
         return false;
