@@ -198,7 +198,7 @@ __host__ __device__ inline int attn_chunks(int total_keys, int kv_heads, int gri
 // distinct banks.  After the chunk's last tile the key/value region (`tiles`
 // floats from kt) takes the chunk records that merge_slice gathers.
 struct AttnLayout {
-    int q, knew, vnew, kt, vt, tiles, p, acc, m, l, corr, total;
+    int q, knew, vnew, kt, vt, tiles, p, acc, m, l, wm, total;
     int kstride, vstride;
 };
 __host__ __device__ inline int round4(int x) { return (x + 3) & ~3; }
@@ -219,9 +219,9 @@ __host__ __device__ inline AttnLayout attn_layout(int group_heads, int dim) {
     o += L.tiles;
     L.p = o;    o += round4(group_heads * kKeyTile);
     L.acc = o;  o += round4(group_heads * dim);
-    L.m = o;    o += round4(group_heads);
-    L.l = o;    o += round4(group_heads);
-    L.corr = o; o += round4(group_heads);
+    L.m = o;    o += round4(2 * group_heads);   // running max, two buffers (tile parity)
+    L.l = o;    o += round4(2 * group_heads);   // running sum, two buffers
+    L.wm = o;   o += round4(4 * group_heads);   // per-warp max, then sum, of the current tile
     L.total = o;
     return L;
 }

@@ -1202,6 +1202,84 @@ __device__ bool merge_slice(const AttnPhase &a, int g, int gq, int chunks, int c
     return true;
 }
 
+// Scores of one key tile with per-warp softmax statistics: element
+// e = i * kKeyTile + t (query head i, key t), so every warp holds 32 keys of
+// one head; p[e] = exp(score - warp max), the warp's max and sum go to
+// wm / wl[e / 32].  Keys t >= nt (and any past the tile) contribute nothing.
+// D: the head dim at compile time (unrolled), 0: at run time.
+template <int D>
+__device__ __forceinline__ void tile_scores(const float *q, const float *kt, int kstride, int d, int gq, int nt,
+                                            float sqrt_d, float *p, float *wm, float *wl) {
+    const int lane = threadIdx.x & 31;
+    const int dim = D ? D : d;
+    for (int e = threadIdx.x; e < gq * kKeyTile; e += kEngineThreads) {
+        const int i = e / kKeyTile, t = e - i * kKeyTile;
+        const bool live = t < nt;
+        const float *qi = q + i * dim, *kr = kt + (live ? t : 0) * kstride;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        if (D || (dim & 3) == 0) {
+#pragma unroll 8
+            for (int j = 0; j < dim; j += 4) {
+                const float4 qa = *reinterpret_cast<const float4 *>(qi + j);
+                const float4 ka = *reinterpret_cast<const float4 *>(kr + j);
+                s0 = fmaf(qa.x, ka.x, s0);
+                s1 = fmaf(qa.y, ka.y, s1);
+                s2 = fmaf(qa.z, ka.z, s2);
+                s3 = fmaf(qa.w, ka.w, s3);
+            }
+        } else {
+            for (int j = 0; j < dim; ++j) s0 = fmaf(qi[j], kr[j], s0);
+        }
+        const float sc = live ? __fdiv_rn((s0 + s1) + (s2 + s3), sqrt_d) : -INFINITY;  // kernels.cl:72
+        const float mw = warp_max(sc);
+        const float pr = (live && mw != -INFINITY) ? expf(sc - mw) : 0.f;
+        const float lw = warp_sum(pr);
+        p[e] = pr;
+        if (lane == 0) {
+            wm[e >> 5] = mw;
+            wl[e >> 5] = lw;
+        }
+    }
+}
+
+// Value mix of one key tile into the running (acc, max m, sum l) of
+// model.py:95-116's softmax: the two warp halves of head i are brought to the
+// common maximum.  m / l are read from buffer `par` and written to par ^ 1
+// (every thread reads the old state of its head).
+template <int D>
+__device__ __forceinline__ void tile_mix(const float *p, const float *vt, int vstride, int d, int gq, int nt,
+                                         const float *wm, const float *wl, float *acc, float *mrow, float *lrow,
+                                         int par) {
+    const int dim = D ? D : d;
+    for (int e = threadIdx.x; e < gq * dim; e += kEngineThreads) {
+        const int i = e / dim, j = e - i * dim;
+        const float m_old = mrow[par * gq + i], m0 = wm[2 * i], m1 = wm[2 * i + 1];
+        const float mx = fmaxf(m_old, fmaxf(m0, m1));
+        const float cf = (m_old == -INFINITY) ? 0.f : expf(m_old - mx);
+        const float f0 = (m0 == -INFINITY) ? 0.f : expf(m0 - mx);
+        const float f1 = (m1 == -INFINITY) ? 0.f : expf(m1 - mx);
+        const float *pi = p + i * kKeyTile;
+        float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+        if (nt == kKeyTile) {
+#pragma unroll
+            for (int t = 0; t < 32; t += 2) {
+                a0 = fmaf(pi[t], vt[t * vstride + j], a0);
+                a1 = fmaf(pi[t + 1], vt[(t + 1) * vstride + j], a1);
+                b0 = fmaf(pi[32 + t], vt[(32 + t) * vstride + j], b0);
+                b1 = fmaf(pi[33 + t], vt[(33 + t) * vstride + j], b1);
+            }
+        } else {  // rows past nt hold stale data: never read them
+            for (int t = 0; t < min(nt, 32); ++t) a0 = fmaf(pi[t], vt[t * vstride + j], a0);
+            for (int t = 32; t < nt; ++t) b0 = fmaf(pi[t], vt[t * vstride + j], b0);
+        }
+        acc[e] = fmaf(f1, b0 + b1, fmaf(f0, a0 + a1, acc[e] * cf));
+        if (j == 0) {
+            mrow[(par ^ 1) * gq + i] = mx;
+            lrow[(par ^ 1) * gq + i] = fmaf(f1, wl[2 * i + 1], fmaf(f0, wl[2 * i], lrow[par * gq + i] * cf));
+        }
+    }
+}
+
 // Work unit = (KV head g, chunk c of the attended rows): one pass over the
 // chunk's keys (in tiles of kKeyTile) for the group's query heads.  The
 // group's raw q rows and (owner) this token's raw k/v rows come from the qkv
@@ -1211,8 +1289,9 @@ __device__ bool merge_slice(const AttnPhase &a, int g, int gq, int chunks, int c
 // words and then merges one slice of the group's output (merge_slice).  With
 // chunks >= 2 there are never more units than CTAs, so a merging unit never
 // waits for work queued behind it on its own CTA.
-__device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph, const Smem &sm,
-                               bool first_tile_issued, StepState *st, const Tracer &tr) {
+template <int D>
+__device__ bool attn_gqa_phase_t(const AttnPhase &a, const StepInfo &info, int ph, const Smem &sm,
+                                 bool first_tile_issued, StepState *st, const Tracer &tr) {
     const int G = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = a.dim, gq = a.heads / a.kv_heads;
@@ -1221,13 +1300,12 @@ __device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph,
     const int chunks = geo.chunks, chunk_len = geo.chunk_len;
     const float sqrt_d = __fsqrt_rn(static_cast<float>(d));  // divisor, kernels.cl:72
     const int stride = d + 2;
-    const bool vec = (d & 3) == 0;
     const unsigned in_tag = info.tag_base + ph - 1, out_tag = info.tag_base + ph;
 
     const AttnLayout L = attn_layout(gq, d);
     float *q = sm.attn + L.q, *knew = sm.attn + L.knew, *vnew = sm.attn + L.vnew;
     float *kt = sm.attn + L.kt, *vt = sm.attn + L.vt, *p = sm.attn + L.p, *acc = sm.attn + L.acc;
-    float *mrow = sm.attn + L.m, *lrow = sm.attn + L.l, *corr = sm.attn + L.corr;
+    float *mrow = sm.attn + L.m, *lrow = sm.attn + L.l, *wm = sm.attn + L.wm, *wl = wm + 2 * gq;
     float *gains = sm.c->gains;
 
     for (int unit = blockIdx.x; unit < a.kv_heads * chunks; unit += G) {
@@ -1246,6 +1324,7 @@ __device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph,
             mrow[threadIdx.x] = -INFINITY;
             lrow[threadIdx.x] = 0.f;
         }
+        int par = 0;  // the running max / sum are in buffer par
         // 2. the group's q rows and (owner) this token's k / v rows
         bool ok = true;
         const int nq = gq * d, nread = nq + (owner ? 2 * d : 0);
@@ -1304,62 +1383,12 @@ __device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph,
                 }
                 csync();
             }
-            // 4. scores (4 independent partial sums per dot product)
-            for (int e = threadIdx.x; e < gq * nt; e += kEngineThreads) {
-                const int i = e / nt, t = e - i * nt;
-                const float *qi = q + i * d, *kr = kt + t * L.kstride;
-                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-                if (vec) {
-                    for (int j = 0; j < d; j += 4) {
-                        const float4 qa = *reinterpret_cast<const float4 *>(qi + j);
-                        const float4 ka = *reinterpret_cast<const float4 *>(kr + j);
-                        s0 = fmaf(qa.x, ka.x, s0);
-                        s1 = fmaf(qa.y, ka.y, s1);
-                        s2 = fmaf(qa.z, ka.z, s2);
-                        s3 = fmaf(qa.w, ka.w, s3);
-                    }
-                } else {
-                    for (int j = 0; j < d; ++j) s0 = fmaf(qi[j], kr[j], s0);
-                }
-                p[i * kKeyTile + t] = __fdiv_rn((s0 + s1) + (s2 + s3), sqrt_d);
-            }
+            // 4. scores, with the softmax statistics of each warp's 32 keys
+            tile_scores<D>(q, kt, L.kstride, d, gq, nt, sqrt_d, p, wm, wl);
             csync();
-            // 5. online softmax per query head
-            for (int i = warp; i < gq; i += kEngineWarps) {
-                float mt = -INFINITY;
-                for (int t = lane; t < nt; t += 32) mt = fmaxf(mt, p[i * kKeyTile + t]);
-                mt = warp_max(mt);
-                const float m_old = mrow[i], m_new = fmaxf(m_old, mt);
-                float sum = 0.f;
-                for (int t = lane; t < nt; t += 32) {
-                    const float e = (m_new == -INFINITY) ? 0.f : expf(p[i * kKeyTile + t] - m_new);
-                    p[i * kKeyTile + t] = e;
-                    sum += e;
-                }
-                sum = warp_sum(sum);
-                if (lane == 0) {
-                    const float cf = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-                    corr[i] = cf;
-                    lrow[i] = lrow[i] * cf + sum;
-                    mrow[i] = m_new;
-                }
-            }
-            csync();
-            // 6. value mix (4 independent partial sums)
-            for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
-                const int i = e / d, j = e - i * d;
-                const float *pi = p + i * kKeyTile;
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-                int t = 0;
-                for (; t + 3 < nt; t += 4) {
-                    a0 = fmaf(pi[t], vt[t * L.vstride + j], a0);
-                    a1 = fmaf(pi[t + 1], vt[(t + 1) * L.vstride + j], a1);
-                    a2 = fmaf(pi[t + 2], vt[(t + 2) * L.vstride + j], a2);
-                    a3 = fmaf(pi[t + 3], vt[(t + 3) * L.vstride + j], a3);
-                }
-                for (; t < nt; ++t) a0 = fmaf(pi[t], vt[t * L.vstride + j], a0);
-                acc[e] = fmaf(acc[e], corr[i], (a0 + a1) + (a2 + a3));
-            }
+            // 5. value mix and the running softmax state
+            tile_mix<D>(p, vt, L.vstride, d, gq, nt, wm, wl, acc, mrow, lrow, par);
+            par ^= 1;
             csync();
             if (tb + kKeyTile < t1) issue_tile(a, g, tb + kKeyTile, min(kKeyTile, t1 - tb - kKeyTile), start, length, L, kt, vt);
         }
@@ -1368,7 +1397,7 @@ __device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph,
         if (chunks == 1) {
             for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
                 const int i = e / d, j = e - i * d;
-                st_word(a.out + static_cast<size_t>(g * gq + i) * d + j, __fdiv_rn(acc[e], lrow[i]), out_tag);
+                st_word(a.out + static_cast<size_t>(g * gq + i) * d + j, __fdiv_rn(acc[e], lrow[par * gq + i]), out_tag);
             }
         } else {
             for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
@@ -1377,14 +1406,23 @@ __device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph,
             }
             if (threadIdx.x < gq) {
                 Word *rec = a.partial + (static_cast<size_t>(g * gq + threadIdx.x) * kMaxAttnChunks + c) * stride;
-                st_word(rec + d, mrow[threadIdx.x], out_tag);
-                st_word(rec + d + 1, lrow[threadIdx.x], out_tag);
+                st_word(rec + d, mrow[par * gq + threadIdx.x], out_tag);
+                st_word(rec + d + 1, lrow[par * gq + threadIdx.x], out_tag);
             }
             if (!merge_slice(a, g, gq, chunks, c, kt, out_tag, st, ph)) return false;  // the tiles are free
         }
         csync();
     }
     return true;
+}
+
+__device__ bool attn_gqa_phase(const AttnPhase &a, const StepInfo &info, int ph, const Smem &sm,
+                               bool first_tile_issued, StepState *st, const Tracer &tr) {
+    switch (a.dim) {
+        case 64: return attn_gqa_phase_t<64>(a, info, ph, sm, first_tile_issued, st, tr);
+        case 128: return attn_gqa_phase_t<128>(a, info, ph, sm, first_tile_issued, st, tr);
+        default: return attn_gqa_phase_t<0>(a, info, ph, sm, first_tile_issued, st, tr);
+    }
 }
 
 }  // namespace
