@@ -56,8 +56,6 @@ struct Control {
     float rope_sin[kMaxHeadDim / 2];
     GroupTable group[2][2];            // piece-group tables: [phase parity][group parity]
     int2 rowinfo[2][kRowBatch];        // row tables of alternate groups (build_rows)
-    unsigned long long rbar;           // the next phase's records landed (descriptor + first group table)
-    unsigned long long gbar;           // a later group table of the current phase landed
     float red[kEngineWarps];
     unsigned long long best[kEngineWarps];
     int ok;
@@ -145,20 +143,6 @@ __device__ __forceinline__ void st_word(Word *p, float v, unsigned tag) {
 }
 __device__ __forceinline__ bool word_ok(Word w, unsigned tag) { return static_cast<unsigned>(w >> 32) == tag; }
 __device__ __forceinline__ float word_value(Word w) { return __uint_as_float(static_cast<unsigned>(w)); }
-
-// Bulk copy of a record without an arrival (the caller arrives once with the
-// transaction bytes of all copies that complete on `bar`).
-__device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t bytes, unsigned long long *bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar))
-        : "memory");
-}
-__device__ __forceinline__ void mbar_expect(unsigned long long *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
-                 : "memory");
-}
 
 // ---- mbarrier / bulk copy primitives --------------------------------------------------
 __device__ __forceinline__ void mbar_init(unsigned long long *bar, int count) {
@@ -880,16 +864,16 @@ __device__ void group_epilogue(const GemvPhase &g, const GroupTable &t, const in
 
 // Record copies on an mbarrier: issued and awaited counts (thread 0), so that
 // an early exit can wait for a copy still in flight.
-struct RecordCopies {
-    int issued = 0, waited = 0;
-    __device__ int next_parity() { return waited++ & 1; }
-    __device__ void drain(unsigned long long *bar) {
-        const uint64_t start = global_ns();
-        for (; waited < issued; ++waited)
-            while (!mbar_wait_sleep(bar, waited & 1))
-                if (global_ns() - start > kWaitLimitNs) return;
-    }
-};
+// Warp 0 requests a record (`bytes`, a multiple of 16) into shared memory:
+// 16 bytes per lane per pass with cp.async, which leaves the bulk-copy
+// engine to the weight stream (a record queued behind weight pieces there
+// would hold up the warp that leads every phase).  Complete once the issuing
+// lanes have passed cp_async_wait_all.
+__device__ __forceinline__ void warp_fetch(void *dst, const void *src, int bytes) {
+    for (int o = (threadIdx.x & 31) * 16; o < bytes; o += 32 * 16)
+        cp_async16_cg(static_cast<char *>(dst) + o, static_cast<const char *>(src) + o);
+    cp_async_commit();
+}
 
 // GEMV whose weights stream through the shared-memory ring.  `cidx` is the
 // index of the next piece of this CTA's stream (the same in every thread).
@@ -899,7 +883,7 @@ struct RecordCopies {
 // sum of squares is taken while the input is scaled by the gain, and its
 // factor is applied in the epilogue.
 __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepInfo &info, const StepControl &ctl,
-                          const Smem &sm, int &cidx, RecordCopies &gcopies, const Tracer &tr) {
+                          const Smem &sm, int &cidx, const Tracer &tr) {
     Control &c = *sm.c;
     GroupTable *tables = c.group[p & 1];
     if (tables[0].count == 0 && !tables[0].more) return true;  // no rows here
@@ -908,11 +892,7 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
     const GroupTable *src = ctl.groups + g.group_offset + static_cast<size_t>(blockIdx.x) * g.group_stride;
     float *in = sm.scratch;
     bool ok = true;
-    if (threadIdx.x == 0 && tables[0].more) {  // later group tables arrive one group ahead
-        mbar_expect(&c.gbar, sizeof(GroupTable));
-        bulk_copy(&tables[1], src + 1, sizeof(GroupTable), &c.gbar);
-        ++gcopies.issued;
-    }
+    if (threadIdx.x < 32 && tables[0].more) warp_fetch(&tables[1], src + 1, sizeof(GroupTable));  // one group ahead
     float ss = 0.f;
     if (threadIdx.x < 32) {
         // warp 0: the first group's pieces, then its row table, while warps 1.. bring in the input
@@ -962,9 +942,9 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
         if (!more) break;
         ok = true;
         if (threadIdx.x < 32) {
-            if (threadIdx.x == 0) ok = wait_bar(&c.gbar, gcopies.next_parity(), st, c, p, false);  // table gi + 1
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (ok) ok = wait_group(c, cidx, tables[(gi + 1) & 1].count, st, p, tracing);
+            cp_async_wait_all();  // table gi + 1
+            __syncwarp();
+            ok = wait_group(c, cidx, tables[(gi + 1) & 1].count, st, p, tracing);
             if (ok) build_rows(g, tables[(gi + 1) & 1], cidx, c, c.rowinfo[(gi + 1) & 1], threadIdx.x, 32);
         }
         if (!csync_and(ok)) {
@@ -972,12 +952,7 @@ __device__ bool gemv_bulk(const GemvPhase &g, int p, StepState *st, const StepIn
             return false;
         }
         // every thread has finished group gi's epilogue: its table buffer takes group gi + 2
-        if (threadIdx.x == 0 && tables[(gi + 1) & 1].more) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_expect(&c.gbar, sizeof(GroupTable));
-            bulk_copy(&tables[gi & 1], src + gi + 2, sizeof(GroupTable), &c.gbar);
-            ++gcopies.issued;
-        }
+        if (threadIdx.x < 32 && tables[(gi + 1) & 1].more) warp_fetch(&tables[gi & 1], src + gi + 2, sizeof(GroupTable));
     }
     tr.mark(2);
     tr.waits(c.wait_ns, c.late);
@@ -1467,8 +1442,6 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
                 mbar_init(&c.full[i], 1);
                 mbar_init(&c.empty[i], 1);
             }
-            mbar_init(&c.rbar, 1);
-            mbar_init(&c.gbar, 1);
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
             c.abort = 0;
             c.wait_ns = 0;
@@ -1492,21 +1465,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     for (int i = threadIdx.x; i < info.xr1 - info.xr0; i += kEngineThreads)
         c.xres[i] = load_weight(ctl.embed, ctl.embed_dtype, static_cast<size_t>(info.token) * ctl.hidden + info.xr0 + i);
     // the first phase's records: descriptor, then its first group table (two round trips, once per launch)
-    RecordCopies rcopies, gcopies;
     bool ok = true;
-    if (threadIdx.x == 0) {
-        mbar_expect(&c.rbar, sizeof(Phase));
-        bulk_copy(&c.phase[0], &phases[0], sizeof(Phase), &c.rbar);
-        ++rcopies.issued;
-        ok = wait_bar(&c.rbar, rcopies.next_parity(), st, c, 0, false);
-        if (ok && c.phase[0].kind == PH_GEMV && c.phase[0].gemv.bulk) {
-            mbar_expect(&c.rbar, sizeof(GroupTable));
-            bulk_copy(&c.group[0][0],
-                      ctl.groups + c.phase[0].gemv.group_offset +
-                          static_cast<size_t>(blockIdx.x) * c.phase[0].gemv.group_stride,
-                      sizeof(GroupTable), &c.rbar);
-            ++rcopies.issued;
-            ok = wait_bar(&c.rbar, rcopies.next_parity(), st, c, 0, false);
+    if (threadIdx.x < 32) {
+        warp_fetch(&c.phase[0], &phases[0], sizeof(Phase));
+        cp_async_wait_all();
+        __syncwarp();
+        if (c.phase[0].kind == PH_GEMV && c.phase[0].gemv.bulk) {
+            warp_fetch(&c.group[0][0],
+                       ctl.groups + c.phase[0].gemv.group_offset +
+                           static_cast<size_t>(blockIdx.x) * c.phase[0].gemv.group_stride,
+                       sizeof(GroupTable));
+            cp_async_wait_all();
         }
     }
     ok = csync_and(ok);
@@ -1516,31 +1485,25 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         const Phase &ph = c.phase[p & 1];
         if (ph.layer < 0 && !need_head) break;  // the head is the last phase before the step end
         const bool prefetch = p + 1 < nphases - 1;
-        if (threadIdx.x == 0 && prefetch) {
-            // the next phase's descriptor and first group table: two bulk copies on one barrier
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            const bool table = ph.next_groups >= 0;
-            mbar_expect(&c.rbar, sizeof(Phase) + (table ? sizeof(GroupTable) : 0));
-            bulk_copy(&c.phase[(p + 1) & 1], &phases[p + 1], sizeof(Phase), &c.rbar);
-            if (table)
-                bulk_copy(&c.group[(p + 1) & 1][0],
-                          ctl.groups + ph.next_groups + static_cast<size_t>(blockIdx.x) * ph.next_group_stride,
-                          sizeof(GroupTable), &c.rbar);
-            ++rcopies.issued;
+        if (threadIdx.x < 32 && prefetch) {  // the next phase's descriptor and first group table
+            warp_fetch(&c.phase[(p + 1) & 1], &phases[p + 1], sizeof(Phase));
+            if (ph.next_groups >= 0)
+                warp_fetch(&c.group[(p + 1) & 1][0],
+                           ctl.groups + ph.next_groups + static_cast<size_t>(blockIdx.x) * ph.next_group_stride,
+                           sizeof(GroupTable));
         }
         const Tracer tr{ctl.trace ? ctl.trace + 1 + static_cast<size_t>(executed) * (gridDim.x * kTraceStamps + 1)
                                   : nullptr};
         if (ph.kind == PH_GEMV) {
-            if (ph.gemv.bulk) ok = gemv_bulk(ph.gemv, p, st, info, ctl, sm, cidx, gcopies, tr);
+            if (ph.gemv.bulk) ok = gemv_bulk(ph.gemv, p, st, info, ctl, sm, cidx, tr);
             else ok = gemv_direct(ph.gemv, p, st, info, sm);
         } else if (ph.kind == PH_ATTN_GQA) {
             ok = attn_gqa_phase(ph.attn, info, p, sm, tile_issued, st, tr);
             tile_issued = false;
         }
         if (!ok) break;
-        cp_async_wait_all();
         // the next phase's records have landed (normally long since); the barrier publishes them
-        if (threadIdx.x == 0 && prefetch) ok = wait_bar(&c.rbar, rcopies.next_parity(), st, c, p, false);
+        cp_async_wait_all();
         ok = csync_and(ok);
         if (!ok) break;
         // an attention phase next: its first key/value tile loads while the q/k/v words are awaited
@@ -1557,12 +1520,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         ++barriers;
         ok = grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, nphases - 2, c, [] {});
     }
-    if (!ok) {
-        if (threadIdx.x == 0) {
-            c.abort = 1;
-            rcopies.drain(&c.rbar);  // no record copy may land after the CTA has left
-            gcopies.drain(&c.gbar);
-        }
+    if (!ok) {  // every copy this CTA requested has landed (cp_async_wait_all above)
+        if (threadIdx.x == 0) c.abort = 1;
         return;
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) {
