@@ -46,7 +46,7 @@ constexpr int kBlockThreads = kEngineThreads + 32;  // + the weight-stream produ
 constexpr int kMaxSegments = 3;
 constexpr int kRowBatch = 256;       // rows of one piece (and of one direct-load batch)
 constexpr int kQueue = 32;           // pieces in flight per CTA (one mbarrier each)
-constexpr int kMaxAttnChunks = 16;   // key chunks per KV head (merged by the consumer)
+constexpr int kMaxAttnChunks = 64;   // key chunks per KV head (at most grid / KV heads are used)
 constexpr int kKeysPerChunk = 64;    // target keys per attention work unit
 constexpr int kKeyTile = 64;         // keys per attention tile
 constexpr int kSmemLimit = 227 * 1024;

@@ -1154,8 +1154,8 @@ __device__ bool merge_slice(const AttnPhase &a, int g, int gq, int chunks, int c
         },
         tag, vals, st, phase);
     if (!csync_and(ok)) return false;
-    if (threadIdx.x < npair) {
-        const int i = threadIdx.x / chunks, cc = threadIdx.x - i * chunks;
+    for (int r = threadIdx.x; r < npair; r += kEngineThreads) {
+        const int i = r / chunks, cc = r - i * chunks;
         const float *mi = ml + 2 * i * chunks;
         float mx = -INFINITY;
         for (int u = 0; u < chunks; ++u) mx = fmaxf(mx, mi[2 * u]);
@@ -1165,7 +1165,7 @@ __device__ bool merge_slice(const AttnPhase &a, int g, int gq, int chunks, int c
             den += (mu == -INFINITY) ? 0.f : expf(mu - mx) * mi[2 * u + 1];
         }
         const float m = mi[2 * cc];
-        wgt[threadIdx.x] = (m == -INFINITY) ? 0.f : expf(m - mx) / den;
+        wgt[r] = (m == -INFINITY) ? 0.f : expf(m - mx) / den;
     }
     csync();
     for (int k = threadIdx.x; k < e1 - e0; k += kEngineThreads) {
