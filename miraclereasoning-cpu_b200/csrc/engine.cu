@@ -769,10 +769,12 @@ int mr_model_finalize(mr_model *m) {
     int max_cols = 0;
     for (auto &kv : m->tensors)
         if (kv.second.shape.size() == 2) max_cols = std::max(max_cols, (int)kv.second.shape[1]);
-    // the attention region follows the GEMV input vector, so that an attention
-    // tile can be requested while the preceding GEMV phase still uses its input
-    m->attn_base = (max_cols + 31) & ~31;
-    m->scratch_floats = m->attn_base + attn_layout(gq_max, d).total;
+    // The attention region overlays the GEMV input vector: a phase's first key
+    // tile is requested only after the compute barrier that ends the preceding
+    // GEMV phase, and a GEMV phase reads its input only after the barrier that
+    // ends the attention phase before it.  The ring gets what the overlay frees.
+    m->attn_base = 0;
+    m->scratch_floats = std::max((max_cols + 31) & ~31, attn_layout(gq_max, d).total);
     const size_t control = decode_control_bytes();
     const size_t scratch = ((size_t)m->scratch_floats * 4 + 127) & ~size_t(127);
     const long long ring = (long long)kSmemLimit - 1024 - (long long)control - (long long)scratch;
