@@ -252,6 +252,30 @@ Phase gemv_phase(int layer, const Word *in, const TensorSlot *norm_gain, float e
     return ph;
 }
 
+// Piece and group caps of a phase (bytes).  While a CTA's rows of the phase
+// fit in half the ring (one group), pieces are at most a quarter of the ring
+// and groups at most half.  Phases that stream more per CTA take groups of up
+// to two thirds of the ring with pieces of at most a sixth: fewer group turns
+// (each costs a barrier and a row table; -4% step time on FlashLite), and a
+// group, the gain piece and a piece lost to a wrap still fit the ring together.
+void phase_caps(const mr_model *m, const GemvPhase &g, int &piece_cap, int &group_cap) {
+    const int ring = m->ring_bytes, n = m->grid - g.skip;
+    long long per_cta = 0;
+    int widest = 0;
+    for (int i = 0; i < g.nseg; ++i) {
+        const int row_bytes = g.seg[i].cols * (int)dtype_size(g.seg[i].dtype);
+        per_cta += (long long)((g.seg[i].rows + n - 1) / n) * row_bytes;
+        widest = std::max(widest, row_bytes);
+    }
+    if (per_cta <= ring / 2 || widest > ring / 6) {
+        piece_cap = ring / 4;
+        group_cap = ring / 2;
+    } else {
+        piece_cap = ring / 6;
+        group_cap = (int)((long long)ring * 2 / 3);
+    }
+}
+
 int build_plan(mr_model *m) {
     const mr_model_config &c = m->cfg;
     if (!is_gqa_family(c.family))
@@ -340,12 +364,13 @@ int build_plan(mr_model *m) {
     end.kind = PH_STEP_END;
     end.layer = -2;
     m->phases.push_back(end);
-    // Weight streaming through the shared-memory ring: pieces of at most a
-    // quarter of the ring, whole 16-byte rows (cp.async.bulk granularity).
-    const int piece_cap = m->ring_bytes / 4;
+    // Weight streaming through the shared-memory ring: pieces of whole 16-byte
+    // rows (cp.async.bulk granularity) within the phase's piece cap.
     for (Phase &ph : m->phases) {
         if (ph.kind != PH_GEMV) continue;
         GemvPhase &g = ph.gemv;
+        int piece_cap, group_cap;
+        phase_caps(m, g, piece_cap, group_cap);
         bool bulk = true;
         for (int i = 0; i < g.nseg; ++i) {
             const int row_bytes = g.seg[i].cols * (int)dtype_size(g.seg[i].dtype);
@@ -439,13 +464,16 @@ int build_pieces(mr_model *m) {
 
 // Piece groups of every (bulk phase, CTA), in the stream order of
 // build_pieces: greedy, a group closes before the piece (or gate/up pair) that
-// would take its rows past half the ring, kRowBatch rows or kGroupPieces pieces.
+// would take its rows past the phase's group cap, kRowBatch rows or kGroupPieces
+// pieces.
 int build_groups(mr_model *m) {
-    const int G = m->grid, cap = m->ring_bytes / 2;
+    const int G = m->grid;
     std::vector<GroupTable> flat;
     for (Phase &ph : m->phases) {
         if (ph.kind != PH_GEMV || !ph.gemv.bulk) continue;
         GemvPhase &g = ph.gemv;
+        int piece_cap, cap;
+        phase_caps(m, g, piece_cap, cap);
         const bool paired = g.epilogue == EPI_SWIGLU;
         const int cols = g.seg[0].cols, per = paired ? 2 : 1;
         std::vector<std::vector<GroupTable>> per_cta(G);

@@ -125,12 +125,13 @@ struct AttnPhase {
 
 // The compute warps take a bulk phase's pieces in groups, precomputed on the
 // host per (phase, CTA): consecutive pieces (a SwiGLU gate/up pair is never
-// split) of at most half the ring of rows (plus, in the first group, the norm
+// split) of at most half the ring of rows, or two thirds in phases that
+// stream more than half a ring per CTA (plus, in the first group, the norm
 // gain vector), kRowBatch rows and kGroupPieces pieces, awaited together and
 // computed in one pass.  Every older piece has been released when a group is
-// awaited and no piece exceeds a quarter of the ring, so a whole group (at
-// most three quarters of the ring, plus less than a piece lost to a wrap)
-// always fits in the ring at once.
+// awaited and pieces are at most a quarter (a sixth) of the ring, so a whole
+// group, its gain piece and less than a piece lost to a wrap always fit in
+// the ring at once.
 constexpr int kGroupPieces = kQueue / 2;
 
 struct GroupPiece {
