@@ -83,6 +83,7 @@ SIGNATURES = {
     "mr_model_fill_synthetic": (_I, [_P, C.c_char_p, _I, _I, C.POINTER(C.c_int64), C.c_uint64, _I, _F, _F]),
     "mr_model_finalize": (_I, [_P]),
     "mr_model_reset": (_I, [_P]),
+    "mr_model_set_batched_prefill": (_I, [_P, _I, _IP]),
     "mr_model_position": (_I, [_P, _IP]),
     "mr_model_weight_bytes": (_I, [_P, C.POINTER(C.c_uint64)]),
     "mr_model_step": (_I, [_P, _I, _FP, _IP]),

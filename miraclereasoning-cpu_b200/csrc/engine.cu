@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "engine.cuh"
+#include "prefill.cuh"
 
 namespace mr {
 
@@ -122,6 +123,10 @@ struct mr_model {
     Phase *d_phases = nullptr;
     std::vector<Phase> phases;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    // batched prefill (prefill.cu): available for BF16 models of the engine families
+    bool prefill_ok = false, prefill_on = true;
+    PrefillModel pm{};
+    PrefillWork pw{};
 };
 
 namespace {
@@ -635,6 +640,103 @@ int ready(mr_model *m) {
 
 // Runs n fed tokens starting at the current position; logits of the selected
 // rows are copied to `out` (return_all: n rows, else the last row only).
+constexpr int kPrefillChunk = 512;  // tokens per batched prefill chunk
+
+// The batched prefill applies when every projection and the lm_head are BF16
+// and the widths are whole 16-byte rows; otherwise prompts run token by token
+// through the decode kernel.
+void setup_prefill(mr_model *m) {
+    const mr_model_config &c = m->cfg;
+    const int d = c.head_dim, q = c.query_heads * d;
+    m->prefill_ok = false;
+    if (c.hidden_size % 8 || q % 8 || c.ffn_dim % 8 || d % 2) return;
+    auto bf16 = [&](const std::string &name) {
+        const TensorSlot *t = tensor(m, name);
+        return t && t->dtype == MR_DTYPE_BF16 ? t->ptr : nullptr;
+    };
+    PrefillModel &pm = m->pm;
+    pm.stream = m->ctx->stream;
+    pm.hidden = c.hidden_size;
+    pm.heads = c.query_heads;
+    pm.head_dim = d;
+    pm.ffn = c.ffn_dim;
+    pm.vocab = c.vocab_size;
+    pm.kv_max = *std::max_element(m->layer_kvh.begin(), m->layer_kvh.end());
+    pm.eps = c.norm_eps;
+    pm.residual_scale = c.residual_scale;
+    pm.qk_norm = c.qk_norm;
+    pm.split_half = c.split_half_rope;
+    const TensorSlot *embed = tensor(m, "embed"), *norm = tensor(m, "norm");
+    pm.embed = embed->ptr;
+    pm.embed_dt = embed->dtype;
+    pm.final_norm = norm->ptr;
+    pm.final_norm_dt = norm->dtype;
+    pm.head = bf16(c.tie_embeddings ? "embed" : "output");
+    pm.inv_freq = m->d_inv_freq;
+    if (!pm.head) return;
+    pm.layers.clear();
+    for (int l = 0; l < c.layers; ++l) {
+        const std::string p = "layers." + std::to_string(l) + ".";
+        PrefillLayer L{};
+        const TensorSlot *an = tensor(m, p + "a_norm"), *fn = tensor(m, p + "f_norm");
+        L.a_norm = an->ptr;
+        L.a_norm_dt = an->dtype;
+        L.f_norm = fn->ptr;
+        L.f_norm_dt = fn->dtype;
+        if (c.qk_norm) {
+            const TensorSlot *qn = tensor(m, p + "q_norm"), *kn = tensor(m, p + "k_norm");
+            L.q_norm = qn->ptr;
+            L.k_norm = kn->ptr;
+            L.qk_norm_dt = qn->dtype;
+        }
+        L.q = bf16(p + "q");
+        L.k = bf16(p + "k");
+        L.v = bf16(p + "v");
+        L.o = bf16(p + "o");
+        L.gate = bf16(p + "ffn.gate");
+        L.up = bf16(p + "ffn.up");
+        L.down = bf16(p + "ffn.down");
+        if (!L.q || !L.k || !L.v || !L.o || !L.gate || !L.up || !L.down) return;
+        L.k_cache = m->k_cache[l];
+        L.v_cache = m->v_cache[l];
+        L.capacity = m->cache_capacity[l];
+        L.kv_heads = m->layer_kvh[l];
+        pm.layers.push_back(L);
+    }
+    m->prefill_ok = true;
+}
+
+// Batched prefill: chunks of up to kPrefillChunk tokens through prefill_chunk,
+// then the device step state moves to the new position.
+int run_feed_batched(mr_model *m, int n, int return_all, float *out) {
+    const int V = m->cfg.vocab_size;
+    cudaStream_t st = m->ctx->stream;
+    int rc = prefill_reserve(m->pm, m->pw, std::min(n, kPrefillChunk), return_all != 0);
+    if (rc) return rc;
+    for (int done = 0; done < n;) {
+        const int T = std::min(kPrefillChunk, n - done);
+        rc = prefill_chunk(m->pm, m->pw, m->feed + done, T, m->position + done, return_all != 0);
+        if (rc) {
+            m->failed = true;
+            return rc;
+        }
+        if (return_all && out)
+            MR_CUDA_TRY(cudaMemcpyAsync(out + (size_t)done * V, m->pw.logits, sizeof(float) * (size_t)T * V,
+                                        cudaMemcpyDeviceToHost, st));
+        done += T;
+    }
+    if (!return_all && out) MR_CUDA_TRY(cudaMemcpyAsync(out, m->pw.logits, sizeof(float) * V, cudaMemcpyDeviceToHost, st));
+    const int position = m->position + n;
+    MR_CUDA_TRY(cudaMemcpyAsync(&m->state->position, &position, sizeof(int), cudaMemcpyHostToDevice, st));
+    cudaError_t err = cudaStreamSynchronize(st);
+    if (err != cudaSuccess) {
+        m->failed = true;
+        return cuda_error(err, "batched prefill");
+    }
+    m->position = position;
+    return MR_OK;
+}
+
 int run_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
     const int V = m->cfg.vocab_size;
     for (int i = 0; i < n; ++i) MR_REQUIRE(ids[i] >= 0 && ids[i] < V, "input token is outside the vocabulary");
@@ -643,6 +745,7 @@ int run_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
     int rc = ensure_feed(m, n);
     if (rc) return rc;
     MR_CUDA_TRY(cudaMemcpyAsync(m->feed, ids, sizeof(int) * n, cudaMemcpyHostToDevice, m->ctx->stream));
+    if (m->prefill_ok && m->prefill_on && n > 1) return run_feed_batched(m, n, return_all, out);
     StepControl ctl = base_control(m);
     ctl.feed_len = n;
     ctl.return_all = return_all;
@@ -730,6 +833,7 @@ int mr_model_destroy(mr_model *m) {
     cudaSetDevice(m->ctx->device);
     cudaStreamSynchronize(m->ctx->stream);
     for (void *p : m->allocations) cudaFree(p);
+    prefill_release(m->pw);
     if (m->ev0) cudaEventDestroy(m->ev0);
     if (m->ev1) cudaEventDestroy(m->ev1);
     mr_context *ctx = m->ctx;
@@ -864,8 +968,16 @@ int mr_model_finalize(mr_model *m) {
     MR_REQUIRE(per_sm >= 1, "decode kernel cannot be resident (occupancy 0)");
     MR_CUDA_TRY(cudaEventCreate(&m->ev0));
     MR_CUDA_TRY(cudaEventCreate(&m->ev1));
+    setup_prefill(m);
     m->finalized = true;
     return mr_model_reset(m);
+}
+
+int mr_model_set_batched_prefill(mr_model *m, int enable, int *available) {
+    MR_REQUIRE(m, "model is NULL");
+    m->prefill_on = enable != 0;
+    if (available) *available = m->prefill_ok ? 1 : 0;
+    return MR_OK;
 }
 
 int mr_model_reset(mr_model *m) {

@@ -1,0 +1,550 @@
+// Batched prompt processing (see prefill.cuh).
+//
+// Per layer, for a chunk of T tokens (model.py:257-285 for each token):
+//   RMSNorm rows -> BF16x3 planes -> GEMM q|k|v -> per-head q/k RMSNorm + RoPE
+//   -> causal attention over ring + chunk keys (-> planes) -> GEMM o, x += s*o
+//   -> RMSNorm rows -> planes -> GEMM gate|up -> SwiGLU (-> planes)
+//   -> GEMM down, x += s*down -> append the chunk's keys / values to the ring.
+// Then the final RMSNorm and the lm_head GEMM for the rows whose logits are
+// wanted.  Element-wise steps keep the reference's rounding (kernels.cl:19-56:
+// separate multiplies and adds); reductions (sums of squares, dot products,
+// softmax sums) are in FP32 in a different order than the reference's serial
+// loops, within the parity tolerance.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+
+#include "prefill.cuh"
+
+namespace mr {
+namespace {
+
+constexpr int kBM = 64;       // GEMM tile: tokens
+constexpr int kBN = 64;       // GEMM tile: output features
+constexpr int kBK = 32;       // GEMM tile: reduction (two k16 steps)
+constexpr int kPadK = kBK + 8;  // shared row stride (bf16): 80 bytes, conflict-free ldmatrix
+constexpr int kStages = 3;
+constexpr int kGemmThreads = 256;  // 8 warps: 2 (tokens) x 4 (features), warp tile 32 x 16
+
+__device__ __forceinline__ uint16_t to_bf16(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+__device__ __forceinline__ float from_bf16(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
+
+// x = p0 + p1 + p2 (BF16 parts; the residuals are exact in FP32).
+__device__ __forceinline__ void split3(float x, uint16_t &a, uint16_t &b, uint16_t &c) {
+    a = to_bf16(x);
+    const float r1 = __fsub_rn(x, from_bf16(a));
+    b = to_bf16(r1);
+    const float r2 = __fsub_rn(r1, from_bf16(b));
+    c = to_bf16(r2);
+}
+__device__ __forceinline__ void put_planes(uint16_t *planes, size_t plane_stride, size_t idx, float v) {
+    uint16_t a, b, c;
+    split3(v, a, b, c);
+    planes[idx] = a;
+    planes[plane_stride + idx] = b;
+    planes[2 * plane_stride + idx] = c;
+}
+
+__device__ __forceinline__ float block_reduce_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; ++i) t += red[i];
+    return t;
+}
+
+// ---- row kernels -----------------------------------------------------------------------
+// x[t] = embedding row of ids[t] (widened exactly).
+__global__ void k_embed_rows(const int *ids, int T, const void *embed, int dt, int h, float *x) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    const size_t row = static_cast<size_t>(ids[t]) * h;
+    for (int j = threadIdx.x; j < h; j += blockDim.x) x[static_cast<size_t>(t) * h + j] = load_weight(embed, dt, row + j);
+}
+
+// planes[row r - r0] = split((x[r] * scale) * gain) (kernels.cl:19-28), for rows r0 .. r0 + n - 1.
+__global__ void k_rms_planes(const float *x, int r0, int h, const void *gain, int gain_dt, float eps, uint16_t *planes,
+                             size_t plane_stride, int ld) {
+    __shared__ float red[32];
+    const int r = r0 + blockIdx.x;
+    const float *xr = x + static_cast<size_t>(r) * h;
+    float ss = 0.f;
+    for (int j = threadIdx.x; j < h; j += blockDim.x) ss = fmaf(xr[j], xr[j], ss);
+    ss = block_reduce_sum(ss, red);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)h), eps)));
+    for (int j = threadIdx.x; j < h; j += blockDim.x) {
+        const float gv = gain ? load_weight(gain, gain_dt, j) : 1.0f;
+        put_planes(planes, plane_stride, static_cast<size_t>(blockIdx.x) * ld + j, __fmul_rn(__fmul_rn(xr[j], scale), gv));
+    }
+}
+
+// planes[t] = split(silu(gate) * up) (kernels.cl:46-50).
+__global__ void k_swiglu_planes(const float *g, const float *u, int T, int f, uint16_t *planes, size_t plane_stride,
+                                int ld) {
+    const size_t n = static_cast<size_t>(T) * f;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t t = i / f, j = i - t * f;
+        const float gv = g[i];
+        put_planes(planes, plane_stride, t * ld + j, __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), u[i]));
+    }
+}
+
+// Per (token, head row) of q|k|v: q / k rows RMSNorm'd (q/k norm) then rotated
+// (kernels.cl:30-44: angle = position * frequency); v rows copied.  One warp per
+// row: rows 0..H-1 queries, H..H+KV-1 keys, H+KV..H+2KV-1 values.
+__global__ void k_qk_rope(const float *qkv, int T, int p0, int H, int KV, int d, int ldqkv, int qk_norm,
+                          const void *q_gain, const void *k_gain, int gain_dt, float eps, const float *inv_freq,
+                          int split_half, float *qh, float *kc, float *vc) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int rows = H + 2 * KV;
+    if (warp >= T * rows) return;
+    const int t = warp / rows, r = warp - t * rows;
+    const float *src;
+    float *dst;
+    const void *gain = nullptr;
+    bool rotate = true;
+    if (r < H) {
+        src = qkv + static_cast<size_t>(t) * ldqkv + static_cast<size_t>(r) * d;
+        dst = qh + (static_cast<size_t>(t) * H + r) * d;
+        gain = q_gain;
+    } else if (r < H + KV) {
+        src = qkv + static_cast<size_t>(t) * ldqkv + static_cast<size_t>(H + (r - H)) * d;
+        dst = kc + (static_cast<size_t>(t) * KV + (r - H)) * d;
+        gain = k_gain;
+    } else {
+        src = qkv + static_cast<size_t>(t) * ldqkv + static_cast<size_t>(H + KV + (r - H - KV)) * d;
+        dst = vc + (static_cast<size_t>(t) * KV + (r - H - KV)) * d;
+        rotate = false;
+    }
+    if (!rotate) {
+        for (int j = lane; j < d; j += 32) dst[j] = src[j];
+        return;
+    }
+    float scale = 1.0f;
+    if (qk_norm) {
+        float ss = 0.f;
+        for (int j = lane; j < d; j += 32) ss = fmaf(src[j], src[j], ss);
+        ss = warp_sum(ss);
+        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)d), eps)));
+    }
+    auto val = [&](int j) {
+        if (!qk_norm) return src[j];
+        return __fmul_rn(__fmul_rn(src[j], scale), gain ? load_weight(gain, gain_dt, j) : 1.0f);
+    };
+    const int half = d / 2;
+    const float pos = static_cast<float>(p0 + t);
+    for (int p = lane; p < half; p += 32) {
+        const int j = split_half ? p : 2 * p, k = split_half ? p + half : 2 * p + 1;
+        const float angle = __fmul_rn(pos, inv_freq[p]);
+        const float c = cosf(angle), s = sinf(angle);
+        const float u = val(j), v = val(k);
+        dst[j] = __fsub_rn(__fmul_rn(u, c), __fmul_rn(v, s));
+        dst[k] = __fadd_rn(__fmul_rn(u, s), __fmul_rn(v, c));
+    }
+}
+
+// ---- causal attention over the ring and the chunk ------------------------------------------
+constexpr int kAttnThreads = 256;
+constexpr int kAttnRows = 64;  // query rows per CTA (tokens x group heads)
+constexpr int kKT = 32;        // keys per tile
+
+// CTA = (block of QT tokens, KV head g), rows r = (token, group head).  Token t
+// at position p = p0 + t attends to positions (p - capacity, p]: those below p0
+// from the ring (slot = position % capacity), the rest from the chunk (model.py
+// :95-116; the ring holds min(count, capacity) keys).  Online softmax over key
+// tiles; the output rows go out as BF16x3 planes of the o projection's input.
+__global__ void __launch_bounds__(kAttnThreads) k_attention(const float *qh, const float *kc, const float *vc,
+                                                            const float *k_cache, const float *v_cache, int T, int p0,
+                                                            int H, int KV, int d, int cap, int QT, uint16_t *planes,
+                                                            size_t plane_stride, int ld) {
+    extern __shared__ __align__(16) float sm[];
+    const int gq = H / KV, g = blockIdx.y, t0 = blockIdx.x * QT;
+    const int nt = min(QT, T - t0), R = nt * gq;
+    const int ks = d + 4;
+    float *q = sm;                       // [kAttnRows][d]
+    float *kt = q + kAttnRows * d;       // [kKT][d + 4]
+    float *vt = kt + kKT * ks;           // [kKT][d]
+    float *s = vt + kKT * d;             // [kAttnRows][kKT]
+    float *acc = s + kAttnRows * kKT;    // [kAttnRows][d]
+    float *mrow = acc + kAttnRows * d;   // [kAttnRows]
+    float *lrow = mrow + kAttnRows;
+    float *corr = lrow + kAttnRows;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = kAttnThreads / 32;
+    for (int e = threadIdx.x; e < R * d; e += kAttnThreads) {
+        const int r = e / d, j = e - r * d, tt = r / gq, i = r - tt * gq;
+        q[e] = qh[(static_cast<size_t>(t0 + tt) * H + g * gq + i) * d + j];
+        acc[e] = 0.f;
+    }
+    for (int r = threadIdx.x; r < R; r += kAttnThreads) {
+        mrow[r] = -INFINITY;
+        lrow[r] = 0.f;
+    }
+    const float sqrt_d = __fsqrt_rn(static_cast<float>(d));
+    const int p_first = p0 + t0, p_last = p0 + t0 + nt - 1;
+    const int lo = max(0, p_first - cap + 1);
+    for (int kb = lo; kb <= p_last; kb += kKT) {
+        const int nk = min(kKT, p_last + 1 - kb);
+        __syncthreads();  // the previous tile's readers are done
+        for (int e = threadIdx.x; e < nk * d; e += kAttnThreads) {
+            const int kk = e / d, j = e - kk * d, pos = kb + kk;
+            float kv, vv;
+            if (pos < p0) {
+                const size_t row = (static_cast<size_t>(g) * cap + pos % cap) * d + j;
+                kv = k_cache[row];
+                vv = v_cache[row];
+            } else {
+                const size_t row = (static_cast<size_t>(pos - p0) * KV + g) * d + j;
+                kv = kc[row];
+                vv = vc[row];
+            }
+            kt[kk * ks + j] = kv;
+            vt[kk * d + j] = vv;
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < R * kKT; e += kAttnThreads) {
+            const int r = e / kKT, kk = e - r * kKT, pos = kb + kk;
+            const int p = p_first + r / gq;
+            float v = -INFINITY;
+            if (kk < nk && pos <= p && pos > p - cap) {
+                const float *qr = q + r * d, *kr = kt + kk * ks;
+                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+                int j = 0;
+                for (; j + 3 < d; j += 4) {
+                    s0 = fmaf(qr[j], kr[j], s0);
+                    s1 = fmaf(qr[j + 1], kr[j + 1], s1);
+                    s2 = fmaf(qr[j + 2], kr[j + 2], s2);
+                    s3 = fmaf(qr[j + 3], kr[j + 3], s3);
+                }
+                for (; j < d; ++j) s0 = fmaf(qr[j], kr[j], s0);
+                v = __fdiv_rn((s0 + s1) + (s2 + s3), sqrt_d);  // kernels.cl:72
+            }
+            s[e] = v;
+        }
+        __syncthreads();
+        for (int r = warp; r < R; r += nw) {
+            const float v = s[r * kKT + lane];  // kKT == 32: one key per lane
+            const float mt = warp_max(v);
+            const float m_old = mrow[r], m_new = fmaxf(m_old, mt);
+            const float pr = (v == -INFINITY) ? 0.f : expf(v - m_new);
+            const float sum = warp_sum(pr);
+            s[r * kKT + lane] = pr;
+            if (lane == 0) {
+                const float cf = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+                corr[r] = cf;
+                lrow[r] = fmaf(lrow[r], cf, sum);
+                mrow[r] = m_new;
+            }
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < R * d; e += kAttnThreads) {
+            const int r = e / d, j = e - r * d;
+            const float *pr = s + r * kKT;
+            float a0 = 0.f, a1 = 0.f;
+            int kk = 0;
+            for (; kk + 1 < nk; kk += 2) {
+                a0 = fmaf(pr[kk], vt[kk * d + j], a0);
+                a1 = fmaf(pr[kk + 1], vt[(kk + 1) * d + j], a1);
+            }
+            if (kk < nk) a0 = fmaf(pr[kk], vt[kk * d + j], a0);
+            acc[e] = fmaf(acc[e], corr[r], a0 + a1);
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < R * d; e += kAttnThreads) {
+        const int r = e / d, j = e - r * d, tt = r / gq, i = r - tt * gq;
+        put_planes(planes, plane_stride, static_cast<size_t>(t0 + tt) * ld + (g * gq + i) * d + j,
+                   __fdiv_rn(acc[e], lrow[r]));
+    }
+}
+
+// The chunk's keys / values into the ring (after the attention that reads the
+// ring's older rows): positions p0 .. p0 + T - 1, of which only the last
+// `capacity` survive.
+__global__ void k_ring_append(const float *kc, const float *vc, int T, int p0, int KV, int d, int cap, float *k_cache,
+                              float *v_cache) {
+    const int first = max(0, T - cap);
+    const size_t n = static_cast<size_t>(T - first) * KV * d;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int j = static_cast<int>(i % d);
+        const size_t rest = i / d;
+        const int g = static_cast<int>(rest % KV), t = first + static_cast<int>(rest / KV);
+        const size_t src = (static_cast<size_t>(t) * KV + g) * d + j;
+        const size_t dst = (static_cast<size_t>(g) * cap + (p0 + t) % cap) * d + j;
+        k_cache[dst] = kc[src];
+        v_cache[dst] = vc[src];
+    }
+}
+
+// ---- GEMM on the tensor cores ----------------------------------------------------------------
+// Y[m][col0 + n] (+)= sum_k X[m][k] * W[n][k] for a segment of output features,
+// X given as three BF16 planes (x = x0 + x1 + x2) and W BF16 [N][K] row-major:
+// three mma.sync m16n8k16 BF16 products per step, FP32 accumulation.  `resid`:
+// Y = Y + scale * acc (kernels.cl:52-56), else Y = acc.
+struct GemmSeg {
+    const uint16_t *w;
+    int n, col0, tiles;  // features, first output column, feature tiles before this segment
+};
+struct GemmArgs {
+    const uint16_t *planes;
+    size_t plane_stride;
+    int lda, M, K;
+    float *y;
+    int ldy, resid;
+    float scale;
+    GemmSeg seg[3];
+    int nseg;
+};
+
+__device__ __forceinline__ void cp16(void *dst, const void *src, bool valid) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+    const int bytes = valid ? 16 : 0;  // 0: zero-fill, no global read
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(kGemmThreads) k_gemm_bf16x3(GemmArgs args) {
+    extern __shared__ __align__(16) uint16_t gs[];
+    // locate the segment of this feature tile
+    int si = 0;
+    while (si + 1 < args.nseg && static_cast<int>(blockIdx.x) >= args.seg[si + 1].tiles) ++si;
+    const GemmSeg seg = args.seg[si];
+    const int n0 = (blockIdx.x - seg.tiles) * kBN, m0 = blockIdx.y * kBM;
+    const int K = args.K, ktiles = (K + kBK - 1) / kBK;
+    constexpr int kStageA = 3 * kBM * kPadK, kStage = kStageA + kBN * kPadK;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wm = warp >> 2, wn = warp & 3;  // warp tile: tokens wm*32 .. +32, features wn*16 .. +16
+
+    auto load_stage = [&](int stage, int kt) {
+        uint16_t *a = gs + stage * kStage, *b = a + kStageA;
+        const int k0 = kt * kBK;
+        // A: 3 planes x 64 rows x 4 chunks; B: 64 rows x 4 chunks -> 1024 chunks, 4 per thread
+        for (int c = tid; c < (3 * kBM + kBN) * 4; c += kGemmThreads) {
+            const int row = c >> 2, ch = c & 3, k = k0 + ch * 8;
+            if (row < 3 * kBM) {
+                const int pl = row / kBM, r = row - pl * kBM, m = m0 + r;
+                const bool ok = m < args.M && k < K;
+                const uint16_t *src = args.planes + (ok ? pl * args.plane_stride + static_cast<size_t>(m) * args.lda + k : 0);
+                cp16(a + (pl * kBM + r) * kPadK + ch * 8, src, ok);
+            } else {
+                const int r = row - 3 * kBM, n = n0 + r;
+                const bool ok = n < seg.n && k < K;
+                const uint16_t *src = seg.w + (ok ? static_cast<size_t>(n) * K + k : 0);
+                cp16(b + r * kPadK + ch * 8, src, ok);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    // the leading part's products and the two small parts' products are summed
+    // apart (each small-part term would otherwise round at the large sum's ulp)
+    float acc[2][2][4], lo[2][2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[i][j][e] = lo[i][j][e] = 0.f;
+
+    for (int s = 0; s < kStages - 1; ++s) {
+        if (s < ktiles) load_stage(s, s);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    for (int kt = 0; kt < ktiles; ++kt) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 2) : "memory");
+        __syncthreads();
+        const int nk = kt + kStages - 1;
+        if (nk < ktiles) load_stage(nk % kStages, nk);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        const uint16_t *a = gs + (kt % kStages) * kStage, *b = a + kStageA;
+#pragma unroll
+        for (int ks = 0; ks < kBK; ks += 16) {
+            // B fragments: features wn*16 + {0..7, 8..15}, k ks .. ks+15
+            uint32_t bf[4];
+            ldsm_x4(bf, b + (wn * 16 + (lane & 7) + ((lane >> 4) << 3)) * kPadK + ks + ((lane >> 3) & 1) * 8);
+#pragma unroll
+            for (int pl = 0; pl < 3; ++pl) {
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    uint32_t af[4];
+                    ldsm_x4(af, a + (pl * kBM + wm * 32 + i * 16 + (lane & 15)) * kPadK + ks + (lane >> 4) * 8);
+                    mma_bf16(pl == 0 ? acc[i][0] : lo[i][0], af, bf[0], bf[1]);
+                    mma_bf16(pl == 0 ? acc[i][1] : lo[i][1], af, bf[2], bf[3]);
+                }
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    // epilogue: D rows = tokens (lane / 4, + 8), columns = features 2 (lane % 4) + {0, 1}
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int m = m0 + wm * 32 + i * 16 + (lane >> 2) + h * 8;
+                const int n = n0 + wn * 16 + j * 8 + (lane & 3) * 2;
+                if (m >= args.M) continue;
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    if (n + e >= seg.n) continue;
+                    float *dst = args.y + static_cast<size_t>(m) * args.ldy + seg.col0 + n + e;
+                    const float v = acc[i][j][2 * h + e] + lo[i][j][2 * h + e];
+                    *dst = args.resid ? __fadd_rn(*dst, __fmul_rn(args.scale, v)) : v;
+                }
+            }
+}
+
+constexpr size_t kGemmSmem = static_cast<size_t>(kStages) * (3 * kBM + kBN) * kPadK * sizeof(uint16_t);
+
+int gemm(cudaStream_t stream, const uint16_t *planes, size_t plane_stride, int lda, int M, int K,
+         std::initializer_list<GemmSeg> segs, float *y, int ldy, bool resid, float scale) {
+    GemmArgs a{};
+    a.planes = planes;
+    a.plane_stride = plane_stride;
+    a.lda = lda;
+    a.M = M;
+    a.K = K;
+    a.y = y;
+    a.ldy = ldy;
+    a.resid = resid ? 1 : 0;
+    a.scale = scale;
+    int tiles = 0;
+    for (const GemmSeg &s : segs) {
+        GemmSeg t = s;
+        t.tiles = tiles;
+        a.seg[a.nseg++] = t;
+        tiles += (s.n + kBN - 1) / kBN;
+    }
+    const dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>((M + kBM - 1) / kBM));
+    k_gemm_bf16x3<<<grid, kGemmThreads, kGemmSmem, stream>>>(a);
+    MR_CUDA_TRY(cudaGetLastError());
+    return MR_OK;
+}
+
+size_t attn_smem(int d) {
+    return sizeof(float) * (static_cast<size_t>(kAttnRows) * d + kKT * (d + 4) + static_cast<size_t>(kKT) * d +
+                            kAttnRows * kKT + static_cast<size_t>(kAttnRows) * d + 3 * kAttnRows);
+}
+
+}  // namespace
+
+void prefill_release(PrefillWork &w) {
+    for (void *p : {static_cast<void *>(w.x), static_cast<void *>(w.planes), static_cast<void *>(w.qkv),
+                    static_cast<void *>(w.qh), static_cast<void *>(w.kc), static_cast<void *>(w.vc),
+                    static_cast<void *>(w.gate), static_cast<void *>(w.up), static_cast<void *>(w.logits)})
+        if (p) cudaFree(p);
+    w = PrefillWork{};
+}
+
+int prefill_reserve(const PrefillModel &pm, PrefillWork &w, int tokens, bool all_logits) {
+    if (w.tokens >= tokens && (w.all_logits || !all_logits)) return MR_OK;
+    const int T = std::max(tokens, w.tokens);
+    const bool all = all_logits || w.all_logits;
+    prefill_release(w);
+    const int q = pm.heads * pm.head_dim, kv = pm.kv_max * pm.head_dim;
+    w.kmax = std::max({pm.hidden, q, pm.ffn});
+    auto alloc = [&](void **p, size_t bytes) -> int {
+        MR_CUDA_TRY(cudaMalloc(p, bytes ? bytes : 16));
+        return MR_OK;
+    };
+    int rc = alloc(reinterpret_cast<void **>(&w.x), sizeof(float) * T * pm.hidden);
+    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.planes), sizeof(uint16_t) * 3 * static_cast<size_t>(T) * w.kmax);
+    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.qkv), sizeof(float) * T * static_cast<size_t>(q + 2 * kv));
+    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.qh), sizeof(float) * T * static_cast<size_t>(q));
+    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.kc), sizeof(float) * T * static_cast<size_t>(kv));
+    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.vc), sizeof(float) * T * static_cast<size_t>(kv));
+    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.gate), sizeof(float) * T * static_cast<size_t>(pm.ffn));
+    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.up), sizeof(float) * T * static_cast<size_t>(pm.ffn));
+    if (!rc)
+        rc = alloc(reinterpret_cast<void **>(&w.logits), sizeof(float) * (all ? T : 1) * static_cast<size_t>(pm.vocab));
+    if (rc) {
+        prefill_release(w);
+        return rc;
+    }
+    w.tokens = T;
+    w.all_logits = all;
+    return MR_OK;
+}
+
+int prefill_chunk(const PrefillModel &pm, PrefillWork &w, const int *d_ids, int T, int p0, bool all_logits) {
+    MR_REQUIRE(T > 0 && T <= w.tokens && (!all_logits || w.all_logits), "prefill workspace too small");
+    cudaStream_t st = pm.stream;
+    const int h = pm.hidden, H = pm.heads, d = pm.head_dim, f = pm.ffn, q = H * d;
+    const size_t ps = static_cast<size_t>(w.tokens) * w.kmax;  // plane stride
+    MR_CUDA_TRY(cudaFuncSetAttribute(k_gemm_bf16x3, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem));
+    MR_CUDA_TRY(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(d)));
+    k_embed_rows<<<T, 256, 0, st>>>(d_ids, T, pm.embed, pm.embed_dt, h, w.x);
+    MR_CUDA_TRY(cudaGetLastError());
+    for (const PrefillLayer &L : pm.layers) {
+        const int KV = L.kv_heads, kv = KV * d, ldqkv = q + 2 * kv;
+        // 1. RMSNorm -> q | k | v
+        k_rms_planes<<<T, 256, 0, st>>>(w.x, 0, h, L.a_norm, L.a_norm_dt, pm.eps, w.planes, ps, w.kmax);
+        int rc = gemm(st, w.planes, ps, w.kmax, T, h,
+                      {GemmSeg{static_cast<const uint16_t *>(L.q), q, 0, 0},
+                       GemmSeg{static_cast<const uint16_t *>(L.k), kv, q, 0},
+                       GemmSeg{static_cast<const uint16_t *>(L.v), kv, q + kv, 0}},
+                      w.qkv, ldqkv, false, 0.f);
+        if (rc) return rc;
+        // 2. q / k norm + RoPE; the chunk's keys and values
+        {
+            const int warps = T * (H + 2 * KV);
+            k_qk_rope<<<(warps * 32 + 255) / 256, 256, 0, st>>>(w.qkv, T, p0, H, KV, d, ldqkv, pm.qk_norm, L.q_norm,
+                                                                L.k_norm, L.qk_norm_dt, pm.eps, pm.inv_freq,
+                                                                pm.split_half, w.qh, w.kc, w.vc);
+            MR_CUDA_TRY(cudaGetLastError());
+        }
+        // 3. attention (reads the ring's older rows), then the ring append
+        {
+            const int gq = H / KV, QT = std::max(1, kAttnRows / gq);
+            const dim3 grid(static_cast<unsigned>((T + QT - 1) / QT), static_cast<unsigned>(KV));
+            k_attention<<<grid, kAttnThreads, attn_smem(d), st>>>(w.qh, w.kc, w.vc, L.k_cache, L.v_cache, T, p0, H, KV,
+                                                                  d, L.capacity, QT, w.planes, ps, w.kmax);
+            MR_CUDA_TRY(cudaGetLastError());
+            k_ring_append<<<256, 256, 0, st>>>(w.kc, w.vc, T, p0, KV, d, L.capacity, L.k_cache, L.v_cache);
+            MR_CUDA_TRY(cudaGetLastError());
+        }
+        // 4. o projection, x += s * o (model.py:282)
+        rc = gemm(st, w.planes, ps, w.kmax, T, q, {GemmSeg{static_cast<const uint16_t *>(L.o), h, 0, 0}}, w.x, h, true,
+                  pm.residual_scale);
+        if (rc) return rc;
+        // 5. RMSNorm -> gate | up -> SwiGLU -> down, x += s * down (model.py:87-89, 283)
+        k_rms_planes<<<T, 256, 0, st>>>(w.x, 0, h, L.f_norm, L.f_norm_dt, pm.eps, w.planes, ps, w.kmax);
+        rc = gemm(st, w.planes, ps, w.kmax, T, h, {GemmSeg{static_cast<const uint16_t *>(L.gate), f, 0, 0}}, w.gate, f,
+                  false, 0.f);
+        if (!rc)
+            rc = gemm(st, w.planes, ps, w.kmax, T, h, {GemmSeg{static_cast<const uint16_t *>(L.up), f, 0, 0}}, w.up, f,
+                      false, 0.f);
+        if (rc) return rc;
+        k_swiglu_planes<<<592, 256, 0, st>>>(w.gate, w.up, T, f, w.planes, ps, w.kmax);
+        MR_CUDA_TRY(cudaGetLastError());
+        rc = gemm(st, w.planes, ps, w.kmax, T, f, {GemmSeg{static_cast<const uint16_t *>(L.down), h, 0, 0}}, w.x, h,
+                  true, pm.residual_scale);
+        if (rc) return rc;
+    }
+    // final RMSNorm + lm_head for the rows whose logits are wanted (model.py:285, 307)
+    const int r0 = all_logits ? 0 : T - 1, rows = all_logits ? T : 1;
+    k_rms_planes<<<rows, 256, 0, st>>>(w.x, r0, h, pm.final_norm, pm.final_norm_dt, pm.eps, w.planes, ps, w.kmax);
+    return gemm(st, w.planes, ps, w.kmax, rows, h, {GemmSeg{static_cast<const uint16_t *>(pm.head), pm.vocab, 0, 0}},
+                w.logits, pm.vocab, false, 0.f);
+}
+
+}  // namespace mr

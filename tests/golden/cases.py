@@ -135,3 +135,34 @@ def bench_case(name):
 BENCH_CASES = ("nano15", "nano17")
 LOGIT_SUBSET = 1024     # leading logits stored per step for wide vocabularies
 TOPK_STORED = 64
+
+
+# Batched-prefill cases: the micro architectures with BF16 matrices (the
+# engine's tensor-core prefill applies to BF16 models) and a prompt long enough
+# to wrap the local window several times.
+PREFILL_CASES = ("nano17", "lite")
+PREFILL_CONTEXT = 96
+PREFILL_SPLIT = 13
+
+
+def prefill_config(name):
+    return replace(micro_config(name), max_positions=PREFILL_CONTEXT)
+
+
+def prefill_prompt(name):
+    return np.random.default_rng(11).integers(0, prefill_config(name).vocab_size, 48).tolist()
+
+
+def bf16_bits(array):
+    """Round-to-nearest-even BF16 bits of a float32 array."""
+    bits = np.ascontiguousarray(array, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return ((bits + 0x7FFF + ((bits >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def prefill_weights(config):
+    """micro_weights with every matrix stored as BF16 (uint16 bits); 1-D tensors stay float32."""
+    return {k: (bf16_bits(v) if v.ndim == 2 else v) for k, v in micro_weights(config).items()}
+
+
+def widen_bf16(bits):
+    return (bits.astype(np.uint32) << 16).view(np.float32)

@@ -19,7 +19,10 @@ saved:
   top-k blocks, MoE experts and weights, latent positions), greedy and sampled
   ``generate`` ids;
 * ``bench_<case>.npz`` — benchmark-architecture cases with short token
-  windows: leading logits, top-64 ids/values and the greedy ids.
+  windows: leading logits, top-64 ids/values and the greedy ids;
+* ``prefill_<case>.npz`` — micro architectures with BF16 matrices and a
+  48-token prompt: all-token logits, two-chunk logits, cache state, greedy
+  decode steps after the prompt.
 
 Discrete decisions are observed by wrapping the reference model's methods on
 the instance (no reference source is changed).
@@ -257,6 +260,34 @@ def run_kernels():
     np.savez_compressed(HERE / "kernels.npz", **out)
 
 
+def run_prefill(name, rc, rm):
+    """BF16 micro model: all-token logits of a 48-token prompt, the same prompt
+    in two chunks, and greedy decode steps after it (the reference widens
+    BF16 exactly, so it runs on the widened values)."""
+    config = cases.prefill_config(name)
+    ref_config = rc.ModelConfig.from_dict(config.to_dict())
+    weights = {k: (cases.widen_bf16(v) if v.dtype == np.uint16 else v)
+               for k, v in cases.prefill_weights(config).items()}
+    model = rm.MiracleModel(ref_config, weights, backend=HostBackend("reference"),
+                            context_length=cases.PREFILL_CONTEXT)
+    prompt = cases.prefill_prompt(name)
+    logits = model.prefill(prompt, return_all=True)
+    summary = state_summary(model)
+    steps, tokens = [], []
+    for _ in range(4):
+        tokens.append(int(np.argmax(steps[-1] if steps else logits[-1])))
+        steps.append(model.decode(tokens[-1]))
+    model.reset()
+    split = cases.PREFILL_SPLIT
+    chunked = np.concatenate([model.prefill(prompt[:split], return_all=True),
+                              model.prefill(prompt[split:], return_all=True)])
+    np.savez_compressed(
+        HERE / f"prefill_{name}.npz", logits=logits.astype(np.float32), chunked=chunked.astype(np.float32),
+        steps=np.stack(steps).astype(np.float32), tokens=np.asarray(tokens, np.int64),
+        prompt=np.asarray(prompt, np.int64), meta=json.dumps({"state": summary}))
+    return logits.shape
+
+
 def main(argv=None):
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference-root", type=Path, default=Path("/root/reference"))
@@ -264,7 +295,8 @@ def main(argv=None):
     args = parser.parse_args(argv)
     rc, rm = _ref_modules(args.reference_root)
     todo = args.only or ["kernels", "configs", *[f"micro_{c}" for c in cases.MICRO_CASES],
-                         *[f"bench_{c}" for c in cases.BENCH_CASES]]
+                         *[f"bench_{c}" for c in cases.BENCH_CASES],
+                         *[f"prefill_{c}" for c in cases.PREFILL_CASES]]
     for item in todo:
         t0 = time.time()
         if item == "kernels":
@@ -275,6 +307,8 @@ def main(argv=None):
             result = "ok"
         elif item.startswith("micro_"):
             result = run_micro(item[6:], rc, rm)
+        elif item.startswith("prefill_"):
+            result = run_prefill(item[8:], rc, rm)
         else:
             result = run_bench(item[6:], rc, rm)
         print(f"{item}: {result} ({time.time() - t0:.1f}s)", flush=True)

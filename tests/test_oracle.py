@@ -173,3 +173,16 @@ def test_oracle_bench_nano15_greedy_decode():
         logits.append(model.decode(tokens[-1]))
     assert tokens == golden["tokens"].tolist()
     np.testing.assert_array_equal(np.stack(logits), golden["full"])
+
+
+@pytest.mark.parametrize("name", cases.PREFILL_CASES)
+def test_oracle_prefill_bf16_cases(name):
+    """The BF16 prefill fixtures (reference-generated) reproduced bit for bit."""
+    golden = np.load(GOLDEN / f"prefill_{name}.npz")
+    config = cases.prefill_config(name)
+    weights = {k: (cases.widen_bf16(v) if v.dtype == np.uint16 else v) for k, v in cases.prefill_weights(config).items()}
+    model = ReferenceModel(config, weights, backend=HostBackend("oracle"), context_length=cases.PREFILL_CONTEXT)
+    prompt = cases.prefill_prompt(name)
+    np.testing.assert_array_equal(model.prefill(prompt, return_all=True), golden["logits"])
+    steps = [model.decode(int(t)) for t in golden["tokens"]]
+    np.testing.assert_array_equal(np.stack(steps), golden["steps"])
