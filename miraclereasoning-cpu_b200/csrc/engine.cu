@@ -649,7 +649,7 @@ void setup_prefill(mr_model *m) {
     const mr_model_config &c = m->cfg;
     const int d = c.head_dim, q = c.query_heads * d;
     m->prefill_ok = false;
-    if (c.hidden_size % 8 || q % 8 || c.ffn_dim % 8 || d % 2) return;
+    if (c.hidden_size % 8 || q % 8 || c.ffn_dim % 8 || d % 4) return;
     auto bf16 = [&](const std::string &name) {
         const TensorSlot *t = tensor(m, name);
         return t && t->dtype == MR_DTYPE_BF16 ? t->ptr : nullptr;

@@ -152,13 +152,17 @@ __global__ void k_qk_rope(const float *qkv, int T, int p0, int H, int KV, int d,
 // ---- causal attention over the ring and the chunk ------------------------------------------
 constexpr int kAttnThreads = 256;
 constexpr int kAttnRows = 64;  // query rows per CTA (tokens x group heads)
-constexpr int kKT = 32;        // keys per tile
+constexpr int kKT = 32;        // keys per tile (one per lane in the softmax step)
 
 // CTA = (block of QT tokens, KV head g), rows r = (token, group head).  Token t
 // at position p = p0 + t attends to positions (p - capacity, p]: those below p0
 // from the ring (slot = position % capacity), the rest from the chunk (model.py
 // :95-116; the ring holds min(count, capacity) keys).  Online softmax over key
-// tiles; the output rows go out as BF16x3 planes of the o projection's input.
+// tiles.  Register blocking keeps shared-memory traffic below the arithmetic:
+// a thread scores 2 rows x 4 keys from float4 loads, and accumulates a
+// 4-row x 4-dim block of the output (two blocks for head dims above 64) in
+// registers across the tiles.  The output rows go out as BF16x3 planes of
+// the o projection's input.  Head dims are multiples of 4.
 __global__ void __launch_bounds__(kAttnThreads) k_attention(const float *qh, const float *kc, const float *vc,
                                                             const float *k_cache, const float *v_cache, int T, int p0,
                                                             int H, int KV, int d, int cap, int QT, uint16_t *planes,
@@ -167,73 +171,91 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const float *qh, con
     const int gq = H / KV, g = blockIdx.y, t0 = blockIdx.x * QT;
     const int nt = min(QT, T - t0), R = nt * gq;
     const int ks = d + 4;
-    float *q = sm;                       // [kAttnRows][d]
-    float *kt = q + kAttnRows * d;       // [kKT][d + 4]
+    float *q = sm;                       // [kAttnRows][d + 4]
+    float *kt = q + kAttnRows * ks;      // [kKT][d + 4]
     float *vt = kt + kKT * ks;           // [kKT][d]
-    float *s = vt + kKT * d;             // [kAttnRows][kKT]
-    float *acc = s + kAttnRows * kKT;    // [kAttnRows][d]
-    float *mrow = acc + kAttnRows * d;   // [kAttnRows]
+    float *s = vt + kKT * d;             // [kAttnRows][kKT + 1]
+    float *mrow = s + kAttnRows * (kKT + 1);
     float *lrow = mrow + kAttnRows;
     float *corr = lrow + kAttnRows;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = kAttnThreads / 32;
-    for (int e = threadIdx.x; e < R * d; e += kAttnThreads) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = kAttnThreads / 32;
+    for (int e = tid; e < kAttnRows * d; e += kAttnThreads) {
         const int r = e / d, j = e - r * d, tt = r / gq, i = r - tt * gq;
-        q[e] = qh[(static_cast<size_t>(t0 + tt) * H + g * gq + i) * d + j];
-        acc[e] = 0.f;
+        q[r * ks + j] = r < R ? qh[(static_cast<size_t>(t0 + tt) * H + g * gq + i) * d + j] : 0.f;
     }
-    for (int r = threadIdx.x; r < R; r += kAttnThreads) {
+    for (int r = tid; r < kAttnRows; r += kAttnThreads) {
         mrow[r] = -INFINITY;
         lrow[r] = 0.f;
     }
+    // score block of this thread: rows sr, sr + 1; keys sk .. sk + 3
+    const int sr = (tid >> 3) * 2, sk = (tid & 7) * 4;
+    // output blocks: rows 4 * (b / (d / 4)) .. + 3, dims 4 * (b % (d / 4)) .. + 3, b = tid, tid + 256
+    const int dq = d / 4, nblk = (kAttnRows / 4) * dq;
+    float acc[2][16];
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) acc[b][e] = 0.f;
     const float sqrt_d = __fsqrt_rn(static_cast<float>(d));
     const int p_first = p0 + t0, p_last = p0 + t0 + nt - 1;
     const int lo = max(0, p_first - cap + 1);
     for (int kb = lo; kb <= p_last; kb += kKT) {
         const int nk = min(kKT, p_last + 1 - kb);
         __syncthreads();  // the previous tile's readers are done
-        for (int e = threadIdx.x; e < nk * d; e += kAttnThreads) {
-            const int kk = e / d, j = e - kk * d, pos = kb + kk;
-            float kv, vv;
-            if (pos < p0) {
-                const size_t row = (static_cast<size_t>(g) * cap + pos % cap) * d + j;
-                kv = k_cache[row];
-                vv = v_cache[row];
-            } else {
-                const size_t row = (static_cast<size_t>(pos - p0) * KV + g) * d + j;
-                kv = kc[row];
-                vv = vc[row];
-            }
-            kt[kk * ks + j] = kv;
-            vt[kk * d + j] = vv;
-        }
-        __syncthreads();
-        for (int e = threadIdx.x; e < R * kKT; e += kAttnThreads) {
-            const int r = e / kKT, kk = e - r * kKT, pos = kb + kk;
-            const int p = p_first + r / gq;
-            float v = -INFINITY;
-            if (kk < nk && pos <= p && pos > p - cap) {
-                const float *qr = q + r * d, *kr = kt + kk * ks;
-                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-                int j = 0;
-                for (; j + 3 < d; j += 4) {
-                    s0 = fmaf(qr[j], kr[j], s0);
-                    s1 = fmaf(qr[j + 1], kr[j + 1], s1);
-                    s2 = fmaf(qr[j + 2], kr[j + 2], s2);
-                    s3 = fmaf(qr[j + 3], kr[j + 3], s3);
+        for (int e = tid; e < kKT * dq; e += kAttnThreads) {
+            const int kk = e / dq, j = (e - kk * dq) * 4, pos = kb + kk;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (kk < nk) {
+                const float *ksrc, *vsrc;
+                if (pos < p0) {
+                    const size_t row = (static_cast<size_t>(g) * cap + pos % cap) * d + j;
+                    ksrc = k_cache + row;
+                    vsrc = v_cache + row;
+                } else {
+                    const size_t row = (static_cast<size_t>(pos - p0) * KV + g) * d + j;
+                    ksrc = kc + row;
+                    vsrc = vc + row;
                 }
-                for (; j < d; ++j) s0 = fmaf(qr[j], kr[j], s0);
-                v = __fdiv_rn((s0 + s1) + (s2 + s3), sqrt_d);  // kernels.cl:72
+                kv = *reinterpret_cast<const float4 *>(ksrc);
+                vv = *reinterpret_cast<const float4 *>(vsrc);
             }
-            s[e] = v;
+            *reinterpret_cast<float4 *>(kt + kk * ks + j) = kv;
+            *reinterpret_cast<float4 *>(vt + kk * d + j) = vv;
         }
         __syncthreads();
-        for (int r = warp; r < R; r += nw) {
-            const float v = s[r * kKT + lane];  // kKT == 32: one key per lane
+        {  // scores: 2 rows x 4 keys per thread
+            float a[2][4];
+#pragma unroll
+            for (int x = 0; x < 2; ++x)
+#pragma unroll
+                for (int y = 0; y < 4; ++y) a[x][y] = 0.f;
+            for (int j = 0; j < d; j += 4) {
+                const float4 q0 = *reinterpret_cast<const float4 *>(q + sr * ks + j);
+                const float4 q1 = *reinterpret_cast<const float4 *>(q + (sr + 1) * ks + j);
+#pragma unroll
+                for (int y = 0; y < 4; ++y) {
+                    const float4 kv = *reinterpret_cast<const float4 *>(kt + (sk + y) * ks + j);
+                    a[0][y] = fmaf(q0.x, kv.x, fmaf(q0.y, kv.y, fmaf(q0.z, kv.z, fmaf(q0.w, kv.w, a[0][y]))));
+                    a[1][y] = fmaf(q1.x, kv.x, fmaf(q1.y, kv.y, fmaf(q1.z, kv.z, fmaf(q1.w, kv.w, a[1][y]))));
+                }
+            }
+#pragma unroll
+            for (int x = 0; x < 2; ++x)
+#pragma unroll
+                for (int y = 0; y < 4; ++y) {
+                    const int r = sr + x, kk = sk + y, pos = kb + kk, p = p_first + r / gq;
+                    const bool live = r < R && kk < nk && pos <= p && pos > p - cap;
+                    s[r * (kKT + 1) + kk] = live ? __fdiv_rn(a[x][y], sqrt_d) : -INFINITY;  // kernels.cl:72
+                }
+        }
+        __syncthreads();
+        for (int r = warp; r < R; r += nw) {  // online softmax, one key per lane
+            const float v = s[r * (kKT + 1) + lane];
             const float mt = warp_max(v);
             const float m_old = mrow[r], m_new = fmaxf(m_old, mt);
             const float pr = (v == -INFINITY) ? 0.f : expf(v - m_new);
             const float sum = warp_sum(pr);
-            s[r * kKT + lane] = pr;
+            s[r * (kKT + 1) + lane] = pr;
             if (lane == 0) {
                 const float cf = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
                 corr[r] = cf;
@@ -242,24 +264,49 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const float *qh, con
             }
         }
         __syncthreads();
-        for (int e = threadIdx.x; e < R * d; e += kAttnThreads) {
-            const int r = e / d, j = e - r * d;
-            const float *pr = s + r * kKT;
-            float a0 = 0.f, a1 = 0.f;
-            int kk = 0;
-            for (; kk + 1 < nk; kk += 2) {
-                a0 = fmaf(pr[kk], vt[kk * d + j], a0);
-                a1 = fmaf(pr[kk + 1], vt[(kk + 1) * d + j], a1);
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {  // value mix: 4 rows x 4 dims per block
+            const int blk = tid + b * kAttnThreads;
+            if (blk >= nblk) continue;
+            const int r0 = (blk / dq) * 4, j0 = (blk % dq) * 4;
+            if (r0 >= R) continue;
+            float *ac = acc[b];
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+                const float cf = corr[r0 + x];
+#pragma unroll
+                for (int y = 0; y < 4; ++y) ac[x * 4 + y] *= cf;
             }
-            if (kk < nk) a0 = fmaf(pr[kk], vt[kk * d + j], a0);
-            acc[e] = fmaf(acc[e], corr[r], a0 + a1);
+            for (int kk = 0; kk < nk; ++kk) {
+                const float4 vv = *reinterpret_cast<const float4 *>(vt + kk * d + j0);
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+                    const float pr = s[(r0 + x) * (kKT + 1) + kk];
+                    ac[x * 4 + 0] = fmaf(pr, vv.x, ac[x * 4 + 0]);
+                    ac[x * 4 + 1] = fmaf(pr, vv.y, ac[x * 4 + 1]);
+                    ac[x * 4 + 2] = fmaf(pr, vv.z, ac[x * 4 + 2]);
+                    ac[x * 4 + 3] = fmaf(pr, vv.w, ac[x * 4 + 3]);
+                }
+            }
         }
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < R * d; e += kAttnThreads) {
-        const int r = e / d, j = e - r * d, tt = r / gq, i = r - tt * gq;
-        put_planes(planes, plane_stride, static_cast<size_t>(t0 + tt) * ld + (g * gq + i) * d + j,
-                   __fdiv_rn(acc[e], lrow[r]));
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        const int blk = tid + b * kAttnThreads;
+        if (blk >= nblk) continue;
+        const int r0 = (blk / dq) * 4, j0 = (blk % dq) * 4;
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+            const int r = r0 + x;
+            if (r >= R) continue;
+            const int tt = r / gq, i = r - tt * gq;
+            const float l = lrow[r];
+#pragma unroll
+            for (int y = 0; y < 4; ++y)
+                put_planes(planes, plane_stride, static_cast<size_t>(t0 + tt) * ld + (g * gq + i) * d + j0 + y,
+                           __fdiv_rn(acc[b][x * 4 + y], l));
+        }
     }
 }
 
@@ -441,8 +488,8 @@ int gemm(cudaStream_t stream, const uint16_t *planes, size_t plane_stride, int l
 }
 
 size_t attn_smem(int d) {
-    return sizeof(float) * (static_cast<size_t>(kAttnRows) * d + kKT * (d + 4) + static_cast<size_t>(kKT) * d +
-                            kAttnRows * kKT + static_cast<size_t>(kAttnRows) * d + 3 * kAttnRows);
+    return sizeof(float) * (static_cast<size_t>(kAttnRows) * (d + 4) + kKT * (d + 4) + static_cast<size_t>(kKT) * d +
+                            kAttnRows * (kKT + 1) + 3 * kAttnRows);
 }
 
 }  // namespace
