@@ -191,8 +191,10 @@ MR_API int mr_model_reset(mr_model *model);
 /* Prompts of two or more tokens run batched (tensor-core GEMMs, causal
  * attention over the chunk) when every projection and the lm_head are BF16;
  * otherwise, or with enable = 0, token by token through the decode kernel
- * (the reference's serial order, model.py:295-312).  *available (optional)
- * reports whether the batched path applies to this model. */
+ * (the reference's serial order, model.py:295-312).  enable = 1: GEMMs on
+ * tcgen05 (default); enable = 2: on mma.sync (the legacy tensor-core path,
+ * kept as a comparison baseline).  *available (optional) reports whether the
+ * batched path applies to this model. */
 MR_API int mr_model_set_batched_prefill(mr_model *model, int enable, int *available);
 MR_API int mr_model_position(const mr_model *model, int *position);
 MR_API int mr_model_weight_bytes(const mr_model *model, uint64_t *bytes);

@@ -733,6 +733,11 @@ int run_feed_batched(mr_model *m, int n, int return_all, float *out) {
         m->failed = true;
         return cuda_error(err, "batched prefill");
     }
+    rc = prefill_status(m->pm, m->pw);
+    if (rc) {
+        m->failed = true;
+        return rc;
+    }
     m->position = position;
     return MR_OK;
 }
@@ -975,7 +980,9 @@ int mr_model_finalize(mr_model *m) {
 
 int mr_model_set_batched_prefill(mr_model *m, int enable, int *available) {
     MR_REQUIRE(m, "model is NULL");
+    MR_REQUIRE(enable >= 0 && enable <= 2, "enable must be 0, 1 or 2");
     m->prefill_on = enable != 0;
+    m->pw.tcgen05 = enable != 2;
     if (available) *available = m->prefill_ok ? 1 : 0;
     return MR_OK;
 }

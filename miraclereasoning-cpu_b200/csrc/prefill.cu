@@ -10,7 +10,9 @@
 // separate multiplies and adds); reductions (sums of squares, dot products,
 // softmax sums) are in FP32 in a different order than the reference's serial
 // loops, within the parity tolerance.
+#include <cuda.h>
 #include <cuda_bf16.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 
@@ -460,10 +462,233 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_bf16x3(GemmArgs args) {
             }
 }
 
+// ---- GEMM on the 5th-generation tensor cores (tcgen05) ----------------------------------------
+// Same product as k_gemm_bf16x3, one CTA per 128-token x 128-feature tile:
+// warp 0 lane 0 streams K tiles of 64 (three X planes + the W tile, 64 KB a
+// stage, 128-byte swizzle) by TMA into a 3-stage ring; warp 1 lane 0 issues
+// tcgen05.mma (M 128, N 128, K 16, BF16 -> FP32) into two TMEM accumulators
+// (the leading part, and the two small parts: summed apart as in
+// k_gemm_bf16x3) and hands each stage back with tcgen05.commit; warps 2-5
+// read the accumulators (tcgen05.ld, one TMEM lane = one token row per
+// thread) and apply the epilogue.  Every wait is bounded (kTcWaitNs): a wait
+// that gives up sets *err and the CTA winds down.
+constexpr int kTM = 128, kTN = 128, kTK = 64, kTStages = 3, kTcThreads = 192;
+constexpr uint32_t kTileBytes = kTM * kTK * 2;                       // 16 KB: one 128 x 64 BF16 tile
+constexpr uint32_t kTStageBytes = 4 * kTileBytes;                    // three X planes + W
+constexpr size_t kTcSmem = 1024 + kTStages * kTStageBytes + 256;     // alignment slack, tiles, barriers
+constexpr unsigned long long kTcWaitNs = 2000000000ull;
+
+struct TcMaps {
+    CUtensorMap a;     // X planes: {k, token, plane}
+    CUtensorMap b[3];  // W of each segment: {k, feature}
+};
+
+__device__ __forceinline__ uint64_t tc_now() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ uint32_t saddr(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ bool tc_try_wait(uint64_t *bar, int parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(saddr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait; false (and *err set) when it gives up or another wait already did
+__device__ bool tc_wait(uint64_t *bar, int parity, int *err) {
+    if (tc_try_wait(bar, parity)) return true;
+    const uint64_t start = tc_now();
+    for (unsigned spin = 0;; ++spin) {
+        if (tc_try_wait(bar, parity)) return true;
+        if ((spin & 255u) == 255u) {
+            if (*reinterpret_cast<volatile int *>(err)) return false;
+            if (tc_now() - start > kTcWaitNs) {
+                atomicExch(err, 1);
+                return false;
+            }
+        }
+    }
+}
+// K-major operand tile in shared memory, 128-byte swizzle: rows of 128 bytes,
+// 8-row groups 1024 bytes apart (stride byte offset), descriptor version 1
+// (sm100); the start address steps 32 bytes per K16 step inside the swizzle atom.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
+}
+// kind::f16 instruction descriptor: D F32, A and B BF16, both K-major, N = 128, M = 128
+constexpr uint32_t kTcIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kTN >> 3) << 17) |
+                              (static_cast<uint32_t>(kTM >> 4) << 24);
+
+__global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ TcMaps maps, GemmArgs args,
+                                                           int *err) {
+    extern __shared__ uint8_t tc_raw[];
+    uint8_t *tiles = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(tiles + kTStages * kTStageBytes);
+    uint64_t *empty = full + kTStages, *accf = empty + kTStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accf + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int si = 0;
+    while (si + 1 < args.nseg && static_cast<int>(blockIdx.x) >= args.seg[si + 1].tiles) ++si;
+    const GemmSeg seg = args.seg[si];
+    const int n0 = (blockIdx.x - seg.tiles) * kTN, m0 = blockIdx.y * kTM;
+    const int ktiles = (args.K + kTK - 1) / kTK;
+    if (tid == 0) {
+        for (int st = 0; st < kTStages; ++st) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&full[st])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&empty[st])) : "memory");
+        }
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(accf)) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {  // 256 TMEM columns: accumulator of the leading part (0..127) and of the small parts (128..255)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(saddr(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    if (warp == 0 && lane == 0) {  // TMA producer
+        const CUtensorMap *mb = &maps.b[si];
+        int issued = 0;
+        for (int kt = 0; kt < ktiles; ++kt) {
+            const int st = kt % kTStages;
+            if (kt >= kTStages && !tc_wait(&empty[st], ((kt / kTStages) - 1) & 1, err)) break;
+            uint8_t *base = tiles + st * kTStageBytes;
+            const uint32_t bar = saddr(&full[st]);
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kTStageBytes)
+                         : "memory");
+            const int k0 = kt * kTK;
+            for (int pl = 0; pl < 3; ++pl)
+                asm volatile(
+                    "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+                    "[%5];" ::"r"(saddr(base + pl * kTileBytes)),
+                    "l"(&maps.a), "r"(k0), "r"(m0), "r"(pl), "r"(bar)
+                    : "memory");
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                    saddr(base + 3 * kTileBytes)),
+                "l"(mb), "r"(k0), "r"(n0), "r"(bar)
+                : "memory");
+            ++issued;
+        }
+        // no copy may land after the CTA has left: every issued stage is awaited (bounded)
+        for (int kt = std::max(0, issued - kTStages); kt < issued; ++kt) {
+            const uint64_t start = tc_now();
+            while (!tc_try_wait(&full[kt % kTStages], (kt / kTStages) & 1) && tc_now() - start < kTcWaitNs) {
+            }
+        }
+    } else if (warp == 1 && lane == 0) {  // MMA issuer
+        bool ok = true;
+        for (int kt = 0; kt < ktiles && ok; ++kt) {
+            const int st = kt % kTStages;
+            ok = tc_wait(&full[st], (kt / kTStages) & 1, err);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t base = saddr(tiles + st * kTStageBytes);
+#pragma unroll
+            for (int ks = 0; ks < kTK / 16; ++ks) {
+                const uint64_t bd = sw128_desc(base + 3 * kTileBytes + ks * 32);
+#pragma unroll
+                for (int pl = 0; pl < 3; ++pl) {
+                    const uint64_t ad = sw128_desc(base + pl * kTileBytes + ks * 32);
+                    const uint32_t d = pl == 0 ? tmem : tmem + kTN;
+                    const uint32_t accumulate = pl == 0 ? (kt > 0 || ks > 0) : !(kt == 0 && ks == 0 && pl == 1);
+                    asm volatile(
+                        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+                        "l"(ad), "l"(bd), "r"(kTcIdesc), "r"(accumulate)
+                        : "memory");
+                }
+            }
+            // the stage is free once these MMAs have read it
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             saddr(&empty[st]))
+                         : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(accf))
+                     : "memory");
+    } else if (warp >= 2) {  // epilogue: thread = TMEM lane = token row of the tile
+        const bool ready = __all_sync(0xffffffffu, tc_wait(accf, 0, err));  // warp-uniform: tcgen05.ld is collective
+        if (ready && ktiles > 0) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int quarter = warp & 3, row = quarter * 32 + lane, m = m0 + row;
+            const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+            for (int c = 0; c < kTN; c += 32) {
+                uint32_t hi[32], lo[32];
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(hi[0]), "=r"(hi[1]), "=r"(hi[2]), "=r"(hi[3]), "=r"(hi[4]), "=r"(hi[5]), "=r"(hi[6]),
+                      "=r"(hi[7]), "=r"(hi[8]), "=r"(hi[9]), "=r"(hi[10]), "=r"(hi[11]), "=r"(hi[12]), "=r"(hi[13]),
+                      "=r"(hi[14]), "=r"(hi[15]), "=r"(hi[16]), "=r"(hi[17]), "=r"(hi[18]), "=r"(hi[19]),
+                      "=r"(hi[20]), "=r"(hi[21]), "=r"(hi[22]), "=r"(hi[23]), "=r"(hi[24]), "=r"(hi[25]),
+                      "=r"(hi[26]), "=r"(hi[27]), "=r"(hi[28]), "=r"(hi[29]), "=r"(hi[30]), "=r"(hi[31])
+                    : "r"(lane_base + c));
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(lo[0]), "=r"(lo[1]), "=r"(lo[2]), "=r"(lo[3]), "=r"(lo[4]), "=r"(lo[5]), "=r"(lo[6]),
+                      "=r"(lo[7]), "=r"(lo[8]), "=r"(lo[9]), "=r"(lo[10]), "=r"(lo[11]), "=r"(lo[12]), "=r"(lo[13]),
+                      "=r"(lo[14]), "=r"(lo[15]), "=r"(lo[16]), "=r"(lo[17]), "=r"(lo[18]), "=r"(lo[19]),
+                      "=r"(lo[20]), "=r"(lo[21]), "=r"(lo[22]), "=r"(lo[23]), "=r"(lo[24]), "=r"(lo[25]),
+                      "=r"(lo[26]), "=r"(lo[27]), "=r"(lo[28]), "=r"(lo[29]), "=r"(lo[30]), "=r"(lo[31])
+                    : "r"(lane_base + kTN + c));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (m < args.M) {
+                    float *dst = args.y + static_cast<size_t>(m) * args.ldy + seg.col0 + n0 + c;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (n0 + c + j >= seg.n) break;
+                        const float v = __uint_as_float(hi[j]) + __uint_as_float(lo[j]);
+                        dst[j] = args.resid ? __fadd_rn(dst[j], __fmul_rn(args.scale, v)) : v;
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// BF16 tensor map, box 64 (K) x 128 rows, 128-byte swizzle; rows past the extent read as zeros.
+int encode_map(CUtensorMap *map, const void *base, int rank, const cuuint64_t *dims, const cuuint64_t *strides) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return set_error(MR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTK), 128u, 1u}, estride[3] = {1u, 1u, 1u};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void *>(base),
+                           dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(MR_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return MR_OK;
+}
+
 constexpr size_t kGemmSmem = static_cast<size_t>(kStages) * (3 * kBM + kBN) * kPadK * sizeof(uint16_t);
 
-int gemm(cudaStream_t stream, const uint16_t *planes, size_t plane_stride, int lda, int M, int K,
-         std::initializer_list<GemmSeg> segs, float *y, int ldy, bool resid, float scale) {
+int gemm(const PrefillWork &w, cudaStream_t stream, const uint16_t *planes, size_t plane_stride, int lda, int M,
+         int K, std::initializer_list<GemmSeg> segs, float *y, int ldy, bool resid, float scale) {
     GemmArgs a{};
     a.planes = planes;
     a.plane_stride = plane_stride;
@@ -481,8 +706,28 @@ int gemm(cudaStream_t stream, const uint16_t *planes, size_t plane_stride, int l
         a.seg[a.nseg++] = t;
         tiles += (s.n + kBN - 1) / kBN;
     }
-    const dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>((M + kBM - 1) / kBM));
-    k_gemm_bf16x3<<<grid, kGemmThreads, kGemmSmem, stream>>>(a);
+    if (!w.tcgen05) {
+        const dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>((M + kBM - 1) / kBM));
+        k_gemm_bf16x3<<<grid, kGemmThreads, kGemmSmem, stream>>>(a);
+        MR_CUDA_TRY(cudaGetLastError());
+        return MR_OK;
+    }
+    // tcgen05 path: 128 x 128 tiles, operands by TMA
+    TcMaps maps{};
+    const cuuint64_t adims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M), 3};
+    const cuuint64_t astr[2] = {static_cast<cuuint64_t>(lda) * 2, static_cast<cuuint64_t>(plane_stride) * 2};
+    int rc = encode_map(&maps.a, planes, 3, adims, astr);
+    int tc_tiles = 0;
+    for (int i = 0; i < a.nseg && !rc; ++i) {
+        const cuuint64_t bdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(a.seg[i].n)};
+        const cuuint64_t bstr[1] = {static_cast<cuuint64_t>(K) * 2};
+        rc = encode_map(&maps.b[i], a.seg[i].w, 2, bdims, bstr);
+        a.seg[i].tiles = tc_tiles;
+        tc_tiles += (a.seg[i].n + kTN - 1) / kTN;
+    }
+    if (rc) return rc;
+    const dim3 grid(static_cast<unsigned>(tc_tiles), static_cast<unsigned>((M + kTM - 1) / kTM));
+    k_gemm_tc<<<grid, kTcThreads, kTcSmem, stream>>>(maps, a, w.err);
     MR_CUDA_TRY(cudaGetLastError());
     return MR_OK;
 }
@@ -497,9 +742,12 @@ size_t attn_smem(int d) {
 void prefill_release(PrefillWork &w) {
     for (void *p : {static_cast<void *>(w.x), static_cast<void *>(w.planes), static_cast<void *>(w.qkv),
                     static_cast<void *>(w.qh), static_cast<void *>(w.kc), static_cast<void *>(w.vc),
-                    static_cast<void *>(w.gate), static_cast<void *>(w.up), static_cast<void *>(w.logits)})
+                    static_cast<void *>(w.gate), static_cast<void *>(w.up), static_cast<void *>(w.logits),
+                    static_cast<void *>(w.err)})
         if (p) cudaFree(p);
+    const bool tc = w.tcgen05;
     w = PrefillWork{};
+    w.tcgen05 = tc;
 }
 
 int prefill_reserve(const PrefillModel &pm, PrefillWork &w, int tokens, bool all_logits) {
@@ -523,6 +771,7 @@ int prefill_reserve(const PrefillModel &pm, PrefillWork &w, int tokens, bool all
     if (!rc) rc = alloc(reinterpret_cast<void **>(&w.up), sizeof(float) * T * static_cast<size_t>(pm.ffn));
     if (!rc)
         rc = alloc(reinterpret_cast<void **>(&w.logits), sizeof(float) * (all ? T : 1) * static_cast<size_t>(pm.vocab));
+    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.err), sizeof(int));
     if (rc) {
         prefill_release(w);
         return rc;
@@ -532,12 +781,22 @@ int prefill_reserve(const PrefillModel &pm, PrefillWork &w, int tokens, bool all
     return MR_OK;
 }
 
+int prefill_status(const PrefillModel &pm, PrefillWork &w) {
+    int err = 0;
+    MR_CUDA_TRY(cudaMemcpyAsync(&err, w.err, sizeof(int), cudaMemcpyDeviceToHost, pm.stream));
+    MR_CUDA_TRY(cudaStreamSynchronize(pm.stream));
+    if (err) return set_error(MR_ERR_TIMEOUT, "prefill GEMM: a bounded wait gave up");
+    return MR_OK;
+}
+
 int prefill_chunk(const PrefillModel &pm, PrefillWork &w, const int *d_ids, int T, int p0, bool all_logits) {
     MR_REQUIRE(T > 0 && T <= w.tokens && (!all_logits || w.all_logits), "prefill workspace too small");
     cudaStream_t st = pm.stream;
     const int h = pm.hidden, H = pm.heads, d = pm.head_dim, f = pm.ffn, q = H * d;
     const size_t ps = static_cast<size_t>(w.tokens) * w.kmax;  // plane stride
     MR_CUDA_TRY(cudaFuncSetAttribute(k_gemm_bf16x3, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem));
+    MR_CUDA_TRY(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
+    MR_CUDA_TRY(cudaMemsetAsync(w.err, 0, sizeof(int), st));
     MR_CUDA_TRY(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(d)));
     k_embed_rows<<<T, 256, 0, st>>>(d_ids, T, pm.embed, pm.embed_dt, h, w.x);
     MR_CUDA_TRY(cudaGetLastError());
@@ -545,7 +804,7 @@ int prefill_chunk(const PrefillModel &pm, PrefillWork &w, const int *d_ids, int 
         const int KV = L.kv_heads, kv = KV * d, ldqkv = q + 2 * kv;
         // 1. RMSNorm -> q | k | v
         k_rms_planes<<<T, 256, 0, st>>>(w.x, 0, h, L.a_norm, L.a_norm_dt, pm.eps, w.planes, ps, w.kmax);
-        int rc = gemm(st, w.planes, ps, w.kmax, T, h,
+        int rc = gemm(w, st, w.planes, ps, w.kmax, T, h,
                       {GemmSeg{static_cast<const uint16_t *>(L.q), q, 0, 0},
                        GemmSeg{static_cast<const uint16_t *>(L.k), kv, q, 0},
                        GemmSeg{static_cast<const uint16_t *>(L.v), kv, q + kv, 0}},
@@ -570,27 +829,27 @@ int prefill_chunk(const PrefillModel &pm, PrefillWork &w, const int *d_ids, int 
             MR_CUDA_TRY(cudaGetLastError());
         }
         // 4. o projection, x += s * o (model.py:282)
-        rc = gemm(st, w.planes, ps, w.kmax, T, q, {GemmSeg{static_cast<const uint16_t *>(L.o), h, 0, 0}}, w.x, h, true,
+        rc = gemm(w, st, w.planes, ps, w.kmax, T, q, {GemmSeg{static_cast<const uint16_t *>(L.o), h, 0, 0}}, w.x, h, true,
                   pm.residual_scale);
         if (rc) return rc;
         // 5. RMSNorm -> gate | up -> SwiGLU -> down, x += s * down (model.py:87-89, 283)
         k_rms_planes<<<T, 256, 0, st>>>(w.x, 0, h, L.f_norm, L.f_norm_dt, pm.eps, w.planes, ps, w.kmax);
-        rc = gemm(st, w.planes, ps, w.kmax, T, h, {GemmSeg{static_cast<const uint16_t *>(L.gate), f, 0, 0}}, w.gate, f,
+        rc = gemm(w, st, w.planes, ps, w.kmax, T, h, {GemmSeg{static_cast<const uint16_t *>(L.gate), f, 0, 0}}, w.gate, f,
                   false, 0.f);
         if (!rc)
-            rc = gemm(st, w.planes, ps, w.kmax, T, h, {GemmSeg{static_cast<const uint16_t *>(L.up), f, 0, 0}}, w.up, f,
+            rc = gemm(w, st, w.planes, ps, w.kmax, T, h, {GemmSeg{static_cast<const uint16_t *>(L.up), f, 0, 0}}, w.up, f,
                       false, 0.f);
         if (rc) return rc;
         k_swiglu_planes<<<592, 256, 0, st>>>(w.gate, w.up, T, f, w.planes, ps, w.kmax);
         MR_CUDA_TRY(cudaGetLastError());
-        rc = gemm(st, w.planes, ps, w.kmax, T, f, {GemmSeg{static_cast<const uint16_t *>(L.down), h, 0, 0}}, w.x, h,
+        rc = gemm(w, st, w.planes, ps, w.kmax, T, f, {GemmSeg{static_cast<const uint16_t *>(L.down), h, 0, 0}}, w.x, h,
                   true, pm.residual_scale);
         if (rc) return rc;
     }
     // final RMSNorm + lm_head for the rows whose logits are wanted (model.py:285, 307)
     const int r0 = all_logits ? 0 : T - 1, rows = all_logits ? T : 1;
     k_rms_planes<<<rows, 256, 0, st>>>(w.x, r0, h, pm.final_norm, pm.final_norm_dt, pm.eps, w.planes, ps, w.kmax);
-    return gemm(st, w.planes, ps, w.kmax, rows, h, {GemmSeg{static_cast<const uint16_t *>(pm.head), pm.vocab, 0, 0}},
+    return gemm(w, st, w.planes, ps, w.kmax, rows, h, {GemmSeg{static_cast<const uint16_t *>(pm.head), pm.vocab, 0, 0}},
                 w.logits, pm.vocab, false, 0.f);
 }
 

@@ -48,11 +48,16 @@ struct PrefillWork {
     float *kc = nullptr, *vc = nullptr;  // [T][kv_max * d] the chunk's keys / values
     float *gate = nullptr, *up = nullptr;  // [T][ffn]
     float *logits = nullptr;   // [T or 1][vocab]
+    int *err = nullptr;        // a bounded wait of the tcgen05 GEMM gave up
+    bool tcgen05 = true;       // GEMMs on tcgen05 (else mma.sync, kept as the comparison baseline)
 };
 
 // Allocates (or grows) the workspace on the model's stream.
 int prefill_reserve(const PrefillModel &pm, PrefillWork &w, int tokens, bool all_logits);
 void prefill_release(PrefillWork &w);
+
+// Reads back the GEMMs' wait status (synchronises the stream).
+int prefill_status(const PrefillModel &pm, PrefillWork &w);
 
 // Runs T tokens (device ids) at positions p0 .. p0 + T - 1 through every
 // layer, appending their keys and values to the rings, and writes the logits

@@ -92,3 +92,19 @@ def test_batched_prefill_full_size_nano17(backend):
     scale = float(np.abs(ls).max())
     np.testing.assert_allclose(lb, ls, atol=4 * ATOL * max(1.0, scale), rtol=4 * RTOL)
     np.testing.assert_allclose(nb, ns, atol=4 * ATOL * max(1.0, scale), rtol=4 * RTOL)
+
+
+def test_tcgen05_and_mma_sync_gemms_agree(backend):
+    """The prefill's tcgen05 GEMMs against the mma.sync baseline kernel on a
+    full-size nano-1.7 prompt (both sum the same exact BF16 products in FP32)."""
+    config = submodule("synthetic").config_for("nano17")
+    MiracleModel = submodule("model").MiracleModel
+    prompt = submodule("synthetic").prompt_ids(config.vocab_size, 300).tolist()
+    outs = []
+    for mode in (1, 2):
+        model = MiracleModel.synthetic(config, stored="BF16", backend=backend, context_length=1024)
+        submodule("_native").call("mr_model_set_batched_prefill", model._handle, mode, None)
+        outs.append(model.prefill(prompt, return_all=True))
+        del model
+    scale = float(np.abs(outs[1]).max())
+    np.testing.assert_allclose(outs[0], outs[1], atol=2 * ATOL * max(1.0, scale), rtol=2 * RTOL)
