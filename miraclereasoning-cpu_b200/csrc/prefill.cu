@@ -85,15 +85,14 @@ __global__ void k_rms_planes(const float *x, int r0, int h, const void *gain, in
     }
 }
 
-// planes[t] = split(silu(gate) * up) (kernels.cl:46-50).
-__global__ void k_swiglu_planes(const float *g, const float *u, int T, int f, uint16_t *planes, size_t plane_stride,
-                                int ld) {
+// planes[t] = split(silu(gate) * up) (kernels.cl:46-50); gu[t] = gate row | up row.
+__global__ void k_swiglu_planes(const float *gu, int T, int f, uint16_t *planes, size_t plane_stride, int ld) {
     const size_t n = static_cast<size_t>(T) * f;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const size_t t = i / f, j = i - t * f;
-        const float gv = g[i];
-        put_planes(planes, plane_stride, t * ld + j, __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), u[i]));
+        const float gv = gu[t * 2 * f + j], uv = gu[t * 2 * f + f + j];
+        put_planes(planes, plane_stride, t * ld + j, __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv));
     }
 }
 
@@ -463,18 +462,20 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_bf16x3(GemmArgs args) {
 }
 
 // ---- GEMM on the 5th-generation tensor cores (tcgen05) ----------------------------------------
-// Same product as k_gemm_bf16x3, one CTA per 128-token x 128-feature tile:
-// warp 0 lane 0 streams K tiles of 64 (three X planes + the W tile, 64 KB a
+// Same product as k_gemm_bf16x3, one CTA per 128-token x 64-feature tile
+// (64 rather than 128 features: a prompt chunk has few 128-token tiles, and
+// the narrower tile doubles the CTAs that share the GPU):
+// warp 0 lane 0 streams K tiles of 64 (three X planes + the W tile, 56 KB a
 // stage, 128-byte swizzle) by TMA into a 3-stage ring; warp 1 lane 0 issues
-// tcgen05.mma (M 128, N 128, K 16, BF16 -> FP32) into two TMEM accumulators
+// tcgen05.mma (M 128, N 64, K 16, BF16 -> FP32) into two TMEM accumulators
 // (the leading part, and the two small parts: summed apart as in
 // k_gemm_bf16x3) and hands each stage back with tcgen05.commit; warps 2-5
 // read the accumulators (tcgen05.ld, one TMEM lane = one token row per
 // thread) and apply the epilogue.  Every wait is bounded (kTcWaitNs): a wait
 // that gives up sets *err and the CTA winds down.
-constexpr int kTM = 128, kTN = 128, kTK = 64, kTStages = 3, kTcThreads = 192;
-constexpr uint32_t kTileBytes = kTM * kTK * 2;                       // 16 KB: one 128 x 64 BF16 tile
-constexpr uint32_t kTStageBytes = 4 * kTileBytes;                    // three X planes + W
+constexpr int kTM = 128, kTN = 64, kTK = 64, kTStages = 3, kTcThreads = 192;
+constexpr uint32_t kTileBytes = kTM * kTK * 2;                       // 16 KB: one 128 x 64 BF16 X tile
+constexpr uint32_t kTStageBytes = 3 * kTileBytes + kTN * kTK * 2;    // three X planes + the 64 x 64 W tile
 constexpr size_t kTcSmem = 1024 + kTStages * kTStageBytes + 256;     // alignment slack, tiles, barriers
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
@@ -520,7 +521,7 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
     return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
            (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
 }
-// kind::f16 instruction descriptor: D F32, A and B BF16, both K-major, N = 128, M = 128
+// kind::f16 instruction descriptor: D F32, A and B BF16, both K-major, N = kTN, M = 128
 constexpr uint32_t kTcIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kTN >> 3) << 17) |
                               (static_cast<uint32_t>(kTM >> 4) << 24);
 
@@ -545,8 +546,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(accf)) : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) {  // 256 TMEM columns: accumulator of the leading part (0..127) and of the small parts (128..255)
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(saddr(tmem_slot))
+    if (warp == 1) {  // 128 TMEM columns: accumulator of the leading part (0..63) and of the small parts (64..127)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(saddr(tmem_slot))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -657,7 +658,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem) : "memory");
     }
 }
 
@@ -673,11 +674,12 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// BF16 tensor map, box 64 (K) x 128 rows, 128-byte swizzle; rows past the extent read as zeros.
-int encode_map(CUtensorMap *map, const void *base, int rank, const cuuint64_t *dims, const cuuint64_t *strides) {
+// BF16 tensor map, box 64 (K) x `rows`, 128-byte swizzle; rows past the extent read as zeros.
+int encode_map(CUtensorMap *map, const void *base, int rank, const cuuint64_t *dims, const cuuint64_t *strides,
+               int rows) {
     auto enc = tensor_map_encoder();
     if (!enc) return set_error(MR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTK), 128u, 1u}, estride[3] = {1u, 1u, 1u};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTK), static_cast<cuuint32_t>(rows), 1u}, estride[3] = {1u, 1u, 1u};
     const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void *>(base),
                            dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -716,12 +718,12 @@ int gemm(const PrefillWork &w, cudaStream_t stream, const uint16_t *planes, size
     TcMaps maps{};
     const cuuint64_t adims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M), 3};
     const cuuint64_t astr[2] = {static_cast<cuuint64_t>(lda) * 2, static_cast<cuuint64_t>(plane_stride) * 2};
-    int rc = encode_map(&maps.a, planes, 3, adims, astr);
+    int rc = encode_map(&maps.a, planes, 3, adims, astr, kTM);
     int tc_tiles = 0;
     for (int i = 0; i < a.nseg && !rc; ++i) {
         const cuuint64_t bdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(a.seg[i].n)};
         const cuuint64_t bstr[1] = {static_cast<cuuint64_t>(K) * 2};
-        rc = encode_map(&maps.b[i], a.seg[i].w, 2, bdims, bstr);
+        rc = encode_map(&maps.b[i], a.seg[i].w, 2, bdims, bstr, kTN);
         a.seg[i].tiles = tc_tiles;
         tc_tiles += (a.seg[i].n + kTN - 1) / kTN;
     }
@@ -742,7 +744,7 @@ size_t attn_smem(int d) {
 void prefill_release(PrefillWork &w) {
     for (void *p : {static_cast<void *>(w.x), static_cast<void *>(w.planes), static_cast<void *>(w.qkv),
                     static_cast<void *>(w.qh), static_cast<void *>(w.kc), static_cast<void *>(w.vc),
-                    static_cast<void *>(w.gate), static_cast<void *>(w.up), static_cast<void *>(w.logits),
+                    static_cast<void *>(w.gu), static_cast<void *>(w.logits),
                     static_cast<void *>(w.err)})
         if (p) cudaFree(p);
     const bool tc = w.tcgen05;
@@ -767,8 +769,7 @@ int prefill_reserve(const PrefillModel &pm, PrefillWork &w, int tokens, bool all
     if (!rc) rc = alloc(reinterpret_cast<void **>(&w.qh), sizeof(float) * T * static_cast<size_t>(q));
     if (!rc) rc = alloc(reinterpret_cast<void **>(&w.kc), sizeof(float) * T * static_cast<size_t>(kv));
     if (!rc) rc = alloc(reinterpret_cast<void **>(&w.vc), sizeof(float) * T * static_cast<size_t>(kv));
-    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.gate), sizeof(float) * T * static_cast<size_t>(pm.ffn));
-    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.up), sizeof(float) * T * static_cast<size_t>(pm.ffn));
+    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.gu), sizeof(float) * T * 2 * static_cast<size_t>(pm.ffn));
     if (!rc)
         rc = alloc(reinterpret_cast<void **>(&w.logits), sizeof(float) * (all ? T : 1) * static_cast<size_t>(pm.vocab));
     if (!rc) rc = alloc(reinterpret_cast<void **>(&w.err), sizeof(int));
@@ -834,13 +835,12 @@ int prefill_chunk(const PrefillModel &pm, PrefillWork &w, const int *d_ids, int 
         if (rc) return rc;
         // 5. RMSNorm -> gate | up -> SwiGLU -> down, x += s * down (model.py:87-89, 283)
         k_rms_planes<<<T, 256, 0, st>>>(w.x, 0, h, L.f_norm, L.f_norm_dt, pm.eps, w.planes, ps, w.kmax);
-        rc = gemm(w, st, w.planes, ps, w.kmax, T, h, {GemmSeg{static_cast<const uint16_t *>(L.gate), f, 0, 0}}, w.gate, f,
-                  false, 0.f);
-        if (!rc)
-            rc = gemm(w, st, w.planes, ps, w.kmax, T, h, {GemmSeg{static_cast<const uint16_t *>(L.up), f, 0, 0}}, w.up, f,
-                      false, 0.f);
+        rc = gemm(w, st, w.planes, ps, w.kmax, T, h,
+                  {GemmSeg{static_cast<const uint16_t *>(L.gate), f, 0, 0},
+                   GemmSeg{static_cast<const uint16_t *>(L.up), f, f, 0}},
+                  w.gu, 2 * f, false, 0.f);
         if (rc) return rc;
-        k_swiglu_planes<<<592, 256, 0, st>>>(w.gate, w.up, T, f, w.planes, ps, w.kmax);
+        k_swiglu_planes<<<592, 256, 0, st>>>(w.gu, T, f, w.planes, ps, w.kmax);
         MR_CUDA_TRY(cudaGetLastError());
         rc = gemm(w, st, w.planes, ps, w.kmax, T, f, {GemmSeg{static_cast<const uint16_t *>(L.down), h, 0, 0}}, w.x, h,
                   true, pm.residual_scale);

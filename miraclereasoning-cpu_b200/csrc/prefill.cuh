@@ -46,7 +46,7 @@ struct PrefillWork {
     float *qkv = nullptr;      // [T][q + 2 kv_max]
     float *qh = nullptr;       // [T][heads * d] normalised, rotated queries
     float *kc = nullptr, *vc = nullptr;  // [T][kv_max * d] the chunk's keys / values
-    float *gate = nullptr, *up = nullptr;  // [T][ffn]
+    float *gu = nullptr;       // [T][2 ffn]: gate row | up row
     float *logits = nullptr;   // [T or 1][vocab]
     int *err = nullptr;        // a bounded wait of the tcgen05 GEMM gave up
     bool tcgen05 = true;       // GEMMs on tcgen05 (else mma.sync, kept as the comparison baseline)
