@@ -649,7 +649,8 @@ void setup_prefill(mr_model *m) {
     const mr_model_config &c = m->cfg;
     const int d = c.head_dim, q = c.query_heads * d;
     m->prefill_ok = false;
-    if (c.hidden_size % 8 || q % 8 || c.ffn_dim % 8 || d % 4) return;
+    const int gq_max = c.query_heads / *std::min_element(m->layer_kvh.begin(), m->layer_kvh.end());
+    if (c.hidden_size % 8 || q % 8 || c.ffn_dim % 8 || d % 4 || gq_max > 32) return;
     auto bf16 = [&](const std::string &name) {
         const TensorSlot *t = tensor(m, name);
         return t && t->dtype == MR_DTYPE_BF16 ? t->ptr : nullptr;

@@ -152,18 +152,26 @@ __global__ void k_qk_rope(const float *qkv, int T, int p0, int H, int KV, int d,
 
 // ---- causal attention over the ring and the chunk ------------------------------------------
 constexpr int kAttnThreads = 256;
-constexpr int kAttnRows = 64;  // query rows per CTA (tokens x group heads)
+constexpr int kAttnRows = 32;  // query rows per CTA (tokens x group heads)
 constexpr int kKT = 32;        // keys per tile (one per lane in the softmax step)
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src)
+                 : "memory");
+}
 
 // CTA = (block of QT tokens, KV head g), rows r = (token, group head).  Token t
 // at position p = p0 + t attends to positions (p - capacity, p]: those below p0
 // from the ring (slot = position % capacity), the rest from the chunk (model.py
 // :95-116; the ring holds min(count, capacity) keys).  Online softmax over key
-// tiles.  Register blocking keeps shared-memory traffic below the arithmetic:
-// a thread scores 2 rows x 4 keys from float4 loads, and accumulates a
-// 4-row x 4-dim block of the output (two blocks for head dims above 64) in
-// registers across the tiles.  The output rows go out as BF16x3 planes of
-// the o projection's input.  Head dims are multiples of 4.
+// tiles, double-buffered (the next tile loads with cp.async while the current
+// one is used).  Register blocking keeps shared-memory traffic below the
+// arithmetic: a thread scores 1 row x 4 keys (strided by 8) from float4 loads and
+// accumulates 2-row x 4-dim output blocks (two for head dims above 64) in
+// registers across the tiles; each warp updates the softmax state of its four
+// rows together.  The output rows go out as BF16x3 planes of the o
+// projection's input.  Head dims are multiples of 4.
 __global__ void __launch_bounds__(kAttnThreads) k_attention(const float *qh, const float *kc, const float *vc,
                                                             const float *k_cache, const float *v_cache, int T, int p0,
                                                             int H, int KV, int d, int cap, int QT, uint16_t *planes,
@@ -172,14 +180,37 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const float *qh, con
     const int gq = H / KV, g = blockIdx.y, t0 = blockIdx.x * QT;
     const int nt = min(QT, T - t0), R = nt * gq;
     const int ks = d + 4;
-    float *q = sm;                       // [kAttnRows][d + 4]
-    float *kt = q + kAttnRows * ks;      // [kKT][d + 4]
-    float *vt = kt + kKT * ks;           // [kKT][d]
-    float *s = vt + kKT * d;             // [kAttnRows][kKT + 1]
+    float *q = sm;                         // [kAttnRows][d + 4]
+    float *kt = q + kAttnRows * ks;        // [2][kKT][d + 4]
+    float *vt = kt + 2 * kKT * ks;         // [2][kKT][d]
+    float *s = vt + 2 * kKT * d;           // [kAttnRows][kKT + 1]
     float *mrow = s + kAttnRows * (kKT + 1);
     float *lrow = mrow + kAttnRows;
     float *corr = lrow + kAttnRows;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = kAttnThreads / 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int dq = d / 4;
+    const int p_first = p0 + t0, p_last = p0 + t0 + nt - 1;
+    const int lo = max(0, p_first - cap + 1);
+    auto issue = [&](int kb, int buf) {  // keys kb .. kb + 31 into buffer buf (rows past the last key: not loaded)
+        const int nk = min(kKT, p_last + 1 - kb);
+        for (int e = tid; e < nk * dq; e += kAttnThreads) {
+            const int kk = e / dq, j = (e - kk * dq) * 4, pos = kb + kk;
+            const float *ksrc, *vsrc;
+            if (pos < p0) {
+                const size_t row = (static_cast<size_t>(g) * cap + pos % cap) * d + j;
+                ksrc = k_cache + row;
+                vsrc = v_cache + row;
+            } else {
+                const size_t row = (static_cast<size_t>(pos - p0) * KV + g) * d + j;
+                ksrc = kc + row;
+                vsrc = vc + row;
+            }
+            cp_async16(kt + (buf * kKT + kk) * ks + j, ksrc);
+            cp_async16(vt + (buf * kKT + kk) * d + j, vsrc);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    issue(lo, 0);
     for (int e = tid; e < kAttnRows * d; e += kAttnThreads) {
         const int r = e / d, j = e - r * d, tt = r / gq, i = r - tt * gq;
         q[r * ks + j] = r < R ? qh[(static_cast<size_t>(t0 + tt) * H + g * gq + i) * d + j] : 0.f;
@@ -188,117 +219,119 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const float *qh, con
         mrow[r] = -INFINITY;
         lrow[r] = 0.f;
     }
-    // score block of this thread: rows sr, sr + 1; keys sk .. sk + 3
-    const int sr = (tid >> 3) * 2, sk = (tid & 7) * 4;
-    // output blocks: rows 4 * (b / (d / 4)) .. + 3, dims 4 * (b % (d / 4)) .. + 3, b = tid, tid + 256
-    const int dq = d / 4, nblk = (kAttnRows / 4) * dq;
-    float acc[2][16];
+    // score block: row sr, keys sk, sk + 8, sk + 16, sk + 24 (the eight key threads of a
+    // row read eight consecutive key rows: distinct banks with the d + 4 row stride)
+    const int sr = tid >> 3, sk = tid & 7;
+    const int nblk = (kAttnRows / 2) * dq;               // output blocks: 2 rows x 4 dims
+    float acc[2][8];
 #pragma unroll
     for (int b = 0; b < 2; ++b)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) acc[b][e] = 0.f;
+        for (int e = 0; e < 8; ++e) acc[b][e] = 0.f;
     const float sqrt_d = __fsqrt_rn(static_cast<float>(d));
-    const int p_first = p0 + t0, p_last = p0 + t0 + nt - 1;
-    const int lo = max(0, p_first - cap + 1);
-    for (int kb = lo; kb <= p_last; kb += kKT) {
+    int buf = 0;
+    for (int kb = lo; kb <= p_last; kb += kKT, buf ^= 1) {
         const int nk = min(kKT, p_last + 1 - kb);
-        __syncthreads();  // the previous tile's readers are done
-        for (int e = tid; e < kKT * dq; e += kAttnThreads) {
-            const int kk = e / dq, j = (e - kk * dq) * 4, pos = kb + kk;
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (kk < nk) {
-                const float *ksrc, *vsrc;
-                if (pos < p0) {
-                    const size_t row = (static_cast<size_t>(g) * cap + pos % cap) * d + j;
-                    ksrc = k_cache + row;
-                    vsrc = v_cache + row;
-                } else {
-                    const size_t row = (static_cast<size_t>(pos - p0) * KV + g) * d + j;
-                    ksrc = kc + row;
-                    vsrc = vc + row;
-                }
-                kv = *reinterpret_cast<const float4 *>(ksrc);
-                vv = *reinterpret_cast<const float4 *>(vsrc);
-            }
-            *reinterpret_cast<float4 *>(kt + kk * ks + j) = kv;
-            *reinterpret_cast<float4 *>(vt + kk * d + j) = vv;
+        if (kb + kKT <= p_last) {
+            issue(kb + kKT, buf ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
-        __syncthreads();
-        {  // scores: 2 rows x 4 keys per thread
-            float a[2][4];
-#pragma unroll
-            for (int x = 0; x < 2; ++x)
-#pragma unroll
-                for (int y = 0; y < 4; ++y) a[x][y] = 0.f;
+        __syncthreads();  // tile buf (and, first time, q and the softmax state) visible
+        const float *ktb = kt + buf * kKT * ks, *vtb = vt + buf * kKT * d;
+        {  // scores: 1 row x 4 keys per thread
+            float a[4] = {0.f, 0.f, 0.f, 0.f};
             for (int j = 0; j < d; j += 4) {
                 const float4 q0 = *reinterpret_cast<const float4 *>(q + sr * ks + j);
-                const float4 q1 = *reinterpret_cast<const float4 *>(q + (sr + 1) * ks + j);
 #pragma unroll
                 for (int y = 0; y < 4; ++y) {
-                    const float4 kv = *reinterpret_cast<const float4 *>(kt + (sk + y) * ks + j);
-                    a[0][y] = fmaf(q0.x, kv.x, fmaf(q0.y, kv.y, fmaf(q0.z, kv.z, fmaf(q0.w, kv.w, a[0][y]))));
-                    a[1][y] = fmaf(q1.x, kv.x, fmaf(q1.y, kv.y, fmaf(q1.z, kv.z, fmaf(q1.w, kv.w, a[1][y]))));
+                    const float4 kv = *reinterpret_cast<const float4 *>(ktb + (sk + 8 * y) * ks + j);
+                    a[y] = fmaf(q0.x, kv.x, fmaf(q0.y, kv.y, fmaf(q0.z, kv.z, fmaf(q0.w, kv.w, a[y]))));
                 }
             }
+            const int p = p_first + sr / gq;
 #pragma unroll
-            for (int x = 0; x < 2; ++x)
-#pragma unroll
-                for (int y = 0; y < 4; ++y) {
-                    const int r = sr + x, kk = sk + y, pos = kb + kk, p = p_first + r / gq;
-                    const bool live = r < R && kk < nk && pos <= p && pos > p - cap;
-                    s[r * (kKT + 1) + kk] = live ? __fdiv_rn(a[x][y], sqrt_d) : -INFINITY;  // kernels.cl:72
-                }
-        }
-        __syncthreads();
-        for (int r = warp; r < R; r += nw) {  // online softmax, one key per lane
-            const float v = s[r * (kKT + 1) + lane];
-            const float mt = warp_max(v);
-            const float m_old = mrow[r], m_new = fmaxf(m_old, mt);
-            const float pr = (v == -INFINITY) ? 0.f : expf(v - m_new);
-            const float sum = warp_sum(pr);
-            s[r * (kKT + 1) + lane] = pr;
-            if (lane == 0) {
-                const float cf = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-                corr[r] = cf;
-                lrow[r] = fmaf(lrow[r], cf, sum);
-                mrow[r] = m_new;
+            for (int y = 0; y < 4; ++y) {
+                const int kk = sk + 8 * y, pos = kb + kk;
+                const bool live = sr < R && kk < nk && pos <= p && pos > p - cap;
+                s[sr * (kKT + 1) + kk] = live ? __fdiv_rn(a[y], sqrt_d) : -INFINITY;  // kernels.cl:72
             }
         }
         __syncthreads();
-#pragma unroll
-        for (int b = 0; b < 2; ++b) {  // value mix: 4 rows x 4 dims per block
-            const int blk = tid + b * kAttnThreads;
-            if (blk >= nblk) continue;
-            const int r0 = (blk / dq) * 4, j0 = (blk % dq) * 4;
-            if (r0 >= R) continue;
-            float *ac = acc[b];
+        {  // online softmax: warp w updates rows w, w + 8, w + 16, w + 24 together, one key per lane
+            float v[4], mt[4], pr[4], sum[4];
 #pragma unroll
             for (int x = 0; x < 4; ++x) {
-                const float cf = corr[r0 + x];
-#pragma unroll
-                for (int y = 0; y < 4; ++y) ac[x * 4 + y] *= cf;
+                v[x] = s[(warp + 8 * x) * (kKT + 1) + lane];
+                mt[x] = v[x];
             }
-            for (int kk = 0; kk < nk; ++kk) {
-                const float4 vv = *reinterpret_cast<const float4 *>(vt + kk * d + j0);
 #pragma unroll
-                for (int x = 0; x < 4; ++x) {
-                    const float pr = s[(r0 + x) * (kKT + 1) + kk];
-                    ac[x * 4 + 0] = fmaf(pr, vv.x, ac[x * 4 + 0]);
-                    ac[x * 4 + 1] = fmaf(pr, vv.y, ac[x * 4 + 1]);
-                    ac[x * 4 + 2] = fmaf(pr, vv.z, ac[x * 4 + 2]);
-                    ac[x * 4 + 3] = fmaf(pr, vv.w, ac[x * 4 + 3]);
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int x = 0; x < 4; ++x) mt[x] = fmaxf(mt[x], __shfl_xor_sync(0xffffffffu, mt[x], o));
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+                const int r = warp + 8 * x;
+                const float m_new = fmaxf(mrow[r], mt[x]);
+                pr[x] = (v[x] == -INFINITY) ? 0.f : expf(v[x] - m_new);
+                sum[x] = pr[x];
+                mt[x] = m_new;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int x = 0; x < 4; ++x) sum[x] += __shfl_xor_sync(0xffffffffu, sum[x], o);
+            __syncwarp();
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+                const int r = warp + 8 * x;
+                s[r * (kKT + 1) + lane] = pr[x];
+                if (lane == 0) {
+                    const float m_old = mrow[r];
+                    const float cf = (m_old == -INFINITY) ? 0.f : expf(m_old - mt[x]);
+                    corr[r] = cf;
+                    lrow[r] = fmaf(lrow[r], cf, sum[x]);
+                    mrow[r] = mt[x];
                 }
             }
         }
+        __syncthreads();
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {  // value mix: 2 rows x 4 dims per block
+            const int blk = tid + b * kAttnThreads;
+            if (blk >= nblk) continue;
+            const int r0 = (blk / dq) * 2, j0 = (blk % dq) * 4;
+            if (r0 >= R) continue;
+            const float c0 = corr[r0], c1 = corr[r0 + 1];
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+                acc[b][y] *= c0;
+                acc[b][4 + y] *= c1;
+            }
+            const float *s0 = s + r0 * (kKT + 1), *s1 = s0 + (kKT + 1);
+            for (int kk = 0; kk < nk; ++kk) {
+                const float4 vv = *reinterpret_cast<const float4 *>(vtb + kk * d + j0);
+                const float p0v = s0[kk], p1v = s1[kk];
+                acc[b][0] = fmaf(p0v, vv.x, acc[b][0]);
+                acc[b][1] = fmaf(p0v, vv.y, acc[b][1]);
+                acc[b][2] = fmaf(p0v, vv.z, acc[b][2]);
+                acc[b][3] = fmaf(p0v, vv.w, acc[b][3]);
+                acc[b][4] = fmaf(p1v, vv.x, acc[b][4]);
+                acc[b][5] = fmaf(p1v, vv.y, acc[b][5]);
+                acc[b][6] = fmaf(p1v, vv.z, acc[b][6]);
+                acc[b][7] = fmaf(p1v, vv.w, acc[b][7]);
+            }
+        }
+        __syncthreads();  // every reader of buffer buf is done before it is refilled
     }
-    __syncthreads();
 #pragma unroll
     for (int b = 0; b < 2; ++b) {
         const int blk = tid + b * kAttnThreads;
         if (blk >= nblk) continue;
-        const int r0 = (blk / dq) * 4, j0 = (blk % dq) * 4;
+        const int r0 = (blk / dq) * 2, j0 = (blk % dq) * 4;
 #pragma unroll
-        for (int x = 0; x < 4; ++x) {
+        for (int x = 0; x < 2; ++x) {
             const int r = r0 + x;
             if (r >= R) continue;
             const int tt = r / gq, i = r - tt * gq;
@@ -735,8 +768,8 @@ int gemm(const PrefillWork &w, cudaStream_t stream, const uint16_t *planes, size
 }
 
 size_t attn_smem(int d) {
-    return sizeof(float) * (static_cast<size_t>(kAttnRows) * (d + 4) + kKT * (d + 4) + static_cast<size_t>(kKT) * d +
-                            kAttnRows * (kKT + 1) + 3 * kAttnRows);
+    return sizeof(float) * (static_cast<size_t>(kAttnRows) * (d + 4) + 2 * kKT * (d + 4) +
+                            2 * static_cast<size_t>(kKT) * d + kAttnRows * (kKT + 1) + 3 * kAttnRows);
 }
 
 }  // namespace
