@@ -495,21 +495,24 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_bf16x3(GemmArgs args) {
 }
 
 // ---- GEMM on the 5th-generation tensor cores (tcgen05) ----------------------------------------
-// Same product as k_gemm_bf16x3, one CTA per 128-token x 64-feature tile
-// (64 rather than 128 features: a prompt chunk has few 128-token tiles, and
-// the narrower tile doubles the CTAs that share the GPU):
-// warp 0 lane 0 streams K tiles of 64 (three X planes + the W tile, 56 KB a
-// stage, 128-byte swizzle) by TMA into a 3-stage ring; warp 1 lane 0 issues
-// tcgen05.mma (M 128, N 64, K 16, BF16 -> FP32) into two TMEM accumulators
+// Same product as k_gemm_bf16x3, one CTA per 128-token x BN-feature tile
+// (BN 128 where that still gives a wave of CTAs, else 64: a prompt chunk has
+// few 128-token tiles, and the narrower tile doubles the CTAs; the wider one
+// halves the re-reads of the X planes):
+// warp 0 lane 0 streams K tiles of 64 (three X planes + the W tile, 56 or 64 KB
+// a stage, 128-byte swizzle) by TMA into a 3-stage ring; warp 1 lane 0 issues
+// tcgen05.mma (M 128, N BN, K 16, BF16 -> FP32) into two TMEM accumulators
 // (the leading part, and the two small parts: summed apart as in
 // k_gemm_bf16x3) and hands each stage back with tcgen05.commit; warps 2-5
 // read the accumulators (tcgen05.ld, one TMEM lane = one token row per
 // thread) and apply the epilogue.  Every wait is bounded (kTcWaitNs): a wait
 // that gives up sets *err and the CTA winds down.
-constexpr int kTM = 128, kTN = 64, kTK = 64, kTStages = 3, kTcThreads = 192;
-constexpr uint32_t kTileBytes = kTM * kTK * 2;                       // 16 KB: one 128 x 64 BF16 X tile
-constexpr uint32_t kTStageBytes = 3 * kTileBytes + kTN * kTK * 2;    // three X planes + the 64 x 64 W tile
-constexpr size_t kTcSmem = 1024 + kTStages * kTStageBytes + 256;     // alignment slack, tiles, barriers
+constexpr int kTM = 128, kTK = 64, kTStages = 3, kTcThreads = 192;
+constexpr uint32_t kTileBytes = kTM * kTK * 2;  // 16 KB: one 128 x 64 BF16 X tile
+template <int BN>
+constexpr uint32_t tc_stage_bytes() { return 3 * kTileBytes + BN * kTK * 2; }  // three X planes + the W tile
+template <int BN>
+constexpr size_t tc_smem() { return 1024 + kTStages * tc_stage_bytes<BN>() + 256; }  // alignment slack, tiles, barriers
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
 struct TcMaps {
@@ -554,12 +557,19 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
     return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
            (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
 }
-// kind::f16 instruction descriptor: D F32, A and B BF16, both K-major, N = kTN, M = 128
-constexpr uint32_t kTcIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kTN >> 3) << 17) |
-                              (static_cast<uint32_t>(kTM >> 4) << 24);
+// kind::f16 instruction descriptor: D F32, A and B BF16, both K-major, N = BN, M = 128
+template <int BN>
+constexpr uint32_t tc_idesc() {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+           (static_cast<uint32_t>(kTM >> 4) << 24);
+}
 
+template <int BN>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ TcMaps maps, GemmArgs args,
                                                            int *err) {
+    constexpr uint32_t kTStageBytes = tc_stage_bytes<BN>();
+    constexpr int kTN = BN;
+    constexpr uint32_t kTcols = 2 * BN;  // TMEM columns: the two accumulators
     extern __shared__ uint8_t tc_raw[];
     uint8_t *tiles = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(tiles + kTStages * kTStageBytes);
@@ -579,8 +589,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(accf)) : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) {  // 128 TMEM columns: accumulator of the leading part (0..63) and of the small parts (64..127)
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(saddr(tmem_slot))
+    if (warp == 1) {  // accumulator of the leading part (columns 0..BN-1) and of the small parts (BN..2BN-1)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                     "n"(kTcols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -637,7 +648,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
                     asm volatile(
                         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d),
-                        "l"(ad), "l"(bd), "r"(kTcIdesc), "r"(accumulate)
+                        "l"(ad), "l"(bd), "r"(tc_idesc<BN>()), "r"(accumulate)
                         : "memory");
                 }
             }
@@ -691,7 +702,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kTcols) : "memory");
     }
 }
 
@@ -752,17 +763,23 @@ int gemm(const PrefillWork &w, cudaStream_t stream, const uint16_t *planes, size
     const cuuint64_t adims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M), 3};
     const cuuint64_t astr[2] = {static_cast<cuuint64_t>(lda) * 2, static_cast<cuuint64_t>(plane_stride) * 2};
     int rc = encode_map(&maps.a, planes, 3, adims, astr, kTM);
+    // 128-feature tiles when they still fill a wave of SMs, else 64
+    const int mtiles = (M + kTM - 1) / kTM;
+    int wide = 0;
+    for (int i = 0; i < a.nseg; ++i) wide += (a.seg[i].n + 127) / 128;
+    const int BN = wide * mtiles >= 148 ? 128 : 64;
     int tc_tiles = 0;
     for (int i = 0; i < a.nseg && !rc; ++i) {
         const cuuint64_t bdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(a.seg[i].n)};
         const cuuint64_t bstr[1] = {static_cast<cuuint64_t>(K) * 2};
-        rc = encode_map(&maps.b[i], a.seg[i].w, 2, bdims, bstr, kTN);
+        rc = encode_map(&maps.b[i], a.seg[i].w, 2, bdims, bstr, BN);
         a.seg[i].tiles = tc_tiles;
-        tc_tiles += (a.seg[i].n + kTN - 1) / kTN;
+        tc_tiles += (a.seg[i].n + BN - 1) / BN;
     }
     if (rc) return rc;
-    const dim3 grid(static_cast<unsigned>(tc_tiles), static_cast<unsigned>((M + kTM - 1) / kTM));
-    k_gemm_tc<<<grid, kTcThreads, kTcSmem, stream>>>(maps, a, w.err);
+    const dim3 grid(static_cast<unsigned>(tc_tiles), static_cast<unsigned>(mtiles));
+    if (BN == 128) k_gemm_tc<128><<<grid, kTcThreads, tc_smem<128>(), stream>>>(maps, a, w.err);
+    else k_gemm_tc<64><<<grid, kTcThreads, tc_smem<64>(), stream>>>(maps, a, w.err);
     MR_CUDA_TRY(cudaGetLastError());
     return MR_OK;
 }
@@ -829,7 +846,8 @@ int prefill_chunk(const PrefillModel &pm, PrefillWork &w, const int *d_ids, int 
     const int h = pm.hidden, H = pm.heads, d = pm.head_dim, f = pm.ffn, q = H * d;
     const size_t ps = static_cast<size_t>(w.tokens) * w.kmax;  // plane stride
     MR_CUDA_TRY(cudaFuncSetAttribute(k_gemm_bf16x3, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem));
-    MR_CUDA_TRY(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
+    MR_CUDA_TRY(cudaFuncSetAttribute(k_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc_smem<64>()));
+    MR_CUDA_TRY(cudaFuncSetAttribute(k_gemm_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc_smem<128>()));
     MR_CUDA_TRY(cudaMemsetAsync(w.err, 0, sizeof(int), st));
     MR_CUDA_TRY(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(d)));
     k_embed_rows<<<T, 256, 0, st>>>(d_ids, T, pm.embed, pm.embed_dt, h, w.x);
