@@ -500,19 +500,21 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_bf16x3(GemmArgs args) {
 // few 128-token tiles, and the narrower tile doubles the CTAs; the wider one
 // halves the re-reads of the X planes):
 // warp 0 lane 0 streams K tiles of 64 (three X planes + the W tile, 56 or 64 KB
-// a stage, 128-byte swizzle) by TMA into a 3-stage ring; warp 1 lane 0 issues
+// a stage, 128-byte swizzle) by TMA into a 3- or 4-stage ring; warp 1 lane 0 issues
 // tcgen05.mma (M 128, N BN, K 16, BF16 -> FP32) into two TMEM accumulators
 // (the leading part, and the two small parts: summed apart as in
 // k_gemm_bf16x3) and hands each stage back with tcgen05.commit; warps 2-5
 // read the accumulators (tcgen05.ld, one TMEM lane = one token row per
 // thread) and apply the epilogue.  Every wait is bounded (kTcWaitNs): a wait
 // that gives up sets *err and the CTA winds down.
-constexpr int kTM = 128, kTK = 64, kTStages = 3, kTcThreads = 192;
+constexpr int kTM = 128, kTK = 64, kTcThreads = 192;
 constexpr uint32_t kTileBytes = kTM * kTK * 2;  // 16 KB: one 128 x 64 BF16 X tile
 template <int BN>
 constexpr uint32_t tc_stage_bytes() { return 3 * kTileBytes + BN * kTK * 2; }  // three X planes + the W tile
 template <int BN>
-constexpr size_t tc_smem() { return 1024 + kTStages * tc_stage_bytes<BN>() + 256; }  // alignment slack, tiles, barriers
+constexpr int tc_stages() { return BN == 64 ? 4 : 3; }  // as many 56 / 64 KB stages as shared memory holds
+template <int BN>
+constexpr size_t tc_smem() { return 1024 + tc_stages<BN>() * tc_stage_bytes<BN>() + 256; }  // slack, tiles, barriers
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
 struct TcMaps {
@@ -568,6 +570,7 @@ template <int BN>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ TcMaps maps, GemmArgs args,
                                                            int *err) {
     constexpr uint32_t kTStageBytes = tc_stage_bytes<BN>();
+    constexpr int kTStages = tc_stages<BN>();
     constexpr int kTN = BN;
     constexpr uint32_t kTcols = 2 * BN;  // TMEM columns: the two accumulators
     extern __shared__ uint8_t tc_raw[];
