@@ -302,6 +302,28 @@ def run_profile_case(args):
     return 0
 
 
+def run_profile_prefill(args):
+    """Prefill of the benchmark prompt, repeated, for ncu captures of the
+    batched prefill kernels; prints the wall time of each (not a bench value)."""
+    syn = _pkg("synthetic")
+    config = syn.config_for(args.config)
+    context, prompt_len, _ = syn.WORKLOADS[args.config]
+    backend = _pkg("backend").CUDABackend(device_index=int(os.environ.get("LOCAL_RANK", "0")))
+    model = _pkg("model").MiracleModel.synthetic(config, stored=syn.STORED_DTYPE[args.config], backend=backend,
+                                                 context_length=context)
+    prompt = syn.prompt_ids(config.vocab_size, prompt_len, seed=1)
+    times = []
+    for _ in range(args.profile_prefill):
+        model.reset()
+        backend.finish()
+        t0 = time.perf_counter()
+        model.prefill(prompt)
+        backend.finish()
+        times.append(round((time.perf_counter() - t0) * 1e3, 3))
+    print(json.dumps({"profile_prefill": args.config, "prompt": prompt_len, "ms": times}))
+    return 0
+
+
 def run_trace(args, steps=8):
     """Per-phase timing of decode steps from the kernel's globaltimer stamps.
 
@@ -381,6 +403,8 @@ def main(argv=None):
     parser.add_argument("--profile-steps", type=int, default=0,
                         help="profiling workload for ncu: build the model, prefill the prompt, run this many "
                              "decode steps, print no measurement")
+    parser.add_argument("--profile-prefill", type=int, default=0,
+                        help="profiling workload for ncu: build the model, prefill the prompt this many times")
     args = parser.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -410,6 +434,8 @@ def main(argv=None):
 
     if args.profile_steps:
         return run_profile_case(args)
+    if args.profile_prefill:
+        return run_profile_prefill(args)
     if args.trace:
         return run_trace(args)
     ranks = Ranks(args.gpus)
