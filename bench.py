@@ -1,6 +1,6 @@
 """Benchmark: batch-1 decode tok/s of the MiracleReasoning token loop on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config nano17] [--impl cuda|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config nano17] [--impl cuda|reference] [--tp]
 
 Workload: flashnano-1.7, random-init BF16 weights
 built in HBM by the seeded counter-hash generator, context 2048, a 512-token
@@ -23,7 +23,10 @@ Printed JSON line keys, beyond the driver contract's:
 
 N > 1: one process per GPU (torchrun), each rank decodes its own sequence on
 its own GPU (independent replicas, weak scaling, no data-path collective);
-value = tokens of all ranks / max time over ranks.
+value = tokens of all ranks / max time over ranks.  With --tp the N GPUs decode
+ONE sequence together (tensor parallel: every projection and the lm_head split
+by output row, attention by KV head, exchange words stored into every rank's
+memory over NVLink; strong scaling), value = that sequence's tokens / max time.
 
 --impl reference: the reference CPU implementation alone (rank 0 only), on a
 bounded sample of the same workload.
@@ -77,6 +80,11 @@ class Ranks:
         t = torch.tensor([value], dtype=torch.float64)
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
+
+    def all_gather(self, data):
+        items = [None] * self.world
+        self.dist.all_gather_object(items, data)
+        return items
 
     def close(self):
         if self.dist:
@@ -203,9 +211,17 @@ def run_cuda(args, ranks):
     if prompt_len + 1 + args.warmup + args.steps > context:
         raise SystemExit("warmup + steps exceed the context window")
     backend = backend_mod.CUDABackend(device_index=ranks.local)
-    model = model_mod.MiracleModel.synthetic(config, stored=stored, seed=ranks.rank, backend=backend,
-                                             context_length=context)
-    prompt = syn.prompt_ids(config.vocab_size, prompt_len, seed=1 + ranks.rank)
+    tp = args.tp and ranks.world > 1
+    if tp:  # one model, one sequence, split over the ranks
+        model = model_mod.MiracleModel.synthetic(config, stored=stored, seed=0, backend=backend,
+                                                 context_length=context,
+                                                 tensor_parallel=(ranks.rank, ranks.world, ranks.all_gather))
+        prompt = syn.prompt_ids(config.vocab_size, prompt_len, seed=1)
+    else:
+        model = model_mod.MiracleModel.synthetic(config, stored=stored, seed=ranks.rank, backend=backend,
+                                                 context_length=context)
+        prompt = syn.prompt_ids(config.vocab_size, prompt_len, seed=1 + ranks.rank)
+    sequences = 1 if tp else ranks.world
 
     # prefill, timed after one untimed pass (workspace allocation): batched on the
     # tensor cores for BF16 models, else token by token through the decode kernel
@@ -231,9 +247,10 @@ def run_cuda(args, ranks):
         backend.finish()
         ranks.barrier()
         device_ms = ranks.max(ms.value)
-        # keep the same decode load under the clock sampler for at least ~1.5 s
-        extra_until = time.perf_counter() + 1.5
-        while time.perf_counter() < extra_until:
+        # keep the same decode load under the clock sampler for ~1.5 s more (the same
+        # number of calls on every rank: tensor-parallel ranks step together)
+        extra_steps = min(1024, context - 16)
+        for _ in range(max(1, math.ceil(1.5e3 / (device_ms / args.steps * extra_steps)))):
             model.reset()
             model.prefill(prompt[:8])
             native.call("mr_model_bench_decode", model._handle, token, min(1024, context - 16), C.byref(ms))
@@ -254,26 +271,29 @@ def run_cuda(args, ranks):
     step_bytes = weight_bytes(config, stored) + sum(kv_bytes(config, context, p) for p in positions) / args.steps
     step_s = device_ms / 1e3 / args.steps
     peak, peak_kind = measured_hbm()
+    if tp:  # each GPU streams its slice of the weights and KV rows
+        step_bytes /= ranks.world
     achieved = step_bytes / step_s / 1e9
-    value = ranks.world * args.steps / (device_ms / 1e3)
+    value = sequences * args.steps / (device_ms / 1e3)
     result = {
         "metric": f"batch-1 decode tok/s ({config.family}, context {context}, prompt {prompt_len})",
         "value": round(value, 2), "unit": "tok/s", "n_gpus": ranks.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(device_ms / args.steps, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{args.config}: {config.family} decode, {stored} weights "
                                f"({weight_bytes(config, stored) / 1e9:.3f} GB/step), greedy, positions "
                                f"{first_position}..{first_position + args.steps - 1}",
                    "context": context, "prompt": prompt_len, "weights_dtype": stored,
                    "l2": "inputs larger than L2 (weights stream from HBM every step)",
-                   "parallelism": "replicas" if ranks.world > 1 else "single"},
+                   "parallelism": f"tp{ranks.world}" if tp else ("replicas" if ranks.world > 1 else "single")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "bytes_per_step": int(step_bytes), "traffic": ncu_traffic(args.config)},
-        "e2e": {"value": round(ranks.world * e2e_steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                     "bytes_per_step": int(step_bytes), "per": "GPU" if tp else "step",
+                     "traffic": None if tp else ncu_traffic(args.config)},
+        "e2e": {"value": round(sequences * e2e_steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * config.vocab_size, "steps": e2e_steps,
                 "path": "MiracleModel.decode (Python API -> C ABI), logits to host each step"},
-        "prefill": {"value": round(ranks.world * prompt_len / prefill_s, 2), "unit": "tok/s",
+        "prefill": {"value": round(sequences * prompt_len / prefill_s, 2), "unit": "tok/s",
                     "tokens": prompt_len,
                     "note": ("batched prefill: tensor-core GEMMs (BF16 weights x FP32 activations split in three BF16 "
                              "parts) + causal attention over the chunk, logits of the last token to host"
@@ -398,6 +418,8 @@ def main(argv=None):
     parser.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     parser.add_argument("--cpu-tokens", type=int, default=12, help="decode tokens of the CPU baseline sample")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--tp", action="store_true",
+                        help="with N > 1: the N GPUs decode one sequence tensor-parallel (default: N replicas)")
     parser.add_argument("--trace", action="store_true",
                         help="print per-phase device timings of decode steps (phase tracing) and exit")
     parser.add_argument("--profile-steps", type=int, default=0,

@@ -196,6 +196,20 @@ MR_API int mr_model_reset(mr_model *model);
  * kept as a comparison baseline).  *available (optional) reports whether the
  * batched path applies to this model. */
 MR_API int mr_model_set_batched_prefill(mr_model *model, int enable, int *available);
+
+/* Tensor-parallel decode over `ranks` GPUs, one process per GPU (reference:
+ * the token loop of model.py:257-285, each projection and the lm_head split
+ * by output row, attention by KV head).  Call mr_model_set_tensor_parallel
+ * before mr_model_finalize; then every rank exports its exchange arena
+ * (mr_model_tp_handle: a CUDA IPC handle, bytes >= 64), the handles are
+ * exchanged (any host channel), and mr_model_tp_connect maps the others'
+ * arenas (handles: ranks x bytes_each, in rank order).  Every rank then makes
+ * the same calls in the same order; each step's words are stored into every
+ * rank's arena over NVLink and the argmax is agreed at the step end.  KV head
+ * counts must divide by `ranks`. */
+MR_API int mr_model_set_tensor_parallel(mr_model *model, int rank, int ranks);
+MR_API int mr_model_tp_handle(mr_model *model, void *handle, size_t bytes);
+MR_API int mr_model_tp_connect(mr_model *model, const void *handles, size_t bytes_each);
 MR_API int mr_model_position(const mr_model *model, int *position);
 MR_API int mr_model_weight_bytes(const mr_model *model, uint64_t *bytes);
 

@@ -84,6 +84,9 @@ SIGNATURES = {
     "mr_model_finalize": (_I, [_P]),
     "mr_model_reset": (_I, [_P]),
     "mr_model_set_batched_prefill": (_I, [_P, _I, _IP]),
+    "mr_model_set_tensor_parallel": (_I, [_P, _I, _I]),
+    "mr_model_tp_handle": (_I, [_P, _P, _SZ]),
+    "mr_model_tp_connect": (_I, [_P, _P, _SZ]),
     "mr_model_position": (_I, [_P, _IP]),
     "mr_model_weight_bytes": (_I, [_P, C.POINTER(C.c_uint64)]),
     "mr_model_step": (_I, [_P, _I, _FP, _IP]),

@@ -123,6 +123,16 @@ struct mr_model {
     Phase *d_phases = nullptr;
     std::vector<Phase> phases;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    // tensor parallel: this rank of `ranks`; every exchange buffer lives in one arena
+    // whose IPC handle the other ranks open (peer[j] = rank j's arena, mapped here)
+    int rank = 0, ranks = 1;
+    char *arena = nullptr;
+    size_t arena_bytes = 0;
+    char *peer[kMaxRanks] = {};
+    bool peer_open[kMaxRanks] = {};
+    bool connected = false;
+    Word *best_slots = nullptr;
+    int xres_lo = 0, xres_n = 0;
     // batched prefill (prefill.cu): available for BF16 models of the engine families
     bool prefill_ok = false, prefill_on = true;
     PrefillModel pm{};
@@ -269,7 +279,7 @@ void phase_caps(const mr_model *m, const GemvPhase &g, int &piece_cap, int &grou
     int widest = 0;
     for (int i = 0; i < g.nseg; ++i) {
         const int row_bytes = g.seg[i].cols * (int)dtype_size(g.seg[i].dtype);
-        per_cta += (long long)((g.seg[i].rows + n - 1) / n) * row_bytes;
+        per_cta += (long long)((g.seg[i].row_n + n - 1) / n) * row_bytes;
         widest = std::max(widest, row_bytes);
     }
     if (per_cta <= ring / 2 || widest > ring / 6) {
@@ -369,6 +379,16 @@ int build_plan(mr_model *m) {
     end.kind = PH_STEP_END;
     end.layer = -2;
     m->phases.push_back(end);
+    // Tensor parallel: each rank computes a contiguous slice of every segment's
+    // rows (the o / down slices are its residual rows) and of the KV heads.
+    for (Phase &ph : m->phases) {
+        if (ph.kind == PH_GEMV) {
+            for (int i = 0; i < ph.gemv.nseg; ++i)
+                rank_rows(ph.gemv.seg[i].rows, m->rank, m->ranks, ph.gemv.seg[i].row_lo, ph.gemv.seg[i].row_n);
+        } else if (ph.kind == PH_ATTN_GQA) {
+            rank_rows(ph.attn.kv_heads, m->rank, m->ranks, ph.attn.kv_lo, ph.attn.kv_n);
+        }
+    }
     // Weight streaming through the shared-memory ring: pieces of whole 16-byte
     // rows (cp.async.bulk granularity) within the phase's piece cap.
     for (Phase &ph : m->phases) {
@@ -401,7 +421,7 @@ int build_plan(mr_model *m) {
 bool cta_has_rows(const GemvPhase &g, int b, int G) {
     for (int s = 0; s < g.nseg; ++s) {
         int r0, r1;
-        cta_row_range(g.seg[s].rows, b, G, g.skip, r0, r1);
+        seg_cta_rows(g.seg[s], b, G, g.skip, r0, r1);
         if (r1 > r0) return true;
     }
     return false;
@@ -440,7 +460,7 @@ int build_pieces(mr_model *m) {
             for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
                 const int rpp = g.seg[s].rows_per_piece;
                 int r0, r1;
-                cta_row_range(g.seg[s].rows, b, G, g.skip, r0, r1);
+                seg_cta_rows(g.seg[s], b, G, g.skip, r0, r1);
                 for (int row0 = r0; row0 < r1; row0 += rpp) {
                     const int n = std::min(rpp, r1 - row0);
                     add(v, s, row0, n);
@@ -505,7 +525,7 @@ int build_groups(mr_model *m) {
             for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
                 const int rpp = g.seg[s].rows_per_piece;
                 int r0, r1;
-                cta_row_range(g.seg[s].rows, b, G, g.skip, r0, r1);
+                seg_cta_rows(g.seg[s], b, G, g.skip, r0, r1);
                 for (int row0 = r0; row0 < r1; row0 += rpp) {
                     const int n = std::min(rpp, r1 - row0);
                     int ubytes = n * cols * (int)dtype_size(g.seg[s].dtype);
@@ -618,6 +638,13 @@ StepControl base_control(mr_model *m) {
     ctl.embed_dtype = embed->dtype;
     ctl.hidden = m->cfg.hidden_size;
     ctl.xres_skip = m->xres_skip;
+    ctl.xres_lo = m->xres_lo;
+    ctl.xres_n = m->xres_n;
+    ctl.ranks = m->ranks;
+    ctl.rank = m->rank;
+    ctl.arena = m->arena;
+    for (int j = 0; j < m->ranks; ++j) ctl.peers[j] = m->peer[j];
+    ctl.best_slots = m->best_slots;
     ctl.ring_bytes = m->ring_bytes;
     ctl.pieces = m->d_pieces;
     ctl.groups = m->d_groups;
@@ -634,6 +661,8 @@ int ready(mr_model *m) {
                          "the op kernels (mr_model_linear and mr_op_*)", m->cfg.family);
     if (m->failed)
         return set_error(MR_ERR_STATE, "A previous device operation failed; call reset() before reusing this model");
+    if (m->ranks > 1 && !m->connected)
+        return set_error(MR_ERR_STATE, "tensor-parallel model: mr_model_tp_connect has not been called");
     MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
     return MR_OK;
 }
@@ -838,6 +867,8 @@ int mr_model_destroy(mr_model *m) {
     if (!m) return MR_OK;
     cudaSetDevice(m->ctx->device);
     cudaStreamSynchronize(m->ctx->stream);
+    for (int j = 0; j < kMaxRanks; ++j)
+        if (m->peer_open[j]) cudaIpcCloseMemHandle(m->peer[j]);
     for (void *p : m->allocations) cudaFree(p);
     prefill_release(m->pw);
     if (m->ev0) cudaEventDestroy(m->ev0);
@@ -920,17 +951,39 @@ int mr_model_finalize(mr_model *m) {
     m->ring_bytes = (int)(ring & ~127ll);
     m->smem_bytes = control + scratch + (size_t)m->ring_bytes;
     auto falloc = [&](size_t n) { return static_cast<float *>(device_alloc(m, n * sizeof(float), &rc)); };
-    auto walloc = [&](size_t n) { return static_cast<Word *>(device_alloc(m, n * sizeof(Word), &rc)); };
     m->d_inv_freq = falloc(d / 2);
-    m->x = walloc(c.hidden_size);
-    m->q_raw = walloc((size_t)H * d);
-    m->k_raw = walloc((size_t)max_kvh * d);
-    m->v_raw = walloc((size_t)max_kvh * d);
-    m->ffn = walloc(c.ffn_dim);
-    m->attn_out = walloc((size_t)H * d);
+    // The exchange buffers (and the logits) live in one arena: with tensor
+    // parallelism every rank maps every other rank's arena and stores a word
+    // at the same offset of each.
+    {
+        size_t off = 0;
+        auto take = [&](size_t bytes) {
+            const size_t at = off;
+            off += (bytes + 255) & ~size_t(255);
+            return at;
+        };
+        const size_t o_x = take(sizeof(Word) * c.hidden_size), o_q = take(sizeof(Word) * H * d),
+                     o_k = take(sizeof(Word) * max_kvh * d), o_v = take(sizeof(Word) * max_kvh * d),
+                     o_f = take(sizeof(Word) * c.ffn_dim), o_a = take(sizeof(Word) * H * d),
+                     o_p = take(sizeof(Word) * H * kMaxAttnChunks * (d + 2)),
+                     o_l = take(sizeof(float) * 64 * (size_t)c.vocab_size), o_b = take(sizeof(Word) * 4 * kMaxRanks);
+        m->arena = static_cast<char *>(device_alloc(m, off, &rc));
+        if (rc) return rc;
+        MR_CUDA_TRY(cudaMemset(m->arena, 0, off));
+        m->arena_bytes = off;
+        m->x = reinterpret_cast<Word *>(m->arena + o_x);
+        m->q_raw = reinterpret_cast<Word *>(m->arena + o_q);
+        m->k_raw = reinterpret_cast<Word *>(m->arena + o_k);
+        m->v_raw = reinterpret_cast<Word *>(m->arena + o_v);
+        m->ffn = reinterpret_cast<Word *>(m->arena + o_f);
+        m->attn_out = reinterpret_cast<Word *>(m->arena + o_a);
+        m->partial = reinterpret_cast<Word *>(m->arena + o_p);
+        m->logits = reinterpret_cast<float *>(m->arena + o_l);
+        m->best_slots = reinterpret_cast<Word *>(m->arena + o_b);
+        m->peer[m->rank] = m->arena;
+        m->connected = m->ranks == 1;
+    }
     m->logits_rows = 64;
-    m->logits = falloc((size_t)m->logits_rows * c.vocab_size);
-    m->partial = walloc((size_t)H * kMaxAttnChunks * (d + 2));
     m->state = static_cast<StepState *>(device_alloc(m, sizeof(StepState), &rc));
     if (rc) return rc;
     m->k_cache.resize(c.layers);
@@ -953,11 +1006,16 @@ int mr_model_finalize(mr_model *m) {
     // the fewest units any layer has at full context, unless that is more
     // than a quarter of the grid.
     int skip = m->grid;
-    for (int l = 0; l < c.layers; ++l)
-        skip = std::min(skip, m->layer_kvh[l] * attn_chunks(m->cache_capacity[l], m->layer_kvh[l], m->grid));
+    for (int l = 0; l < c.layers; ++l) {
+        MR_REQUIRE(m->layer_kvh[l] % m->ranks == 0, "layer %d: %d KV heads do not split over %d ranks", l,
+                   m->layer_kvh[l], m->ranks);
+        const int kv_n = m->layer_kvh[l] / m->ranks;
+        skip = std::min(skip, kv_n * attn_chunks(m->cache_capacity[l], kv_n, m->grid));
+    }
     if (skip > m->grid / 4) skip = 0;  // too many units to spare their CTAs: no CTA is set aside
     m->xres_skip = skip;
-    MR_REQUIRE((c.hidden_size + m->grid - skip - 1) / (m->grid - skip) <= kRowBatch,
+    rank_rows(c.hidden_size, m->rank, m->ranks, m->xres_lo, m->xres_n);
+    MR_REQUIRE((m->xres_n + m->grid - skip - 1) / (m->grid - skip) <= kRowBatch,
                "hidden size %d above the engine limit (rows per CTA)", c.hidden_size);
     rc = build_plan(m);
     if (!rc) rc = build_pieces(m);
@@ -977,6 +1035,47 @@ int mr_model_finalize(mr_model *m) {
     setup_prefill(m);
     m->finalized = true;
     return mr_model_reset(m);
+}
+
+int mr_model_set_tensor_parallel(mr_model *m, int rank, int ranks) {
+    MR_REQUIRE(m, "model is NULL");
+    MR_REQUIRE(!m->finalized, "tensor parallelism is set before mr_model_finalize");
+    MR_REQUIRE(ranks >= 1 && ranks <= kMaxRanks && rank >= 0 && rank < ranks, "rank %d of %d ranks (at most %d)",
+               rank, ranks, kMaxRanks);
+    MR_REQUIRE(ranks == 1 || is_gqa_family(m->cfg.family), "tensor parallelism needs a decode-engine family");
+    m->rank = rank;
+    m->ranks = ranks;
+    return MR_OK;
+}
+
+int mr_model_tp_handle(mr_model *m, void *handle, size_t bytes) {
+    MR_REQUIRE(m && handle, "NULL argument");
+    MR_REQUIRE(m->finalized && m->arena, "model is not finalized");
+    MR_REQUIRE(bytes >= sizeof(cudaIpcMemHandle_t), "handle buffer needs %zu bytes", sizeof(cudaIpcMemHandle_t));
+    MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
+    cudaIpcMemHandle_t h;
+    MR_CUDA_TRY(cudaIpcGetMemHandle(&h, m->arena));
+    memcpy(handle, &h, sizeof(h));
+    return MR_OK;
+}
+
+int mr_model_tp_connect(mr_model *m, const void *handles, size_t bytes_each) {
+    MR_REQUIRE(m && handles, "NULL argument");
+    MR_REQUIRE(m->finalized && m->arena, "model is not finalized");
+    MR_REQUIRE(bytes_each >= sizeof(cudaIpcMemHandle_t), "handles of %zu bytes, need %zu", bytes_each,
+               sizeof(cudaIpcMemHandle_t));
+    MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
+    for (int j = 0; j < m->ranks; ++j) {
+        if (j == m->rank || m->peer_open[j]) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char *>(handles) + (size_t)j * bytes_each, sizeof(h));
+        void *p = nullptr;
+        MR_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        m->peer[j] = static_cast<char *>(p);
+        m->peer_open[j] = true;
+    }
+    m->connected = true;
+    return MR_OK;
 }
 
 int mr_model_set_batched_prefill(mr_model *m, int enable, int *available) {

@@ -78,7 +78,16 @@ struct Segment {
     int rows, cols;
     int rows_per_piece; // rows per bulk piece (bulk phases)
     Word *out;          // EPI_STORE destination (rows words)
+    int row_lo, row_n;  // this rank's rows (tensor parallel: a contiguous slice; else all)
 };
+
+constexpr int kMaxRanks = 8;  // tensor-parallel ranks (one GPU each)
+
+// Rows [lo, lo + n) of `rows` owned by rank r of `ranks` (contiguous slices).
+__host__ __device__ inline void rank_rows(int rows, int r, int ranks, int &lo, int &n) {
+    lo = static_cast<int>(static_cast<long long>(rows) * r / ranks);
+    n = static_cast<int>(static_cast<long long>(rows) * (r + 1) / ranks) - lo;
+}
 
 struct GemvPhase {
     int input_kind;
@@ -105,6 +114,10 @@ struct GemvPhase {
     int skip;                   // CTAs 0 .. skip-1 own no rows of the phase (see cta_row_range)
 };
 
+// Rows [r0, r1) of segment s owned by CTA b of G: the CTA's share of the
+// rank's slice of the segment.
+__host__ __device__ inline void seg_cta_rows(const Segment &s, int b, int G, int skip, int &r0, int &r1);
+
 struct AttnPhase {
     const Word *q_raw, *k_raw, *v_raw;
     int qk_norm;                    // per-head RMSNorm of q and k before RoPE
@@ -121,6 +134,7 @@ struct AttnPhase {
     int relay_capacity;
     Word *partial;                  // [heads][kMaxAttnChunks][dim + 2]: chunks 1.. (acc[dim], max, sum)
     Word *out;                      // [heads * dim] attention output (the o projection's input)
+    int kv_lo, kv_n;                // this rank's KV heads (tensor parallel: a contiguous slice; else all)
 };
 
 // The compute warps take a bulk phase's pieces in groups, precomputed on the
@@ -183,6 +197,12 @@ __host__ __device__ inline void cta_row_range(int rows, int b, int G, int skip, 
     }
     r0 = static_cast<int>(static_cast<long long>(rows) * (b - skip) / (G - skip));
     r1 = static_cast<int>(static_cast<long long>(rows) * (b + 1 - skip) / (G - skip));
+}
+
+__host__ __device__ inline void seg_cta_rows(const Segment &s, int b, int G, int skip, int &r0, int &r1) {
+    cta_row_range(s.row_n, b, G, skip, r0, r1);
+    r0 += s.row_lo;
+    r1 += s.row_lo;
 }
 
 __host__ __device__ inline int attn_chunks(int total_keys, int kv_heads, int grid) {
@@ -261,6 +281,14 @@ struct StepControl {
     const void *embed;                // embedding [vocab, hidden]: this CTA's rows of the residual stream
     int embed_dtype, hidden;          //   start as the token's embedding
     int xres_skip;                    // CTAs owning no residual rows (cta_row_range)
+    int xres_lo, xres_n;              // this rank's rows of the residual stream
+    // Tensor parallel: every exchange word (and logit) goes to the same offset
+    // of every rank's exchange arena; readers poll their own.
+    int ranks;                        // 1: single GPU
+    char *arena;                      // this rank's arena (the base of every exchange buffer)
+    char *peers[kMaxRanks];           // every rank's arena, mapped here (peers[rank] == arena)
+    Word *best_slots;                 // [kMaxRanks][4] step-end argmax exchange (this rank's arena)
+    int rank;
     int ring_bytes;                   // shared-memory weight ring
     const PieceDesc *pieces;          // [grid][piece_stride] weight stream of each CTA
     const GroupTable *groups;         // piece groups of every (bulk phase, CTA)

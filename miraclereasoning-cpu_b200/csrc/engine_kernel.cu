@@ -59,6 +59,9 @@ struct Control {
     float red[kEngineWarps];
     unsigned long long best[kEngineWarps];
     int ok;
+    int ranks;                         // tensor-parallel ranks (1: single GPU)
+    char *arena;                       // this rank's exchange arena
+    char *peers[kMaxRanks];            // every rank's arena (exchange stores go to all)
     int abort;                         // the compute warps stopped: the producer stops too
     unsigned long long wait_ns;        // tracing: time thread 0 spent in take_piece this phase
     int late;                          // tracing: pieces not resident at their first probe
@@ -132,17 +135,39 @@ __device__ __forceinline__ void cp_async_wait_all() {
 }
 
 // ---- exchange words (see engine.cuh) --------------------------------------------------
+// Readers poll at system scope: with tensor parallelism the words of a phase
+// are stored into this GPU's memory by every rank's GPU.
 __device__ __forceinline__ Word ld_word(const Word *p) {
     Word v;
-    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
+// A word only this GPU reads (attention chunk partials).
 __device__ __forceinline__ void st_word(Word *p, float v, unsigned tag) {
     const Word w = (static_cast<Word>(tag) << 32) | __float_as_uint(v);
     asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+__device__ __forceinline__ void st_word_sys(Word *p, Word w) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
 __device__ __forceinline__ bool word_ok(Word w, unsigned tag) { return static_cast<unsigned>(w >> 32) == tag; }
 __device__ __forceinline__ float word_value(Word w) { return __uint_as_float(static_cast<unsigned>(w)); }
+
+// The same offset of another rank's arena.
+template <typename T>
+__device__ __forceinline__ T *peer_ptr(const Control &c, int j, T *p) {
+    return reinterpret_cast<T *>(c.peers[j] + (reinterpret_cast<char *>(p) - c.arena));
+}
+// A word every rank reads: stored into every rank's arena (NVLink peer
+// stores for the others) when tensor parallel.
+__device__ __forceinline__ void st_word_all(const Control &c, Word *p, float v, unsigned tag) {
+    if (c.ranks == 1) {
+        st_word(p, v, tag);
+        return;
+    }
+    const Word w = (static_cast<Word>(tag) << 32) | __float_as_uint(v);
+    for (int j = 0; j < c.ranks; ++j) st_word_sys(peer_ptr(c, j, p), w);
+}
 
 // ---- mbarrier / bulk copy primitives --------------------------------------------------
 __device__ __forceinline__ void mbar_init(unsigned long long *bar, int count) {
@@ -675,24 +700,29 @@ __device__ __forceinline__ void finish_row(const GemvPhase &g, int s, int r, flo
                                            Control &c, Epi &e) {
     const unsigned tag = info.tag_base + p;
     switch (g.epilogue) {
-        case EPI_STORE: st_word(g.seg[s].out + r, val, tag); break;
+        case EPI_STORE: st_word_all(c, g.seg[s].out + r, val, tag); break;
         case EPI_RESIDUAL: {  // model.py:282-283; x rows of this CTA live in shared memory
             const float xn = __fadd_rn(c.xres[r - info.xr0], __fmul_rn(g.scale, val));
             c.xres[r - info.xr0] = xn;
-            st_word(g.x + r, xn, tag);
+            st_word_all(c, g.x + r, xn, tag);
             break;
         }
-        case EPI_LOGITS:
-            g.logits[static_cast<size_t>(info.logits_row) * g.seg[0].rows + r] = val;
+        case EPI_LOGITS: {
+            float *dst = g.logits + static_cast<size_t>(info.logits_row) * g.seg[0].rows + r;
+            if (c.ranks == 1) *dst = val;
+            else
+                for (int j = 0; j < c.ranks; ++j) *peer_ptr(c, j, dst) = val;  // every rank holds all logits
             if (!isfinite(val)) e.nonfinite = 1;
             else e.best = max(e.best, argmax_key(val, r));
             break;
+        }
         default: break;  // EPI_SWIGLU: see swiglu_row
     }
 }
 // kernels.cl:46-50: out = (g / (1 + exp(-g))) * u
-__device__ __forceinline__ void swiglu_row(const GemvPhase &g, int r, float gt, float up, const StepInfo &info, int p) {
-    st_word(g.out + r, __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up), info.tag_base + p);
+__device__ __forceinline__ void swiglu_row(const GemvPhase &g, int r, float gt, float up, const StepInfo &info, int p,
+                                           const Control &c) {
+    st_word_all(c, g.out + r, __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up), info.tag_base + p);
 }
 
 __device__ void finish_logits(StepState *st, Control &c, Epi &e) {
@@ -858,7 +888,7 @@ __device__ void group_epilogue(const GemvPhase &g, const GroupTable &t, const in
         finish_row(g, s, r, val, info, p, c, e);
     } else if (s == 1) {  // the gate row of the same output is in the previous piece
         const float gy = y[row_partner(ri)];
-        swiglu_row(g, r, g.norm ? __fmul_rn(gy, scale) : gy, val, info, p);
+        swiglu_row(g, r, g.norm ? __fmul_rn(gy, scale) : gy, val, info, p, c);
     }
 }
 
@@ -968,7 +998,7 @@ __device__ bool gemv_direct(const GemvPhase &g, int p, StepState *st, const Step
     bool mine = false;
     for (int s = 0; s < g.nseg; ++s) {
         int r0, r1;
-        cta_row_range(g.seg[s].rows, b, G, g.skip, r0, r1);
+        seg_cta_rows(g.seg[s], b, G, g.skip, r0, r1);
         mine = mine || r1 > r0;
     }
     if (!mine) return true;
@@ -985,7 +1015,7 @@ __device__ bool gemv_direct(const GemvPhase &g, int p, StepState *st, const Step
     const bool paired = g.epilogue == EPI_SWIGLU;
     for (int s = 0; s < (paired ? 1 : g.nseg); ++s) {
         int r0, r1;
-        cta_row_range(g.seg[s].rows, b, G, g.skip, r0, r1);
+        seg_cta_rows(g.seg[s], b, G, g.skip, r0, r1);
         for (int rb = r0; rb < r1; rb += kRowBatch) {
             const int n = min(kRowBatch, r1 - rb);
             for (int part = 0; part < (paired ? 2 : 1); ++part) {
@@ -996,7 +1026,7 @@ __device__ bool gemv_direct(const GemvPhase &g, int p, StepState *st, const Step
                 for (int i = threadIdx.x; i < n; i += kEngineThreads) {
                     if (!paired) finish_row(g, s, rb + i, c.y[buf][i], info, p, c, e);
                     else if (part == 0) c.gate[i] = c.y[buf][i];
-                    else swiglu_row(g, rb + i, c.gate[i], c.y[buf][i], info, p);
+                    else swiglu_row(g, rb + i, c.gate[i], c.y[buf][i], info, p, c);
                 }
                 buf ^= 1;
             }
@@ -1079,7 +1109,7 @@ struct AttnGeometry {
         length = min(count, a.capacity);
         start = (count - length) % a.capacity;
         total = length + (a.relay_count ? __ldcg(a.relay_count) : 0);
-        chunks = attn_chunks(total, a.kv_heads, gridDim.x);
+        chunks = attn_chunks(total, a.kv_n, gridDim.x);
         chunk_len = (total + chunks - 1) / chunks;
     }
 };
@@ -1092,8 +1122,8 @@ struct AttnGeometry {
 __device__ bool attn_first_tile(const AttnPhase &a, const StepInfo &info, const Smem &sm) {
     const AttnGeometry geo(a, info);
     const int unit = blockIdx.x;
-    if (unit >= a.kv_heads * geo.chunks) return false;
-    const int g = unit / geo.chunks, c = unit % geo.chunks;
+    if (unit >= a.kv_n * geo.chunks) return false;
+    const int g = a.kv_lo + unit / geo.chunks, c = unit % geo.chunks;
     const int t0 = c * geo.chunk_len, t1 = min(geo.total, t0 + geo.chunk_len);
     if (t0 >= t1) return false;
     const AttnLayout L = attn_layout(a.heads / a.kv_heads, a.dim);
@@ -1133,7 +1163,7 @@ __device__ bool read_to_smem(int n, Addr addr, unsigned tag, float *dst, StepSta
 // one polling round), the weights are formed per (head, chunk), and the
 // output rows go out as exchange words for the o projection.
 __device__ bool merge_slice(const AttnPhase &a, int g, int gq, int chunks, int c, float *scratch, unsigned tag,
-                            StepState *st, int phase) {
+                            StepState *st, int phase, const Control &ctl) {
     const int d = a.dim, stride = d + 2, n = gq * d;
     const int per = (n + chunks - 1) / chunks, e0 = c * per, e1 = min(n, e0 + per);
     const int nacc = max(0, e1 - e0) * chunks, npair = gq * chunks;
@@ -1172,7 +1202,7 @@ __device__ bool merge_slice(const AttnPhase &a, int g, int gq, int chunks, int c
         const int e = e0 + k, i = e / d;
         float sum = 0.f;
         for (int cc = 0; cc < chunks; ++cc) sum = fmaf(wgt[i * chunks + cc], vals[k * chunks + cc], sum);
-        st_word(a.out + static_cast<size_t>(g * gq) * d + e, sum, tag);
+        st_word_all(ctl, a.out + static_cast<size_t>(g * gq) * d + e, sum, tag);
     }
     return true;
 }
@@ -1283,8 +1313,8 @@ __device__ bool attn_gqa_phase_t(const AttnPhase &a, const StepInfo &info, int p
     float *mrow = sm.attn + L.m, *lrow = sm.attn + L.l, *wm = sm.attn + L.wm, *wl = wm + 2 * gq;
     float *gains = sm.c->gains;
 
-    for (int unit = blockIdx.x; unit < a.kv_heads * chunks; unit += G) {
-        const int g = unit / chunks, c = unit % chunks;
+    for (int unit = blockIdx.x; unit < a.kv_n * chunks; unit += G) {
+        const int g = a.kv_lo + unit / chunks, c = unit % chunks;
         const int t0 = c * chunk_len, t1 = min(total, t0 + chunk_len);
         const int newest = length - 1;
         const bool owner = newest >= t0 && newest < t1;
@@ -1372,7 +1402,8 @@ __device__ bool attn_gqa_phase_t(const AttnPhase &a, const StepInfo &info, int p
         if (chunks == 1) {
             for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
                 const int i = e / d, j = e - i * d;
-                st_word(a.out + static_cast<size_t>(g * gq + i) * d + j, __fdiv_rn(acc[e], lrow[par * gq + i]), out_tag);
+                st_word_all(*sm.c, a.out + static_cast<size_t>(g * gq + i) * d + j, __fdiv_rn(acc[e], lrow[par * gq + i]),
+                            out_tag);
             }
         } else {
             for (int e = threadIdx.x; e < gq * d; e += kEngineThreads) {
@@ -1384,7 +1415,7 @@ __device__ bool attn_gqa_phase_t(const AttnPhase &a, const StepInfo &info, int p
                 st_word(rec + d, mrow[par * gq + threadIdx.x], out_tag);
                 st_word(rec + d + 1, lrow[par * gq + threadIdx.x], out_tag);
             }
-            if (!merge_slice(a, g, gq, chunks, c, kt, out_tag, st, ph)) return false;  // the tiles are free
+            if (!merge_slice(a, g, gq, chunks, c, kt, out_tag, st, ph, *sm.c)) return false;  // the tiles are free
         }
         csync();
     }
@@ -1424,10 +1455,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         const int rel = pos - ctl.feed_base;
         info.position = pos;
         info.token = (rel >= 0 && rel < ctl.feed_len) ? ctl.feed[rel] : vs->token;
-        need_head = ctl.return_all || rel >= ctl.feed_len - 1;
+        // split over ranks, every step ends with the argmax exchange: no rank starts the next
+        // step (and overwrites exchange words in the others' arenas) before all have finished
+        need_head = ctl.return_all || rel >= ctl.feed_len - 1 || ctl.ranks > 1;
         info.logits_row = ctl.return_all ? rel % ctl.logits_rows : 0;
         info.tag_base = ctl.tag_base;
-        cta_row_range(ctl.hidden, blockIdx.x, gridDim.x, ctl.xres_skip, info.xr0, info.xr1);
+        cta_row_range(ctl.xres_n, blockIdx.x, gridDim.x, ctl.xres_skip, info.xr0, info.xr1);
+        info.xr0 += ctl.xres_lo;
+        info.xr1 += ctl.xres_lo;
         base = vs->barrier_base;
         if (!skip && pos >= ctl.context_length) {
             if (blockIdx.x == 0) atomicCAS(&st->error, 0, 3);
@@ -1446,6 +1481,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             c.abort = 0;
             c.wait_ns = 0;
             c.late = 0;
+            c.ranks = ctl.ranks;
+            c.arena = ctl.arena;
+            for (int j = 0; j < kMaxRanks; ++j) c.peers[j] = ctl.peers[j];
         }
         if (!skip && ctl.trace && blockIdx.x == 0) ctl.trace[0] = global_ns();
     }
@@ -1516,6 +1554,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     cp_async_wait_all();
     // one grid barrier per step: every CTA's logits and argmax are in before the step ends
     int barriers = 0;
+    if (c.ranks > 1 && need_head) __threadfence_system();  // this thread's logits in every rank's arena
     if (ok && need_head) {
         ++barriers;
         ok = grid_barrier(st, base + static_cast<unsigned long long>(barriers) * gridDim.x, nphases - 2, c, [] {});
@@ -1529,7 +1568,38 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         const int pos = info.position;
         const int rel = pos - ctl.feed_base;
         if (need_head) {
-            const unsigned long long key = s->best;
+            unsigned long long key = s->best;
+            if (c.ranks > 1) {
+                // every rank's argmax of its vocabulary rows (and its non-finite flag) to every
+                // rank; then the greatest (ties: the lowest index, as numpy.argmax)
+                const unsigned tag = info.tag_base + nphases;  // no phase of this launch uses it
+                Word *mine = ctl.best_slots + 4 * ctl.rank;
+                const unsigned parts[3] = {static_cast<unsigned>(key >> 32), static_cast<unsigned>(key),
+                                           static_cast<unsigned>(s->nonfinite)};
+                __threadfence_system();
+                for (int j = 0; j < c.ranks; ++j)
+                    for (int q = 0; q < 3; ++q)
+                        st_word_sys(peer_ptr(c, j, mine + q), (static_cast<Word>(tag) << 32) | parts[q]);
+                const uint64_t start = global_ns();
+                for (int j = 0; j < c.ranks; ++j) {
+                    Word w[3];
+                    for (int q = 0; q < 3; ++q) {
+                        for (;;) {
+                            w[q] = ld_word(ctl.best_slots + 4 * j + q);
+                            if (word_ok(w[q], tag)) break;
+                            if (global_ns() - start > kWaitLimitNs) {
+                                atomicCAS(&st->error, 0, 1000 + nphases);
+                                break;
+                            }
+                        }
+                    }
+                    const unsigned long long kj = (static_cast<unsigned long long>(static_cast<unsigned>(w[0])) << 32) |
+                                                  static_cast<unsigned>(w[1]);
+                    key = max(key, kj);
+                    if (static_cast<unsigned>(w[2])) s->nonfinite = 1;
+                }
+                __threadfence_system();  // the logits every rank stored here are in before the step ends
+            }
             const int arg = key ? argmax_index(key) : -1;
             s->last_argmax = arg;
             s->best = 0ull;

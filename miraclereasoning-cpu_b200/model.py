@@ -91,7 +91,11 @@ class MiracleModel:
     """
 
     def __init__(self, config, weights=None, *, backend=None, context_length=None,
-                 weight_cache_bytes=256 * 1024 * 1024, _synthetic=None):
+                 weight_cache_bytes=256 * 1024 * 1024, tensor_parallel=None, _synthetic=None):
+        """``tensor_parallel=(rank, ranks, all_gather)``: this process decodes on one of
+        ``ranks`` GPUs, each computing a slice of every projection's rows and of the
+        KV heads (every rank makes the same calls in the same order; see
+        mr_model_set_tensor_parallel)."""
         self.config = config
         if context_length is None:
             context_length = min(2048, config.max_positions)
@@ -119,7 +123,12 @@ class MiracleModel:
             self._load(self.weights)
         else:
             self._fill_synthetic(*_synthetic)
+        if tensor_parallel is not None:
+            rank, ranks, _ = tensor_parallel
+            _native.call("mr_model_set_tensor_parallel", self._handle, int(rank), int(ranks))
         _native.call("mr_model_finalize", self._handle)
+        if tensor_parallel is not None and tensor_parallel[1] > 1:
+            self._connect(*tensor_parallel)
         used = C.c_uint64()
         _native.call("mr_model_weight_bytes", self._handle, C.byref(used))
         self.weight_cache = ResidentWeights(int(used.value), weight_cache_bytes)
@@ -132,6 +141,18 @@ class MiracleModel:
         if handle and _native._lib is not None:
             _native._lib.mr_model_destroy(handle)
             self._handle = None
+
+    def _connect(self, rank, ranks, all_gather):
+        """Maps every rank's exchange arena: ``all_gather(bytes) -> [bytes of rank 0, ...]``
+        is any host channel between the ranks (e.g. torch.distributed.all_gather_object)."""
+        size = 64
+        mine = (C.c_char * size)()
+        _native.call("mr_model_tp_handle", self._handle, C.cast(mine, C.c_void_p), size)
+        handles = all_gather(bytes(mine))
+        if len(handles) != ranks or any(len(h) != size for h in handles):
+            raise RuntimeError("tensor parallel: one handle per rank expected")
+        joined = (C.c_char * (size * ranks)).from_buffer_copy(b"".join(handles))
+        _native.call("mr_model_tp_connect", self._handle, C.cast(joined, C.c_void_p), size)
 
     def _load(self, weights):
         for name, shape in expected_shapes(self.config).items():

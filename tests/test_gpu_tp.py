@@ -1,0 +1,44 @@
+"""Tensor-parallel decode (every projection and the lm_head split by output row
+over the GPUs, attention by KV head, exchange words stored into every rank's
+arena over NVLink) against the single-GPU engine on the same model and prompt.
+
+Needs two GPUs: runs tests/tp_worker.py as two processes under
+torch.distributed.run (127.0.0.1 rendezvous); skipped with fewer GPUs.
+"""
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def _gpus():
+    try:
+        out = subprocess.run(["nvidia-smi", "-L"], capture_output=True, text=True, timeout=30).stdout
+    except (OSError, subprocess.TimeoutExpired):
+        return 0
+    return sum(1 for line in out.splitlines() if line.startswith("GPU "))
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="tensor-parallel decode needs two GPUs")
+@pytest.mark.parametrize("config", ["nano17"])
+def test_tensor_parallel_decode_matches_single_gpu(tmp_path, config):
+    out = tmp_path / "tp.json"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29517",
+           str(REPO / "tests" / "tp_worker.py"), str(out), config, "6"]
+    proc = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=420)
+    assert proc.returncode == 0, proc.stdout[-2000:] + proc.stderr[-4000:]
+    result = json.loads(out.read_text())
+    assert result["tokens"] == result["ref_tokens"]
+    # both sum every dot product in the same order per row: the split only moves rows between GPUs
+    assert result["max_abs_diff"] <= 2e-5 * max(1.0, result["scale"])
