@@ -1007,10 +1007,10 @@ int mr_model_finalize(mr_model *m) {
     // than a quarter of the grid.
     int skip = m->grid;
     for (int l = 0; l < c.layers; ++l) {
-        MR_REQUIRE(m->layer_kvh[l] % m->ranks == 0, "layer %d: %d KV heads do not split over %d ranks", l,
-                   m->layer_kvh[l], m->ranks);
-        const int kv_n = m->layer_kvh[l] / m->ranks;
-        skip = std::min(skip, kv_n * attn_chunks(m->cache_capacity[l], kv_n, m->grid));
+        // this rank's KV heads of the layer (none when the layer has fewer heads than ranks)
+        int kv_lo, kv_n;
+        rank_rows(m->layer_kvh[l], m->rank, m->ranks, kv_lo, kv_n);
+        skip = kv_n > 0 ? std::min(skip, kv_n * attn_chunks(m->cache_capacity[l], kv_n, m->grid)) : 0;
     }
     if (skip > m->grid / 4) skip = 0;  // too many units to spare their CTAs: no CTA is set aside
     m->xres_skip = skip;

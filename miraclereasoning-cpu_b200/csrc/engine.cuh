@@ -206,7 +206,7 @@ __host__ __device__ inline void seg_cta_rows(const Segment &s, int b, int G, int
 }
 
 __host__ __device__ inline int attn_chunks(int total_keys, int kv_heads, int grid) {
-    int chunks = grid / kv_heads;
+    int chunks = kv_heads > 0 ? grid / kv_heads : 1;  // a rank can hold no KV head of a layer
     const int by_keys = (total_keys + kKeysPerChunk - 1) / kKeysPerChunk;
     if (by_keys < chunks) chunks = by_keys;
     if (kMaxAttnChunks < chunks) chunks = kMaxAttnChunks;

@@ -2,8 +2,9 @@
 over the GPUs, attention by KV head, exchange words stored into every rank's
 arena over NVLink) against the single-GPU engine on the same model and prompt.
 
-Needs two GPUs: runs tests/tp_worker.py as two processes under
-torch.distributed.run (127.0.0.1 rendezvous); skipped with fewer GPUs.
+Runs tests/tp_worker.py as one process per GPU under torch.distributed.run
+(127.0.0.1 rendezvous); a case is skipped when the box has fewer GPUs than it
+has ranks.
 """
 from __future__ import annotations
 
@@ -28,13 +29,18 @@ def _gpus():
     return sum(1 for line in out.splitlines() if line.startswith("GPU "))
 
 
-@pytest.mark.skipif(_gpus() < 2, reason="tensor-parallel decode needs two GPUs")
-@pytest.mark.parametrize("config", ["nano17"])
-def test_tensor_parallel_decode_matches_single_gpu(tmp_path, config):
+GPUS = _gpus()
+
+
+# 8 ranks over nano-1.7's 4 local KV heads: half the ranks hold no head of those layers
+@pytest.mark.parametrize("config,ranks", [("nano17", 2), ("lite", 2), ("nano17", 4), ("nano17", 8)])
+def test_tensor_parallel_decode_matches_single_gpu(tmp_path, config, ranks):
+    if GPUS < ranks:
+        pytest.skip(f"tensor-parallel decode over {ranks} GPUs needs {ranks} GPUs")
     out = tmp_path / "tp.json"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29517",
+           "--nproc-per-node", str(ranks), "--master-addr", "127.0.0.1", "--master-port", str(29500 + 17 * ranks),
            str(REPO / "tests" / "tp_worker.py"), str(out), config, "6"]
     proc = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=420)
     assert proc.returncode == 0, proc.stdout[-2000:] + proc.stderr[-4000:]
