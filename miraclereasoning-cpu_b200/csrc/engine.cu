@@ -35,6 +35,19 @@ bool is_gqa_family(int f) {
     return f == MR_FAMILY_FLASHNANO_15 || f == MR_FAMILY_FLASHNANO_17 || f == MR_FAMILY_FLASHLITE_20;
 }
 
+// FlashLighting with no memory slots (the family default) compacts its latent
+// cache by dropping the oldest row (model.py:171-176): attention then covers
+// the newest `window` latents, whose keys and values (normed, rotated at the
+// latent's own position) never change once computed.  The engine keeps them in
+// a ring of `window` rows, computing one row per token, which gives the same
+// keys and values the reference recomputes from the stored latents every step.
+bool is_lighting_ring(const mr_model_config &c) {
+    return c.family == MR_FAMILY_FLASHLIGHTING_20 && c.memory_slots == 0 && c.window > 0;
+}
+
+// Families the persistent decode kernel plans (the others step on the host).
+bool is_engine_family(const mr_model_config &c) { return is_gqa_family(c.family) || is_lighting_ring(c); }
+
 size_t dtype_size(int dtype) { return dtype == MR_DTYPE_F32 ? 4 : 2; }
 
 // ---- synthetic weights (counter hash, bit-identical to synthetic.py) -------------
@@ -101,6 +114,7 @@ struct mr_model {
     // device buffers
     float *d_inv_freq = nullptr;
     Word *x = nullptr, *q_raw = nullptr, *k_raw = nullptr, *v_raw = nullptr, *ffn = nullptr;  // exchange words
+    Word *latent = nullptr;  // FlashLighting: the layer's latent row
     Word *attn_out = nullptr;
     unsigned long long launches = 0;  // launches so far: each gets its own exchange tags
     float *logits = nullptr;
@@ -258,6 +272,7 @@ Phase gemv_phase(int layer, const Word *in, const TensorSlot *norm_gain, float e
     ph.layer = layer;
     ph.gemv.input_kind = IN_VECTOR;
     ph.gemv.in = in;
+    ph.gemv.in_back = 1;
     if (norm_gain) {
         ph.gemv.norm = 1;
         ph.gemv.norm_gain = norm_gain->ptr;
@@ -291,13 +306,146 @@ void phase_caps(const mr_model *m, const GemvPhase &g, int &piece_cap, int &grou
     }
 }
 
+// The attention phase of layer l: q words from `q_back` phases back, this
+// token's k / v words from the phase just before.
+int attn_phase(mr_model *m, int l, bool qk_norm, int q_back, Phase &at) {
+    const mr_model_config &c = m->cfg;
+    const std::string p = "layers." + std::to_string(l) + ".";
+    at = Phase{};
+    at.kind = PH_ATTN_GQA;
+    at.layer = l;
+    AttnPhase &a = at.attn;
+    a.q_raw = m->q_raw;
+    a.k_raw = m->k_raw;
+    a.v_raw = m->v_raw;
+    a.q_back = q_back;
+    a.qk_norm = qk_norm;
+    if (qk_norm) {
+        const TensorSlot *qn = tensor(m, p + "q_norm"), *kn = tensor(m, p + "k_norm");
+        if (qn->dtype != kn->dtype) return set_error(MR_ERR_ARGUMENT, "q_norm/k_norm dtypes differ");
+        a.q_gain = qn->ptr;
+        a.k_gain = kn->ptr;
+        a.gain_dtype = qn->dtype;
+    }
+    a.norm_eps = c.norm_eps;
+    a.heads = c.query_heads;
+    a.kv_heads = m->layer_kvh[l];
+    a.dim = c.head_dim;
+    a.split_half = c.split_half_rope;
+    a.inv_freq = m->d_inv_freq;
+    a.k_cache = m->k_cache[l];
+    a.v_cache = m->v_cache[l];
+    a.capacity = m->cache_capacity[l];
+    a.partial = m->partial;
+    a.out = m->attn_out;
+    return MR_OK;
+}
+
+// A one-element tensor (a FlashLighting gate) widened to float on the host.
+int read_scalar(mr_model *m, const std::string &name, float &value) {
+    const TensorSlot *t = tensor(m, name);
+    MR_REQUIRE(t && t->ptr, "missing tensor %s", name.c_str());
+    uint32_t raw = 0;
+    MR_CUDA_TRY(cudaMemcpy(&raw, t->ptr, dtype_size(t->dtype), cudaMemcpyDeviceToHost));
+    if (t->dtype == MR_DTYPE_F32) {
+        memcpy(&value, &raw, 4);
+    } else if (t->dtype == MR_DTYPE_BF16) {
+        const uint32_t bits = raw << 16;
+        memcpy(&value, &bits, 4);
+    } else {
+        __half h;
+        memcpy(&h, &raw, 2);
+        value = __half2float(h);
+    }
+    return MR_OK;
+}
+
+// FlashLighting layer (model.py:146-190, 272-278) on the ring form above.
+// Both branches read the same RMSNorm(x): phases
+//   1. q | latent       = W (a_norm x)
+//   2. SwiGLU(gate, up) of a_norm x                        (independent of 1)
+//   3. k | v            = W (latent_norm latent)
+//   4. attention: q from phase 1, k / v from phase 3 (q_norm / k_norm + RoPE)
+//   5. x += (residual_scale * attention_gate) * (W_o attended)   (kept in shared memory)
+//   6. x += (residual_scale * ffn_gate) * (W_down ffn)            (published)
+// The gates are weights read once here.  The reference forms
+// x + s * (ag * o + fg * f); this sums the two scaled branches into x one at a
+// time (a float32 rounding difference).  Only phase 6 publishes x, so no
+// phase of the layer overwrites x words that phases 1 and 2 of another CTA may
+// still be reading (phase 6 needs every CTA's phase-2 output first).
+int plan_lighting_layer(mr_model *m, int l) {
+    const mr_model_config &c = m->cfg;
+    const std::string p = "layers." + std::to_string(l) + ".";
+    const TensorSlot *embed = tensor(m, "embed");
+    auto input = [&](Phase &ph, int back) {
+        ph.gemv.in_back = back;
+        if (l == 0) {
+            ph.gemv.input_kind = IN_EMBED_ROW;
+            ph.gemv.embed = embed->ptr;
+            ph.gemv.embed_dtype = embed->dtype;
+        }
+    };
+    Phase ql = gemv_phase(l, m->x, tensor(m, p + "a_norm"), c.norm_eps);
+    input(ql, 1);
+    ql.gemv.nseg = 2;
+    ql.gemv.seg[0] = segment(tensor(m, p + "q"), m->q_raw);
+    ql.gemv.seg[1] = segment(tensor(m, p + "latent"), m->latent);
+    ql.gemv.epilogue = EPI_STORE;
+    ql.gemv.skip = m->xres_skip;
+    m->phases.push_back(ql);
+    Phase gu = gemv_phase(l, m->x, tensor(m, p + "a_norm"), c.norm_eps);
+    input(gu, 2);
+    gu.gemv.nseg = 2;
+    gu.gemv.seg[0] = segment(tensor(m, p + "ffn.gate"));
+    gu.gemv.seg[1] = segment(tensor(m, p + "ffn.up"));
+    gu.gemv.epilogue = EPI_SWIGLU;
+    gu.gemv.out = m->ffn;
+    m->phases.push_back(gu);
+    Phase kv = gemv_phase(l, m->latent, tensor(m, p + "latent_norm"), c.norm_eps);
+    kv.gemv.in_back = 2;
+    kv.gemv.nseg = 2;
+    kv.gemv.seg[0] = segment(tensor(m, p + "k"), m->k_raw);
+    kv.gemv.seg[1] = segment(tensor(m, p + "v"), m->v_raw);
+    kv.gemv.epilogue = EPI_STORE;
+    kv.gemv.skip = m->xres_skip;
+    m->phases.push_back(kv);
+    Phase at;
+    if (int rc = attn_phase(m, l, true, 3, at)) return rc;
+    m->phases.push_back(at);
+    float ag = 0.f, fg = 0.f;
+    if (int rc = read_scalar(m, p + "attention_gate", ag)) return rc;
+    if (int rc = read_scalar(m, p + "ffn_gate", fg)) return rc;
+    Phase o = gemv_phase(l, m->attn_out, nullptr, 0.f);
+    o.gemv.nseg = 1;
+    o.gemv.seg[0] = segment(tensor(m, p + "o"));
+    o.gemv.epilogue = EPI_RESIDUAL_KEEP;
+    o.gemv.scale = c.residual_scale * ag;
+    o.gemv.x = m->x;
+    o.gemv.skip = m->xres_skip;
+    m->phases.push_back(o);
+    Phase dn = gemv_phase(l, m->ffn, nullptr, 0.f);
+    dn.gemv.in_back = 4;
+    dn.gemv.nseg = 1;
+    dn.gemv.seg[0] = segment(tensor(m, p + "ffn.down"));
+    dn.gemv.epilogue = EPI_RESIDUAL;
+    dn.gemv.scale = c.residual_scale * fg;
+    dn.gemv.x = m->x;
+    dn.gemv.skip = m->xres_skip;
+    m->phases.push_back(dn);
+    return MR_OK;
+}
+
 int build_plan(mr_model *m) {
     const mr_model_config &c = m->cfg;
-    if (!is_gqa_family(c.family))
+    if (!is_engine_family(c))
         return set_error(MR_ERR_ARGUMENT, "family %d is not supported by this engine build yet", c.family);
     m->phases.clear();
     const TensorSlot *embed = tensor(m, "embed");
     for (int l = 0; l < c.layers; ++l) {
+        if (is_lighting_ring(c)) {
+            if (int rc = plan_lighting_layer(m, l)) return rc;
+            continue;
+        }
         const std::string p = "layers." + std::to_string(l) + ".";
         // 1. RMSNorm(x) -> q, k, v (layer 0 reads the embedding row directly)
         Phase qkv = gemv_phase(l, m->x, tensor(m, p + "a_norm"), c.norm_eps);
@@ -315,31 +463,7 @@ int build_plan(mr_model *m) {
         m->phases.push_back(qkv);
         // 2. attention
         Phase at{};
-        at.kind = PH_ATTN_GQA;
-        at.layer = l;
-        AttnPhase &a = at.attn;
-        a.q_raw = m->q_raw;
-        a.k_raw = m->k_raw;
-        a.v_raw = m->v_raw;
-        a.qk_norm = c.qk_norm;
-        if (c.qk_norm) {
-            const TensorSlot *qn = tensor(m, p + "q_norm"), *kn = tensor(m, p + "k_norm");
-            if (qn->dtype != kn->dtype) return set_error(MR_ERR_ARGUMENT, "q_norm/k_norm dtypes differ");
-            a.q_gain = qn->ptr;
-            a.k_gain = kn->ptr;
-            a.gain_dtype = qn->dtype;
-        }
-        a.norm_eps = c.norm_eps;
-        a.heads = c.query_heads;
-        a.kv_heads = m->layer_kvh[l];
-        a.dim = c.head_dim;
-        a.split_half = c.split_half_rope;
-        a.inv_freq = m->d_inv_freq;
-        a.k_cache = m->k_cache[l];
-        a.v_cache = m->v_cache[l];
-        a.capacity = m->cache_capacity[l];
-        a.partial = m->partial;
-        a.out = m->attn_out;
+        if (int rc = attn_phase(m, l, c.qk_norm, 1, at)) return rc;
         m->phases.push_back(at);
         // 3. o projection of the attention output + residual (model.py:282)
         Phase o = gemv_phase(l, m->attn_out, nullptr, 0.f);
@@ -678,6 +802,7 @@ void setup_prefill(mr_model *m) {
     const mr_model_config &c = m->cfg;
     const int d = c.head_dim, q = c.query_heads * d;
     m->prefill_ok = false;
+    if (!is_gqa_family(c.family)) return;
     const int gq_max = c.query_heads / *std::min_element(m->layer_kvh.begin(), m->layer_kvh.end());
     if (c.hidden_size % 8 || q % 8 || c.ffn_dim % 8 || d % 4 || gq_max > 32) return;
     auto bf16 = [&](const std::string &name) {
@@ -919,7 +1044,7 @@ int mr_model_finalize(mr_model *m) {
     for (auto &kv : m->tensors)
         if (!kv.second.ptr || kv.second.dtype < 0)
             return set_error(MR_ERR_ARGUMENT, "Missing tensor %s", kv.first.c_str());
-    if (!is_gqa_family(m->cfg.family)) {
+    if (!is_engine_family(m->cfg)) {
         // resident weights only; the host drives the op kernels (tensor_ops.cu)
         m->op_path = true;
         m->finalized = true;
@@ -965,6 +1090,7 @@ int mr_model_finalize(mr_model *m) {
         const size_t o_x = take(sizeof(Word) * c.hidden_size), o_q = take(sizeof(Word) * H * d),
                      o_k = take(sizeof(Word) * max_kvh * d), o_v = take(sizeof(Word) * max_kvh * d),
                      o_f = take(sizeof(Word) * c.ffn_dim), o_a = take(sizeof(Word) * H * d),
+                     o_lat = take(sizeof(Word) * std::max(1, c.latent_dim)),
                      o_p = take(sizeof(Word) * H * kMaxAttnChunks * (d + 2)),
                      o_l = take(sizeof(float) * 64 * (size_t)c.vocab_size), o_b = take(sizeof(Word) * 4 * kMaxRanks);
         m->arena = static_cast<char *>(device_alloc(m, off, &rc));
@@ -976,6 +1102,7 @@ int mr_model_finalize(mr_model *m) {
         m->k_raw = reinterpret_cast<Word *>(m->arena + o_k);
         m->v_raw = reinterpret_cast<Word *>(m->arena + o_v);
         m->ffn = reinterpret_cast<Word *>(m->arena + o_f);
+        m->latent = reinterpret_cast<Word *>(m->arena + o_lat);
         m->attn_out = reinterpret_cast<Word *>(m->arena + o_a);
         m->partial = reinterpret_cast<Word *>(m->arena + o_p);
         m->logits = reinterpret_cast<float *>(m->arena + o_l);
@@ -990,8 +1117,9 @@ int mr_model_finalize(mr_model *m) {
     m->v_cache.resize(c.layers);
     m->cache_capacity.resize(c.layers);
     for (int l = 0; l < c.layers; ++l) {
-        // model.py:105: capacity = min(window or context, context)
-        const int w = m->layer_window[l];
+        // model.py:105: capacity = min(window or context, context); FlashLighting's
+        // window applies to every layer (model.py:167)
+        const int w = is_lighting_ring(c) ? c.window : m->layer_window[l];
         const int cap = std::min(w > 0 ? w : c.context_length, c.context_length);
         m->cache_capacity[l] = cap;
         const size_t n = (size_t)m->layer_kvh[l] * cap * d;
@@ -1042,7 +1170,7 @@ int mr_model_set_tensor_parallel(mr_model *m, int rank, int ranks) {
     MR_REQUIRE(!m->finalized, "tensor parallelism is set before mr_model_finalize");
     MR_REQUIRE(ranks >= 1 && ranks <= kMaxRanks && rank >= 0 && rank < ranks, "rank %d of %d ranks (at most %d)",
                rank, ranks, kMaxRanks);
-    MR_REQUIRE(ranks == 1 || is_gqa_family(m->cfg.family), "tensor parallelism needs a decode-engine family");
+    MR_REQUIRE(ranks == 1 || is_engine_family(m->cfg), "tensor parallelism needs a decode-engine family");
     m->rank = rank;
     m->ranks = ranks;
     return MR_OK;
@@ -1184,16 +1312,26 @@ int mr_model_layer_state(const mr_model *m, int layer, int loop, mr_layer_state 
     out->ring_capacity = cap;
     out->ring_length = std::min(m->position, cap);
     out->ring_start = (m->position - out->ring_length) % cap;
+    if (is_lighting_ring(m->cfg)) {  // the latent cache after this step's compaction (drop path)
+        out->latent_rows = out->ring_length;
+        out->memory_size = 0;
+    }
     return MR_OK;
 }
 
 int mr_model_latent_positions(const mr_model *m, int layer, int *out, int capacity, int *rows) {
     MR_REQUIRE(m && rows, "NULL argument");
-    (void)layer;
-    (void)out;
-    (void)capacity;
+    MR_REQUIRE(layer >= 0 && layer < m->cfg.layers, "layer out of range");
     *rows = 0;
-    return set_error(MR_ERR_ARGUMENT, "model has no latent cache");
+    if (!m->finalized || m->op_path || !is_lighting_ring(m->cfg))
+        return set_error(MR_ERR_ARGUMENT, "model has no latent cache");
+    // the drop path keeps the newest rows, each at its own token position
+    const int n = std::min(m->position, m->cache_capacity[layer]);
+    MR_REQUIRE(out || n == 0, "NULL argument");
+    MR_REQUIRE(capacity >= n, "positions buffer holds %d rows, need %d", capacity, n);
+    for (int i = 0; i < n; ++i) out[i] = m->position - n + i;
+    *rows = n;
+    return MR_OK;
 }
 
 int mr_model_last_topk(const mr_model *m, int layer, int loop, int *blocks, int capacity) {

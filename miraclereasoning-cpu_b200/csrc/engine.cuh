@@ -63,6 +63,8 @@ enum Epilogue : int {
     EPI_RESIDUAL = 1,   // x[r] = x[r] + scale * y_0[r]              (kernels.cl:52-56)
     EPI_SWIGLU = 2,     // out[r] = (g/(1+exp(-g))) * u, g=y_0, u=y_1 (kernels.cl:46-50)
     EPI_LOGITS = 3,     // logits[r] = y_0[r]; running argmax
+    EPI_RESIDUAL_KEEP = 4,  // as EPI_RESIDUAL, but only this CTA's shared-memory rows are updated (a
+                            // later residual phase of the layer publishes them)
 };
 
 enum InputKind : int {
@@ -112,6 +114,7 @@ struct GemvPhase {
     int group_offset;           // bulk: this phase's group tables in StepControl::groups,
     int group_stride;           //   CTA b's g-th at group_offset + b * group_stride + g
     int skip;                   // CTAs 0 .. skip-1 own no rows of the phase (see cta_row_range)
+    int in_back;                // the input words carry the tag of the phase this many phases back
 };
 
 // Rows [r0, r1) of segment s owned by CTA b of G: the CTA's share of the
@@ -135,6 +138,7 @@ struct AttnPhase {
     Word *partial;                  // [heads][kMaxAttnChunks][dim + 2]: chunks 1.. (acc[dim], max, sum)
     Word *out;                      // [heads * dim] attention output (the o projection's input)
     int kv_lo, kv_n;                // this rank's KV heads (tensor parallel: a contiguous slice; else all)
+    int q_back;                     // the q words come from the phase this many phases back (k / v: 1)
 };
 
 // The compute warps take a bulk phase's pieces in groups, precomputed on the

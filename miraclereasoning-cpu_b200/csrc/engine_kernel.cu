@@ -197,13 +197,22 @@ __device__ __forceinline__ bool mbar_wait_sleep(unsigned long long *bar, int par
 __device__ __forceinline__ void mbar_arrive(unsigned long long *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
-__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, unsigned long long *bar) {
+// L2 policy of the weight stream: read once per step and far larger than L2,
+// it is evicted first, so that what is re-read every step (key/value rings, the
+// plan's records, exchange words) stays in L2 across steps.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, unsigned long long *bar,
+                                          uint64_t policy) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                  : "memory");
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
             smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
         : "memory");
 }
 
@@ -231,23 +240,24 @@ __device__ bool wait_bar(unsigned long long *bar, int parity, StepState *st, con
 }
 
 // Reads N exchange words at addr(0) .. addr(N - 1) (NULL: none), polling each
-// until it carries `tag`; bounded like every wait (gives up early when
-// another wait recorded an error).  Every load is issued before the first
+// until it carries its tag (tag_of(u); read_words: one tag for all);
+// bounded like every wait (gives up early when another wait recorded an error).  Every load is issued before the first
 // check; addresses are recomputed rather than held, to spare registers.
-template <int N, typename Addr>
-__device__ __forceinline__ bool read_words(Addr addr, unsigned tag, float (&out)[N], StepState *st, int phase) {
+template <int N, typename Addr, typename TagOf>
+__device__ __forceinline__ bool read_words_tagged(Addr addr, TagOf tag_of, float (&out)[N], StepState *st,
+                                                  int phase) {
     Word w[N];
 #pragma unroll
     for (int u = 0; u < N; ++u) {
         const Word *src = addr(u);
-        w[u] = src ? ld_word(src) : (static_cast<Word>(tag) << 32);
+        w[u] = src ? ld_word(src) : (static_cast<Word>(tag_of(u)) << 32);
     }
     uint64_t start = 0;
     for (unsigned spin = 0;; ++spin) {
         bool all = true;
 #pragma unroll
         for (int u = 0; u < N; ++u)
-            if (!word_ok(w[u], tag)) {
+            if (!word_ok(w[u], tag_of(u))) {
                 all = false;
                 w[u] = ld_word(addr(u));
             }
@@ -266,6 +276,10 @@ __device__ __forceinline__ bool read_words(Addr addr, unsigned tag, float (&out)
 #pragma unroll
     for (int u = 0; u < N; ++u) out[u] = word_value(w[u]);
     return true;
+}
+template <int N, typename Addr>
+__device__ __forceinline__ bool read_words(Addr addr, unsigned tag, float (&out)[N], StepState *st, int phase) {
+    return read_words_tagged(addr, [tag](int) { return tag; }, out, st, phase);
 }
 
 // ---- the weight-stream producer (lane 0 of warp 16) -----------------------------------
@@ -292,6 +306,7 @@ __device__ void produce(const StepControl &ctl, bool need_head, int head_phase, 
           q3 = ld_desc(table, 3, count);
     int tail = 0, head_off = 0, issued = 0;
     bool ok = true;
+    const uint64_t policy = l2_evict_first();
     while (ok && issued < count) {
         const uint4 d = q0;
         q0 = q1;
@@ -334,7 +349,7 @@ __device__ void produce(const StepControl &ctl, bool need_head, int head_phase, 
         c.offset[slot] = off;
         // the region was last read through the generic proxy
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        bulk_load(sm.ring + off, src, static_cast<uint32_t>(bytes), &c.full[slot]);
+        bulk_load(sm.ring + off, src, static_cast<uint32_t>(bytes), &c.full[slot], policy);
         head_off = off + bytes;
         ++issued;
     }
@@ -659,7 +674,7 @@ __device__ bool read_input(const GemvPhase &g, int cols, const StepInfo &info, i
             put(j, load_weight(g.embed, g.embed_dtype, static_cast<size_t>(info.token) * cols + j));
         return true;
     }
-    const unsigned tag = info.tag_base + p - 1;
+    const unsigned tag = info.tag_base + p - g.in_back;
     bool ok = true;
     for (int base = 0; base < cols && ok; base += 4 * count) {
         float v[4];
@@ -701,10 +716,11 @@ __device__ __forceinline__ void finish_row(const GemvPhase &g, int s, int r, flo
     const unsigned tag = info.tag_base + p;
     switch (g.epilogue) {
         case EPI_STORE: st_word_all(c, g.seg[s].out + r, val, tag); break;
-        case EPI_RESIDUAL: {  // model.py:282-283; x rows of this CTA live in shared memory
+        case EPI_RESIDUAL:  // model.py:282-283; x rows of this CTA live in shared memory
+        case EPI_RESIDUAL_KEEP: {
             const float xn = __fadd_rn(c.xres[r - info.xr0], __fmul_rn(g.scale, val));
             c.xres[r - info.xr0] = xn;
-            st_word_all(c, g.x + r, xn, tag);
+            if (g.epilogue == EPI_RESIDUAL) st_word_all(c, g.x + r, xn, tag);
             break;
         }
         case EPI_LOGITS: {
@@ -1306,6 +1322,7 @@ __device__ bool attn_gqa_phase_t(const AttnPhase &a, const StepInfo &info, int p
     const float sqrt_d = __fsqrt_rn(static_cast<float>(d));  // divisor, kernels.cl:72
     const int stride = d + 2;
     const unsigned in_tag = info.tag_base + ph - 1, out_tag = info.tag_base + ph;
+    const unsigned q_tag = info.tag_base + ph - a.q_back;
 
     const AttnLayout L = attn_layout(gq, d);
     float *q = sm.attn + L.q, *knew = sm.attn + L.knew, *vnew = sm.attn + L.vnew;
@@ -1335,7 +1352,7 @@ __device__ bool attn_gqa_phase_t(const AttnPhase &a, const StepInfo &info, int p
         const int nq = gq * d, nread = nq + (owner ? 2 * d : 0);
         for (int base = 0; base < nread && ok; base += 4 * kEngineThreads) {
             float v[4];
-            ok = read_words(
+            ok = read_words_tagged(
                 [&](int u) -> const Word * {
                     const int e = base + u * kEngineThreads + threadIdx.x;
                     return e >= nread ? nullptr
@@ -1343,7 +1360,8 @@ __device__ bool attn_gqa_phase_t(const AttnPhase &a, const StepInfo &info, int p
                            : e < nq + d ? a.k_raw + static_cast<size_t>(g) * d + (e - nq)
                                         : a.v_raw + static_cast<size_t>(g) * d + (e - nq - d);
                 },
-                in_tag, v, st, ph);
+                [&](int u) { return base + u * kEngineThreads + static_cast<int>(threadIdx.x) < nq ? q_tag : in_tag; },
+                v, st, ph);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int e = base + u * kEngineThreads + threadIdx.x;

@@ -11,9 +11,11 @@ What runs underneath is different: the checkpoint's stored bytes are copied
 once into HBM (no LRU, no host widening).  For the grouped-query families
 (flashnano-1.5/1.7, FlashLite) each token is one launch of the persistent
 decode kernel (csrc/engine_kernel.cu) and greedy ``generate`` runs entirely on
-the device (argmax feeds the next step).  flashnano-1.6, FlashLighting and
-Heavy Medium step on the host over the op kernels against the resident
-weights (stepper.py).  Sampled ``generate`` reads the logits each step and
+the device (argmax feeds the next step).  FlashLighting without memory slots
+runs on the same kernel (its latent cache as a key/value ring, see
+``engine_plans``).  flashnano-1.6, FlashLighting with memory slots and Heavy
+Medium step on the host over the op kernels against the resident weights
+(stepper.py).  Sampled ``generate`` reads the logits each step and
 samples on the host with the reference's exact NumPy procedure.
 """
 from __future__ import annotations
@@ -84,6 +86,35 @@ class LatentView:
         self.shape = (rows, width)
 
 
+def engine_plans(config):
+    """Whether the persistent decode kernel runs this model: the grouped-query
+    families, and FlashLighting without memory slots (its latent cache then
+    only drops the oldest row, which the engine keeps as a key/value ring)."""
+    if config.family not in HOST_STEPPED:
+        return True
+    return config.family == "flashlighting-2.0" and config.memory_slots == 0 and bool(config.window)
+
+
+class RingDecisions:
+    """FlashLighting's per-token latent decisions on the engine's ring (drop
+    path): after the step at position p every layer keeps the latents of
+    positions max(0, p + 1 - window) .. p and no memory rows.  Built on
+    demand, in the stepper's format (one list per token of one dict per layer)."""
+
+    def __init__(self, model):
+        self._model = model
+
+    def __len__(self):
+        return self._model.position
+
+    def __getitem__(self, t):
+        if not 0 <= t < len(self):
+            raise IndexError(t)
+        c = self._model.config
+        kept = list(range(max(0, t + 1 - c.window), t + 1))
+        return [{"latent_positions": [list(kept)], "memory_size": [0]} for _ in range(c.layers)]
+
+
 class MiracleModel:
     """FP32 next-token engine for six Miracle architectures on one B200.
 
@@ -133,7 +164,7 @@ class MiracleModel:
         _native.call("mr_model_weight_bytes", self._handle, C.byref(used))
         self.weight_cache = ResidentWeights(int(used.value), weight_cache_bytes)
         self.frequencies = backend.upload(inv)
-        self._stepper = OpStepper(self) if config.family in HOST_STEPPED else None
+        self._stepper = None if engine_plans(config) else OpStepper(self)
         self.reset()
 
     def __del__(self):
@@ -218,7 +249,9 @@ class MiracleModel:
     def decisions(self):
         """Per token and layer, the discrete choices of the host-stepped families
         (heavy top-k blocks, MoE experts and weights, latent positions)."""
-        return self._stepper.decisions if self._stepper is not None else []
+        if self._stepper is not None:
+            return self._stepper.decisions
+        return RingDecisions(self) if self.config.family == "flashlighting-2.0" else []
 
     @property
     def states(self):
@@ -245,6 +278,7 @@ class MiracleModel:
                     entry["latent"] = LatentView(st.latent_rows, c.latent_dim)
                     entry["memory_size"] = st.memory_size
                     entry["positions"] = self._latent_positions(layer, st.latent_rows)
+                    entry["counts"] = [1.0] * st.latent_rows  # each kept row stands for one token
                 else:
                     entry["ring"] = RingView(st.ring_count, st.ring_capacity, st.ring_length, st.ring_start, width)
                     if c.family == "flashnano-1.6" and st.relay_count:
