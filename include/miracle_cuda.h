@@ -245,6 +245,10 @@ MR_API int mr_model_latent_positions(const mr_model *model, int layer, int *out,
 MR_API int mr_model_last_topk(const mr_model *model, int layer, int loop, int *blocks, int capacity);
 MR_API int mr_model_last_experts(const mr_model *model, int layer, int loop, int *experts,
                                  float *weights, int capacity);
+/* heavy-medium-2.0: float32 log1p(d) for d = 0 .. context_length-1, computed by
+ * the host (the reference's distance penalty applies NumPy's float32 log1p,
+ * model.py:221-222).  Required before the first token. */
+MR_API int mr_model_set_log1p_table(mr_model *model, const float *values, int n);
 
 /* Benchmark helper: run `steps` greedy decode steps back to back on the
  * device (each step's token = previous argmax), starting from the current

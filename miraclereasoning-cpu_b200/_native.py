@@ -96,6 +96,7 @@ SIGNATURES = {
     "mr_model_latent_positions": (_I, [_P, _I, _IP, _I, _IP]),
     "mr_model_last_topk": (_I, [_P, _I, _I, _IP, _I]),
     "mr_model_last_experts": (_I, [_P, _I, _I, _IP, _FP, _I]),
+    "mr_model_set_log1p_table": (_I, [_P, _FP, _I]),
     "mr_model_bench_decode": (_I, [_P, _I, _I, _FP]),
     "mr_model_trace_decode": (_I, [_P, _I, C.POINTER(C.c_uint64), _I, _IP, _IP]),
     "mr_attention_static_scratch": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I]),

@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "engine.cuh"
+#include "heavy.cuh"
 #include "prefill.cuh"
 
 namespace mr {
@@ -109,6 +110,7 @@ struct mr_model {
     bool finalized = false;
     bool failed = false;
     bool op_path = false;  // no decode plan: the token step runs on the host over the op kernels
+    HeavyEngine *heavy = nullptr;  // heavy-medium-2.0: the token step as kernel launches (heavy.cu)
     int position = 0;
     int grid = 0;
     // device buffers
@@ -791,6 +793,41 @@ int ready(mr_model *m) {
     return MR_OK;
 }
 
+int host_argmax(const float *v, int n) {  // numpy.argmax: the first maximum
+    int best = 0;
+    for (int i = 1; i < n; ++i)
+        if (v[i] > v[best]) best = i;
+    return best;
+}
+
+// heavy-medium-2.0: n tokens through the device token step; the logits of
+// every token (return_all) or of the last one are copied to `out`.
+int heavy_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
+    const int V = m->cfg.vocab_size;
+    for (int i = 0; i < n; ++i) MR_REQUIRE(ids[i] >= 0 && ids[i] < V, "input token is outside the vocabulary");
+    MR_REQUIRE(m->position + n <= m->cfg.context_length,
+               "input would exceed context_length; reset or allocate a larger context");
+    for (int i = 0; i < n; ++i) {
+        int rc = heavy_token(m->heavy, ids[i], m->position);
+        if (!rc && (return_all || i == n - 1)) {
+            const cudaError_t err = cudaMemcpyAsync(out + (return_all ? (size_t)i * V : 0), heavy_logits(m->heavy),
+                                                    sizeof(float) * V, cudaMemcpyDeviceToHost, m->ctx->stream);
+            if (err != cudaSuccess) rc = cuda_error(err, "logits read");
+        }
+        if (rc) {
+            m->failed = true;
+            return rc;
+        }
+        ++m->position;
+    }
+    const cudaError_t err = cudaStreamSynchronize(m->ctx->stream);
+    if (err != cudaSuccess) {
+        m->failed = true;
+        return cuda_error(err, "heavy-medium-2.0 token step");
+    }
+    return MR_OK;
+}
+
 // Runs n fed tokens starting at the current position; logits of the selected
 // rows are copied to `out` (return_all: n rows, else the last row only).
 constexpr int kPrefillChunk = 512;  // tokens per batched prefill chunk
@@ -996,6 +1033,7 @@ int mr_model_destroy(mr_model *m) {
         if (m->peer_open[j]) cudaIpcCloseMemHandle(m->peer[j]);
     for (void *p : m->allocations) cudaFree(p);
     prefill_release(m->pw);
+    heavy_destroy(m->heavy);
     if (m->ev0) cudaEventDestroy(m->ev0);
     if (m->ev1) cudaEventDestroy(m->ev1);
     mr_context *ctx = m->ctx;
@@ -1044,6 +1082,15 @@ int mr_model_finalize(mr_model *m) {
     for (auto &kv : m->tensors)
         if (!kv.second.ptr || kv.second.dtype < 0)
             return set_error(MR_ERR_ARGUMENT, "Missing tensor %s", kv.first.c_str());
+    if (m->cfg.family == MR_FAMILY_HEAVY_MEDIUM_20) {
+        m->finalized = true;  // the tensors are complete: heavy_create reads them by name
+        const int rc = heavy_create(m, m->cfg, m->ctx->stream, m->inv_freq.data(), &m->heavy);
+        if (rc) {
+            m->finalized = false;
+            return rc;
+        }
+        return mr_model_reset(m);
+    }
     if (!is_engine_family(m->cfg)) {
         // resident weights only; the host drives the op kernels (tensor_ops.cu)
         m->op_path = true;
@@ -1220,7 +1267,7 @@ int mr_model_reset(mr_model *m) {
     MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
     if (!m->finalized) return set_error(MR_ERR_STATE, "model is not finalized");
     MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
-    if (!m->op_path) MR_CUDA_TRY(cudaMemset(m->state, 0, sizeof(StepState)));
+    if (!m->op_path && !m->heavy) MR_CUDA_TRY(cudaMemset(m->state, 0, sizeof(StepState)));
     m->position = 0;
     m->failed = false;
     return MR_OK;
@@ -1243,6 +1290,14 @@ int mr_model_weight_bytes(const mr_model *m, uint64_t *bytes) {
 int mr_model_step(mr_model *m, int token, float *logits_out, int *argmax_out) {
     int rc = ready(m);
     if (rc) return rc;
+    if (m->heavy) {
+        std::vector<float> row(m->cfg.vocab_size);
+        rc = heavy_feed(m, &token, 1, 0, row.data());
+        if (rc) return rc;
+        if (logits_out) memcpy(logits_out, row.data(), sizeof(float) * row.size());
+        if (argmax_out) *argmax_out = host_argmax(row.data(), (int)row.size());
+        return MR_OK;
+    }
     rc = run_feed(m, &token, 1, 0, logits_out);
     if (rc) return rc;
     if (argmax_out) {
@@ -1257,6 +1312,7 @@ int mr_model_prefill(mr_model *m, const int *ids, int n, int return_all, float *
     int rc = ready(m);
     if (rc) return rc;
     MR_REQUIRE(ids && n > 0, "input_ids must be a non-empty 1D integer sequence");
+    if (m->heavy) return heavy_feed(m, ids, n, return_all, out);
     return run_feed(m, ids, n, return_all, out);
 }
 
@@ -1270,6 +1326,24 @@ int mr_model_generate_greedy(mr_model *m, const int *ids, int n, int max_new, in
     for (int i = 0; i < n; ++i) MR_REQUIRE(ids[i] >= 0 && ids[i] < V, "input token is outside the vocabulary");
     MR_REQUIRE(m->position + n + max_new - 1 <= m->cfg.context_length,
                "prompt plus requested generation exceeds context_length");
+    if (m->heavy) {  // greedy on the host over the device token step (model.py:318-357)
+        std::vector<float> row(V);
+        *out_count = 0;
+        *out_nonfinite = 0;
+        rc = heavy_feed(m, ids, n, 0, row.data());
+        for (int i = 0; !rc && i < max_new; ++i) {
+            for (float v : row)
+                if (!std::isfinite(v)) {
+                    *out_nonfinite = 1;
+                    return MR_OK;
+                }
+            const int token = host_argmax(row.data(), V);
+            out_tokens[(*out_count)++] = token;
+            if (token == eos || i + 1 == max_new) break;
+            rc = heavy_feed(m, &token, 1, 0, row.data());
+        }
+        return rc;
+    }
     rc = ensure_feed(m, n);
     if (!rc) rc = ensure_gen(m, max_new);
     if (rc) return rc;
@@ -1307,7 +1381,7 @@ int mr_model_layer_state(const mr_model *m, int layer, int loop, mr_layer_state 
     memset(out, 0, sizeof(*out));
     out->present = m->position > 0;
     if (!out->present || !m->finalized) return MR_OK;
-    const int cap = m->cache_capacity[layer];
+    const int cap = m->heavy ? m->cfg.context_length : m->cache_capacity[layer];
     out->ring_count = m->position;
     out->ring_capacity = cap;
     out->ring_length = std::min(m->position, cap);
@@ -1335,22 +1409,26 @@ int mr_model_latent_positions(const mr_model *m, int layer, int *out, int capaci
 }
 
 int mr_model_last_topk(const mr_model *m, int layer, int loop, int *blocks, int capacity) {
-    (void)layer;
-    (void)loop;
-    (void)blocks;
-    (void)capacity;
-    MR_REQUIRE(m, "NULL argument");
-    return set_error(MR_ERR_ARGUMENT, "model has no sparse block attention");
+    MR_REQUIRE(m && blocks, "NULL argument");
+    if (!m->heavy) return set_error(MR_ERR_ARGUMENT, "model has no sparse block attention");
+    MR_REQUIRE(layer >= 0 && layer < m->cfg.layers && loop >= 0 && loop < std::max(1, m->cfg.inner_loop_steps),
+               "layer / loop out of range");
+    return heavy_last_topk(m->heavy, layer, loop, blocks, capacity);
 }
 
 int mr_model_last_experts(const mr_model *m, int layer, int loop, int *experts, float *weights, int capacity) {
-    (void)layer;
-    (void)loop;
-    (void)experts;
-    (void)weights;
-    (void)capacity;
-    MR_REQUIRE(m, "NULL argument");
-    return set_error(MR_ERR_ARGUMENT, "model has no experts");
+    MR_REQUIRE(m && experts && weights, "NULL argument");
+    if (!m->heavy) return set_error(MR_ERR_ARGUMENT, "model has no experts");
+    MR_REQUIRE(layer >= 0 && layer < m->cfg.layers && loop >= 0 && loop < std::max(1, m->cfg.inner_loop_steps),
+               "layer / loop out of range");
+    return heavy_last_experts(m->heavy, layer, loop, experts, weights, capacity);
+}
+
+int mr_model_set_log1p_table(mr_model *m, const float *values, int n) {
+    MR_REQUIRE(m && values, "NULL argument");
+    if (!m->heavy) return set_error(MR_ERR_ARGUMENT, "model has no sparse block attention");
+    MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
+    return heavy_set_log1p(m->heavy, values, n);
 }
 
 int mr_model_trace_decode(mr_model *m, int token, uint64_t *stamps, int capacity, int *phases, int *grid) {

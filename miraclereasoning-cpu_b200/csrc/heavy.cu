@@ -1,0 +1,884 @@
+// Heavy Medium 2.0 token step on the device (miracle_reasoning/model.py:
+// 192-285): latent sparse attention with top-k global blocks, then the
+// adaptive mixture of experts, two inner loops per layer, with every discrete
+// decision taken on the GPU.  One call runs a token end to end from the host
+// with kernel launches only: no host round trip inside a step.
+//
+// Per (layer, inner loop):
+//   1. h = RMSNorm(x, a_norm)                                    k_rms_row
+//   2. q = W_q h, latent = W_latent h                            k_gemv (two segments)
+//   3. kv = W_kv_up latent                                       k_gemv
+//   4. q = RoPE(RMSNorm_noaffine(q)); k = RoPE(RMSNorm_noaffine(kv[:w]));
+//      append k, v = kv[w:] to the loop's ring                   k_heads_norm_rope
+//   5. mean key / value of the newest block (older blocks' means
+//      never change once full)                                   k_block_mean_last
+//   6. scores over the local window and every block mean        k_sparse_scores
+//   7. block columns minus the distance penalty, stable top
+//      `global_slots` per head, the rest masked (model.py:219-225) k_block_topk
+//   8. softmax + value mix over window rows and kept blocks     k_sparse_attend
+//   9. x += s * W_o attended                                     k_gemv (residual)
+//  10. f = RMSNorm(x, f_norm); router logits                     k_rms_row, k_gemv
+//  11. routing (model.py:235-250): biases, temperature, softmax,
+//      stable top-k, confidence / entropy -> active count,
+//      renormalised weights                                      k_route
+//  12. the chosen experts and the shared experts, batched:
+//      SwiGLU(gate, up), then down                               k_expert_gate_up, k_expert_down
+//  13. result = sum in rank order, shared experts at
+//      residual_scale / S; x += s * result                       k_expert_combine
+//
+// Arithmetic: the discrete decisions follow the reference's float32
+// expressions in the reference's order (block means as running sums, the
+// distance penalty from a table of NumPy's own float32 log1p values supplied
+// by the host, the router softmax as one running sum, NumPy's pairwise
+// summation for the routing entropy and the weight renormalisation, stable
+// ordering with ties to the lower index).  The projections and attention sums
+// are float32 with their own summation order, so logits agree with the
+// reference within the parity tolerance and decisions agree except where the
+// reference's own values tie within rounding.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "heavy.cuh"
+
+namespace mr {
+
+int model_tensor(mr_model *m, const char *name, const void **ptr, int *dtype, int64_t *rows, int64_t *cols);
+
+namespace {
+
+constexpr int kGemvThreads = 256;            // 8 warps
+constexpr int kRowsPerWarp = 2;
+constexpr int kGemvRows = 8 * kRowsPerWarp;  // rows per block
+constexpr int kMaxSegs = 4;
+
+#define FADD __fadd_rn
+#define FMUL __fmul_rn
+
+__device__ __forceinline__ uint4 ld_stream16(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// 16 bytes of weights (8 BF16 / F16 or 4 F32) dotted with the matching x.
+__device__ __forceinline__ float dot16(const uint4 &w, const float *x, int dtype) {
+    if (dtype == MR_DTYPE_F32) {
+        const float4 a = *reinterpret_cast<const float4 *>(x);
+        return __uint_as_float(w.x) * a.x + __uint_as_float(w.y) * a.y + __uint_as_float(w.z) * a.z +
+               __uint_as_float(w.w) * a.w;
+    }
+    const float4 a = *reinterpret_cast<const float4 *>(x), b = *reinterpret_cast<const float4 *>(x + 4);
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+    float lo[4], hi[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (dtype == MR_DTYPE_BF16) {
+            lo[i] = __uint_as_float(u[i] << 16);
+            hi[i] = __uint_as_float(u[i] & 0xffff0000u);
+        } else {
+            lo[i] = __half2float(__ushort_as_half(static_cast<uint16_t>(u[i] & 0xffffu)));
+            hi[i] = __half2float(__ushort_as_half(static_cast<uint16_t>(u[i] >> 16)));
+        }
+    }
+    float s = lo[0] * a.x;
+    s = fmaf(hi[0], a.y, s);
+    s = fmaf(lo[1], a.z, s);
+    s = fmaf(hi[1], a.w, s);
+    s = fmaf(lo[2], b.x, s);
+    s = fmaf(hi[2], b.y, s);
+    s = fmaf(lo[3], b.z, s);
+    s = fmaf(hi[3], b.w, s);
+    return s;
+}
+
+// One warp: dot products of two rows (cols elements of `dtype` at p0, p1;
+// p1 NULL: one row) with x (shared memory); every lane gets the sums.
+__device__ __forceinline__ void warp_dot2(const char *p0, const char *p1, int dtype, int cols, const float *x,
+                                          float &y0, float &y1) {
+    const int lane = threadIdx.x & 31;
+    const int esz = dtype == MR_DTYPE_F32 ? 4 : 2, per = 16 / esz;
+    const size_t row_bytes = static_cast<size_t>(cols) * esz;
+    const bool two = p1 != nullptr;
+    if (!two) p1 = p0;
+    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+    if ((row_bytes & 15) == 0) {
+        const int nv = cols / per;
+        int c = lane;
+        if (two) {
+            for (; c + 32 < nv; c += 64) {
+                const uint4 w00 = ld_stream16(p0 + 16 * c), w01 = ld_stream16(p0 + 16 * (c + 32));
+                const uint4 w10 = ld_stream16(p1 + 16 * c), w11 = ld_stream16(p1 + 16 * (c + 32));
+                a0 += dot16(w00, x + per * c, dtype);
+                b0 += dot16(w01, x + per * (c + 32), dtype);
+                a1 += dot16(w10, x + per * c, dtype);
+                b1 += dot16(w11, x + per * (c + 32), dtype);
+            }
+            if (c < nv) {
+                a0 += dot16(ld_stream16(p0 + 16 * c), x + per * c, dtype);
+                a1 += dot16(ld_stream16(p1 + 16 * c), x + per * c, dtype);
+            }
+        } else {
+            for (; c + 96 < nv; c += 128) {
+                const uint4 w0 = ld_stream16(p0 + 16 * c), w1 = ld_stream16(p0 + 16 * (c + 32));
+                const uint4 w2 = ld_stream16(p0 + 16 * (c + 64)), w3 = ld_stream16(p0 + 16 * (c + 96));
+                a0 += dot16(w0, x + per * c, dtype);
+                b0 += dot16(w1, x + per * (c + 32), dtype);
+                a1 += dot16(w2, x + per * (c + 64), dtype);
+                b1 += dot16(w3, x + per * (c + 96), dtype);
+            }
+            for (; c < nv; c += 32) a0 += dot16(ld_stream16(p0 + 16 * c), x + per * c, dtype);
+            a0 = (a0 + b0) + (a1 + b1);
+            a1 = b0 = b1 = 0.f;
+        }
+    } else {  // rows that are not whole 16-byte chunks: element by element
+        for (int j = lane; j < cols; j += 32) {
+            a0 = fmaf(load_weight(p0, dtype, j), x[j], a0);
+            if (two) a1 = fmaf(load_weight(p1, dtype, j), x[j], a1);
+        }
+    }
+    y0 = warp_sum(a0 + b0);
+    y1 = warp_sum(a1 + b1);
+}
+
+struct GemvSeg {
+    const void *w;
+    int dtype, rows, cols;
+    const float *x;
+    float *y;
+    int residual;  // y = y + scale * (W x) (kernels.cl add), else y = W x
+    float scale;
+};
+struct GemvArgs {
+    GemvSeg s[kMaxSegs];
+    int first[kMaxSegs + 1];  // first block of each segment
+    int nseg;
+};
+
+// y = W x for up to kMaxSegs matrices; each block takes kGemvRows rows of one
+// segment and stages that segment's x in shared memory.
+__global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a) {
+    extern __shared__ __align__(16) float xs[];
+    int si = 0;
+    while (si + 1 < a.nseg && static_cast<int>(blockIdx.x) >= a.first[si + 1]) ++si;
+    const GemvSeg &s = a.s[si];
+    for (int i = threadIdx.x; i < s.cols; i += blockDim.x) xs[i] = s.x[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = (blockIdx.x - a.first[si]) * kGemvRows + warp * kRowsPerWarp;
+    if (r0 >= s.rows) return;
+    const int r1 = r0 + 1 < s.rows ? r0 + 1 : -1;
+    const size_t row_bytes = static_cast<size_t>(s.cols) * (s.dtype == MR_DTYPE_F32 ? 4 : 2);
+    const char *base = static_cast<const char *>(s.w);
+    float y0, y1;
+    warp_dot2(base + r0 * row_bytes, r1 >= 0 ? base + r1 * row_bytes : nullptr, s.dtype, s.cols, xs, y0, y1);
+    if (lane == 0) {
+        if (s.residual) {
+            s.y[r0] = FADD(s.y[r0], FMUL(s.scale, y0));
+            if (r1 >= 0) s.y[r1] = FADD(s.y[r1], FMUL(s.scale, y1));
+        } else {
+            s.y[r0] = y0;
+            if (r1 >= 0) s.y[r1] = y1;
+        }
+    }
+}
+
+// y = (x * (1 / sqrt(mean(x^2) + eps))) * gain (kernels.cl:19-28), one row, one block.
+__global__ void k_rms_row(const float *x, const void *gain, int gain_dtype, float *y, int width, float eps) {
+    __shared__ float red[32];
+    float ss = 0.f;
+    for (int j = threadIdx.x; j < width; j += blockDim.x) ss = fmaf(x[j], x[j], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(FADD(__fdiv_rn(red[0], static_cast<float>(width)), eps)));
+    for (int j = threadIdx.x; j < width; j += blockDim.x) {
+        const float g = gain ? load_weight(gain, gain_dtype, j) : 1.0f;
+        y[j] = FMUL(FMUL(x[j], scale), g);
+    }
+}
+
+__global__ void k_embed_row(const void *embed, int dtype, int token, int width, float *x) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < width; j += gridDim.x * blockDim.x)
+        x[j] = load_weight(embed, dtype, static_cast<size_t>(token) * width + j);
+}
+
+// One warp per head: q heads (blocks 0 .. H-1) and key heads (H .. H+KVH-1):
+// non-affine RMSNorm (eps 1e-6, model.py:194, 201) then RoPE at `position`
+// (kernels.cl:30-44); keys and values go to ring row `row`.
+__global__ void k_heads_norm_rope(float *q, const float *kv, float *k_ring, float *v_ring, const float *inv_freq,
+                                  int heads, int kv_heads, int dim, int split_half, int position, int row) {
+    const int h = blockIdx.x, lane = threadIdx.x;
+    const int width = kv_heads * dim;
+    float *dst;
+    const float *src;
+    if (h < heads) {
+        src = q + static_cast<size_t>(h) * dim;
+        dst = q + static_cast<size_t>(h) * dim;
+    } else {
+        const int kh = h - heads;
+        src = kv + static_cast<size_t>(kh) * dim;
+        dst = k_ring + static_cast<size_t>(row) * width + static_cast<size_t>(kh) * dim;
+        for (int j = lane; j < dim; j += 32)
+            v_ring[static_cast<size_t>(row) * width + static_cast<size_t>(kh) * dim + j] = kv[width + kh * dim + j];
+    }
+    float ss = 0.f;
+    for (int j = lane; j < dim; j += 32) ss = fmaf(src[j], src[j], ss);
+    ss = warp_sum(ss);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(FADD(__fdiv_rn(ss, static_cast<float>(dim)), 1e-6f)));
+    const int half = dim / 2;
+    float u[4], v[4];
+    int n = 0;
+    for (int p = lane; p < half && n < 4; p += 32, ++n) {
+        const int j = split_half ? p : 2 * p, k = split_half ? p + half : 2 * p + 1;
+        u[n] = FMUL(src[j], scale);
+        v[n] = FMUL(src[k], scale);
+    }
+    __syncwarp();
+    n = 0;
+    for (int p = lane; p < half && n < 4; p += 32, ++n) {
+        const int j = split_half ? p : 2 * p, k = split_half ? p + half : 2 * p + 1;
+        const float angle = FMUL(static_cast<float>(position), inv_freq[p]);
+        const float c = cosf(angle), s = sinf(angle);
+        dst[j] = __fsub_rn(FMUL(u[n], c), FMUL(v[n], s));
+        dst[k] = FADD(FMUL(u[n], s), FMUL(v[n], c));
+    }
+}
+
+// Mean of the newest block's rows (kernels.cl:139-148: running sum in row
+// order, then one division) for keys and values; full blocks never change.
+__global__ void k_block_mean_last(const float *k_ring, const float *v_ring, float *k_mean, float *v_mean, int count,
+                                  int width, int block) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= 2 * width) return;
+    const int j = i % width;
+    const float *src = i < width ? k_ring : v_ring;
+    float *dst = i < width ? k_mean : v_mean;
+    const int b = (count - 1) / block, start = b * block, stop = min(start + block, count);
+    float v = 0.f;
+    for (int t = start; t < stop; ++t) v = FADD(v, src[static_cast<size_t>(t) * width + j]);
+    dst[static_cast<size_t>(b) * width + j] = __fdiv_rn(v, static_cast<float>(stop - start));
+}
+
+// scores[h][t], t < length: local ring rows start .. start+length-1; t >= length:
+// block means (kernels.cl:59-74).  One warp per score.
+__global__ void k_sparse_scores(const float *q, const float *k_ring, const float *k_mean, float *scores, int heads,
+                                int kv_heads, int dim, int start, int length, int blocks) {
+    const int total = length + blocks;
+    const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (item >= heads * total) return;
+    const int h = item / total, t = item - h * total;
+    const int kh = h / (heads / kv_heads), width = kv_heads * dim;
+    const float *kr = t < length ? k_ring + static_cast<size_t>(start + t) * width + static_cast<size_t>(kh) * dim
+                                 : k_mean + static_cast<size_t>(t - length) * width + static_cast<size_t>(kh) * dim;
+    const float *qh = q + static_cast<size_t>(h) * dim;
+    float v = 0.f;
+    for (int j = lane; j < dim; j += 32) v = fmaf(qh[j], kr[j], v);
+    v = warp_sum(v);
+    if (lane == 0) scores[static_cast<size_t>(h) * total + t] = __fdiv_rn(v, __fsqrt_rn(static_cast<float>(dim)));
+}
+
+// model.py:219-225 per head (one block): block column b loses
+// slope * log1p(position - end_b) (end_b = min((b + 1) * block - 1, position),
+// the log1p value from the host's table), the `slots` best columns (stable
+// descending order: ties go to the lower index) stay, the rest become -inf.
+// The kept block ids go to `kept` in ascending order, -1 padded to `slots_max`.
+__global__ void k_block_topk(float *scores, int total, int length, int blocks, int block, int position,
+                             const float *log1p_table, float slope, int slots, int slots_max, int *kept) {
+    extern __shared__ float sb[];
+    int *keep = reinterpret_cast<int *>(sb + blocks);
+    const int h = blockIdx.x;
+    float *row = scores + static_cast<size_t>(h) * total + length;
+    for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
+        const int end = min((b + 1) * block - 1, position);
+        sb[b] = __fsub_rn(row[b], FMUL(slope, log1p_table[position - end]));
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
+        const float v = sb[b];
+        int rank = 0;
+        for (int j = 0; j < blocks; ++j) {
+            const float u = sb[j];
+            rank += (u > v) || (u == v && j < b);
+        }
+        keep[b] = rank < slots && v != -INFINITY;
+        row[b] = rank < slots ? v : -INFINITY;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // ascending ids of the kept columns (np.flatnonzero order)
+        int n = 0;
+        for (int b = 0; b < blocks && n < slots_max; ++b)
+            if (keep[b]) kept[h * slots_max + n++] = b;
+        for (; n < slots_max; ++n) kept[h * slots_max + n] = -1;
+    }
+}
+
+// Softmax over one head's scores, then the value mix over window rows and
+// block mean values (kernels.cl:76-107).  One block per head.
+__global__ void k_sparse_attend(const float *scores, const float *v_ring, const float *v_mean, float *out, int heads,
+                                int kv_heads, int dim, int start, int length, int blocks) {
+    extern __shared__ float p[];
+    __shared__ float red[32];
+    const int h = blockIdx.x, total = length + blocks;
+    const int kh = h / (heads / kv_heads), width = kv_heads * dim;
+    const float *s = scores + static_cast<size_t>(h) * total;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    float m = -INFINITY;
+    for (int t = threadIdx.x; t < total; t += blockDim.x) m = fmaxf(m, s[t]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = -INFINITY;
+    for (int w = 0; w < nwarps; ++w) m = fmaxf(m, red[w]);
+    __syncthreads();
+    float den = 0.f;
+    for (int t = threadIdx.x; t < total; t += blockDim.x) {
+        const float e = s[t] == -INFINITY ? 0.f : expf(__fsub_rn(s[t], m));
+        p[t] = e;
+        den += e;
+    }
+    den = warp_sum(den);
+    if (lane == 0) red[warp] = den;
+    __syncthreads();
+    den = 0.f;
+    for (int w = 0; w < nwarps; ++w) den += red[w];
+    // value mix: thread (j, part) sums keys part, part + parts, ...
+    const int parts = blockDim.x / dim;
+    const int j = threadIdx.x % dim, part = threadIdx.x / dim;
+    float acc = 0.f;
+    if (part < parts) {
+        for (int t = part; t < total; t += parts) {
+            const float w = p[t];
+            if (w == 0.f) continue;
+            const float v = t < length ? v_ring[static_cast<size_t>(start + t) * width + static_cast<size_t>(kh) * dim + j]
+                                       : v_mean[static_cast<size_t>(t - length) * width + static_cast<size_t>(kh) * dim + j];
+            acc = fmaf(w, v, acc);
+        }
+    }
+    __syncthreads();
+    float *partial = p;  // the weights are no longer needed
+    if (part < parts) partial[part * dim + j] = acc;
+    __syncthreads();
+    if (threadIdx.x < dim) {
+        float sum = 0.f;
+        for (int q = 0; q < parts; ++q) sum += partial[q * dim + threadIdx.x];
+        out[static_cast<size_t>(h) * dim + threadIdx.x] = __fdiv_rn(sum, den);
+    }
+}
+
+// NumPy's pairwise float32 summation (np.add.reduce over a contiguous axis):
+// fewer than 8 terms in order; up to 128 in eight interleaved running sums
+// combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) plus the tail in order;
+// larger halves recursively (at a multiple of 8).
+__device__ float numpy_pairwise_sum(const float *a, int n) {
+    if (n < 8) {
+        float res = 0.f;
+        for (int i = 0; i < n; ++i) res = FADD(res, a[i]);
+        return res;
+    }
+    if (n <= 128) {
+        float r[8];
+        for (int j = 0; j < 8; ++j) r[j] = a[j];
+        int i = 8;
+        for (; i < n - (n % 8); i += 8)
+            for (int j = 0; j < 8; ++j) r[j] = FADD(r[j], a[i + j]);
+        float res = FADD(FADD(FADD(r[0], r[1]), FADD(r[2], r[3])), FADD(FADD(r[4], r[5]), FADD(r[6], r[7])));
+        for (; i < n; ++i) res = FADD(res, a[i]);
+        return res;
+    }
+    int n2 = n / 2;
+    n2 -= n2 % 8;
+    return FADD(numpy_pairwise_sum(a, n2), numpy_pairwise_sum(a + n2, n - n2));
+}
+
+struct RouteArgs {
+    const float *router;         // [groups + experts]: coarse logits, then fine
+    const void *coarse_bias, *group_bias, *fine_bias, *expert_bias;
+    int bias_dtype[4];
+    int experts, groups, per_group, max_k, min_k;
+    float temperature, log_experts;  // float32(max(T, 1e-4)), float32(log(E))
+    int *chosen;                 // [max_k] expert ids in rank order, -1 after the active ones
+    float *weights;              // [max_k]
+    int *active;                 // 1
+};
+
+// model.py:233-250 for one token, one thread (at most 256 experts).
+__global__ void k_route(RouteArgs a) {
+    __shared__ float coarse[256], logits[256], probs[256], terms[256];
+    __shared__ int order[64];
+    if (threadIdx.x != 0) return;
+    const int E = a.experts, G = a.groups;
+    for (int g = 0; g < G; ++g)
+        coarse[g] = FADD(a.router[g], FADD(load_weight(a.coarse_bias, a.bias_dtype[0], g),
+                                           load_weight(a.group_bias, a.bias_dtype[1], g)));
+    for (int e = 0; e < E; ++e) {
+        const float fine = FADD(a.router[G + e], FADD(load_weight(a.fine_bias, a.bias_dtype[2], e),
+                                                     load_weight(a.expert_bias, a.bias_dtype[3], e)));
+        const int g = min(e / a.per_group, G - 1);
+        logits[e] = __fdiv_rn(FADD(fine, coarse[g]), a.temperature);
+    }
+    // the softmax kernel (kernels.cl:76-84): max, one running sum, divisions
+    float m = -INFINITY;
+    for (int e = 0; e < E; ++e) m = fmaxf(m, logits[e]);
+    float den = 0.f;
+    for (int e = 0; e < E; ++e) den = FADD(den, expf(__fsub_rn(logits[e], m)));
+    for (int e = 0; e < E; ++e) probs[e] = __fdiv_rn(expf(__fsub_rn(logits[e], m)), den);
+    // np.argsort(-probs, kind="stable")[:max_k]
+    const int K = a.max_k;
+    for (int k = 0; k < K; ++k) order[k] = -1;
+    for (int e = 0; e < E; ++e) {
+        int rank = 0;
+        for (int j = 0; j < E; ++j) rank += (probs[j] > probs[e]) || (probs[j] == probs[e] && j < e);
+        if (rank < K) order[rank] = e;
+    }
+    float sel[64];
+    for (int k = 0; k < K; ++k) sel[k] = order[k] >= 0 ? probs[order[k]] : 0.f;
+    const float confidence = __fsub_rn(sel[0], sel[min(K - 1, 1)]);
+    for (int e = 0; e < E; ++e) terms[e] = FMUL(probs[e], logf(fmaxf(probs[e], 1e-9f)));
+    const float entropy = -numpy_pairwise_sum(terms, E);
+    const float width = rintf(FADD(FMUL(__fsub_rn(1.0f, confidence), 2.0f),
+                                   __fdiv_rn(entropy, fmaxf(a.log_experts, 1.0f))));
+    const float total = FADD(static_cast<float>(a.min_k), width);
+    const int active = static_cast<int>(fminf(fmaxf(total, static_cast<float>(a.min_k)), static_cast<float>(K)));
+    for (int k = active; k < K; ++k) sel[k] = 0.f;
+    const float sum = numpy_pairwise_sum(sel, K);
+    const float norm = fmaxf(sum, 1e-9f);
+    for (int k = 0; k < K; ++k) {
+        a.chosen[k] = k < active ? order[k] : -1;
+        a.weights[k] = k < active ? __fdiv_rn(sel[k], norm) : 0.f;
+    }
+    *a.active = active;
+}
+
+struct ExpertArgs {
+    const void *const *gate;  // [experts + shared] matrix pointers (routed, then shared)
+    const void *const *up;
+    const void *const *down;
+    int dtype, ffn, hidden, experts, max_k, shared;
+    const int *chosen, *active;
+    const float *x;           // RMSNorm(x, f_norm)
+    float *act;               // [max_k + shared][ffn] SwiGLU activations
+    float *out;               // [max_k + shared][hidden]
+};
+
+// Expert id of slot `slot` (routed slots in rank order, then the shared
+// experts), or -1 when the slot is not active this token.
+__device__ __forceinline__ int slot_expert(const ExpertArgs &a, int slot) {
+    if (slot < a.max_k) return slot < *a.active ? a.chosen[slot] : -1;
+    return a.experts + (slot - a.max_k);
+}
+
+// act[slot][r] = silu(gate_r . x) * (up_r . x) (kernels.cl:46-50); grid (row blocks, slots).
+__global__ void __launch_bounds__(kGemvThreads) k_expert_gate_up(ExpertArgs a) {
+    extern __shared__ __align__(16) float xs[];
+    const int slot = blockIdx.y, e = slot_expert(a, slot);
+    if (e < 0) return;
+    for (int i = threadIdx.x; i < a.hidden; i += blockDim.x) xs[i] = a.x[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + warp;
+    if (r >= a.ffn) return;
+    const size_t row_bytes = static_cast<size_t>(a.hidden) * (a.dtype == MR_DTYPE_F32 ? 4 : 2);
+    float g, u;
+    warp_dot2(static_cast<const char *>(a.gate[e]) + r * row_bytes, static_cast<const char *>(a.up[e]) + r * row_bytes,
+              a.dtype, a.hidden, xs, g, u);
+    if (lane == 0) a.act[static_cast<size_t>(slot) * a.ffn + r] = FMUL(__fdiv_rn(g, FADD(1.0f, expf(-g))), u);
+}
+
+// out[slot][r] = down_r . act[slot]; grid (row blocks, slots).
+__global__ void __launch_bounds__(kGemvThreads) k_expert_down(ExpertArgs a) {
+    extern __shared__ __align__(16) float xs[];
+    const int slot = blockIdx.y, e = slot_expert(a, slot);
+    if (e < 0) return;
+    for (int i = threadIdx.x; i < a.ffn; i += blockDim.x) xs[i] = a.act[static_cast<size_t>(slot) * a.ffn + i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = blockIdx.x * kGemvRows + warp * kRowsPerWarp;
+    if (r0 >= a.hidden) return;
+    const int r1 = r0 + 1 < a.hidden ? r0 + 1 : -1;
+    const size_t row_bytes = static_cast<size_t>(a.ffn) * (a.dtype == MR_DTYPE_F32 ? 4 : 2);
+    const char *base = static_cast<const char *>(a.down[e]);
+    float y0, y1;
+    warp_dot2(base + r0 * row_bytes, r1 >= 0 ? base + r1 * row_bytes : nullptr, a.dtype, a.ffn, xs, y0, y1);
+    if (lane == 0) {
+        a.out[static_cast<size_t>(slot) * a.hidden + r0] = y0;
+        if (r1 >= 0) a.out[static_cast<size_t>(slot) * a.hidden + r1] = y1;
+    }
+}
+
+// model.py:251-255 then 266: result = 0; result += w_k * expert_k (rank
+// order); result += (residual_scale / S) * shared_i; x += s * result, each an
+// add kernel (x + scale * y, two roundings).
+__global__ void k_expert_combine(ExpertArgs a, const float *weights, float shared_scale, float scale, float *x) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= a.hidden) return;
+    float res = 0.f;
+    const int active = *a.active;
+    for (int k = 0; k < active; ++k) res = FADD(res, FMUL(weights[k], a.out[static_cast<size_t>(k) * a.hidden + r]));
+    for (int i = 0; i < a.shared; ++i)
+        res = FADD(res, FMUL(shared_scale, a.out[static_cast<size_t>(a.max_k + i) * a.hidden + r]));
+    x[r] = FADD(x[r], FMUL(scale, res));
+}
+
+}  // namespace
+
+// ---- host side -------------------------------------------------------------------
+struct HeavyLayer {
+    const void *a_norm, *f_norm;
+    int a_norm_dt, f_norm_dt;
+    GemvSeg q, latent, kv_up, o, coarse, fine;
+    const void *coarse_bias, *group_bias, *fine_bias, *expert_bias;
+    int bias_dt[4];
+    const void **d_gate, **d_up, **d_down;  // device pointer tables [experts + shared]
+    int expert_dtype;
+};
+
+struct HeavyEngine {
+    mr_model *m = nullptr;
+    cudaStream_t stream = nullptr;
+    int H, KVH, d, hidden, latent, ffn, vocab, layers, loops, context, window, block, slots, experts, groups,
+        per_group, max_k, min_k, shared, split_half, tied;
+    float eps, residual_scale, temperature, slope, log_experts;
+    const void *embed, *final_norm, *head;
+    int embed_dt, final_norm_dt, head_dt;
+    std::vector<HeavyLayer> L;
+    // device work buffers
+    float *x = nullptr, *h = nullptr, *q = nullptr, *lat = nullptr, *kv = nullptr, *attn = nullptr,
+          *scores = nullptr, *router = nullptr, *act = nullptr, *eout = nullptr, *logits = nullptr,
+          *inv_freq = nullptr, *log1p_table = nullptr;
+    std::vector<float *> k_ring, v_ring, k_mean, v_mean;  // per (layer, loop)
+    int *kept = nullptr;      // [layers][loops][H][slots]
+    int *chosen = nullptr;    // [layers][loops][max_k]
+    float *weights = nullptr; // [layers][loops][max_k]
+    int *active = nullptr;    // [layers][loops]
+    std::vector<void *> allocations;
+    bool table_set = false;
+};
+
+namespace {
+
+int halloc(HeavyEngine &e, size_t bytes, void **out) {
+    void *p = nullptr;
+    MR_CUDA_TRY(cudaMalloc(&p, std::max<size_t>(bytes, 16)));
+    e.allocations.push_back(p);
+    *out = p;
+    return MR_OK;
+}
+template <typename T>
+int halloc_n(HeavyEngine &e, size_t n, T **out) {
+    void *p = nullptr;
+    int rc = halloc(e, n * sizeof(T), &p);
+    *out = static_cast<T *>(p);
+    return rc;
+}
+
+int tensor_of(mr_model *m, const std::string &name, const void **ptr, int *dtype, int64_t *rows, int64_t *cols) {
+    return model_tensor(m, name.c_str(), ptr, dtype, rows, cols);
+}
+
+int seg_of(mr_model *m, const std::string &name, const float *x, float *y, GemvSeg &s) {
+    int64_t rows = 0, cols = 0;
+    s = GemvSeg{};
+    if (int rc = tensor_of(m, name, &s.w, &s.dtype, &rows, &cols)) return rc;
+    s.rows = static_cast<int>(rows);
+    s.cols = static_cast<int>(cols);
+    s.x = x;
+    s.y = y;
+    return MR_OK;
+}
+
+int launch_gemv(HeavyEngine &e, std::initializer_list<GemvSeg> segs) {
+    GemvArgs a{};
+    int blocks = 0, cols = 0;
+    for (const GemvSeg &s : segs) {
+        a.first[a.nseg] = blocks;
+        a.s[a.nseg++] = s;
+        blocks += (s.rows + kGemvRows - 1) / kGemvRows;
+        cols = std::max(cols, s.cols);
+    }
+    a.first[a.nseg] = blocks;
+    k_gemv<<<blocks, kGemvThreads, static_cast<size_t>(cols) * sizeof(float) + 16, e.stream>>>(a);
+    MR_CUDA_TRY(cudaGetLastError());
+    return MR_OK;
+}
+
+}  // namespace
+
+int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, const float *inv_freq_host,
+                 HeavyEngine **out) {
+    auto *e = new HeavyEngine();
+    e->m = m;
+    e->stream = stream;
+    e->H = c.query_heads;
+    e->KVH = c.kv_heads;
+    e->d = c.head_dim;
+    e->hidden = c.hidden_size;
+    e->latent = c.latent_dim;
+    e->ffn = c.ffn_dim;
+    e->vocab = c.vocab_size;
+    e->layers = c.layers;
+    e->loops = std::max(1, c.inner_loop_steps);
+    e->context = c.context_length;
+    e->window = c.window;
+    e->block = c.block_size;
+    e->slots = c.global_slots;
+    e->experts = c.routed_experts;
+    e->groups = c.router_groups;
+    e->per_group = (c.routed_experts + c.router_groups - 1) / c.router_groups;
+    e->max_k = c.router_top_k_max;
+    e->min_k = c.router_top_k_min;
+    e->shared = c.shared_experts;
+    e->split_half = c.split_half_rope;
+    e->tied = c.tie_embeddings;
+    e->eps = c.norm_eps;
+    e->residual_scale = c.residual_scale;
+    e->temperature = c.router_temperature;
+    e->slope = c.alibi_slope;
+    e->log_experts = static_cast<float>(std::log(static_cast<double>(c.routed_experts)));
+    auto fail = [&](int rc) {
+        heavy_destroy(e);
+        return rc;
+    };
+    if (!(e->window > 0 && e->block > 0 && e->latent > 0 && e->experts > 0 && e->experts <= 256 && e->groups > 0 &&
+          e->max_k >= 1 && e->max_k <= 64 && e->min_k >= 0 && e->slots >= 0 && e->shared >= 0 &&
+          e->H % e->KVH == 0 && e->d <= 1024 && e->d % 2 == 0 && e->d / 2 <= 128)) {
+        heavy_destroy(e);
+        return set_error(MR_ERR_ARGUMENT, "heavy-medium-2.0 geometry outside the device path's limits");
+    }
+    const int width = e->KVH * e->d;
+    int64_t rows = 0, cols = 0;
+    int rc = MR_OK;
+    if ((rc = tensor_of(m, "embed", &e->embed, &e->embed_dt, &rows, &cols))) return fail(rc);
+    if ((rc = tensor_of(m, "norm", &e->final_norm, &e->final_norm_dt, &rows, &cols))) return fail(rc);
+    if ((rc = tensor_of(m, e->tied ? "embed" : "output", &e->head, &e->head_dt, &rows, &cols))) return fail(rc);
+    // work buffers
+    const int maxblocks = (e->context + e->block - 1) / e->block;
+    const int slots_total = e->max_k + e->shared;
+    if ((rc = halloc_n(*e, e->hidden, &e->x)) || (rc = halloc_n(*e, std::max(e->hidden, e->ffn), &e->h)) ||
+        (rc = halloc_n(*e, static_cast<size_t>(e->H) * e->d, &e->q)) || (rc = halloc_n(*e, e->latent, &e->lat)) ||
+        (rc = halloc_n(*e, 2 * static_cast<size_t>(width), &e->kv)) ||
+        (rc = halloc_n(*e, static_cast<size_t>(e->H) * e->d, &e->attn)) ||
+        (rc = halloc_n(*e, static_cast<size_t>(e->H) * (std::min(e->window, e->context) + maxblocks), &e->scores)) ||
+        (rc = halloc_n(*e, e->groups + e->experts, &e->router)) ||
+        (rc = halloc_n(*e, static_cast<size_t>(slots_total) * e->ffn, &e->act)) ||
+        (rc = halloc_n(*e, static_cast<size_t>(slots_total) * e->hidden, &e->eout)) ||
+        (rc = halloc_n(*e, e->vocab, &e->logits)) || (rc = halloc_n(*e, e->d / 2, &e->inv_freq)) ||
+        (rc = halloc_n(*e, e->context + 1, &e->log1p_table)))
+        return fail(rc);
+    const size_t per = static_cast<size_t>(e->layers) * e->loops;
+    if ((rc = halloc_n(*e, per * e->H * std::max(1, e->slots), &e->kept)) ||
+        (rc = halloc_n(*e, per * e->max_k, &e->chosen)) || (rc = halloc_n(*e, per * e->max_k, &e->weights)) ||
+        (rc = halloc_n(*e, per, &e->active)))
+        return fail(rc);
+    MR_CUDA_TRY(cudaMemcpy(e->inv_freq, inv_freq_host, sizeof(float) * (e->d / 2), cudaMemcpyHostToDevice));
+    for (size_t i = 0; i < per; ++i) {
+        float *kr, *vr, *km, *vm;
+        if ((rc = halloc_n(*e, static_cast<size_t>(e->context) * width, &kr)) ||
+            (rc = halloc_n(*e, static_cast<size_t>(e->context) * width, &vr)) ||
+            (rc = halloc_n(*e, static_cast<size_t>(maxblocks) * width, &km)) ||
+            (rc = halloc_n(*e, static_cast<size_t>(maxblocks) * width, &vm)))
+            return fail(rc);
+        e->k_ring.push_back(kr);
+        e->v_ring.push_back(vr);
+        e->k_mean.push_back(km);
+        e->v_mean.push_back(vm);
+    }
+    // per-layer weights
+    e->L.resize(e->layers);
+    for (int l = 0; l < e->layers; ++l) {
+        HeavyLayer &Ly = e->L[l];
+        const std::string p = "layers." + std::to_string(l) + ".";
+        if ((rc = tensor_of(m, p + "a_norm", &Ly.a_norm, &Ly.a_norm_dt, &rows, &cols)) ||
+            (rc = tensor_of(m, p + "f_norm", &Ly.f_norm, &Ly.f_norm_dt, &rows, &cols)) ||
+            (rc = seg_of(m, p + "q", e->h, e->q, Ly.q)) || (rc = seg_of(m, p + "latent", e->h, e->lat, Ly.latent)) ||
+            (rc = seg_of(m, p + "kv_up", e->lat, e->kv, Ly.kv_up)) || (rc = seg_of(m, p + "o", e->attn, e->x, Ly.o)) ||
+            (rc = seg_of(m, p + "router.coarse.weight", e->h, e->router, Ly.coarse)) ||
+            (rc = seg_of(m, p + "router.fine.weight", e->h, e->router + e->groups, Ly.fine)) ||
+            (rc = tensor_of(m, p + "router.coarse.bias", &Ly.coarse_bias, &Ly.bias_dt[0], &rows, &cols)) ||
+            (rc = tensor_of(m, p + "router.group_bias", &Ly.group_bias, &Ly.bias_dt[1], &rows, &cols)) ||
+            (rc = tensor_of(m, p + "router.fine.bias", &Ly.fine_bias, &Ly.bias_dt[2], &rows, &cols)) ||
+            (rc = tensor_of(m, p + "router.expert_bias", &Ly.expert_bias, &Ly.bias_dt[3], &rows, &cols)))
+            return fail(rc);
+        Ly.o.residual = 1;
+        std::vector<const void *> gate, up, down;
+        int dtype = -1;
+        for (int i = 0; i < e->experts + e->shared; ++i) {
+            const std::string root = i < e->experts ? p + "experts." + std::to_string(i) + "."
+                                                    : p + "shared." + std::to_string(i - e->experts) + ".";
+            const void *g, *u, *dn;
+            int dg, du, dd;
+            if ((rc = tensor_of(m, root + "gate", &g, &dg, &rows, &cols)) ||
+                (rc = tensor_of(m, root + "up", &u, &du, &rows, &cols)) ||
+                (rc = tensor_of(m, root + "down", &dn, &dd, &rows, &cols)))
+                return fail(rc);
+            if (dtype < 0) dtype = dg;
+            if (dg != dtype || du != dtype || dd != dtype) {
+                heavy_destroy(e);
+                return set_error(MR_ERR_ARGUMENT, "layer %d: the experts' matrices must share one dtype", l);
+            }
+            gate.push_back(g);
+            up.push_back(u);
+            down.push_back(dn);
+        }
+        Ly.expert_dtype = dtype;
+        const size_t n = gate.size();
+        if ((rc = halloc_n(*e, n, &Ly.d_gate)) || (rc = halloc_n(*e, n, &Ly.d_up)) || (rc = halloc_n(*e, n, &Ly.d_down)))
+            return fail(rc);
+        MR_CUDA_TRY(cudaMemcpy(Ly.d_gate, gate.data(), n * sizeof(void *), cudaMemcpyHostToDevice));
+        MR_CUDA_TRY(cudaMemcpy(Ly.d_up, up.data(), n * sizeof(void *), cudaMemcpyHostToDevice));
+        MR_CUDA_TRY(cudaMemcpy(Ly.d_down, down.data(), n * sizeof(void *), cudaMemcpyHostToDevice));
+    }
+    MR_CUDA_TRY(cudaMemset(e->kept, 0xff, per * e->H * std::max(1, e->slots) * sizeof(int)));
+    MR_CUDA_TRY(cudaMemset(e->chosen, 0xff, per * e->max_k * sizeof(int)));
+    MR_CUDA_TRY(cudaMemset(e->weights, 0, per * e->max_k * sizeof(float)));
+    MR_CUDA_TRY(cudaMemset(e->active, 0, per * sizeof(int)));
+    *out = e;
+    return MR_OK;
+}
+
+void heavy_destroy(HeavyEngine *e) {
+    if (!e) return;
+    for (void *p : e->allocations) cudaFree(p);
+    delete e;
+}
+
+int heavy_set_log1p(HeavyEngine *e, const float *values, int n) {
+    MR_REQUIRE(e && values, "NULL argument");
+    MR_REQUIRE(n >= e->context, "the log1p table needs %d values (distances 0 .. context-1), got %d", e->context, n);
+    MR_CUDA_TRY(cudaMemcpy(e->log1p_table, values, sizeof(float) * e->context, cudaMemcpyHostToDevice));
+    e->table_set = true;
+    return MR_OK;
+}
+
+// One token at `position`: x = embed[token], every layer and inner loop, the
+// final norm and the head; logits (vocab floats) stay in e->logits.
+int heavy_token(HeavyEngine *e, int token, int position) {
+    MR_REQUIRE(e->table_set, "heavy-medium-2.0: the distance-penalty table has not been set");
+    MR_REQUIRE(position >= 0 && position < e->context, "position %d outside the context", position);
+    MR_REQUIRE(token >= 0 && token < e->vocab, "input token is outside the vocabulary");
+    cudaStream_t s = e->stream;
+    const int width = e->KVH * e->d, count = position + 1;
+    const int length = std::min(e->window, count), start = count - length;
+    const int blocks = (count + e->block - 1) / e->block;
+    const int slots = std::min(e->slots, blocks), total = length + blocks;
+    const int slots_total = e->max_k + e->shared;
+    const float loop_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::sqrt((double)e->loops));
+    const float shared_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::max(e->shared, 1));
+    k_embed_row<<<(e->hidden + 255) / 256, 256, 0, s>>>(e->embed, e->embed_dt, token, e->hidden, e->x);
+    for (int l = 0; l < e->layers; ++l) {
+        HeavyLayer &Ly = e->L[l];
+        for (int loop = 0; loop < e->loops; ++loop) {
+            const size_t li = static_cast<size_t>(l) * e->loops + loop;
+            // attention (model.py:192-229)
+            k_rms_row<<<1, 1024, 0, s>>>(e->x, Ly.a_norm, Ly.a_norm_dt, e->h, e->hidden, e->eps);
+            if (int rc = launch_gemv(*e, {Ly.q, Ly.latent})) return rc;
+            if (int rc = launch_gemv(*e, {Ly.kv_up})) return rc;
+            k_heads_norm_rope<<<e->H + e->KVH, 32, 0, s>>>(e->q, e->kv, e->k_ring[li], e->v_ring[li], e->inv_freq, e->H,
+                                                          e->KVH, e->d, e->split_half, position, position);
+            k_block_mean_last<<<(2 * width + 255) / 256, 256, 0, s>>>(e->k_ring[li], e->v_ring[li], e->k_mean[li],
+                                                                     e->v_mean[li], count, width, e->block);
+            const int items = e->H * total;
+            k_sparse_scores<<<(items + 7) / 8, 256, 0, s>>>(e->q, e->k_ring[li], e->k_mean[li], e->scores, e->H, e->KVH,
+                                                           e->d, start, length, blocks);
+            int *kept = e->kept + li * e->H * std::max(1, e->slots);
+            k_block_topk<<<e->H, 256, static_cast<size_t>(blocks) * (sizeof(float) + sizeof(int)), s>>>(
+                e->scores, total, length, blocks, e->block, position, e->log1p_table, e->slope, slots,
+                std::max(1, e->slots), kept);
+            const int attend_threads = std::max(128, std::min(1024, (1024 / e->d) * e->d));
+            const size_t attend_smem = std::max<size_t>(total, static_cast<size_t>(attend_threads)) * sizeof(float);
+            k_sparse_attend<<<e->H, attend_threads, attend_smem, s>>>(e->scores, e->v_ring[li], e->v_mean[li], e->attn,
+                                                                     e->H, e->KVH, e->d, start, length, blocks);
+            GemvSeg o = Ly.o;
+            o.scale = loop_scale;
+            if (int rc = launch_gemv(*e, {o})) return rc;
+            // mixture of experts (model.py:231-255)
+            k_rms_row<<<1, 1024, 0, s>>>(e->x, Ly.f_norm, Ly.f_norm_dt, e->h, e->hidden, e->eps);
+            if (int rc = launch_gemv(*e, {Ly.coarse, Ly.fine})) return rc;
+            RouteArgs ra{};
+            ra.router = e->router;
+            ra.coarse_bias = Ly.coarse_bias;
+            ra.group_bias = Ly.group_bias;
+            ra.fine_bias = Ly.fine_bias;
+            ra.expert_bias = Ly.expert_bias;
+            for (int i = 0; i < 4; ++i) ra.bias_dtype[i] = Ly.bias_dt[i];
+            ra.experts = e->experts;
+            ra.groups = e->groups;
+            ra.per_group = e->per_group;
+            ra.max_k = e->max_k;
+            ra.min_k = e->min_k;
+            ra.temperature = e->temperature;
+            ra.log_experts = e->log_experts;
+            ra.chosen = e->chosen + li * e->max_k;
+            ra.weights = e->weights + li * e->max_k;
+            ra.active = e->active + li;
+            k_route<<<1, 32, 0, s>>>(ra);
+            ExpertArgs ea{};
+            ea.gate = Ly.d_gate;
+            ea.up = Ly.d_up;
+            ea.down = Ly.d_down;
+            ea.dtype = Ly.expert_dtype;
+            ea.ffn = e->ffn;
+            ea.hidden = e->hidden;
+            ea.experts = e->experts;
+            ea.max_k = e->max_k;
+            ea.shared = e->shared;
+            ea.chosen = ra.chosen;
+            ea.active = ra.active;
+            ea.x = e->h;
+            ea.act = e->act;
+            ea.out = e->eout;
+            k_expert_gate_up<<<dim3((e->ffn + 7) / 8, slots_total), kGemvThreads,
+                               static_cast<size_t>(e->hidden) * sizeof(float) + 16, s>>>(ea);
+            k_expert_down<<<dim3((e->hidden + kGemvRows - 1) / kGemvRows, slots_total), kGemvThreads,
+                            static_cast<size_t>(e->ffn) * sizeof(float) + 16, s>>>(ea);
+            k_expert_combine<<<(e->hidden + 255) / 256, 256, 0, s>>>(ea, ra.weights, shared_scale, loop_scale, e->x);
+            MR_CUDA_TRY(cudaGetLastError());
+        }
+    }
+    k_rms_row<<<1, 1024, 0, s>>>(e->x, e->final_norm, e->final_norm_dt, e->h, e->hidden, e->eps);
+    GemvSeg head{};
+    head.w = e->head;
+    head.dtype = e->head_dt;
+    head.rows = e->vocab;
+    head.cols = e->hidden;
+    head.x = e->h;
+    head.y = e->logits;
+    if (int rc = launch_gemv(*e, {head})) return rc;
+    MR_CUDA_TRY(cudaGetLastError());
+    return MR_OK;
+}
+
+const float *heavy_logits(const HeavyEngine *e) { return e->logits; }
+
+int heavy_last_topk(const HeavyEngine *e, int layer, int loop, int *blocks, int capacity) {
+    const int per = e->H * std::max(1, e->slots);
+    MR_REQUIRE(capacity >= e->H * e->slots, "blocks holds %d ints, need %d", capacity, e->H * e->slots);
+    std::vector<int> tmp(per);
+    MR_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    MR_CUDA_TRY(cudaMemcpy(tmp.data(), e->kept + (static_cast<size_t>(layer) * e->loops + loop) * per,
+                           sizeof(int) * per, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < e->H * e->slots; ++i) blocks[i] = tmp[i];
+    return MR_OK;
+}
+
+int heavy_last_experts(const HeavyEngine *e, int layer, int loop, int *experts, float *weights, int capacity) {
+    MR_REQUIRE(capacity >= e->max_k, "buffers hold %d entries, need %d", capacity, e->max_k);
+    const size_t li = static_cast<size_t>(layer) * e->loops + loop;
+    MR_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    MR_CUDA_TRY(cudaMemcpy(experts, e->chosen + li * e->max_k, sizeof(int) * e->max_k, cudaMemcpyDeviceToHost));
+    MR_CUDA_TRY(cudaMemcpy(weights, e->weights + li * e->max_k, sizeof(float) * e->max_k, cudaMemcpyDeviceToHost));
+    return MR_OK;
+}
+
+}  // namespace mr

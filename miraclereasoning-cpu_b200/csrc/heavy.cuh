@@ -1,0 +1,33 @@
+// Heavy Medium 2.0 on the device (heavy.cu): the token step of
+// miracle_reasoning/model.py:192-285 as kernel launches, with the block top-k
+// and the expert routing taken on the GPU.
+#pragma once
+
+#include "common.cuh"
+
+namespace mr {
+
+struct HeavyEngine;
+
+// Reads the model's resident tensors (the model must be finalized) and
+// allocates the work buffers and one key/value ring per (layer, inner loop).
+int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, const float *inv_freq_host,
+                 HeavyEngine **out);
+void heavy_destroy(HeavyEngine *e);
+
+// float32 log1p(d) for distances d = 0 .. context-1, as the host computes them
+// (the reference applies NumPy's float32 log1p, model.py:221-222).
+int heavy_set_log1p(HeavyEngine *e, const float *values, int n);
+
+// Queues one token at `position` on the engine's stream; the logits (vocab
+// floats) are then at heavy_logits(e).
+int heavy_token(HeavyEngine *e, int token, int position);
+const float *heavy_logits(const HeavyEngine *e);
+
+// Decisions of the last token (synchronise the stream): kept block ids
+// (heads x global_slots, ascending per head, -1 padded) and the experts in
+// rank order with their weights (router_top_k_max entries, -1 / 0 padded).
+int heavy_last_topk(const HeavyEngine *e, int layer, int loop, int *blocks, int capacity);
+int heavy_last_experts(const HeavyEngine *e, int layer, int loop, int *experts, float *weights, int capacity);
+
+}  // namespace mr

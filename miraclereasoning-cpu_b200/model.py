@@ -13,9 +13,10 @@ once into HBM (no LRU, no host widening).  For the grouped-query families
 decode kernel (csrc/engine_kernel.cu) and greedy ``generate`` runs entirely on
 the device (argmax feeds the next step).  FlashLighting without memory slots
 runs on the same kernel (its latent cache as a key/value ring, see
-``engine_plans``).  flashnano-1.6, FlashLighting with memory slots and Heavy
-Medium step on the host over the op kernels against the resident weights
-(stepper.py).  Sampled ``generate`` reads the logits each step and
+``engine_plans``); Heavy Medium runs its token step as device kernel launches
+with the block top-k and expert routing on the GPU (csrc/heavy.cu).
+flashnano-1.6 and FlashLighting with memory slots step on the host over the
+op kernels against the resident weights (stepper.py).  Sampled ``generate`` reads the logits each step and
 samples on the host with the reference's exact NumPy procedure.
 """
 from __future__ import annotations
@@ -87,10 +88,12 @@ class LatentView:
 
 
 def engine_plans(config):
-    """Whether the persistent decode kernel runs this model: the grouped-query
-    families, and FlashLighting without memory slots (its latent cache then
-    only drops the oldest row, which the engine keeps as a key/value ring)."""
-    if config.family not in HOST_STEPPED:
+    """Whether the token step runs on the device without the host stepper: the
+    grouped-query families and FlashLighting without memory slots (its latent
+    cache then only drops the oldest row, which the persistent decode kernel
+    keeps as a key/value ring), and Heavy Medium (csrc/heavy.cu: kernel
+    launches with the block top-k and the expert routing on the GPU)."""
+    if config.family not in HOST_STEPPED or config.family == "heavy-medium-2.0":
         return True
     return config.family == "flashlighting-2.0" and config.memory_slots == 0 and bool(config.window)
 
@@ -122,11 +125,14 @@ class MiracleModel:
     """
 
     def __init__(self, config, weights=None, *, backend=None, context_length=None,
-                 weight_cache_bytes=256 * 1024 * 1024, tensor_parallel=None, _synthetic=None):
+                 weight_cache_bytes=256 * 1024 * 1024, tensor_parallel=None, record_decisions=False,
+                 _synthetic=None):
         """``tensor_parallel=(rank, ranks, all_gather)``: this process decodes on one of
         ``ranks`` GPUs, each computing a slice of every projection's rows and of the
         KV heads (every rank makes the same calls in the same order; see
-        mr_model_set_tensor_parallel)."""
+        mr_model_set_tensor_parallel).  ``record_decisions``: keep Heavy Medium's
+        per-token top-k blocks and experts in ``decisions`` (each token then reads
+        them back from the device)."""
         self.config = config
         if context_length is None:
             context_length = min(2048, config.max_positions)
@@ -158,6 +164,13 @@ class MiracleModel:
             rank, ranks, _ = tensor_parallel
             _native.call("mr_model_set_tensor_parallel", self._handle, int(rank), int(ranks))
         _native.call("mr_model_finalize", self._handle)
+        if config.family == "heavy-medium-2.0":
+            # the distance penalty's float32 log1p values, as the reference computes
+            # them with NumPy (model.py:221-222), for every distance in the context
+            table = np.ascontiguousarray(np.log1p(np.arange(context_length, dtype=np.float32)), dtype=np.float32)
+            _native.call("mr_model_set_log1p_table", self._handle, table.ctypes.data_as(_F32), len(table))
+        self.record_decisions = bool(record_decisions) and config.family == "heavy-medium-2.0"
+        self._decisions = []
         if tensor_parallel is not None and tensor_parallel[1] > 1:
             self._connect(*tensor_parallel)
         used = C.c_uint64()
@@ -235,6 +248,7 @@ class MiracleModel:
         _native.call("mr_model_reset", self._handle)
         if self._stepper is not None:
             self._stepper.reset()
+        self._decisions = []
         self._failed = False
 
     @property
@@ -251,7 +265,28 @@ class MiracleModel:
         (heavy top-k blocks, MoE experts and weights, latent positions)."""
         if self._stepper is not None:
             return self._stepper.decisions
-        return RingDecisions(self) if self.config.family == "flashlighting-2.0" else []
+        if self.config.family == "flashlighting-2.0":
+            return RingDecisions(self)
+        return self._decisions
+
+    def _read_decisions(self):
+        """Heavy Medium: the last token's top-k blocks and experts, per layer and loop."""
+        c, s = self.config, self.config.source
+        heads, slots, max_k = c.query_heads, s["long_context"]["global_slots"], s["router_top_k_max"]
+        blocks = (C.c_int * max(heads * slots, 1))()
+        experts, weights = (C.c_int * max_k)(), (C.c_float * max_k)()
+        record = []
+        for layer in range(c.layers):
+            entry = {"topk": [], "experts": [], "expert_weights": []}
+            for loop in range(c.inner_loop_steps):
+                _native.call("mr_model_last_topk", self._handle, layer, loop, blocks, heads * slots)
+                entry["topk"].append([[b for b in blocks[h * slots:(h + 1) * slots] if b >= 0] for h in range(heads)])
+                _native.call("mr_model_last_experts", self._handle, layer, loop, experts, weights, max_k)
+                chosen = [e for e in experts[:max_k] if e >= 0]
+                entry["experts"].append(chosen)
+                entry["expert_weights"].append([float(np.float32(w)) for w in weights[:len(chosen)]])
+            record.append(entry)
+        self._decisions.append(record)
 
     @property
     def states(self):
@@ -319,6 +354,16 @@ class MiracleModel:
                         out[i] = self._stepper.logits(hidden)
                     elif i == len(ids) - 1:
                         out[:] = self._stepper.logits(hidden)
+            elif self.record_decisions:
+                for i in range(len(ids)):
+                    row = np.empty(V, dtype=np.float32)
+                    _native.call("mr_model_prefill", self._handle, ids[i:].ctypes.data_as(_I32), 1, 0,
+                                 row.ctypes.data_as(_F32))
+                    self._read_decisions()
+                    if return_all:
+                        out[i] = row
+                    elif i == len(ids) - 1:
+                        out[:] = row
             else:
                 _native.call("mr_model_prefill", self._handle, ids.ctypes.data_as(_I32), len(ids), int(return_all),
                              out.ctypes.data_as(_F32))
@@ -349,7 +394,7 @@ class MiracleModel:
         self.reset()
         if max_new_tokens == 0:
             return []
-        if temperature == 0 and self._stepper is None:
+        if temperature == 0 and self._stepper is None and not self.record_decisions:
             return self._generate_greedy(tokens, max_new_tokens, eos)
         rng, generated = np.random.default_rng(seed), []
         logits = self.prefill(tokens)

@@ -22,10 +22,11 @@ ATOL, RTOL = 2e-5, 2e-4
 ENGINE_CASES = ("nano15", "nano15_untied", "nano17", "lite", "lite_noqk")
 
 
-def _model(backend, name):
+def _model(backend, name, **kwargs):
     config = cases.micro_config(name)
     MiracleModel = submodule("model").MiracleModel
-    return MiracleModel(config, cases.micro_weights(config), backend=backend, context_length=cases.micro_context(name))
+    return MiracleModel(config, cases.micro_weights(config), backend=backend, context_length=cases.micro_context(name),
+                        **kwargs)
 
 
 def _near_tie(logits):
@@ -82,7 +83,10 @@ def test_generate_greedy_and_sampled(backend, name):
     assert tokens == golden["greedy"].tolist()
 
 
-# ---- families stepped on the host over the op kernels (stepper.py) -----------------
+# ---- families beyond the grouped-query engine: flashnano-1.6 and FlashLighting with
+# memory slots step on the host over the op kernels (stepper.py); FlashLighting without
+# memory slots runs on the decode kernel (key/value ring), Heavy Medium on the device
+# token step (csrc/heavy.cu) with its decisions read back per token ----------------------
 OP_CASES = ("nano16", "lighting", "lighting_drop", "heavy", "heavy_mid")
 
 
@@ -123,7 +127,7 @@ def _decisions(model):
 def test_op_path_prefill_state_and_decisions(backend, name):
     golden = np.load(cases.GOLDEN_DIR / f"micro_{name}.npz")
     meta = json.loads(str(golden["meta"]))
-    model = _model(backend, name)
+    model = _model(backend, name, record_decisions=True)
     prompt = cases.micro_prompt(name)
     logits = model.prefill(prompt, return_all=True)
     np.testing.assert_allclose(logits, golden["logits"], atol=ATOL, rtol=RTOL)
