@@ -93,13 +93,26 @@ class Ranks:
 
 
 # ---- roofline bookkeeping ----------------------------------------------------------
-def weight_bytes(config, stored="BF16"):
-    """Bytes of every weight a decode step reads once (tied head = embed)."""
+def weight_bytes(config, stored="BF16", active_experts=None):
+    """Bytes of every weight a decode step reads once (tied head = embed).
+
+    Heavy Medium reads, per layer and inner loop, its attention and router
+    matrices, the shared experts and the routed experts it chose:
+    ``active_experts`` = the mean number chosen per (layer, loop)."""
     shapes = _pkg("weights").expected_shapes(config)
     total = 0
+    expert = 0
     for name, shape in shapes.items():
-        n = math.prod(shape)
-        total += n * (2 if (stored == "BF16" and len(shape) == 2) else 4)
+        n = math.prod(shape) * (2 if (stored == "BF16" and len(shape) == 2) else 4)
+        if ".experts." in name:
+            if name.startswith("layers.0.experts.0."):
+                expert += n
+            continue
+        if config.family == "heavy-medium-2.0" and name.startswith("layers."):
+            n *= config.inner_loop_steps  # both inner loops read the layer's weights
+        total += n
+    if config.family == "heavy-medium-2.0":
+        total += expert * active_experts * config.layers * config.inner_loop_steps
     # the embedding is read twice: one row for the input, the whole matrix for the tied head
     return total + config.hidden_size * (2 if stored == "BF16" else 4)
 
@@ -107,6 +120,13 @@ def weight_bytes(config, stored="BF16"):
 def kv_bytes(config, context, position):
     """float32 K/V bytes attended (read) and appended (written) at `position`."""
     total = 0
+    if config.family == "heavy-medium-2.0":
+        # per layer and inner loop: the local window's rows, every block mean (keys
+        # and values), the newest block's rows for its mean, the appended row
+        width = config.kv_heads * config.head_dim
+        block = config.source["long_context"]["global_block_size"]
+        rows = min(position + 1, config.window) + (position + block) // block + position % block + 1 + 1
+        return config.layers * config.inner_loop_steps * rows * width * 2 * 4
     for layer in range(config.layers):
         width = config.layer_kv_heads(layer) * config.head_dim
         cap = min(config.layer_window(layer) or context, context)
@@ -134,6 +154,30 @@ def ncu_traffic(config_name):
         if line.startswith("traffic_bytes_per_launch:"):
             return float(line.split(":", 1)[1].strip())
     return None
+
+
+def launches_per_step(config):
+    """Kernels one decode step launches: the persistent decode kernel once, or
+    Heavy Medium's device step (embedding row; per layer and inner loop 15
+    kernels; final norm, head, greedy argmax)."""
+    if config.family == "heavy-medium-2.0":
+        return 1 + 15 * config.layers * config.inner_loop_steps + 3
+    return 1
+
+
+def mean_active_experts(model):
+    """Heavy Medium: routed experts chosen per (layer, inner loop), averaged
+    over the last decoded token's decisions (read back from the device)."""
+    import ctypes as C
+    c, s = model.config, model.config.source
+    max_k = s["router_top_k_max"]
+    experts, weights = (C.c_int * max_k)(), (C.c_float * max_k)()
+    counts = []
+    for layer in range(c.layers):
+        for loop in range(c.inner_loop_steps):
+            _pkg("_native").call("mr_model_last_experts", model._handle, layer, loop, experts, weights, max_k)
+            counts.append(sum(1 for e in experts[:max_k] if e >= 0))
+    return sum(counts) / len(counts)
 
 
 # ---- clocks ------------------------------------------------------------------------
@@ -224,11 +268,16 @@ def run_cuda(args, ranks):
     sequences = 1 if tp else ranks.world
 
     # prefill, timed after one untimed pass (workspace allocation): batched on the
-    # tensor cores for BF16 models, else token by token through the decode kernel
+    # tensor cores for BF16 models of the grouped-query families; else token by
+    # token (FlashLighting on the decode kernel, Heavy Medium on its device step),
+    # which is timed on its only pass
     batched = C.c_int(0)
-    native.call("mr_model_set_batched_prefill", model._handle, 1, C.byref(batched))
-    model.prefill(prompt)
-    model.reset()
+    if model._stepper is None and config.family != "heavy-medium-2.0":
+        native.call("mr_model_set_batched_prefill", model._handle, 1, C.byref(batched))
+    serial = not batched.value
+    if not serial:
+        model.prefill(prompt)
+        model.reset()
     backend.finish()
     ranks.barrier()
     t0 = time.perf_counter()
@@ -247,28 +296,36 @@ def run_cuda(args, ranks):
         backend.finish()
         ranks.barrier()
         device_ms = ranks.max(ms.value)
+        active = mean_active_experts(model) if config.family == "heavy-medium-2.0" else None
+
+        # end to end through the public API: token id in, float32 logits out, every step
+        def end_to_end(logits):
+            steps = min(args.steps, 128)
+            ranks.barrier()
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                logits = model.decode(int(np.argmax(logits)))
+            return steps, ranks.max(time.perf_counter() - t0)
+
+        if serial:  # continue from here rather than run the prompt token by token again
+            e2e_steps, e2e_s = end_to_end(np.eye(1, config.vocab_size, token, dtype=np.float32)[0])
         # keep the same decode load under the clock sampler for ~1.5 s more (the same
         # number of calls on every rank: tensor-parallel ranks step together)
-        extra_steps = min(1024, context - 16)
-        for _ in range(max(1, math.ceil(1.5e3 / (device_ms / args.steps * extra_steps)))):
+        step_ms = device_ms / args.steps
+        extra_steps = max(16, min(1024, context - 16, int(1.5e3 / step_ms)))
+        for _ in range(max(1, math.ceil(1.5e3 / (step_ms * extra_steps)))):
             model.reset()
             model.prefill(prompt[:8])
-            native.call("mr_model_bench_decode", model._handle, token, min(1024, context - 16), C.byref(ms))
+            native.call("mr_model_bench_decode", model._handle, token, extra_steps, C.byref(ms))
     clock_summary = clocks.summary()
 
-    # end to end through the public API: token id in, float32 logits out, every step
-    model.reset()
-    logits = model.prefill(prompt)
-    e2e_steps = min(args.steps, 128)
-    ranks.barrier()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        logits = model.decode(int(np.argmax(logits)))
-    e2e_s = ranks.max(time.perf_counter() - t0)
+    if not serial:
+        model.reset()
+        e2e_steps, e2e_s = end_to_end(model.prefill(prompt))
 
     # roofline
     positions = range(first_position, first_position + args.steps)
-    step_bytes = weight_bytes(config, stored) + sum(kv_bytes(config, context, p) for p in positions) / args.steps
+    step_bytes = weight_bytes(config, stored, active) + sum(kv_bytes(config, context, p) for p in positions) / args.steps
     step_s = device_ms / 1e3 / args.steps
     peak, peak_kind = measured_hbm()
     if tp:  # each GPU streams its slice of the weights and KV rows
@@ -281,7 +338,9 @@ def run_cuda(args, ranks):
         "warmup": args.warmup, "ms_per_step": round(device_ms / args.steps, 5), "higher_is_better": True,
         "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{args.config}: {config.family} decode, {stored} weights "
-                               f"({weight_bytes(config, stored) / 1e9:.3f} GB/step), greedy, positions "
+                               f"({weight_bytes(config, stored, active) / 1e9:.3f} GB/step"
+                               + (f" at {active:.2f} routed experts per layer and loop" if active else "")
+                               + "), greedy, positions "
                                f"{first_position}..{first_position + args.steps - 1}",
                    "context": context, "prompt": prompt_len, "weights_dtype": stored,
                    "l2": "inputs larger than L2 (weights stream from HBM every step)",
@@ -297,9 +356,12 @@ def run_cuda(args, ranks):
                     "tokens": prompt_len,
                     "note": ("batched prefill: tensor-core GEMMs (BF16 weights x FP32 activations split in three BF16 "
                              "parts) + causal attention over the chunk, logits of the last token to host"
-                             if batched.value else "prompt runs through the decode kernel token by token")},
+                             if batched.value else
+                             "prompt token by token through the device token step (heavy.cu kernels)"
+                             if config.family == "heavy-medium-2.0" else
+                             "prompt runs through the decode kernel token by token")},
         "clocks": clock_summary,
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * launches_per_step(config),
     }
     return result, config, context, prompt
 
@@ -414,7 +476,7 @@ def main(argv=None):
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=480)
     parser.add_argument("--warmup", type=int, default=16)
-    parser.add_argument("--config", default="nano17", choices=["nano15", "nano17", "lite"])
+    parser.add_argument("--config", default="nano17", choices=["nano15", "nano17", "lite", "lighting", "heavy"])
     parser.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     parser.add_argument("--cpu-tokens", type=int, default=12, help="decode tokens of the CPU baseline sample")
     parser.add_argument("--no-cpu-baseline", action="store_true")

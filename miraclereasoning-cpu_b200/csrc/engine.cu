@@ -1469,6 +1469,21 @@ int mr_model_bench_decode(mr_model *m, int first_token, int steps, float *device
     MR_REQUIRE(device_ms && steps > 0, "bad arguments");
     MR_REQUIRE(first_token >= 0 && first_token < m->cfg.vocab_size, "token outside the vocabulary");
     MR_REQUIRE(m->position + steps <= m->cfg.context_length, "decode steps exceed context_length");
+    if (m->heavy) {
+        if (!m->ev0) MR_CUDA_TRY(cudaEventCreate(&m->ev0));
+        if (!m->ev1) MR_CUDA_TRY(cudaEventCreate(&m->ev1));
+        MR_CUDA_TRY(cudaEventRecord(m->ev0, m->ctx->stream));
+        rc = heavy_greedy_chain(m->heavy, first_token, m->position, steps);
+        if (!rc) MR_CUDA_TRY(cudaEventRecord(m->ev1, m->ctx->stream));
+        const cudaError_t err = cudaStreamSynchronize(m->ctx->stream);
+        if (rc || err != cudaSuccess) {
+            m->failed = true;
+            return rc ? rc : cuda_error(err, "heavy-medium-2.0 decode");
+        }
+        MR_CUDA_TRY(cudaEventElapsedTime(device_ms, m->ev0, m->ev1));
+        m->position += steps;
+        return MR_OK;
+    }
     rc = ensure_feed(m, 1);
     if (!rc) rc = ensure_gen(m, steps);
     if (rc) return rc;

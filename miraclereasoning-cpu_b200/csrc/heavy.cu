@@ -209,9 +209,45 @@ __global__ void k_rms_row(const float *x, const void *gain, int gain_dtype, floa
     }
 }
 
-__global__ void k_embed_row(const void *embed, int dtype, int token, int width, float *x) {
+// x = embed[token]; the token from `dtoken` (device) when given.
+__global__ void k_embed_row(const void *embed, int dtype, const int *dtoken, int token, int width, float *x) {
+    if (dtoken) token = *dtoken;
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < width; j += gridDim.x * blockDim.x)
         x[j] = load_weight(embed, dtype, static_cast<size_t>(token) * width + j);
+}
+
+// numpy.argmax of the logits (the first maximum) into *token: the next greedy token.
+__global__ void k_argmax(const float *v, int n, int *token) {
+    __shared__ float best_v[32];
+    __shared__ int best_i[32];
+    float bv = -INFINITY;
+    int bi = n;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        if (v[i] > bv || (v[i] == bv && i < bi)) {
+            bv = v[i];
+            bi = i;
+        }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        best_v[threadIdx.x >> 5] = bv;
+        best_i[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+            if (best_v[w] > bv || (best_v[w] == bv && best_i[w] < bi)) {
+                bv = best_v[w];
+                bi = best_i[w];
+            }
+        *token = bi < n ? bi : 0;
+    }
 }
 
 // One warp per head: q heads (blocks 0 .. H-1) and key heads (H .. H+KVH-1):
@@ -562,6 +598,7 @@ struct HeavyEngine {
     int *chosen = nullptr;    // [layers][loops][max_k]
     float *weights = nullptr; // [layers][loops][max_k]
     int *active = nullptr;    // [layers][loops]
+    int *d_token = nullptr;   // device-resident greedy decode: the next token
     std::vector<void *> allocations;
     bool table_set = false;
 };
@@ -679,7 +716,7 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
     const size_t per = static_cast<size_t>(e->layers) * e->loops;
     if ((rc = halloc_n(*e, per * e->H * std::max(1, e->slots), &e->kept)) ||
         (rc = halloc_n(*e, per * e->max_k, &e->chosen)) || (rc = halloc_n(*e, per * e->max_k, &e->weights)) ||
-        (rc = halloc_n(*e, per, &e->active)))
+        (rc = halloc_n(*e, per, &e->active)) || (rc = halloc_n(*e, 1, &e->d_token)))
         return fail(rc);
     MR_CUDA_TRY(cudaMemcpy(e->inv_freq, inv_freq_host, sizeof(float) * (e->d / 2), cudaMemcpyHostToDevice));
     for (size_t i = 0; i < per; ++i) {
@@ -763,10 +800,29 @@ int heavy_set_log1p(HeavyEngine *e, const float *values, int n) {
 
 // One token at `position`: x = embed[token], every layer and inner loop, the
 // final norm and the head; logits (vocab floats) stay in e->logits.
+namespace {
+int token_step(HeavyEngine *e, const int *dtoken, int token, int position);
+}
+
 int heavy_token(HeavyEngine *e, int token, int position) {
+    MR_REQUIRE(token >= 0 && token < e->vocab, "input token is outside the vocabulary");
+    return token_step(e, nullptr, token, position);
+}
+
+int heavy_greedy_chain(HeavyEngine *e, int first_token, int position, int steps) {
+    MR_REQUIRE(first_token >= 0 && first_token < e->vocab, "input token is outside the vocabulary");
+    for (int i = 0; i < steps; ++i) {
+        if (int rc = token_step(e, i ? e->d_token : nullptr, first_token, position + i)) return rc;
+        k_argmax<<<1, 1024, 0, e->stream>>>(e->logits, e->vocab, e->d_token);
+    }
+    MR_CUDA_TRY(cudaGetLastError());
+    return MR_OK;
+}
+
+namespace {
+int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
     MR_REQUIRE(e->table_set, "heavy-medium-2.0: the distance-penalty table has not been set");
     MR_REQUIRE(position >= 0 && position < e->context, "position %d outside the context", position);
-    MR_REQUIRE(token >= 0 && token < e->vocab, "input token is outside the vocabulary");
     cudaStream_t s = e->stream;
     const int width = e->KVH * e->d, count = position + 1;
     const int length = std::min(e->window, count), start = count - length;
@@ -775,7 +831,7 @@ int heavy_token(HeavyEngine *e, int token, int position) {
     const int slots_total = e->max_k + e->shared;
     const float loop_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::sqrt((double)e->loops));
     const float shared_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::max(e->shared, 1));
-    k_embed_row<<<(e->hidden + 255) / 256, 256, 0, s>>>(e->embed, e->embed_dt, token, e->hidden, e->x);
+    k_embed_row<<<(e->hidden + 255) / 256, 256, 0, s>>>(e->embed, e->embed_dt, dtoken, token, e->hidden, e->x);
     for (int l = 0; l < e->layers; ++l) {
         HeavyLayer &Ly = e->L[l];
         for (int loop = 0; loop < e->loops; ++loop) {
@@ -858,6 +914,7 @@ int heavy_token(HeavyEngine *e, int token, int position) {
     MR_CUDA_TRY(cudaGetLastError());
     return MR_OK;
 }
+}  // namespace
 
 const float *heavy_logits(const HeavyEngine *e) { return e->logits; }
 

@@ -24,6 +24,10 @@ int heavy_set_log1p(HeavyEngine *e, const float *values, int n);
 int heavy_token(HeavyEngine *e, int token, int position);
 const float *heavy_logits(const HeavyEngine *e);
 
+// Greedy decode entirely on the device: `steps` tokens from `position`, each
+// step's input the previous step's argmax (the first: first_token).
+int heavy_greedy_chain(HeavyEngine *e, int first_token, int position, int steps);
+
 // Decisions of the last token (synchronise the stream): kept block ids
 // (heads x global_slots, ascending per head, -1 padded) and the experts in
 // rank order with their weights (router_top_k_max entries, -1 / 0 padded).
