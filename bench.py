@@ -158,10 +158,10 @@ def ncu_traffic(config_name):
 
 def launches_per_step(config):
     """Kernels one decode step launches: the persistent decode kernel once, or
-    Heavy Medium's device step (embedding row; per layer and inner loop 15
-    kernels; final norm, head, greedy argmax)."""
+    Heavy Medium's device step (embedding row; per layer and inner loop 13
+    kernels; the head with its norm, greedy argmax)."""
     if config.family == "heavy-medium-2.0":
-        return 1 + 15 * config.layers * config.inner_loop_steps + 3
+        return 1 + 13 * config.layers * config.inner_loop_steps + 2
     return 1
 
 
@@ -372,6 +372,7 @@ def run_profile_case(args):
     syn = _pkg("synthetic")
     config = syn.config_for(args.config)
     context, prompt_len, _ = syn.WORKLOADS[args.config]
+    prompt_len = args.profile_prompt or prompt_len
     backend = _pkg("backend").CUDABackend(device_index=int(os.environ.get("LOCAL_RANK", "0")))
     model = _pkg("model").MiracleModel.synthetic(config, stored=syn.STORED_DTYPE[args.config], backend=backend,
                                                  context_length=context)
@@ -487,6 +488,8 @@ def main(argv=None):
     parser.add_argument("--profile-steps", type=int, default=0,
                         help="profiling workload for ncu: build the model, prefill the prompt, run this many "
                              "decode steps, print no measurement")
+    parser.add_argument("--profile-prompt", type=int, default=0,
+                        help="with --profile-steps: a prompt of this many tokens instead of the workload's")
     parser.add_argument("--profile-prefill", type=int, default=0,
                         help="profiling workload for ncu: build the model, prefill the prompt this many times")
     args = parser.parse_args(argv)

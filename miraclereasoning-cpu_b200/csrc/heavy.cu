@@ -5,8 +5,8 @@
 // with kernel launches only: no host round trip inside a step.
 //
 // Per (layer, inner loop):
-//   1. h = RMSNorm(x, a_norm)                                    k_rms_row
-//   2. q = W_q h, latent = W_latent h                            k_gemv (two segments)
+//   1-2. h = RMSNorm(x, a_norm) (while staging the input);
+//      q = W_q h, latent = W_latent h                            k_gemv (two segments)
 //   3. kv = W_kv_up latent                                       k_gemv
 //   4. q = RoPE(RMSNorm_noaffine(q)); k = RoPE(RMSNorm_noaffine(kv[:w]));
 //      append k, v = kv[w:] to the loop's ring                   k_heads_norm_rope
@@ -17,7 +17,7 @@
 //      `global_slots` per head, the rest masked (model.py:219-225) k_block_topk
 //   8. softmax + value mix over window rows and kept blocks     k_sparse_attend
 //   9. x += s * W_o attended                                     k_gemv (residual)
-//  10. f = RMSNorm(x, f_norm); router logits                     k_rms_row, k_gemv
+//  10. f = RMSNorm(x, f_norm) (while staging); router logits    k_gemv
 //  11. routing (model.py:235-250): biases, temperature, softmax,
 //      stable top-k, confidence / entropy -> active count,
 //      renormalised weights                                      k_route
@@ -50,9 +50,8 @@ int model_tensor(mr_model *m, const char *name, const void **ptr, int *dtype, in
 
 namespace {
 
-constexpr int kGemvThreads = 256;            // 8 warps
-constexpr int kRowsPerWarp = 2;
-constexpr int kGemvRows = 8 * kRowsPerWarp;  // rows per block
+constexpr int kGemvThreads = 256;  // 8 warps
+constexpr int kGemvRows = 8;       // rows per block (one per warp)
 constexpr int kMaxSegs = 4;
 
 #define FADD __fadd_rn
@@ -97,53 +96,71 @@ __device__ __forceinline__ float dot16(const uint4 &w, const float *x, int dtype
     return s;
 }
 
-// One warp: dot products of two rows (cols elements of `dtype` at p0, p1;
-// p1 NULL: one row) with x (shared memory); every lane gets the sums.
+// One warp: dot products of up to two rows (cols elements of `dtype` at p0,
+// p1; p1 NULL: one row) with x (shared memory); every lane gets the sums.
+// Each lane keeps eight 16-byte loads of a row in flight.
 __device__ __forceinline__ void warp_dot2(const char *p0, const char *p1, int dtype, int cols, const float *x,
                                           float &y0, float &y1) {
     const int lane = threadIdx.x & 31;
     const int esz = dtype == MR_DTYPE_F32 ? 4 : 2, per = 16 / esz;
     const size_t row_bytes = static_cast<size_t>(cols) * esz;
-    const bool two = p1 != nullptr;
-    if (!two) p1 = p0;
-    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+    float a0 = 0.f, a1 = 0.f;
     if ((row_bytes & 15) == 0) {
         const int nv = cols / per;
-        int c = lane;
-        if (two) {
-            for (; c + 32 < nv; c += 64) {
-                const uint4 w00 = ld_stream16(p0 + 16 * c), w01 = ld_stream16(p0 + 16 * (c + 32));
-                const uint4 w10 = ld_stream16(p1 + 16 * c), w11 = ld_stream16(p1 + 16 * (c + 32));
-                a0 += dot16(w00, x + per * c, dtype);
-                b0 += dot16(w01, x + per * (c + 32), dtype);
-                a1 += dot16(w10, x + per * c, dtype);
-                b1 += dot16(w11, x + per * (c + 32), dtype);
+        for (int c0 = lane; c0 < nv; c0 += 32 * 8) {
+            uint4 w0[8], w1[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + 32 * u;
+                w0[u] = c < nv ? ld_stream16(p0 + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
+                w1[u] = (p1 && c < nv) ? ld_stream16(p1 + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
             }
-            if (c < nv) {
-                a0 += dot16(ld_stream16(p0 + 16 * c), x + per * c, dtype);
-                a1 += dot16(ld_stream16(p1 + 16 * c), x + per * c, dtype);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + 32 * u;
+                if (c < nv) {
+                    a0 += dot16(w0[u], x + per * c, dtype);
+                    if (p1) a1 += dot16(w1[u], x + per * c, dtype);
+                }
             }
-        } else {
-            for (; c + 96 < nv; c += 128) {
-                const uint4 w0 = ld_stream16(p0 + 16 * c), w1 = ld_stream16(p0 + 16 * (c + 32));
-                const uint4 w2 = ld_stream16(p0 + 16 * (c + 64)), w3 = ld_stream16(p0 + 16 * (c + 96));
-                a0 += dot16(w0, x + per * c, dtype);
-                b0 += dot16(w1, x + per * (c + 32), dtype);
-                a1 += dot16(w2, x + per * (c + 64), dtype);
-                b1 += dot16(w3, x + per * (c + 96), dtype);
-            }
-            for (; c < nv; c += 32) a0 += dot16(ld_stream16(p0 + 16 * c), x + per * c, dtype);
-            a0 = (a0 + b0) + (a1 + b1);
-            a1 = b0 = b1 = 0.f;
         }
     } else {  // rows that are not whole 16-byte chunks: element by element
         for (int j = lane; j < cols; j += 32) {
             a0 = fmaf(load_weight(p0, dtype, j), x[j], a0);
-            if (two) a1 = fmaf(load_weight(p1, dtype, j), x[j], a1);
+            if (p1) a1 = fmaf(load_weight(p1, dtype, j), x[j], a1);
         }
     }
-    y0 = warp_sum(a0 + b0);
-    y1 = warp_sum(a1 + b1);
+    y0 = warp_sum(a0);
+    y1 = warp_sum(a1);
+}
+
+// Stages x (n floats) in shared memory, or RMSNorm(x) with `gain`
+// (kernels.cl:19-28: (x * (1 / sqrt(mean(x^2) + eps))) * gain) when `norm`:
+// every block computes the same factor from the same sums.
+__device__ void stage_input(const float *x, int n, bool norm, const void *gain, int gain_dtype, float eps,
+                            float *xs) {
+    __shared__ float red[32];
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = x[i];
+        xs[i] = v;
+        ss = fmaf(v, v, ss);
+    }
+    if (!norm) {
+        __syncthreads();
+        return;
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float total = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) total += red[w];
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(FADD(__fdiv_rn(total, static_cast<float>(n)), eps)));
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float g = gain ? load_weight(gain, gain_dtype, i) : 1.0f;
+        xs[i] = FMUL(FMUL(xs[i], scale), g);
+    }
+    __syncthreads();
 }
 
 struct GemvSeg {
@@ -153,6 +170,10 @@ struct GemvSeg {
     float *y;
     int residual;  // y = y + scale * (W x) (kernels.cl add), else y = W x
     float scale;
+    int norm;      // the input is RMSNorm(x, gain) (computed while staging)
+    const void *gain;
+    int gain_dtype;
+    float eps;
 };
 struct GemvArgs {
     GemvSeg s[kMaxSegs];
@@ -160,53 +181,21 @@ struct GemvArgs {
     int nseg;
 };
 
-// y = W x for up to kMaxSegs matrices; each block takes kGemvRows rows of one
-// segment and stages that segment's x in shared memory.
+// y = W x for up to kMaxSegs matrices; each block takes kGemvRows rows (one
+// per warp) of one segment and stages that segment's input in shared memory.
 __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a) {
     extern __shared__ __align__(16) float xs[];
     int si = 0;
     while (si + 1 < a.nseg && static_cast<int>(blockIdx.x) >= a.first[si + 1]) ++si;
     const GemvSeg &s = a.s[si];
-    for (int i = threadIdx.x; i < s.cols; i += blockDim.x) xs[i] = s.x[i];
-    __syncthreads();
+    stage_input(s.x, s.cols, s.norm != 0, s.gain, s.gain_dtype, s.eps, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int r0 = (blockIdx.x - a.first[si]) * kGemvRows + warp * kRowsPerWarp;
-    if (r0 >= s.rows) return;
-    const int r1 = r0 + 1 < s.rows ? r0 + 1 : -1;
+    const int r = (blockIdx.x - a.first[si]) * kGemvRows + warp;
+    if (r >= s.rows) return;
     const size_t row_bytes = static_cast<size_t>(s.cols) * (s.dtype == MR_DTYPE_F32 ? 4 : 2);
-    const char *base = static_cast<const char *>(s.w);
-    float y0, y1;
-    warp_dot2(base + r0 * row_bytes, r1 >= 0 ? base + r1 * row_bytes : nullptr, s.dtype, s.cols, xs, y0, y1);
-    if (lane == 0) {
-        if (s.residual) {
-            s.y[r0] = FADD(s.y[r0], FMUL(s.scale, y0));
-            if (r1 >= 0) s.y[r1] = FADD(s.y[r1], FMUL(s.scale, y1));
-        } else {
-            s.y[r0] = y0;
-            if (r1 >= 0) s.y[r1] = y1;
-        }
-    }
-}
-
-// y = (x * (1 / sqrt(mean(x^2) + eps))) * gain (kernels.cl:19-28), one row, one block.
-__global__ void k_rms_row(const float *x, const void *gain, int gain_dtype, float *y, int width, float eps) {
-    __shared__ float red[32];
-    float ss = 0.f;
-    for (int j = threadIdx.x; j < width; j += blockDim.x) ss = fmaf(x[j], x[j], ss);
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-        v = warp_sum(v);
-        if (threadIdx.x == 0) red[0] = v;
-    }
-    __syncthreads();
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(FADD(__fdiv_rn(red[0], static_cast<float>(width)), eps)));
-    for (int j = threadIdx.x; j < width; j += blockDim.x) {
-        const float g = gain ? load_weight(gain, gain_dtype, j) : 1.0f;
-        y[j] = FMUL(FMUL(x[j], scale), g);
-    }
+    float y, unused;
+    warp_dot2(static_cast<const char *>(s.w) + r * row_bytes, nullptr, s.dtype, s.cols, xs, y, unused);
+    if (lane == 0) s.y[r] = s.residual ? FADD(s.y[r], FMUL(s.scale, y)) : y;
 }
 
 // x = embed[token]; the token from `dtoken` (device) when given.
@@ -392,15 +381,18 @@ __global__ void k_sparse_attend(const float *scores, const float *v_ring, const 
     // value mix: thread (j, part) sums keys part, part + parts, ...
     const int parts = blockDim.x / dim;
     const int j = threadIdx.x % dim, part = threadIdx.x / dim;
-    float acc = 0.f;
+    float acc = 0.f, acc2 = 0.f;
     if (part < parts) {
-        for (int t = part; t < total; t += parts) {
+        const float *vr = v_ring + static_cast<size_t>(start) * width + static_cast<size_t>(kh) * dim + j;
+        const float *vm = v_mean + static_cast<size_t>(kh) * dim + j;
+        int t = part;
+#pragma unroll 4
+        for (; t < length; t += parts) acc = fmaf(p[t], vr[static_cast<size_t>(t) * width], acc);
+        for (; t < total; t += parts) {  // block means: only the kept ones carry weight
             const float w = p[t];
-            if (w == 0.f) continue;
-            const float v = t < length ? v_ring[static_cast<size_t>(start + t) * width + static_cast<size_t>(kh) * dim + j]
-                                       : v_mean[static_cast<size_t>(t - length) * width + static_cast<size_t>(kh) * dim + j];
-            acc = fmaf(w, v, acc);
+            if (w != 0.f) acc2 = fmaf(w, vm[static_cast<size_t>(t - length) * width], acc2);
         }
+        acc += acc2;
     }
     __syncthreads();
     float *partial = p;  // the weights are no longer needed
@@ -449,47 +441,61 @@ struct RouteArgs {
     int *active;                 // 1
 };
 
-// model.py:233-250 for one token, one thread (at most 256 experts).
-__global__ void k_route(RouteArgs a) {
-    __shared__ float coarse[256], logits[256], probs[256], terms[256];
+// model.py:233-250 for one token (at most 256 experts, one thread each):
+// the element-wise steps in parallel, the running sums and the final
+// arithmetic in thread 0 in the reference's order.
+__global__ void __launch_bounds__(256) k_route(RouteArgs a) {
+    __shared__ float coarse[256], logits[256], ex[256], probs[256], terms[256];
     __shared__ int order[64];
-    if (threadIdx.x != 0) return;
-    const int E = a.experts, G = a.groups;
-    for (int g = 0; g < G; ++g)
-        coarse[g] = FADD(a.router[g], FADD(load_weight(a.coarse_bias, a.bias_dtype[0], g),
-                                           load_weight(a.group_bias, a.bias_dtype[1], g)));
-    for (int e = 0; e < E; ++e) {
-        const float fine = FADD(a.router[G + e], FADD(load_weight(a.fine_bias, a.bias_dtype[2], e),
-                                                     load_weight(a.expert_bias, a.bias_dtype[3], e)));
-        const int g = min(e / a.per_group, G - 1);
-        logits[e] = __fdiv_rn(FADD(fine, coarse[g]), a.temperature);
+    __shared__ float m_s, den_s;
+    const int t = threadIdx.x, E = a.experts, G = a.groups, K = a.max_k;
+    if (t < G)
+        coarse[t] = FADD(a.router[t], FADD(load_weight(a.coarse_bias, a.bias_dtype[0], t),
+                                           load_weight(a.group_bias, a.bias_dtype[1], t)));
+    if (t < K) order[t] = -1;
+    __syncthreads();
+    if (t < E) {
+        const float fine = FADD(a.router[G + t], FADD(load_weight(a.fine_bias, a.bias_dtype[2], t),
+                                                     load_weight(a.expert_bias, a.bias_dtype[3], t)));
+        logits[t] = __fdiv_rn(FADD(fine, coarse[min(t / a.per_group, G - 1)]), a.temperature);
     }
-    // the softmax kernel (kernels.cl:76-84): max, one running sum, divisions
-    float m = -INFINITY;
-    for (int e = 0; e < E; ++e) m = fmaxf(m, logits[e]);
-    float den = 0.f;
-    for (int e = 0; e < E; ++e) den = FADD(den, expf(__fsub_rn(logits[e], m)));
-    for (int e = 0; e < E; ++e) probs[e] = __fdiv_rn(expf(__fsub_rn(logits[e], m)), den);
-    // np.argsort(-probs, kind="stable")[:max_k]
-    const int K = a.max_k;
-    for (int k = 0; k < K; ++k) order[k] = -1;
-    for (int e = 0; e < E; ++e) {
+    __syncthreads();
+    if (t == 0) {  // the softmax kernel (kernels.cl:76-84): the maximum, then one running sum
+        float m = -INFINITY;
+        for (int e = 0; e < E; ++e) m = fmaxf(m, logits[e]);
+        m_s = m;
+    }
+    __syncthreads();
+    if (t < E) ex[t] = expf(__fsub_rn(logits[t], m_s));
+    __syncthreads();
+    if (t == 0) {
+        float den = 0.f;
+        for (int e = 0; e < E; ++e) den = FADD(den, ex[e]);
+        den_s = den;
+    }
+    __syncthreads();
+    if (t < E) probs[t] = __fdiv_rn(ex[t], den_s);
+    __syncthreads();
+    if (t < E) {
+        // np.argsort(-probs, kind="stable")[:max_k]: rank = greater values, then equal ones before it
+        const float v = probs[t];
         int rank = 0;
-        for (int j = 0; j < E; ++j) rank += (probs[j] > probs[e]) || (probs[j] == probs[e] && j < e);
-        if (rank < K) order[rank] = e;
+        for (int j = 0; j < E; ++j) rank += (probs[j] > v) || (probs[j] == v && j < t);
+        if (rank < K) order[rank] = t;
+        terms[t] = FMUL(v, logf(fmaxf(v, 1e-9f)));
     }
+    __syncthreads();
+    if (t != 0) return;
     float sel[64];
     for (int k = 0; k < K; ++k) sel[k] = order[k] >= 0 ? probs[order[k]] : 0.f;
     const float confidence = __fsub_rn(sel[0], sel[min(K - 1, 1)]);
-    for (int e = 0; e < E; ++e) terms[e] = FMUL(probs[e], logf(fmaxf(probs[e], 1e-9f)));
     const float entropy = -numpy_pairwise_sum(terms, E);
     const float width = rintf(FADD(FMUL(__fsub_rn(1.0f, confidence), 2.0f),
                                    __fdiv_rn(entropy, fmaxf(a.log_experts, 1.0f))));
     const float total = FADD(static_cast<float>(a.min_k), width);
     const int active = static_cast<int>(fminf(fmaxf(total, static_cast<float>(a.min_k)), static_cast<float>(K)));
     for (int k = active; k < K; ++k) sel[k] = 0.f;
-    const float sum = numpy_pairwise_sum(sel, K);
-    const float norm = fmaxf(sum, 1e-9f);
+    const float norm = fmaxf(numpy_pairwise_sum(sel, K), 1e-9f);
     for (int k = 0; k < K; ++k) {
         a.chosen[k] = k < active ? order[k] : -1;
         a.weights[k] = k < active ? __fdiv_rn(sel[k], norm) : 0.f;
@@ -503,7 +509,10 @@ struct ExpertArgs {
     const void *const *down;
     int dtype, ffn, hidden, experts, max_k, shared;
     const int *chosen, *active;
-    const float *x;           // RMSNorm(x, f_norm)
+    const float *x;           // the residual stream; the experts read RMSNorm(x, f_norm)
+    const void *norm_gain;
+    int norm_dtype;
+    float eps;
     float *act;               // [max_k + shared][ffn] SwiGLU activations
     float *out;               // [max_k + shared][hidden]
 };
@@ -520,8 +529,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_expert_gate_up(ExpertArgs a) {
     extern __shared__ __align__(16) float xs[];
     const int slot = blockIdx.y, e = slot_expert(a, slot);
     if (e < 0) return;
-    for (int i = threadIdx.x; i < a.hidden; i += blockDim.x) xs[i] = a.x[i];
-    __syncthreads();
+    stage_input(a.x, a.hidden, true, a.norm_gain, a.norm_dtype, a.eps, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.x * 8 + warp;
     if (r >= a.ffn) return;
@@ -537,20 +545,14 @@ __global__ void __launch_bounds__(kGemvThreads) k_expert_down(ExpertArgs a) {
     extern __shared__ __align__(16) float xs[];
     const int slot = blockIdx.y, e = slot_expert(a, slot);
     if (e < 0) return;
-    for (int i = threadIdx.x; i < a.ffn; i += blockDim.x) xs[i] = a.act[static_cast<size_t>(slot) * a.ffn + i];
-    __syncthreads();
+    stage_input(a.act + static_cast<size_t>(slot) * a.ffn, a.ffn, false, nullptr, 0, 0.f, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int r0 = blockIdx.x * kGemvRows + warp * kRowsPerWarp;
-    if (r0 >= a.hidden) return;
-    const int r1 = r0 + 1 < a.hidden ? r0 + 1 : -1;
+    const int r = blockIdx.x * kGemvRows + warp;
+    if (r >= a.hidden) return;
     const size_t row_bytes = static_cast<size_t>(a.ffn) * (a.dtype == MR_DTYPE_F32 ? 4 : 2);
-    const char *base = static_cast<const char *>(a.down[e]);
-    float y0, y1;
-    warp_dot2(base + r0 * row_bytes, r1 >= 0 ? base + r1 * row_bytes : nullptr, a.dtype, a.ffn, xs, y0, y1);
-    if (lane == 0) {
-        a.out[static_cast<size_t>(slot) * a.hidden + r0] = y0;
-        if (r1 >= 0) a.out[static_cast<size_t>(slot) * a.hidden + r1] = y1;
-    }
+    float y, unused;
+    warp_dot2(static_cast<const char *>(a.down[e]) + r * row_bytes, nullptr, a.dtype, a.ffn, xs, y, unused);
+    if (lane == 0) a.out[static_cast<size_t>(slot) * a.hidden + r] = y;
 }
 
 // model.py:251-255 then 266: result = 0; result += w_k * expert_k (rank
@@ -748,6 +750,14 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
             (rc = tensor_of(m, p + "router.expert_bias", &Ly.expert_bias, &Ly.bias_dt[3], &rows, &cols)))
             return fail(rc);
         Ly.o.residual = 1;
+        for (GemvSeg *g : {&Ly.q, &Ly.latent, &Ly.coarse, &Ly.fine}) {  // inputs: RMSNorm(x, a_norm / f_norm)
+            const bool attention = g == &Ly.q || g == &Ly.latent;
+            g->x = e->x;
+            g->norm = 1;
+            g->gain = attention ? Ly.a_norm : Ly.f_norm;
+            g->gain_dtype = attention ? Ly.a_norm_dt : Ly.f_norm_dt;
+            g->eps = e->eps;
+        }
         std::vector<const void *> gate, up, down;
         int dtype = -1;
         for (int i = 0; i < e->experts + e->shared; ++i) {
@@ -837,7 +847,6 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
         for (int loop = 0; loop < e->loops; ++loop) {
             const size_t li = static_cast<size_t>(l) * e->loops + loop;
             // attention (model.py:192-229)
-            k_rms_row<<<1, 1024, 0, s>>>(e->x, Ly.a_norm, Ly.a_norm_dt, e->h, e->hidden, e->eps);
             if (int rc = launch_gemv(*e, {Ly.q, Ly.latent})) return rc;
             if (int rc = launch_gemv(*e, {Ly.kv_up})) return rc;
             k_heads_norm_rope<<<e->H + e->KVH, 32, 0, s>>>(e->q, e->kv, e->k_ring[li], e->v_ring[li], e->inv_freq, e->H,
@@ -859,7 +868,6 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             o.scale = loop_scale;
             if (int rc = launch_gemv(*e, {o})) return rc;
             // mixture of experts (model.py:231-255)
-            k_rms_row<<<1, 1024, 0, s>>>(e->x, Ly.f_norm, Ly.f_norm_dt, e->h, e->hidden, e->eps);
             if (int rc = launch_gemv(*e, {Ly.coarse, Ly.fine})) return rc;
             RouteArgs ra{};
             ra.router = e->router;
@@ -878,7 +886,7 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             ra.chosen = e->chosen + li * e->max_k;
             ra.weights = e->weights + li * e->max_k;
             ra.active = e->active + li;
-            k_route<<<1, 32, 0, s>>>(ra);
+            k_route<<<1, 256, 0, s>>>(ra);
             ExpertArgs ea{};
             ea.gate = Ly.d_gate;
             ea.up = Ly.d_up;
@@ -891,7 +899,10 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             ea.shared = e->shared;
             ea.chosen = ra.chosen;
             ea.active = ra.active;
-            ea.x = e->h;
+            ea.x = e->x;
+            ea.norm_gain = Ly.f_norm;
+            ea.norm_dtype = Ly.f_norm_dt;
+            ea.eps = e->eps;
             ea.act = e->act;
             ea.out = e->eout;
             k_expert_gate_up<<<dim3((e->ffn + 7) / 8, slots_total), kGemvThreads,
@@ -902,14 +913,17 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             MR_CUDA_TRY(cudaGetLastError());
         }
     }
-    k_rms_row<<<1, 1024, 0, s>>>(e->x, e->final_norm, e->final_norm_dt, e->h, e->hidden, e->eps);
     GemvSeg head{};
     head.w = e->head;
     head.dtype = e->head_dt;
     head.rows = e->vocab;
     head.cols = e->hidden;
-    head.x = e->h;
+    head.x = e->x;
     head.y = e->logits;
+    head.norm = 1;
+    head.gain = e->final_norm;
+    head.gain_dtype = e->final_norm_dt;
+    head.eps = e->eps;
     if (int rc = launch_gemv(*e, {head})) return rc;
     MR_CUDA_TRY(cudaGetLastError());
     return MR_OK;
