@@ -57,6 +57,15 @@ constexpr int kMaxSegs = 4;
 #define FADD __fadd_rn
 #define FMUL __fmul_rn
 
+// Programmatic dependent launch: every kernel lets the next one be scheduled
+// as soon as it starts (pdl_trigger), and waits for the previous one to
+// complete, with its writes visible, before it reads anything an earlier
+// kernel wrote or writes anything (pdl_wait).  Only loads of the weights,
+// which nothing writes, come before the wait: the weight stream of a GEMV
+// starts while the kernel before it finishes.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint4 ld_stream16(const void *p) {
     uint4 v;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -96,33 +105,56 @@ __device__ __forceinline__ float dot16(const uint4 &w, const float *x, int dtype
     return s;
 }
 
+// The first N 16-byte chunks per lane of up to two rows, loaded before the
+// block stages its input so that the weight stream starts at once.  (Sixteen
+// per lane, a whole 4096-wide BF16 row, measured no faster: the registers
+// halve the resident blocks.)
+constexpr int kBatch = 8;
+template <int N>
+struct RowBatchT {
+    uint4 w0[N], w1[N];
+};
+__device__ __forceinline__ bool whole_chunks(int dtype, int cols) {
+    return ((static_cast<size_t>(cols) * (dtype == MR_DTYPE_F32 ? 4 : 2)) & 15) == 0;
+}
+template <int N>
+__device__ __forceinline__ void load_batch(const char *p0, const char *p1, int nv, int c0, RowBatchT<N> &b) {
+#pragma unroll
+    for (int u = 0; u < N; ++u) {
+        const int c = c0 + 32 * u;
+        b.w0[u] = c < nv ? ld_stream16(p0 + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
+        b.w1[u] = (p1 && c < nv) ? ld_stream16(p1 + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+template <int N>
+__device__ __forceinline__ void prefetch_rows(const char *p0, const char *p1, int dtype, int cols, RowBatchT<N> &b) {
+    if (whole_chunks(dtype, cols)) load_batch(p0, p1, cols / (dtype == MR_DTYPE_F32 ? 4 : 8), threadIdx.x & 31, b);
+}
+
 // One warp: dot products of up to two rows (cols elements of `dtype` at p0,
-// p1; p1 NULL: one row) with x (shared memory); every lane gets the sums.
-// Each lane keeps eight 16-byte loads of a row in flight.
+// p1; p1 NULL: one row) with x (shared memory), the first chunks already in
+// `b` (prefetch_rows); every lane gets the sums.  Each lane keeps N 16-byte
+// loads of a row in flight.
+template <int N>
 __device__ __forceinline__ void warp_dot2(const char *p0, const char *p1, int dtype, int cols, const float *x,
-                                          float &y0, float &y1) {
+                                          RowBatchT<N> &b, float &y0, float &y1) {
     const int lane = threadIdx.x & 31;
-    const int esz = dtype == MR_DTYPE_F32 ? 4 : 2, per = 16 / esz;
-    const size_t row_bytes = static_cast<size_t>(cols) * esz;
+    const int per = dtype == MR_DTYPE_F32 ? 4 : 8;
     float a0 = 0.f, a1 = 0.f;
-    if ((row_bytes & 15) == 0) {
+    if (whole_chunks(dtype, cols)) {
         const int nv = cols / per;
-        for (int c0 = lane; c0 < nv; c0 += 32 * 8) {
-            uint4 w0[8], w1[8];
+        for (int c0 = lane;;) {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int c = c0 + 32 * u;
-                w0[u] = c < nv ? ld_stream16(p0 + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
-                w1[u] = (p1 && c < nv) ? ld_stream16(p1 + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < N; ++u) {
                 const int c = c0 + 32 * u;
                 if (c < nv) {
-                    a0 += dot16(w0[u], x + per * c, dtype);
-                    if (p1) a1 += dot16(w1[u], x + per * c, dtype);
+                    a0 += dot16(b.w0[u], x + per * c, dtype);
+                    if (p1) a1 += dot16(b.w1[u], x + per * c, dtype);
                 }
             }
+            c0 += 32 * N;
+            if (c0 >= nv) break;
+            load_batch(p0, p1, nv, c0, b);
         }
     } else {  // rows that are not whole 16-byte chunks: element by element
         for (int j = lane; j < cols; j += 32) {
@@ -185,21 +217,28 @@ struct GemvArgs {
 // per warp) of one segment and stages that segment's input in shared memory.
 __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a) {
     extern __shared__ __align__(16) float xs[];
+    pdl_trigger();
     int si = 0;
     while (si + 1 < a.nseg && static_cast<int>(blockIdx.x) >= a.first[si + 1]) ++si;
     const GemvSeg &s = a.s[si];
-    stage_input(s.x, s.cols, s.norm != 0, s.gain, s.gain_dtype, s.eps, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = (blockIdx.x - a.first[si]) * kGemvRows + warp;
-    if (r >= s.rows) return;
     const size_t row_bytes = static_cast<size_t>(s.cols) * (s.dtype == MR_DTYPE_F32 ? 4 : 2);
+    const char *row = static_cast<const char *>(s.w) + static_cast<size_t>(min(r, s.rows - 1)) * row_bytes;
+    RowBatchT<kBatch> b;
+    if (r < s.rows) prefetch_rows(row, nullptr, s.dtype, s.cols, b);
+    pdl_wait();
+    stage_input(s.x, s.cols, s.norm != 0, s.gain, s.gain_dtype, s.eps, xs);
+    if (r >= s.rows) return;
     float y, unused;
-    warp_dot2(static_cast<const char *>(s.w) + r * row_bytes, nullptr, s.dtype, s.cols, xs, y, unused);
+    warp_dot2(row, nullptr, s.dtype, s.cols, xs, b, y, unused);
     if (lane == 0) s.y[r] = s.residual ? FADD(s.y[r], FMUL(s.scale, y)) : y;
 }
 
 // x = embed[token]; the token from `dtoken` (device) when given.
 __global__ void k_embed_row(const void *embed, int dtype, const int *dtoken, int token, int width, float *x) {
+    pdl_trigger();
+    pdl_wait();
     if (dtoken) token = *dtoken;
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < width; j += gridDim.x * blockDim.x)
         x[j] = load_weight(embed, dtype, static_cast<size_t>(token) * width + j);
@@ -207,6 +246,8 @@ __global__ void k_embed_row(const void *embed, int dtype, const int *dtoken, int
 
 // numpy.argmax of the logits (the first maximum) into *token: the next greedy token.
 __global__ void k_argmax(const float *v, int n, int *token) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float best_v[32];
     __shared__ int best_i[32];
     float bv = -INFINITY;
@@ -244,6 +285,8 @@ __global__ void k_argmax(const float *v, int n, int *token) {
 // (kernels.cl:30-44); keys and values go to ring row `row`.
 __global__ void k_heads_norm_rope(float *q, const float *kv, float *k_ring, float *v_ring, const float *inv_freq,
                                   int heads, int kv_heads, int dim, int split_half, int position, int row) {
+    pdl_trigger();
+    pdl_wait();
     const int h = blockIdx.x, lane = threadIdx.x;
     const int width = kv_heads * dim;
     float *dst;
@@ -285,6 +328,8 @@ __global__ void k_heads_norm_rope(float *q, const float *kv, float *k_ring, floa
 // order, then one division) for keys and values; full blocks never change.
 __global__ void k_block_mean_last(const float *k_ring, const float *v_ring, float *k_mean, float *v_mean, int count,
                                   int width, int block) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= 2 * width) return;
     const int j = i % width;
@@ -300,6 +345,8 @@ __global__ void k_block_mean_last(const float *k_ring, const float *v_ring, floa
 // block means (kernels.cl:59-74).  One warp per score.
 __global__ void k_sparse_scores(const float *q, const float *k_ring, const float *k_mean, float *scores, int heads,
                                 int kv_heads, int dim, int start, int length, int blocks) {
+    pdl_trigger();
+    pdl_wait();
     const int total = length + blocks;
     const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (item >= heads * total) return;
@@ -321,6 +368,8 @@ __global__ void k_sparse_scores(const float *q, const float *k_ring, const float
 // The kept block ids go to `kept` in ascending order, -1 padded to `slots_max`.
 __global__ void k_block_topk(float *scores, int total, int length, int blocks, int block, int position,
                              const float *log1p_table, float slope, int slots, int slots_max, int *kept) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float sb[];
     int *keep = reinterpret_cast<int *>(sb + blocks);
     const int h = blockIdx.x;
@@ -353,6 +402,8 @@ __global__ void k_block_topk(float *scores, int total, int length, int blocks, i
 // block mean values (kernels.cl:76-107).  One block per head.
 __global__ void k_sparse_attend(const float *scores, const float *v_ring, const float *v_mean, float *out, int heads,
                                 int kv_heads, int dim, int start, int length, int blocks) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float p[];
     __shared__ float red[32];
     const int h = blockIdx.x, total = length + blocks;
@@ -445,6 +496,8 @@ struct RouteArgs {
 // the element-wise steps in parallel, the running sums and the final
 // arithmetic in thread 0 in the reference's order.
 __global__ void __launch_bounds__(256) k_route(RouteArgs a) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float coarse[256], logits[256], ex[256], probs[256], terms[256];
     __shared__ int order[64];
     __shared__ float m_s, den_s;
@@ -526,32 +579,42 @@ __device__ __forceinline__ int slot_expert(const ExpertArgs &a, int slot) {
 
 // act[slot][r] = silu(gate_r . x) * (up_r . x) (kernels.cl:46-50); grid (row blocks, slots).
 __global__ void __launch_bounds__(kGemvThreads) k_expert_gate_up(ExpertArgs a) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) float xs[];
     const int slot = blockIdx.y, e = slot_expert(a, slot);
     if (e < 0) return;
-    stage_input(a.x, a.hidden, true, a.norm_gain, a.norm_dtype, a.eps, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.x * 8 + warp;
-    if (r >= a.ffn) return;
     const size_t row_bytes = static_cast<size_t>(a.hidden) * (a.dtype == MR_DTYPE_F32 ? 4 : 2);
+    const size_t off = static_cast<size_t>(min(r, a.ffn - 1)) * row_bytes;
+    const char *gp = static_cast<const char *>(a.gate[e]) + off, *up = static_cast<const char *>(a.up[e]) + off;
+    RowBatchT<kBatch> b;
+    if (r < a.ffn) prefetch_rows(gp, up, a.dtype, a.hidden, b);
+    stage_input(a.x, a.hidden, true, a.norm_gain, a.norm_dtype, a.eps, xs);
+    if (r >= a.ffn) return;
     float g, u;
-    warp_dot2(static_cast<const char *>(a.gate[e]) + r * row_bytes, static_cast<const char *>(a.up[e]) + r * row_bytes,
-              a.dtype, a.hidden, xs, g, u);
+    warp_dot2(gp, up, a.dtype, a.hidden, xs, b, g, u);
     if (lane == 0) a.act[static_cast<size_t>(slot) * a.ffn + r] = FMUL(__fdiv_rn(g, FADD(1.0f, expf(-g))), u);
 }
 
 // out[slot][r] = down_r . act[slot]; grid (row blocks, slots).
 __global__ void __launch_bounds__(kGemvThreads) k_expert_down(ExpertArgs a) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) float xs[];
     const int slot = blockIdx.y, e = slot_expert(a, slot);
     if (e < 0) return;
-    stage_input(a.act + static_cast<size_t>(slot) * a.ffn, a.ffn, false, nullptr, 0, 0.f, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.x * kGemvRows + warp;
-    if (r >= a.hidden) return;
     const size_t row_bytes = static_cast<size_t>(a.ffn) * (a.dtype == MR_DTYPE_F32 ? 4 : 2);
+    const char *row = static_cast<const char *>(a.down[e]) + static_cast<size_t>(min(r, a.hidden - 1)) * row_bytes;
+    RowBatchT<kBatch> b;
+    if (r < a.hidden) prefetch_rows(row, nullptr, a.dtype, a.ffn, b);
+    stage_input(a.act + static_cast<size_t>(slot) * a.ffn, a.ffn, false, nullptr, 0, 0.f, xs);
+    if (r >= a.hidden) return;
     float y, unused;
-    warp_dot2(static_cast<const char *>(a.down[e]) + r * row_bytes, nullptr, a.dtype, a.ffn, xs, y, unused);
+    warp_dot2(row, nullptr, a.dtype, a.ffn, xs, b, y, unused);
     if (lane == 0) a.out[static_cast<size_t>(slot) * a.hidden + r] = y;
 }
 
@@ -559,6 +622,8 @@ __global__ void __launch_bounds__(kGemvThreads) k_expert_down(ExpertArgs a) {
 // order); result += (residual_scale / S) * shared_i; x += s * result, each an
 // add kernel (x + scale * y, two roundings).
 __global__ void k_expert_combine(ExpertArgs a, const float *weights, float shared_scale, float scale, float *x) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= a.hidden) return;
     float res = 0.f;
@@ -637,6 +702,23 @@ int seg_of(mr_model *m, const std::string &name, const float *x, float *y, GemvS
     return MR_OK;
 }
 
+// Launch with programmatic stream serialization (see pdl_trigger / pdl_wait).
+template <typename... Params, typename... Args>
+int launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MR_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...));
+    return MR_OK;
+}
+
 int launch_gemv(HeavyEngine &e, std::initializer_list<GemvSeg> segs) {
     GemvArgs a{};
     int blocks = 0, cols = 0;
@@ -647,7 +729,7 @@ int launch_gemv(HeavyEngine &e, std::initializer_list<GemvSeg> segs) {
         cols = std::max(cols, s.cols);
     }
     a.first[a.nseg] = blocks;
-    k_gemv<<<blocks, kGemvThreads, static_cast<size_t>(cols) * sizeof(float) + 16, e.stream>>>(a);
+    if (int rc = launch(k_gemv, blocks, kGemvThreads, static_cast<size_t>(cols) * sizeof(float) + 16, e.stream, a)) return rc;
     MR_CUDA_TRY(cudaGetLastError());
     return MR_OK;
 }
@@ -823,7 +905,7 @@ int heavy_greedy_chain(HeavyEngine *e, int first_token, int position, int steps)
     MR_REQUIRE(first_token >= 0 && first_token < e->vocab, "input token is outside the vocabulary");
     for (int i = 0; i < steps; ++i) {
         if (int rc = token_step(e, i ? e->d_token : nullptr, first_token, position + i)) return rc;
-        k_argmax<<<1, 1024, 0, e->stream>>>(e->logits, e->vocab, e->d_token);
+        if (int rc = launch(k_argmax, 1, 1024, 0, e->stream, e->logits, e->vocab, e->d_token)) return rc;
     }
     MR_CUDA_TRY(cudaGetLastError());
     return MR_OK;
@@ -841,7 +923,7 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
     const int slots_total = e->max_k + e->shared;
     const float loop_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::sqrt((double)e->loops));
     const float shared_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::max(e->shared, 1));
-    k_embed_row<<<(e->hidden + 255) / 256, 256, 0, s>>>(e->embed, e->embed_dt, dtoken, token, e->hidden, e->x);
+    if (int rc = launch(k_embed_row, (e->hidden + 255) / 256, 256, 0, s, e->embed, e->embed_dt, dtoken, token, e->hidden, e->x)) return rc;
     for (int l = 0; l < e->layers; ++l) {
         HeavyLayer &Ly = e->L[l];
         for (int loop = 0; loop < e->loops; ++loop) {
@@ -849,21 +931,21 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             // attention (model.py:192-229)
             if (int rc = launch_gemv(*e, {Ly.q, Ly.latent})) return rc;
             if (int rc = launch_gemv(*e, {Ly.kv_up})) return rc;
-            k_heads_norm_rope<<<e->H + e->KVH, 32, 0, s>>>(e->q, e->kv, e->k_ring[li], e->v_ring[li], e->inv_freq, e->H,
-                                                          e->KVH, e->d, e->split_half, position, position);
-            k_block_mean_last<<<(2 * width + 255) / 256, 256, 0, s>>>(e->k_ring[li], e->v_ring[li], e->k_mean[li],
-                                                                     e->v_mean[li], count, width, e->block);
+            if (int rc = launch(k_heads_norm_rope, e->H + e->KVH, 32, 0, s, e->q, e->kv, e->k_ring[li], e->v_ring[li], e->inv_freq, e->H,
+                                                          e->KVH, e->d, e->split_half, position, position)) return rc;
+            if (int rc = launch(k_block_mean_last, (2 * width + 255) / 256, 256, 0, s, e->k_ring[li], e->v_ring[li], e->k_mean[li],
+                                                                     e->v_mean[li], count, width, e->block)) return rc;
             const int items = e->H * total;
-            k_sparse_scores<<<(items + 7) / 8, 256, 0, s>>>(e->q, e->k_ring[li], e->k_mean[li], e->scores, e->H, e->KVH,
-                                                           e->d, start, length, blocks);
+            if (int rc = launch(k_sparse_scores, (items + 7) / 8, 256, 0, s, e->q, e->k_ring[li], e->k_mean[li], e->scores, e->H, e->KVH,
+                                                           e->d, start, length, blocks)) return rc;
             int *kept = e->kept + li * e->H * std::max(1, e->slots);
-            k_block_topk<<<e->H, 256, static_cast<size_t>(blocks) * (sizeof(float) + sizeof(int)), s>>>(
+            if (int rc = launch(k_block_topk, e->H, 256, static_cast<size_t>(blocks) * (sizeof(float) + sizeof(int)), s, 
                 e->scores, total, length, blocks, e->block, position, e->log1p_table, e->slope, slots,
-                std::max(1, e->slots), kept);
+                std::max(1, e->slots), kept)) return rc;
             const int attend_threads = std::max(128, std::min(1024, (1024 / e->d) * e->d));
             const size_t attend_smem = std::max<size_t>(total, static_cast<size_t>(attend_threads)) * sizeof(float);
-            k_sparse_attend<<<e->H, attend_threads, attend_smem, s>>>(e->scores, e->v_ring[li], e->v_mean[li], e->attn,
-                                                                     e->H, e->KVH, e->d, start, length, blocks);
+            if (int rc = launch(k_sparse_attend, e->H, attend_threads, attend_smem, s, e->scores, e->v_ring[li], e->v_mean[li], e->attn,
+                                                                     e->H, e->KVH, e->d, start, length, blocks)) return rc;
             GemvSeg o = Ly.o;
             o.scale = loop_scale;
             if (int rc = launch_gemv(*e, {o})) return rc;
@@ -886,7 +968,7 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             ra.chosen = e->chosen + li * e->max_k;
             ra.weights = e->weights + li * e->max_k;
             ra.active = e->active + li;
-            k_route<<<1, 256, 0, s>>>(ra);
+            if (int rc = launch(k_route, 1, 256, 0, s, ra)) return rc;
             ExpertArgs ea{};
             ea.gate = Ly.d_gate;
             ea.up = Ly.d_up;
@@ -905,11 +987,9 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             ea.eps = e->eps;
             ea.act = e->act;
             ea.out = e->eout;
-            k_expert_gate_up<<<dim3((e->ffn + 7) / 8, slots_total), kGemvThreads,
-                               static_cast<size_t>(e->hidden) * sizeof(float) + 16, s>>>(ea);
-            k_expert_down<<<dim3((e->hidden + kGemvRows - 1) / kGemvRows, slots_total), kGemvThreads,
-                            static_cast<size_t>(e->ffn) * sizeof(float) + 16, s>>>(ea);
-            k_expert_combine<<<(e->hidden + 255) / 256, 256, 0, s>>>(ea, ra.weights, shared_scale, loop_scale, e->x);
+            if (int rc = launch(k_expert_gate_up, dim3((e->ffn + 7) / 8, slots_total), kGemvThreads, static_cast<size_t>(e->hidden) * sizeof(float) + 16, s, ea)) return rc;
+            if (int rc = launch(k_expert_down, dim3((e->hidden + kGemvRows - 1) / kGemvRows, slots_total), kGemvThreads, static_cast<size_t>(e->ffn) * sizeof(float) + 16, s, ea)) return rc;
+            if (int rc = launch(k_expert_combine, (e->hidden + 255) / 256, 256, 0, s, ea, ra.weights, shared_scale, loop_scale, e->x)) return rc;
             MR_CUDA_TRY(cudaGetLastError());
         }
     }
