@@ -156,12 +156,13 @@ def ncu_traffic(config_name):
     return None
 
 
-def launches_per_step(config):
+def launches_per_step(config, expert_parallel=False):
     """Kernels one decode step launches: the persistent decode kernel once, or
     Heavy Medium's device step (embedding row; per layer and inner loop 13
-    kernels; the head with its norm, greedy argmax)."""
+    kernels, 14 with the expert-parallel flag kernel; the head with its norm,
+    greedy argmax)."""
     if config.family == "heavy-medium-2.0":
-        return 1 + 13 * config.layers * config.inner_loop_steps + 2
+        return 1 + (14 if expert_parallel else 13) * config.layers * config.inner_loop_steps + 2
     return 1
 
 
@@ -344,7 +345,8 @@ def run_cuda(args, ranks):
                                f"{first_position}..{first_position + args.steps - 1}",
                    "context": context, "prompt": prompt_len, "weights_dtype": stored,
                    "l2": "inputs larger than L2 (weights stream from HBM every step)",
-                   "parallelism": f"tp{ranks.world}" if tp else ("replicas" if ranks.world > 1 else "single")},
+                   "parallelism": (f"ep{ranks.world}" if config.family == "heavy-medium-2.0" else f"tp{ranks.world}")
+                                  if tp else ("replicas" if ranks.world > 1 else "single")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "bytes_per_step": int(step_bytes), "per": "GPU" if tp else "step",
@@ -361,7 +363,7 @@ def run_cuda(args, ranks):
                              if config.family == "heavy-medium-2.0" else
                              "prompt runs through the decode kernel token by token")},
         "clocks": clock_summary,
-        "gpu_launches": args.steps * launches_per_step(config),
+        "gpu_launches": args.steps * launches_per_step(config, tp),
     }
     return result, config, context, prompt
 
@@ -482,7 +484,8 @@ def main(argv=None):
     parser.add_argument("--cpu-tokens", type=int, default=12, help="decode tokens of the CPU baseline sample")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--tp", action="store_true",
-                        help="with N > 1: the N GPUs decode one sequence tensor-parallel (default: N replicas)")
+                        help="with N > 1: the N GPUs decode one sequence, tensor-parallel (Heavy Medium: "
+                             "expert-parallel); default: N replicas")
     parser.add_argument("--trace", action="store_true",
                         help="print per-phase device timings of decode steps (phase tracing) and exit")
     parser.add_argument("--profile-steps", type=int, default=0,

@@ -825,6 +825,11 @@ int heavy_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
         m->failed = true;
         return cuda_error(err, "heavy-medium-2.0 token step");
     }
+    if (m->ranks > 1) {
+        const int rc = heavy_status(m->heavy);
+        if (rc) m->failed = true;
+        return rc;
+    }
     return MR_OK;
 }
 
@@ -1084,11 +1089,14 @@ int mr_model_finalize(mr_model *m) {
             return set_error(MR_ERR_ARGUMENT, "Missing tensor %s", kv.first.c_str());
     if (m->cfg.family == MR_FAMILY_HEAVY_MEDIUM_20) {
         m->finalized = true;  // the tensors are complete: heavy_create reads them by name
-        const int rc = heavy_create(m, m->cfg, m->ctx->stream, m->inv_freq.data(), &m->heavy);
+        const int rc = heavy_create(m, m->cfg, m->ctx->stream, m->inv_freq.data(), m->rank, m->ranks, &m->heavy);
         if (rc) {
             m->finalized = false;
             return rc;
         }
+        if (m->ranks > 1) heavy_arena(m->heavy, &m->arena, &m->arena_bytes);
+        m->peer[m->rank] = m->arena;
+        m->connected = m->ranks == 1;
         return mr_model_reset(m);
     }
     if (!is_engine_family(m->cfg)) {
@@ -1217,7 +1225,8 @@ int mr_model_set_tensor_parallel(mr_model *m, int rank, int ranks) {
     MR_REQUIRE(!m->finalized, "tensor parallelism is set before mr_model_finalize");
     MR_REQUIRE(ranks >= 1 && ranks <= kMaxRanks && rank >= 0 && rank < ranks, "rank %d of %d ranks (at most %d)",
                rank, ranks, kMaxRanks);
-    MR_REQUIRE(ranks == 1 || is_engine_family(m->cfg), "tensor parallelism needs a decode-engine family");
+    MR_REQUIRE(ranks == 1 || is_engine_family(m->cfg) || m->cfg.family == MR_FAMILY_HEAVY_MEDIUM_20,
+               "tensor / expert parallelism needs a decode-engine family or heavy-medium-2.0");
     m->rank = rank;
     m->ranks = ranks;
     return MR_OK;
@@ -1249,6 +1258,7 @@ int mr_model_tp_connect(mr_model *m, const void *handles, size_t bytes_each) {
         m->peer[j] = static_cast<char *>(p);
         m->peer_open[j] = true;
     }
+    if (m->heavy) heavy_connect(m->heavy, m->peer);
     m->connected = true;
     return MR_OK;
 }
@@ -1476,6 +1486,7 @@ int mr_model_bench_decode(mr_model *m, int first_token, int steps, float *device
         rc = heavy_greedy_chain(m->heavy, first_token, m->position, steps);
         if (!rc) MR_CUDA_TRY(cudaEventRecord(m->ev1, m->ctx->stream));
         const cudaError_t err = cudaStreamSynchronize(m->ctx->stream);
+        if (!rc && err == cudaSuccess && m->ranks > 1) rc = heavy_status(m->heavy);
         if (rc || err != cudaSuccess) {
             m->failed = true;
             return rc ? rc : cuda_error(err, "heavy-medium-2.0 decode");

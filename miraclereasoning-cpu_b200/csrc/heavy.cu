@@ -53,6 +53,14 @@ namespace {
 constexpr int kGemvThreads = 256;  // 8 warps
 constexpr int kGemvRows = 8;       // rows per block (one per warp)
 constexpr int kMaxSegs = 4;
+constexpr int kMaxHeavyRanks = 8;
+constexpr uint64_t kHeavyWaitNs = 2000000000ull;  // 2 s: a rank that never publishes is an error, not a hang
+
+__device__ __forceinline__ uint64_t global_time_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
 
 #define FADD __fadd_rn
 #define FMUL __fmul_rn
@@ -567,14 +575,23 @@ struct ExpertArgs {
     int norm_dtype;
     float eps;
     float *act;               // [max_k + shared][ffn] SwiGLU activations
-    float *out;               // [max_k + shared][hidden]
+    float *out;               // [max_k + shared][hidden] (expert parallel: this step's buffer in the arena)
+    // expert parallel: expert e runs on rank e % ranks, which stores its output
+    // rows into every rank's `out` (peer[j] + out_offset), then raises its flag
+    int rank, ranks;
+    char *peer[kMaxHeavyRanks];    // every rank's exchange arena (this rank's included)
+    size_t out_offset;             // byte offset of `out` inside an arena
+    unsigned long long *flags;     // this rank's arena: one word per rank
+    size_t flags_offset;
+    unsigned long long tag;        // this MoE step's flag value
+    int *err;                      // a bounded wait gave up
 };
 
 // Expert id of slot `slot` (routed slots in rank order, then the shared
-// experts), or -1 when the slot is not active this token.
+// experts), or -1 when the slot is not active this token or another rank runs it.
 __device__ __forceinline__ int slot_expert(const ExpertArgs &a, int slot) {
-    if (slot < a.max_k) return slot < *a.active ? a.chosen[slot] : -1;
-    return a.experts + (slot - a.max_k);
+    const int e = slot < a.max_k ? (slot < *a.active ? a.chosen[slot] : -1) : a.experts + (slot - a.max_k);
+    return (e >= 0 && e % a.ranks == a.rank) ? e : -1;
 }
 
 // act[slot][r] = silu(gate_r . x) * (up_r . x) (kernels.cl:46-50); grid (row blocks, slots).
@@ -615,15 +632,59 @@ __global__ void __launch_bounds__(kGemvThreads) k_expert_down(ExpertArgs a) {
     if (r >= a.hidden) return;
     float y, unused;
     warp_dot2(row, nullptr, a.dtype, a.ffn, xs, b, y, unused);
-    if (lane == 0) a.out[static_cast<size_t>(slot) * a.hidden + r] = y;
+    const size_t at = (static_cast<size_t>(slot) * a.hidden + r) * sizeof(float);
+    if (lane == 0) {
+        if (a.ranks == 1) {
+            a.out[static_cast<size_t>(slot) * a.hidden + r] = y;
+        } else {
+            for (int j = 0; j < a.ranks; ++j) *reinterpret_cast<float *>(a.peer[j] + a.out_offset + at) = y;
+        }
+    }
+    if (a.ranks > 1) __threadfence_system();  // the rows reach every rank before the flag (k_moe_publish)
 }
 
 // model.py:251-255 then 266: result = 0; result += w_k * expert_k (rank
 // order); result += (residual_scale / S) * shared_i; x += s * result, each an
 // add kernel (x + scale * y, two roundings).
+// Expert parallel: after every rank's expert rows of this step are stored,
+// raise this rank's flag in every rank's arena (release, system scope).
+__global__ void k_moe_publish(ExpertArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    __threadfence_system();
+    const int j = threadIdx.x;
+    if (j < a.ranks) {
+        unsigned long long *f = reinterpret_cast<unsigned long long *>(a.peer[j] + a.flags_offset) + a.rank;
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(a.tag) : "memory");
+    }
+}
+
 __global__ void k_expert_combine(ExpertArgs a, const float *weights, float shared_scale, float scale, float *x) {
     pdl_trigger();
     pdl_wait();
+    if (a.ranks > 1) {
+        // every rank's flag: its expert rows of this step are here (and it has finished
+        // reading the buffer of the step two back, which this step's parity reuses)
+        __shared__ int ok;
+        if (threadIdx.x == 0) {
+            const uint64_t start = global_time_ns();
+            ok = 1;
+            for (int j = 0; j < a.ranks && ok; ++j) {
+                for (;;) {
+                    unsigned long long v;
+                    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a.flags + j) : "memory");
+                    if (v >= a.tag) break;
+                    if (global_time_ns() - start > kHeavyWaitNs) {
+                        atomicExch(a.err, 1);
+                        ok = 0;
+                        break;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (!ok) return;
+    }
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= a.hidden) return;
     float res = 0.f;
@@ -666,6 +727,14 @@ struct HeavyEngine {
     float *weights = nullptr; // [layers][loops][max_k]
     int *active = nullptr;    // [layers][loops]
     int *d_token = nullptr;   // device-resident greedy decode: the next token
+    // expert parallel: the exchange arena (expert rows of two steps, one flag per
+    // rank), mapped by every rank; peers[j] = rank j's arena
+    int rank = 0, ranks = 1;
+    char *arena = nullptr;
+    size_t arena_bytes = 0, out_bytes = 0, flags_offset = 0;
+    char *peers[kMaxHeavyRanks] = {};
+    unsigned long long moe_tag = 0;
+    int *err = nullptr;
     std::vector<void *> allocations;
     bool table_set = false;
 };
@@ -736,9 +805,11 @@ int launch_gemv(HeavyEngine &e, std::initializer_list<GemvSeg> segs) {
 
 }  // namespace
 
-int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, const float *inv_freq_host,
-                 HeavyEngine **out) {
+int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, const float *inv_freq_host, int rank,
+                 int ranks, HeavyEngine **out) {
     auto *e = new HeavyEngine();
+    e->rank = rank;
+    e->ranks = ranks;
     e->m = m;
     e->stream = stream;
     e->H = c.query_heads;
@@ -800,8 +871,24 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
     const size_t per = static_cast<size_t>(e->layers) * e->loops;
     if ((rc = halloc_n(*e, per * e->H * std::max(1, e->slots), &e->kept)) ||
         (rc = halloc_n(*e, per * e->max_k, &e->chosen)) || (rc = halloc_n(*e, per * e->max_k, &e->weights)) ||
-        (rc = halloc_n(*e, per, &e->active)) || (rc = halloc_n(*e, 1, &e->d_token)))
+        (rc = halloc_n(*e, per, &e->active)) || (rc = halloc_n(*e, 1, &e->d_token)) ||
+        (rc = halloc_n(*e, 1, &e->err)))
         return fail(rc);
+    MR_CUDA_TRY(cudaMemset(e->err, 0, sizeof(int)));
+    if (ranks > 1) {
+        if (ranks > kMaxHeavyRanks) {
+            heavy_destroy(e);
+            return set_error(MR_ERR_ARGUMENT, "at most %d ranks", kMaxHeavyRanks);
+        }
+        e->out_bytes = (static_cast<size_t>(slots_total) * e->hidden * sizeof(float) + 255) & ~size_t(255);
+        e->flags_offset = 2 * e->out_bytes;
+        e->arena_bytes = e->flags_offset + 256;
+        void *arena = nullptr;
+        if ((rc = halloc(*e, e->arena_bytes, &arena))) return fail(rc);
+        e->arena = static_cast<char *>(arena);
+        MR_CUDA_TRY(cudaMemset(e->arena, 0, e->arena_bytes));
+        e->peers[rank] = e->arena;
+    }
     MR_CUDA_TRY(cudaMemcpy(e->inv_freq, inv_freq_host, sizeof(float) * (e->d / 2), cudaMemcpyHostToDevice));
     for (size_t i = 0; i < per; ++i) {
         float *kr, *vr, *km, *vm;
@@ -987,8 +1074,21 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             ea.eps = e->eps;
             ea.act = e->act;
             ea.out = e->eout;
+            ea.rank = e->rank;
+            ea.ranks = e->ranks;
+            ea.err = e->err;
+            if (e->ranks > 1) {  // this step's half of the arena (the other half: the step before)
+                ea.tag = ++e->moe_tag;
+                ea.out_offset = (ea.tag & 1) * e->out_bytes;
+                ea.out = reinterpret_cast<float *>(e->arena + ea.out_offset);
+                ea.flags = reinterpret_cast<unsigned long long *>(e->arena + e->flags_offset);
+                ea.flags_offset = e->flags_offset;
+                for (int j = 0; j < e->ranks; ++j) ea.peer[j] = e->peers[j];
+            }
             if (int rc = launch(k_expert_gate_up, dim3((e->ffn + 7) / 8, slots_total), kGemvThreads, static_cast<size_t>(e->hidden) * sizeof(float) + 16, s, ea)) return rc;
             if (int rc = launch(k_expert_down, dim3((e->hidden + kGemvRows - 1) / kGemvRows, slots_total), kGemvThreads, static_cast<size_t>(e->ffn) * sizeof(float) + 16, s, ea)) return rc;
+            if (e->ranks > 1)
+                if (int rc = launch(k_moe_publish, 1, 32, 0, s, ea)) return rc;
             if (int rc = launch(k_expert_combine, (e->hidden + 255) / 256, 256, 0, s, ea, ra.weights, shared_scale, loop_scale, e->x)) return rc;
             MR_CUDA_TRY(cudaGetLastError());
         }
@@ -1011,6 +1111,22 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
 }  // namespace
 
 const float *heavy_logits(const HeavyEngine *e) { return e->logits; }
+
+void heavy_arena(const HeavyEngine *e, char **arena, size_t *bytes) {
+    *arena = e->arena;
+    *bytes = e->arena_bytes;
+}
+
+void heavy_connect(HeavyEngine *e, char *const *peers) {
+    for (int j = 0; j < e->ranks; ++j) e->peers[j] = peers[j];
+}
+
+int heavy_status(const HeavyEngine *e) {
+    int err = 0;
+    MR_CUDA_TRY(cudaMemcpy(&err, e->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) return set_error(MR_ERR_CUDA, "expert parallel: a rank's expert rows did not arrive within 2 s");
+    return MR_OK;
+}
 
 int heavy_last_topk(const HeavyEngine *e, int layer, int loop, int *blocks, int capacity) {
     const int per = e->H * std::max(1, e->slots);

@@ -11,8 +11,15 @@ struct HeavyEngine;
 
 // Reads the model's resident tensors (the model must be finalized) and
 // allocates the work buffers and one key/value ring per (layer, inner loop).
-int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, const float *inv_freq_host,
-                 HeavyEngine **out);
+// With ranks > 1 (expert parallel) every rank runs the attention, router and
+// head itself and the experts e with e % ranks == rank, exchanging expert rows
+// through an arena that every rank maps (heavy_arena / heavy_connect).
+int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, const float *inv_freq_host, int rank,
+                 int ranks, HeavyEngine **out);
+void heavy_arena(const HeavyEngine *e, char **arena, size_t *bytes);
+void heavy_connect(HeavyEngine *e, char *const *peers);
+// Reads the wait status of the expert-parallel exchange (synchronous).
+int heavy_status(const HeavyEngine *e);
 void heavy_destroy(HeavyEngine *e);
 
 // float32 log1p(d) for distances d = 0 .. context-1, as the host computes them

@@ -1,6 +1,8 @@
 """Tensor-parallel decode (every projection and the lm_head split by output row
 over the GPUs, attention by KV head, exchange words stored into every rank's
-arena over NVLink) against the single-GPU engine on the same model and prompt.
+arena over NVLink) and Heavy Medium expert-parallel decode (experts by id
+modulo ranks, expert rows stored into every rank's arena) against the
+single-GPU engine on the same model and prompt.
 
 Runs tests/tp_worker.py as one process per GPU under torch.distributed.run
 (127.0.0.1 rendezvous); a case is skipped when the box has fewer GPUs than it
@@ -32,8 +34,10 @@ def _gpus():
 GPUS = _gpus()
 
 
-# 8 ranks over nano-1.7's 4 local KV heads: half the ranks hold no head of those layers
-@pytest.mark.parametrize("config,ranks", [("nano17", 2), ("lite", 2), ("nano17", 4), ("nano17", 8)])
+# 8 ranks over nano-1.7's 4 local KV heads: half the ranks hold no head of those layers;
+# heavy_small: Heavy Medium expert parallel (experts by id modulo ranks)
+@pytest.mark.parametrize("config,ranks", [("nano17", 2), ("lite", 2), ("heavy_small", 2), ("nano17", 4),
+                                          ("heavy_small", 4), ("nano17", 8)])
 def test_tensor_parallel_decode_matches_single_gpu(tmp_path, config, ranks):
     if GPUS < ranks:
         pytest.skip(f"tensor-parallel decode over {ranks} GPUs needs {ranks} GPUs")
@@ -48,3 +52,5 @@ def test_tensor_parallel_decode_matches_single_gpu(tmp_path, config, ranks):
     assert result["tokens"] == result["ref_tokens"]
     # both sum every dot product in the same order per row: the split only moves rows between GPUs
     assert result["max_abs_diff"] <= 2e-5 * max(1.0, result["scale"])
+    if config == "heavy_small":  # the same kernels compute each expert, wherever it runs
+        assert result["max_abs_diff"] == 0.0

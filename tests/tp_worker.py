@@ -1,5 +1,5 @@
-"""One rank of the tensor-parallel decode check (launched by tests/test_gpu_tp.py
-under torch.distributed.run, one process per GPU).
+"""One rank of the tensor- / expert-parallel decode check (launched by
+tests/test_gpu_tp.py under torch.distributed.run, one process per GPU).
 
 Rank 0 first runs the prompt and greedy decode steps on a single-GPU model;
 then every rank builds the same model split over the ranks and repeats them.
@@ -24,6 +24,17 @@ MiracleModel = importlib.import_module(PKG + ".model").MiracleModel
 CUDABackend = importlib.import_module(PKG + ".backend").CUDABackend
 
 
+def small_heavy():
+    """Heavy Medium at test size: 16 routed experts (8 per rank at 2 ranks), 2 shared."""
+    return importlib.import_module(PKG + ".config").ModelConfig(
+        family="heavy-medium-2.0", vocab_size=512, hidden_size=256, layers=2, query_heads=4, kv_heads=2,
+        head_dim=64, ffn_dim=128, max_positions=2048, window=32, latent_dim=64, inner_loop_steps=2,
+        source={"routed_experts": 16, "router_groups": 4, "router_top_k_max": 4, "router_top_k_min": 2,
+                "shared_experts": 2,
+                "long_context": {"local_window": 32, "global_block_size": 8, "global_slots": 3,
+                                 "target_context": 2048}})
+
+
 def run(model, prompt, steps):
     logits = [model.prefill(prompt)]
     tokens = []
@@ -38,7 +49,7 @@ def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     backend = CUDABackend(device_index=int(os.environ.get("LOCAL_RANK", "0")))
-    config = syn.config_for(config_name)
+    config = small_heavy() if config_name == "heavy_small" else syn.config_for(config_name)
     prompt = syn.prompt_ids(config.vocab_size, 40, seed=3).tolist()
     context = 1024
     if rank == 0:
