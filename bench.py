@@ -329,8 +329,13 @@ def run_cuda(args, ranks):
     step_bytes = weight_bytes(config, stored, active) + sum(kv_bytes(config, context, p) for p in positions) / args.steps
     step_s = device_ms / 1e3 / args.steps
     peak, peak_kind = measured_hbm()
-    if tp:  # each GPU streams its slice of the weights and KV rows
+    per = "step"
+    if tp and config.family == "heavy-medium-2.0":  # attention replicated, experts split: the whole job's bytes
+        peak *= ranks.world
+        per = f"job ({ranks.world} GPUs, peak x {ranks.world})"
+    elif tp:  # each GPU streams its slice of the weights and KV rows
         step_bytes /= ranks.world
+        per = "GPU"
     achieved = step_bytes / step_s / 1e9
     value = sequences * args.steps / (device_ms / 1e3)
     result = {
@@ -349,7 +354,7 @@ def run_cuda(args, ranks):
                                   if tp else ("replicas" if ranks.world > 1 else "single")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "bytes_per_step": int(step_bytes), "per": "GPU" if tp else "step",
+                     "bytes_per_step": int(step_bytes), "per": per,
                      "traffic": None if tp else ncu_traffic(args.config)},
         "e2e": {"value": round(sequences * e2e_steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * config.vocab_size, "steps": e2e_steps,

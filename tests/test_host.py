@@ -5,6 +5,7 @@ tests/test_inference.py:102-106) to this package and pins the config tables
 against fixtures the reference produced (tests/golden/configs.npz).
 """
 import ctypes
+import importlib
 import json
 import re
 import struct
@@ -165,3 +166,44 @@ def test_engine_config_flattening():
     assert (cfg.family, cfg.routed_experts, cfg.block_size, cfg.global_slots) == (5, 16, 4, 3)
     assert cfg.alibi_slope == pytest.approx(0.015 / 4)
     assert ctypes.sizeof(cfg) == 30 * 4  # 30 four-byte fields of mr_model_config, no padding
+
+
+# ---- which device path runs a family, and the decisions it reports ------------------
+def test_engine_plans_routes_families():
+    model = importlib.import_module("miraclereasoning-cpu_b200.model")
+    for name in ("nano15", "nano17", "lite", "lighting", "heavy"):
+        assert model.engine_plans(cases.synthetic.config_for(name)), name
+    assert not model.engine_plans(cases.micro_config("nano16"))           # chunk relays: host-stepped
+    assert not model.engine_plans(cases.micro_config("lighting"))         # memory slots: weighted merge
+    assert model.engine_plans(cases.micro_config("lighting_drop"))
+
+
+def test_ring_decisions_follow_the_drop_path():
+    """FlashLighting without memory slots keeps positions max(0, p + 1 - window) .. p."""
+    model = importlib.import_module("miraclereasoning-cpu_b200.model")
+    config = cases.micro_config("lighting_drop")
+
+    class Stub:
+        pass
+
+    stub = Stub()
+    stub.config, stub.position = config, 7
+    decisions = model.RingDecisions(stub)
+    assert len(decisions) == 7
+    assert decisions[0] == [{"latent_positions": [[0]], "memory_size": [0]}] * config.layers
+    w = config.window
+    assert decisions[6][0]["latent_positions"] == [list(range(7 - w, 7))]
+    with pytest.raises(IndexError):
+        decisions[7]
+
+
+def test_bench_heavy_byte_accounting():
+    """Heavy Medium reads its layer weights once per inner loop and only the chosen experts."""
+    bench = importlib.import_module("bench")
+    config = cases.micro_config("heavy_mid")
+    shapes = cases.expected_shapes(config)
+    expert = sum(int(np.prod(shapes[f"layers.0.experts.0.{k}"])) * 4 for k in ("gate", "up", "down"))
+    base = bench.weight_bytes(config, "F32", 0)
+    assert bench.weight_bytes(config, "F32", 2) - base == 2 * expert * config.layers * config.inner_loop_steps
+    assert bench.launches_per_step(config) == 1 + 13 * config.layers * config.inner_loop_steps + 2
+    assert bench.launches_per_step(cases.micro_config("nano15")) == 1
