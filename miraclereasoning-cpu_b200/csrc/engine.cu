@@ -844,9 +844,11 @@ void setup_prefill(mr_model *m) {
     const mr_model_config &c = m->cfg;
     const int d = c.head_dim, q = c.query_heads * d;
     m->prefill_ok = false;
-    if (!is_gqa_family(c.family)) return;
+    const bool lighting = is_lighting_ring(c);
+    if (!is_gqa_family(c.family) && !lighting) return;
     const int gq_max = c.query_heads / *std::min_element(m->layer_kvh.begin(), m->layer_kvh.end());
     if (c.hidden_size % 8 || q % 8 || c.ffn_dim % 8 || d % 4 || gq_max > 32) return;
+    if (lighting && c.latent_dim % 8) return;
     auto bf16 = [&](const std::string &name) {
         const TensorSlot *t = tensor(m, name);
         return t && t->dtype == MR_DTYPE_BF16 ? t->ptr : nullptr;
@@ -861,8 +863,10 @@ void setup_prefill(mr_model *m) {
     pm.kv_max = *std::max_element(m->layer_kvh.begin(), m->layer_kvh.end());
     pm.eps = c.norm_eps;
     pm.residual_scale = c.residual_scale;
-    pm.qk_norm = c.qk_norm;
+    pm.qk_norm = lighting ? 1 : c.qk_norm;
     pm.split_half = c.split_half_rope;
+    pm.lighting = lighting;
+    pm.latent_dim = c.latent_dim;
     const TensorSlot *embed = tensor(m, "embed"), *norm = tensor(m, "norm");
     pm.embed = embed->ptr;
     pm.embed_dt = embed->dtype;
@@ -875,12 +879,24 @@ void setup_prefill(mr_model *m) {
     for (int l = 0; l < c.layers; ++l) {
         const std::string p = "layers." + std::to_string(l) + ".";
         PrefillLayer L{};
-        const TensorSlot *an = tensor(m, p + "a_norm"), *fn = tensor(m, p + "f_norm");
+        const TensorSlot *an = tensor(m, p + "a_norm");
         L.a_norm = an->ptr;
         L.a_norm_dt = an->dtype;
-        L.f_norm = fn->ptr;
-        L.f_norm_dt = fn->dtype;
-        if (c.qk_norm) {
+        if (!lighting) {
+            const TensorSlot *fn = tensor(m, p + "f_norm");
+            L.f_norm = fn->ptr;
+            L.f_norm_dt = fn->dtype;
+        } else {
+            const TensorSlot *ln = tensor(m, p + "latent_norm");
+            L.latent_norm = ln->ptr;
+            L.latent_norm_dt = ln->dtype;
+            L.latent = bf16(p + "latent");
+            float ag = 0.f, fg = 0.f;
+            if (read_scalar(m, p + "attention_gate", ag) || read_scalar(m, p + "ffn_gate", fg) || !L.latent) return;
+            L.o_scale = c.residual_scale * ag;
+            L.down_scale = c.residual_scale * fg;
+        }
+        if (c.qk_norm || lighting) {
             const TensorSlot *qn = tensor(m, p + "q_norm"), *kn = tensor(m, p + "k_norm");
             L.q_norm = qn->ptr;
             L.k_norm = kn->ptr;

@@ -70,11 +70,11 @@ __global__ void k_embed_rows(const int *ids, int T, const void *embed, int dt, i
 }
 
 // planes[row r - r0] = split((x[r] * scale) * gain) (kernels.cl:19-28), for rows r0 .. r0 + n - 1.
-__global__ void k_rms_planes(const float *x, int r0, int h, const void *gain, int gain_dt, float eps, uint16_t *planes,
-                             size_t plane_stride, int ld) {
+__global__ void k_rms_planes(const float *x, int r0, int h, int ldx, const void *gain, int gain_dt, float eps,
+                             uint16_t *planes, size_t plane_stride, int ld) {
     __shared__ float red[32];
     const int r = r0 + blockIdx.x;
-    const float *xr = x + static_cast<size_t>(r) * h;
+    const float *xr = x + static_cast<size_t>(r) * ldx;
     float ss = 0.f;
     for (int j = threadIdx.x; j < h; j += blockDim.x) ss = fmaf(xr[j], xr[j], ss);
     ss = block_reduce_sum(ss, red);
@@ -787,6 +787,12 @@ int gemm(const PrefillWork &w, cudaStream_t stream, const uint16_t *planes, size
     return MR_OK;
 }
 
+// Row width of the q | k | v buffer: FlashLighting's q | latent fits too.
+int qkv_width(const PrefillModel &pm) {
+    const int q = pm.heads * pm.head_dim, kv = pm.kv_max * pm.head_dim;
+    return q + std::max(2 * kv, pm.lighting ? pm.latent_dim : 0);
+}
+
 size_t attn_smem(int d) {
     return sizeof(float) * (static_cast<size_t>(kAttnRows) * (d + 4) + 2 * kKT * (d + 4) +
                             2 * static_cast<size_t>(kKT) * d + kAttnRows * (kKT + 1) + 3 * kAttnRows);
@@ -811,14 +817,14 @@ int prefill_reserve(const PrefillModel &pm, PrefillWork &w, int tokens, bool all
     const bool all = all_logits || w.all_logits;
     prefill_release(w);
     const int q = pm.heads * pm.head_dim, kv = pm.kv_max * pm.head_dim;
-    w.kmax = std::max({pm.hidden, q, pm.ffn});
+    w.kmax = std::max({pm.hidden, q, pm.ffn, pm.lighting ? pm.latent_dim : 0});
     auto alloc = [&](void **p, size_t bytes) -> int {
         MR_CUDA_TRY(cudaMalloc(p, bytes ? bytes : 16));
         return MR_OK;
     };
     int rc = alloc(reinterpret_cast<void **>(&w.x), sizeof(float) * T * pm.hidden);
     if (!rc) rc = alloc(reinterpret_cast<void **>(&w.planes), sizeof(uint16_t) * 3 * static_cast<size_t>(T) * w.kmax);
-    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.qkv), sizeof(float) * T * static_cast<size_t>(q + 2 * kv));
+    if (!rc) rc = alloc(reinterpret_cast<void **>(&w.qkv), sizeof(float) * T * static_cast<size_t>(qkv_width(pm)));
     if (!rc) rc = alloc(reinterpret_cast<void **>(&w.qh), sizeof(float) * T * static_cast<size_t>(q));
     if (!rc) rc = alloc(reinterpret_cast<void **>(&w.kc), sizeof(float) * T * static_cast<size_t>(kv));
     if (!rc) rc = alloc(reinterpret_cast<void **>(&w.vc), sizeof(float) * T * static_cast<size_t>(kv));
@@ -856,9 +862,54 @@ int prefill_chunk(const PrefillModel &pm, PrefillWork &w, const int *d_ids, int 
     k_embed_rows<<<T, 256, 0, st>>>(d_ids, T, pm.embed, pm.embed_dt, h, w.x);
     MR_CUDA_TRY(cudaGetLastError());
     for (const PrefillLayer &L : pm.layers) {
-        const int KV = L.kv_heads, kv = KV * d, ldqkv = q + 2 * kv;
+        const int KV = L.kv_heads, kv = KV * d, ldqkv = pm.lighting ? qkv_width(pm) : q + 2 * kv;
+        if (pm.lighting) {
+            // FlashLighting (model.py:146-190, 272-278): both branches read a_norm(x)
+            const int lat = pm.latent_dim;
+            k_rms_planes<<<T, 256, 0, st>>>(w.x, 0, h, h, L.a_norm, L.a_norm_dt, pm.eps, w.planes, ps, w.kmax);
+            int rc = gemm(w, st, w.planes, ps, w.kmax, T, h,
+                          {GemmSeg{static_cast<const uint16_t *>(L.q), q, 0, 0},
+                           GemmSeg{static_cast<const uint16_t *>(L.latent), lat, q, 0}},
+                          w.qkv, ldqkv, false, 0.f);
+            if (!rc)
+                rc = gemm(w, st, w.planes, ps, w.kmax, T, h,
+                          {GemmSeg{static_cast<const uint16_t *>(L.gate), f, 0, 0},
+                           GemmSeg{static_cast<const uint16_t *>(L.up), f, f, 0}},
+                          w.gu, 2 * f, false, 0.f);
+            if (rc) return rc;
+            // k | v from latent_norm(latent), written over the latent columns
+            k_rms_planes<<<T, 256, 0, st>>>(w.qkv + q, 0, lat, ldqkv, L.latent_norm, L.latent_norm_dt, pm.eps, w.planes,
+                                            ps, w.kmax);
+            rc = gemm(w, st, w.planes, ps, w.kmax, T, lat,
+                      {GemmSeg{static_cast<const uint16_t *>(L.k), kv, q, 0},
+                       GemmSeg{static_cast<const uint16_t *>(L.v), kv, q + kv, 0}},
+                      w.qkv, ldqkv, false, 0.f);
+            if (rc) return rc;
+            const int warps = T * (H + 2 * KV);
+            k_qk_rope<<<(warps * 32 + 255) / 256, 256, 0, st>>>(w.qkv, T, p0, H, KV, d, ldqkv, 1, L.q_norm, L.k_norm,
+                                                                L.qk_norm_dt, pm.eps, pm.inv_freq, pm.split_half, w.qh,
+                                                                w.kc, w.vc);
+            MR_CUDA_TRY(cudaGetLastError());
+            const int gq = H / KV, QT = std::max(1, kAttnRows / gq);
+            const dim3 grid(static_cast<unsigned>((T + QT - 1) / QT), static_cast<unsigned>(KV));
+            k_attention<<<grid, kAttnThreads, attn_smem(d), st>>>(w.qh, w.kc, w.vc, L.k_cache, L.v_cache, T, p0, H, KV,
+                                                                  d, L.capacity, QT, w.planes, ps, w.kmax);
+            MR_CUDA_TRY(cudaGetLastError());
+            k_ring_append<<<256, 256, 0, st>>>(w.kc, w.vc, T, p0, KV, d, L.capacity, L.k_cache, L.v_cache);
+            MR_CUDA_TRY(cudaGetLastError());
+            // x += (s * attention_gate) * o, then x += (s * ffn_gate) * down (the two branches in turn)
+            rc = gemm(w, st, w.planes, ps, w.kmax, T, q, {GemmSeg{static_cast<const uint16_t *>(L.o), h, 0, 0}}, w.x, h,
+                      true, L.o_scale);
+            if (rc) return rc;
+            k_swiglu_planes<<<592, 256, 0, st>>>(w.gu, T, f, w.planes, ps, w.kmax);
+            MR_CUDA_TRY(cudaGetLastError());
+            rc = gemm(w, st, w.planes, ps, w.kmax, T, f, {GemmSeg{static_cast<const uint16_t *>(L.down), h, 0, 0}}, w.x,
+                      h, true, L.down_scale);
+            if (rc) return rc;
+            continue;
+        }
         // 1. RMSNorm -> q | k | v
-        k_rms_planes<<<T, 256, 0, st>>>(w.x, 0, h, L.a_norm, L.a_norm_dt, pm.eps, w.planes, ps, w.kmax);
+        k_rms_planes<<<T, 256, 0, st>>>(w.x, 0, h, h, L.a_norm, L.a_norm_dt, pm.eps, w.planes, ps, w.kmax);
         int rc = gemm(w, st, w.planes, ps, w.kmax, T, h,
                       {GemmSeg{static_cast<const uint16_t *>(L.q), q, 0, 0},
                        GemmSeg{static_cast<const uint16_t *>(L.k), kv, q, 0},
@@ -888,7 +939,7 @@ int prefill_chunk(const PrefillModel &pm, PrefillWork &w, const int *d_ids, int 
                   pm.residual_scale);
         if (rc) return rc;
         // 5. RMSNorm -> gate | up -> SwiGLU -> down, x += s * down (model.py:87-89, 283)
-        k_rms_planes<<<T, 256, 0, st>>>(w.x, 0, h, L.f_norm, L.f_norm_dt, pm.eps, w.planes, ps, w.kmax);
+        k_rms_planes<<<T, 256, 0, st>>>(w.x, 0, h, h, L.f_norm, L.f_norm_dt, pm.eps, w.planes, ps, w.kmax);
         rc = gemm(w, st, w.planes, ps, w.kmax, T, h,
                   {GemmSeg{static_cast<const uint16_t *>(L.gate), f, 0, 0},
                    GemmSeg{static_cast<const uint16_t *>(L.up), f, f, 0}},
@@ -902,7 +953,7 @@ int prefill_chunk(const PrefillModel &pm, PrefillWork &w, const int *d_ids, int 
     }
     // final RMSNorm + lm_head for the rows whose logits are wanted (model.py:285, 307)
     const int r0 = all_logits ? 0 : T - 1, rows = all_logits ? T : 1;
-    k_rms_planes<<<rows, 256, 0, st>>>(w.x, r0, h, pm.final_norm, pm.final_norm_dt, pm.eps, w.planes, ps, w.kmax);
+    k_rms_planes<<<rows, 256, 0, st>>>(w.x, r0, h, h, pm.final_norm, pm.final_norm_dt, pm.eps, w.planes, ps, w.kmax);
     return gemm(w, st, w.planes, ps, w.kmax, rows, h, {GemmSeg{static_cast<const uint16_t *>(pm.head), pm.vocab, 0, 0}},
                 w.logits, pm.vocab, false, 0.f);
 }

@@ -20,6 +20,12 @@ struct PrefillLayer {
     const void *q, *k, *v, *o, *gate, *up, *down;    // BF16 matrices [out, in]
     float *k_cache, *v_cache;                        // [kv_heads][capacity][head_dim]
     int capacity, kv_heads;
+    // FlashLighting (no memory slots): q | latent and gate | up from a_norm(x),
+    // k | v (BF16 [kv, latent]) from latent_norm(latent), residual scales
+    // residual_scale * attention_gate and residual_scale * ffn_gate
+    const void *latent, *latent_norm;
+    int latent_norm_dt;
+    float o_scale, down_scale;
 };
 
 struct PrefillModel {
@@ -27,6 +33,7 @@ struct PrefillModel {
     int hidden, heads, head_dim, ffn, vocab, kv_max;
     float eps, residual_scale;
     int qk_norm, split_half;
+    int lighting, latent_dim;  // FlashLighting layers (PrefillLayer's latent path)
     const void *embed;  // [vocab, hidden] stored dtype
     int embed_dt;
     const void *final_norm;

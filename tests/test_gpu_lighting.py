@@ -52,3 +52,35 @@ def test_lighting_ring_engine_matches_oracle(backend):
     # greedy continuation, device loop vs the oracle's
     ids = model.generate(prompt[:20], max_new_tokens=8)
     assert ids == oracle.generate(prompt[:20], max_new_tokens=8)
+
+
+def test_lighting_batched_prefill_matches_token_by_token(backend):
+    """The tensor-core prompt path (q | latent and gate | up GEMMs, latent_norm ->
+    k | v GEMM, causal attention over ring + chunk) against the decode kernel
+    run token by token, on a prompt longer than the window."""
+    import ctypes as C
+    config, weights, prompt = _case()
+    native = submodule("_native")
+    model = submodule("model").MiracleModel(config, weights, backend=backend, context_length=200)
+    available = C.c_int(0)
+    native.call("mr_model_set_batched_prefill", model._handle, 1, C.byref(available))
+    assert available.value == 1
+    batched = model.prefill(prompt, return_all=True)
+    model.reset()
+    native.call("mr_model_set_batched_prefill", model._handle, 0, C.byref(available))
+    serial = model.prefill(prompt, return_all=True)
+    np.testing.assert_allclose(batched, serial, atol=ATOL, rtol=RTOL)
+    # decoding on from the batched prompt's ring gives the serial path's next logits
+    model.reset()
+    native.call("mr_model_set_batched_prefill", model._handle, 1, C.byref(available))
+    model.prefill(prompt)
+    np.testing.assert_allclose(model.decode(7), _serial_next(config, weights, prompt, backend), atol=ATOL, rtol=RTOL)
+
+
+def _serial_next(config, weights, prompt, backend):
+    import ctypes as C
+    model = submodule("model").MiracleModel(config, weights, backend=backend, context_length=200)
+    available = C.c_int(0)
+    submodule("_native").call("mr_model_set_batched_prefill", model._handle, 0, C.byref(available))
+    model.prefill(prompt)
+    return model.decode(7)
