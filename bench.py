@@ -158,11 +158,11 @@ def ncu_traffic(config_name):
 
 def launches_per_step(config, expert_parallel=False):
     """Kernels one decode step launches: the persistent decode kernel once, or
-    Heavy Medium's device step (embedding row; per layer and inner loop 13
-    kernels, 14 with the expert-parallel flag kernel; the head with its norm,
+    Heavy Medium's device step (embedding row; per layer and inner loop 11
+    kernels, 12 with the expert-parallel flag kernel; the head with its norm,
     greedy argmax)."""
     if config.family == "heavy-medium-2.0":
-        return 1 + (14 if expert_parallel else 13) * config.layers * config.inner_loop_steps + 2
+        return 1 + (12 if expert_parallel else 11) * config.layers * config.inner_loop_steps + 2
     return 1
 
 

@@ -9,13 +9,12 @@
 //      q = W_q h, latent = W_latent h                            k_gemv (two segments)
 //   3. kv = W_kv_up latent                                       k_gemv
 //   4. q = RoPE(RMSNorm_noaffine(q)); k = RoPE(RMSNorm_noaffine(kv[:w]));
-//      append k, v = kv[w:] to the loop's ring                   k_heads_norm_rope
-//   5. mean key / value of the newest block (older blocks' means
-//      never change once full)                                   k_block_mean_last
+//      append k, v = kv[w:] to the loop's ring; mean key / value
+//      of the newest block (older blocks' means never change)    k_heads_norm_rope
 //   6. scores over the local window and every block mean        k_sparse_scores
-//   7. block columns minus the distance penalty, stable top
-//      `global_slots` per head, the rest masked (model.py:219-225) k_block_topk
-//   8. softmax + value mix over window rows and kept blocks     k_sparse_attend
+//   7-8. block columns minus the distance penalty, stable top
+//      `global_slots` per head, the rest masked (model.py:219-225);
+//      softmax + value mix over window rows and kept blocks     k_sparse_attend
 //   9. x += s * W_o attended                                     k_gemv (residual)
 //  10. f = RMSNorm(x, f_norm) (while staging); router logits    k_gemv
 //  11. routing (model.py:235-250): biases, temperature, softmax,
@@ -120,14 +119,30 @@ __device__ __forceinline__ bool whole_chunks(int dtype, int cols) {
 // Stages x (n floats) in shared memory, or RMSNorm(x) with `gain`
 // (kernels.cl:19-28: (x * (1 / sqrt(mean(x^2) + eps))) * gain) when `norm`:
 // every block computes the same factor from the same sums.
+// The loads are 16-byte vectors issued several at a time: a loop of
+// dependent scalar loads here costs more than the block's whole weight stream.
 __device__ void stage_input(const float *x, int n, bool norm, const void *gain, int gain_dtype, float eps,
                             float *xs) {
     __shared__ float red[32];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = x[i];
-        xs[i] = v;
-        ss = fmaf(v, v, ss);
+    const bool vec = (n & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    if (vec) {
+#pragma unroll 4
+        for (int i = 4 * threadIdx.x; i < n; i += 4 * blockDim.x) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(x + i));
+            *reinterpret_cast<float4 *>(xs + i) = v;
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+        }
+    } else {
+#pragma unroll 4
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const float v = x[i];
+            xs[i] = v;
+            ss = fmaf(v, v, ss);
+        }
     }
     if (!norm) {
         __syncthreads();
@@ -139,9 +154,24 @@ __device__ void stage_input(const float *x, int n, bool norm, const void *gain, 
     float total = 0.f;
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) total += red[w];
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(FADD(__fdiv_rn(total, static_cast<float>(n)), eps)));
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float g = gain ? load_weight(gain, gain_dtype, i) : 1.0f;
-        xs[i] = FMUL(FMUL(xs[i], scale), g);
+    if (vec && gain && gain_dtype != MR_DTYPE_F32 && (reinterpret_cast<uintptr_t>(gain) & 7) == 0) {
+#pragma unroll 4
+        for (int i = 4 * threadIdx.x; i < n; i += 4 * blockDim.x) {  // four 16-bit gains per 8-byte load
+            const uint2 g = __ldg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(gain) + i));
+            const uint16_t h[4] = {static_cast<uint16_t>(g.x & 0xffffu), static_cast<uint16_t>(g.x >> 16),
+                                   static_cast<uint16_t>(g.y & 0xffffu), static_cast<uint16_t>(g.y >> 16)};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float gv = gain_dtype == MR_DTYPE_BF16 ? widen_bf16(h[k]) : widen_f16(h[k]);
+                xs[i + k] = FMUL(FMUL(xs[i + k], scale), gv);
+            }
+        }
+    } else {
+#pragma unroll 4
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const float g = gain ? load_weight(gain, gain_dtype, i) : 1.0f;
+            xs[i] = FMUL(FMUL(xs[i], scale), g);
+        }
     }
     __syncthreads();
 }
@@ -319,7 +349,8 @@ __global__ void k_argmax(const float *v, int n, int *token) {
 // non-affine RMSNorm (eps 1e-6, model.py:194, 201) then RoPE at `position`
 // (kernels.cl:30-44); keys and values go to ring row `row`.
 __global__ void k_heads_norm_rope(float *q, const float *kv, float *k_ring, float *v_ring, const float *inv_freq,
-                                  int heads, int kv_heads, int dim, int split_half, int position, int row) {
+                                  int heads, int kv_heads, int dim, int split_half, int position, int row,
+                                  float *k_mean, float *v_mean, int block) {
     pdl_trigger();
     pdl_wait();
     const int h = blockIdx.x, lane = threadIdx.x;
@@ -333,10 +364,12 @@ __global__ void k_heads_norm_rope(float *q, const float *kv, float *k_ring, floa
         const int kh = h - heads;
         src = kv + static_cast<size_t>(kh) * dim;
         dst = k_ring + static_cast<size_t>(row) * width + static_cast<size_t>(kh) * dim;
+#pragma unroll 4
         for (int j = lane; j < dim; j += 32)
             v_ring[static_cast<size_t>(row) * width + static_cast<size_t>(kh) * dim + j] = kv[width + kh * dim + j];
     }
     float ss = 0.f;
+#pragma unroll 4
     for (int j = lane; j < dim; j += 32) ss = fmaf(src[j], src[j], ss);
     ss = warp_sum(ss);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(FADD(__fdiv_rn(ss, static_cast<float>(dim)), 1e-6f)));
@@ -357,23 +390,24 @@ __global__ void k_heads_norm_rope(float *q, const float *kv, float *k_ring, floa
         dst[j] = __fsub_rn(FMUL(u[n], c), FMUL(v[n], s));
         dst[k] = FADD(FMUL(u[n], s), FMUL(v[n], c));
     }
-}
-
-// Mean of the newest block's rows (kernels.cl:139-148: running sum in row
-// order, then one division) for keys and values; full blocks never change.
-__global__ void k_block_mean_last(const float *k_ring, const float *v_ring, float *k_mean, float *v_mean, int count,
-                                  int width, int block) {
-    pdl_trigger();
-    pdl_wait();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= 2 * width) return;
-    const int j = i % width;
-    const float *src = i < width ? k_ring : v_ring;
-    float *dst = i < width ? k_mean : v_mean;
-    const int b = (count - 1) / block, start = b * block, stop = min(start + block, count);
-    float v = 0.f;
-    for (int t = start; t < stop; ++t) v = FADD(v, src[static_cast<size_t>(t) * width + j]);
-    dst[static_cast<size_t>(b) * width + j] = __fdiv_rn(v, static_cast<float>(stop - start));
+    if (h < heads) return;
+    // key heads: the mean of the newest block's rows of this head (kernels.cl:139-148:
+    // a running sum in row order, then one division) for keys and values; full
+    // blocks' means never change once written
+    __syncwarp();  // this warp's key / value row is in
+    const int kh = h - heads, count = row + 1, b = (count - 1) / block, start = b * block;
+    const float rows = static_cast<float>(count - start);
+    for (int j = lane; j < dim; j += 32) {
+        const size_t col = static_cast<size_t>(kh) * dim + j;
+        float sk = 0.f, sv = 0.f;
+#pragma unroll 8
+        for (int t = start; t < count; ++t) {
+            sk = FADD(sk, k_ring[static_cast<size_t>(t) * width + col]);
+            sv = FADD(sv, v_ring[static_cast<size_t>(t) * width + col]);
+        }
+        k_mean[static_cast<size_t>(b) * width + col] = __fdiv_rn(sk, rows);
+        v_mean[static_cast<size_t>(b) * width + col] = __fdiv_rn(sv, rows);
+    }
 }
 
 // scores[h][t], t < length: local ring rows start .. start+length-1; t >= length:
@@ -391,60 +425,60 @@ __global__ void k_sparse_scores(const float *q, const float *k_ring, const float
                                  : k_mean + static_cast<size_t>(t - length) * width + static_cast<size_t>(kh) * dim;
     const float *qh = q + static_cast<size_t>(h) * dim;
     float v = 0.f;
+#pragma unroll 4
     for (int j = lane; j < dim; j += 32) v = fmaf(qh[j], kr[j], v);
     v = warp_sum(v);
     if (lane == 0) scores[static_cast<size_t>(h) * total + t] = __fdiv_rn(v, __fsqrt_rn(static_cast<float>(dim)));
 }
 
-// model.py:219-225 per head (one block): block column b loses
-// slope * log1p(position - end_b) (end_b = min((b + 1) * block - 1, position),
-// the log1p value from the host's table), the `slots` best columns (stable
-// descending order: ties go to the lower index) stay, the rest become -inf.
-// The kept block ids go to `kept` in ascending order, -1 padded to `slots_max`.
-__global__ void k_block_topk(float *scores, int total, int length, int blocks, int block, int position,
-                             const float *log1p_table, float slope, int slots, int slots_max, int *kept) {
+// One block per head: the global-block selection of model.py:219-225, then
+// the softmax over the head's scores and the value mix over window rows and
+// kept block means (kernels.cl:76-107).
+// Selection: block column b loses slope * log1p(position - end_b)
+// (end_b = min((b + 1) * block - 1, position), the log1p value from the host's
+// table); the `slots` best columns (stable descending order: ties go to the
+// lower index) stay, the rest become -inf.  The kept block ids go to `kept` in
+// ascending order, -1 padded to `slots_max`.
+__global__ void k_sparse_attend(const float *scores, const float *v_ring, const float *v_mean, float *out, int heads,
+                                int kv_heads, int dim, int start, int length, int blocks, int block, int position,
+                                const float *log1p_table, float slope, int slots, int slots_max, int *kept) {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ float sb[];
-    int *keep = reinterpret_cast<int *>(sb + blocks);
-    const int h = blockIdx.x;
-    float *row = scores + static_cast<size_t>(h) * total + length;
-    for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
-        const int end = min((b + 1) * block - 1, position);
-        sb[b] = __fsub_rn(row[b], FMUL(slope, log1p_table[position - end]));
+    extern __shared__ float p[];  // [max(total, blockDim)] scores, then weights, then partial sums
+    __shared__ float red[32];
+    const int h = blockIdx.x, total = length + blocks;
+    const int kh = h / (heads / kv_heads), width = kv_heads * dim;
+    int *keep = reinterpret_cast<int *>(p + max(total, static_cast<int>(blockDim.x)));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    for (int t = threadIdx.x; t < total; t += blockDim.x) {
+        float v = scores[static_cast<size_t>(h) * total + t];
+        if (t >= length) {
+            const int b = t - length, end = min((b + 1) * block - 1, position);
+            v = __fsub_rn(v, FMUL(slope, log1p_table[position - end]));
+        }
+        p[t] = v;
     }
     __syncthreads();
     for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
-        const float v = sb[b];
+        const float v = p[length + b];
         int rank = 0;
         for (int j = 0; j < blocks; ++j) {
-            const float u = sb[j];
+            const float u = p[length + j];
             rank += (u > v) || (u == v && j < b);
         }
-        keep[b] = rank < slots && v != -INFINITY;
-        row[b] = rank < slots ? v : -INFINITY;
+        keep[b] = rank < slots;
     }
     __syncthreads();
+    for (int b = threadIdx.x; b < blocks; b += blockDim.x)
+        if (!keep[b]) p[length + b] = -INFINITY;
     if (threadIdx.x == 0) {  // ascending ids of the kept columns (np.flatnonzero order)
         int n = 0;
         for (int b = 0; b < blocks && n < slots_max; ++b)
             if (keep[b]) kept[h * slots_max + n++] = b;
         for (; n < slots_max; ++n) kept[h * slots_max + n] = -1;
     }
-}
-
-// Softmax over one head's scores, then the value mix over window rows and
-// block mean values (kernels.cl:76-107).  One block per head.
-__global__ void k_sparse_attend(const float *scores, const float *v_ring, const float *v_mean, float *out, int heads,
-                                int kv_heads, int dim, int start, int length, int blocks) {
-    pdl_trigger();
-    pdl_wait();
-    extern __shared__ float p[];
-    __shared__ float red[32];
-    const int h = blockIdx.x, total = length + blocks;
-    const int kh = h / (heads / kv_heads), width = kv_heads * dim;
-    const float *s = scores + static_cast<size_t>(h) * total;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    __syncthreads();
+    const float *s = p;
     float m = -INFINITY;
     for (int t = threadIdx.x; t < total; t += blockDim.x) m = fmaxf(m, s[t]);
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -454,7 +488,7 @@ __global__ void k_sparse_attend(const float *scores, const float *v_ring, const 
     for (int w = 0; w < nwarps; ++w) m = fmaxf(m, red[w]);
     __syncthreads();
     float den = 0.f;
-    for (int t = threadIdx.x; t < total; t += blockDim.x) {
+    for (int t = threadIdx.x; t < total; t += blockDim.x) {  // each thread rewrites only its own entries
         const float e = s[t] == -INFINITY ? 0.f : expf(__fsub_rn(s[t], m));
         p[t] = e;
         den += e;
@@ -821,9 +855,28 @@ __global__ void k_expert_combine(ExpertArgs a, const float *weights, float share
     if (r >= a.hidden) return;
     float res = 0.f;
     const int active = *a.active;
-    for (int k = 0; k < active; ++k) res = FADD(res, FMUL(weights[k], a.out[static_cast<size_t>(k) * a.hidden + r]));
-    for (int i = 0; i < a.shared; ++i)
-        res = FADD(res, FMUL(shared_scale, a.out[static_cast<size_t>(a.max_k + i) * a.hidden + r]));
+    // eight slots' rows and weights loaded at once, then summed in rank order
+    for (int k0 = 0; k0 < active; k0 += 8) {
+        float v[8], w[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const bool in = k0 + u < active;
+            v[u] = in ? a.out[static_cast<size_t>(k0 + u) * a.hidden + r] : 0.f;
+            w[u] = in ? weights[k0 + u] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (k0 + u < active) res = FADD(res, FMUL(w[u], v[u]));
+    }
+    for (int i0 = 0; i0 < a.shared; i0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            v[u] = i0 + u < a.shared ? a.out[static_cast<size_t>(a.max_k + i0 + u) * a.hidden + r] : 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (i0 + u < a.shared) res = FADD(res, FMUL(shared_scale, v[u]));
+    }
     x[r] = FADD(x[r], FMUL(scale, res));
 }
 
@@ -1149,7 +1202,7 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
     MR_REQUIRE(e->table_set, "heavy-medium-2.0: the distance-penalty table has not been set");
     MR_REQUIRE(position >= 0 && position < e->context, "position %d outside the context", position);
     cudaStream_t s = e->stream;
-    const int width = e->KVH * e->d, count = position + 1;
+    const int count = position + 1;
     const int length = std::min(e->window, count), start = count - length;
     const int blocks = (count + e->block - 1) / e->block;
     const int slots = std::min(e->slots, blocks), total = length + blocks;
@@ -1164,21 +1217,21 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             // attention (model.py:192-229)
             if (int rc = launch_gemv(*e, {Ly.q, Ly.latent})) return rc;
             if (int rc = launch_gemv(*e, {Ly.kv_up})) return rc;
-            if (int rc = launch(k_heads_norm_rope, e->H + e->KVH, 32, 0, s, e->q, e->kv, e->k_ring[li], e->v_ring[li], e->inv_freq, e->H,
-                                                          e->KVH, e->d, e->split_half, position, position)) return rc;
-            if (int rc = launch(k_block_mean_last, (2 * width + 255) / 256, 256, 0, s, e->k_ring[li], e->v_ring[li], e->k_mean[li],
-                                                                     e->v_mean[li], count, width, e->block)) return rc;
+            if (int rc = launch(k_heads_norm_rope, e->H + e->KVH, 32, 0, s, e->q, e->kv, e->k_ring[li], e->v_ring[li],
+                                e->inv_freq, e->H, e->KVH, e->d, e->split_half, position, position, e->k_mean[li],
+                                e->v_mean[li], e->block))
+                return rc;
             const int items = e->H * total;
             if (int rc = launch(k_sparse_scores, (items + 7) / 8, 256, 0, s, e->q, e->k_ring[li], e->k_mean[li], e->scores, e->H, e->KVH,
                                                            e->d, start, length, blocks)) return rc;
             int *kept = e->kept + li * e->H * std::max(1, e->slots);
-            if (int rc = launch(k_block_topk, e->H, 256, static_cast<size_t>(blocks) * (sizeof(float) + sizeof(int)), s, 
-                e->scores, total, length, blocks, e->block, position, e->log1p_table, e->slope, slots,
-                std::max(1, e->slots), kept)) return rc;
             const int attend_threads = std::max(128, std::min(1024, (1024 / e->d) * e->d));
-            const size_t attend_smem = std::max<size_t>(total, static_cast<size_t>(attend_threads)) * sizeof(float);
-            if (int rc = launch(k_sparse_attend, e->H, attend_threads, attend_smem, s, e->scores, e->v_ring[li], e->v_mean[li], e->attn,
-                                                                     e->H, e->KVH, e->d, start, length, blocks)) return rc;
+            const size_t attend_smem =
+                std::max<size_t>(total, static_cast<size_t>(attend_threads)) * sizeof(float) + blocks * sizeof(int);
+            if (int rc = launch(k_sparse_attend, e->H, attend_threads, attend_smem, s, e->scores, e->v_ring[li],
+                                e->v_mean[li], e->attn, e->H, e->KVH, e->d, start, length, blocks, e->block, position,
+                                e->log1p_table, e->slope, slots, std::max(1, e->slots), kept))
+                return rc;
             GemvSeg o = Ly.o;
             o.scale = loop_scale;
             if (int rc = launch_gemv(*e, {o})) return rc;
