@@ -1087,8 +1087,6 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
         e->peers[rank] = e->arena;
     }
     MR_CUDA_TRY(cudaMemcpy(e->inv_freq, inv_freq_host, sizeof(float) * (e->d / 2), cudaMemcpyHostToDevice));
-    MR_CUDA_TRY(cudaFuncSetAttribute(k_expert_down, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(e->down_smem)));
     for (size_t i = 0; i < per; ++i) {
         float *kr, *vr, *km, *vm;
         if ((rc = halloc_n(*e, static_cast<size_t>(e->context) * width, &kr)) ||
@@ -1199,6 +1197,9 @@ int heavy_greedy_chain(HeavyEngine *e, int first_token, int position, int steps)
 
 namespace {
 int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
+    // the attribute belongs to the kernel, not to this model: set it for this model's size
+    MR_CUDA_TRY(cudaFuncSetAttribute(k_expert_down, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(e->down_smem)));
     MR_REQUIRE(e->table_set, "heavy-medium-2.0: the distance-penalty table has not been set");
     MR_REQUIRE(position >= 0 && position < e->context, "position %d outside the context", position);
     cudaStream_t s = e->stream;
