@@ -158,11 +158,11 @@ def ncu_traffic(config_name):
 
 def launches_per_step(config, expert_parallel=False):
     """Kernels one decode step launches: the persistent decode kernel once, or
-    Heavy Medium's device step (embedding row; per layer and inner loop 11
-    kernels, 12 with the expert-parallel flag kernel; the head with its norm,
+    Heavy Medium's device step (embedding row; per layer and inner loop 13
+    kernels, 14 with the expert-parallel flag kernel; the head with its norm,
     greedy argmax)."""
     if config.family == "heavy-medium-2.0":
-        return 1 + (12 if expert_parallel else 11) * config.layers * config.inner_loop_steps + 2
+        return 1 + (14 if expert_parallel else 13) * config.layers * config.inner_loop_steps + 2
     return 1
 
 
@@ -308,7 +308,9 @@ def run_cuda(args, ranks):
                 logits = model.decode(int(np.argmax(logits)))
             return steps, ranks.max(time.perf_counter() - t0)
 
-        if serial:  # continue from here rather than run the prompt token by token again
+        # a long token-by-token prompt: continue from here rather than run it again
+        continue_e2e = serial and model.position + min(args.steps, 128) <= context
+        if continue_e2e:
             e2e_steps, e2e_s = end_to_end(np.eye(1, config.vocab_size, token, dtype=np.float32)[0])
         # keep the same decode load under the clock sampler for ~1.5 s more (the same
         # number of calls on every rank: tensor-parallel ranks step together)
@@ -320,7 +322,7 @@ def run_cuda(args, ranks):
             native.call("mr_model_bench_decode", model._handle, token, extra_steps, C.byref(ms))
     clock_summary = clocks.summary()
 
-    if not serial:
+    if not continue_e2e:
         model.reset()
         e2e_steps, e2e_s = end_to_end(model.prefill(prompt))
 

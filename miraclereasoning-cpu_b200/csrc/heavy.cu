@@ -9,12 +9,13 @@
 //      q = W_q h, latent = W_latent h                            k_gemv (two segments)
 //   3. kv = W_kv_up latent                                       k_gemv
 //   4. q = RoPE(RMSNorm_noaffine(q)); k = RoPE(RMSNorm_noaffine(kv[:w]));
-//      append k, v = kv[w:] to the loop's ring; mean key / value
-//      of the newest block (older blocks' means never change)    k_heads_norm_rope
+//      append k, v = kv[w:] to the loop's ring                   k_heads_norm_rope
+//   5. mean key / value of the newest block (older blocks' means
+//      never change once full)                                   k_block_mean_last
 //   6. scores over the local window and every block mean        k_sparse_scores
-//   7-8. block columns minus the distance penalty, stable top
-//      `global_slots` per head, the rest masked (model.py:219-225);
-//      softmax + value mix over window rows and kept blocks     k_sparse_attend
+//   7. block columns minus the distance penalty, stable top
+//      `global_slots` per head, the rest masked (model.py:219-225) k_block_topk
+//   8. softmax + value mix over window rows and kept blocks     k_sparse_attend
 //   9. x += s * W_o attended                                     k_gemv (residual)
 //  10. f = RMSNorm(x, f_norm) (while staging); router logits    k_gemv
 //  11. routing (model.py:235-250): biases, temperature, softmax,
@@ -112,8 +113,65 @@ __device__ __forceinline__ float dot16(const uint4 &w, const float *x, int dtype
     return s;
 }
 
+// The first N 16-byte chunks per lane of up to two rows, loaded before the
+// block stages its input so that the weight stream starts at once.  (Sixteen
+// per lane, a whole 4096-wide BF16 row, measured no faster: the registers
+// halve the resident blocks.)
+constexpr int kBatch = 8;
+template <int N>
+struct RowBatchT {
+    uint4 w0[N], w1[N];
+};
 __device__ __forceinline__ bool whole_chunks(int dtype, int cols) {
     return ((static_cast<size_t>(cols) * (dtype == MR_DTYPE_F32 ? 4 : 2)) & 15) == 0;
+}
+template <int N>
+__device__ __forceinline__ void load_batch(const char *p0, const char *p1, int nv, int c0, RowBatchT<N> &b) {
+#pragma unroll
+    for (int u = 0; u < N; ++u) {
+        const int c = c0 + 32 * u;
+        b.w0[u] = c < nv ? ld_stream16(p0 + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
+        b.w1[u] = (p1 && c < nv) ? ld_stream16(p1 + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+template <int N>
+__device__ __forceinline__ void prefetch_rows(const char *p0, const char *p1, int dtype, int cols, RowBatchT<N> &b) {
+    if (whole_chunks(dtype, cols)) load_batch(p0, p1, cols / (dtype == MR_DTYPE_F32 ? 4 : 8), threadIdx.x & 31, b);
+}
+
+// One warp: dot products of up to two rows (cols elements of `dtype` at p0,
+// p1; p1 NULL: one row) with x (shared memory), the first chunks already in
+// `b` (prefetch_rows); every lane gets the sums.  Each lane keeps N 16-byte
+// loads of a row in flight.
+template <int N>
+__device__ __forceinline__ void warp_dot2(const char *p0, const char *p1, int dtype, int cols, const float *x,
+                                          RowBatchT<N> &b, float &y0, float &y1) {
+    const int lane = threadIdx.x & 31;
+    const int per = dtype == MR_DTYPE_F32 ? 4 : 8;
+    float a0 = 0.f, a1 = 0.f;
+    if (whole_chunks(dtype, cols)) {
+        const int nv = cols / per;
+        for (int c0 = lane;;) {
+#pragma unroll
+            for (int u = 0; u < N; ++u) {
+                const int c = c0 + 32 * u;
+                if (c < nv) {
+                    a0 += dot16(b.w0[u], x + per * c, dtype);
+                    if (p1) a1 += dot16(b.w1[u], x + per * c, dtype);
+                }
+            }
+            c0 += 32 * N;
+            if (c0 >= nv) break;
+            load_batch(p0, p1, nv, c0, b);
+        }
+    } else {  // rows that are not whole 16-byte chunks: element by element
+        for (int j = lane; j < cols; j += 32) {
+            a0 = fmaf(load_weight(p0, dtype, j), x[j], a0);
+            if (p1) a1 = fmaf(load_weight(p1, dtype, j), x[j], a1);
+        }
+    }
+    y0 = warp_sum(a0);
+    y1 = warp_sum(a1);
 }
 
 // Stages x (n floats) in shared memory, or RMSNorm(x) with `gain`
@@ -176,39 +234,6 @@ __device__ void stage_input(const float *x, int n, bool norm, const void *gain, 
     __syncthreads();
 }
 
-// ---- streaming GEMV: persistent blocks, each stages its input once; every
-// warp walks its rows in batches of N 16-byte chunks per lane and loads the
-// next batch (of this row or its next one) while it computes the current.
-template <int N>
-struct Chunks {
-    uint4 w[N];
-};
-template <int N>
-__device__ __forceinline__ void load_chunks(const char *p, int nv, int c0, Chunks<N> &b) {
-#pragma unroll
-    for (int u = 0; u < N; ++u) {
-        const int c = c0 + 32 * u;
-        b.w[u] = c < nv ? ld_stream16(p + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
-    }
-}
-template <int N>
-__device__ __forceinline__ float dot_chunks(const Chunks<N> &b, int nv, int c0, const float *x, int dtype) {
-    const int per = dtype == MR_DTYPE_F32 ? 4 : 8;
-    float acc = 0.f;
-#pragma unroll
-    for (int u = 0; u < N; ++u) {
-        const int c = c0 + 32 * u;
-        if (c < nv) acc += dot16(b.w[u], x + per * c, dtype);
-    }
-    return acc;
-}
-// One row that is not whole 16-byte chunks, element by element (one warp).
-__device__ __forceinline__ float warp_dot_scalar(const char *p, int dtype, int cols, const float *x) {
-    float acc = 0.f;
-    for (int j = threadIdx.x & 31; j < cols; j += 32) acc = fmaf(load_weight(p, dtype, j), x[j], acc);
-    return warp_sum(acc);
-}
-
 struct GemvSeg {
     const void *w;
     int dtype, rows, cols;
@@ -227,77 +252,26 @@ struct GemvArgs {
     int nseg;
 };
 
-// y = W x for up to kMaxSegs matrices that read the same input (segment 0's
-// x and RMSNorm), their rows numbered one after another (first[i] = the
-// first row of segment i).  Persistent blocks stage the input once and
-// stream their warps' rows.
-constexpr int kStreamBatch = 8;
-__device__ __forceinline__ int seg_of_row(const GemvArgs &a, int g) {
-    int si = 0;
-    while (si + 1 < a.nseg && g >= a.first[si + 1]) ++si;
-    return si;
-}
-__device__ __forceinline__ const char *seg_row_ptr(const GemvSeg &s, int r) {
-    return static_cast<const char *>(s.w) + static_cast<size_t>(r) * s.cols * (s.dtype == MR_DTYPE_F32 ? 4 : 2);
-}
+// y = W x for up to kMaxSegs matrices; each block takes kGemvRows rows (one
+// per warp) of one segment and stages that segment's input in shared memory.
 __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a) {
     extern __shared__ __align__(16) float xs[];
     pdl_trigger();
-    const int lane = threadIdx.x & 31;
-    const int W = gridDim.x * (kGemvThreads / 32), total = a.first[a.nseg];
-    int g = blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5), c0 = lane;
-    Chunks<kStreamBatch> cur, nxt;
-    if (g < total) {
-        const GemvSeg &s = a.s[seg_of_row(a, g)];
-        if (whole_chunks(s.dtype, s.cols))
-            load_chunks(seg_row_ptr(s, g - a.first[seg_of_row(a, g)]), s.cols / (s.dtype == MR_DTYPE_F32 ? 4 : 8), c0,
-                        cur);
-    }
+    int si = 0;
+    while (si + 1 < a.nseg && static_cast<int>(blockIdx.x) >= a.first[si + 1]) ++si;
+    const GemvSeg &s = a.s[si];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = (blockIdx.x - a.first[si]) * kGemvRows + warp;
+    const size_t row_bytes = static_cast<size_t>(s.cols) * (s.dtype == MR_DTYPE_F32 ? 4 : 2);
+    const char *row = static_cast<const char *>(s.w) + static_cast<size_t>(min(r, s.rows - 1)) * row_bytes;
+    RowBatchT<kBatch> b;
+    if (r < s.rows) prefetch_rows(row, nullptr, s.dtype, s.cols, b);
     pdl_wait();
-    const GemvSeg &s0 = a.s[0];
-    stage_input(s0.x, s0.cols, s0.norm != 0, s0.gain, s0.gain_dtype, s0.eps, xs);
-    float acc = 0.f;
-    while (g < total) {
-        const int si = seg_of_row(a, g), r = g - a.first[si];
-        const GemvSeg &s = a.s[si];
-        float y;
-        int ng = g, nc = c0;
-        if (!whole_chunks(s.dtype, s.cols)) {
-            y = warp_dot_scalar(seg_row_ptr(s, r), s.dtype, s.cols, xs);
-            ng = g + W;
-            nc = lane;
-            if (ng < total) {
-                const int ns = seg_of_row(a, ng);
-                const GemvSeg &t = a.s[ns];
-                if (whole_chunks(t.dtype, t.cols))
-                    load_chunks(seg_row_ptr(t, ng - a.first[ns]), t.cols / (t.dtype == MR_DTYPE_F32 ? 4 : 8), nc, cur);
-            }
-        } else {
-            const int nv = s.cols / (s.dtype == MR_DTYPE_F32 ? 4 : 8);
-            nc = c0 + 32 * kStreamBatch;
-            if (nc >= nv) {
-                ng = g + W;
-                nc = lane;
-            }
-            if (ng < total) {  // the next batch, loaded while this one is summed
-                const int ns = seg_of_row(a, ng);
-                const GemvSeg &t = a.s[ns];
-                if (whole_chunks(t.dtype, t.cols))
-                    load_chunks(seg_row_ptr(t, ng - a.first[ns]), t.cols / (t.dtype == MR_DTYPE_F32 ? 4 : 8), nc, nxt);
-            }
-            acc += dot_chunks(cur, nv, c0, xs, s.dtype);
-            cur = nxt;
-            if (ng == g) {
-                c0 = nc;
-                continue;
-            }
-            y = warp_sum(acc);
-            acc = 0.f;
-        }
-        if (lane == 0) s.y[r] = s.residual ? FADD(s.y[r], FMUL(s.scale, y)) : y;
-        g = ng;
-        c0 = nc;
-    }
+    stage_input(s.x, s.cols, s.norm != 0, s.gain, s.gain_dtype, s.eps, xs);
+    if (r >= s.rows) return;
+    float y, unused;
+    warp_dot2(row, nullptr, s.dtype, s.cols, xs, b, y, unused);
+    if (lane == 0) s.y[r] = s.residual ? FADD(s.y[r], FMUL(s.scale, y)) : y;
 }
 
 // x = embed[token]; the token from `dtoken` (device) when given.
@@ -349,8 +323,7 @@ __global__ void k_argmax(const float *v, int n, int *token) {
 // non-affine RMSNorm (eps 1e-6, model.py:194, 201) then RoPE at `position`
 // (kernels.cl:30-44); keys and values go to ring row `row`.
 __global__ void k_heads_norm_rope(float *q, const float *kv, float *k_ring, float *v_ring, const float *inv_freq,
-                                  int heads, int kv_heads, int dim, int split_half, int position, int row,
-                                  float *k_mean, float *v_mean, int block) {
+                                  int heads, int kv_heads, int dim, int split_half, int position, int row) {
     pdl_trigger();
     pdl_wait();
     const int h = blockIdx.x, lane = threadIdx.x;
@@ -390,24 +363,24 @@ __global__ void k_heads_norm_rope(float *q, const float *kv, float *k_ring, floa
         dst[j] = __fsub_rn(FMUL(u[n], c), FMUL(v[n], s));
         dst[k] = FADD(FMUL(u[n], s), FMUL(v[n], c));
     }
-    if (h < heads) return;
-    // key heads: the mean of the newest block's rows of this head (kernels.cl:139-148:
-    // a running sum in row order, then one division) for keys and values; full
-    // blocks' means never change once written
-    __syncwarp();  // this warp's key / value row is in
-    const int kh = h - heads, count = row + 1, b = (count - 1) / block, start = b * block;
-    const float rows = static_cast<float>(count - start);
-    for (int j = lane; j < dim; j += 32) {
-        const size_t col = static_cast<size_t>(kh) * dim + j;
-        float sk = 0.f, sv = 0.f;
+}
+
+// Mean of the newest block's rows (kernels.cl:139-148: running sum in row
+// order, then one division) for keys and values; full blocks never change.
+__global__ void k_block_mean_last(const float *k_ring, const float *v_ring, float *k_mean, float *v_mean, int count,
+                                  int width, int block) {
+    pdl_trigger();
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= 2 * width) return;
+    const int j = i % width;
+    const float *src = i < width ? k_ring : v_ring;
+    float *dst = i < width ? k_mean : v_mean;
+    const int b = (count - 1) / block, start = b * block, stop = min(start + block, count);
+    float v = 0.f;
 #pragma unroll 8
-        for (int t = start; t < count; ++t) {
-            sk = FADD(sk, k_ring[static_cast<size_t>(t) * width + col]);
-            sv = FADD(sv, v_ring[static_cast<size_t>(t) * width + col]);
-        }
-        k_mean[static_cast<size_t>(b) * width + col] = __fdiv_rn(sk, rows);
-        v_mean[static_cast<size_t>(b) * width + col] = __fdiv_rn(sv, rows);
-    }
+    for (int t = start; t < stop; ++t) v = FADD(v, src[static_cast<size_t>(t) * width + j]);
+    dst[static_cast<size_t>(b) * width + j] = __fdiv_rn(v, static_cast<float>(stop - start));
 }
 
 // scores[h][t], t < length: local ring rows start .. start+length-1; t >= length:
@@ -431,54 +404,55 @@ __global__ void k_sparse_scores(const float *q, const float *k_ring, const float
     if (lane == 0) scores[static_cast<size_t>(h) * total + t] = __fdiv_rn(v, __fsqrt_rn(static_cast<float>(dim)));
 }
 
-// One block per head: the global-block selection of model.py:219-225, then
-// the softmax over the head's scores and the value mix over window rows and
-// kept block means (kernels.cl:76-107).
-// Selection: block column b loses slope * log1p(position - end_b)
-// (end_b = min((b + 1) * block - 1, position), the log1p value from the host's
-// table); the `slots` best columns (stable descending order: ties go to the
-// lower index) stay, the rest become -inf.  The kept block ids go to `kept` in
-// ascending order, -1 padded to `slots_max`.
-__global__ void k_sparse_attend(const float *scores, const float *v_ring, const float *v_mean, float *out, int heads,
-                                int kv_heads, int dim, int start, int length, int blocks, int block, int position,
-                                const float *log1p_table, float slope, int slots, int slots_max, int *kept) {
+// model.py:219-225 per head (one block): block column b loses
+// slope * log1p(position - end_b) (end_b = min((b + 1) * block - 1, position),
+// the log1p value from the host's table), the `slots` best columns (stable
+// descending order: ties go to the lower index) stay, the rest become -inf.
+// The kept block ids go to `kept` in ascending order, -1 padded to `slots_max`.
+__global__ void k_block_topk(float *scores, int total, int length, int blocks, int block, int position,
+                             const float *log1p_table, float slope, int slots, int slots_max, int *kept) {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ float p[];  // [max(total, blockDim)] scores, then weights, then partial sums
-    __shared__ float red[32];
-    const int h = blockIdx.x, total = length + blocks;
-    const int kh = h / (heads / kv_heads), width = kv_heads * dim;
-    int *keep = reinterpret_cast<int *>(p + max(total, static_cast<int>(blockDim.x)));
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    for (int t = threadIdx.x; t < total; t += blockDim.x) {
-        float v = scores[static_cast<size_t>(h) * total + t];
-        if (t >= length) {
-            const int b = t - length, end = min((b + 1) * block - 1, position);
-            v = __fsub_rn(v, FMUL(slope, log1p_table[position - end]));
-        }
-        p[t] = v;
+    extern __shared__ float sb[];
+    int *keep = reinterpret_cast<int *>(sb + blocks);
+    const int h = blockIdx.x;
+    float *row = scores + static_cast<size_t>(h) * total + length;
+    for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
+        const int end = min((b + 1) * block - 1, position);
+        sb[b] = __fsub_rn(row[b], FMUL(slope, log1p_table[position - end]));
     }
     __syncthreads();
     for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
-        const float v = p[length + b];
+        const float v = sb[b];
         int rank = 0;
         for (int j = 0; j < blocks; ++j) {
-            const float u = p[length + j];
+            const float u = sb[j];
             rank += (u > v) || (u == v && j < b);
         }
-        keep[b] = rank < slots;
+        keep[b] = rank < slots && v != -INFINITY;
+        row[b] = rank < slots ? v : -INFINITY;
     }
     __syncthreads();
-    for (int b = threadIdx.x; b < blocks; b += blockDim.x)
-        if (!keep[b]) p[length + b] = -INFINITY;
     if (threadIdx.x == 0) {  // ascending ids of the kept columns (np.flatnonzero order)
         int n = 0;
         for (int b = 0; b < blocks && n < slots_max; ++b)
             if (keep[b]) kept[h * slots_max + n++] = b;
         for (; n < slots_max; ++n) kept[h * slots_max + n] = -1;
     }
-    __syncthreads();
-    const float *s = p;
+}
+
+// Softmax over one head's scores, then the value mix over window rows and
+// block mean values (kernels.cl:76-107).  One block per head.
+__global__ void k_sparse_attend(const float *scores, const float *v_ring, const float *v_mean, float *out, int heads,
+                                int kv_heads, int dim, int start, int length, int blocks) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ float p[];
+    __shared__ float red[32];
+    const int h = blockIdx.x, total = length + blocks;
+    const int kh = h / (heads / kv_heads), width = kv_heads * dim;
+    const float *s = scores + static_cast<size_t>(h) * total;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     float m = -INFINITY;
     for (int t = threadIdx.x; t < total; t += blockDim.x) m = fmaxf(m, s[t]);
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -488,7 +462,7 @@ __global__ void k_sparse_attend(const float *scores, const float *v_ring, const 
     for (int w = 0; w < nwarps; ++w) m = fmaxf(m, red[w]);
     __syncthreads();
     float den = 0.f;
-    for (int t = threadIdx.x; t < total; t += blockDim.x) {  // each thread rewrites only its own entries
+    for (int t = threadIdx.x; t < total; t += blockDim.x) {
         const float e = s[t] == -INFINITY ? 0.f : expf(__fsub_rn(s[t], m));
         p[t] = e;
         den += e;
@@ -655,156 +629,51 @@ __device__ __forceinline__ int slot_expert(const ExpertArgs &a, int slot) {
     return (e >= 0 && e % a.ranks == a.rank) ? e : -1;
 }
 
-// This rank's active slots (in slot order) into shared memory: list[k] =
-// slot, eid[k] = its expert; returns how many.
-__device__ int owned_slots(const ExpertArgs &a, int *list, int *eid) {
-    __shared__ int n;
-    if (threadIdx.x == 0) {
-        int k = 0;
-        for (int slot = 0; slot < a.max_k + a.shared; ++slot) {
-            const int e = slot_expert(a, slot);
-            if (e >= 0) {
-                list[k] = slot;
-                eid[k++] = e;
-            }
-        }
-        n = k;
-    }
-    __syncthreads();
-    return n;
-}
-
-// act[slot][r] = silu(gate_r . x) * (up_r . x) (kernels.cl:46-50) for this
-// rank's active slots: persistent blocks stage RMSNorm(x, f_norm) once, warps
-// stream (slot, row) items, the gate and up rows side by side.
-constexpr int kPairBatch = 4;
+// act[slot][r] = silu(gate_r . x) * (up_r . x) (kernels.cl:46-50); grid (row blocks, slots).
 __global__ void __launch_bounds__(kGemvThreads) k_expert_gate_up(ExpertArgs a) {
     pdl_trigger();
     pdl_wait();
     extern __shared__ __align__(16) float xs[];
-    __shared__ int list[64], eid[64];
-    const int nact = owned_slots(a, list, eid);
-    stage_input(a.x, a.hidden, true, a.norm_gain, a.norm_dtype, a.eps, xs);
-    const int lane = threadIdx.x & 31, W = gridDim.x * (kGemvThreads / 32), total = nact * a.ffn;
+    const int slot = blockIdx.y, e = slot_expert(a, slot);
+    if (e < 0) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + warp;
     const size_t row_bytes = static_cast<size_t>(a.hidden) * (a.dtype == MR_DTYPE_F32 ? 4 : 2);
-    const bool whole = whole_chunks(a.dtype, a.hidden);
-    const int nv = a.hidden / (a.dtype == MR_DTYPE_F32 ? 4 : 8);
-    auto rows_of = [&](int g, const char *&gp, const char *&up) {
-        const int k = g / a.ffn, r = g - k * a.ffn;
-        gp = static_cast<const char *>(a.gate[eid[k]]) + r * row_bytes;
-        up = static_cast<const char *>(a.up[eid[k]]) + r * row_bytes;
-    };
-    int g = blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5), c0 = lane;
-    Chunks<kPairBatch> cg, cu, ng_, nu;
-    const char *gp, *up;
-    if (g < total && whole) {
-        rows_of(g, gp, up);
-        load_chunks(gp, nv, c0, cg);
-        load_chunks(up, nv, c0, cu);
-    }
-    float ag = 0.f, au = 0.f;
-    while (g < total) {
-        const int k = g / a.ffn, r = g - k * a.ffn;
-        float gv, uv;
-        int ng = g, nc = c0;
-        if (!whole) {
-            rows_of(g, gp, up);
-            gv = warp_dot_scalar(gp, a.dtype, a.hidden, xs);
-            uv = warp_dot_scalar(up, a.dtype, a.hidden, xs);
-            ng = g + W;
-            nc = lane;
-        } else {
-            nc = c0 + 32 * kPairBatch;
-            if (nc >= nv) {
-                ng = g + W;
-                nc = lane;
-            }
-            if (ng < total) {
-                const char *pg, *pu;
-                rows_of(ng, pg, pu);
-                load_chunks(pg, nv, nc, ng_);
-                load_chunks(pu, nv, nc, nu);
-            }
-            ag += dot_chunks(cg, nv, c0, xs, a.dtype);
-            au += dot_chunks(cu, nv, c0, xs, a.dtype);
-            cg = ng_;
-            cu = nu;
-            if (ng == g) {
-                c0 = nc;
-                continue;
-            }
-            gv = warp_sum(ag);
-            uv = warp_sum(au);
-            ag = au = 0.f;
-        }
-        if (lane == 0) a.act[static_cast<size_t>(list[k]) * a.ffn + r] = FMUL(__fdiv_rn(gv, FADD(1.0f, expf(-gv))), uv);
-        g = ng;
-        c0 = nc;
-    }
+    const size_t off = static_cast<size_t>(min(r, a.ffn - 1)) * row_bytes;
+    const char *gp = static_cast<const char *>(a.gate[e]) + off, *up = static_cast<const char *>(a.up[e]) + off;
+    RowBatchT<kBatch> b;
+    if (r < a.ffn) prefetch_rows(gp, up, a.dtype, a.hidden, b);
+    stage_input(a.x, a.hidden, true, a.norm_gain, a.norm_dtype, a.eps, xs);
+    if (r >= a.ffn) return;
+    float g, u;
+    warp_dot2(gp, up, a.dtype, a.hidden, xs, b, g, u);
+    if (lane == 0) a.act[static_cast<size_t>(slot) * a.ffn + r] = FMUL(__fdiv_rn(g, FADD(1.0f, expf(-g))), u);
 }
 
-// out[slot][r] = down_r . act[slot] for this rank's active slots: persistent
-// blocks stage every such slot's activations once and stream (slot, row)
-// items.  Expert parallel: every row goes to every rank's arena.
+// out[slot][r] = down_r . act[slot]; grid (row blocks, slots).
 __global__ void __launch_bounds__(kGemvThreads) k_expert_down(ExpertArgs a) {
     pdl_trigger();
     pdl_wait();
     extern __shared__ __align__(16) float xs[];
-    __shared__ int list[64], eid[64];
-    const int nact = owned_slots(a, list, eid);
-    for (int i = threadIdx.x; i < nact * a.ffn; i += blockDim.x) {
-        const int k = i / a.ffn;
-        xs[i] = a.act[static_cast<size_t>(list[k]) * a.ffn + (i - k * a.ffn)];
-    }
-    __syncthreads();
-    const int lane = threadIdx.x & 31, W = gridDim.x * (kGemvThreads / 32), total = nact * a.hidden;
+    const int slot = blockIdx.y, e = slot_expert(a, slot);
+    if (e < 0) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * kGemvRows + warp;
     const size_t row_bytes = static_cast<size_t>(a.ffn) * (a.dtype == MR_DTYPE_F32 ? 4 : 2);
-    const bool whole = whole_chunks(a.dtype, a.ffn);
-    const int nv = a.ffn / (a.dtype == MR_DTYPE_F32 ? 4 : 8);
-    auto row_of = [&](int g) {
-        const int k = g / a.hidden;
-        return static_cast<const char *>(a.down[eid[k]]) + (g - k * a.hidden) * row_bytes;
-    };
-    int g = blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5), c0 = lane;
-    Chunks<kStreamBatch> cur, nxt;
-    if (g < total && whole) load_chunks(row_of(g), nv, c0, cur);
-    float acc = 0.f;
-    while (g < total) {
-        const int k = g / a.hidden, r = g - k * a.hidden;
-        const float *x = xs + static_cast<size_t>(k) * a.ffn;
-        float y;
-        int ng = g, nc = c0;
-        if (!whole) {
-            y = warp_dot_scalar(row_of(g), a.dtype, a.ffn, x);
-            ng = g + W;
-            nc = lane;
+    const char *row = static_cast<const char *>(a.down[e]) + static_cast<size_t>(min(r, a.hidden - 1)) * row_bytes;
+    RowBatchT<kBatch> b;
+    if (r < a.hidden) prefetch_rows(row, nullptr, a.dtype, a.ffn, b);
+    stage_input(a.act + static_cast<size_t>(slot) * a.ffn, a.ffn, false, nullptr, 0, 0.f, xs);
+    if (r >= a.hidden) return;
+    float y, unused;
+    warp_dot2(row, nullptr, a.dtype, a.ffn, xs, b, y, unused);
+    const size_t at = (static_cast<size_t>(slot) * a.hidden + r) * sizeof(float);
+    if (lane == 0) {
+        if (a.ranks == 1) {
+            a.out[static_cast<size_t>(slot) * a.hidden + r] = y;
         } else {
-            nc = c0 + 32 * kStreamBatch;
-            if (nc >= nv) {
-                ng = g + W;
-                nc = lane;
-            }
-            if (ng < total) load_chunks(row_of(ng), nv, nc, nxt);
-            acc += dot_chunks(cur, nv, c0, x, a.dtype);
-            cur = nxt;
-            if (ng == g) {
-                c0 = nc;
-                continue;
-            }
-            y = warp_sum(acc);
-            acc = 0.f;
+            for (int j = 0; j < a.ranks; ++j) *reinterpret_cast<float *>(a.peer[j] + a.out_offset + at) = y;
         }
-        if (lane == 0) {
-            const int slot = list[k];
-            if (a.ranks == 1) {
-                a.out[static_cast<size_t>(slot) * a.hidden + r] = y;
-            } else {
-                const size_t at = (static_cast<size_t>(slot) * a.hidden + r) * sizeof(float);
-                for (int j = 0; j < a.ranks; ++j) *reinterpret_cast<float *>(a.peer[j] + a.out_offset + at) = y;
-            }
-        }
-        g = ng;
-        c0 = nc;
     }
     if (a.ranks > 1) __threadfence_system();  // the rows reach every rank before the flag (k_moe_publish)
 }
@@ -920,7 +789,6 @@ struct HeavyEngine {
     char *peers[kMaxHeavyRanks] = {};
     unsigned long long moe_tag = 0;
     int *err = nullptr;
-    size_t down_smem = 0;  // k_expert_down stages every active slot's activations
     std::vector<void *> allocations;
     bool table_set = false;
 };
@@ -974,26 +842,17 @@ int launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaSt
     return MR_OK;
 }
 
-// Persistent blocks of a streaming kernel: two per SM, fewer when there are
-// fewer warp items.
-unsigned stream_blocks(int items) {
-    return static_cast<unsigned>(std::max(1, std::min(2 * 148, (items + kGemvRows - 1) / kGemvRows)));
-}
-
 int launch_gemv(HeavyEngine &e, std::initializer_list<GemvSeg> segs) {
     GemvArgs a{};
-    int rows = 0;
+    int blocks = 0, cols = 0;
     for (const GemvSeg &s : segs) {
-        // the segments of one launch read one input (segment 0's, with its norm)
-        if (a.nseg && (s.x != a.s[0].x || s.norm != a.s[0].norm || s.gain != a.s[0].gain || s.cols != a.s[0].cols))
-            return set_error(MR_ERR_ARGUMENT, "GEMV segments of one launch must share their input");
-        a.first[a.nseg] = rows;
+        a.first[a.nseg] = blocks;
         a.s[a.nseg++] = s;
-        rows += s.rows;
+        blocks += (s.rows + kGemvRows - 1) / kGemvRows;
+        cols = std::max(cols, s.cols);
     }
-    a.first[a.nseg] = rows;
-    const size_t smem = static_cast<size_t>(a.s[0].cols) * sizeof(float) + 16;
-    if (int rc = launch(k_gemv, stream_blocks(rows), kGemvThreads, smem, e.stream, a)) return rc;
+    a.first[a.nseg] = blocks;
+    if (int rc = launch(k_gemv, blocks, kGemvThreads, static_cast<size_t>(cols) * sizeof(float) + 16, e.stream, a)) return rc;
     MR_CUDA_TRY(cudaGetLastError());
     return MR_OK;
 }
@@ -1037,10 +896,8 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
         heavy_destroy(e);
         return rc;
     };
-    e->down_smem = static_cast<size_t>(e->max_k + e->shared) * e->ffn * sizeof(float) + 16;
     if (!(e->window > 0 && e->block > 0 && e->latent > 0 && e->experts > 0 && e->experts <= 256 && e->groups > 0 &&
-          e->max_k >= 1 && e->max_k + e->shared <= 64 && e->min_k >= 0 && e->slots >= 0 && e->shared >= 0 &&
-          e->down_smem <= 200 * 1024 && static_cast<size_t>(e->hidden) * sizeof(float) + 16 <= 48 * 1024 &&
+          e->max_k >= 1 && e->max_k <= 64 && e->min_k >= 0 && e->slots >= 0 && e->shared >= 0 &&
           e->H % e->KVH == 0 && e->d <= 1024 && e->d % 2 == 0 && e->d / 2 <= 128)) {
         heavy_destroy(e);
         return set_error(MR_ERR_ARGUMENT, "heavy-medium-2.0 geometry outside the device path's limits");
@@ -1197,13 +1054,10 @@ int heavy_greedy_chain(HeavyEngine *e, int first_token, int position, int steps)
 
 namespace {
 int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
-    // the attribute belongs to the kernel, not to this model: set it for this model's size
-    MR_CUDA_TRY(cudaFuncSetAttribute(k_expert_down, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(e->down_smem)));
     MR_REQUIRE(e->table_set, "heavy-medium-2.0: the distance-penalty table has not been set");
     MR_REQUIRE(position >= 0 && position < e->context, "position %d outside the context", position);
     cudaStream_t s = e->stream;
-    const int count = position + 1;
+    const int width = e->KVH * e->d, count = position + 1;
     const int length = std::min(e->window, count), start = count - length;
     const int blocks = (count + e->block - 1) / e->block;
     const int slots = std::min(e->slots, blocks), total = length + blocks;
@@ -1218,21 +1072,21 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             // attention (model.py:192-229)
             if (int rc = launch_gemv(*e, {Ly.q, Ly.latent})) return rc;
             if (int rc = launch_gemv(*e, {Ly.kv_up})) return rc;
-            if (int rc = launch(k_heads_norm_rope, e->H + e->KVH, 32, 0, s, e->q, e->kv, e->k_ring[li], e->v_ring[li],
-                                e->inv_freq, e->H, e->KVH, e->d, e->split_half, position, position, e->k_mean[li],
-                                e->v_mean[li], e->block))
-                return rc;
+            if (int rc = launch(k_heads_norm_rope, e->H + e->KVH, 32, 0, s, e->q, e->kv, e->k_ring[li], e->v_ring[li], e->inv_freq, e->H,
+                                                          e->KVH, e->d, e->split_half, position, position)) return rc;
+            if (int rc = launch(k_block_mean_last, (2 * width + 255) / 256, 256, 0, s, e->k_ring[li], e->v_ring[li], e->k_mean[li],
+                                                                     e->v_mean[li], count, width, e->block)) return rc;
             const int items = e->H * total;
             if (int rc = launch(k_sparse_scores, (items + 7) / 8, 256, 0, s, e->q, e->k_ring[li], e->k_mean[li], e->scores, e->H, e->KVH,
                                                            e->d, start, length, blocks)) return rc;
             int *kept = e->kept + li * e->H * std::max(1, e->slots);
+            if (int rc = launch(k_block_topk, e->H, 256, static_cast<size_t>(blocks) * (sizeof(float) + sizeof(int)), s, 
+                e->scores, total, length, blocks, e->block, position, e->log1p_table, e->slope, slots,
+                std::max(1, e->slots), kept)) return rc;
             const int attend_threads = std::max(128, std::min(1024, (1024 / e->d) * e->d));
-            const size_t attend_smem =
-                std::max<size_t>(total, static_cast<size_t>(attend_threads)) * sizeof(float) + blocks * sizeof(int);
-            if (int rc = launch(k_sparse_attend, e->H, attend_threads, attend_smem, s, e->scores, e->v_ring[li],
-                                e->v_mean[li], e->attn, e->H, e->KVH, e->d, start, length, blocks, e->block, position,
-                                e->log1p_table, e->slope, slots, std::max(1, e->slots), kept))
-                return rc;
+            const size_t attend_smem = std::max<size_t>(total, static_cast<size_t>(attend_threads)) * sizeof(float);
+            if (int rc = launch(k_sparse_attend, e->H, attend_threads, attend_smem, s, e->scores, e->v_ring[li], e->v_mean[li], e->attn,
+                                                                     e->H, e->KVH, e->d, start, length, blocks)) return rc;
             GemvSeg o = Ly.o;
             o.scale = loop_scale;
             if (int rc = launch_gemv(*e, {o})) return rc;
@@ -1285,11 +1139,8 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
                 ea.flags_offset = e->flags_offset;
                 for (int j = 0; j < e->ranks; ++j) ea.peer[j] = e->peers[j];
             }
-            if (int rc = launch(k_expert_gate_up, stream_blocks(slots_total * e->ffn), kGemvThreads,
-                                static_cast<size_t>(e->hidden) * sizeof(float) + 16, s, ea))
-                return rc;
-            if (int rc = launch(k_expert_down, stream_blocks(slots_total * e->hidden), kGemvThreads, e->down_smem, s, ea))
-                return rc;
+            if (int rc = launch(k_expert_gate_up, dim3((e->ffn + 7) / 8, slots_total), kGemvThreads, static_cast<size_t>(e->hidden) * sizeof(float) + 16, s, ea)) return rc;
+            if (int rc = launch(k_expert_down, dim3((e->hidden + kGemvRows - 1) / kGemvRows, slots_total), kGemvThreads, static_cast<size_t>(e->ffn) * sizeof(float) + 16, s, ea)) return rc;
             if (e->ranks > 1)
                 if (int rc = launch(k_moe_publish, 1, 32, 0, s, ea)) return rc;
             if (int rc = launch(k_expert_combine, (e->hidden + 255) / 256, 256, 0, s, ea, ra.weights, shared_scale, loop_scale, e->x)) return rc;
