@@ -852,7 +852,8 @@ int launch_gemv(HeavyEngine &e, std::initializer_list<GemvSeg> segs) {
         cols = std::max(cols, s.cols);
     }
     a.first[a.nseg] = blocks;
-    if (int rc = launch(k_gemv, blocks, kGemvThreads, static_cast<size_t>(cols) * sizeof(float) + 16, e.stream, a)) return rc;
+    if (int rc = launch(k_gemv, blocks, kGemvThreads, static_cast<size_t>(cols) * sizeof(float) + 16, e.stream, a))
+        return rc;
     MR_CUDA_TRY(cudaGetLastError());
     return MR_OK;
 }
@@ -1003,7 +1004,8 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
         }
         Ly.expert_dtype = dtype;
         const size_t n = gate.size();
-        if ((rc = halloc_n(*e, n, &Ly.d_gate)) || (rc = halloc_n(*e, n, &Ly.d_up)) || (rc = halloc_n(*e, n, &Ly.d_down)))
+        if ((rc = halloc_n(*e, n, &Ly.d_gate)) || (rc = halloc_n(*e, n, &Ly.d_up)) ||
+            (rc = halloc_n(*e, n, &Ly.d_down)))
             return fail(rc);
         MR_CUDA_TRY(cudaMemcpy(Ly.d_gate, gate.data(), n * sizeof(void *), cudaMemcpyHostToDevice));
         MR_CUDA_TRY(cudaMemcpy(Ly.d_up, up.data(), n * sizeof(void *), cudaMemcpyHostToDevice));
@@ -1064,7 +1066,9 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
     const int slots_total = e->max_k + e->shared;
     const float loop_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::sqrt((double)e->loops));
     const float shared_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::max(e->shared, 1));
-    if (int rc = launch(k_embed_row, (e->hidden + 255) / 256, 256, 0, s, e->embed, e->embed_dt, dtoken, token, e->hidden, e->x)) return rc;
+    if (int rc = launch(k_embed_row, (e->hidden + 255) / 256, 256, 0, s, e->embed, e->embed_dt, dtoken, token,
+                        e->hidden, e->x))
+        return rc;
     for (int l = 0; l < e->layers; ++l) {
         HeavyLayer &Ly = e->L[l];
         for (int loop = 0; loop < e->loops; ++loop) {
@@ -1072,21 +1076,26 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             // attention (model.py:192-229)
             if (int rc = launch_gemv(*e, {Ly.q, Ly.latent})) return rc;
             if (int rc = launch_gemv(*e, {Ly.kv_up})) return rc;
-            if (int rc = launch(k_heads_norm_rope, e->H + e->KVH, 32, 0, s, e->q, e->kv, e->k_ring[li], e->v_ring[li], e->inv_freq, e->H,
-                                                          e->KVH, e->d, e->split_half, position, position)) return rc;
-            if (int rc = launch(k_block_mean_last, (2 * width + 255) / 256, 256, 0, s, e->k_ring[li], e->v_ring[li], e->k_mean[li],
-                                                                     e->v_mean[li], count, width, e->block)) return rc;
+            if (int rc = launch(k_heads_norm_rope, e->H + e->KVH, 32, 0, s, e->q, e->kv, e->k_ring[li], e->v_ring[li],
+                                e->inv_freq, e->H, e->KVH, e->d, e->split_half, position, position))
+                return rc;
+            if (int rc = launch(k_block_mean_last, (2 * width + 255) / 256, 256, 0, s, e->k_ring[li], e->v_ring[li],
+                                e->k_mean[li], e->v_mean[li], count, width, e->block))
+                return rc;
             const int items = e->H * total;
-            if (int rc = launch(k_sparse_scores, (items + 7) / 8, 256, 0, s, e->q, e->k_ring[li], e->k_mean[li], e->scores, e->H, e->KVH,
-                                                           e->d, start, length, blocks)) return rc;
+            if (int rc = launch(k_sparse_scores, (items + 7) / 8, 256, 0, s, e->q, e->k_ring[li], e->k_mean[li],
+                                e->scores, e->H, e->KVH, e->d, start, length, blocks))
+                return rc;
             int *kept = e->kept + li * e->H * std::max(1, e->slots);
-            if (int rc = launch(k_block_topk, e->H, 256, static_cast<size_t>(blocks) * (sizeof(float) + sizeof(int)), s, 
-                e->scores, total, length, blocks, e->block, position, e->log1p_table, e->slope, slots,
-                std::max(1, e->slots), kept)) return rc;
+            if (int rc = launch(k_block_topk, e->H, 256, static_cast<size_t>(blocks) * (sizeof(float) + sizeof(int)), s,
+                                e->scores, total, length, blocks, e->block, position, e->log1p_table, e->slope, slots,
+                                std::max(1, e->slots), kept))
+                return rc;
             const int attend_threads = std::max(128, std::min(1024, (1024 / e->d) * e->d));
             const size_t attend_smem = std::max<size_t>(total, static_cast<size_t>(attend_threads)) * sizeof(float);
-            if (int rc = launch(k_sparse_attend, e->H, attend_threads, attend_smem, s, e->scores, e->v_ring[li], e->v_mean[li], e->attn,
-                                                                     e->H, e->KVH, e->d, start, length, blocks)) return rc;
+            if (int rc = launch(k_sparse_attend, e->H, attend_threads, attend_smem, s, e->scores, e->v_ring[li],
+                                e->v_mean[li], e->attn, e->H, e->KVH, e->d, start, length, blocks))
+                return rc;
             GemvSeg o = Ly.o;
             o.scale = loop_scale;
             if (int rc = launch_gemv(*e, {o})) return rc;
@@ -1139,11 +1148,17 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
                 ea.flags_offset = e->flags_offset;
                 for (int j = 0; j < e->ranks; ++j) ea.peer[j] = e->peers[j];
             }
-            if (int rc = launch(k_expert_gate_up, dim3((e->ffn + 7) / 8, slots_total), kGemvThreads, static_cast<size_t>(e->hidden) * sizeof(float) + 16, s, ea)) return rc;
-            if (int rc = launch(k_expert_down, dim3((e->hidden + kGemvRows - 1) / kGemvRows, slots_total), kGemvThreads, static_cast<size_t>(e->ffn) * sizeof(float) + 16, s, ea)) return rc;
+            if (int rc = launch(k_expert_gate_up, dim3((e->ffn + 7) / 8, slots_total), kGemvThreads,
+                                static_cast<size_t>(e->hidden) * sizeof(float) + 16, s, ea))
+                return rc;
+            if (int rc = launch(k_expert_down, dim3((e->hidden + kGemvRows - 1) / kGemvRows, slots_total), kGemvThreads,
+                                static_cast<size_t>(e->ffn) * sizeof(float) + 16, s, ea))
+                return rc;
             if (e->ranks > 1)
                 if (int rc = launch(k_moe_publish, 1, 32, 0, s, ea)) return rc;
-            if (int rc = launch(k_expert_combine, (e->hidden + 255) / 256, 256, 0, s, ea, ra.weights, shared_scale, loop_scale, e->x)) return rc;
+            if (int rc = launch(k_expert_combine, (e->hidden + 255) / 256, 256, 0, s, ea, ra.weights, shared_scale,
+                                loop_scale, e->x))
+                return rc;
             MR_CUDA_TRY(cudaGetLastError());
         }
     }

@@ -36,8 +36,8 @@ GPUS = _gpus()
 
 # 8 ranks over nano-1.7's 4 local KV heads: half the ranks hold no head of those layers;
 # heavy_small: Heavy Medium expert parallel (experts by id modulo ranks)
-@pytest.mark.parametrize("config,ranks", [("nano17", 2), ("lite", 2), ("heavy_small", 2), ("nano17", 4),
-                                          ("heavy_small", 4), ("nano17", 8)])
+@pytest.mark.parametrize("config,ranks", [("nano17", 2), ("lite", 2), ("lighting", 2), ("heavy_small", 2),
+                                          ("nano17", 4), ("heavy_small", 4), ("nano17", 8)])
 def test_tensor_parallel_decode_matches_single_gpu(tmp_path, config, ranks):
     if GPUS < ranks:
         pytest.skip(f"tensor-parallel decode over {ranks} GPUs needs {ranks} GPUs")
