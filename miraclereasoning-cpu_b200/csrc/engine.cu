@@ -139,6 +139,11 @@ struct mr_model {
     Phase *d_phases = nullptr;
     std::vector<Phase> phases;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    // page-locked host staging of a decode call: its token ids in, then the
+    // device error word and the logits out, all queued before one synchronise
+    int *h_ids = nullptr, *h_error = nullptr;
+    float *h_logits = nullptr;
+    static constexpr int kHostIds = 256;
     // tensor parallel: this rank of `ranks`; every exchange buffer lives in one arena
     // whose IPC handle the other ranks open (peer[j] = rank j's arena, mapped here)
     int rank = 0, ranks = 1;
@@ -694,17 +699,20 @@ int build_groups(mr_model *m) {
     return MR_OK;
 }
 
+// The device step's error word -> a status (and the latched failure).
+int error_status(mr_model *m, int error, const char *what) {
+    if (!error) return MR_OK;
+    m->failed = true;
+    if (error == 3) return set_error(MR_ERR_STATE, "%s: context_length exceeded on the device", what);
+    if (error == 4) return set_error(MR_ERR_STATE, "%s: a token outside the vocabulary reached the device", what);
+    return set_error(MR_ERR_TIMEOUT, "%s: device wait timed out (code %d); call reset()", what, error);
+}
+
 int sync_and_check(mr_model *m, const char *what) {
     MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
     int error = 0;
     MR_CUDA_TRY(cudaMemcpy(&error, &m->state->error, sizeof(int), cudaMemcpyDeviceToHost));
-    if (error) {
-        m->failed = true;
-        if (error == 3) return set_error(MR_ERR_STATE, "%s: context_length exceeded on the device", what);
-        if (error == 4) return set_error(MR_ERR_STATE, "%s: a token outside the vocabulary reached the device", what);
-        return set_error(MR_ERR_TIMEOUT, "%s: device wait timed out (code %d); call reset()", what, error);
-    }
-    return MR_OK;
+    return error_status(m, error, what);
 }
 
 int ensure_feed(mr_model *m, int n) {
@@ -955,6 +963,31 @@ int run_feed_batched(mr_model *m, int n, int return_all, float *out) {
     return MR_OK;
 }
 
+// Decode calls (a few tokens, last logits only) through page-locked staging:
+// ids in, n launches, then the error word and the logits out, one synchronise.
+int run_feed_staged(mr_model *m, const int *ids, int n, float *out) {
+    cudaStream_t st = m->ctx->stream;
+    const int V = m->cfg.vocab_size;
+    memcpy(m->h_ids, ids, sizeof(int) * n);
+    MR_CUDA_TRY(cudaMemcpyAsync(m->feed, m->h_ids, sizeof(int) * n, cudaMemcpyHostToDevice, st));
+    StepControl ctl = base_control(m);
+    ctl.feed_len = n;
+    for (int i = 0; i < n; ++i) {
+        const int rc = launch_step(m, ctl);
+        if (rc) {
+            m->failed = true;
+            return rc;
+        }
+    }
+    MR_CUDA_TRY(cudaMemcpyAsync(m->h_error, &m->state->error, sizeof(int), cudaMemcpyDeviceToHost, st));
+    if (out) MR_CUDA_TRY(cudaMemcpyAsync(m->h_logits, m->logits, sizeof(float) * V, cudaMemcpyDeviceToHost, st));
+    MR_CUDA_TRY(cudaStreamSynchronize(st));
+    if (const int rc = error_status(m, *m->h_error, "decode")) return rc;
+    if (out) memcpy(out, m->h_logits, sizeof(float) * V);
+    m->position += n;
+    return MR_OK;
+}
+
 int run_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
     const int V = m->cfg.vocab_size;
     for (int i = 0; i < n; ++i) MR_REQUIRE(ids[i] >= 0 && ids[i] < V, "input token is outside the vocabulary");
@@ -962,6 +995,8 @@ int run_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
                "input would exceed context_length; reset or allocate a larger context");
     int rc = ensure_feed(m, n);
     if (rc) return rc;
+    if (!return_all && n <= mr_model::kHostIds && m->h_ids && !(m->prefill_ok && m->prefill_on && n > 1))
+        return run_feed_staged(m, ids, n, out);
     MR_CUDA_TRY(cudaMemcpyAsync(m->feed, ids, sizeof(int) * n, cudaMemcpyHostToDevice, m->ctx->stream));
     if (m->prefill_ok && m->prefill_on && n > 1) return run_feed_batched(m, n, return_all, out);
     StepControl ctl = base_control(m);
@@ -1056,6 +1091,8 @@ int mr_model_destroy(mr_model *m) {
     prefill_release(m->pw);
     heavy_destroy(m->heavy);
     if (m->ev0) cudaEventDestroy(m->ev0);
+    if (m->h_ids) cudaFreeHost(m->h_ids);
+    if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->ev1) cudaEventDestroy(m->ev1);
     mr_context *ctx = m->ctx;
     delete m;
@@ -1231,6 +1268,11 @@ int mr_model_finalize(mr_model *m) {
     MR_REQUIRE(per_sm >= 1, "decode kernel cannot be resident (occupancy 0)");
     MR_CUDA_TRY(cudaEventCreate(&m->ev0));
     MR_CUDA_TRY(cudaEventCreate(&m->ev1));
+    MR_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void **>(&m->h_ids), sizeof(int) * (mr_model::kHostIds + 32),
+                              cudaHostAllocDefault));
+    m->h_error = m->h_ids + mr_model::kHostIds;
+    MR_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void **>(&m->h_logits), sizeof(float) * c.vocab_size,
+                              cudaHostAllocDefault));
     setup_prefill(m);
     m->finalized = true;
     return mr_model_reset(m);
