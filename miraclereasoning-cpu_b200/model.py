@@ -374,6 +374,19 @@ class MiracleModel:
 
     def decode(self, token_id):
         """Append one token to the current sequence and return next-token logits."""
+        V = self.config.vocab_size
+        if (type(token_id) is int and 0 <= token_id < V and self._stepper is None and not self.record_decisions
+                and not self._failed and self.position < self.context_length):
+            # the common case, without building and checking an id array (prefill's checks
+            # would all pass): one token straight to the C entry point
+            out = np.empty(V, dtype=np.float32)
+            try:
+                _native.call("mr_model_prefill", self._handle, C.byref(C.c_int(token_id)), 1, 0,
+                             out.ctypes.data_as(_F32))
+            except Exception:
+                self._failed = True
+                raise
+            return out
         return self.prefill([token_id])
 
     def generate(self, input_ids, *, max_new_tokens=32, temperature=0.0, top_k=0, top_p=1.0, seed=17,
