@@ -6,13 +6,13 @@
  * call returns MR_OK (0) or an MR_ERR_* code; mr_last_error() then returns a
  * thread-local message.  The Python side (ctypes) raises CUDAError, the
  * counterpart of the reference's OpenCLError (miracle_reasoning/opencl.py:
- * 14-20).  A context (one device, one stream) and everything created from it
+ * 14-21).  A context (one device, one stream) and everything created from it
  * is used by one host thread at a time, as the reference backend requires
- * (opencl.py:277-282).
+ * (opencl.py:129-133).
  *
  * Two layers:
  *   1. Buffer and kernel entry points with the reference backend's semantics
- *      (opencl.py:326-451, kernels.cl): float32 buffers addressed in ELEMENTS,
+ *      (opencl.py:178-303, kernels.cl): float32 buffers addressed in ELEMENTS,
  *      bounds-checked copies, and one entry point per reference kernel taking
  *      that kernel's NDRange extents and arguments.  These let the reference's
  *      op-level call sites run unchanged on the GPU.
@@ -70,7 +70,7 @@ typedef struct mr_model mr_model;
 MR_API const char *mr_last_error(void);
 MR_API int mr_abi_version(void);
 
-/* Replaces Device / list_devices (opencl.py:68-115). */
+/* Replaces Device / list_devices (opencl.py:69-115). */
 typedef struct {
     int ordinal;
     int sm_count;
@@ -83,16 +83,16 @@ typedef struct {
 MR_API int mr_device_count(int *count);
 MR_API int mr_device_query(int ordinal, mr_device_info *info);
 
-/* ---- context: one device + one stream (OpenCLBackend.__init__, opencl.py:284-314) */
+/* ---- context: one device + one stream (OpenCLBackend.__init__, opencl.py:136-166) */
 MR_API int mr_context_create(int device_ordinal, mr_context **out);
 /* Releases the caller's reference.  Buffers and models made on the context
  * hold their own references, so handles may be released in any order; the
  * stream is destroyed with the last one. */
 MR_API int mr_context_destroy(mr_context *ctx);
-/* OpenCLBackend.finish (opencl.py:450-451) */
+/* OpenCLBackend.finish (opencl.py:302-303) */
 MR_API int mr_context_finish(mr_context *ctx);
 
-/* ---- float32 buffers (opencl.py:326-365) --------------------------------
+/* ---- float32 buffers (opencl.py:178-217) --------------------------------
  * Sizes, offsets and counts are in float32 ELEMENTS.  Upload and download are
  * blocking, like the reference's blocking clEnqueueWrite/ReadBuffer. */
 MR_API int mr_buffer_alloc(mr_context *ctx, size_t count, mr_buffer **out);          /* empty()  */
@@ -100,13 +100,13 @@ MR_API int mr_buffer_free(mr_buffer *buf);                                      
 MR_API int mr_buffer_count(const mr_buffer *buf, size_t *count);
 MR_API int mr_buffer_upload(mr_buffer *buf, size_t offset, const float *host, size_t count);   /* upload() */
 MR_API int mr_buffer_download(const mr_buffer *buf, size_t offset, float *host, size_t count); /* read() */
-/* copy() (opencl.py:357-365): bounds-checked; count 0 is a no-op. */
+/* copy() (opencl.py:209-217): bounds-checked; count 0 is a no-op. */
 MR_API int mr_buffer_copy(const mr_buffer *src, mr_buffer *dst, size_t src_offset, size_t dst_offset,
                           size_t count);
 
 /* ---- kernels: one entry per kernels.cl kernel ----------------------------
  * g0/g1 are the NDRange extents the reference passes to run() (opencl.py:
- * 367-387); the remaining arguments are the kernel's, in the kernel's order.
+ * 219-239); the remaining arguments are the kernel's, in the kernel's order.
  * Every buffer extent the kernel can touch is checked against its buffer
  * before launch (MR_ERR_ARGUMENT).  All compute in float32 on the device. */
 MR_API int mr_op_linear(mr_context *ctx, size_t g0, size_t g1, const mr_buffer *x, const mr_buffer *w,
@@ -282,7 +282,14 @@ MR_API int mr_model_tensor_download(mr_model *model, const char *name, float *ho
  * input normalised, weights consumed; attention: first tile and q/k/v
  * loaded, q/k prepared, scores/mix done; slot 3: phase done.  A CTA with no
  * work in a phase leaves slots 0-2 zero.
- * *phases receives the number of executed phases, *grid the CTA count.  No
+ * *phases receives the number of executed phases, *grid the CTA count.
+ * heavy-medium-2.0 (a sequence of kernel launches, not one persistent
+ * kernel): stamps[0] = the step's start, stamps[k] = the time the step's k-th
+ * kernel had completed, *phases = the number of kernels, *grid = 0; when
+ * capacity leaves room, the last 8 * P stamps hold 8 probes for each of the P
+ * = 6 * layers * inner loops + 1 projection / attention / router launches
+ * (first CTA start, first CTA past its dependency wait, last CTA done staging,
+ * last CTA done with its main loop, last CTA exit; 3 unused).  No
  * reference counterpart (the reference has no tracing). */
 MR_API int mr_model_trace_decode(mr_model *model, int token, uint64_t *stamps, int capacity, int *phases,
                                  int *grid);
@@ -291,12 +298,16 @@ MR_API int mr_model_trace_decode(mr_model *model, int token, uint64_t *stamps, i
  * reference: it exists for callers that cannot call cudaMalloc while they run
  * (a framework that owns all device memory through its own pool, or code in a
  * section where an allocation could synchronise the device or fail).  Same
- * result as CUDABackend.attention / mr_op_scores + mr_op_softmax + mr_op_mix
- * (opencl.py:432-448), but the [heads x (length + extra_length)] score matrix
+ * result, bit for bit, as CUDABackend.attention / mr_op_scores + mr_op_softmax
+ * + mr_op_mix (the same per-score dot products, the softmax denominator summed
+ * in row order, the value mix in row order), but the [heads x (length +
+ * extra_length)] score matrix
  * lives in a 4 MiB file-scope device array that every GPU loading this library
  * keeps until the process exits.  All pointers are device pointers the caller
  * owns; keys/values are ring buffers [capacity, kv_heads*dim] read in logical
- * order [start, start+length), then extra rows [extra_length, kv_heads*dim].
+ * order [start, start+length) (64-bit row arithmetic: any start >= 0 is
+ * valid), then extra rows [extra_length, kv_heads*dim]; with length 0 the
+ * ring pointers may be NULL and capacity 0.
  * heads * (length + extra_length) above 1048576 fails with MR_ERR_ARGUMENT.
  * The first call on a device looks up the array's address (do it before any
  * stream capture); every call shares the array, so calls that overlap on the

@@ -1,6 +1,6 @@
 """``CUDABackend``: the reference backend's method surface on a B200.
 
-Drop-in for ``OpenCLBackend`` (miracle_reasoning/opencl.py:277-451): the same
+Drop-in for ``OpenCLBackend`` (miracle_reasoning/opencl.py:129-303): the same
 ``empty/upload/read/copy/run/linear/norm/rotate/add/swiglu/softmax/attention/
 mix/finish`` methods with the same argument meaning, shapes and error
 behaviour, and a ``device`` with ``max_allocation_bytes`` and ``to_dict()``.
@@ -95,7 +95,7 @@ class CUDABackend:
             _native._lib.mr_context_destroy(ctx)
             self.context = None
 
-    # buffers (opencl.py:326-365) -------------------------------------------------
+    # buffers (opencl.py:178-217) -------------------------------------------------
     def empty(self, shape):
         shape = tuple(shape)
         if not shape or any(not isinstance(n, int) or n <= 0 for n in shape):
@@ -133,7 +133,7 @@ class CUDABackend:
         if count:
             call("mr_buffer_copy", source.handle, target.handle, source_offset, target_offset, count)
 
-    # dispatch (opencl.py:367-387) -------------------------------------------------
+    # dispatch (opencl.py:219-239) -------------------------------------------------
     def run(self, name, shape, *args):
         if name not in _KERNELS:
             raise CUDAError(f"create kernel {name} failed (no such kernel)")
@@ -161,7 +161,7 @@ class CUDABackend:
             values.append(value)
         call(f"mr_op_{name}", self.context, *shape, *values)
 
-    # op helpers, same launch geometry as opencl.py:389-448 ------------------------
+    # op helpers, same launch geometry as opencl.py:241-300 ------------------------
     def linear(self, x, weight):
         if len(x.shape) != 2 or len(weight.shape) != 2 or x.shape[1] != weight.shape[1]:
             raise ValueError("linear needs x[rows,in] and weight[out,in]")

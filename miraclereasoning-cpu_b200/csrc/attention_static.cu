@@ -51,26 +51,28 @@ int scratch_address(int device, float **out) {
     return MR_OK;
 }
 
-__device__ float block_reduce(float v, bool take_max, float *shared) {
-    for (int offset = 16; offset > 0; offset >>= 1) {
-        const float other = __shfl_xor_sync(0xffffffffu, v, offset);
-        v = take_max ? fmaxf(v, other) : v + other;
-    }
+__device__ float block_max(float v, float *shared) {
+    for (int offset = 16; offset > 0; offset >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, offset));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) shared[warp] = v;
     __syncthreads();
     if (warp == 0) {
-        v = lane < (blockDim.x >> 5) ? shared[lane] : (take_max ? -INFINITY : 0.f);
-        for (int offset = 16; offset > 0; offset >>= 1) {
-            const float other = __shfl_xor_sync(0xffffffffu, v, offset);
-            v = take_max ? fmaxf(v, other) : v + other;
-        }
+        v = lane < static_cast<int>(blockDim.x >> 5) ? shared[lane] : -INFINITY;
+        for (int offset = 16; offset > 0; offset >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, offset));
         if (lane == 0) shared[0] = v;
     }
     __syncthreads();
     v = shared[0];
     __syncthreads();
     return v;
+}
+
+// Row of logical key t: ring rows (start + t) mod capacity for t < length (in
+// 64-bit arithmetic, so a start near INT_MAX cannot wrap), then extra rows.
+// capacity is only used for ring rows, so length 0 with capacity 0 is valid.
+__device__ __forceinline__ size_t logical_row(int t, int start, int length, int capacity) {
+    return t < length ? (static_cast<size_t>(start) + static_cast<size_t>(t)) % static_cast<size_t>(capacity)
+                      : static_cast<size_t>(t - length);
 }
 
 // One block per query head; scores of head h live in scores[h * total ...].
@@ -82,25 +84,34 @@ __global__ void k_attention_static(const float *q, const float *keys, const floa
     float *s = scores + static_cast<size_t>(h) * total;
     const float sqrt_dim = __fsqrt_rn(static_cast<float>(dim));
     for (int t = threadIdx.x; t < total; t += blockDim.x) {
-        const size_t row = t < length ? static_cast<size_t>((start + t) % capacity) : static_cast<size_t>(t - length);
+        const size_t row = logical_row(t, start, length, capacity);
         const float *k = (t < length ? keys : extra_keys) + (row * kv_heads + kh) * dim;
         float dot = 0.f;
         for (int j = 0; j < dim; ++j) dot = __fadd_rn(dot, __fmul_rn(q[h * dim + j], k[j]));
         s[t] = __fdiv_rn(dot, sqrt_dim);
     }
     __syncthreads();
+    // softmax (kernels.cl:75-84): the maximum in any order (fmax is exact), the
+    // exponentials in parallel, their sum by one thread in row order, as the
+    // reference's work item sums it
     float m = -INFINITY;
     for (int t = threadIdx.x; t < total; t += blockDim.x) m = fmaxf(m, s[t]);
-    m = block_reduce(m, true, shared);
-    float denom = 0.f;
-    for (int t = threadIdx.x; t < total; t += blockDim.x) denom += expf(s[t] - m);
-    denom = block_reduce(denom, false, shared);
-    for (int t = threadIdx.x; t < total; t += blockDim.x) s[t] = __fdiv_rn(expf(s[t] - m), denom);
+    m = block_max(m, shared);
+    for (int t = threadIdx.x; t < total; t += blockDim.x) s[t] = expf(__fsub_rn(s[t], m));
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float denom = 0.f;
+        for (int t = 0; t < total; ++t) denom = __fadd_rn(denom, s[t]);
+        shared[0] = denom;
+    }
+    __syncthreads();
+    const float denom = shared[0];
+    for (int t = threadIdx.x; t < total; t += blockDim.x) s[t] = __fdiv_rn(s[t], denom);
     __syncthreads();
     for (int j = threadIdx.x; j < dim; j += blockDim.x) {
         float acc = 0.f;
         for (int t = 0; t < total; ++t) {
-            const size_t row = t < length ? static_cast<size_t>((start + t) % capacity) : static_cast<size_t>(t - length);
+            const size_t row = logical_row(t, start, length, capacity);
             const float *v = (t < length ? values : extra_values) + (row * kv_heads + kh) * dim;
             acc = __fadd_rn(acc, __fmul_rn(s[t], v[j]));
         }

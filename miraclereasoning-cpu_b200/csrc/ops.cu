@@ -1,6 +1,6 @@
 // One CUDA kernel per reference kernel (miracle_reasoning/kernels.cl), behind
 // the mr_op_* entry points.  They serve the reference backend's op surface
-// (opencl.py:367-448), so the reference's own call sites and kernel tests run
+// (opencl.py:219-300), so the reference's own call sites and kernel tests run
 // on the GPU unchanged; the decode hot path uses the fused engine instead.
 //
 // Arithmetic follows kernels.cl work item by work item: the same reduction
@@ -12,6 +12,7 @@
 // Every entry point checks each buffer extent the kernel can touch before it
 // launches, so a bad argument is an MR_ERR_ARGUMENT, never a device fault.
 #include <algorithm>
+#include <climits>
 
 #include "common.cuh"
 
@@ -225,6 +226,8 @@ int check_attention_geometry(Check &ck, int heads, int kv_heads, int dim, int ca
                              int extra_length) {
     ck.nonneg(heads, "heads") && ck.nonneg(dim, "dim") && ck.nonneg(length, "length") &&
         ck.nonneg(extra_length, "extra_length") && ck.nonneg(start, "start");
+    if (!ck.rc && static_cast<long long>(length) + extra_length > INT_MAX)
+        ck.rc = mr::set_error(MR_ERR_ARGUMENT, "length + extra_length exceeds the int range");
     if (!ck.rc && (kv_heads <= 0 || heads < kv_heads))
         ck.rc = mr::set_error(MR_ERR_ARGUMENT, "kv_heads must be in [1, heads]");
     if (!ck.rc && length > 0 && capacity <= 0) ck.rc = mr::set_error(MR_ERR_ARGUMENT, "capacity must be positive");
@@ -311,7 +314,9 @@ int mr_op_scores(mr_context *ctx, size_t g0, size_t g1, const mr_buffer *q, cons
     size_t t = lo(g0, total), h = lo(g1, heads);
     if (t && h) {
         size_t row = (size_t)kv_heads * dim;
-        size_t ring_rows = start + length > capacity ? (size_t)capacity : (size_t)(start + length);
+        // rows [start, start + length) mod capacity: 64-bit, so a start near INT_MAX cannot wrap
+        const long long ring_end = static_cast<long long>(start) + length;
+        size_t ring_rows = ring_end > capacity ? (size_t)capacity : (size_t)ring_end;
         ck.buf(q, h * dim, "q") && ck.buf(s, (h - 1) * (size_t)total + t, "scores") &&
             (length == 0 || ck.buf(k, ring_rows * row, "keys")) &&
             (t <= (size_t)length || ck.buf(extra_k, (t - length) * row, "extra keys"));
@@ -357,7 +362,9 @@ int mr_op_mix(mr_context *ctx, size_t g0, const mr_buffer *p, const mr_buffer *v
     if (items) {
         size_t row = (size_t)kv_heads * dim, total = length + extra_length;
         size_t used_heads = (items + dim - 1) / dim;
-        size_t ring_rows = start + length > capacity ? (size_t)capacity : (size_t)(start + length);
+        // rows [start, start + length) mod capacity: 64-bit, so a start near INT_MAX cannot wrap
+        const long long ring_end = static_cast<long long>(start) + length;
+        size_t ring_rows = ring_end > capacity ? (size_t)capacity : (size_t)ring_end;
         ck.buf(p, used_heads * total, "probabilities") && ck.buf(y, items, "y") &&
             (length == 0 || ck.buf(v, ring_rows * row, "values")) &&
             (extra_length == 0 || ck.buf(extra_v, (size_t)extra_length * row, "extra values"));

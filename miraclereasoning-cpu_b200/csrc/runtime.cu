@@ -1,7 +1,7 @@
 // Errors, devices, contexts and float32 buffers of libmiracle_cuda.so.
 //
 // Buffers replace the reference's clCreateBuffer-per-op tensors
-// (miracle_reasoning/opencl.py:326-365): sizes/offsets in float elements,
+// (miracle_reasoning/opencl.py:178-217): sizes/offsets in float elements,
 // blocking upload/download, bounds-checked device-to-device copies.
 #include <cstdarg>
 #include <cstdio>

@@ -9,7 +9,9 @@
 Both are compiled with ``-ffp-contract=off`` (the reference kernels declare
 ``FP_CONTRACT OFF``) and OpenMP for the independent work items.
 
-Usage: ``python oracle/build.py [--reference-root DIR]``.
+Usage: ``python oracle/build.py [--reference-root DIR]``; without the
+argument the checkout is taken from the ``MIRACLE_REFERENCE_ROOT``
+environment variable, and without either only the C restatement is built.
 """
 from __future__ import annotations
 
@@ -22,7 +24,6 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "liboracle_kernels.so"
 REF_LIB = HERE / "_ref" / "libref_kernels.so"
-DEFAULT_REFERENCE = Path("/root/reference")
 _FLAGS = ["-O2", "-ffp-contract=off", "-fno-fast-math", "-fopenmp", "-shared", "-fPIC"]
 
 
@@ -41,9 +42,9 @@ def build_oracle(force: bool = False) -> Path:
 
 
 def build_reference(reference_root: Path | None = None, force: bool = False) -> Path | None:
-    root = Path(reference_root or os.environ.get("MIRACLE_REFERENCE_ROOT", DEFAULT_REFERENCE))
-    kernels = root / "miracle_reasoning" / "kernels.cl"
-    if not kernels.is_file():
+    root = reference_root or os.environ.get("MIRACLE_REFERENCE_ROOT")
+    kernels = Path(root) / "miracle_reasoning" / "kernels.cl" if root else None
+    if kernels is None or not kernels.is_file():
         return REF_LIB if REF_LIB.exists() else None
     shim = HERE / "ref_host.cpp"
     if force or _stale(REF_LIB, shim, kernels):
