@@ -501,12 +501,20 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_bf16x3(GemmArgs args) {
 // halves the re-reads of the X planes):
 // warp 0 lane 0 streams K tiles of 64 (three X planes + the W tile, 56 or 64 KB
 // a stage, 128-byte swizzle) by TMA into a 3- or 4-stage ring; warp 1 lane 0 issues
-// tcgen05.mma (M 128, N BN, K 16, BF16 -> FP32) into two TMEM accumulators
-// (the leading part, and the two small parts: summed apart as in
-// k_gemm_bf16x3) and hands each stage back with tcgen05.commit; warps 2-5
-// read the accumulators (tcgen05.ld, one TMEM lane = one token row per
-// thread) and apply the epilogue.  Every wait is bounded (kTcWaitNs): a wait
-// that gives up sets *err and the CTA winds down.
+// tcgen05.mma (M 128, N BN, K 16, BF16 -> FP32) into TMEM accumulators (the
+// leading part, and the two small parts: summed apart as in k_gemm_bf16x3)
+// and hands each stage back with tcgen05.commit; warps 2-5 read the
+// accumulators (tcgen05.ld, one TMEM lane = one token row per thread) and
+// apply the epilogue.  Every wait is bounded (kTcWaitNs): a wait that gives up
+// sets *err and the CTA winds down.
+//
+// The tensor core adds each K16 step's products into its FP32 accumulator
+// with one rounding of its own, so over a long K the leading part's error
+// grows with K / 16 (measured: FlashLite logits 7.6e-5 from the exact values
+// against the reference's own 2.0e-5).  The leading part is therefore summed
+// per chunk of kLeadChunk K tiles in one of two TMEM accumulators, and the
+// epilogue warps add each finished chunk into FP32 registers (round to
+// nearest) while the MMAs fill the other accumulator.
 constexpr int kTM = 128, kTK = 64, kTcThreads = 192;
 constexpr uint32_t kTileBytes = kTM * kTK * 2;  // 16 KB: one 128 x 64 BF16 X tile
 template <int BN>
@@ -516,6 +524,7 @@ constexpr int tc_stages() { return BN == 64 ? 4 : 3; }  // as many 56 / 64 KB st
 template <int BN>
 constexpr size_t tc_smem() { return 1024 + tc_stages<BN>() * tc_stage_bytes<BN>() + 256; }  // slack, tiles, barriers
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
+constexpr int kLeadChunk = 4;  // K tiles (256 K) per leading-part accumulator chunk
 
 struct TcMaps {
     CUtensorMap a;     // X planes: {k, token, plane}
@@ -566,18 +575,33 @@ constexpr uint32_t tc_idesc() {
            (static_cast<uint32_t>(kTM >> 4) << 24);
 }
 
+// 32 consecutive TMEM columns of this thread's lane (32x32b shape), waited for.
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(addr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant__ TcMaps maps, GemmArgs args,
                                                            int *err) {
     constexpr uint32_t kTStageBytes = tc_stage_bytes<BN>();
     constexpr int kTStages = tc_stages<BN>();
     constexpr int kTN = BN;
-    constexpr uint32_t kTcols = 2 * BN;  // TMEM columns: the two accumulators
+    // TMEM columns: two leading-part accumulators (chunks alternate), then the small parts'
+    constexpr uint32_t kTcols = BN == 128 ? 512 : 256;
     extern __shared__ uint8_t tc_raw[];
     uint8_t *tiles = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(tiles + kTStages * kTStageBytes);
     uint64_t *empty = full + kTStages, *accf = empty + kTStages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accf + 1);
+    uint64_t *lead_full = accf + 1, *lead_empty = lead_full + 2;  // per leading accumulator
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lead_empty + 2);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     int si = 0;
     while (si + 1 < args.nseg && static_cast<int>(blockIdx.x) >= args.seg[si + 1].tiles) ++si;
@@ -590,9 +614,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&empty[st])) : "memory");
         }
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(accf)) : "memory");
+        for (int b = 0; b < 2; ++b) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&lead_full[b])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(saddr(&lead_empty[b])) : "memory");
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) {  // accumulator of the leading part (columns 0..BN-1) and of the small parts (BN..2BN-1)
+    if (warp == 1) {  // leading-part accumulators (columns 0..BN-1, BN..2BN-1), small parts (2BN..3BN-1)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
                      "n"(kTcols)
                      : "memory");
@@ -636,7 +664,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
         bool ok = true;
         for (int kt = 0; kt < ktiles && ok; ++kt) {
             const int st = kt % kTStages;
+            const int chunk = kt / kLeadChunk, buf = chunk & 1;
+            const bool chunk_start = kt % kLeadChunk == 0;
             ok = tc_wait(&full[st], (kt / kTStages) & 1, err);
+            // a leading accumulator is refilled once the epilogue has read its chunk before last
+            if (ok && chunk_start && chunk >= 2) ok = tc_wait(&lead_empty[buf], ((chunk / 2) - 1) & 1, err);
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t base = saddr(tiles + st * kTStageBytes);
@@ -646,8 +678,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
 #pragma unroll
                 for (int pl = 0; pl < 3; ++pl) {
                     const uint64_t ad = sw128_desc(base + pl * kTileBytes + ks * 32);
-                    const uint32_t d = pl == 0 ? tmem : tmem + kTN;
-                    const uint32_t accumulate = pl == 0 ? (kt > 0 || ks > 0) : !(kt == 0 && ks == 0 && pl == 1);
+                    const uint32_t d = pl == 0 ? tmem + buf * kTN : tmem + 2 * kTN;
+                    const uint32_t accumulate =
+                        pl == 0 ? !(chunk_start && ks == 0) : !(kt == 0 && ks == 0 && pl == 1);
                     asm volatile(
                         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d),
@@ -659,43 +692,53 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                              saddr(&empty[st]))
                          : "memory");
+            if (kt % kLeadChunk == kLeadChunk - 1 || kt == ktiles - 1)  // this chunk's leading sum is complete
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 saddr(&lead_full[buf]))
+                             : "memory");
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(accf))
                      : "memory");
     } else if (warp >= 2) {  // epilogue: thread = TMEM lane = token row of the tile
-        const bool ready = __all_sync(0xffffffffu, tc_wait(accf, 0, err));  // warp-uniform: tcgen05.ld is collective
-        if (ready && ktiles > 0) {
+        const int quarter = warp & 3, row = quarter * 32 + lane, m = m0 + row;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        const int chunks = (ktiles + kLeadChunk - 1) / kLeadChunk;
+        float lead[kTN];
+#pragma unroll
+        for (int j = 0; j < kTN; ++j) lead[j] = 0.f;
+        bool ok = true;
+        for (int chunk = 0; chunk < chunks && ok; ++chunk) {  // the leading part, chunk by chunk, in order
+            const int buf = chunk & 1;
+            ok = __all_sync(0xffffffffu, tc_wait(&lead_full[buf], (chunk / 2) & 1, err));  // tcgen05.ld is collective
+            if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const int quarter = warp & 3, row = quarter * 32 + lane, m = m0 + row;
-            const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll
             for (int c = 0; c < kTN; c += 32) {
-                uint32_t hi[32], lo[32];
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                    : "=r"(hi[0]), "=r"(hi[1]), "=r"(hi[2]), "=r"(hi[3]), "=r"(hi[4]), "=r"(hi[5]), "=r"(hi[6]),
-                      "=r"(hi[7]), "=r"(hi[8]), "=r"(hi[9]), "=r"(hi[10]), "=r"(hi[11]), "=r"(hi[12]), "=r"(hi[13]),
-                      "=r"(hi[14]), "=r"(hi[15]), "=r"(hi[16]), "=r"(hi[17]), "=r"(hi[18]), "=r"(hi[19]),
-                      "=r"(hi[20]), "=r"(hi[21]), "=r"(hi[22]), "=r"(hi[23]), "=r"(hi[24]), "=r"(hi[25]),
-                      "=r"(hi[26]), "=r"(hi[27]), "=r"(hi[28]), "=r"(hi[29]), "=r"(hi[30]), "=r"(hi[31])
-                    : "r"(lane_base + c));
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                    : "=r"(lo[0]), "=r"(lo[1]), "=r"(lo[2]), "=r"(lo[3]), "=r"(lo[4]), "=r"(lo[5]), "=r"(lo[6]),
-                      "=r"(lo[7]), "=r"(lo[8]), "=r"(lo[9]), "=r"(lo[10]), "=r"(lo[11]), "=r"(lo[12]), "=r"(lo[13]),
-                      "=r"(lo[14]), "=r"(lo[15]), "=r"(lo[16]), "=r"(lo[17]), "=r"(lo[18]), "=r"(lo[19]),
-                      "=r"(lo[20]), "=r"(lo[21]), "=r"(lo[22]), "=r"(lo[23]), "=r"(lo[24]), "=r"(lo[25]),
-                      "=r"(lo[26]), "=r"(lo[27]), "=r"(lo[28]), "=r"(lo[29]), "=r"(lo[30]), "=r"(lo[31])
-                    : "r"(lane_base + kTN + c));
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                uint32_t v[32];
+                tmem_ld32(lane_base + buf * kTN + c, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) lead[c + j] = chunk ? __fadd_rn(lead[c + j], __uint_as_float(v[j]))
+                                                                 : __uint_as_float(v[j]);
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(&lead_empty[buf])) : "memory");
+        }
+        // every MMA has completed (also after an error: TMEM is released only then)
+        const bool ready = __all_sync(0xffffffffu, tc_wait(accf, 0, err));
+        if (ok && ready && ktiles > 0) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+            for (int c = 0; c < kTN; c += 32) {
+                uint32_t v[32];
+                tmem_ld32(lane_base + 2 * kTN + c, v);
                 if (m < args.M) {
                     float *dst = args.y + static_cast<size_t>(m) * args.ldy + seg.col0 + n0 + c;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         if (n0 + c + j >= seg.n) break;
-                        const float v = __uint_as_float(hi[j]) + __uint_as_float(lo[j]);
-                        dst[j] = args.resid ? __fadd_rn(dst[j], __fmul_rn(args.scale, v)) : v;
+                        const float val = lead[c + j] + __uint_as_float(v[j]);
+                        dst[j] = args.resid ? __fadd_rn(dst[j], __fmul_rn(args.scale, val)) : val;
                     }
                 }
             }
