@@ -4,7 +4,7 @@
 // mr_model_step / prefill / generate.
 //
 // Replaces the reference's per-op Python dispatch (model.py:257-312), its
-// per-op clCreateBuffer/clEnqueueNDRangeKernel traffic (opencl.py:326-387)
+// per-op clCreateBuffer/clEnqueueNDRangeKernel traffic (opencl.py:178-239)
 // and its LRU weight cache (weights.py:258-297).
 #include <algorithm>
 #include <cmath>
@@ -833,12 +833,9 @@ int heavy_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
         m->failed = true;
         return cuda_error(err, "heavy-medium-2.0 token step");
     }
-    if (m->ranks > 1) {
-        const int rc = heavy_status(m->heavy);
-        if (rc) m->failed = true;
-        return rc;
-    }
-    return MR_OK;
+    const int rc = heavy_status(m->heavy);  // a bounded device wait that gave up
+    if (rc) m->failed = true;
+    return rc;
 }
 
 // Runs n fed tokens starting at the current position; logits of the selected
@@ -1336,6 +1333,10 @@ int mr_model_reset(mr_model *m) {
     if (!m->finalized) return set_error(MR_ERR_STATE, "model is not finalized");
     MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
     if (!m->op_path && !m->heavy) MR_CUDA_TRY(cudaMemset(m->state, 0, sizeof(StepState)));
+    if (m->heavy) {
+        const int rc = heavy_reset(m->heavy);
+        if (rc) return rc;
+    }
     m->position = 0;
     m->failed = false;
     return MR_OK;
@@ -1505,6 +1506,19 @@ int mr_model_trace_decode(mr_model *m, int token, uint64_t *stamps, int capacity
     MR_REQUIRE(stamps && phases && grid, "NULL argument");
     MR_REQUIRE(token >= 0 && token < m->cfg.vocab_size, "token outside the vocabulary");
     MR_REQUIRE(m->position + 1 <= m->cfg.context_length, "context_length exceeded");
+    if (m->heavy) {  // kernel-boundary stamps of the device token step
+        int count = 0;
+        rc = heavy_trace_token(m->heavy, token, m->position, reinterpret_cast<unsigned long long *>(stamps),
+                               capacity, &count);
+        if (rc) {
+            m->failed = true;
+            return rc;
+        }
+        m->position += 1;
+        *phases = count - 1;
+        *grid = 0;
+        return MR_OK;
+    }
     const int executed = (int)m->phases.size() - 1;  // every phase but the step end
     const size_t need = 1 + (size_t)executed * ((size_t)m->grid * kTraceStamps + 1);
     MR_REQUIRE((size_t)capacity >= need, "trace needs %zu stamps", need);
@@ -1544,7 +1558,7 @@ int mr_model_bench_decode(mr_model *m, int first_token, int steps, float *device
         rc = heavy_greedy_chain(m->heavy, first_token, m->position, steps);
         if (!rc) MR_CUDA_TRY(cudaEventRecord(m->ev1, m->ctx->stream));
         const cudaError_t err = cudaStreamSynchronize(m->ctx->stream);
-        if (!rc && err == cudaSuccess && m->ranks > 1) rc = heavy_status(m->heavy);
+        if (!rc && err == cudaSuccess) rc = heavy_status(m->heavy);
         if (rc || err != cudaSuccess) {
             m->failed = true;
             return rc ? rc : cuda_error(err, "heavy-medium-2.0 decode");

@@ -54,7 +54,8 @@ constexpr int kGemvThreads = 256;  // 8 warps
 constexpr int kGemvRows = 8;       // rows per block (one per warp)
 constexpr int kMaxSegs = 4;
 constexpr int kMaxHeavyRanks = 8;
-constexpr uint64_t kHeavyWaitNs = 2000000000ull;  // 2 s: a rank that never publishes is an error, not a hang
+constexpr uint64_t kHeavyWaitNs = 2000000000ull;
+constexpr int kStreamSmem = 227 * 1024;  // dynamic shared memory of a streaming CTA (the ring takes what is left)  // 2 s: a rank that never publishes is an error, not a hang
 
 __device__ __forceinline__ uint64_t global_time_ns() {
     uint64_t t;
@@ -234,6 +235,21 @@ __device__ void stage_input(const float *x, int n, bool norm, const void *gain, 
     __syncthreads();
 }
 
+// Tracing probes of one launch (NULL when not tracing): [0] first CTA start,
+// [1] first CTA past the dependency wait, [2] last CTA done staging its
+// input, [3] last CTA done with its main loop, [4] last CTA exit.
+enum ProbePoint {
+    kProbeStart = 0, kProbeWaited = 1, kProbeStaged = 2, kProbeMain = 3, kProbeExit = 4,
+    kProbeX5 = 5, kProbeX6 = 6, kProbeX7 = 7,  // kernel-specific, latest over CTAs
+    kProbeSlots = 8
+};
+__device__ __forceinline__ void probe(unsigned long long *p, int point) {
+    if (!p) return;
+    const unsigned long long t = global_time_ns();
+    if (point <= kProbeWaited) atomicMin(p + point, t);
+    else atomicMax(p + point, t);
+}
+
 struct GemvSeg {
     const void *w;
     int dtype, rows, cols;
@@ -319,184 +335,13 @@ __global__ void k_argmax(const float *v, int n, int *token) {
     }
 }
 
-// One warp per head: q heads (blocks 0 .. H-1) and key heads (H .. H+KVH-1):
-// non-affine RMSNorm (eps 1e-6, model.py:194, 201) then RoPE at `position`
-// (kernels.cl:30-44); keys and values go to ring row `row`.
-__global__ void k_heads_norm_rope(float *q, const float *kv, float *k_ring, float *v_ring, const float *inv_freq,
-                                  int heads, int kv_heads, int dim, int split_half, int position, int row) {
+// Tracing: records %globaltimer once the kernel before it has completed
+// (after griddepcontrol.wait, so its writes are visible), i.e. the step's
+// kernel-boundary times as the pipelined launches actually run.
+__global__ void k_stamp(unsigned long long *slot) {
     pdl_trigger();
     pdl_wait();
-    const int h = blockIdx.x, lane = threadIdx.x;
-    const int width = kv_heads * dim;
-    float *dst;
-    const float *src;
-    if (h < heads) {
-        src = q + static_cast<size_t>(h) * dim;
-        dst = q + static_cast<size_t>(h) * dim;
-    } else {
-        const int kh = h - heads;
-        src = kv + static_cast<size_t>(kh) * dim;
-        dst = k_ring + static_cast<size_t>(row) * width + static_cast<size_t>(kh) * dim;
-#pragma unroll 4
-        for (int j = lane; j < dim; j += 32)
-            v_ring[static_cast<size_t>(row) * width + static_cast<size_t>(kh) * dim + j] = kv[width + kh * dim + j];
-    }
-    float ss = 0.f;
-#pragma unroll 4
-    for (int j = lane; j < dim; j += 32) ss = fmaf(src[j], src[j], ss);
-    ss = warp_sum(ss);
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(FADD(__fdiv_rn(ss, static_cast<float>(dim)), 1e-6f)));
-    const int half = dim / 2;
-    float u[4], v[4];
-    int n = 0;
-    for (int p = lane; p < half && n < 4; p += 32, ++n) {
-        const int j = split_half ? p : 2 * p, k = split_half ? p + half : 2 * p + 1;
-        u[n] = FMUL(src[j], scale);
-        v[n] = FMUL(src[k], scale);
-    }
-    __syncwarp();
-    n = 0;
-    for (int p = lane; p < half && n < 4; p += 32, ++n) {
-        const int j = split_half ? p : 2 * p, k = split_half ? p + half : 2 * p + 1;
-        const float angle = FMUL(static_cast<float>(position), inv_freq[p]);
-        const float c = cosf(angle), s = sinf(angle);
-        dst[j] = __fsub_rn(FMUL(u[n], c), FMUL(v[n], s));
-        dst[k] = FADD(FMUL(u[n], s), FMUL(v[n], c));
-    }
-}
-
-// Mean of the newest block's rows (kernels.cl:139-148: running sum in row
-// order, then one division) for keys and values; full blocks never change.
-__global__ void k_block_mean_last(const float *k_ring, const float *v_ring, float *k_mean, float *v_mean, int count,
-                                  int width, int block) {
-    pdl_trigger();
-    pdl_wait();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= 2 * width) return;
-    const int j = i % width;
-    const float *src = i < width ? k_ring : v_ring;
-    float *dst = i < width ? k_mean : v_mean;
-    const int b = (count - 1) / block, start = b * block, stop = min(start + block, count);
-    float v = 0.f;
-#pragma unroll 8
-    for (int t = start; t < stop; ++t) v = FADD(v, src[static_cast<size_t>(t) * width + j]);
-    dst[static_cast<size_t>(b) * width + j] = __fdiv_rn(v, static_cast<float>(stop - start));
-}
-
-// scores[h][t], t < length: local ring rows start .. start+length-1; t >= length:
-// block means (kernels.cl:59-74).  One warp per score.
-__global__ void k_sparse_scores(const float *q, const float *k_ring, const float *k_mean, float *scores, int heads,
-                                int kv_heads, int dim, int start, int length, int blocks) {
-    pdl_trigger();
-    pdl_wait();
-    const int total = length + blocks;
-    const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (item >= heads * total) return;
-    const int h = item / total, t = item - h * total;
-    const int kh = h / (heads / kv_heads), width = kv_heads * dim;
-    const float *kr = t < length ? k_ring + static_cast<size_t>(start + t) * width + static_cast<size_t>(kh) * dim
-                                 : k_mean + static_cast<size_t>(t - length) * width + static_cast<size_t>(kh) * dim;
-    const float *qh = q + static_cast<size_t>(h) * dim;
-    float v = 0.f;
-#pragma unroll 4
-    for (int j = lane; j < dim; j += 32) v = fmaf(qh[j], kr[j], v);
-    v = warp_sum(v);
-    if (lane == 0) scores[static_cast<size_t>(h) * total + t] = __fdiv_rn(v, __fsqrt_rn(static_cast<float>(dim)));
-}
-
-// model.py:219-225 per head (one block): block column b loses
-// slope * log1p(position - end_b) (end_b = min((b + 1) * block - 1, position),
-// the log1p value from the host's table), the `slots` best columns (stable
-// descending order: ties go to the lower index) stay, the rest become -inf.
-// The kept block ids go to `kept` in ascending order, -1 padded to `slots_max`.
-__global__ void k_block_topk(float *scores, int total, int length, int blocks, int block, int position,
-                             const float *log1p_table, float slope, int slots, int slots_max, int *kept) {
-    pdl_trigger();
-    pdl_wait();
-    extern __shared__ float sb[];
-    int *keep = reinterpret_cast<int *>(sb + blocks);
-    const int h = blockIdx.x;
-    float *row = scores + static_cast<size_t>(h) * total + length;
-    for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
-        const int end = min((b + 1) * block - 1, position);
-        sb[b] = __fsub_rn(row[b], FMUL(slope, log1p_table[position - end]));
-    }
-    __syncthreads();
-    for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
-        const float v = sb[b];
-        int rank = 0;
-        for (int j = 0; j < blocks; ++j) {
-            const float u = sb[j];
-            rank += (u > v) || (u == v && j < b);
-        }
-        keep[b] = rank < slots && v != -INFINITY;
-        row[b] = rank < slots ? v : -INFINITY;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {  // ascending ids of the kept columns (np.flatnonzero order)
-        int n = 0;
-        for (int b = 0; b < blocks && n < slots_max; ++b)
-            if (keep[b]) kept[h * slots_max + n++] = b;
-        for (; n < slots_max; ++n) kept[h * slots_max + n] = -1;
-    }
-}
-
-// Softmax over one head's scores, then the value mix over window rows and
-// block mean values (kernels.cl:76-107).  One block per head.
-__global__ void k_sparse_attend(const float *scores, const float *v_ring, const float *v_mean, float *out, int heads,
-                                int kv_heads, int dim, int start, int length, int blocks) {
-    pdl_trigger();
-    pdl_wait();
-    extern __shared__ float p[];
-    __shared__ float red[32];
-    const int h = blockIdx.x, total = length + blocks;
-    const int kh = h / (heads / kv_heads), width = kv_heads * dim;
-    const float *s = scores + static_cast<size_t>(h) * total;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    float m = -INFINITY;
-    for (int t = threadIdx.x; t < total; t += blockDim.x) m = fmaxf(m, s[t]);
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[warp] = m;
-    __syncthreads();
-    m = -INFINITY;
-    for (int w = 0; w < nwarps; ++w) m = fmaxf(m, red[w]);
-    __syncthreads();
-    float den = 0.f;
-    for (int t = threadIdx.x; t < total; t += blockDim.x) {
-        const float e = s[t] == -INFINITY ? 0.f : expf(__fsub_rn(s[t], m));
-        p[t] = e;
-        den += e;
-    }
-    den = warp_sum(den);
-    if (lane == 0) red[warp] = den;
-    __syncthreads();
-    den = 0.f;
-    for (int w = 0; w < nwarps; ++w) den += red[w];
-    // value mix: thread (j, part) sums keys part, part + parts, ...
-    const int parts = blockDim.x / dim;
-    const int j = threadIdx.x % dim, part = threadIdx.x / dim;
-    float acc = 0.f, acc2 = 0.f;
-    if (part < parts) {
-        const float *vr = v_ring + static_cast<size_t>(start) * width + static_cast<size_t>(kh) * dim + j;
-        const float *vm = v_mean + static_cast<size_t>(kh) * dim + j;
-        int t = part;
-#pragma unroll 4
-        for (; t < length; t += parts) acc = fmaf(p[t], vr[static_cast<size_t>(t) * width], acc);
-        for (; t < total; t += parts) {  // block means: only the kept ones carry weight
-            const float w = p[t];
-            if (w != 0.f) acc2 = fmaf(w, vm[static_cast<size_t>(t - length) * width], acc2);
-        }
-        acc += acc2;
-    }
-    __syncthreads();
-    float *partial = p;  // the weights are no longer needed
-    if (part < parts) partial[part * dim + j] = acc;
-    __syncthreads();
-    if (threadIdx.x < dim) {
-        float sum = 0.f;
-        for (int q = 0; q < parts; ++q) sum += partial[q * dim + threadIdx.x];
-        out[static_cast<size_t>(h) * dim + threadIdx.x] = __fdiv_rn(sum, den);
-    }
+    if (threadIdx.x == 0) *slot = global_time_ns();
 }
 
 // NumPy's pairwise float32 summation (np.add.reduce over a contiguous axis):
@@ -538,35 +383,43 @@ struct RouteArgs {
 // model.py:233-250 for one token (at most 256 experts, one thread each):
 // the element-wise steps in parallel, the running sums and the final
 // arithmetic in thread 0 in the reference's order.
-__global__ void __launch_bounds__(256) k_route(RouteArgs a) {
-    pdl_trigger();
-    pdl_wait();
+__device__ void route_block(const RouteArgs &a) {
     __shared__ float coarse[256], logits[256], ex[256], probs[256], terms[256];
     __shared__ int order[64];
     __shared__ float m_s, den_s;
     const int t = threadIdx.x, E = a.experts, G = a.groups, K = a.max_k;
     if (t < G)
-        coarse[t] = FADD(a.router[t], FADD(load_weight(a.coarse_bias, a.bias_dtype[0], t),
+        coarse[t] = FADD(__ldcg(a.router + t), FADD(load_weight(a.coarse_bias, a.bias_dtype[0], t),
                                            load_weight(a.group_bias, a.bias_dtype[1], t)));
     if (t < K) order[t] = -1;
     __syncthreads();
     if (t < E) {
-        const float fine = FADD(a.router[G + t], FADD(load_weight(a.fine_bias, a.bias_dtype[2], t),
+        const float fine = FADD(__ldcg(a.router + G + t), FADD(load_weight(a.fine_bias, a.bias_dtype[2], t),
                                                      load_weight(a.expert_bias, a.bias_dtype[3], t)));
         logits[t] = __fdiv_rn(FADD(fine, coarse[min(t / a.per_group, G - 1)]), a.temperature);
     }
     __syncthreads();
-    if (t == 0) {  // the softmax kernel (kernels.cl:76-84): the maximum, then one running sum
+    // the softmax kernel (kernels.cl:76-84): the maximum (exact in any order: warp 0),
+    // then one running sum in expert order (thread 0, eight terms loaded at a time)
+    if (t < 32) {
         float m = -INFINITY;
-        for (int e = 0; e < E; ++e) m = fmaxf(m, logits[e]);
-        m_s = m;
+        for (int e = t; e < E; e += 32) m = fmaxf(m, logits[e]);
+        m = warp_max(m);
+        if (t == 0) m_s = m;
     }
     __syncthreads();
     if (t < E) ex[t] = expf(__fsub_rn(logits[t], m_s));
     __syncthreads();
     if (t == 0) {
         float den = 0.f;
-        for (int e = 0; e < E; ++e) den = FADD(den, ex[e]);
+        for (int e0 = 0; e0 < E; e0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = e0 + k < E ? ex[e0 + k] : 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (e0 + k < E) den = FADD(den, v[k]);
+        }
         den_s = den;
     }
     __syncthreads();
@@ -597,6 +450,65 @@ __global__ void __launch_bounds__(256) k_route(RouteArgs a) {
         a.weights[k] = k < active ? __fdiv_rn(sel[k], norm) : 0.f;
     }
     *a.active = active;
+}
+
+#include "heavy_attn.cuh"
+#include "heavy_stream.cuh"
+
+// The router GEMV (coarse rows, then fine rows; one row per warp, the input
+// RMSNorm(x, f_norm) staged per block, k_gemv's arithmetic) and then, in the
+// last block to finish, the routing of route_block (model.py:233-250).
+struct RouterArgs {
+    RouteArgs ra;                 // routing of the logits at ra.router
+    float *logits;                // = ra.router: coarse then fine logits (groups + experts)
+    const void *coarse, *fine;    // [groups, cols], [experts, cols]
+    int dtype, cols, groups, experts;
+    const float *x;
+    const void *gain;
+    int gain_dtype;
+    float eps;
+    unsigned long long *done;     // monotonic count of finished blocks
+    unsigned long long seq;       // this launch's number (1, 2, ...)
+    unsigned long long *probe;    // tracing only, else NULL
+};
+
+static_assert(kGemvThreads == stream::kConsumers, "the router stages its input with stream::stage (256 threads)");
+__global__ void __launch_bounds__(kGemvThreads) k_router_route(RouterArgs a) {
+    extern __shared__ __align__(16) float xs[];
+    __shared__ int last;
+    pdl_trigger();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rows = a.groups + a.experts, r = blockIdx.x * kGemvRows + warp;
+    const size_t row_bytes = static_cast<size_t>(a.cols) * (a.dtype == MR_DTYPE_F32 ? 4 : 2);
+    const int rr = min(r, rows - 1);
+    const char *row = rr < a.groups ? static_cast<const char *>(a.coarse) + rr * row_bytes
+                                    : static_cast<const char *>(a.fine) + (rr - a.groups) * row_bytes;
+    RowBatchT<kBatch> b;
+    __shared__ float red[32];
+    float gains[stream::kGainRegs];
+    if (threadIdx.x == 0) probe(a.probe, kProbeStart);
+    if (r < rows) prefetch_rows(row, nullptr, a.dtype, a.cols, b);
+    stream::load_gains(a.gain, a.gain_dtype, a.cols, gains);  // weights: before the dependency wait
+    pdl_wait();
+    if (threadIdx.x == 0) probe(a.probe, kProbeWaited);
+    // RMSNorm(x, f_norm) as stage_input computes it (256 threads), plain layout
+    stream::stage(a.x, a.cols, true, a.gain, a.gain_dtype, gains, a.eps, false, xs, red);
+    __syncthreads();
+    if (threadIdx.x == 0) probe(a.probe, kProbeStaged);
+    if (r < rows) {
+        float y, unused;
+        warp_dot2(row, nullptr, a.dtype, a.cols, xs, b, y, unused);
+        if (lane == 0) a.logits[r] = y;
+    }
+    if (threadIdx.x == 0) probe(a.probe, kProbeMain);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(a.done, 1ull) == a.seq * gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    route_block(a.ra);
+    if (threadIdx.x == 0) probe(a.probe, kProbeExit);
 }
 
 struct ExpertArgs {
@@ -759,6 +671,7 @@ struct HeavyLayer {
     const void *coarse_bias, *group_bias, *fine_bias, *expert_bias;
     int bias_dt[4];
     const void **d_gate, **d_up, **d_down;  // device pointer tables [experts + shared]
+    std::vector<const void *> h_gate, h_up, h_down;  // the same tables on the host
     int expert_dtype;
 };
 
@@ -791,6 +704,25 @@ struct HeavyEngine {
     int *err = nullptr;
     std::vector<void *> allocations;
     bool table_set = false;
+    // the streaming / fused kernels: SM count (one streaming CTA per SM), the
+    // fused attention's scratch (raw key / value rows, partial softmax per
+    // unit, per-KV-head counters), the newest block's running key / value sums
+    // per (layer, loop), the router's block counter, and the launch numbers the
+    // monotonic counters are compared against (both zeroed by heavy_reset)
+    int sm_count = 0, attn_chunks = 0;
+    // ring slots per stream::Mode (plain, swiglu, down): measured at 4 to 12 slots, bytes in
+    // flight pay more than room for the next kernel's CTAs beside a smaller ring
+    int stream_slots[3] = {12, 12, 8};
+    float *attn_partial = nullptr;
+    unsigned long long *counters = nullptr;  // [KVH] ready, [KVH] done, [1] router blocks
+    std::vector<float *> k_bsum, v_bsum;
+    unsigned long long attn_seq = 0, route_seq = 0;
+    bool streamable = false;                 // every projection's rows are whole 16-byte chunks
+    // tracing (heavy_trace_token): one stamp after every kernel of a token step
+    unsigned long long *trace = nullptr;
+    int trace_n = 0, trace_cap = 0;
+    unsigned long long *probes = nullptr;  // kProbeSlots per probed launch (tracing)
+    int probe_n = 0, probe_cap = 0;
 };
 
 namespace {
@@ -840,6 +772,18 @@ int launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaSt
     cfg.numAttrs = 1;
     MR_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...));
     return MR_OK;
+}
+
+// The probe slots of the next probed launch (tracing only), else NULL.
+unsigned long long *next_probe(HeavyEngine &e) {
+    if (!e.probes || e.probe_n >= e.probe_cap) return nullptr;
+    return e.probes + static_cast<size_t>(kProbeSlots) * e.probe_n++;
+}
+
+// A stamp after the kernel just queued (tracing only).
+int stamp(HeavyEngine &e) {
+    if (!e.trace || e.trace_n >= e.trace_cap) return MR_OK;
+    return launch(k_stamp, 1, 32, 0, e.stream, e.trace + e.trace_n++);
 }
 
 int launch_gemv(HeavyEngine &e, std::initializer_list<GemvSeg> segs) {
@@ -1003,6 +947,9 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
             down.push_back(dn);
         }
         Ly.expert_dtype = dtype;
+        Ly.h_gate = gate;
+        Ly.h_up = up;
+        Ly.h_down = down;
         const size_t n = gate.size();
         if ((rc = halloc_n(*e, n, &Ly.d_gate)) || (rc = halloc_n(*e, n, &Ly.d_up)) ||
             (rc = halloc_n(*e, n, &Ly.d_down)))
@@ -1010,6 +957,49 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
         MR_CUDA_TRY(cudaMemcpy(Ly.d_gate, gate.data(), n * sizeof(void *), cudaMemcpyHostToDevice));
         MR_CUDA_TRY(cudaMemcpy(Ly.d_up, up.data(), n * sizeof(void *), cudaMemcpyHostToDevice));
         MR_CUDA_TRY(cudaMemcpy(Ly.d_down, down.data(), n * sizeof(void *), cudaMemcpyHostToDevice));
+    }
+    // fused attention and streaming kernels
+    {
+        int dev = 0;
+        MR_CUDA_TRY(cudaGetDevice(&dev));
+        MR_CUDA_TRY(cudaDeviceGetAttribute(&e->sm_count, cudaDevAttrMultiProcessorCount, dev));
+        const int G = e->H / e->KVH;
+        if (G > attn::kMaxG || e->d % 4 != 0 || e->d > attn::kMaxDim) {
+            heavy_destroy(e);
+            return set_error(MR_ERR_ARGUMENT, "heavy-medium-2.0: %d query heads per KV head and head_dim %d are "
+                             "outside the fused attention's limits (<= %d, a multiple of 4 up to %d)",
+                             G, e->d, attn::kMaxG, attn::kMaxDim);
+        }
+        e->attn_chunks = (std::min(e->window, e->context) + attn::kChunk - 1) / attn::kChunk;
+        const size_t units = static_cast<size_t>(e->attn_chunks) + 1;
+        if ((rc = halloc_n(*e, e->KVH * units * G * (e->d + 2), &e->attn_partial)) ||
+            (rc = halloc_n(*e, 2 * static_cast<size_t>(e->KVH) + 1, &e->counters)))
+            return fail(rc);
+        for (size_t i = 0; i < per; ++i) {
+            float *ks, *vs;
+            if ((rc = halloc_n(*e, width, &ks)) || (rc = halloc_n(*e, width, &vs))) return fail(rc);
+            e->k_bsum.push_back(ks);
+            e->v_bsum.push_back(vs);
+        }
+        const size_t attn_smem =
+            attn::smem_bytes(e->latent, G, e->d, maxblocks, std::max(1, e->slots), static_cast<int>(units));
+        MR_REQUIRE(static_cast<size_t>(G) * std::max(1, e->slots) * e->d <= static_cast<size_t>(attn::kChunk) * e->d,
+                   "heavy-medium-2.0: %d kept blocks per query head exceed the attention tiles", e->slots);
+        MR_CUDA_TRY(cudaFuncSetAttribute(attn::k_sparse_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(attn_smem)));
+        // the streaming kernel needs rows of whole 16-byte chunks and one dtype per launch
+        auto whole = [](const GemvSeg &g) { return ((static_cast<size_t>(g.cols) * (g.dtype == MR_DTYPE_F32 ? 4 : 2)) & 15) == 0; };
+        bool ok = ((static_cast<size_t>(e->hidden) * (e->head_dt == MR_DTYPE_F32 ? 4 : 2)) & 15) == 0;
+        for (const HeavyLayer &Ly : e->L) {
+            ok = ok && whole(Ly.q) && whole(Ly.latent) && whole(Ly.o) && Ly.q.dtype == Ly.latent.dtype;
+            const size_t eb = Ly.expert_dtype == MR_DTYPE_F32 ? 4 : 2;
+            ok = ok && ((e->hidden * eb) & 15) == 0 && ((e->ffn * eb) & 15) == 0;
+        }
+        ok = ok && slots_total <= stream::kMaxSegs;
+        e->streamable = ok;
+        for (auto kernel : {stream::k_stream<MR_DTYPE_BF16>, stream::k_stream<MR_DTYPE_F16>,
+                            stream::k_stream<MR_DTYPE_F32>})
+            MR_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem));
     }
     MR_CUDA_TRY(cudaMemset(e->kept, 0xff, per * e->H * std::max(1, e->slots) * sizeof(int)));
     MR_CUDA_TRY(cudaMemset(e->chosen, 0xff, per * e->max_k * sizeof(int)));
@@ -1023,6 +1013,13 @@ void heavy_destroy(HeavyEngine *e) {
     if (!e) return;
     for (void *p : e->allocations) cudaFree(p);
     delete e;
+}
+
+int heavy_reset(HeavyEngine *e) {
+    MR_CUDA_TRY(cudaMemset(e->counters, 0, (2 * static_cast<size_t>(e->KVH) + 1) * sizeof(unsigned long long)));
+    MR_CUDA_TRY(cudaMemset(e->err, 0, sizeof(int)));
+    e->attn_seq = e->route_seq = 0;
+    return MR_OK;
 }
 
 int heavy_set_log1p(HeavyEngine *e, const float *values, int n) {
@@ -1055,52 +1052,131 @@ int heavy_greedy_chain(HeavyEngine *e, int first_token, int position, int steps)
 }
 
 namespace {
+
+// Launches k_stream for one dtype; the ring takes the shared memory the
+// launch's other regions leave.
+int launch_stream(HeavyEngine &e, stream::Args a) {
+    const int grid = e.sm_count;
+    const size_t fixed = stream::fixed_smem(a, grid);
+    const int slots = static_cast<int>((kStreamSmem - fixed) / stream::kSlotBytes);
+    MR_REQUIRE(slots >= 2, "streaming GEMV: %zu bytes of inputs leave no room for the weight ring", fixed);
+    // a whole number of slots per consumer warp (see k_stream)
+    a.probe = next_probe(e);
+    a.slots = std::min({slots, stream::kMaxSlots, e.stream_slots[a.mode]});
+    MR_REQUIRE(a.residual == 0 || a.nseg == 1, "streaming GEMV: a residual launch has one matrix");
+    a.err = e.err;
+    const size_t smem = fixed + static_cast<size_t>(a.slots) * stream::kSlotBytes;
+    switch (a.dtype) {
+        case MR_DTYPE_BF16: return launch(stream::k_stream<MR_DTYPE_BF16>, grid, stream::kThreads, smem, e.stream, a);
+        case MR_DTYPE_F16: return launch(stream::k_stream<MR_DTYPE_F16>, grid, stream::kThreads, smem, e.stream, a);
+        default: return launch(stream::k_stream<MR_DTYPE_F32>, grid, stream::kThreads, smem, e.stream, a);
+    }
+}
+
+// y = W x (or y += scale W x) for matrices of one width and dtype, the input
+// RMSNorm'ed with `gain` when given.
+int stream_plain(HeavyEngine &e, std::initializer_list<GemvSeg> segs, const float *x, const void *gain,
+                 int gain_dtype, int residual, float scale) {
+    stream::Args a{};
+    a.mode = stream::kPlain;
+    for (const GemvSeg &g : segs) {
+        a.dtype = g.dtype;
+        a.cols = g.cols;
+        a.seg[a.nseg++] = stream::Seg{g.w, nullptr, g.y, g.rows, 0};
+    }
+    a.x = x;
+    a.norm = gain != nullptr;
+    a.gain = gain;
+    a.gain_dtype = gain_dtype;
+    a.eps = e.eps;
+    a.residual = residual;
+    a.scale = scale;
+    return launch_stream(e, a);
+}
+
 int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
     MR_REQUIRE(e->table_set, "heavy-medium-2.0: the distance-penalty table has not been set");
     MR_REQUIRE(position >= 0 && position < e->context, "position %d outside the context", position);
     cudaStream_t s = e->stream;
-    const int width = e->KVH * e->d, count = position + 1;
+    const int count = position + 1;
     const int length = std::min(e->window, count), start = count - length;
     const int blocks = (count + e->block - 1) / e->block;
-    const int slots = std::min(e->slots, blocks), total = length + blocks;
+    const int slots = std::min(e->slots, blocks);
     const int slots_total = e->max_k + e->shared;
+    const int G = e->H / e->KVH;
+    const int maxblocks = (e->context + e->block - 1) / e->block;
     const float loop_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::sqrt((double)e->loops));
     const float shared_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::max(e->shared, 1));
+    const size_t attn_smem =
+        attn::smem_bytes(e->latent, G, e->d, maxblocks, std::max(1, e->slots), e->attn_chunks + 1);
     if (int rc = launch(k_embed_row, (e->hidden + 255) / 256, 256, 0, s, e->embed, e->embed_dt, dtoken, token,
                         e->hidden, e->x))
         return rc;
+    if (int rc = stamp(*e)) return rc;
     for (int l = 0; l < e->layers; ++l) {
         HeavyLayer &Ly = e->L[l];
         for (int loop = 0; loop < e->loops; ++loop) {
             const size_t li = static_cast<size_t>(l) * e->loops + loop;
-            // attention (model.py:192-229)
-            if (int rc = launch_gemv(*e, {Ly.q, Ly.latent})) return rc;
-            if (int rc = launch_gemv(*e, {Ly.kv_up})) return rc;
-            if (int rc = launch(k_heads_norm_rope, e->H + e->KVH, 32, 0, s, e->q, e->kv, e->k_ring[li], e->v_ring[li],
-                                e->inv_freq, e->H, e->KVH, e->d, e->split_half, position, position))
+            // 1. q | latent of RMSNorm(x, a_norm)
+            if (e->streamable) {
+                if (int rc = stream_plain(*e, {Ly.q, Ly.latent}, e->x, Ly.a_norm, Ly.a_norm_dt, 0, 1.0f)) return rc;
+            } else if (int rc = launch_gemv(*e, {Ly.q, Ly.latent})) {
                 return rc;
-            if (int rc = launch(k_block_mean_last, (2 * width + 255) / 256, 256, 0, s, e->k_ring[li], e->v_ring[li],
-                                e->k_mean[li], e->v_mean[li], count, width, e->block))
+            }
+            if (int rc = stamp(*e)) return rc;
+            // 2. sparse attention (model.py:192-229) in one launch
+            attn::Args aa{};
+            aa.q = e->q;
+            aa.latent = e->lat;
+            aa.kv_up = Ly.kv_up.w;
+            aa.kv_dtype = Ly.kv_up.dtype;
+            aa.latent_dim = e->latent;
+            aa.kv = e->kv;
+            aa.k_ring = e->k_ring[li];
+            aa.v_ring = e->v_ring[li];
+            aa.k_mean = e->k_mean[li];
+            aa.v_mean = e->v_mean[li];
+            aa.k_bsum = e->k_bsum[li];
+            aa.v_bsum = e->v_bsum[li];
+            aa.inv_freq = e->inv_freq;
+            aa.split_half = e->split_half;
+            aa.H = e->H;
+            aa.KVH = e->KVH;
+            aa.d = e->d;
+            aa.position = position;
+            aa.count = count;
+            aa.length = length;
+            aa.start = start;
+            aa.blocks = blocks;
+            aa.block = e->block;
+            aa.slots = slots;
+            aa.slots_max = std::max(1, e->slots);
+            aa.chunks = e->attn_chunks;
+            aa.max_blocks = maxblocks;
+            aa.log1p_table = e->log1p_table;
+            aa.slope = e->slope;
+            aa.kept = e->kept + li * e->H * std::max(1, e->slots);
+            aa.partial = e->attn_partial;
+            aa.ready = e->counters;
+            aa.done = e->counters + e->KVH;
+            aa.seq = ++e->attn_seq;
+            aa.out = e->attn;
+            aa.err = e->err;
+            aa.probe = next_probe(*e);
+            if (int rc = launch(attn::k_sparse_attention, e->KVH * (e->attn_chunks + 1), attn::kThreads, attn_smem, s,
+                                aa))
                 return rc;
-            const int items = e->H * total;
-            if (int rc = launch(k_sparse_scores, (items + 7) / 8, 256, 0, s, e->q, e->k_ring[li], e->k_mean[li],
-                                e->scores, e->H, e->KVH, e->d, start, length, blocks))
-                return rc;
-            int *kept = e->kept + li * e->H * std::max(1, e->slots);
-            if (int rc = launch(k_block_topk, e->H, 256, static_cast<size_t>(blocks) * (sizeof(float) + sizeof(int)), s,
-                                e->scores, total, length, blocks, e->block, position, e->log1p_table, e->slope, slots,
-                                std::max(1, e->slots), kept))
-                return rc;
-            const int attend_threads = std::max(128, std::min(1024, (1024 / e->d) * e->d));
-            const size_t attend_smem = std::max<size_t>(total, static_cast<size_t>(attend_threads)) * sizeof(float);
-            if (int rc = launch(k_sparse_attend, e->H, attend_threads, attend_smem, s, e->scores, e->v_ring[li],
-                                e->v_mean[li], e->attn, e->H, e->KVH, e->d, start, length, blocks))
-                return rc;
-            GemvSeg o = Ly.o;
-            o.scale = loop_scale;
-            if (int rc = launch_gemv(*e, {o})) return rc;
-            // mixture of experts (model.py:231-255)
-            if (int rc = launch_gemv(*e, {Ly.coarse, Ly.fine})) return rc;
+            if (int rc = stamp(*e)) return rc;
+            // 3. x += s * W_o attended
+            if (e->streamable) {
+                if (int rc = stream_plain(*e, {Ly.o}, e->attn, nullptr, 0, 1, loop_scale)) return rc;
+            } else {
+                GemvSeg o = Ly.o;
+                o.scale = loop_scale;
+                if (int rc = launch_gemv(*e, {o})) return rc;
+            }
+            if (int rc = stamp(*e)) return rc;
+            // 4. router logits of RMSNorm(x, f_norm), then the routing (model.py:231-250)
             RouteArgs ra{};
             ra.router = e->router;
             ra.coarse_bias = Ly.coarse_bias;
@@ -1118,7 +1194,75 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             ra.chosen = e->chosen + li * e->max_k;
             ra.weights = e->weights + li * e->max_k;
             ra.active = e->active + li;
-            if (int rc = launch(k_route, 1, 256, 0, s, ra)) return rc;
+            RouterArgs rt{};
+            rt.ra = ra;
+            rt.logits = e->router;
+            rt.coarse = Ly.coarse.w;
+            rt.fine = Ly.fine.w;
+            rt.dtype = Ly.coarse.dtype;
+            rt.cols = e->hidden;
+            rt.groups = e->groups;
+            rt.experts = e->experts;
+            rt.x = e->x;
+            rt.gain = Ly.f_norm;
+            rt.gain_dtype = Ly.f_norm_dt;
+            rt.eps = e->eps;
+            rt.done = e->counters + 2 * e->KVH;
+            rt.seq = ++e->route_seq;
+            rt.probe = next_probe(*e);
+            const int router_blocks = (e->groups + e->experts + kGemvRows - 1) / kGemvRows;
+            if (int rc = launch(k_router_route, router_blocks, kGemvThreads,
+                                static_cast<size_t>(e->hidden) * sizeof(float) + 16, s, rt))
+                return rc;
+            if (int rc = stamp(*e)) return rc;
+            // 5-6. the chosen and the shared experts, then the rank-order combine (model.py:251-255)
+            if (e->ranks == 1 && e->streamable) {
+                stream::Args g{};
+                g.mode = stream::kSwiglu;
+                g.dtype = Ly.expert_dtype;
+                g.cols = e->hidden;
+                for (int i = 0; i < e->shared; ++i)
+                    g.seg[g.nseg++] = stream::Seg{Ly.h_gate[e->experts + i], Ly.h_up[e->experts + i], nullptr, e->ffn,
+                                                  e->max_k + i};
+                g.dyn_w = Ly.d_gate;
+                g.dyn_w2 = Ly.d_up;
+                g.chosen = ra.chosen;
+                g.active = ra.active;
+                g.max_k = e->max_k;
+                g.dyn_rows = e->ffn;
+                g.experts = e->experts;
+                g.shared = e->shared;
+                g.x = e->x;
+                g.norm = 1;
+                g.gain = Ly.f_norm;
+                g.gain_dtype = Ly.f_norm_dt;
+                g.eps = e->eps;
+                g.act_out = e->act;
+                if (int rc = launch_stream(*e, g)) return rc;
+                if (int rc = stamp(*e)) return rc;
+                stream::Args dn{};
+                dn.mode = stream::kDown;
+                dn.dtype = Ly.expert_dtype;
+                dn.cols = e->ffn;
+                for (int i = 0; i < e->shared; ++i)
+                    dn.seg[dn.nseg++] = stream::Seg{Ly.h_down[e->experts + i], nullptr, nullptr, e->hidden,
+                                                    e->max_k + i};
+                dn.dyn_w = Ly.d_down;
+                dn.chosen = ra.chosen;
+                dn.active = ra.active;
+                dn.max_k = e->max_k;
+                dn.dyn_rows = e->hidden;
+                dn.experts = e->experts;
+                dn.shared = e->shared;
+                dn.acts = e->act;
+                dn.weights = ra.weights;
+                dn.shared_scale = shared_scale;
+                dn.scale = loop_scale;
+                dn.xres = e->x;
+                if (int rc = launch_stream(*e, dn)) return rc;
+                if (int rc = stamp(*e)) return rc;
+                continue;
+            }
             ExpertArgs ea{};
             ea.gate = Ly.d_gate;
             ea.up = Ly.d_up;
@@ -1151,17 +1295,22 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             if (int rc = launch(k_expert_gate_up, dim3((e->ffn + 7) / 8, slots_total), kGemvThreads,
                                 static_cast<size_t>(e->hidden) * sizeof(float) + 16, s, ea))
                 return rc;
+            if (int rc = stamp(*e)) return rc;
             if (int rc = launch(k_expert_down, dim3((e->hidden + kGemvRows - 1) / kGemvRows, slots_total), kGemvThreads,
                                 static_cast<size_t>(e->ffn) * sizeof(float) + 16, s, ea))
                 return rc;
-            if (e->ranks > 1)
+            if (int rc = stamp(*e)) return rc;
+            if (e->ranks > 1) {
                 if (int rc = launch(k_moe_publish, 1, 32, 0, s, ea)) return rc;
+                if (int rc = stamp(*e)) return rc;
+            }
             if (int rc = launch(k_expert_combine, (e->hidden + 255) / 256, 256, 0, s, ea, ra.weights, shared_scale,
                                 loop_scale, e->x))
                 return rc;
-            MR_CUDA_TRY(cudaGetLastError());
+            if (int rc = stamp(*e)) return rc;
         }
     }
+    // the head of RMSNorm(x, norm)
     GemvSeg head{};
     head.w = e->head;
     head.dtype = e->head_dt;
@@ -1173,13 +1322,57 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
     head.gain = e->final_norm;
     head.gain_dtype = e->final_norm_dt;
     head.eps = e->eps;
-    if (int rc = launch_gemv(*e, {head})) return rc;
+    if (e->streamable) {
+        if (int rc = stream_plain(*e, {head}, e->x, e->final_norm, e->final_norm_dt, 0, 1.0f)) return rc;
+    } else if (int rc = launch_gemv(*e, {head})) {
+        return rc;
+    }
+    if (int rc = stamp(*e)) return rc;
     MR_CUDA_TRY(cudaGetLastError());
     return MR_OK;
 }
 }  // namespace
 
 const float *heavy_logits(const HeavyEngine *e) { return e->logits; }
+
+int heavy_trace_token(HeavyEngine *e, int token, int position, unsigned long long *stamps, int capacity, int *count) {
+    MR_REQUIRE(token >= 0 && token < e->vocab, "input token is outside the vocabulary");
+    MR_REQUIRE(stamps && count && capacity >= 2, "NULL argument or no room for stamps");
+    // layout of `stamps`: [0 .. kernels] kernel-boundary stamps, then kProbeSlots per probed launch
+    const int probed = 6 * e->layers * e->loops + 1;
+    const int nstamps = std::max(2, capacity - probed * kProbeSlots);
+    unsigned long long *d = nullptr;
+    MR_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void **>(&d), sizeof(unsigned long long) * capacity, e->stream));
+    MR_CUDA_TRY(cudaMemsetAsync(d, 0, sizeof(unsigned long long) * capacity, e->stream));
+    const bool with_probes = capacity >= nstamps + probed * kProbeSlots;
+    if (with_probes) {  // minima start at the largest value
+        std::vector<unsigned long long> init(static_cast<size_t>(probed) * kProbeSlots, 0ull);
+        for (int i = 0; i < probed; ++i) init[static_cast<size_t>(i) * kProbeSlots + kProbeStart] =
+            init[static_cast<size_t>(i) * kProbeSlots + kProbeWaited] = ~0ull;
+        MR_CUDA_TRY(cudaMemcpyAsync(d + nstamps, init.data(), init.size() * sizeof(unsigned long long),
+                                    cudaMemcpyHostToDevice, e->stream));
+        MR_CUDA_TRY(cudaStreamSynchronize(e->stream));
+        e->probes = d + nstamps;
+        e->probe_n = 0;
+        e->probe_cap = probed;
+    }
+    e->trace = d;
+    e->trace_n = 0;
+    e->trace_cap = nstamps;
+    int rc = stamp(*e);  // the step's start: the work queued before it has completed
+    if (!rc) rc = token_step(e, nullptr, token, position);
+    const int n = e->trace_n;
+    e->trace = e->probes = nullptr;
+    e->trace_n = e->trace_cap = e->probe_n = e->probe_cap = 0;
+    cudaError_t err = cudaStreamSynchronize(e->stream);
+    if (!rc && err == cudaSuccess)
+        err = cudaMemcpy(stamps, d, sizeof(unsigned long long) * capacity, cudaMemcpyDeviceToHost);
+    cudaFreeAsync(d, e->stream);
+    if (rc) return rc;
+    if (err != cudaSuccess) return cuda_error(err, "heavy trace");
+    *count = n;
+    return MR_OK;
+}
 
 void heavy_arena(const HeavyEngine *e, char **arena, size_t *bytes) {
     *arena = e->arena;
@@ -1193,8 +1386,15 @@ void heavy_connect(HeavyEngine *e, char *const *peers) {
 int heavy_status(const HeavyEngine *e) {
     int err = 0;
     MR_CUDA_TRY(cudaMemcpy(&err, e->err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (err) return set_error(MR_ERR_CUDA, "expert parallel: a rank's expert rows did not arrive within 2 s");
-    return MR_OK;
+    switch (err) {
+        case 0: return MR_OK;
+        case 1: return set_error(MR_ERR_TIMEOUT, "expert parallel: a rank's expert rows did not arrive within 2 s");
+        case 2: return set_error(MR_ERR_TIMEOUT, "weight stream: a bulk copy did not land within 2 s");
+        case 3: return set_error(MR_ERR_TIMEOUT, "sparse attention: a key / value row did not arrive within 2 s");
+        case 4: return set_error(MR_ERR_CUDA, "expert routing chose an id outside the expert table (non-finite router "
+                                              "logits?)");
+        default: return set_error(MR_ERR_TIMEOUT, "heavy-medium-2.0: device wait timed out (code %d)", err);
+    }
 }
 
 int heavy_last_topk(const HeavyEngine *e, int layer, int loop, int *blocks, int capacity) {

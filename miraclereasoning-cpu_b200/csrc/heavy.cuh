@@ -21,6 +21,8 @@ void heavy_connect(HeavyEngine *e, char *const *peers);
 // Reads the wait status of the expert-parallel exchange (synchronous).
 int heavy_status(const HeavyEngine *e);
 void heavy_destroy(HeavyEngine *e);
+// A new sequence: zeroes the device counters of the fused kernels and the error word.
+int heavy_reset(HeavyEngine *e);
 
 // float32 log1p(d) for distances d = 0 .. context-1, as the host computes them
 // (the reference applies NumPy's float32 log1p, model.py:221-222).
@@ -30,6 +32,11 @@ int heavy_set_log1p(HeavyEngine *e, const float *values, int n);
 // floats) are then at heavy_logits(e).
 int heavy_token(HeavyEngine *e, int token, int position);
 const float *heavy_logits(const HeavyEngine *e);
+
+// heavy_token with a %globaltimer stamp before the step and after every kernel
+// (stamps[0] = start, stamps[k] = completion of the step's k-th kernel);
+// synchronous.  *count receives the number of stamps written.
+int heavy_trace_token(HeavyEngine *e, int token, int position, unsigned long long *stamps, int capacity, int *count);
 
 // Greedy decode entirely on the device: `steps` tokens from `position`, each
 // step's input the previous step's argmax (the first: first_token).

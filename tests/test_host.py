@@ -205,5 +205,6 @@ def test_bench_heavy_byte_accounting():
     expert = sum(int(np.prod(shapes[f"layers.0.experts.0.{k}"])) * 4 for k in ("gate", "up", "down"))
     base = bench.weight_bytes(config, "F32", 0)
     assert bench.weight_bytes(config, "F32", 2) - base == 2 * expert * config.layers * config.inner_loop_steps
-    assert bench.launches_per_step(config) == 1 + 13 * config.layers * config.inner_loop_steps + 2
+    assert bench.launches_per_step(config) == 1 + 6 * config.layers * config.inner_loop_steps + 2
+    assert bench.launches_per_step(config, True) == 1 + 8 * config.layers * config.inner_loop_steps + 2
     assert bench.launches_per_step(cases.micro_config("nano15")) == 1
