@@ -177,3 +177,59 @@ def synthetic_weights(config: ModelConfig, stored: str = "BF16", seed: int = 0, 
             continue
         weights[name] = BF16Array(hash_normal_bf16(seed, index, shape, std))
     return weights
+
+
+class LazySyntheticWeights:
+    """The synthetic model as a read-only mapping whose BF16 tensors are
+    generated when first read (same bits as ``synthetic_weights``), kept in an
+    LRU of ``budget_bytes`` of BF16: a host can run a model that does not fit
+    its memory (the 73 GB Heavy Medium configuration), generating only what a
+    token touches.  Values support ``shape``, row slicing and ``np.asarray``."""
+
+    def __init__(self, config: ModelConfig, seed: int = 0, budget_bytes: int = 16 << 30):
+        from collections import OrderedDict
+        self._plan = {name: (index, shape, std) for index, name, shape, std in tensor_plan(config)}
+        self._seed, self._budget, self._used, self._cache = seed, budget_bytes, 0, OrderedDict()
+
+    def __iter__(self):
+        return iter(self._plan)
+
+    def __len__(self):
+        return len(self._plan)
+
+    def __contains__(self, name):
+        return name in self._plan
+
+    def keys(self):
+        return self._plan.keys()
+
+    def __getitem__(self, name):
+        index, shape, std = self._plan[name]
+        if std is None:
+            return np.ones(shape, np.float32)
+        return _LazyBF16(self, name, shape)
+
+    def _bits(self, name):
+        if name in self._cache:
+            self._cache.move_to_end(name)
+            return self._cache[name]
+        index, shape, std = self._plan[name]
+        data = hash_normal_bf16(self._seed, index, shape, std)
+        while self._cache and self._used + data.nbytes > self._budget:
+            _, old = self._cache.popitem(last=False)
+            self._used -= old.nbytes
+        self._cache[name] = data
+        self._used += data.nbytes
+        return data
+
+
+class _LazyBF16:
+    def __init__(self, owner, name, shape):
+        self._owner, self._name, self.shape = owner, name, tuple(shape)
+
+    def __getitem__(self, key):
+        return (self._owner._bits(self._name)[key].astype(np.uint32) << np.uint32(16)).view(np.float32)
+
+    def __array__(self, dtype=None, copy=None):
+        result = self[:]
+        return result.astype(dtype, copy=False) if dtype is not None else result

@@ -4,7 +4,7 @@ TEST INFRASTRUCTURE ONLY: the checker the CUDA product is compared against.
 Nothing in the product package imports this module.
 
 ``HostBackend`` offers the method surface of the reference backend
-(miracle_reasoning/opencl.py:277-451): ``empty/upload/read/copy/run/linear/
+(miracle_reasoning/opencl.py:129-303): ``empty/upload/read/copy/run/linear/
 norm/rotate/add/swiglu/softmax/attention/mix/finish`` and ``.device`` with
 ``max_allocation_bytes``.  "Device memory" is host float32 NumPy storage and
 every ``run`` evaluates one NDRange through one of two kernel libraries:
@@ -13,7 +13,7 @@ every ``run`` evaluates one NDRange through one of two kernel libraries:
 * ``kernels="reference"`` — the reference's own kernels.cl compiled on the host
   (oracle/_ref/libref_kernels.so, see oracle/ref_host.cpp).
 
-Argument marshalling follows opencl.py:367-387: Tensor -> pointer, Python/NumPy
+Argument marshalling follows opencl.py:219-239: Tensor -> pointer, Python/NumPy
 float -> float32, int in int32 range -> int32, anything else is rejected.
 """
 from __future__ import annotations
@@ -100,7 +100,8 @@ class HostBackend:
         self.lib, self.prefix = load_kernels(kernels)
         self.kernels = kernels
         self.device = HostDevice(name=f"host-{kernels}", max_allocation_bytes=max_allocation_bytes)
-        self.uploads = []          # optional recording hook (golden generation)
+        self.uploads = []          # optional recording hook (golden generation): True records
+                                   # every upload, a predicate only the arrays it accepts
         self.record_uploads = False
 
     # buffers -----------------------------------------------------------------
@@ -116,7 +117,7 @@ class HostBackend:
         array = np.ascontiguousarray(array, dtype=np.float32)
         out = self.empty(array.shape)
         out.data[:] = array.reshape(-1)
-        if self.record_uploads:
+        if self.record_uploads and (self.record_uploads is True or self.record_uploads(array)):
             self.uploads.append(array.copy())
         return out
 
@@ -161,7 +162,7 @@ class HostBackend:
                 raise ValueError(f"{name}: argument kind mismatch")
         getattr(self.lib, self.prefix + name)(*shape, *values)
 
-    # op helpers (same launch geometry as opencl.py:389-448) ---------------------
+    # op helpers (same launch geometry as opencl.py:241-300) ---------------------
     def linear(self, x, weight):
         if len(x.shape) != 2 or len(weight.shape) != 2 or x.shape[1] != weight.shape[1]:
             raise ValueError("linear needs x[rows,in] and weight[out,in]")

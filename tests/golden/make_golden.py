@@ -2,7 +2,7 @@
 
 Run in a container that has the read-only reference checkout:
 
-    python tests/golden/make_golden.py [--reference-root /path/to/reference]
+    python tests/golden/make_golden.py --reference-root DIR   (or MIRACLE_REFERENCE_ROOT=DIR)
 
 The reference package (miracle_reasoning: model.py, config.py, weights.py) is
 imported unmodified and driven with ``oracle.host_backend.HostBackend
@@ -18,8 +18,9 @@ saved:
   logits, chunked-prefill logits, cache state, discrete decisions (heavy
   top-k blocks, MoE experts and weights, latent positions), greedy and sampled
   ``generate`` ids;
-* ``bench_<case>.npz`` — benchmark-architecture cases with short token
-  windows: leading logits, top-64 ids/values and the greedy ids;
+* ``bench_<case>.npz`` — every benchmark architecture at full size with a
+  short token window: leading logits, every 16th logit, top-64 ids/values,
+  the greedy ids (Heavy Medium: also experts and kept blocks per layer/loop);
 * ``prefill_<case>.npz`` — micro architectures with BF16 matrices and a
   48-token prompt: all-token logits, two-chunk logits, cache state, greedy
   decode steps after the prompt.
@@ -31,6 +32,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import sys
 import time
 from collections.abc import Mapping
@@ -177,27 +179,99 @@ def run_micro(name, rc, rm):
     return logits.shape
 
 
+class LazyWeights(Mapping):
+    """The synthetic BF16 model of a configuration, generated tensor by tensor
+    when the reference reads it (the 36B Heavy Medium model does not fit this
+    host's memory at once).  Generated tensors are kept in an LRU of
+    ``budget_bytes`` of BF16 bits; the values are exactly those of
+    ``synthetic.synthetic_weights`` (and of the device fill kernel)."""
+
+    def __init__(self, config, seed=0, budget_bytes=34 << 30):
+        from collections import OrderedDict
+        self.plan = {name: (index, shape, std) for index, name, shape, std in cases.synthetic.tensor_plan(config)}
+        self.seed, self.budget, self.used, self.cache = seed, budget_bytes, 0, OrderedDict()
+
+    def __iter__(self):
+        return iter(self.plan)
+
+    def __len__(self):
+        return len(self.plan)
+
+    def __contains__(self, key):
+        return key in self.plan
+
+    def __getitem__(self, key):
+        index, shape, std = self.plan[key]
+        if std is None:
+            return np.ones(shape, np.float32)
+        return _LazyTensor(self, key, shape)
+
+    def bits(self, key):
+        if key in self.cache:
+            self.cache.move_to_end(key)
+            return self.cache[key]
+        index, shape, std = self.plan[key]
+        data = cases.synthetic.hash_normal_bf16(self.seed, index, shape, std)
+        while self.cache and self.used + data.nbytes > self.budget:
+            _, old = self.cache.popitem(last=False)
+            self.used -= old.nbytes
+        self.cache[key] = data
+        self.used += data.nbytes
+        return data
+
+
+class _LazyTensor:
+    def __init__(self, owner, key, shape):
+        self.owner, self.key, self.shape = owner, key, tuple(shape)
+
+    def __getitem__(self, index):
+        return cases.widen_bf16(self.owner.bits(self.key)[index])
+
+    def __array__(self, dtype=None, copy=None):
+        result = self[:]
+        return result.astype(dtype, copy=False) if dtype is not None else result
+
+
 def run_bench(name, rc, rm):
+    """A BASELINE architecture at full size: the prompt, then greedy decode
+    steps.  Saved per step (prompt's last token, then each decode step): the
+    leading logits, every LOGIT_STRIDE-th logit (all of them for small
+    vocabularies), the top 64 ids and values, the greedy ids; for Heavy
+    Medium also the routed experts (with their weights) and the kept global
+    blocks of every layer and inner loop."""
     config, stored, ctx, prompt, steps = cases.bench_case(name)
     ref_config = rc.ModelConfig.from_dict(config.to_dict())
-    weights = cases.synthetic.synthetic_weights(config, stored)
-    model = rm.MiracleModel(ref_config, weights, backend=HostBackend("reference"), context_length=ctx)
+    heavy = config.family == "heavy-medium-2.0"
+    log = []
+    weights = LazyWeights(config) if heavy else cases.synthetic.synthetic_weights(config, stored)
+    backend = HostBackend("reference")
+    if heavy:
+        block = config.source["long_context"]["global_block_size"]
+        backend.record_uploads = lambda a: a.ndim == 2 and a.shape[0] == config.query_heads and \
+            a.shape[1] <= config.window + (ctx + block - 1) // block
+        weights = RecordingWeights(weights, log)
+    model = rm.MiracleModel(ref_config, weights, backend=backend, context_length=ctx)
+    decisions = instrument(model, backend, log) if heavy else None
     t0 = time.time()
     logits = [model.prefill(prompt)]
     tokens = []
     for _ in range(steps):
         tokens.append(int(np.argmax(logits[-1])))
         logits.append(model.decode(tokens[-1]))
+        print(f"  {name}: step {len(tokens)} of {steps} ({time.time() - t0:.0f} s)", flush=True)
     elapsed = time.time() - t0
     stack = np.stack(logits).astype(np.float32)
     top = np.argsort(-stack, axis=1, kind="stable")[:, :cases.TOPK_STORED]
+    meta = {"context": ctx, "stored": stored, "seconds": elapsed, "tokens_processed": len(prompt) + steps}
+    if heavy:  # per token (prompt and steps): kept blocks, experts, weights of every (layer, loop)
+        meta["decisions"] = [{k: d[k] for k in ("topk", "experts", "expert_weights")} for d in decisions]
     np.savez_compressed(
         HERE / f"bench_{name}.npz", lead=stack[:, :cases.LOGIT_SUBSET], top_ids=top.astype(np.int64),
         top_values=np.take_along_axis(stack, top, axis=1), tokens=np.asarray(tokens, np.int64),
         prompt=np.asarray(prompt, np.int64),
         full=stack if stack.shape[1] <= 4096 else np.zeros((0,), np.float32),
-        meta=json.dumps({"context": ctx, "stored": stored, "seconds": elapsed,
-                         "tokens_processed": len(prompt) + steps}))
+        strided=stack[:, ::cases.LOGIT_STRIDE],
+        meta=json.dumps(meta))
     return stack.shape, elapsed
 
 
@@ -290,9 +364,12 @@ def run_prefill(name, rc, rm):
 
 def main(argv=None):
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference-root", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--reference-root", type=Path, default=os.environ.get("MIRACLE_REFERENCE_ROOT"),
+                        help="the reference checkout (default: $MIRACLE_REFERENCE_ROOT)")
     parser.add_argument("--only", nargs="*")
     args = parser.parse_args(argv)
+    if args.reference_root is None:
+        parser.error("--reference-root (or MIRACLE_REFERENCE_ROOT) is required")
     rc, rm = _ref_modules(args.reference_root)
     todo = args.only or ["kernels", "configs", *[f"micro_{c}" for c in cases.MICRO_CASES],
                          *[f"bench_{c}" for c in cases.BENCH_CASES],
