@@ -294,6 +294,22 @@ MR_API int mr_model_tensor_download(mr_model *model, const char *name, float *ho
 MR_API int mr_model_trace_decode(mr_model *model, int token, uint64_t *stamps, int capacity, int *phases,
                                  int *grid);
 
+/* Bounded device waits: every wait of the model's kernels on another CTA's or
+ * another rank's data (exchange words, counters, copies in flight) gives up
+ * after `nanoseconds` (default 2 s, at least 1 ms), records an error, and the
+ * call returns MR_ERR_TIMEOUT; the model then refuses further steps until
+ * mr_model_reset (the reference latches _failed, model.py:298-311).  The
+ * setting survives mr_model_reset.  No reference counterpart (the reference
+ * has no device-side waits). */
+MR_API int mr_model_set_wait_limit(mr_model *model, uint64_t nanoseconds);
+
+/* Fault injection for tests of that path, on the host's side: with phase >= 0
+ * the decode kernel does not publish the words of step phase `phase` (Heavy
+ * Medium: the attention units do not count their key / value rows), so the
+ * readers' bounded waits run out; -1 turns it off.  No GPU fault is involved.
+ * No reference counterpart. */
+MR_API int mr_model_inject_fault(mr_model *model, int phase);
+
 /* Attention that allocates nothing on the device.  No counterpart in the
  * reference: it exists for callers that cannot call cudaMalloc while they run
  * (a framework that owns all device memory through its own pool, or code in a

@@ -111,6 +111,8 @@ struct mr_model {
     bool failed = false;
     bool op_path = false;  // no decode plan: the token step runs on the host over the op kernels
     HeavyEngine *heavy = nullptr;  // heavy-medium-2.0: the token step as kernel launches (heavy.cu)
+    unsigned long long wait_limit_ns = 0;  // device waits give up after this (0: the kernels' 2 s)
+    int withhold_phase = -1;               // fault injection for tests (mr_model_inject_fault)
     int position = 0;
     int grid = 0;
     // device buffers
@@ -757,6 +759,7 @@ int launch_step(mr_model *m, const StepControl &ctl) {
 
 StepControl base_control(mr_model *m) {
     StepControl ctl{};
+    ctl.withhold_phase = m->withhold_phase;
     ctl.feed = m->feed;
     ctl.feed_base = m->position;
     ctl.logits_rows = m->logits_rows;
@@ -1332,7 +1335,11 @@ int mr_model_reset(mr_model *m) {
     MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
     if (!m->finalized) return set_error(MR_ERR_STATE, "model is not finalized");
     MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
-    if (!m->op_path && !m->heavy) MR_CUDA_TRY(cudaMemset(m->state, 0, sizeof(StepState)));
+    if (!m->op_path && !m->heavy) {
+        MR_CUDA_TRY(cudaMemset(m->state, 0, sizeof(StepState)));
+        MR_CUDA_TRY(cudaMemcpy(&m->state->wait_limit_ns, &m->wait_limit_ns, sizeof(m->wait_limit_ns),
+                               cudaMemcpyHostToDevice));
+    }
     if (m->heavy) {
         const int rc = heavy_reset(m->heavy);
         if (rc) return rc;
@@ -1498,6 +1505,32 @@ int mr_model_set_log1p_table(mr_model *m, const float *values, int n) {
     if (!m->heavy) return set_error(MR_ERR_ARGUMENT, "model has no sparse block attention");
     MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
     return heavy_set_log1p(m->heavy, values, n);
+}
+
+int mr_model_set_wait_limit(mr_model *m, uint64_t nanoseconds) {
+    MR_REQUIRE(m, "model is NULL");
+    MR_REQUIRE(m->finalized, "model is not finalized");
+    MR_REQUIRE(nanoseconds >= 1000000ull, "a device wait limit below 1 ms would fail ordinary steps");
+    MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
+    MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    m->wait_limit_ns = nanoseconds;
+    if (m->heavy) return heavy_set_wait_limit(m->heavy, nanoseconds);
+    if (!m->op_path)
+        MR_CUDA_TRY(cudaMemcpy(&m->state->wait_limit_ns, &m->wait_limit_ns, sizeof(m->wait_limit_ns),
+                               cudaMemcpyHostToDevice));
+    return MR_OK;
+}
+
+int mr_model_inject_fault(mr_model *m, int phase) {
+    MR_REQUIRE(m, "model is NULL");
+    MR_REQUIRE(m->finalized, "model is not finalized");
+    MR_REQUIRE(!m->op_path, "the host-stepped families have no device waits to exercise");
+    MR_REQUIRE(phase >= -1, "phase must be -1 (off) or a phase index");
+    if (m->heavy) return heavy_inject_fault(m->heavy, phase >= 0);
+    MR_REQUIRE(phase < static_cast<int>(m->phases.size()) - 1, "phase %d outside the step's %d phases", phase,
+               static_cast<int>(m->phases.size()) - 1);
+    m->withhold_phase = phase;
+    return MR_OK;
 }
 
 int mr_model_trace_decode(mr_model *m, int token, uint64_t *stamps, int capacity, int *phases, int *grid) {

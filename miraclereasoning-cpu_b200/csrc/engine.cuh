@@ -265,6 +265,7 @@ struct StepState {
     int nonfinite;                    // a non-finite logit was produced
     int last_argmax;
     int error;                        // 1000 + phase: a bounded wait gave up; 3: context full; 4: bad token
+    unsigned long long wait_limit_ns; // a bounded wait gives up after this long (0: 2 s); survives reset
 };
 
 // Per-launch control, passed by value.
@@ -305,6 +306,10 @@ struct StepControl {
     // resident when first needed) and CTA 0 finishing the phase at
     // 1 + k*rec + grid*kTraceStamps.
     unsigned long long *trace;
+    // Fault injection for tests of the bounded waits (mr_model_inject_fault):
+    // the words of phase `withhold_phase` are not published, so its readers'
+    // waits run out; -1 = off.
+    int withhold_phase;
 };
 
 }  // namespace mr

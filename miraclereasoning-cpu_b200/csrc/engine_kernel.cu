@@ -65,7 +65,15 @@ struct Control {
     int abort;                         // the compute warps stopped: the producer stops too
     unsigned long long wait_ns;        // tracing: time thread 0 spent in take_piece this phase
     int late;                          // tracing: pieces not resident at their first probe
+    int withhold;                      // fault injection: words tagged withhold_tag are not stored
+    unsigned withhold_tag;
 };
+
+// How long a bounded wait may last (mr_model_set_wait_limit; default 2 s).
+__device__ __forceinline__ unsigned long long wait_limit(const StepState *st) {
+    const unsigned long long v = *reinterpret_cast<volatile const unsigned long long *>(&st->wait_limit_ns);
+    return v ? v : kWaitLimitNs;
+}
 
 struct StepInfo {
     int position, token, logits_row;
@@ -161,6 +169,7 @@ __device__ __forceinline__ T *peer_ptr(const Control &c, int j, T *p) {
 // A word every rank reads: stored into every rank's arena (NVLink peer
 // stores for the others) when tensor parallel.
 __device__ __forceinline__ void st_word_all(const Control &c, Word *p, float v, unsigned tag) {
+    if (c.withhold && tag == c.withhold_tag) return;  // an injected fault: this phase publishes nothing
     if (c.ranks == 1) {
         st_word(p, v, tag);
         return;
@@ -218,7 +227,7 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 
 // Bounded wait on one phase of an mbarrier.  Gives up when another wait has
 // already recorded an error, when the compute warps stopped (`watch_abort`),
-// or after kWaitLimitNs (recording 1000 + phase).
+// or after wait_limit(st) (recording 1000 + phase).
 __device__ bool wait_bar(unsigned long long *bar, int parity, StepState *st, const Control &c, int phase,
                          bool watch_abort) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -231,7 +240,7 @@ __device__ bool wait_bar(unsigned long long *bar, int parity, StepState *st, con
             const uint64_t now = global_ns();
             if (!start) {
                 start = now;
-            } else if (now - start > kWaitLimitNs) {
+            } else if (now - start > wait_limit(st)) {
                 atomicCAS(&st->error, 0, 1000 + phase);
                 return false;
             }
@@ -267,7 +276,7 @@ __device__ __forceinline__ bool read_words_tagged(Addr addr, TagOf tag_of, float
             const uint64_t now = global_ns();
             if (!start) {
                 start = now;
-            } else if (now - start > kWaitLimitNs) {
+            } else if (now - start > wait_limit(st)) {
                 atomicCAS(&st->error, 0, 1000 + phase);
                 return false;
             }
@@ -356,7 +365,7 @@ __device__ void produce(const StepControl &ctl, bool need_head, int head_phase, 
     const uint64_t start = global_ns();
     for (int j = max(tail, issued - kQueue); j < issued; ++j) {
         while (!mbar_wait_sleep(&c.full[j % kQueue], (j / kQueue) & 1))
-            if (global_ns() - start > kWaitLimitNs) return;
+            if (global_ns() - start > wait_limit(st)) return;
     }
 }
 
@@ -388,7 +397,7 @@ __device__ bool wait_group(Control &c, int first, int count, StepState *st, int 
 
 // ---- grid barrier ------------------------------------------------------------------
 // Release-add arrival (cumulative over the CTA's writes ordered by the compute
-// barrier), acquire polling by thread 0, bounded by kWaitLimitNs.  `during`
+// barrier), acquire polling by thread 0, bounded by wait_limit(st).  `during`
 // runs in every compute thread after the arrival, overlapping the wait.
 template <typename During>
 __device__ bool grid_barrier(StepState *st, unsigned long long target, int phase, Control &c, During during) {
@@ -408,7 +417,7 @@ __device__ bool grid_barrier(StepState *st, unsigned long long target, int phase
                 const uint64_t now = global_ns();
                 if (!start) {
                     start = now;
-                } else if (now - start > kWaitLimitNs) {
+                } else if (now - start > wait_limit(st)) {
                     atomicCAS(&st->error, 0, 1000 + phase);
                     ok = 0;
                     break;
@@ -1500,6 +1509,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             c.wait_ns = 0;
             c.late = 0;
             c.ranks = ctl.ranks;
+            c.withhold = ctl.withhold_phase >= 0;
+            c.withhold_tag = ctl.tag_base + static_cast<unsigned>(ctl.withhold_phase);
             c.arena = ctl.arena;
             for (int j = 0; j < kMaxRanks; ++j) c.peers[j] = ctl.peers[j];
         }
@@ -1605,7 +1616,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
                         for (;;) {
                             w[q] = ld_word(ctl.best_slots + 4 * j + q);
                             if (word_ok(w[q], tag)) break;
-                            if (global_ns() - start > kWaitLimitNs) {
+                            if (global_ns() - start > wait_limit(st)) {
                                 atomicCAS(&st->error, 0, 1000 + nphases);
                                 break;
                             }

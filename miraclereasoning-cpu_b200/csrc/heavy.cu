@@ -532,6 +532,7 @@ struct ExpertArgs {
     size_t flags_offset;
     unsigned long long tag;        // this MoE step's flag value
     int *err;                      // a bounded wait gave up
+    unsigned long long wait_ns;    // how long the flag wait may last
 };
 
 // Expert id of slot `slot` (routed slots in rank order, then the shared
@@ -621,7 +622,7 @@ __global__ void k_expert_combine(ExpertArgs a, const float *weights, float share
                     unsigned long long v;
                     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a.flags + j) : "memory");
                     if (v >= a.tag) break;
-                    if (global_time_ns() - start > kHeavyWaitNs) {
+                    if (global_time_ns() - start > a.wait_ns) {
                         atomicExch(a.err, 1);
                         ok = 0;
                         break;
@@ -717,6 +718,8 @@ struct HeavyEngine {
     unsigned long long *counters = nullptr;  // [KVH] ready, [KVH] done, [1] router blocks
     std::vector<float *> k_bsum, v_bsum;
     unsigned long long attn_seq = 0, route_seq = 0;
+    unsigned long long wait_ns = kHeavyWaitNs;  // bounded waits (heavy_set_wait_limit)
+    bool withhold = false;                      // fault injection (heavy_inject_fault)
     bool streamable = false;                 // every projection's rows are whole 16-byte chunks
     // tracing (heavy_trace_token): one stamp after every kernel of a token step
     unsigned long long *trace = nullptr;
@@ -1015,6 +1018,16 @@ void heavy_destroy(HeavyEngine *e) {
     delete e;
 }
 
+int heavy_set_wait_limit(HeavyEngine *e, unsigned long long nanoseconds) {
+    e->wait_ns = nanoseconds;
+    return MR_OK;
+}
+
+int heavy_inject_fault(HeavyEngine *e, bool on) {
+    e->withhold = on;
+    return MR_OK;
+}
+
 int heavy_reset(HeavyEngine *e) {
     MR_CUDA_TRY(cudaMemset(e->counters, 0, (2 * static_cast<size_t>(e->KVH) + 1) * sizeof(unsigned long long)));
     MR_CUDA_TRY(cudaMemset(e->err, 0, sizeof(int)));
@@ -1062,6 +1075,7 @@ int launch_stream(HeavyEngine &e, stream::Args a) {
     MR_REQUIRE(slots >= 2, "streaming GEMV: %zu bytes of inputs leave no room for the weight ring", fixed);
     // a whole number of slots per consumer warp (see k_stream)
     a.probe = next_probe(e);
+    a.wait_ns = e.wait_ns;
     a.slots = std::min({slots, stream::kMaxSlots, e.stream_slots[a.mode]});
     MR_REQUIRE(a.residual == 0 || a.nseg == 1, "streaming GEMV: a residual launch has one matrix");
     a.err = e.err;
@@ -1163,6 +1177,8 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             aa.out = e->attn;
             aa.err = e->err;
             aa.probe = next_probe(*e);
+            aa.wait_ns = e->wait_ns;
+            aa.withhold = e->withhold;
             if (int rc = launch(attn::k_sparse_attention, e->KVH * (e->attn_chunks + 1), attn::kThreads, attn_smem, s,
                                 aa))
                 return rc;
@@ -1284,6 +1300,7 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             ea.rank = e->rank;
             ea.ranks = e->ranks;
             ea.err = e->err;
+            ea.wait_ns = e->wait_ns;
             if (e->ranks > 1) {  // this step's half of the arena (the other half: the step before)
                 ea.tag = ++e->moe_tag;
                 ea.out_offset = (ea.tag & 1) * e->out_bytes;
@@ -1388,9 +1405,9 @@ int heavy_status(const HeavyEngine *e) {
     MR_CUDA_TRY(cudaMemcpy(&err, e->err, sizeof(int), cudaMemcpyDeviceToHost));
     switch (err) {
         case 0: return MR_OK;
-        case 1: return set_error(MR_ERR_TIMEOUT, "expert parallel: a rank's expert rows did not arrive within 2 s");
-        case 2: return set_error(MR_ERR_TIMEOUT, "weight stream: a bulk copy did not land within 2 s");
-        case 3: return set_error(MR_ERR_TIMEOUT, "sparse attention: a key / value row did not arrive within 2 s");
+        case 1: return set_error(MR_ERR_TIMEOUT, "expert parallel: a rank's expert rows did not arrive within the wait limit");
+        case 2: return set_error(MR_ERR_TIMEOUT, "weight stream: a bulk copy did not land within the wait limit");
+        case 3: return set_error(MR_ERR_TIMEOUT, "sparse attention: a key / value row did not arrive within the wait limit");
         case 4: return set_error(MR_ERR_CUDA, "expert routing chose an id outside the expert table (non-finite router "
                                               "logits?)");
         default: return set_error(MR_ERR_TIMEOUT, "heavy-medium-2.0: device wait timed out (code %d)", err);

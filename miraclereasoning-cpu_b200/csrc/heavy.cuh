@@ -23,6 +23,11 @@ int heavy_status(const HeavyEngine *e);
 void heavy_destroy(HeavyEngine *e);
 // A new sequence: zeroes the device counters of the fused kernels and the error word.
 int heavy_reset(HeavyEngine *e);
+// How long the kernels' bounded waits last (default 2 s).
+int heavy_set_wait_limit(HeavyEngine *e, unsigned long long nanoseconds);
+// Fault injection for tests: while on, the attention units do not count their
+// key / value rows, so the units that need the new row wait until their limit.
+int heavy_inject_fault(HeavyEngine *e, bool on);
 
 // float32 log1p(d) for distances d = 0 .. context-1, as the host computes them
 // (the reference applies NumPy's float32 log1p, model.py:221-222).

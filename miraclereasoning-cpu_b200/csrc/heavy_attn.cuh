@@ -34,7 +34,6 @@ constexpr int kPad = kChunk + 1;  // transposed tile row: column t of key row j 
 constexpr int kMaxG = 8;        // query heads per KV head
 constexpr int kMaxDim = 128;
 constexpr int kMergeBatch = 32;
-constexpr uint64_t kWaitNs = 2000000000ull;
 
 struct Args {
     const float *q;                      // [H * d] raw queries
@@ -57,15 +56,19 @@ struct Args {
     float *out;                          // [H * d]
     int *err;
     unsigned long long *probe;           // tracing only (heavy.cu probe), else NULL
+    unsigned long long wait_ns;          // how long the key / value wait may last
+    int withhold;                        // fault injection: the units do not count their rows
 };
 
-__device__ __forceinline__ bool wait_count(const unsigned long long *c, unsigned long long target, int *err) {
+__device__ __forceinline__ bool wait_count(const unsigned long long *c, unsigned long long target, int *err,
+                                           uint64_t limit) {
     const uint64_t start = global_time_ns();
     for (;;) {
         unsigned long long v;
         asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(c) : "memory");
         if (v >= target) return true;
-        if (global_time_ns() - start > kWaitNs) {
+        if (*reinterpret_cast<volatile int *>(err)) return false;  // another wait already gave up
+        if (global_time_ns() - start > limit) {
             atomicCAS(err, 0, 3);
             return false;
         }
@@ -227,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_sparse_attention(Args a) {
     __threadfence();  // each writer's rows are visible device-wide before the count goes up
     __syncthreads();
     if (threadIdx.x == 0) {
-        atomicAdd(&a.ready[kh], 1ull);
+        if (!a.withhold) atomicAdd(&a.ready[kh], 1ull);
         probe(a.probe, kProbeStaged);
     }
     // 2. the group's queries, normalised and rotated
@@ -241,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_sparse_attention(Args a) {
     const bool needs_new = block_unit || (newest >= t0 && newest < t0 + kChunk);
     bool ok = true;
     if (needs_new) {
-        if (threadIdx.x == 0) wait_count(&a.ready[kh], a.seq * units, a.err);
+        if (threadIdx.x == 0) wait_count(&a.ready[kh], a.seq * units, a.err, a.wait_ns);
         __syncthreads();
         ok = !*reinterpret_cast<volatile int *>(a.err);
         if (ok) {

@@ -38,7 +38,6 @@ constexpr int kSlotBytes = 16384;
 constexpr int kMaxSlots = 12;
 constexpr int kMaxSegs = 12;
 constexpr int kMaxPieceRows = 4;
-constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: a copy that never lands is an error, not a hang
 
 enum Mode { kPlain = 0, kSwiglu = 1, kDown = 2 };
 
@@ -74,6 +73,7 @@ struct Args {
     float *xres;                   // kDown: x += scale * combine
     int *err;
     unsigned long long *probe;     // tracing only (heavy.cu probe), else NULL
+    unsigned long long wait_ns;    // how long a bounded wait may last
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -91,13 +91,13 @@ __device__ __forceinline__ bool bar_try(unsigned long long *b, int parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait on one phase; false (and *err set) after kWaitNs.
-__device__ __forceinline__ bool bar_wait(unsigned long long *b, int parity, int *err) {
+// Bounded wait on one phase; false (and *err set) after `limit` ns.
+__device__ __forceinline__ bool bar_wait(unsigned long long *b, int parity, int *err, uint64_t limit) {
     if (bar_try(b, parity)) return true;
     const uint64_t start = global_time_ns();
     for (;;) {
         if (bar_try(b, parity)) return true;
-        if (global_time_ns() - start > kWaitNs) {
+        if (global_time_ns() - start > limit) {
             atomicCAS(err, 0, 2);
             return false;
         }
@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(Args a) {
         auto issue = [&](int n, const Piece &p) {
             if (!ok) return;
             const int s = n % S;
-            if (n >= S && !bar_wait(&empty[s], ((n / S) - 1) & 1, a.err)) {
+            if (n >= S && !bar_wait(&empty[s], ((n / S) - 1) & 1, a.err, a.wait_ns)) {
                 ok = false;
                 return;
             }
@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(Args a) {
         // every copy issued must land before the CTA exits (the consumers have
         // normally waited for them all; after an error, wait here, bounded)
         for (int n = max(0, issued - S); n < issued; ++n)
-            if (!bar_wait(&full[n % S], (n / S) & 1, a.err)) break;
+            if (!bar_wait(&full[n % S], (n / S) & 1, a.err, a.wait_ns)) break;
         return;
     }
 
@@ -408,13 +408,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(Args a) {
         if (*issued_count <= n) {  // piece n's phase is armed only once it is issued
             const uint64_t start = global_time_ns();
             while (*issued_count <= n)
-                if (global_time_ns() - start > kWaitNs) {
+                if (global_time_ns() - start > a.wait_ns) {
                     atomicCAS(a.err, 0, 2);
                     ok = false;
                     return;
                 }
         }
-        if (!bar_wait(&full[s], (n / S) & 1, a.err)) {
+        if (!bar_wait(&full[s], (n / S) & 1, a.err, a.wait_ns)) {
             ok = false;
             return;
         }

@@ -54,3 +54,23 @@ def test_tensor_parallel_decode_matches_single_gpu(tmp_path, config, ranks):
     assert result["max_abs_diff"] <= 2e-5 * max(1.0, result["scale"])
     if config == "heavy_small":  # the same kernels compute each expert, wherever it runs
         assert result["max_abs_diff"] == 0.0
+
+
+def test_a_rank_that_skips_a_step_makes_the_other_time_out(tmp_path):
+    """Two ranks decode one sequence; rank 1 stays alive but skips one decode
+    call.  Rank 0's bounded waits for rank 1's words run out: its call raises
+    MR_ERR_TIMEOUT quickly, the model latches until reset(), and both ranks
+    release their models in order and exit cleanly (tests/tp_worker.py
+    run_failure).  No GPU is faulted; NVLS is off."""
+    if GPUS < 2:
+        pytest.skip("needs 2 GPUs")
+    out = tmp_path / "fail.json"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29611",
+           str(REPO / "tests" / "tp_worker.py"), str(out), "fail", "0"]
+    proc = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=420)
+    assert proc.returncode == 0, proc.stdout[-2000:] + proc.stderr[-4000:]
+    result = json.loads(out.read_text())
+    assert result["code"] == 4, result  # MR_ERR_TIMEOUT
+    assert result["seconds"] < 30.0 and result["latched"], result

@@ -44,11 +44,56 @@ def run(model, prompt, steps):
     return tokens, np.stack(logits)
 
 
+def run_failure(out_path, rank, world, backend, all_gather):
+    """Rank 1 stays alive but skips one decode call: rank 0's step waits for
+    rank 1's exchange words, its bounded wait runs out (200 ms) and the call
+    raises; then the ranks tear down in order (a barrier before and after the
+    models are released, so no rank frees its arena while a peer's kernel
+    could still store into it)."""
+    import gc
+    import time
+    native = importlib.import_module(PKG + "._native")
+    config = syn.config_for("nano17")
+    model = MiracleModel.synthetic(config, stored="BF16", backend=backend, context_length=256,
+                                   tensor_parallel=(rank, world, all_gather))
+    native.call("mr_model_set_wait_limit", model._handle, 200_000_000)
+    prompt = syn.prompt_ids(config.vocab_size, 8, seed=3).tolist()
+    token = int(np.argmax(model.prefill(prompt)))
+    token = int(np.argmax(model.decode(token)))  # one step together
+    dist.barrier()
+    outcome = {"rank1_skipped": True}
+    if rank == 0:
+        t0 = time.perf_counter()
+        try:
+            model.decode(token)
+            outcome.update(code=0, message="no error")
+        except native.CUDAError as exc:
+            outcome.update(code=exc.code, message=str(exc))
+        outcome["seconds"] = time.perf_counter() - t0
+        try:
+            model.decode(token)
+        except RuntimeError as exc:
+            outcome["latched"] = "reset" in str(exc)
+    dist.barrier()  # tear down in order
+    del model
+    gc.collect()
+    dist.barrier()
+    if rank == 0:
+        Path(out_path).write_text(json.dumps(outcome))
+    dist.destroy_process_group()
+
+
 def main():
     out_path, config_name, steps = sys.argv[1], sys.argv[2], int(sys.argv[3])
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     backend = CUDABackend(device_index=int(os.environ.get("LOCAL_RANK", "0")))
+    if config_name == "fail":
+        def gather(data):
+            items = [None] * world
+            dist.all_gather_object(items, data)
+            return items
+        return run_failure(out_path, rank, world, backend, gather)
     config = small_heavy() if config_name == "heavy_small" else syn.config_for(config_name)
     prompt = syn.prompt_ids(config.vocab_size, 40, seed=3).tolist()
     context = 1024
