@@ -176,6 +176,15 @@ MR_API int mr_model_destroy(mr_model *model);
  * of the host memory. */
 MR_API int mr_model_load_tensor(mr_model *model, const char *name, int dtype, int ndim,
                                 const int64_t *shape, const void *host);
+
+/* The same, read by the library straight from a checkpoint file: `bytes of
+ * the tensor` starting at byte `offset` of the file at `path` (a safetensors
+ * data span), through two page-locked 64 MB buffers, each read (pread) while
+ * the other is copied to HBM.  Nothing is widened or held on the host.
+ * Replaces the reference's mmap + widening read of a safetensors tensor
+ * (weights.py:58-61, 64-74) on the way to HBM residency. */
+MR_API int mr_model_load_file(mr_model *model, const char *name, int dtype, int ndim, const int64_t *shape,
+                              const char *path, uint64_t offset);
 /* Synthetic benchmark weights generated on the device (no host copy): BF16
  * values of the counter-hash generator of synthetic.py (seed, tensor_index,
  * scale = float32(std / 65536)); scale 0 fills every element with fill.  No

@@ -101,6 +101,7 @@ SIGNATURES = {
     "mr_model_trace_decode": (_I, [_P, _I, C.POINTER(C.c_uint64), _I, _IP, _IP]),
     "mr_attention_static_scratch": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I]),
     "mr_model_set_wait_limit": (_I, [_P, C.c_uint64]),
+    "mr_model_load_file": (_I, [_P, C.c_char_p, _I, _I, C.POINTER(C.c_int64), C.c_char_p, C.c_uint64]),
     "mr_model_inject_fault": (_I, [_P, _I]),
     "mr_model_linear": (_I, [_P, C.c_char_p, _P, _I, _P]),
     "mr_model_tensor_rows": (_I, [_P, C.c_char_p, C.c_int64, C.c_int64, _P]),

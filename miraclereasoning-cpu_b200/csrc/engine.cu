@@ -14,6 +14,9 @@
 #include <string>
 #include <vector>
 
+#include <fcntl.h>
+#include <unistd.h>
+
 #include "engine.cuh"
 #include "heavy.cuh"
 #include "prefill.cuh"
@@ -112,6 +115,9 @@ struct mr_model {
     bool op_path = false;  // no decode plan: the token step runs on the host over the op kernels
     HeavyEngine *heavy = nullptr;  // heavy-medium-2.0: the token step as kernel launches (heavy.cu)
     unsigned long long wait_limit_ns = 0;  // device waits give up after this (0: the kernels' 2 s)
+    // mr_model_load_file: two page-locked staging buffers and the copy out of each
+    unsigned char *staging[2] = {nullptr, nullptr};
+    cudaEvent_t staged[2] = {nullptr, nullptr};
     int withhold_phase = -1;               // fault injection for tests (mr_model_inject_fault)
     int position = 0;
     int grid = 0;
@@ -1094,6 +1100,10 @@ int mr_model_destroy(mr_model *m) {
     if (m->h_ids) cudaFreeHost(m->h_ids);
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->ev1) cudaEventDestroy(m->ev1);
+    for (int i = 0; i < 2; ++i) {
+        if (m->staging[i]) cudaFreeHost(m->staging[i]);
+        if (m->staged[i]) cudaEventDestroy(m->staged[i]);
+    }
     mr_context *ctx = m->ctx;
     delete m;
     mr::context_release(ctx);
@@ -1108,6 +1118,55 @@ int mr_model_load_tensor(mr_model *m, const char *name, int dtype, int ndim, con
     int rc = check_tensor(m, name, dtype, ndim, shape, &t);
     if (rc) return rc;
     MR_CUDA_TRY(cudaMemcpyAsync(t->ptr, host, t->bytes, cudaMemcpyHostToDevice, m->ctx->stream));
+    MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    return MR_OK;
+}
+
+namespace {
+constexpr size_t kStagingBytes = size_t(64) << 20;
+
+// Closes a file descriptor on every return path.
+struct FileHandle {
+    int fd = -1;
+    ~FileHandle() {
+        if (fd >= 0) close(fd);
+    }
+};
+}  // namespace
+
+int mr_model_load_file(mr_model *m, const char *name, int dtype, int ndim, const int64_t *shape, const char *path,
+                       uint64_t offset) {
+    MR_REQUIRE(m && path, "NULL argument");
+    MR_CUDA_TRY(cudaSetDevice(m->ctx->device));
+    TensorSlot *t = nullptr;
+    int rc = check_tensor(m, name, dtype, ndim, shape, &t);
+    if (rc) return rc;
+    for (int i = 0; i < 2; ++i) {
+        if (!m->staging[i]) MR_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void **>(&m->staging[i]), kStagingBytes,
+                                                      cudaHostAllocDefault));
+        if (!m->staged[i]) MR_CUDA_TRY(cudaEventCreateWithFlags(&m->staged[i], cudaEventDisableTiming));
+    }
+    FileHandle file;
+    file.fd = open(path, O_RDONLY | O_CLOEXEC);
+    MR_REQUIRE(file.fd >= 0, "%s: cannot open %s", name, path);
+    posix_fadvise(file.fd, static_cast<off_t>(offset), static_cast<off_t>(t->bytes), POSIX_FADV_SEQUENTIAL);
+    // chunk i is read into buffer i % 2 while chunk i - 1 is copied to HBM from the other one
+    size_t done = 0;
+    for (int i = 0; done < t->bytes; ++i) {
+        const int b = i & 1;
+        const size_t n = std::min(kStagingBytes, t->bytes - done);
+        MR_CUDA_TRY(cudaEventSynchronize(m->staged[b]));  // the copy out of this buffer (chunk i - 2) is done
+        for (size_t got = 0; got < n;) {
+            const ssize_t r = pread(file.fd, m->staging[b] + got, n - got, static_cast<off_t>(offset + done + got));
+            MR_REQUIRE(r > 0, "%s: %s ends before the tensor's %zu bytes at offset %llu", name, path, t->bytes,
+                       static_cast<unsigned long long>(offset));
+            got += static_cast<size_t>(r);
+        }
+        MR_CUDA_TRY(cudaMemcpyAsync(static_cast<unsigned char *>(t->ptr) + done, m->staging[b], n,
+                                    cudaMemcpyHostToDevice, m->ctx->stream));
+        MR_CUDA_TRY(cudaEventRecord(m->staged[b], m->ctx->stream));
+        done += n;
+    }
     MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
     return MR_OK;
 }

@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import ctypes as C
 import json
+import os
 import math
 from pathlib import Path
 
@@ -199,9 +200,24 @@ class MiracleModel:
         _native.call("mr_model_tp_connect", self._handle, C.cast(joined, C.c_void_p), size)
 
     def _load(self, weights):
+        """Every tensor's stored bytes into HBM: read by the engine straight from a
+        safetensors file when the mapping knows the tensor's file span, else copied
+        from a host array."""
+        span_of = getattr(weights, "file_span", None)
         for name, shape in expected_shapes(self.config).items():
-            dtype, array = stored_tensor(weights, name)
             dims = (C.c_int64 * len(shape))(*shape)
+            span = None
+            if span_of is not None:
+                try:
+                    span = span_of(name)
+                except (AttributeError, KeyError):
+                    span = None
+            if span is not None:
+                path, offset, _, dtype = span
+                _native.call("mr_model_load_file", self._handle, name.encode(), dtype, len(shape), dims,
+                             os.fsencode(path), offset)
+                continue
+            dtype, array = stored_tensor(weights, name)
             _native.call("mr_model_load_tensor", self._handle, name.encode(), dtype, len(shape), dims,
                          array.ctypes.data)
 

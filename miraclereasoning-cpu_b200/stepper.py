@@ -1,11 +1,13 @@
-"""Host-driven token step for the families the decode engine does not plan.
+"""Host-driven token step for the two paths the device engines do not plan:
+flashnano-1.6 (chunk relays) and FlashLighting 2.0 with memory slots (latent
+attention with weighted compaction).  Neither is a BASELINE configuration;
+FlashLighting without memory slots runs on the decode kernel and Heavy Medium
+on its device token step (csrc/heavy.cu).
 
-flashnano-1.6 (chunk relays), FlashLighting 2.0 (latent attention) and Heavy
-Medium 2.0 (sparse long-context attention + adaptive MoE) run one token the way
-the reference's ``MiracleModel._step`` does (miracle_reasoning/model.py:
-118-285): the host sequences the op kernels (csrc/ops.cu, each the reference's
-kernels.cl work item restated in CUDA) and makes the discrete decisions
-(block top-k, expert routing, latent compaction) with the same float32 NumPy
+One token runs the way the reference's ``MiracleModel._step`` does
+(miracle_reasoning/model.py:95-190, 257-285): the host sequences the op
+kernels (csrc/ops.cu, each the reference's kernels.cl work item restated in
+CUDA) and makes the latent compaction decision with the same float32 NumPy
 expressions.  What changes is where the weights live: they stay resident in
 HBM in their stored dtype, and every projection reads them there
 (``mr_model_linear``, bit-identical to the reference's linear over widened
@@ -13,20 +15,19 @@ weights).  The op kernels reproduce the reference's per-element arithmetic, so
 logits and decisions follow the reference's.
 
 Each step records its discrete decisions in ``decisions`` (one dict per layer:
-``topk``, ``experts``, ``expert_weights``, ``latent_positions``,
-``memory_size``), which the parity tests compare with the reference's.
+``latent_positions``, ``memory_size``), which the parity tests compare with
+the reference's.
 """
 from __future__ import annotations
 
 import ctypes as C
-import math
 
 import numpy as np
 
 from . import _native
 from .weights import expected_shapes
 
-FAMILIES = ("flashnano-1.6", "flashlighting-2.0", "heavy-medium-2.0")
+FAMILIES = ("flashnano-1.6", "flashlighting-2.0")
 
 
 class Ring:
@@ -53,7 +54,7 @@ class Ring:
 
 
 class OpStepper:
-    """One sequence of a flashnano-1.6 / FlashLighting / Heavy Medium model."""
+    """One sequence of a flashnano-1.6 model or of a FlashLighting model with memory slots."""
 
     def __init__(self, model):
         self.model, self.config, self.b = model, model.config, model.backend
@@ -215,78 +216,6 @@ class OpStepper:
         self._note("memory_size", memory_size)
         return self.linear(attended, prefix + "o")
 
-    # Heavy Medium sparse long-context attention (model.py:192-229) --------------------
-    def heavy_attention(self, x, prefix, state, position):
-        b, c = self.b, self.config
-        query = self.norm(self.linear(x, prefix + "q"), None, c.head_dim, 1e-6)
-        kv = self.linear(self.linear(x, prefix + "latent"), prefix + "kv_up")
-        width = c.kv_heads * c.head_dim
-        key, value = b.empty((1, width)), b.empty((1, width))
-        b.copy(kv, key, count=width)
-        b.copy(kv, value, source_offset=width, count=width)
-        query = self.rotate(query, position, c.query_heads)
-        key = self.rotate(self.norm(key, None, c.head_dim, 1e-6), position, c.kv_heads)
-        ring = state.get("ring")
-        if ring is None:
-            ring = state["ring"] = Ring(b, self.context_length, width)
-        ring.append(b, key, value)
-        length = min(c.window, ring.count)
-        start = ring.count - length
-        geometry = c.source["long_context"]
-        block = geometry["global_block_size"]
-        blocks = (ring.count + block - 1) // block
-        mean_keys, mean_values = b.empty((blocks, width)), b.empty((blocks, width))
-        for src, dst in ((ring.k, mean_keys), (ring.v, mean_values)):
-            b.run("block_means", (width, blocks), src, dst, ring.count, width, block)
-        scores = b.empty((c.query_heads, length + blocks))
-        b.run("scores", (length + blocks, c.query_heads), query, ring.k, mean_keys, scores, c.query_heads,
-              c.kv_heads, c.head_dim, ring.capacity, start, length, blocks)
-        # host: distance penalty on the block columns, stable top-k per head, mask the rest
-        host = b.read(scores)
-        ends = np.minimum((np.arange(blocks) + 1) * block - 1, self.position)
-        slope = np.float32(geometry.get("alibi_slope_scale", 0.015) / math.sqrt(c.head_dim))
-        host[:, length:] -= slope * np.log1p((self.position - ends).astype(np.float32))
-        slots = min(geometry["global_slots"], blocks)
-        rank = np.argsort(-host[:, length:], axis=1, kind="stable")
-        for h in range(c.query_heads):
-            host[h, length + rank[h, slots:]] = -np.inf
-        self._note("topk", [np.flatnonzero(np.isfinite(row)).tolist() for row in host[:, length:]])
-        attended = b.mix(b.softmax(b.upload(host)), ring.v, c.query_heads, c.kv_heads, c.head_dim, start, length,
-                         mean_values, blocks)
-        return self.linear(attended, prefix + "o")
-
-    # Heavy Medium adaptive MoE (model.py:231-255) -------------------------------------
-    def moe(self, x, prefix):
-        b, c, s = self.b, self.config, self.config.source
-        coarse = b.read(self.linear(x, prefix + "router.coarse.weight"))[0]
-        fine = b.read(self.linear(x, prefix + "router.fine.weight"))[0]
-        coarse += self.host(prefix + "router.coarse.bias") + self.host(prefix + "router.group_bias")
-        fine += self.host(prefix + "router.fine.bias") + self.host(prefix + "router.expert_bias")
-        experts, groups = s["routed_experts"], s["router_groups"]
-        per_group = (experts + groups - 1) // groups
-        group_of = np.minimum(np.arange(experts) // per_group, groups - 1)
-        logits = (fine + coarse[group_of]) / np.float32(max(s.get("router_temperature", 1.0), 1e-4))
-        probs = b.read(b.softmax(b.upload(logits.reshape(1, -1))))[0]
-        max_k, min_k = s["router_top_k_max"], s["router_top_k_min"]
-        order = np.argsort(-probs, kind="stable")[:max_k]
-        chosen = probs[order].copy()
-        confidence = chosen[0] - chosen[min(max_k - 1, 1)]
-        entropy = -(probs * np.log(np.maximum(probs, np.float32(1e-9)))).sum()
-        width = np.rint((np.float32(1) - confidence) * np.float32(2) +
-                        entropy / max(np.float32(np.log(experts)), np.float32(1)))
-        active = int(np.clip(min_k + width, min_k, max_k))
-        chosen[active:] = 0
-        chosen /= max(chosen.sum(), np.float32(1e-9))
-        self._note("experts", [int(e) for e in order[:active]])
-        self._note("expert_weights", [float(w) for w in chosen[:active]])
-        result = b.upload(np.zeros(x.shape, dtype=np.float32))
-        for expert, weight in zip(order[:active], chosen[:active]):
-            result = b.add(result, self.ffn(x, prefix + f"experts.{expert}."), float(weight))
-        for shared in range(s["shared_experts"]):
-            result = b.add(result, self.ffn(x, prefix + f"shared.{shared}."),
-                           c.residual_scale / max(s["shared_experts"], 1))
-        return result
-
     # one token (model.py:257-285) -------------------------------------------------------
     def step(self, token):
         """Run one token; returns the final-normed hidden state [1, hidden] on the device."""
@@ -297,14 +226,7 @@ class OpStepper:
         for layer, state in enumerate(self.states):
             prefix = f"layers.{layer}."
             self._layer = {}
-            if c.family == "heavy-medium-2.0":
-                loops = state.setdefault("loops", [{} for _ in range(c.inner_loop_steps)])
-                scale = c.residual_scale / math.sqrt(c.inner_loop_steps)
-                for inner in loops:
-                    attended = self.heavy_attention(self.norm(hidden, prefix + "a_norm"), prefix, inner, position)
-                    hidden = b.add(hidden, attended, scale)
-                    hidden = b.add(hidden, self.moe(self.norm(hidden, prefix + "f_norm"), prefix), scale)
-            elif c.family == "flashlighting-2.0":
+            if c.family == "flashlighting-2.0":
                 normalized = self.norm(hidden, prefix + "a_norm")
                 attended = self.lighting(normalized, prefix, state, position)
                 attention_gate = float(self.host(prefix + "attention_gate")[0])

@@ -1,72 +1,125 @@
 """Checkpoint reading, name adaptation and shape validation (host side).
 
-Keeps the reference's loading semantics (miracle_reasoning/weights.py):
-memory-mapped F32/F16/BF16 safetensors with the same header checks (14-61),
-BF16 widened by ``u16 << 16`` (64-74), sharded indexes with path containment
-(77-99), the native-checkpoint name tables (145-208), the expected shape table
-(211-245) and validation of every tensor before any device allocation
-(248-255).
+Loading semantics are the reference's (miracle_reasoning/weights.py): F32,
+F16 and BF16 safetensors only, the header checked before anything is read
+(14-61), BF16 widened exactly to float32 where float32 values are asked for
+(64-74), sharded indexes whose files must stay inside the model directory
+(77-99), native-checkpoint name tables (145-208), the expected shape table
+(211-245), and every tensor validated before any device allocation (248-255).
 
-What changes is residency: the reference widens each weight to float32 on the
-host and keeps a budgeted LRU of device copies (weights.py:258-297).  Here each
-tensor's STORED bytes (F32, F16 or BF16) are handed once to the CUDA engine,
-which keeps the whole model resident in HBM and widens in registers.
-``stored_tensor`` returns those raw bytes without widening.
+Residency differs: the reference widens each weight to float32 on the host
+and keeps a budgeted LRU of device copies (weights.py:258-297).  Here each
+tensor's STORED bytes go to the CUDA engine once and stay resident in HBM.
+For a safetensors checkpoint the engine reads them itself, straight from the
+file into HBM through page-locked double buffers (``file_span`` gives it the
+file, offset and size; ``mr_model_load_file``); other mappings hand over a
+host array of the stored bytes (``stored_tensor``).
 """
 from __future__ import annotations
 
 import json
 import math
+import os
 import struct
 from collections.abc import Mapping
+from dataclasses import dataclass
 from pathlib import Path
 
 import numpy as np
 
 # dtype codes shared with include/miracle_cuda.h (MR_DTYPE_*)
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
-_SAFETENSORS_TYPES = {"F32": ("<f4", DTYPE_F32), "F16": ("<f2", DTYPE_F16), "BF16": ("<u2", DTYPE_BF16)}
-_MAX_HEADER = 100_000_000
+# safetensors dtype -> (little-endian NumPy storage type, engine dtype code)
+_STORAGE = {"F32": ("<f4", DTYPE_F32), "F16": ("<f2", DTYPE_F16), "BF16": ("<u2", DTYPE_BF16)}
+_HEADER_LIMIT = 100_000_000
+
+
+@dataclass(frozen=True)
+class TensorEntry:
+    """One tensor of a safetensors file: its stored kind, shape and byte span
+    [begin, end) relative to the start of the data section."""
+    kind: str
+    shape: tuple
+    begin: int
+    end: int
+
+    @property
+    def storage(self):
+        return np.dtype(_STORAGE[self.kind][0])
+
+    @property
+    def code(self):
+        return _STORAGE[self.kind][1]
+
+
+def _fail(message):
+    raise ValueError(message)
+
+
+def read_safetensors_header(path):
+    """(offset of the data section, {name: TensorEntry}) of a safetensors file,
+    after checking everything the loader relies on: the header length, the
+    dtypes, shapes and offsets, that every span lies inside the file and
+    matches its shape, and that no two spans overlap."""
+    size = os.path.getsize(path)
+    with open(path, "rb") as handle:
+        head = handle.read(8)
+        if len(head) < 8:
+            _fail("Truncated safetensors header")
+        header_bytes = struct.unpack("<Q", head)[0]
+        if header_bytes > min(_HEADER_LIMIT, size - 8):
+            _fail("Invalid safetensors header length")
+        header = json.loads(handle.read(header_bytes))
+    data_start, data_size = 8 + header_bytes, size - 8 - header_bytes
+    entries = {}
+    for name, info in header.items():
+        if name == "__metadata__":
+            continue
+        kind = info["dtype"]
+        if kind not in _STORAGE:
+            _fail(f"Unsupported weight dtype {kind} in {name}; export to FP32 first")
+        shape, span = info["shape"], info["data_offsets"]
+        if not isinstance(shape, list) or not all(type(n) is int and n >= 0 for n in shape):
+            _fail(f"Invalid shape for {name}")
+        if len(span) != 2 or not all(type(n) is int for n in span):
+            _fail(f"Invalid offsets for {name}")
+        entry = TensorEntry(kind, tuple(shape), span[0], span[1])
+        if entry.begin < 0 or entry.end > data_size or \
+                entry.end - entry.begin != math.prod(entry.shape) * entry.storage.itemsize:
+            _fail(f"Invalid safetensors extent for {name}")
+        entries[name] = entry
+    ordered = sorted(entries.values(), key=lambda e: (e.begin, e.end))
+    for left, right in zip(ordered, ordered[1:]):
+        if right.begin < left.end:
+            _fail("Overlapping safetensors data")
+    return data_start, entries
+
+
+class BF16Array:
+    """BF16 weights kept as their uint16 bits; the rows asked for come back as
+    float32 (bits << 16, exact)."""
+
+    def __init__(self, bits):
+        self.data = bits
+        self.shape = bits.shape
+
+    def __getitem__(self, index):
+        widened = np.left_shift(np.asarray(self.data[index], dtype=np.uint32), np.uint32(16))
+        return widened.view(np.float32)
+
+    def __array__(self, dtype=None, copy=None):
+        values = self[...]
+        return values if dtype is None else values.astype(dtype, copy=False)
 
 
 class SafeTensors(Mapping):
-    """Memory-mapped F32/F16/BF16 safetensors file (no PyTorch needed)."""
+    """A safetensors file: stored-dtype views of one read-only memory map of
+    its data section (BF16 tensors as ``BF16Array``)."""
 
     def __init__(self, path):
         self.path = Path(path)
-        size = self.path.stat().st_size
-        with self.path.open("rb") as handle:
-            prefix = handle.read(8)
-            if len(prefix) != 8:
-                raise ValueError("Truncated safetensors header")
-            (length,) = struct.unpack("<Q", prefix)
-            if length > min(_MAX_HEADER, size - 8):
-                raise ValueError("Invalid safetensors header length")
-            metadata = json.loads(handle.read(length))
-        self.offset = 8 + length
-        self.entries = {}
-        spans = []
-        for name, entry in metadata.items():
-            if name == "__metadata__":
-                continue
-            kind = entry["dtype"]
-            if kind not in _SAFETENSORS_TYPES:
-                raise ValueError(f"Unsupported weight dtype {kind} in {name}; export to FP32 first")
-            shape, offsets = entry["shape"], entry["data_offsets"]
-            if not isinstance(shape, list) or any(type(n) is not int or n < 0 for n in shape):
-                raise ValueError(f"Invalid shape for {name}")
-            if len(offsets) != 2 or any(type(n) is not int for n in offsets):
-                raise ValueError(f"Invalid offsets for {name}")
-            start, end = offsets
-            numpy_type = _SAFETENSORS_TYPES[kind][0]
-            if start < 0 or end - start != math.prod(shape) * np.dtype(numpy_type).itemsize \
-                    or end > size - self.offset:
-                raise ValueError(f"Invalid safetensors extent for {name}")
-            self.entries[name] = (tuple(shape), kind, numpy_type, start)
-            spans.append((start, end))
-        spans.sort()
-        if any(later[0] < earlier[1] for earlier, later in zip(spans, spans[1:])):
-            raise ValueError("Overlapping safetensors data")
+        self._data_start, self.entries = read_safetensors_header(self.path)
+        self._map = None
 
     def __iter__(self):
         return iter(self.entries)
@@ -74,64 +127,71 @@ class SafeTensors(Mapping):
     def __len__(self):
         return len(self.entries)
 
-    def raw(self, key):
-        shape, _, numpy_type, start = self.entries[key]
-        return np.memmap(self.path, mode="r", offset=self.offset + start, dtype=numpy_type, shape=shape)
+    def _bytes(self):
+        if self._map is None:
+            data_size = os.path.getsize(self.path) - self._data_start
+            self._map = np.memmap(self.path, mode="r", dtype=np.uint8, offset=self._data_start,
+                                  shape=(data_size,)) if data_size else np.zeros(0, np.uint8)
+        return self._map
 
-    def __getitem__(self, key):
-        data = self.raw(key)
-        return BF16Array(data) if self.entries[key][1] == "BF16" else data
+    def raw(self, name):
+        """The tensor in its stored dtype (uint16 bits for BF16), not widened."""
+        entry = self.entries[name]
+        return self._bytes()[entry.begin:entry.end].view(entry.storage).reshape(entry.shape)
 
+    def __getitem__(self, name):
+        values = self.raw(name)
+        return BF16Array(values) if self.entries[name].kind == "BF16" else values
 
-class BF16Array:
-    """BF16 storage (uint16 bits) widened to float32 only where indexed."""
-
-    def __init__(self, data):
-        self.data, self.shape = data, data.shape
-
-    def __getitem__(self, key):
-        return (np.asarray(self.data[key], dtype=np.uint32) << 16).view(np.float32)
-
-    def __array__(self, dtype=None, copy=None):
-        widened = self[:]
-        return widened.astype(dtype, copy=False) if dtype is not None else widened
+    def file_span(self, name):
+        """(path, absolute byte offset, byte count, engine dtype code) of a tensor."""
+        entry = self.entries[name]
+        return str(self.path), self._data_start + entry.begin, entry.end - entry.begin, entry.code
 
 
 class ShardedSafeTensors(Mapping):
-    """``model.safetensors.index.json`` over several safetensors files."""
+    """``model.safetensors.index.json``: every name served by the shard file
+    the index assigns it, each shard inside the index's directory."""
 
     def __init__(self, index):
         index = Path(index)
-        self.names = json.loads(index.read_text(encoding="utf-8"))["weight_map"]
+        weight_map = json.loads(index.read_text(encoding="utf-8"))["weight_map"]
         root = index.parent.resolve()
-        self.shards = {}
-        for filename in set(self.names.values()):
+        files = {}
+        for filename in sorted(set(weight_map.values())):
             path = (root / filename).resolve()
-            if not path.is_relative_to(root):
-                raise ValueError("Safetensors shard path escapes the model directory")
-            self.shards[filename] = SafeTensors(path)
-        for key, filename in self.names.items():
-            if key not in self.shards[filename]:
-                raise ValueError(f"Shard {filename} does not contain {key}")
+            if os.path.commonpath([root, path]) != str(root):
+                _fail("Safetensors shard path escapes the model directory")
+            files[filename] = SafeTensors(path)
+        self._where = {}
+        for name, filename in weight_map.items():
+            if name not in files[filename]:
+                _fail(f"Shard {filename} does not contain {name}")
+            self._where[name] = files[filename]
+        self.names, self.shards = weight_map, files
 
     def __iter__(self):
-        return iter(self.names)
+        return iter(self._where)
 
     def __len__(self):
-        return len(self.names)
+        return len(self._where)
 
-    def __getitem__(self, key):
-        return self.shards[self.names[key]][key]
+    def __getitem__(self, name):
+        return self._where[name][name]
+
+    def file_span(self, name):
+        return self._where[name].file_span(name)
 
 
 class AliasedWeights(Mapping):
-    """Canonical names resolved through a native-checkpoint name table."""
+    """Canonical names over a checkpoint that uses its training code's names
+    (the native name tables below); every aliased tensor must exist."""
 
     def __init__(self, original, names):
+        absent = [native for native in names.values() if native not in original]
+        if absent:
+            _fail(f"Missing checkpoint tensors: {', '.join(absent[:12])}")
         self.original, self.names = original, names
-        missing = [v for v in names.values() if v not in original]
-        if missing:
-            raise ValueError(f"Missing checkpoint tensors: {', '.join(missing[:12])}")
 
     def __iter__(self):
         return iter(self.names)
@@ -139,8 +199,13 @@ class AliasedWeights(Mapping):
     def __len__(self):
         return len(self.names)
 
-    def __getitem__(self, key):
-        return self.original[self.names[key]]
+    def __getitem__(self, name):
+        return self.original[self.names[name]]
+
+    def file_span(self, name):
+        if not hasattr(self.original, "file_span"):
+            raise AttributeError("file_span")
+        return self.original.file_span(self.names[name])
 
 
 def save_safetensors(path, arrays, dtype="F32"):
