@@ -158,7 +158,7 @@ def ncu_traffic(config_name):
     summary's name: a separate capture, not measured in this run."""
     for path in sorted((REPO / "profiles").glob(f"*_{config_name}.md")):
         for line in path.read_text().splitlines():
-            if line.startswith("traffic_bytes_per_launch:"):
+            if line.startswith(("traffic_bytes_per_launch:", "traffic_bytes_per_step:")):
                 return float(line.split(":", 1)[1].strip()), f"profiles/{path.name} (ncu, separate capture)"
     return None, None
 
@@ -453,8 +453,12 @@ def run_profile_case(args):
                                                  context_length=context)
     logits = model.prefill(syn.prompt_ids(config.vocab_size, prompt_len, seed=1))
     ms = C.c_float()
+    import torch  # the profiler range (ncu --profile-from-start off) covers the decode steps only
+    backend.finish()
+    torch.cuda.profiler.start()
     _pkg("_native").call("mr_model_bench_decode", model._handle, int(np.argmax(logits)), args.profile_steps,
                          C.byref(ms))
+    torch.cuda.profiler.stop()
     print(json.dumps({"profile_case": args.config, "prompt": prompt_len, "decode_steps": args.profile_steps,
                       "position": model.position}))
     return 0
