@@ -318,7 +318,7 @@ def measure(name, args, ranks, mode, steps, warmup, sample_clocks):
     # prefill: batched on the tensor cores for BF16 models of the engine families (timed
     # after one untimed pass: workspace allocation), else token by token (timed on its only pass)
     batched = C.c_int(0)
-    if model._stepper is None and not heavy:
+    if model._stepper is None:
         native.call("mr_model_set_batched_prefill", model._handle, 1, C.byref(batched))
     serial = not batched.value
     if not serial:
@@ -408,7 +408,11 @@ def measure(name, args, ranks, mode, steps, warmup, sample_clocks):
                 "positions": f"{e2e_first}..{e2e_first + e2e_steps - 1}",
                 "path": "MiracleModel.decode (Python API -> C ABI), logits to host each step"},
         "prefill": {"value": round(sequences * len(prompt) / prefill_s, 2), "unit": "tok/s", "tokens": len(prompt),
-                    "note": ("batched prefill: tensor-core GEMMs (BF16 weights x FP32 activations split in three "
+                    "note": ("batched prefill (heavy_prefill.cuh): tcgen05 GEMMs (BF16 weights x FP32 activations "
+                             "split in three BF16 parts), routed experts as grouped GEMMs over the tokens sorted "
+                             "by expert, sparse attention per token; logits of the last token to host"
+                             if batched.value and heavy else
+                             "batched prefill: tensor-core GEMMs (BF16 weights x FP32 activations split in three "
                              "BF16 parts) + causal attention over the chunk, logits of the last token to host"
                              if batched.value else
                              "prompt token by token through the device token step (heavy.cu kernels)"

@@ -819,12 +819,34 @@ int host_argmax(const float *v, int n) {  // numpy.argmax: the first maximum
 
 // heavy-medium-2.0: n tokens through the device token step; the logits of
 // every token (return_all) or of the last one are copied to `out`.
+constexpr int kHeavyChunk = 4096;  // tokens per Heavy Medium batched chunk
 int heavy_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
     const int V = m->cfg.vocab_size;
     for (int i = 0; i < n; ++i) MR_REQUIRE(ids[i] >= 0 && ids[i] < V, "input token is outside the vocabulary");
     MR_REQUIRE(m->position + n <= m->cfg.context_length,
                "input would exceed context_length; reset or allocate a larger context");
-    for (int i = 0; i < n; ++i) {
+    // a prompt of several tokens: batched chunks (GEMMs on tcgen05), else the token step
+    int first = 0;
+    if (n > 1 && m->prefill_on && heavy_batchable(m->heavy)) {
+        for (; first < n;) {
+            const int T = std::min(kHeavyChunk, n - first);
+            int rc = heavy_prefill(m->heavy, ids + first, T, m->position, return_all != 0);
+            if (!rc && (return_all || first + T == n)) {
+                const size_t rows = return_all ? T : 1;
+                const cudaError_t err =
+                    cudaMemcpyAsync(out + (return_all ? static_cast<size_t>(first) * V : 0), heavy_prefill_logits(m->heavy),
+                                    sizeof(float) * V * rows, cudaMemcpyDeviceToHost, m->ctx->stream);
+                if (err != cudaSuccess) rc = cuda_error(err, "logits read");
+            }
+            if (rc) {
+                m->failed = true;
+                return rc;
+            }
+            m->position += T;
+            first += T;
+        }
+    }
+    for (int i = first; i < n; ++i) {
         int rc = heavy_token(m->heavy, ids[i], m->position);
         if (!rc && (return_all || i == n - 1)) {
             const cudaError_t err = cudaMemcpyAsync(out + (return_all ? (size_t)i * V : 0), heavy_logits(m->heavy),
@@ -1385,7 +1407,7 @@ int mr_model_set_batched_prefill(mr_model *m, int enable, int *available) {
     MR_REQUIRE(enable >= 0 && enable <= 2, "enable must be 0, 1 or 2");
     m->prefill_on = enable != 0;
     m->pw.tcgen05 = enable != 2;
-    if (available) *available = m->prefill_ok ? 1 : 0;
+    if (available) *available = (m->heavy ? heavy_batchable(m->heavy) : m->prefill_ok) ? 1 : 0;
     return MR_OK;
 }
 

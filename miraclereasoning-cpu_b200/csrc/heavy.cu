@@ -39,10 +39,12 @@
 #include <cmath>
 #include <cstring>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "common.cuh"
 #include "heavy.cuh"
+#include "prefill.cuh"
 
 namespace mr {
 
@@ -54,8 +56,8 @@ constexpr int kGemvThreads = 256;  // 8 warps
 constexpr int kGemvRows = 8;       // rows per block (one per warp)
 constexpr int kMaxSegs = 4;
 constexpr int kMaxHeavyRanks = 8;
-constexpr uint64_t kHeavyWaitNs = 2000000000ull;
-constexpr int kStreamSmem = 227 * 1024;  // dynamic shared memory of a streaming CTA (the ring takes what is left)  // 2 s: a rank that never publishes is an error, not a hang
+constexpr uint64_t kHeavyWaitNs = 2000000000ull;  // 2 s: a rank that never publishes is an error, not a hang
+constexpr int kStreamSmem = 227 * 1024;  // dynamic shared memory of a streaming CTA (the ring takes what is left)
 
 __device__ __forceinline__ uint64_t global_time_ns() {
     uint64_t t;
@@ -454,6 +456,7 @@ __device__ void route_block(const RouteArgs &a) {
 
 #include "heavy_attn.cuh"
 #include "heavy_stream.cuh"
+#include "heavy_prefill.cuh"
 
 // The router GEMV (coarse rows, then fine rows; one row per warp, the input
 // RMSNorm(x, f_norm) staged per block, k_gemv's arithmetic) and then, in the
@@ -676,6 +679,26 @@ struct HeavyLayer {
     int expert_dtype;
 };
 
+// Workspace of the batched prompt (heavy_prefill.cuh) for chunks of up to `cap`
+// tokens, allocated on first use: activations of the chunk, the routed rows
+// sorted by expert (up to cap * max_k), the tile table, and per layer the
+// router's coarse | fine rows as one BF16 matrix and the experts' weight maps.
+struct HeavyBatch {
+    int cap = 0, kmax = 0, max_tiles = 0;
+    bool all_logits = false, ready = false;
+    std::vector<void *> buffers;     // freed on growth and with the engine
+    int *ids = nullptr, *err = nullptr;
+    float *x = nullptr, *qlat = nullptr, *kv = nullptr, *qh = nullptr, *sum_k = nullptr, *sum_v = nullptr,
+          *rlog = nullptr, *weights = nullptr, *gu = nullptr, *rout = nullptr, *sgu = nullptr, *sout = nullptr,
+          *logits = nullptr;
+    uint16_t *planes = nullptr, *gplanes = nullptr, *gsplanes = nullptr;
+    int *chosen = nullptr, *active = nullptr, *row_of = nullptr, *token_of = nullptr, *tiles = nullptr,
+        *tile_count = nullptr, *rows = nullptr;
+    // per layer, kept with the engine: router rows, expert maps (gate | up pairs, down)
+    uint16_t *router_w = nullptr;
+    unsigned char *maps_gu = nullptr, *maps_dn = nullptr;
+};
+
 struct HeavyEngine {
     mr_model *m = nullptr;
     cudaStream_t stream = nullptr;
@@ -713,7 +736,7 @@ struct HeavyEngine {
     int sm_count = 0, attn_chunks = 0;
     // ring slots per stream::Mode (plain, swiglu, down): measured at 4 to 12 slots, bytes in
     // flight pay more than room for the next kernel's CTAs beside a smaller ring
-    int stream_slots[3] = {12, 12, 8};
+    int stream_slots[3] = {12, 12, 10};
     float *attn_partial = nullptr;
     unsigned long long *counters = nullptr;  // [KVH] ready, [KVH] done, [1] router blocks
     std::vector<float *> k_bsum, v_bsum;
@@ -726,6 +749,9 @@ struct HeavyEngine {
     int trace_n = 0, trace_cap = 0;
     unsigned long long *probes = nullptr;  // kProbeSlots per probed launch (tracing)
     int probe_n = 0, probe_cap = 0;
+    // batched prompt (heavy_prefill): possible when every matrix is BF16 and the engine is alone
+    bool batchable = false;
+    HeavyBatch batch;
 };
 
 namespace {
@@ -1000,6 +1026,17 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
         }
         ok = ok && slots_total <= stream::kMaxSegs;
         e->streamable = ok;
+        // the batched prompt: BF16 matrices whose rows are whole 16-byte pieces, one engine
+        // (the routed experts of other ranks are not here), limits of its attention kernel
+        bool batch = e->ranks == 1 && e->head_dt == MR_DTYPE_BF16 && e->hidden % 8 == 0 && e->latent % 8 == 0 &&
+                     e->ffn % 8 == 0 && (e->H * e->d) % 8 == 0 && e->slots <= hp::kMaxSlots && G <= hp::kRows &&
+                     e->experts <= 256 && e->max_k <= 64;
+        for (const HeavyLayer &Ly : e->L)
+            for (const GemvSeg *g : {&Ly.q, &Ly.latent, &Ly.kv_up, &Ly.o, &Ly.coarse, &Ly.fine})
+                batch = batch && g->dtype == MR_DTYPE_BF16;
+        for (const HeavyLayer &Ly : e->L) batch = batch && Ly.expert_dtype == MR_DTYPE_BF16;
+        batch = batch && hp::attention_smem(e->d, maxblocks) <= 227 * 1024;
+        e->batchable = batch;
         for (auto kernel : {stream::k_stream<MR_DTYPE_BF16>, stream::k_stream<MR_DTYPE_F16>,
                             stream::k_stream<MR_DTYPE_F32>})
             MR_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem));
@@ -1014,6 +1051,7 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
 
 void heavy_destroy(HeavyEngine *e) {
     if (!e) return;
+    for (void *p : e->batch.buffers) cudaFree(p);
     for (void *p : e->allocations) cudaFree(p);
     delete e;
 }
@@ -1031,6 +1069,7 @@ int heavy_inject_fault(HeavyEngine *e, bool on) {
 int heavy_reset(HeavyEngine *e) {
     MR_CUDA_TRY(cudaMemset(e->counters, 0, (2 * static_cast<size_t>(e->KVH) + 1) * sizeof(unsigned long long)));
     MR_CUDA_TRY(cudaMemset(e->err, 0, sizeof(int)));
+    if (e->batch.err) MR_CUDA_TRY(cudaMemset(e->batch.err, 0, sizeof(int)));
     e->attn_seq = e->route_seq = 0;
     return MR_OK;
 }
@@ -1400,11 +1439,265 @@ void heavy_connect(HeavyEngine *e, char *const *peers) {
     for (int j = 0; j < e->ranks; ++j) e->peers[j] = peers[j];
 }
 
+
+// ---- batched prompt (heavy_prefill.cuh) ---------------------------------------------------
+namespace {
+
+void batch_release(HeavyBatch &b) {
+    for (void *p : b.buffers) cudaFree(p);
+    b = HeavyBatch{};
+}
+
+// Grows the workspace to chunks of `tokens` tokens; on first use also the
+// per-layer router matrices and expert weight maps.
+int batch_reserve(HeavyEngine &e, int tokens, bool all_logits) {
+    HeavyBatch &b = e.batch;
+    if (b.ready && b.cap >= tokens && (b.all_logits || !all_logits)) return MR_OK;
+    const int T = std::max(tokens, b.cap);
+    const bool all = all_logits || b.all_logits;
+    batch_release(b);
+    const int h = e.hidden, qd = e.H * e.d, width = e.KVH * e.d, f = e.ffn, E = e.experts, K = e.max_k;
+    const size_t R = static_cast<size_t>(T) * K;
+    b.kmax = std::max({h, qd, e.latent, f});
+    b.max_tiles = static_cast<int>(R / kBatchTileRows) + E + 1;
+    auto get = [&](size_t bytes, auto **out) -> int {
+        void *p = nullptr;
+        MR_CUDA_TRY(cudaMalloc(&p, std::max<size_t>(bytes, 256)));
+        b.buffers.push_back(p);
+        *out = static_cast<std::remove_reference_t<decltype(**out)> *>(p);
+        return MR_OK;
+    };
+    const size_t f4 = sizeof(float), u2 = sizeof(uint16_t), i4 = sizeof(int);
+    int rc = get(T * i4, &b.ids);
+    if (!rc) rc = get(i4, &b.err);
+    if (!rc) rc = get(f4 * T * h, &b.x);
+    if (!rc) rc = get(u2 * 3 * static_cast<size_t>(T) * b.kmax, &b.planes);
+    if (!rc) rc = get(f4 * T * static_cast<size_t>(qd + e.latent), &b.qlat);
+    if (!rc) rc = get(f4 * T * 2 * static_cast<size_t>(width), &b.kv);
+    if (!rc) rc = get(f4 * T * static_cast<size_t>(qd), &b.qh);
+    if (!rc) rc = get(f4 * T * static_cast<size_t>(width), &b.sum_k);
+    if (!rc) rc = get(f4 * T * static_cast<size_t>(width), &b.sum_v);
+    if (!rc) rc = get(f4 * T * static_cast<size_t>(e.groups + E), &b.rlog);
+    if (!rc) rc = get(i4 * R, &b.chosen);
+    if (!rc) rc = get(f4 * R, &b.weights);
+    if (!rc) rc = get(i4 * T, &b.active);
+    if (!rc) rc = get(i4 * R, &b.row_of);
+    if (!rc) rc = get(i4 * R, &b.token_of);
+    if (!rc) rc = get(4 * i4 * static_cast<size_t>(b.max_tiles), &b.tiles);
+    if (!rc) rc = get(i4, &b.tile_count);
+    if (!rc) rc = get(i4, &b.rows);
+    if (!rc) rc = get(u2 * 3 * R * h, &b.gplanes);
+    if (!rc) rc = get(f4 * R * 2 * f, &b.gu);
+    if (!rc) rc = get(u2 * 3 * R * f, &b.gsplanes);
+    if (!rc) rc = get(f4 * R * h, &b.rout);
+    if (!rc) rc = get(f4 * T * 2 * static_cast<size_t>(f) * std::max(1, e.shared), &b.sgu);
+    if (!rc) rc = get(f4 * T * static_cast<size_t>(h) * std::max(1, e.shared), &b.sout);
+    if (!rc) rc = get(f4 * (all ? T : 1) * static_cast<size_t>(e.vocab), &b.logits);
+    // per layer: coarse | fine router rows as one matrix, the experts' weight maps
+    const size_t router_rows = static_cast<size_t>(e.groups) + E;
+    if (!rc) rc = get(u2 * router_rows * h * e.layers, &b.router_w);
+    if (!rc) rc = get(kBatchMapBytes * 2 * E * static_cast<size_t>(e.layers), &b.maps_gu);
+    if (!rc) rc = get(kBatchMapBytes * E * static_cast<size_t>(e.layers), &b.maps_dn);
+    if (rc) {
+        batch_release(b);
+        return rc;
+    }
+    std::vector<unsigned char> gu(kBatchMapBytes * 2 * E * e.layers), dn(kBatchMapBytes * E * e.layers);
+    for (int l = 0; l < e.layers && !rc; ++l) {
+        const HeavyLayer &Ly = e.L[l];
+        uint16_t *rw = b.router_w + static_cast<size_t>(l) * router_rows * h;
+        const cudaError_t c1 = cudaMemcpyAsync(rw, Ly.coarse.w, u2 * e.groups * h, cudaMemcpyDeviceToDevice, e.stream);
+        const cudaError_t c2 =
+            cudaMemcpyAsync(rw + static_cast<size_t>(e.groups) * h, Ly.fine.w, u2 * E * h, cudaMemcpyDeviceToDevice, e.stream);
+        if (c1 != cudaSuccess || c2 != cudaSuccess) rc = set_error(MR_ERR_CUDA, "router rows copy failed");
+        for (int x = 0; x < E && !rc; ++x) {
+            const size_t at = static_cast<size_t>(l) * E + x;
+            rc = batch_weight_map(gu.data() + (2 * at) * kBatchMapBytes, Ly.h_gate[x], f, h);
+            if (!rc) rc = batch_weight_map(gu.data() + (2 * at + 1) * kBatchMapBytes, Ly.h_up[x], f, h);
+            if (!rc) rc = batch_weight_map(dn.data() + at * kBatchMapBytes, Ly.h_down[x], h, f);
+        }
+    }
+    if (!rc && (cudaMemcpy(b.maps_gu, gu.data(), gu.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemcpy(b.maps_dn, dn.data(), dn.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemset(b.err, 0, sizeof(int)) != cudaSuccess))
+        rc = set_error(MR_ERR_CUDA, "batched prompt setup failed");
+    if (!rc) rc = batch_setup();
+    if (!rc)
+        MR_CUDA_TRY(cudaFuncSetAttribute(hp::k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(hp::attention_smem(e.d, (e.context + e.block - 1) / e.block))));
+    if (rc) {
+        batch_release(b);
+        return rc;
+    }
+    b.cap = T;
+    b.all_logits = all;
+    b.ready = true;
+    return MR_OK;
+}
+
+int grid_for(size_t n, int threads = 256) {
+    return static_cast<int>(std::min<size_t>((n + threads - 1) / threads, 148 * 16));
+}
+
+}  // namespace
+
+bool heavy_batchable(const HeavyEngine *e) { return e->batchable; }
+const float *heavy_prefill_logits(const HeavyEngine *e) { return e->batch.logits; }
+
+int heavy_prefill(HeavyEngine *e, const int *ids, int T, int p0, bool all_logits) {
+    MR_REQUIRE(e->batchable, "heavy-medium-2.0: this model does not qualify for the batched prompt");
+    MR_REQUIRE(e->table_set, "heavy-medium-2.0: the distance-penalty table has not been set");
+    MR_REQUIRE(T > 0 && p0 >= 0 && p0 + T <= e->context, "positions %d .. %d outside the context", p0, p0 + T - 1);
+    for (int i = 0; i < T; ++i) MR_REQUIRE(ids[i] >= 0 && ids[i] < e->vocab, "input token is outside the vocabulary");
+    if (int rc = batch_reserve(*e, T, all_logits)) return rc;
+    HeavyBatch &b = e->batch;
+    cudaStream_t s = e->stream;
+    const int h = e->hidden, H = e->H, d = e->d, qd = H * d, lat = e->latent, KVH = e->KVH, width = KVH * d;
+    const int f = e->ffn, E = e->experts, K = e->max_k, G = H / KVH, RG = e->groups + E;
+    const size_t ps = static_cast<size_t>(b.cap) * b.kmax;           // plane strides
+    const size_t R = static_cast<size_t>(b.cap) * K;
+    const size_t gps = R * h, gsps = R * f;
+    const int ldq = qd + lat, slots_max = std::max(1, e->slots);
+    const float loop_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::sqrt((double)e->loops));
+    const float shared_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::max(e->shared, 1));
+    const int nb = (p0 + T - 1) / e->block + 1;
+    MR_CUDA_TRY(cudaMemcpyAsync(b.ids, ids, sizeof(int) * T, cudaMemcpyHostToDevice, s));
+    hp::k_embed<<<T, 256, 0, s>>>(b.ids, T, e->embed, e->embed_dt, h, b.x);
+    MR_CUDA_TRY(cudaGetLastError());
+    int rc = MR_OK;
+    for (int l = 0; l < e->layers && !rc; ++l) {
+        const HeavyLayer &Ly = e->L[l];
+        for (int loop = 0; loop < e->loops && !rc; ++loop) {
+            const size_t li = static_cast<size_t>(l) * e->loops + loop;
+            // q | latent of RMSNorm(x, a_norm); kv = W_kv_up latent
+            rc = batch_rms_planes(s, b.x, 0, T, h, h, Ly.a_norm, Ly.a_norm_dt, e->eps, b.planes, ps, b.kmax);
+            const BatchSeg ql[2] = {{Ly.q.w, qd, 0}, {Ly.latent.w, lat, qd}};
+            if (!rc) rc = batch_gemm(s, b.err, b.planes, ps, b.kmax, T, h, ql, 2, b.qlat, ldq, false, 0.f);
+            if (rc) break;
+            hp::k_split<<<grid_for(static_cast<size_t>(T) * lat), 256, 0, s>>>(b.qlat + qd, ldq, lat, T, b.planes, ps,
+                                                                               b.kmax);
+            const BatchSeg kvs = {Ly.kv_up.w, 2 * width, 0};
+            rc = batch_gemm(s, b.err, b.planes, ps, b.kmax, T, lat, &kvs, 1, b.kv, 2 * width, false, 0.f);
+            if (rc) break;
+            // queries, keys and values at the chunk's positions; block sums and means
+            hp::k_qk<<<(T * (H + 2 * KVH) * 32 + 255) / 256, 256, 0, s>>>(b.qlat, ldq, b.kv, T, p0, H, KVH, d,
+                                                                           e->split_half, e->inv_freq, b.qh, e->k_ring[li],
+                                                                           e->v_ring[li]);
+            hp::k_block_sums<<<grid_for(static_cast<size_t>((p0 + T - 1) / e->block - p0 / e->block + 1) * width * 2),
+                               256, 0, s>>>(e->k_ring[li], e->v_ring[li], T, p0, width, e->block, e->k_bsum[li],
+                                            e->v_bsum[li], e->k_mean[li], e->v_mean[li], b.sum_k, b.sum_v);
+            // sparse attention of every token -> planes of the o projection's input
+            hp::AttnArgs aa{};
+            aa.qh = b.qh;
+            aa.k_rows = e->k_ring[li];
+            aa.v_rows = e->v_ring[li];
+            aa.k_mean = e->k_mean[li];
+            aa.v_mean = e->v_mean[li];
+            aa.sum_k = b.sum_k;
+            aa.sum_v = b.sum_v;
+            aa.log1p_table = e->log1p_table;
+            aa.slope = e->slope;
+            aa.T = T;
+            aa.p0 = p0;
+            aa.H = H;
+            aa.KVH = KVH;
+            aa.d = d;
+            aa.window = e->window;
+            aa.block = e->block;
+            aa.slots = e->slots;
+            aa.slots_max = slots_max;
+            aa.nb = nb;
+            aa.planes = b.planes;
+            aa.ps = ps;
+            aa.ld = b.kmax;
+            aa.kept_last = e->kept + li * H * slots_max;
+            const int QT = hp::kRows / G;
+            hp::k_attention<<<dim3((T + QT - 1) / QT, KVH), hp::kThreads, hp::attention_smem(d, nb), s>>>(aa);
+            MR_CUDA_TRY(cudaGetLastError());
+            // x += s W_o attended
+            const BatchSeg os = {Ly.o.w, h, 0};
+            rc = batch_gemm(s, b.err, b.planes, ps, b.kmax, T, qd, &os, 1, b.x, h, true, loop_scale);
+            // router logits of RMSNorm(x, f_norm) and the routing of every token
+            if (!rc) rc = batch_rms_planes(s, b.x, 0, T, h, h, Ly.f_norm, Ly.f_norm_dt, e->eps, b.planes, ps, b.kmax);
+            const BatchSeg rs = {b.router_w + static_cast<size_t>(l) * RG * h, RG, 0};
+            if (!rc) rc = batch_gemm(s, b.err, b.planes, ps, b.kmax, T, h, &rs, 1, b.rlog, RG, false, 0.f);
+            if (rc) break;
+            hp::RouteRows rr{};
+            rr.ra.router = b.rlog;
+            rr.ra.coarse_bias = Ly.coarse_bias;
+            rr.ra.group_bias = Ly.group_bias;
+            rr.ra.fine_bias = Ly.fine_bias;
+            rr.ra.expert_bias = Ly.expert_bias;
+            for (int i = 0; i < 4; ++i) rr.ra.bias_dtype[i] = Ly.bias_dt[i];
+            rr.ra.experts = E;
+            rr.ra.groups = e->groups;
+            rr.ra.per_group = e->per_group;
+            rr.ra.max_k = K;
+            rr.ra.min_k = e->min_k;
+            rr.ra.temperature = e->temperature;
+            rr.ra.log_experts = e->log_experts;
+            rr.ra.chosen = b.chosen;
+            rr.ra.weights = b.weights;
+            rr.ra.active = b.active;
+            rr.ld_router = RG;
+            rr.T = T;
+            hp::k_route<<<T, 256, 0, s>>>(rr);
+            // the routed rows sorted by expert, gathered; grouped gate | up, SwiGLU, down
+            hp::k_moe_plan<<<1, 1024, 0, s>>>(b.chosen, b.active, T, K, E, b.row_of, b.token_of,
+                                              reinterpret_cast<int4 *>(b.tiles), b.tile_count, b.max_tiles, b.rows,
+                                              e->err);
+            hp::k_gather<<<grid_for(R * (h / 8) * 3 / 4), 256, 0, s>>>(b.planes, ps, b.kmax, b.token_of, b.rows, h,
+                                                                       b.gplanes, gps, h);
+            MR_CUDA_TRY(cudaGetLastError());
+            const BatchSeg gus[2] = {{nullptr, f, 0}, {nullptr, f, f}};
+            rc = batch_gemm_grouped(s, b.err, b.gplanes, gps, h, static_cast<int>(R), h,
+                                    b.maps_gu + static_cast<size_t>(l) * E * 2 * kBatchMapBytes, gus, 2, b.tiles,
+                                    b.tile_count, b.max_tiles, b.gu, 2 * f);
+            if (rc) break;
+            hp::k_swiglu<<<grid_for(R * f / 4), 256, 0, s>>>(b.gu, b.rows, 0, f, b.gsplanes, gsps, f);
+            const BatchSeg dns = {nullptr, h, 0};
+            rc = batch_gemm_grouped(s, b.err, b.gsplanes, gsps, f, static_cast<int>(R), f,
+                                    b.maps_dn + static_cast<size_t>(l) * E * kBatchMapBytes, &dns, 1, b.tiles,
+                                    b.tile_count, b.max_tiles, b.rout, h);
+            // the shared experts over every token (their gate | up first: the planes are reused)
+            for (int j = 0; j < e->shared && !rc; ++j) {
+                const BatchSeg sg[2] = {{Ly.h_gate[E + j], f, 0}, {Ly.h_up[E + j], f, f}};
+                rc = batch_gemm(s, b.err, b.planes, ps, b.kmax, T, h, sg, 2,
+                                b.sgu + static_cast<size_t>(j) * T * 2 * f, 2 * f, false, 0.f);
+            }
+            for (int j = 0; j < e->shared && !rc; ++j) {
+                hp::k_swiglu<<<grid_for(static_cast<size_t>(T) * f), 256, 0, s>>>(
+                    b.sgu + static_cast<size_t>(j) * T * 2 * f, nullptr, T, f, b.planes, ps, b.kmax);
+                const BatchSeg sd = {Ly.h_down[E + j], h, 0};
+                rc = batch_gemm(s, b.err, b.planes, ps, b.kmax, T, f, &sd, 1, b.sout + static_cast<size_t>(j) * T * h, h,
+                                false, 0.f);
+            }
+            if (rc) break;
+            hp::k_combine<<<grid_for(static_cast<size_t>(T) * h), 256, 0, s>>>(
+                b.x, T, h, b.active, b.weights, b.row_of, K, b.rout, b.sout, e->shared, shared_scale, loop_scale);
+            MR_CUDA_TRY(cudaGetLastError());
+            // the last token's experts, where the token step leaves its own
+            MR_CUDA_TRY(cudaMemcpyAsync(e->chosen + li * K, b.chosen + static_cast<size_t>(T - 1) * K, sizeof(int) * K,
+                                        cudaMemcpyDeviceToDevice, s));
+            MR_CUDA_TRY(cudaMemcpyAsync(e->weights + li * K, b.weights + static_cast<size_t>(T - 1) * K,
+                                        sizeof(float) * K, cudaMemcpyDeviceToDevice, s));
+            MR_CUDA_TRY(cudaMemcpyAsync(e->active + li, b.active + T - 1, sizeof(int), cudaMemcpyDeviceToDevice, s));
+        }
+    }
+    if (rc) return rc;
+    // final RMSNorm and the head for the rows whose logits are wanted
+    const int r0 = all_logits ? 0 : T - 1, rows = all_logits ? T : 1;
+    rc = batch_rms_planes(s, b.x, r0, rows, h, h, e->final_norm, e->final_norm_dt, e->eps, b.planes, ps, b.kmax);
+    const BatchSeg hs = {e->head, e->vocab, 0};
+    if (!rc) rc = batch_gemm(s, b.err, b.planes, ps, b.kmax, rows, h, &hs, 1, b.logits, e->vocab, false, 0.f);
+    return rc;
+}
+
 int heavy_status(const HeavyEngine *e) {
     int err = 0;
     MR_CUDA_TRY(cudaMemcpy(&err, e->err, sizeof(int), cudaMemcpyDeviceToHost));
     switch (err) {
-        case 0: return MR_OK;
+        case 0: break;
         case 1: return set_error(MR_ERR_TIMEOUT, "expert parallel: a rank's expert rows did not arrive within the wait limit");
         case 2: return set_error(MR_ERR_TIMEOUT, "weight stream: a bulk copy did not land within the wait limit");
         case 3: return set_error(MR_ERR_TIMEOUT, "sparse attention: a key / value row did not arrive within the wait limit");
@@ -1412,6 +1705,11 @@ int heavy_status(const HeavyEngine *e) {
                                               "logits?)");
         default: return set_error(MR_ERR_TIMEOUT, "heavy-medium-2.0: device wait timed out (code %d)", err);
     }
+    if (e->batch.err) {
+        MR_CUDA_TRY(cudaMemcpy(&err, e->batch.err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (err) return set_error(MR_ERR_TIMEOUT, "batched prompt: a GEMM's bounded wait gave up");
+    }
+    return MR_OK;
 }
 
 int heavy_last_topk(const HeavyEngine *e, int layer, int loop, int *blocks, int capacity) {

@@ -43,6 +43,15 @@ const float *heavy_logits(const HeavyEngine *e);
 // synchronous.  *count receives the number of stamps written.
 int heavy_trace_token(HeavyEngine *e, int token, int position, unsigned long long *stamps, int capacity, int *count);
 
+// Batched prompt (heavy_prefill.cuh): T tokens (host ids) at positions p0 ..
+// p0 + T - 1 through every layer at once, GEMMs on tcgen05, leaving the state
+// heavy_token continues from; the logits of every token (all_logits) or of the
+// last one are then at heavy_prefill_logits(e).  Only for models with
+// heavy_batchable (BF16 matrices, one engine).
+bool heavy_batchable(const HeavyEngine *e);
+int heavy_prefill(HeavyEngine *e, const int *ids, int T, int p0, bool all_logits);
+const float *heavy_prefill_logits(const HeavyEngine *e);
+
 // Greedy decode entirely on the device: `steps` tokens from `position`, each
 // step's input the previous step's argmax (the first: first_token).
 int heavy_greedy_chain(HeavyEngine *e, int first_token, int position, int steps);

@@ -1,0 +1,525 @@
+// Heavy Medium batched prompt (included by heavy.cu only): the token step of
+// model.py:192-285 applied to a chunk of T prompt tokens at once, layer by
+// layer and inner loop by inner loop, leaving exactly the state the device
+// token step continues from (key / value rows, block means, the newest
+// block's running sums, the last token's kept blocks and experts).
+//
+// Per layer and inner loop:
+//   RMSNorm(x, a_norm) -> planes -> GEMM q | latent -> planes(latent) -> GEMM kv_up
+//   -> per-head q / k norm + RoPE, key / value rows into the rows store
+//   -> running block sums of the chunk's positions, block means of the blocks it fills
+//   -> sparse attention per token (block scores, top-k, window) -> planes
+//   -> GEMM o, x += s o -> RMSNorm(x, f_norm) -> planes -> GEMM router -> routing per token
+//   -> tokens sorted by routed expert -> grouped GEMMs gate | up, SwiGLU, down
+//   -> dense GEMMs of the shared experts -> rank-order combine, x += s moe.
+// GEMMs run on tcgen05 with the activations split into three BF16 parts
+// (batch_gemm, prefill.cu), so every product is exact and only the FP32
+// accumulation order differs from the token step's; element-wise steps, the
+// block sums (in position order), the block scores, the top-k, the routing
+// and the combine use the token step's expressions.
+#pragma once
+
+namespace hp {
+
+constexpr int kThreads = 256;
+constexpr int kRows = 32;     // attention: query rows per CTA (tokens x group heads)
+constexpr int kKT = 32;       // attention: keys (or blocks) per tile
+constexpr int kMaxSlots = 32;  // kept blocks per query head the attention supports
+
+// x[t] = embedding row of ids[t], widened exactly.
+__global__ void k_embed(const int *ids, int T, const void *embed, int dt, int h, float *x) {
+    const int t = blockIdx.x;
+    const size_t row = static_cast<size_t>(__ldg(ids + t)) * h;
+    for (int j = threadIdx.x; j < h; j += blockDim.x) x[static_cast<size_t>(t) * h + j] = load_weight(embed, dt, row + j);
+}
+
+// planes[t][j] = split(src[t][j]) for j < cols (no normalisation).
+__global__ void k_split(const float *src, int ld, int cols, int T, uint16_t *planes, size_t ps, int lda) {
+    const size_t n = static_cast<size_t>(T) * cols;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t t = i / cols, j = i - t * cols;
+        put_planes(planes, ps, t * lda + j, src[t * ld + j]);
+    }
+}
+
+// One warp per (token, row): rows 0..H-1 the queries (normalised, rotated into
+// qh), H..H+KVH-1 the keys (normalised, rotated into the rows store at the
+// token's position), H+KVH.. the values (copied there): attn::norm_rope, the
+// token step's arithmetic.
+__global__ void k_qk(const float *qlat, int ldq, const float *kv, int T, int p0, int H, int KVH, int d, int split_half,
+                     const float *inv_freq, float *qh, float *k_rows, float *v_rows) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int per = H + 2 * KVH, width = KVH * d;
+    if (warp >= T * per) return;
+    const int t = warp / per, r = warp % per, p = p0 + t;
+    if (r < H) {
+        attn::norm_rope(qlat + static_cast<size_t>(t) * ldq + r * d, qh + (static_cast<size_t>(t) * H + r) * d, d,
+                        split_half, p, inv_freq);
+    } else if (r < H + KVH) {
+        const int kh = r - H;
+        attn::norm_rope(kv + static_cast<size_t>(t) * 2 * width + kh * d, k_rows + static_cast<size_t>(p) * width + kh * d,
+                        d, split_half, p, inv_freq);
+    } else {
+        const int kh = r - H - KVH;
+        for (int j = lane; j < d; j += 32)
+            v_rows[static_cast<size_t>(p) * width + kh * d + j] = kv[static_cast<size_t>(t) * 2 * width + width + kh * d + j];
+    }
+}
+
+// Running block sums at every position of the chunk, per column, in position
+// order (the token step's k_bsum / v_bsum recurrence: a block's first row
+// starts from 0, later rows add to the sum; a chunk that starts inside a block
+// continues the carried sum).  Each block the chunk reaches gets its mean at
+// the chunk's last row in it (the mean the token step would have left), the
+// newest block's running sums are carried on.  Thread = (block, column, k|v).
+__global__ void k_block_sums(const float *k_rows, const float *v_rows, int T, int p0, int width, int block,
+                             float *k_bsum, float *v_bsum, float *k_mean, float *v_mean, float *sum_k, float *sum_v) {
+    const int b_first = p0 / block, b_last = (p0 + T - 1) / block;
+    const size_t n = static_cast<size_t>(b_last - b_first + 1) * width * 2;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % width), kind = static_cast<int>((i / width) & 1);
+        const int b = b_first + static_cast<int>(i / (2 * static_cast<size_t>(width)));
+        const float *rows = kind ? v_rows : k_rows;
+        float *carry = kind ? v_bsum : k_bsum, *mean = kind ? v_mean : k_mean, *at = kind ? sum_v : sum_k;
+        const int lo = max(p0, b * block), hi = min(p0 + T - 1, (b + 1) * block - 1);
+        float s = lo % block == 0 ? 0.f : carry[c];
+        for (int p = lo; p <= hi; ++p) {
+            const float v = rows[static_cast<size_t>(p) * width + c];
+            s = p % block == 0 ? FADD(0.f, v) : FADD(s, v);
+            at[static_cast<size_t>(p - p0) * width + c] = s;
+        }
+        mean[static_cast<size_t>(b) * width + c] = __fdiv_rn(s, static_cast<float>(hi - b * block + 1));
+        if (b == b_last) carry[c] = s;
+    }
+}
+
+// The routing of every token (route_block per token, model.py:233-250).
+struct RouteRows {
+    RouteArgs ra;      // router / chosen / weights / active of token 0; strides below
+    int ld_router, T;
+};
+__global__ void __launch_bounds__(256) k_route(RouteRows a) {
+    RouteArgs ra = a.ra;
+    const int t = blockIdx.x;
+    ra.router += static_cast<size_t>(t) * a.ld_router;
+    ra.chosen += static_cast<size_t>(t) * ra.max_k;
+    ra.weights += static_cast<size_t>(t) * ra.max_k;
+    ra.active += t;
+    route_block(ra);
+}
+
+// Tokens sorted by routed expert: counts, offsets, each (token, rank) pair's
+// row in the sorted order (row_of, -1 past the token's active experts), each
+// row's token (token_of), and the tile table of the grouped GEMMs: one entry
+// {expert, row0, row_end, 0} per 128 rows of an expert.  One CTA.  The order
+// of rows inside an expert is not fixed (atomics); every row is computed on
+// its own, so the results are.
+__global__ void __launch_bounds__(1024) k_moe_plan(const int *chosen, const int *active, int T, int max_k, int experts,
+                                                   int *row_of, int *token_of, int4 *tiles, int *tile_count,
+                                                   int max_tiles, int *rows, int *err) {
+    __shared__ int count[256], cursor[256];
+    for (int e = threadIdx.x; e < experts; e += blockDim.x) count[e] = 0;
+    __syncthreads();
+    const int n = T * max_k;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int t = i / max_k, k = i % max_k;
+        const int e = k < __ldg(active + t) ? __ldg(chosen + i) : -1;
+        if (k < __ldg(active + t) && (e < 0 || e >= experts)) atomicCAS(err, 0, 4);
+        else if (e >= 0) atomicAdd(&count[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int off = 0, nt = 0;
+        for (int e = 0; e < experts; ++e) {
+            cursor[e] = off;
+            for (int r0 = 0; r0 < count[e] && nt < max_tiles; r0 += kBatchTileRows)
+                tiles[nt++] = make_int4(e, off + r0, off + count[e], 0);
+            off += count[e];
+        }
+        *tile_count = nt;
+        *rows = off;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int t = i / max_k, k = i % max_k;
+        const int e = k < __ldg(active + t) ? __ldg(chosen + i) : -1;
+        int row = -1;
+        if (e >= 0 && e < experts) {
+            row = atomicAdd(&cursor[e], 1);
+            token_of[row] = t;
+        }
+        row_of[i] = row;
+    }
+}
+
+// dst row r = src row token_of[r] (three planes, 16-byte pieces), r < rows.
+__global__ void k_gather(const uint16_t *src, size_t sps, int lds, const int *token_of, const int *rows, int h,
+                         uint16_t *dst, size_t dps, int ldd) {
+    const int n = __ldg(rows), q = h / 8;
+    const size_t total = static_cast<size_t>(n) * q * 3;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int pl = static_cast<int>(i % 3), c = static_cast<int>((i / 3) % q), r = static_cast<int>(i / (3 * q));
+        const int t = __ldg(token_of + r);
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src + pl * sps + static_cast<size_t>(t) * lds) + c);
+        reinterpret_cast<uint4 *>(dst + pl * dps + static_cast<size_t>(r) * ldd)[c] = v;
+    }
+}
+
+// planes[r] = split(silu(gate) * up) of gu[r] = gate row | up row, r < *rows
+// (or r < T when rows is NULL): the token step's expression.
+__global__ void k_swiglu(const float *gu, const int *rows, int T, int f, uint16_t *planes, size_t ps, int ld) {
+    const size_t n = static_cast<size_t>(rows ? __ldg(rows) : T) * f;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t r = i / f, j = i - r * f;
+        const float g = gu[r * 2 * f + j], u = gu[r * 2 * f + f + j];
+        put_planes(planes, ps, r * ld + j, FMUL(__fdiv_rn(g, FADD(1.0f, expf(-g))), u));
+    }
+}
+
+// x[t] += scale * (sum over the token's experts in rank order of weight *
+// down row, then each shared expert's down row * shared_scale): the token
+// step's combine (model.py:251-255).
+__global__ void k_combine(float *x, int T, int h, const int *active, const float *weights, const int *row_of, int max_k,
+                          const float *routed, const float *shared_out, int shared, float shared_scale, float scale) {
+    const size_t n = static_cast<size_t>(T) * h;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int t = static_cast<int>(i / h), c = static_cast<int>(i % h);
+        const int act = __ldg(active + t);
+        float res = 0.f;
+        for (int k = 0; k < act; ++k) {
+            const int r = __ldg(row_of + t * max_k + k);
+            if (r < 0) continue;  // an id outside the expert table (reported through err by k_moe_plan)
+            res = FADD(res, FMUL(__ldg(weights + t * max_k + k), routed[static_cast<size_t>(r) * h + c]));
+        }
+        for (int j = 0; j < shared; ++j)
+            res = FADD(res, FMUL(shared_scale, shared_out[(static_cast<size_t>(j) * T + t) * h + c]));
+        x[i] = FADD(x[i], FMUL(scale, res));
+    }
+}
+
+
+// ---- sparse attention of a chunk ------------------------------------------------------------
+struct AttnArgs {
+    const float *qh;               // [T][H * d] normalised, rotated queries
+    const float *k_rows, *v_rows;  // [context][width] every position's key / value
+    const float *k_mean, *v_mean;  // [blocks][width] block means (final for every block before a token's own)
+    const float *sum_k, *sum_v;    // [T][width] running sums of each token's own block at the token
+    const float *log1p_table;
+    float slope;
+    int T, p0, H, KVH, d, window, block, slots, slots_max, nb;  // nb: blocks of the chunk's last token
+    uint16_t *planes;              // output: planes of the o projection's input [3][T][ld]
+    size_t ps;
+    int ld;
+    int *kept_last;                // [H][slots_max]: the chunk's last token's kept blocks
+};
+
+// q . k / sqrt(d) with the token step's association (attn::tile_score): four
+// FMA chains over the columns in order, (a0 + a1) + (a2 + a3).
+__device__ __forceinline__ float score4(const float *q, const float *k, int d, float sqrt_d) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int j = 0; j < d; j += 4) {
+        const float4 q4 = *reinterpret_cast<const float4 *>(q + j), k4 = *reinterpret_cast<const float4 *>(k + j);
+        a0 = fmaf(q4.x, k4.x, a0);
+        a1 = fmaf(q4.y, k4.y, a1);
+        a2 = fmaf(q4.z, k4.z, a2);
+        a3 = fmaf(q4.w, k4.w, a3);
+    }
+    return __fdiv_rn((a0 + a1) + (a2 + a3), sqrt_d);
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src)
+                 : "memory");
+}
+
+// CTA = (QT consecutive tokens, KV head kh); rows r = (token, group head).
+// A. Block part (model.py:210-226 per token): every block's mean key scored
+//    against the row's query minus the distance penalty (the token's own,
+//    unfinished block from its running sum), the best `slots` kept (larger
+//    score first, ties to the lower block, as the stable argsort), and their
+//    softmax terms over the blocks' mean values, in ascending block order,
+//    become the row's starting online-softmax state.
+// B. Window part: keys (p - window, p] in tiles of 32 (double-buffered
+//    cp.async), online softmax continued.  Output rows as BF16x3 planes.
+__global__ void __launch_bounds__(kThreads) k_attention(AttnArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    const int G = a.H / a.KVH, QT = kRows / G, kh = blockIdx.y, t0 = blockIdx.x * QT;
+    const int nt = min(QT, a.T - t0), R = nt * G, d = a.d, width = a.KVH * d, ks = d + 4, dq = d / 4;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float *q = sm;                        // [kRows][d + 4]
+    float *kt = q + kRows * ks;           // [2][kKT][d + 4]
+    float *vt = kt + 2 * kKT * ks;        // [2][kKT][d]; phase A: each token's own block mean key | value
+    float *s = vt + 2 * kKT * d;          // [kRows][kKT + 1]
+    float *mrow = s + kRows * (kKT + 1), *lrow = mrow + kRows, *corr = lrow + kRows;
+    float *bscore = corr + kRows;         // [kRows][nb]
+    float *ksc = bscore + static_cast<size_t>(kRows) * a.nb;  // [kRows][kMaxSlots] kept scores
+    int *kid = reinterpret_cast<int *>(ksc + kRows * kMaxSlots);  // [kRows][kMaxSlots] kept blocks, ascending
+    int *nkept = kid + kRows * kMaxSlots;                       // [kRows]
+    float *cur_k = vt, *cur_v = vt + QT * d;
+    const int p_first = a.p0 + t0, p_last = p_first + nt - 1;
+    const int nb = p_last / a.block + 1;  // blocks of the CTA's last token
+    const float sqrt_d = __fsqrt_rn(static_cast<float>(d));
+
+    for (int e = tid; e < kRows * d; e += kThreads) {
+        const int r = e / d, j = e - r * d, tt = r / G, g = r - tt * G;
+        q[r * ks + j] = r < R ? __ldg(a.qh + (static_cast<size_t>(t0 + tt) * a.H + kh * G + g) * d + j) : 0.f;
+    }
+    for (int e = tid; e < nt * d; e += kThreads) {  // each token's own block: its running mean at the token
+        const int tt = e / d, j = e - tt * d, p = p_first + tt;
+        const float n = static_cast<float>(p - (p / a.block) * a.block + 1);
+        const size_t at = static_cast<size_t>(t0 + tt) * width + kh * d + j;
+        cur_k[tt * d + j] = __fdiv_rn(__ldg(a.sum_k + at), n);
+        cur_v[tt * d + j] = __fdiv_rn(__ldg(a.sum_v + at), n);
+    }
+    const int sr = tid >> 3, sk = tid & 7;  // score mapping: row sr, keys sk, sk + 8, sk + 16, sk + 24
+    // A1. block scores, kKT block means at a time (the token's own block is scored below)
+    for (int b0 = 0; b0 < nb; b0 += kKT) {
+        const int nbt = min(kKT, nb - b0);
+        __syncthreads();
+        for (int e = tid; e < nbt * dq; e += kThreads) {
+            const int kk = e / dq, j = (e - kk * dq) * 4;
+            *reinterpret_cast<float4 *>(kt + kk * ks + j) =
+                __ldg(reinterpret_cast<const float4 *>(a.k_mean + static_cast<size_t>(b0 + kk) * width + kh * d + j));
+        }
+        __syncthreads();
+        if (sr < R) {
+            const int p = p_first + sr / G, own = p / a.block;
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+                const int kk = sk + 8 * y, b = b0 + kk;
+                if (kk >= nbt) continue;
+                float v = -INFINITY;
+                if (b < own) {
+                    v = __fsub_rn(score4(q + sr * ks, kt + kk * ks, d, sqrt_d),
+                                  FMUL(a.slope, __ldg(a.log1p_table + p - min((b + 1) * a.block - 1, p))));
+                }
+                bscore[static_cast<size_t>(sr) * a.nb + b] = v;
+            }
+        }
+    }
+    __syncthreads();
+    for (int r = tid; r < R; r += kThreads) {  // A2. the token's own block
+        const int tt = r / G, p = p_first + tt, own = p / a.block;
+        bscore[static_cast<size_t>(r) * a.nb + own] =
+            __fsub_rn(score4(q + r * ks, cur_k + tt * d, d, sqrt_d), FMUL(a.slope, __ldg(a.log1p_table + 0)));
+    }
+    __syncthreads();
+    // A3. the best `slots` blocks of each row: repeated warp argmax (larger score, then lower block)
+    for (int x = 0; x < kRows / 8; ++x) {
+        const int r = warp + 8 * x;
+        if (r >= R) continue;
+        const int p = p_first + r / G, nbr = p / a.block + 1, want = min(a.slots, nbr);
+        float *row = bscore + static_cast<size_t>(r) * a.nb;
+        int n = 0;
+        for (; n < want; ++n) {
+            float best = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int b = lane; b < nbr; b += 32) {
+                const float v = row[b];
+                if (v != -INFINITY && (v > best || (v == best && b < bi))) {
+                    best = v;
+                    bi = b;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ob > best || (ob == best && oi < bi)) {
+                    best = ob;
+                    bi = oi;
+                }
+            }
+            if (bi == 0x7fffffff) break;
+            if (lane == 0) {
+                kid[r * kMaxSlots + n] = bi;
+                ksc[r * kMaxSlots + n] = best;
+            }
+            if (lane == (bi & 31)) row[bi] = -INFINITY;
+            __syncwarp();
+        }
+        if (lane == 0) {  // ascending block order (np.flatnonzero), as the token step keeps them
+            for (int i = 1; i < n; ++i)
+                for (int j = i; j > 0 && kid[r * kMaxSlots + j - 1] > kid[r * kMaxSlots + j]; --j) {
+                    const int ti = kid[r * kMaxSlots + j];
+                    const float ts = ksc[r * kMaxSlots + j];
+                    kid[r * kMaxSlots + j] = kid[r * kMaxSlots + j - 1];
+                    ksc[r * kMaxSlots + j] = ksc[r * kMaxSlots + j - 1];
+                    kid[r * kMaxSlots + j - 1] = ti;
+                    ksc[r * kMaxSlots + j - 1] = ts;
+                }
+            nkept[r] = n;
+            if (t0 + r / G == a.T - 1) {
+                const int h = kh * G + r % G;
+                for (int i = 0; i < a.slots_max; ++i) a.kept_last[h * a.slots_max + i] = i < n ? kid[r * kMaxSlots + i] : -1;
+            }
+        }
+    }
+    __syncthreads();
+    // A4. the kept blocks' softmax terms: the rows' starting state
+    for (int r = tid; r < kRows; r += kThreads) {
+        float m = -INFINITY, l = 0.f;
+        if (r < R) {
+            for (int i = 0; i < nkept[r]; ++i) m = fmaxf(m, ksc[r * kMaxSlots + i]);
+            for (int i = 0; i < nkept[r]; ++i) l += expf(__fsub_rn(ksc[r * kMaxSlots + i], m));
+        }
+        mrow[r] = m;
+        lrow[r] = l;
+    }
+    __syncthreads();
+    const int nblk = (kRows / 2) * dq;  // output blocks: 2 rows x 4 dims
+    float acc[2][8];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[b][e] = 0.f;
+        const int blk = tid + b * kThreads;
+        if (blk >= nblk) continue;
+        const int r0 = (blk / dq) * 2, j0 = (blk % dq) * 4;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+            const int r = r0 + x;
+            if (r >= R) continue;
+            const int tt = r / G, own = (p_first + tt) / a.block;
+            for (int i = 0; i < nkept[r]; ++i) {
+                const int bb = kid[r * kMaxSlots + i];
+                const float w = expf(__fsub_rn(ksc[r * kMaxSlots + i], mrow[r]));
+                const float *vs = bb == own ? cur_v + tt * d : a.v_mean + static_cast<size_t>(bb) * width + kh * d;
+#pragma unroll
+                for (int y = 0; y < 4; ++y) acc[b][x * 4 + y] = fmaf(w, vs[j0 + y], acc[b][x * 4 + y]);
+            }
+        }
+    }
+    __syncthreads();  // phase A's means in vt are read; the window tiles take it over
+    // B. the window (p - window, p] of every row
+    const int lo = max(0, p_first - a.window + 1);
+    auto issue = [&](int kb, int buf) {
+        const int nk = min(kKT, p_last + 1 - kb);
+        for (int e = tid; e < nk * dq; e += kThreads) {
+            const int kk = e / dq, j = (e - kk * dq) * 4;
+            const size_t row = static_cast<size_t>(kb + kk) * width + kh * d + j;
+            cp_async16(kt + (buf * kKT + kk) * ks + j, a.k_rows + row);
+            cp_async16(vt + (buf * kKT + kk) * d + j, a.v_rows + row);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    issue(lo, 0);
+    int buf = 0;
+    for (int kb = lo; kb <= p_last; kb += kKT, buf ^= 1) {
+        const int nk = min(kKT, p_last + 1 - kb);
+        if (kb + kKT <= p_last) {
+            issue(kb + kKT, buf ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const float *ktb = kt + buf * kKT * ks, *vtb = vt + buf * kKT * d;
+        {
+            const int p = p_first + sr / G;
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+                const int kk = sk + 8 * y, pos = kb + kk;
+                const bool live = sr < R && kk < nk && pos <= p && pos > p - a.window;
+                s[sr * (kKT + 1) + kk] = live ? score4(q + sr * ks, ktb + kk * ks, d, sqrt_d) : -INFINITY;
+            }
+        }
+        __syncthreads();
+        {  // online softmax: warp w updates rows w, w + 8, w + 16, w + 24, one key per lane
+            float v[4], mt[4], pr[4], sum[4];
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+                v[x] = s[(warp + 8 * x) * (kKT + 1) + lane];
+                mt[x] = v[x];
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int x = 0; x < 4; ++x) mt[x] = fmaxf(mt[x], __shfl_xor_sync(0xffffffffu, mt[x], o));
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+                const int r = warp + 8 * x;
+                const float m_new = fmaxf(mrow[r], mt[x]);
+                pr[x] = v[x] == -INFINITY ? 0.f : expf(__fsub_rn(v[x], m_new));
+                sum[x] = pr[x];
+                mt[x] = m_new;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int x = 0; x < 4; ++x) sum[x] += __shfl_xor_sync(0xffffffffu, sum[x], o);
+            __syncwarp();
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+                const int r = warp + 8 * x;
+                s[r * (kKT + 1) + lane] = pr[x];
+                if (lane == 0) {
+                    const float m_old = mrow[r];
+                    const float cf = m_old == -INFINITY ? 0.f : expf(__fsub_rn(m_old, mt[x]));
+                    corr[r] = cf;
+                    lrow[r] = fmaf(lrow[r], cf, sum[x]);
+                    mrow[r] = mt[x];
+                }
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {  // value mix: 2 rows x 4 dims per block
+            const int blk = tid + b * kThreads;
+            if (blk >= nblk) continue;
+            const int r0 = (blk / dq) * 2, j0 = (blk % dq) * 4;
+            if (r0 >= R) continue;
+            const float c0 = corr[r0], c1 = corr[r0 + 1];
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+                acc[b][y] *= c0;
+                acc[b][4 + y] *= c1;
+            }
+            const float *s0 = s + r0 * (kKT + 1), *s1 = s0 + (kKT + 1);
+            for (int kk = 0; kk < nk; ++kk) {
+                const float4 vv = *reinterpret_cast<const float4 *>(vtb + kk * d + j0);
+                const float w0 = s0[kk], w1 = s1[kk];
+                acc[b][0] = fmaf(w0, vv.x, acc[b][0]);
+                acc[b][1] = fmaf(w0, vv.y, acc[b][1]);
+                acc[b][2] = fmaf(w0, vv.z, acc[b][2]);
+                acc[b][3] = fmaf(w0, vv.w, acc[b][3]);
+                acc[b][4] = fmaf(w1, vv.x, acc[b][4]);
+                acc[b][5] = fmaf(w1, vv.y, acc[b][5]);
+                acc[b][6] = fmaf(w1, vv.z, acc[b][6]);
+                acc[b][7] = fmaf(w1, vv.w, acc[b][7]);
+            }
+        }
+        __syncthreads();  // every reader of buffer buf is done before it is refilled
+    }
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        const int blk = tid + b * kThreads;
+        if (blk >= nblk) continue;
+        const int r0 = (blk / dq) * 2, j0 = (blk % dq) * 4;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+            const int r = r0 + x;
+            if (r >= R) continue;
+            const int tt = r / G, g = r - tt * G;
+#pragma unroll
+            for (int y = 0; y < 4; ++y)
+                put_planes(a.planes, a.ps, static_cast<size_t>(t0 + tt) * a.ld + (kh * G + g) * d + j0 + y,
+                           __fdiv_rn(acc[b][x * 4 + y], lrow[r]));
+        }
+    }
+}
+
+// Shared memory of k_attention for head dim d and nb blocks.
+inline size_t attention_smem(int d, int nb) {
+    return sizeof(float) * (static_cast<size_t>(kRows) * (d + 4) + 2 * kKT * (d + 4) + 2 * static_cast<size_t>(kKT) * d +
+                            kRows * (kKT + 1) + 3 * kRows + static_cast<size_t>(kRows) * nb + 2 * kRows * kMaxSlots +
+                            kRows);
+}
+
+}  // namespace hp

@@ -37,7 +37,7 @@ constexpr int kThreads = kConsumers + 32;  // + the producer warp
 constexpr int kSlotBytes = 16384;
 constexpr int kMaxSlots = 12;
 constexpr int kMaxSegs = 12;
-constexpr int kMaxPieceRows = 4;
+constexpr int kMaxPieceRows = 5;
 
 enum Mode { kPlain = 0, kSwiglu = 1, kDown = 2 };
 
@@ -224,7 +224,7 @@ template <int DT>
 __device__ __forceinline__ void rows_dot(const char *slot, int n, int row_bytes, int nv, const float *xlo,
                                          const float *xhi, float (&y)[kMaxPieceRows]) {
     const int lane = threadIdx.x & 31;
-    float acc[kMaxPieceRows] = {0.f, 0.f, 0.f, 0.f};
+    float acc[kMaxPieceRows] = {};
     for (int c = lane; c < nv; c += 32) {
 #pragma unroll
         for (int r = 0; r < kMaxPieceRows; ++r)

@@ -28,27 +28,6 @@ constexpr int kPadK = kBK + 8;  // shared row stride (bf16): 80 bytes, conflict-
 constexpr int kStages = 3;
 constexpr int kGemmThreads = 256;  // 8 warps: 2 (tokens) x 4 (features), warp tile 32 x 16
 
-__device__ __forceinline__ uint16_t to_bf16(float f) {
-    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
-}
-__device__ __forceinline__ float from_bf16(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
-
-// x = p0 + p1 + p2 (BF16 parts; the residuals are exact in FP32).
-__device__ __forceinline__ void split3(float x, uint16_t &a, uint16_t &b, uint16_t &c) {
-    a = to_bf16(x);
-    const float r1 = __fsub_rn(x, from_bf16(a));
-    b = to_bf16(r1);
-    const float r2 = __fsub_rn(r1, from_bf16(b));
-    c = to_bf16(r2);
-}
-__device__ __forceinline__ void put_planes(uint16_t *planes, size_t plane_stride, size_t idx, float v) {
-    uint16_t a, b, c;
-    split3(v, a, b, c);
-    planes[idx] = a;
-    planes[plane_stride + idx] = b;
-    planes[2 * plane_stride + idx] = c;
-}
-
 __device__ __forceinline__ float block_reduce_sum(float v, float *red) {
     v = warp_sum(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -381,6 +360,11 @@ struct GemmArgs {
     float scale;
     GemmSeg seg[3];
     int nseg;
+    // grouped (tcgen05 only): grid row y < *tile_count takes tiles[y] = {group, row0, row_end}
+    // and the W maps gmaps[group * nseg + segment] (global memory)
+    const int4 *tiles;
+    const int *tile_count;
+    const CUtensorMap *gmaps;
 };
 
 __device__ __forceinline__ void cp16(void *dst, const void *src, bool valid) {
@@ -606,7 +590,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     int si = 0;
     while (si + 1 < args.nseg && static_cast<int>(blockIdx.x) >= args.seg[si + 1].tiles) ++si;
     const GemmSeg seg = args.seg[si];
-    const int n0 = (blockIdx.x - seg.tiles) * kTN, m0 = blockIdx.y * kTM;
+    const int n0 = (blockIdx.x - seg.tiles) * kTN;
+    int m0 = blockIdx.y * kTM, m_end = args.M;
+    const CUtensorMap *mb = &maps.b[si];
+    if (args.tiles) {  // grouped: rows and weights of this grid row's tile (unused grid rows leave at once)
+        if (static_cast<int>(blockIdx.y) >= __ldg(args.tile_count)) return;
+        const int4 t = __ldg(args.tiles + blockIdx.y);
+        m0 = t.y;
+        m_end = t.z;
+        mb = args.gmaps + static_cast<size_t>(t.x) * args.nseg + si;
+    }
     const int ktiles = (args.K + kTK - 1) / kTK;
     if (tid == 0) {
         for (int st = 0; st < kTStages; ++st) {
@@ -631,7 +624,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
     if (warp == 0 && lane == 0) {  // TMA producer
-        const CUtensorMap *mb = &maps.b[si];
         int issued = 0;
         for (int kt = 0; kt < ktiles; ++kt) {
             const int st = kt % kTStages;
@@ -732,7 +724,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const __grid_constant
             for (int c = 0; c < kTN; c += 32) {
                 uint32_t v[32];
                 tmem_ld32(lane_base + 2 * kTN + c, v);
-                if (m < args.M) {
+                if (m < m_end) {
                     float *dst = args.y + static_cast<size_t>(m) * args.ldy + seg.col0 + n0 + c;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
@@ -779,8 +771,9 @@ int encode_map(CUtensorMap *map, const void *base, int rank, const cuuint64_t *d
 
 constexpr size_t kGemmSmem = static_cast<size_t>(kStages) * (3 * kBM + kBN) * kPadK * sizeof(uint16_t);
 
-int gemm(const PrefillWork &w, cudaStream_t stream, const uint16_t *planes, size_t plane_stride, int lda, int M,
-         int K, std::initializer_list<GemmSeg> segs, float *y, int ldy, bool resid, float scale) {
+int run_gemm(bool tcgen05, int *err, cudaStream_t stream, const uint16_t *planes, size_t plane_stride, int lda, int M,
+             int K, const GemmSeg *segs, int nseg, float *y, int ldy, bool resid, float scale) {
+    MR_REQUIRE(nseg >= 1 && nseg <= 3, "a batched GEMM takes 1 to 3 weight segments");
     GemmArgs a{};
     a.planes = planes;
     a.plane_stride = plane_stride;
@@ -792,13 +785,13 @@ int gemm(const PrefillWork &w, cudaStream_t stream, const uint16_t *planes, size
     a.resid = resid ? 1 : 0;
     a.scale = scale;
     int tiles = 0;
-    for (const GemmSeg &s : segs) {
-        GemmSeg t = s;
+    for (int i = 0; i < nseg; ++i) {
+        GemmSeg t = segs[i];
         t.tiles = tiles;
         a.seg[a.nseg++] = t;
-        tiles += (s.n + kBN - 1) / kBN;
+        tiles += (t.n + kBN - 1) / kBN;
     }
-    if (!w.tcgen05) {
+    if (!tcgen05) {
         const dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>((M + kBM - 1) / kBM));
         k_gemm_bf16x3<<<grid, kGemmThreads, kGemmSmem, stream>>>(a);
         MR_CUDA_TRY(cudaGetLastError());
@@ -824,10 +817,16 @@ int gemm(const PrefillWork &w, cudaStream_t stream, const uint16_t *planes, size
     }
     if (rc) return rc;
     const dim3 grid(static_cast<unsigned>(tc_tiles), static_cast<unsigned>(mtiles));
-    if (BN == 128) k_gemm_tc<128><<<grid, kTcThreads, tc_smem<128>(), stream>>>(maps, a, w.err);
-    else k_gemm_tc<64><<<grid, kTcThreads, tc_smem<64>(), stream>>>(maps, a, w.err);
+    if (BN == 128) k_gemm_tc<128><<<grid, kTcThreads, tc_smem<128>(), stream>>>(maps, a, err);
+    else k_gemm_tc<64><<<grid, kTcThreads, tc_smem<64>(), stream>>>(maps, a, err);
     MR_CUDA_TRY(cudaGetLastError());
     return MR_OK;
+}
+
+int gemm(const PrefillWork &w, cudaStream_t stream, const uint16_t *planes, size_t plane_stride, int lda, int M,
+         int K, std::initializer_list<GemmSeg> segs, float *y, int ldy, bool resid, float scale) {
+    return run_gemm(w.tcgen05, w.err, stream, planes, plane_stride, lda, M, K, segs.begin(), static_cast<int>(segs.size()),
+                    y, ldy, resid, scale);
 }
 
 // Row width of the q | k | v buffer: FlashLighting's q | latent fits too.
@@ -842,6 +841,67 @@ size_t attn_smem(int d) {
 }
 
 }  // namespace
+
+int batch_setup() {
+    MR_CUDA_TRY(cudaFuncSetAttribute(k_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc_smem<64>()));
+    MR_CUDA_TRY(cudaFuncSetAttribute(k_gemm_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc_smem<128>()));
+    return MR_OK;
+}
+
+int batch_gemm(cudaStream_t stream, int *err, const uint16_t *planes, size_t plane_stride, int lda, int M, int K,
+               const BatchSeg *segs, int nseg, float *y, int ldy, bool resid, float scale) {
+    MR_REQUIRE(nseg >= 1 && nseg <= 3, "a batched GEMM takes 1 to 3 weight segments");
+    GemmSeg g[3];
+    for (int i = 0; i < nseg; ++i) g[i] = GemmSeg{static_cast<const uint16_t *>(segs[i].w), segs[i].n, segs[i].col0, 0};
+    return run_gemm(true, err, stream, planes, plane_stride, lda, M, K, g, nseg, y, ldy, resid, scale);
+}
+
+int batch_weight_map(void *map, const void *w, int n, int K) {
+    static_assert(sizeof(CUtensorMap) == kBatchMapBytes, "tensor map size");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(n)};
+    const cuuint64_t str[1] = {static_cast<cuuint64_t>(K) * 2};
+    return encode_map(static_cast<CUtensorMap *>(map), w, 2, dims, str, 128);
+}
+
+int batch_gemm_grouped(cudaStream_t stream, int *err, const uint16_t *planes, size_t plane_stride, int lda, int rows,
+                       int K, const void *maps, const BatchSeg *segs, int nseg, const int *tiles,
+                       const int *tile_count, int max_tiles, float *y, int ldy) {
+    MR_REQUIRE(nseg >= 1 && nseg <= 3 && max_tiles > 0, "grouped GEMM arguments");
+    MR_REQUIRE((reinterpret_cast<uintptr_t>(maps) & 63) == 0 && (reinterpret_cast<uintptr_t>(tiles) & 15) == 0,
+               "grouped GEMM: tensor maps 64-byte and tiles 16-byte aligned");
+    GemmArgs a{};
+    a.planes = planes;
+    a.plane_stride = plane_stride;
+    a.lda = lda;
+    a.M = rows;
+    a.K = K;
+    a.y = y;
+    a.ldy = ldy;
+    a.tiles = reinterpret_cast<const int4 *>(tiles);
+    a.tile_count = tile_count;
+    a.gmaps = static_cast<const CUtensorMap *>(maps);
+    int ntiles = 0;
+    for (int i = 0; i < nseg; ++i) {
+        a.seg[a.nseg++] = GemmSeg{nullptr, segs[i].n, segs[i].col0, ntiles};
+        ntiles += (segs[i].n + 127) / 128;
+    }
+    TcMaps tm{};
+    const cuuint64_t adims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows), 3};
+    const cuuint64_t astr[2] = {static_cast<cuuint64_t>(lda) * 2, static_cast<cuuint64_t>(plane_stride) * 2};
+    if (int rc = encode_map(&tm.a, planes, 3, adims, astr, kTM)) return rc;
+    const dim3 grid(static_cast<unsigned>(ntiles), static_cast<unsigned>(max_tiles));
+    k_gemm_tc<128><<<grid, kTcThreads, tc_smem<128>(), stream>>>(tm, a, err);
+    MR_CUDA_TRY(cudaGetLastError());
+    return MR_OK;
+}
+
+int batch_rms_planes(cudaStream_t stream, const float *x, int row0, int rows, int h, int ldx, const void *gain,
+                     int gain_dt, float eps, uint16_t *planes, size_t plane_stride, int ld) {
+    if (rows <= 0) return MR_OK;
+    k_rms_planes<<<rows, 256, 0, stream>>>(x, row0, h, ldx, gain, gain_dt, eps, planes, plane_stride, ld);
+    MR_CUDA_TRY(cudaGetLastError());
+    return MR_OK;
+}
 
 void prefill_release(PrefillWork &w) {
     for (void *p : {static_cast<void *>(w.x), static_cast<void *>(w.planes), static_cast<void *>(w.qkv),

@@ -10,6 +10,8 @@
 
 #include <vector>
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 
 namespace mr {
@@ -70,5 +72,58 @@ int prefill_status(const PrefillModel &pm, PrefillWork &w);
 // layer, appending their keys and values to the rings, and writes the logits
 // of every token (all_logits) or of the last one into w.logits.
 int prefill_chunk(const PrefillModel &pm, PrefillWork &w, const int *d_ids, int T, int p0, bool all_logits);
+
+// ---- building blocks shared with Heavy Medium's batched prompt (heavy_prefill.cuh) ----
+
+// One BF16 weight matrix [n][K] (row-major) whose products land in output
+// columns col0 .. col0 + n - 1.
+struct BatchSeg {
+    const void *w;
+    int n, col0;
+};
+
+// Y[m][col0 + j] = sum_k X[m][k] W[j][k] (resid: Y = Y + scale * that) for M
+// rows of X given as BF16x3 planes ([3][rows][lda], plane_stride elements
+// apart), up to 3 segments, on tcgen05 (*err: a bounded wait gave up).
+int batch_gemm(cudaStream_t stream, int *err, const uint16_t *planes, size_t plane_stride, int lda, int M, int K,
+               const BatchSeg *segs, int nseg, float *y, int ldy, bool resid, float scale);
+
+// Grouped form: grid row y < *tile_count takes tiles[y] = {group, row0, row_end}:
+// X rows [row0, row0 + 128) against group's weights (maps[group * nseg + s],
+// encoded by batch_weight_map), output rows below row_end only.  `segs`
+// gives each segment's n and col0 (its w is not read); max_tiles bounds the grid.
+int batch_gemm_grouped(cudaStream_t stream, int *err, const uint16_t *planes, size_t plane_stride, int lda, int rows,
+                       int K, const void *maps, const BatchSeg *segs, int nseg, const int *tiles,
+                       const int *tile_count, int max_tiles, float *y, int ldy);
+constexpr int kBatchTileRows = 128;  // X rows per tile of batch_gemm_grouped
+constexpr size_t kBatchMapBytes = 128;  // one encoded weight map
+
+// Encodes the tensor map batch_gemm_grouped reads for a BF16 [n][K] matrix
+// into `map` (kBatchMapBytes, host memory; copy it to the device array).
+int batch_weight_map(void *map, const void *w, int n, int K);
+
+// planes[i] = split(RMSNorm(x[row0 + i]) * gain) for `rows` rows of width h
+// (gain NULL: 1), kernels.cl:19-28.
+int batch_rms_planes(cudaStream_t stream, const float *x, int row0, int rows, int h, int ldx, const void *gain,
+                     int gain_dt, float eps, uint16_t *planes, size_t plane_stride, int ld);
+
+// Shared-memory opt-ins of the GEMM kernels (once per device).
+int batch_setup();
+
+#ifdef __CUDACC__
+// x = p0 + p1 + p2 in BF16 parts (each residual is exact in FP32), the form
+// every batched GEMM input takes.
+__device__ __forceinline__ uint16_t bf16_bits(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+__device__ __forceinline__ float bf16_value(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
+__device__ __forceinline__ void put_planes(uint16_t *planes, size_t plane_stride, size_t idx, float v) {
+    const uint16_t a = bf16_bits(v);
+    const float r1 = __fsub_rn(v, bf16_value(a));
+    const uint16_t b = bf16_bits(r1);
+    const float r2 = __fsub_rn(r1, bf16_value(b));
+    planes[idx] = a;
+    planes[plane_stride + idx] = b;
+    planes[2 * plane_stride + idx] = bf16_bits(r2);
+}
+#endif
 
 }  // namespace mr

@@ -68,8 +68,15 @@ def test_heavy_device_step_matches_oracle(backend):
         assert experts == ref["experts"], token
         masked = masked or any(len(head) == 3 and token >= 24 for loop in topk for head in loop)
     assert masked  # the top-k did choose among more blocks than slots
-    # the device path without per-token reads gives the same logits
+    # the device path without per-token reads: the token step gives the same logits bit for
+    # bit, the batched prompt (tcgen05 GEMMs, another summation order) within the tolerance
     fast = submodule("model").MiracleModel(config, weights, backend=backend, context_length=120)
+    native = submodule("_native")
+    native.call("mr_model_set_batched_prefill", fast._handle, 0, None)
     np.testing.assert_array_equal(fast.prefill(prompt, return_all=True), got)
+    fast.reset()
+    native.call("mr_model_set_batched_prefill", fast._handle, 1, None)
+    np.testing.assert_allclose(fast.prefill(prompt, return_all=True), got, atol=ATOL, rtol=RTOL)
+    fast.reset()
     # greedy continuation matches the oracle's
     assert fast.generate(prompt[:30], max_new_tokens=8) == oracle.generate(prompt[:30], max_new_tokens=8)
