@@ -472,20 +472,26 @@ def run_profile_prefill(args):
     """Prefill of the benchmark prompt, repeated, for ncu captures of the
     batched prefill kernels; prints the wall time of each (not a bench value)."""
     syn = _pkg("synthetic")
-    config = syn.config_for(args.config)
-    context, prompt_len, _ = syn.WORKLOADS[args.config]
+    config, context, prompt_len = profile_config(args)
+    prompt_len = args.profile_prompt or prompt_len
     backend = _pkg("backend").CUDABackend(device_index=int(os.environ.get("LOCAL_RANK", "0")))
     model = _pkg("model").MiracleModel.synthetic(config, stored=syn.STORED_DTYPE[args.config], backend=backend,
                                                  context_length=context)
     prompt = syn.prompt_ids(config.vocab_size, prompt_len, seed=1)
     times = []
-    for _ in range(args.profile_prefill):
+    import torch  # the profiler range (ncu --profile-from-start off) covers the last prefill only
+    for i in range(args.profile_prefill):
         model.reset()
         backend.finish()
+        last = i == args.profile_prefill - 1
+        if last:
+            torch.cuda.profiler.start()
         t0 = time.perf_counter()
         model.prefill(prompt)
         backend.finish()
         times.append(round((time.perf_counter() - t0) * 1e3, 3))
+        if last:
+            torch.cuda.profiler.stop()
     print(json.dumps({"profile_prefill": args.config, "prompt": prompt_len, "ms": times}))
     return 0
 

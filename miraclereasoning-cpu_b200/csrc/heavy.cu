@@ -736,7 +736,7 @@ struct HeavyEngine {
     int sm_count = 0, attn_chunks = 0;
     // ring slots per stream::Mode (plain, swiglu, down): measured at 4 to 12 slots, bytes in
     // flight pay more than room for the next kernel's CTAs beside a smaller ring
-    int stream_slots[3] = {12, 12, 10};
+    int stream_slots[3] = {12, 12, 8};
     float *attn_partial = nullptr;
     unsigned long long *counters = nullptr;  // [KVH] ready, [KVH] done, [1] router blocks
     std::vector<float *> k_bsum, v_bsum;

@@ -37,7 +37,7 @@ constexpr int kThreads = kConsumers + 32;  // + the producer warp
 constexpr int kSlotBytes = 16384;
 constexpr int kMaxSlots = 12;
 constexpr int kMaxSegs = 12;
-constexpr int kMaxPieceRows = 5;
+constexpr int kMaxPieceRows = 4;
 
 enum Mode { kPlain = 0, kSwiglu = 1, kDown = 2 };
 
