@@ -318,8 +318,7 @@ def measure(name, args, ranks, mode, steps, warmup, sample_clocks):
     # prefill: batched on the tensor cores for BF16 models of the engine families (timed
     # after one untimed pass: workspace allocation), else token by token (timed on its only pass)
     batched = C.c_int(0)
-    if model._stepper is None:
-        native.call("mr_model_set_batched_prefill", model._handle, 1, C.byref(batched))
+    native.call("mr_model_set_batched_prefill", model._handle, 1, C.byref(batched))
     serial = not batched.value
     if not serial:
         model.prefill(prompt)

@@ -248,6 +248,9 @@ typedef struct {
 MR_API int mr_model_layer_state(const mr_model *model, int layer, int loop, mr_layer_state *out);
 /* flashlighting-2.0: positions of the latent rows (rows ints) of one layer. */
 MR_API int mr_model_latent_positions(const mr_model *model, int layer, int *out, int capacity, int *rows);
+/* flashlighting-2.0: how many tokens each latent row stands for (rows floats;
+ * memory rows first, as the reference's state["counts"], model.py:183-185). */
+MR_API int mr_model_latent_counts(const mr_model *model, int layer, float *out, int capacity, int *rows);
 /* Discrete decisions of the LAST step, for parity tests:
  * heavy top-k:  blocks[heads * global_slots], -1 padded, ascending per head;
  * MoE:          experts[router_top_k_max] (-1 padded, rank order), weights[...] */

@@ -94,6 +94,7 @@ SIGNATURES = {
     "mr_model_generate_greedy": (_I, [_P, _IP, _I, _I, _I, _IP, _IP, _IP]),
     "mr_model_layer_state": (_I, [_P, _I, _I, C.POINTER(LayerState)]),
     "mr_model_latent_positions": (_I, [_P, _I, _IP, _I, _IP]),
+    "mr_model_latent_counts": (_I, [_P, _I, _FP, _I, _IP]),
     "mr_model_last_topk": (_I, [_P, _I, _I, _IP, _I]),
     "mr_model_last_experts": (_I, [_P, _I, _I, _IP, _FP, _I]),
     "mr_model_set_log1p_table": (_I, [_P, _FP, _I]),

@@ -20,6 +20,7 @@
 #include "engine.cuh"
 #include "heavy.cuh"
 #include "prefill.cuh"
+#include "aux_step.cuh"
 
 namespace mr {
 
@@ -49,8 +50,22 @@ bool is_lighting_ring(const mr_model_config &c) {
     return c.family == MR_FAMILY_FLASHLIGHTING_20 && c.memory_slots == 0 && c.window > 0;
 }
 
+// FlashLighting with memory slots: the same ring for the window, and memory rows
+// (absorbed and merged latents) that the work between steps keeps (aux_step.cuh).
+bool is_lighting_memory(const mr_model_config &c) {
+    return c.family == MR_FAMILY_FLASHLIGHTING_20 && c.memory_slots > 0 && c.window > 0;
+}
+bool is_lighting(const mr_model_config &c) { return is_lighting_ring(c) || is_lighting_memory(c); }
+
+// flashnano-1.6: grouped-query attention plus chunk relays (aux_step.cuh).
+bool is_cbr(const mr_model_config &c) {
+    return c.family == MR_FAMILY_FLASHNANO_16 && c.cbr_chunk_size > 0 && c.cbr_slots > 0;
+}
+
 // Families the persistent decode kernel plans (the others step on the host).
-bool is_engine_family(const mr_model_config &c) { return is_gqa_family(c.family) || is_lighting_ring(c); }
+bool is_engine_family(const mr_model_config &c) {
+    return is_gqa_family(c.family) || is_lighting(c) || is_cbr(c);
+}
 
 size_t dtype_size(int dtype) { return dtype == MR_DTYPE_F32 ? 4 : 2; }
 
@@ -162,6 +177,13 @@ struct mr_model {
     bool connected = false;
     Word *best_slots = nullptr;
     int xres_lo = 0, xres_n = 0;
+    // flashnano-1.6 chunk relays / FlashLighting memory slots: the work between two
+    // steps (aux_step.cuh), its layer table on the device and a host copy of it
+    bool aux_on = false;
+    aux::Model aux_model{};
+    aux::Layer *aux_layers = nullptr;
+    std::vector<aux::Layer> aux_host;
+    int aux_kvh = 0;  // the most KV heads of any layer (grid of the projections)
     // batched prefill (prefill.cu): available for BF16 models of the engine families
     bool prefill_ok = false, prefill_on = true;
     PrefillModel pm{};
@@ -423,9 +445,19 @@ int plan_lighting_layer(mr_model *m, int l) {
     kv.gemv.seg[1] = segment(tensor(m, p + "v"), m->v_raw);
     kv.gemv.epilogue = EPI_STORE;
     kv.gemv.skip = m->xres_skip;
+    if (is_lighting_memory(c)) {  // the raw latents, for rows that leave the window into memory
+        kv.gemv.save_in = m->aux_host[l].lat_ring;
+        kv.gemv.save_rows = m->cache_capacity[l];
+    }
     m->phases.push_back(kv);
     Phase at;
     if (int rc = attn_phase(m, l, true, 3, at)) return rc;
+    if (is_lighting_memory(c)) {  // the window ring, then the memory rows (model.py:160-165)
+        at.attn.relay_k = m->aux_host[l].relay_k;
+        at.attn.relay_v = m->aux_host[l].relay_v;
+        at.attn.relay_count = m->aux_host[l].relay_count;
+        at.attn.relay_capacity = m->aux_host[l].relay_cap;
+    }
     m->phases.push_back(at);
     float ag = 0.f, fg = 0.f;
     if (int rc = read_scalar(m, p + "attention_gate", ag)) return rc;
@@ -450,6 +482,128 @@ int plan_lighting_layer(mr_model *m, int l) {
     return MR_OK;
 }
 
+int reset_aux(mr_model *m);
+
+// Buffers and the layer table of the work between steps (aux_step.cuh).
+int setup_aux(mr_model *m) {
+    const mr_model_config &c = m->cfg;
+    m->aux_on = is_cbr(c) || is_lighting_memory(c);
+    if (!m->aux_on) return MR_OK;
+    MR_REQUIRE(m->ranks == 1, "chunk relays and latent memory run on one GPU");
+    const int d = c.head_dim, h = c.hidden_size;
+    int rc = MR_OK;
+    auto falloc = [&](size_t n) { return static_cast<float *>(device_alloc(m, std::max<size_t>(n, 1) * 4, &rc)); };
+    auto ialloc = [&](size_t n) { return static_cast<int *>(device_alloc(m, std::max<size_t>(n, 1) * 4, &rc)); };
+    aux::Model &am = m->aux_model;
+    am = aux::Model{};
+    am.layers = c.layers;
+    am.hidden = h;
+    am.d = d;
+    am.split_half = c.split_half_rope;
+    am.norm_eps = c.norm_eps;
+    am.inv_freq = m->d_inv_freq;
+    am.lighting = is_lighting_memory(c) ? 1 : 0;
+    am.chunk = c.cbr_chunk_size;
+    am.slots = c.cbr_slots;
+    am.memory_slots = c.memory_slots;
+    am.latent = c.latent_dim;
+    int *counts = ialloc(c.layers);
+    if (rc) return rc;
+    m->aux_host.assign(c.layers, aux::Layer{});
+    m->aux_kvh = 0;
+    for (int l = 0; l < c.layers && !rc; ++l) {
+        const std::string p = "layers." + std::to_string(l) + ".";
+        aux::Layer &L = m->aux_host[l];
+        const TensorSlot *wk = tensor(m, p + "k"), *wv = tensor(m, p + "v"), *kn = tensor(m, p + "k_norm");
+        MR_REQUIRE(wk && wv && kn && wk->dtype == wv->dtype, "layer %d: k / v / k_norm tensors", l);
+        L.wk = wk->ptr;
+        L.wv = wv->ptr;
+        L.w_dt = wk->dtype;
+        L.k_norm = kn->ptr;
+        L.k_norm_dt = kn->dtype;
+        L.kv_heads = m->layer_kvh[l];
+        L.kv_width = L.kv_heads * d;
+        m->aux_kvh = std::max(m->aux_kvh, L.kv_heads);
+        L.relay_count = counts + l;
+        L.last_pos = -1;
+        L.stash_pos[0] = L.stash_pos[1] = -1;
+        if (am.lighting) {
+            const int cap = m->cache_capacity[l], ms = c.memory_slots, lat = c.latent_dim;
+            MR_REQUIRE(lat <= 4096 && d <= 128, "latent memory: latent_dim %d / head_dim %d above 4096 / 128", lat, d);
+            am.window = cap;
+            const TensorSlot *ln = tensor(m, p + "latent_norm");
+            MR_REQUIRE(ln, "layer %d: latent_norm", l);
+            L.latent_norm = ln->ptr;
+            L.latent_norm_dt = ln->dtype;
+            L.lat_ring = falloc(static_cast<size_t>(cap) * lat);
+            L.k_cache = m->k_cache[l];
+            L.v_cache = m->v_cache[l];
+            L.mem_lat = falloc(static_cast<size_t>(ms) * lat);
+            L.mem_pos = ialloc(ms);
+            L.mem_cnt = falloc(ms);
+            L.mem_slot = ialloc(ms);
+            L.stash_k = falloc(2 * static_cast<size_t>(L.kv_width));
+            L.stash_v = falloc(2 * static_cast<size_t>(L.kv_width));
+            L.stash_lat = falloc(2 * static_cast<size_t>(lat));
+            L.relay_cap = ms;
+        } else {
+            const int C = c.cbr_chunk_size, S = c.cbr_slots;
+            MR_REQUIRE(h <= 4096 && d <= 128, "chunk relays: hidden %d / head_dim %d above 4096 / 128", h, d);
+            const TensorSlot *an = tensor(m, p + "a_norm"), *cbr = tensor(m, p + "cbr");
+            MR_REQUIRE(an && cbr, "layer %d: a_norm / cbr", l);
+            L.a_norm = an->ptr;
+            L.a_norm_dt = an->dtype;
+            L.pending = falloc(static_cast<size_t>(C) * h);
+            float *q = falloc(static_cast<size_t>(S) * h);
+            L.queries = q;
+            L.u = falloc(static_cast<size_t>(C) * h);
+            L.scores = falloc(static_cast<size_t>(S) * C);
+            L.pooled = falloc(static_cast<size_t>(S) * h);
+            L.anchors = falloc(S);
+            L.relay_cap = (c.context_length / C) * S;
+            if (rc) break;
+            aux::k_norm_rows<<<S, 32, 0, m->ctx->stream>>>(cbr->ptr, cbr->dtype, S, h, c.cbr_norm_eps, q);
+            MR_CUDA_TRY(cudaGetLastError());
+        }
+        L.relay_k = falloc(static_cast<size_t>(L.kv_heads) * std::max(1, L.relay_cap) * d);
+        L.relay_v = falloc(static_cast<size_t>(L.kv_heads) * std::max(1, L.relay_cap) * d);
+    }
+    if (rc) return rc;
+    m->aux_layers = static_cast<aux::Layer *>(device_alloc(m, sizeof(aux::Layer) * c.layers, &rc));
+    if (rc) return rc;
+    return reset_aux(m);
+}
+
+// A new sequence: the layer table as built (no relays, no memory, nothing planned).
+int reset_aux(mr_model *m) {
+    if (!m->aux_on) return MR_OK;
+    MR_CUDA_TRY(cudaMemcpyAsync(m->aux_layers, m->aux_host.data(), sizeof(aux::Layer) * m->aux_host.size(),
+                                cudaMemcpyHostToDevice, m->ctx->stream));
+    MR_CUDA_TRY(cudaMemsetAsync(m->aux_host[0].relay_count, 0, sizeof(int) * m->aux_host.size(), m->ctx->stream));
+    MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    return MR_OK;
+}
+
+// The work after one decode step (aux_step.cuh), queued behind it.
+int launch_aux(mr_model *m) {
+    cudaStream_t s = m->ctx->stream;
+    const aux::Model &am = m->aux_model;
+    const unsigned layers = static_cast<unsigned>(am.layers);
+    aux::k_aux_plan<<<(am.layers + 127) / 128, 128, 0, s>>>(am, m->aux_layers, m->state);
+    if (am.lighting) {
+        aux::k_aux_merge<<<dim3(2, layers), aux::kThreads, 0, s>>>(am, m->aux_layers);
+        aux::k_aux_move<<<dim3(8, layers), aux::kThreads, 0, s>>>(am, m->aux_layers);
+        aux::k_aux_merged_kv<<<dim3(2 * m->aux_kvh, layers), aux::kThreads, 0, s>>>(am, m->aux_layers);
+    } else {
+        aux::k_cbr_scores<<<dim3(am.chunk, layers), aux::kThreads, 0, s>>>(am, m->aux_layers);
+        aux::k_cbr_pool<<<dim3(am.slots, layers), aux::kThreads, sizeof(float) * am.chunk, s>>>(am, m->aux_layers,
+                                                                                               m->state);
+        aux::k_cbr_kv<<<dim3(am.slots * 2 * m->aux_kvh, layers), aux::kThreads, 0, s>>>(am, m->aux_layers);
+    }
+    MR_CUDA_TRY(cudaGetLastError());
+    return MR_OK;
+}
+
 int build_plan(mr_model *m) {
     const mr_model_config &c = m->cfg;
     if (!is_engine_family(c))
@@ -457,7 +611,7 @@ int build_plan(mr_model *m) {
     m->phases.clear();
     const TensorSlot *embed = tensor(m, "embed");
     for (int l = 0; l < c.layers; ++l) {
-        if (is_lighting_ring(c)) {
+        if (is_lighting(c)) {
             if (int rc = plan_lighting_layer(m, l)) return rc;
             continue;
         }
@@ -475,10 +629,20 @@ int build_plan(mr_model *m) {
         qkv.gemv.seg[2] = segment(tensor(m, p + "v"), m->v_raw);
         qkv.gemv.epilogue = EPI_STORE;
         qkv.gemv.skip = m->xres_skip;
+        if (is_cbr(c)) {  // the chunk's layer inputs, pooled into relays between steps
+            qkv.gemv.save_in = m->aux_host[l].pending;
+            qkv.gemv.save_rows = c.cbr_chunk_size;
+        }
         m->phases.push_back(qkv);
-        // 2. attention
+        // 2. attention (flashnano-1.6: the ring, then the relay rows)
         Phase at{};
         if (int rc = attn_phase(m, l, c.qk_norm, 1, at)) return rc;
+        if (is_cbr(c)) {
+            at.attn.relay_k = m->aux_host[l].relay_k;
+            at.attn.relay_v = m->aux_host[l].relay_v;
+            at.attn.relay_count = m->aux_host[l].relay_count;
+            at.attn.relay_capacity = m->aux_host[l].relay_cap;
+        }
         m->phases.push_back(at);
         // 3. o projection of the attention output + residual (model.py:282)
         Phase o = gemv_phase(l, m->attn_out, nullptr, 0.f);
@@ -760,7 +924,7 @@ int launch_step(mr_model *m, const StepControl &ctl) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     MR_CUDA_TRY(cudaLaunchKernelExC(&cfg, reinterpret_cast<const void *>(decode_step_kernel), args));
-    return MR_OK;
+    return m->aux_on ? launch_aux(m) : MR_OK;
 }
 
 StepControl base_control(mr_model *m) {
@@ -1308,7 +1472,7 @@ int mr_model_finalize(mr_model *m) {
     for (int l = 0; l < c.layers; ++l) {
         // model.py:105: capacity = min(window or context, context); FlashLighting's
         // window applies to every layer (model.py:167)
-        const int w = is_lighting_ring(c) ? c.window : m->layer_window[l];
+        const int w = is_lighting(c) ? c.window : m->layer_window[l];
         const int cap = std::min(w > 0 ? w : c.context_length, c.context_length);
         m->cache_capacity[l] = cap;
         const size_t n = (size_t)m->layer_kvh[l] * cap * d;
@@ -1334,7 +1498,8 @@ int mr_model_finalize(mr_model *m) {
     rank_rows(c.hidden_size, m->rank, m->ranks, m->xres_lo, m->xres_n);
     MR_REQUIRE((m->xres_n + m->grid - skip - 1) / (m->grid - skip) <= kRowBatch,
                "hidden size %d above the engine limit (rows per CTA)", c.hidden_size);
-    rc = build_plan(m);
+    rc = setup_aux(m);
+    if (!rc) rc = build_plan(m);
     if (!rc) rc = build_pieces(m);
     if (!rc) rc = build_groups(m);
     if (rc) return rc;
@@ -1425,6 +1590,7 @@ int mr_model_reset(mr_model *m) {
         const int rc = heavy_reset(m->heavy);
         if (rc) return rc;
     }
+    if (const int rc = reset_aux(m)) return rc;
     m->position = 0;
     m->failed = false;
     return MR_OK;
@@ -1547,20 +1713,81 @@ int mr_model_layer_state(const mr_model *m, int layer, int loop, mr_layer_state 
         out->latent_rows = out->ring_length;
         out->memory_size = 0;
     }
+    if (m->aux_on) {  // relay rows (flashnano-1.6) or memory rows (FlashLighting), read back
+        int count = 0;
+        MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+        MR_CUDA_TRY(cudaMemcpy(&count, m->aux_host[layer].relay_count, sizeof(int), cudaMemcpyDeviceToHost));
+        if (is_cbr(m->cfg)) {
+            out->relay_count = count;
+        } else {
+            out->memory_size = count;
+            out->latent_rows = count + out->ring_length;
+        }
+    }
     return MR_OK;
 }
+
+}  // extern "C"
+
+namespace {
+// FlashLighting with memory slots: positions and token counts of the memory rows
+// (logical order), then the window's rows (one token each).
+int latent_rows(const mr_model *m, int layer, std::vector<int> &pos, std::vector<float> &cnt) {
+    pos.clear();
+    cnt.clear();
+    const int n = std::min(m->position, m->cache_capacity[layer]);
+    if (m->aux_on) {
+        const aux::Layer &L = m->aux_host[layer];
+        int size = 0;
+        MR_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+        MR_CUDA_TRY(cudaMemcpy(&size, L.relay_count, sizeof(int), cudaMemcpyDeviceToHost));
+        pos.resize(size);
+        cnt.resize(size);
+        if (size) {
+            MR_CUDA_TRY(cudaMemcpy(pos.data(), L.mem_pos, sizeof(int) * size, cudaMemcpyDeviceToHost));
+            MR_CUDA_TRY(cudaMemcpy(cnt.data(), L.mem_cnt, sizeof(float) * size, cudaMemcpyDeviceToHost));
+        }
+    }
+    for (int i = 0; i < n; ++i) {
+        pos.push_back(m->position - n + i);
+        cnt.push_back(1.0f);
+    }
+    return MR_OK;
+}
+}  // namespace
+
+extern "C" {
 
 int mr_model_latent_positions(const mr_model *m, int layer, int *out, int capacity, int *rows) {
     MR_REQUIRE(m && rows, "NULL argument");
     MR_REQUIRE(layer >= 0 && layer < m->cfg.layers, "layer out of range");
     *rows = 0;
-    if (!m->finalized || m->op_path || !is_lighting_ring(m->cfg))
+    if (!m->finalized || m->op_path || !is_lighting(m->cfg))
         return set_error(MR_ERR_ARGUMENT, "model has no latent cache");
-    // the drop path keeps the newest rows, each at its own token position
-    const int n = std::min(m->position, m->cache_capacity[layer]);
+    std::vector<int> pos;
+    std::vector<float> cnt;
+    if (int rc = latent_rows(m, layer, pos, cnt)) return rc;
+    const int n = static_cast<int>(pos.size());
     MR_REQUIRE(out || n == 0, "NULL argument");
     MR_REQUIRE(capacity >= n, "positions buffer holds %d rows, need %d", capacity, n);
-    for (int i = 0; i < n; ++i) out[i] = m->position - n + i;
+    for (int i = 0; i < n; ++i) out[i] = pos[i];
+    *rows = n;
+    return MR_OK;
+}
+
+int mr_model_latent_counts(const mr_model *m, int layer, float *out, int capacity, int *rows) {
+    MR_REQUIRE(m && rows, "NULL argument");
+    MR_REQUIRE(layer >= 0 && layer < m->cfg.layers, "layer out of range");
+    *rows = 0;
+    if (!m->finalized || m->op_path || !is_lighting(m->cfg))
+        return set_error(MR_ERR_ARGUMENT, "model has no latent cache");
+    std::vector<int> pos;
+    std::vector<float> cnt;
+    if (int rc = latent_rows(m, layer, pos, cnt)) return rc;
+    const int n = static_cast<int>(cnt.size());
+    MR_REQUIRE(out || n == 0, "NULL argument");
+    MR_REQUIRE(capacity >= n, "counts buffer holds %d rows, need %d", capacity, n);
+    for (int i = 0; i < n; ++i) out[i] = cnt[i];
     *rows = n;
     return MR_OK;
 }

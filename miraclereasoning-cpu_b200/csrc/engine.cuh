@@ -115,6 +115,8 @@ struct GemvPhase {
     int group_stride;           //   CTA b's g-th at group_offset + b * group_stride + g
     int skip;                   // CTAs 0 .. skip-1 own no rows of the phase (see cta_row_range)
     int in_back;                // the input words carry the tag of the phase this many phases back
+    float *save_in;             // or NULL: the raw input row is also stored at row position % save_rows
+    int save_rows;              //   (flashnano-1.6 chunk inputs, FlashLighting latents; aux_step.cuh)
 };
 
 // Rows [r0, r1) of segment s owned by CTA b of G: the CTA's share of the

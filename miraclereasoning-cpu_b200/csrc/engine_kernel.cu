@@ -670,7 +670,16 @@ __device__ bool read_input(const GemvPhase &g, int cols, const StepInfo &info, i
                            bool norm, const void *gain, float &ss, int first, int count) {
     const int t = threadIdx.x - first;
     ss = 0.f;
+    // the phase's raw input row, kept for the work between steps (aux_step.cuh): stored by
+    // the CTA that owns row 0 of the first segment
+    float *saved = nullptr;
+    if (g.save_in) {
+        int r0, r1;
+        seg_cta_rows(g.seg[0], blockIdx.x, gridDim.x, g.skip, r0, r1);
+        if (r0 == 0 && r1 > 0) saved = g.save_in + static_cast<size_t>(info.position % g.save_rows) * cols;
+    }
     auto put = [&](int j, float v) {
+        if (saved) saved[j] = v;
         if (norm) {
             ss = fmaf(v, v, ss);
             if (gain) v = __fmul_rn(v, load_weight(gain, g.norm_gain_dtype, j));

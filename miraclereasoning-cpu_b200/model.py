@@ -13,11 +13,13 @@ once into HBM (no LRU, no host widening).  For the grouped-query families
 decode kernel (csrc/engine_kernel.cu) and greedy ``generate`` runs entirely on
 the device (argmax feeds the next step).  FlashLighting without memory slots
 runs on the same kernel (its latent cache as a key/value ring, see
-``engine_plans``); Heavy Medium runs its token step as device kernel launches
-with the block top-k and expert routing on the GPU (csrc/heavy.cu).
-flashnano-1.6 and FlashLighting with memory slots step on the host over the
-op kernels against the resident weights (stepper.py).  Sampled ``generate`` reads the logits each step and
-samples on the host with the reference's exact NumPy procedure.
+``engine_plans``), and so do flashnano-1.6 (chunk relays pooled on the device
+between steps) and FlashLighting with memory slots (rows that leave the window
+absorbed into memory rows, the oldest two merged, on the device between steps;
+csrc/aux_step.cuh); Heavy Medium runs its token step as device kernel launches
+with the block top-k and expert routing on the GPU (csrc/heavy.cu).  Sampled
+``generate`` reads the logits each step and samples on the host with the
+reference's exact NumPy procedure.
 """
 from __future__ import annotations
 
@@ -32,7 +34,6 @@ import numpy as np
 from . import _native
 from .backend import CUDABackend
 from .config import ModelConfig
-from .stepper import FAMILIES as HOST_STEPPED, OpStepper
 from .weights import DTYPE_BF16, DTYPE_F32, SafeTensors, ShardedSafeTensors, adapt_weights, expected_shapes, \
     stored_tensor
 
@@ -89,21 +90,17 @@ class LatentView:
 
 
 def engine_plans(config):
-    """Whether the token step runs on the device without the host stepper: the
-    grouped-query families and FlashLighting without memory slots (its latent
-    cache then only drops the oldest row, which the persistent decode kernel
-    keeps as a key/value ring), and Heavy Medium (csrc/heavy.cu: kernel
-    launches with the block top-k and the expert routing on the GPU)."""
-    if config.family not in HOST_STEPPED or config.family == "heavy-medium-2.0":
-        return True
-    return config.family == "flashlighting-2.0" and config.memory_slots == 0 and bool(config.window)
+    """Whether the device engine runs this configuration: every family does, given
+    a FlashLighting attention window (the reference's latent mask needs one,
+    model.py:165)."""
+    return config.family != "flashlighting-2.0" or bool(config.window)
 
 
 class RingDecisions:
     """FlashLighting's per-token latent decisions on the engine's ring (drop
     path): after the step at position p every layer keeps the latents of
     positions max(0, p + 1 - window) .. p and no memory rows.  Built on
-    demand, in the stepper's format (one list per token of one dict per layer)."""
+    demand, in the format the reference records (one list per token of one dict per layer)."""
 
     def __init__(self, model):
         self._model = model
@@ -135,6 +132,8 @@ class MiracleModel:
         per-token top-k blocks and experts in ``decisions`` (each token then reads
         them back from the device)."""
         self.config = config
+        if not engine_plans(config):
+            raise ValueError("flashlighting-2.0 needs an attention window (window / local_window)")
         if context_length is None:
             context_length = min(2048, config.max_positions)
         if type(context_length) is not int or not 0 < context_length <= config.max_positions:
@@ -170,7 +169,9 @@ class MiracleModel:
             # them with NumPy (model.py:221-222), for every distance in the context
             table = np.ascontiguousarray(np.log1p(np.arange(context_length, dtype=np.float32)), dtype=np.float32)
             _native.call("mr_model_set_log1p_table", self._handle, table.ctypes.data_as(_F32), len(table))
-        self.record_decisions = bool(record_decisions) and config.family == "heavy-medium-2.0"
+        self.record_decisions = bool(record_decisions) and (
+            config.family in ("heavy-medium-2.0", "flashnano-1.6")
+            or (config.family == "flashlighting-2.0" and config.memory_slots > 0))
         self._decisions = []
         if tensor_parallel is not None and tensor_parallel[1] > 1:
             self._connect(*tensor_parallel)
@@ -178,7 +179,6 @@ class MiracleModel:
         _native.call("mr_model_weight_bytes", self._handle, C.byref(used))
         self.weight_cache = ResidentWeights(int(used.value), weight_cache_bytes)
         self.frequencies = backend.upload(inv)
-        self._stepper = None if engine_plans(config) else OpStepper(self)
         self.reset()
 
     def __del__(self):
@@ -262,32 +262,39 @@ class MiracleModel:
     def reset(self):
         """Release sequence caches while retaining weights."""
         _native.call("mr_model_reset", self._handle)
-        if self._stepper is not None:
-            self._stepper.reset()
         self._decisions = []
         self._failed = False
 
     @property
     def position(self):
-        if self._stepper is not None:
-            return self._stepper.position
         value = C.c_int()
         _native.call("mr_model_position", self._handle, C.byref(value))
         return value.value
 
     @property
     def decisions(self):
-        """Per token and layer, the discrete choices of the host-stepped families
-        (heavy top-k blocks, MoE experts and weights, latent positions)."""
-        if self._stepper is not None:
-            return self._stepper.decisions
-        if self.config.family == "flashlighting-2.0":
+        """Per token and layer, the discrete choices the reference records
+        (heavy top-k blocks, MoE experts and weights, latent positions and memory size)."""
+        if self.config.family == "flashlighting-2.0" and not self.config.memory_slots:
             return RingDecisions(self)
         return self._decisions
 
     def _read_decisions(self):
-        """Heavy Medium: the last token's top-k blocks and experts, per layer and loop."""
+        """The last token's decisions per layer: Heavy Medium's top-k blocks and experts
+        per loop; FlashLighting's latent positions and memory size after compaction."""
         c, s = self.config, self.config.source
+        if c.family == "flashnano-1.6":  # chunk relays: no discrete choice to record
+            self._decisions.append([{} for _ in range(c.layers)])
+            return
+        if c.family == "flashlighting-2.0":
+            record = []
+            for layer in range(c.layers):
+                st = _native.LayerState()
+                _native.call("mr_model_layer_state", self._handle, layer, 0, C.byref(st))
+                record.append({"latent_positions": [self._latent_positions(layer, st.latent_rows)],
+                               "memory_size": [st.memory_size]})
+            self._decisions.append(record)
+            return
         heads, slots, max_k = c.query_heads, s["long_context"]["global_slots"], s["router_top_k_max"]
         blocks = (C.c_int * max(heads * slots, 1))()
         experts, weights = (C.c_int * max_k)(), (C.c_float * max_k)()
@@ -307,8 +314,6 @@ class MiracleModel:
     @property
     def states(self):
         """Per-layer cache views with the attributes the reference exposes."""
-        if self._stepper is not None:
-            return self._stepper.states
         c = self.config
         views = []
         for layer in range(c.layers):
@@ -329,7 +334,7 @@ class MiracleModel:
                     entry["latent"] = LatentView(st.latent_rows, c.latent_dim)
                     entry["memory_size"] = st.memory_size
                     entry["positions"] = self._latent_positions(layer, st.latent_rows)
-                    entry["counts"] = [1.0] * st.latent_rows  # each kept row stands for one token
+                    entry["counts"] = self._latent_counts(layer, st.latent_rows)
                 else:
                     entry["ring"] = RingView(st.ring_count, st.ring_capacity, st.ring_length, st.ring_start, width)
                     if c.family == "flashnano-1.6" and st.relay_count:
@@ -342,6 +347,12 @@ class MiracleModel:
         n = C.c_int()
         _native.call("mr_model_latent_positions", self._handle, layer, out, max(rows, 1), C.byref(n))
         return list(out[:n.value])
+
+    def _latent_counts(self, layer, rows):
+        out = (C.c_float * max(rows, 1))()
+        n = C.c_int()
+        _native.call("mr_model_latent_counts", self._handle, layer, out, max(rows, 1), C.byref(n))
+        return [float(v) for v in out[:n.value]]
 
     # token loop -------------------------------------------------------------------
     def _tokens(self, ids):
@@ -363,14 +374,7 @@ class MiracleModel:
         V = self.config.vocab_size
         out = np.empty((len(ids), V) if return_all else (V,), dtype=np.float32)
         try:
-            if self._stepper is not None:
-                for i, token in enumerate(ids):
-                    hidden = self._stepper.step(int(token))
-                    if return_all:
-                        out[i] = self._stepper.logits(hidden)
-                    elif i == len(ids) - 1:
-                        out[:] = self._stepper.logits(hidden)
-            elif self.record_decisions:
+            if self.record_decisions:
                 for i in range(len(ids)):
                     row = np.empty(V, dtype=np.float32)
                     _native.call("mr_model_prefill", self._handle, ids[i:].ctypes.data_as(_I32), 1, 0,
@@ -391,7 +395,7 @@ class MiracleModel:
     def decode(self, token_id):
         """Append one token to the current sequence and return next-token logits."""
         V = self.config.vocab_size
-        if (type(token_id) is int and 0 <= token_id < V and self._stepper is None and not self.record_decisions
+        if (type(token_id) is int and 0 <= token_id < V and not self.record_decisions
                 and not self._failed and self.position < self.context_length):
             # the common case, without building and checking an id array (prefill's checks
             # would all pass): one token straight to the C entry point
@@ -423,7 +427,7 @@ class MiracleModel:
         self.reset()
         if max_new_tokens == 0:
             return []
-        if temperature == 0 and self._stepper is None and not self.record_decisions:
+        if temperature == 0 and not self.record_decisions:
             return self._generate_greedy(tokens, max_new_tokens, eos)
         rng, generated = np.random.default_rng(seed), []
         logits = self.prefill(tokens)

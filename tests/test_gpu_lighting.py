@@ -38,7 +38,6 @@ def _case():
 def test_lighting_ring_engine_matches_oracle(backend):
     config, weights, prompt = _case()
     model = submodule("model").MiracleModel(config, weights, backend=backend, context_length=200)
-    assert model._stepper is None  # the persistent decode kernel runs it
     oracle = ReferenceModel(config, weights, backend=HostBackend("oracle"), context_length=200)
     got = model.prefill(prompt, return_all=True)
     want = oracle.prefill(prompt, return_all=True)

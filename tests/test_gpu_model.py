@@ -83,10 +83,10 @@ def test_generate_greedy_and_sampled(backend, name):
     assert tokens == golden["greedy"].tolist()
 
 
-# ---- families beyond the grouped-query engine: flashnano-1.6 and FlashLighting with
-# memory slots step on the host over the op kernels (stepper.py); FlashLighting without
-# memory slots runs on the decode kernel (key/value ring), Heavy Medium on the device
-# token step (csrc/heavy.cu) with its decisions read back per token ----------------------
+# ---- families beyond the grouped-query ring: flashnano-1.6 (chunk relays) and FlashLighting
+# (memory slots merged, or dropped) on the decode kernel with the work between steps of
+# csrc/aux_step.cuh, Heavy Medium on the device token step (csrc/heavy.cu); decisions are
+# read back per token ----------------------------------------------------------------------
 OP_CASES = ("nano16", "lighting", "lighting_drop", "heavy", "heavy_mid")
 
 

@@ -5,6 +5,7 @@ tests/test_inference.py:102-106) to this package and pins the config tables
 against fixtures the reference produced (tests/golden/configs.npz).
 """
 import ctypes
+import dataclasses
 import importlib
 import json
 import re
@@ -173,9 +174,12 @@ def test_engine_plans_routes_families():
     model = importlib.import_module("miraclereasoning-cpu_b200.model")
     for name in ("nano15", "nano17", "lite", "lighting", "heavy"):
         assert model.engine_plans(cases.synthetic.config_for(name)), name
-    assert not model.engine_plans(cases.micro_config("nano16"))           # chunk relays: host-stepped
-    assert not model.engine_plans(cases.micro_config("lighting"))         # memory slots: weighted merge
+    assert model.engine_plans(cases.micro_config("nano16"))         # chunk relays pooled between steps
+    assert model.engine_plans(cases.micro_config("lighting"))       # memory slots merged between steps
     assert model.engine_plans(cases.micro_config("lighting_drop"))
+    # FlashLighting's latent mask needs a window (the reference fails without one)
+    windowless = dataclasses.replace(cases.micro_config("lighting_drop"), window=None)
+    assert not model.engine_plans(windowless)
 
 
 def test_ring_decisions_follow_the_drop_path():
