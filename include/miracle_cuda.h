@@ -236,6 +236,18 @@ MR_API int mr_model_prefill(mr_model *model, const int *ids, int n, int return_a
  * logit sets *out_nonfinite and stops. */
 MR_API int mr_model_generate_greedy(mr_model *model, const int *ids, int n, int max_new, int eos,
                                     int *out_tokens, int *out_count, int *out_nonfinite);
+/* Seeded sampling on the device (reference: generate with temperature > 0,
+ * model.py:318-357 and the sampling procedure of model.py:343-352): the prompt,
+ * then per token the stable descending order of the logits, float64
+ * softmax at `temperature` over the top_k (0: all), the top_p cutoff and
+ * NumPy Generator.choice, every sum in NumPy's order, the draws from the PCG64
+ * state of numpy.random.default_rng(seed) given as pcg_state[4] = {state >> 64,
+ * state & (2^64-1), inc >> 64, inc & (2^64-1)}.  temperature 0 takes the argmax.
+ * Stops after eos or max_new tokens; *out_nonfinite = 1 when a non-finite
+ * logit stopped it (the reference raises there).  One GPU. */
+MR_API int mr_model_generate_sampled(mr_model *model, const int *ids, int n, int max_new, int eos, double temperature,
+                                     int top_k, double top_p, const uint64_t *pcg_state, int *out_tokens,
+                                     int *out_count, int *out_nonfinite);
 
 /* Cache state of one layer (and inner loop for heavy-medium-2.0), mirroring
  * what the reference keeps in MiracleModel.states (model.py:15-33, 104-190). */

@@ -92,6 +92,8 @@ SIGNATURES = {
     "mr_model_step": (_I, [_P, _I, _FP, _IP]),
     "mr_model_prefill": (_I, [_P, _IP, _I, _I, _FP]),
     "mr_model_generate_greedy": (_I, [_P, _IP, _I, _I, _I, _IP, _IP, _IP]),
+    "mr_model_generate_sampled": (_I, [_P, _IP, _I, _I, _I, C.c_double, _I, C.c_double, C.POINTER(C.c_uint64), _IP,
+                                      _IP, _IP]),
     "mr_model_layer_state": (_I, [_P, _I, _I, C.POINTER(LayerState)]),
     "mr_model_latent_positions": (_I, [_P, _I, _IP, _I, _IP]),
     "mr_model_latent_counts": (_I, [_P, _I, _FP, _I, _IP]),

@@ -21,6 +21,7 @@
 #include "heavy.cuh"
 #include "prefill.cuh"
 #include "aux_step.cuh"
+#include "sampler.cuh"
 
 namespace mr {
 
@@ -184,6 +185,7 @@ struct mr_model {
     aux::Layer *aux_layers = nullptr;
     std::vector<aux::Layer> aux_host;
     int aux_kvh = 0;  // the most KV heads of any layer (grid of the projections)
+    Sampler *sampler = nullptr;  // device sampling (sampler.cu), created on first use
     // batched prefill (prefill.cu): available for BF16 models of the engine families
     bool prefill_ok = false, prefill_on = true;
     PrefillModel pm{};
@@ -995,7 +997,7 @@ int heavy_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
         for (; first < n;) {
             const int T = std::min(kHeavyChunk, n - first);
             int rc = heavy_prefill(m->heavy, ids + first, T, m->position, return_all != 0);
-            if (!rc && (return_all || first + T == n)) {
+            if (!rc && out && (return_all || first + T == n)) {
                 const size_t rows = return_all ? T : 1;
                 const cudaError_t err =
                     cudaMemcpyAsync(out + (return_all ? static_cast<size_t>(first) * V : 0), heavy_prefill_logits(m->heavy),
@@ -1012,7 +1014,7 @@ int heavy_feed(mr_model *m, const int *ids, int n, int return_all, float *out) {
     }
     for (int i = first; i < n; ++i) {
         int rc = heavy_token(m->heavy, ids[i], m->position);
-        if (!rc && (return_all || i == n - 1)) {
+        if (!rc && out && (return_all || i == n - 1)) {
             const cudaError_t err = cudaMemcpyAsync(out + (return_all ? (size_t)i * V : 0), heavy_logits(m->heavy),
                                                     sizeof(float) * V, cudaMemcpyDeviceToHost, m->ctx->stream);
             if (err != cudaSuccess) rc = cuda_error(err, "logits read");
@@ -1282,6 +1284,7 @@ int mr_model_destroy(mr_model *m) {
     for (void *p : m->allocations) cudaFree(p);
     prefill_release(m->pw);
     heavy_destroy(m->heavy);
+    sampler_destroy(m->sampler);
     if (m->ev0) cudaEventDestroy(m->ev0);
     if (m->h_ids) cudaFreeHost(m->h_ids);
     if (m->h_logits) cudaFreeHost(m->h_logits);
@@ -1694,6 +1697,87 @@ int mr_model_generate_greedy(mr_model *m, const int *ids, int n, int max_new, in
     // leave the state ready for further decode calls
     MR_CUDA_TRY(cudaMemset(&m->state->stopped, 0, sizeof(int)));
     MR_CUDA_TRY(cudaMemset(&m->state->gen_count, 0, sizeof(int)));
+    return MR_OK;
+}
+
+int mr_model_generate_sampled(mr_model *m, const int *ids, int n, int max_new, int eos, double temperature,
+                              int top_k, double top_p, const uint64_t *pcg_state, int *out_tokens, int *out_count,
+                              int *out_nonfinite) {
+    int rc = ready(m);
+    if (rc) return rc;
+    MR_REQUIRE(ids && n > 0 && pcg_state && out_tokens && out_count && out_nonfinite, "NULL argument");
+    MR_REQUIRE(max_new > 0, "max_new must be positive");
+    MR_REQUIRE(std::isfinite(temperature) && temperature >= 0, "temperature must be finite and non-negative");
+    MR_REQUIRE(top_k >= 0 && std::isfinite(top_p) && top_p > 0 && top_p <= 1,
+               "top_k must be non-negative and top_p must be in (0,1]");
+    MR_REQUIRE(m->ranks == 1, "device sampling runs on one GPU");
+    const int V = m->cfg.vocab_size;
+    for (int i = 0; i < n; ++i) MR_REQUIRE(ids[i] >= 0 && ids[i] < V, "input token is outside the vocabulary");
+    MR_REQUIRE(eos >= 0 && eos < V, "eos_token_id is outside vocabulary");
+    MR_REQUIRE(m->position + n + max_new - 1 <= m->cfg.context_length,
+               "prompt plus requested generation exceeds context_length");
+    if (!m->sampler && (rc = sampler_create(V, &m->sampler))) return rc;
+    if ((rc = ensure_gen(m, max_new))) return rc;
+    cudaStream_t st = m->ctx->stream;
+    const unsigned long long pcg[4] = {pcg_state[0], pcg_state[1], pcg_state[2], pcg_state[3]};
+    if ((rc = sampler_seed(m->sampler, st, pcg))) return rc;
+    const SampleParams sp{temperature, top_p, top_k, eos, max_new};
+    *out_count = 0;
+    *out_nonfinite = 0;
+    int count = 0, nonfinite = 0;
+    if (m->heavy) {
+        // prompt (batched where it applies), then per token: sample on the device, the
+        // step from the sampled id; the host reads back only the stop state
+        const bool batched = n > 1 && m->prefill_on && heavy_batchable(m->heavy);
+        rc = heavy_feed(m, ids, n, 0, nullptr);
+        const float *logits = batched ? heavy_prefill_logits(m->heavy) : heavy_logits(m->heavy);
+        for (int i = 0; !rc && i < max_new; ++i) {
+            rc = sampler_step(m->sampler, st, logits, sp, heavy_token_slot(m->heavy), m->gen_out, nullptr);
+            if (!rc) rc = sampler_result(m->sampler, st, &count, &nonfinite);
+            if (rc || nonfinite || count < i + 1 || count == max_new || i + 1 == max_new) break;
+            int token = 0;
+            MR_CUDA_TRY(cudaMemcpy(&token, m->gen_out + i, sizeof(int), cudaMemcpyDeviceToHost));
+            if (token == eos) break;
+            rc = heavy_token_from_slot(m->heavy, m->position);
+            if (!rc) {
+                ++m->position;
+                logits = heavy_logits(m->heavy);
+            }
+        }
+        if (!rc) {
+            const cudaError_t err = cudaStreamSynchronize(st);
+            rc = err != cudaSuccess ? cuda_error(err, "heavy-medium-2.0 sampling") : heavy_status(m->heavy);
+        }
+        if (rc) {
+            m->failed = true;
+            return rc;
+        }
+    } else {
+        // prompt, then sample -> step -> sample ... queued without a synchronise: the step
+        // reads its token from the step state the sampler writes, and skips once stopped
+        const bool batched = m->prefill_ok && m->prefill_on && n > 1;
+        if ((rc = run_feed(m, ids, n, 0, nullptr))) return rc;
+        const float *logits = batched ? m->pw.logits : m->logits;
+        StepControl ctl = base_control(m);
+        for (int i = 0; i < max_new; ++i) {
+            rc = sampler_step(m->sampler, st, logits, sp, &m->state->token, m->gen_out, &m->state->stopped);
+            if (!rc && i + 1 < max_new) rc = launch_step(m, ctl);
+            if (rc) {
+                m->failed = true;
+                return rc;
+            }
+            logits = m->logits;
+        }
+        if ((rc = sync_and_check(m, "generate"))) return rc;
+        if ((rc = sampler_result(m->sampler, st, &count, &nonfinite))) return rc;
+        StepState s;
+        MR_CUDA_TRY(cudaMemcpy(&s, m->state, sizeof(s), cudaMemcpyDeviceToHost));
+        m->position = s.position;
+        MR_CUDA_TRY(cudaMemset(&m->state->stopped, 0, sizeof(int)));  // ready for further decode calls
+    }
+    *out_count = count;
+    *out_nonfinite = nonfinite;
+    if (count) MR_CUDA_TRY(cudaMemcpy(out_tokens, m->gen_out, sizeof(int) * count, cudaMemcpyDeviceToHost));
     return MR_OK;
 }
 

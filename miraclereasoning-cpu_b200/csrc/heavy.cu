@@ -1093,6 +1093,9 @@ int heavy_token(HeavyEngine *e, int token, int position) {
     return token_step(e, nullptr, token, position);
 }
 
+int heavy_token_from_slot(HeavyEngine *e, int position) { return token_step(e, e->d_token, 0, position); }
+int *heavy_token_slot(HeavyEngine *e) { return e->d_token; }
+
 int heavy_greedy_chain(HeavyEngine *e, int first_token, int position, int steps) {
     MR_REQUIRE(first_token >= 0 && first_token < e->vocab, "input token is outside the vocabulary");
     for (int i = 0; i < steps; ++i) {
@@ -1270,15 +1273,26 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
                                 static_cast<size_t>(e->hidden) * sizeof(float) + 16, s, rt))
                 return rc;
             if (int rc = stamp(*e)) return rc;
-            // 5-6. the chosen and the shared experts, then the rank-order combine (model.py:251-255)
-            if (e->ranks == 1 && e->streamable) {
+            // 5-6. the chosen and the shared experts, then the rank-order combine (model.py:251-255);
+            // expert parallel: this rank's experts, their rows to every rank, then the combine
+            unsigned long long tag = 0;
+            size_t out_offset = 0;
+            if (e->ranks > 1) {  // this step's half of the arena (the other half: the step before)
+                tag = ++e->moe_tag;
+                out_offset = (tag & 1) * e->out_bytes;
+            }
+            auto mine = [&](int expert) { return e->ranks == 1 || expert % e->ranks == e->rank; };
+            if (e->streamable) {
                 stream::Args g{};
                 g.mode = stream::kSwiglu;
                 g.dtype = Ly.expert_dtype;
                 g.cols = e->hidden;
                 for (int i = 0; i < e->shared; ++i)
-                    g.seg[g.nseg++] = stream::Seg{Ly.h_gate[e->experts + i], Ly.h_up[e->experts + i], nullptr, e->ffn,
-                                                  e->max_k + i};
+                    if (mine(e->experts + i))
+                        g.seg[g.nseg++] = stream::Seg{Ly.h_gate[e->experts + i], Ly.h_up[e->experts + i], nullptr,
+                                                      e->ffn, e->max_k + i};
+                g.rank = e->rank;
+                g.ranks = e->ranks;
                 g.dyn_w = Ly.d_gate;
                 g.dyn_w2 = Ly.d_up;
                 g.chosen = ra.chosen;
@@ -1300,8 +1314,13 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
                 dn.dtype = Ly.expert_dtype;
                 dn.cols = e->ffn;
                 for (int i = 0; i < e->shared; ++i)
-                    dn.seg[dn.nseg++] = stream::Seg{Ly.h_down[e->experts + i], nullptr, nullptr, e->hidden,
-                                                    e->max_k + i};
+                    if (mine(e->experts + i))
+                        dn.seg[dn.nseg++] = stream::Seg{Ly.h_down[e->experts + i], nullptr, nullptr, e->hidden,
+                                                        e->max_k + i};
+                dn.rank = e->rank;
+                dn.ranks = e->ranks;
+                dn.out_offset = out_offset;
+                for (int j = 0; j < e->ranks && e->ranks > 1; ++j) dn.peer[j] = e->peers[j];
                 dn.dyn_w = Ly.d_down;
                 dn.chosen = ra.chosen;
                 dn.active = ra.active;
@@ -1316,7 +1335,7 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
                 dn.xres = e->x;
                 if (int rc = launch_stream(*e, dn)) return rc;
                 if (int rc = stamp(*e)) return rc;
-                continue;
+                if (e->ranks == 1) continue;
             }
             ExpertArgs ea{};
             ea.gate = Ly.d_gate;
@@ -1340,22 +1359,24 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             ea.ranks = e->ranks;
             ea.err = e->err;
             ea.wait_ns = e->wait_ns;
-            if (e->ranks > 1) {  // this step's half of the arena (the other half: the step before)
-                ea.tag = ++e->moe_tag;
-                ea.out_offset = (ea.tag & 1) * e->out_bytes;
+            if (e->ranks > 1) {
+                ea.tag = tag;
+                ea.out_offset = out_offset;
                 ea.out = reinterpret_cast<float *>(e->arena + ea.out_offset);
                 ea.flags = reinterpret_cast<unsigned long long *>(e->arena + e->flags_offset);
                 ea.flags_offset = e->flags_offset;
                 for (int j = 0; j < e->ranks; ++j) ea.peer[j] = e->peers[j];
             }
-            if (int rc = launch(k_expert_gate_up, dim3((e->ffn + 7) / 8, slots_total), kGemvThreads,
-                                static_cast<size_t>(e->hidden) * sizeof(float) + 16, s, ea))
-                return rc;
-            if (int rc = stamp(*e)) return rc;
-            if (int rc = launch(k_expert_down, dim3((e->hidden + kGemvRows - 1) / kGemvRows, slots_total), kGemvThreads,
-                                static_cast<size_t>(e->ffn) * sizeof(float) + 16, s, ea))
-                return rc;
-            if (int rc = stamp(*e)) return rc;
+            if (!e->streamable) {  // rows that are not whole 16-byte pieces: the per-expert kernels
+                if (int rc = launch(k_expert_gate_up, dim3((e->ffn + 7) / 8, slots_total), kGemvThreads,
+                                    static_cast<size_t>(e->hidden) * sizeof(float) + 16, s, ea))
+                    return rc;
+                if (int rc = stamp(*e)) return rc;
+                if (int rc = launch(k_expert_down, dim3((e->hidden + kGemvRows - 1) / kGemvRows, slots_total),
+                                    kGemvThreads, static_cast<size_t>(e->ffn) * sizeof(float) + 16, s, ea))
+                    return rc;
+                if (int rc = stamp(*e)) return rc;
+            }
             if (e->ranks > 1) {
                 if (int rc = launch(k_moe_publish, 1, 32, 0, s, ea)) return rc;
                 if (int rc = stamp(*e)) return rc;

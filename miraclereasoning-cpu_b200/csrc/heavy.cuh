@@ -43,6 +43,11 @@ const float *heavy_logits(const HeavyEngine *e);
 // synchronous.  *count receives the number of stamps written.
 int heavy_trace_token(HeavyEngine *e, int token, int position, unsigned long long *stamps, int capacity, int *count);
 
+// The token step with its input token read from heavy_token_slot(e) (device
+// sampling writes it there), and that slot.
+int heavy_token_from_slot(HeavyEngine *e, int position);
+int *heavy_token_slot(HeavyEngine *e);
+
 // Batched prompt (heavy_prefill.cuh): T tokens (host ids) at positions p0 ..
 // p0 + T - 1 through every layer at once, GEMMs on tcgen05, leaving the state
 // heavy_token continues from; the logits of every token (all_logits) or of the

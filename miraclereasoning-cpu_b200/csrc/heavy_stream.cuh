@@ -38,6 +38,7 @@ constexpr int kSlotBytes = 16384;
 constexpr int kMaxSlots = 12;
 constexpr int kMaxSegs = 12;
 constexpr int kMaxPieceRows = 4;
+constexpr int kMaxPeers = 8;
 
 enum Mode { kPlain = 0, kSwiglu = 1, kDown = 2 };
 
@@ -71,6 +72,12 @@ struct Args {
     const float *weights;          // kDown: routed weights [max_k]
     float shared_scale;            // kDown: residual_scale / S
     float *xres;                   // kDown: x += scale * combine
+    // expert parallel (ranks > 1): only this rank's experts (id % ranks == rank) are streamed,
+    // and kDown stores each of its slots' rows into every rank's arena (peer[j] + out_offset,
+    // [max_k + shared][dyn_rows] floats) instead of combining; k_expert_combine sums them
+    int rank, ranks;
+    char *peer[kMaxPeers];
+    size_t out_offset;
     int *err;
     unsigned long long *probe;     // tracing only (heavy.cu probe), else NULL
     unsigned long long wait_ns;    // how long a bounded wait may last
@@ -177,6 +184,7 @@ __device__ __forceinline__ void for_each_piece(const Args &a, bool dynamic, int 
             atomicCAS(a.err, 0, 4);
             return;
         }
+        if (a.ranks > 1 && e % a.ranks != a.rank) continue;  // another rank's expert
         const char *w = static_cast<const char *>(a.dyn_w[e]);
         const char *w2 = a.dyn_w2 ? static_cast<const char *>(a.dyn_w2[e]) : nullptr;
         for (int r = lo; r < hi; r += P) {
@@ -471,6 +479,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(Args a) {
     consumers_sync();
     if (!ok) return;
     const int hi_dyn = slice_lo(a.dyn_rows, blockIdx.x + 1, gridDim.x);
+    if (a.ranks > 1) {  // expert parallel: this rank's slots' rows to every rank
+        for (int i = threadIdx.x; i < hi_dyn - lo_dyn; i += kConsumers) {
+            auto put = [&](int slot) {
+                const float v = outs[slot * rows_cta + i];
+                const size_t at = a.out_offset + (static_cast<size_t>(slot) * a.dyn_rows + lo_dyn + i) * sizeof(float);
+                for (int j = 0; j < a.ranks; ++j) *reinterpret_cast<float *>(a.peer[j] + at) = v;
+            };
+            for (int s = 0; s < a.nseg; ++s) put(a.seg[s].slot);
+            for (int k = 0; k < active; ++k)
+                if (a.chosen[k] % a.ranks == a.rank) put(k);
+        }
+        __threadfence_system();  // before k_moe_publish raises this rank's flag
+        return;
+    }
     for (int i = threadIdx.x; i < hi_dyn - lo_dyn; i += kConsumers) {
         float res = 0.f;
         for (int k = 0; k < active; ++k) res = FADD(res, FMUL(a.weights[k], outs[k * rows_cta + i]));

@@ -160,8 +160,10 @@ class MiracleModel:
             self._load(self.weights)
         else:
             self._fill_synthetic(*_synthetic)
+        self._ranks = 1
         if tensor_parallel is not None:
             rank, ranks, _ = tensor_parallel
+            self._ranks = int(ranks)
             _native.call("mr_model_set_tensor_parallel", self._handle, int(rank), int(ranks))
         _native.call("mr_model_finalize", self._handle)
         if config.family == "heavy-medium-2.0":
@@ -427,6 +429,10 @@ class MiracleModel:
         self.reset()
         if max_new_tokens == 0:
             return []
+        if not self.record_decisions and self._ranks == 1 and (temperature > 0 or self.config.family == "heavy-medium-2.0"):
+            # sampling (and Heavy Medium's argmax) on the device, the reference's procedure to the bit
+            return self._generate_on_device(tokens, max_new_tokens, eos, float(temperature), int(top_k),
+                                            float(top_p), np.random.default_rng(seed))
         if temperature == 0 and not self.record_decisions:
             return self._generate_greedy(tokens, max_new_tokens, eos)
         rng, generated = np.random.default_rng(seed), []
@@ -440,6 +446,24 @@ class MiracleModel:
                 break
             logits = self.decode(token)
         return generated
+
+    def _generate_on_device(self, tokens, max_new_tokens, eos, temperature, top_k, top_p, rng):
+        state = rng.bit_generator.state["state"]
+        mask = (1 << 64) - 1
+        pcg = (C.c_uint64 * 4)(state["state"] >> 64, state["state"] & mask, state["inc"] >> 64, state["inc"] & mask)
+        ids = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros(max_new_tokens, dtype=np.int32)
+        count, nonfinite = C.c_int(), C.c_int()
+        try:
+            _native.call("mr_model_generate_sampled", self._handle, ids.ctypes.data_as(_I32), len(ids),
+                         max_new_tokens, eos, temperature, top_k, top_p, pcg, out.ctypes.data_as(_I32),
+                         C.byref(count), C.byref(nonfinite))
+        except Exception:
+            self._failed = True
+            raise
+        if nonfinite.value:  # as the reference, which raises without latching (model.py:331-332)
+            raise FloatingPointError("non-finite output logits")
+        return [int(t) for t in out[:count.value]]
 
     def _generate_greedy(self, tokens, max_new_tokens, eos):
         ids = np.ascontiguousarray(tokens, dtype=np.int32)
