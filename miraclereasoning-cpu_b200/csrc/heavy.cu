@@ -350,25 +350,60 @@ __global__ void k_stamp(unsigned long long *slot) {
 // fewer than 8 terms in order; up to 128 in eight interleaved running sums
 // combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) plus the tail in order;
 // larger halves recursively (at a multiple of 8).
-__device__ float numpy_pairwise_sum(const float *a, int n) {
+// NumPy's pairwise summation of float32 (identity start; eight running sums up
+// to 128 values; halves above, the first a multiple of 8), without recursion:
+// an explicit stack visits the halves in the same order.
+__device__ float numpy_pairwise_leaf(const float *a, int n) {
     if (n < 8) {
         float res = 0.f;
         for (int i = 0; i < n; ++i) res = FADD(res, a[i]);
         return res;
     }
-    if (n <= 128) {
-        float r[8];
-        for (int j = 0; j < 8; ++j) r[j] = a[j];
-        int i = 8;
-        for (; i < n - (n % 8); i += 8)
-            for (int j = 0; j < 8; ++j) r[j] = FADD(r[j], a[i + j]);
-        float res = FADD(FADD(FADD(r[0], r[1]), FADD(r[2], r[3])), FADD(FADD(r[4], r[5]), FADD(r[6], r[7])));
-        for (; i < n; ++i) res = FADD(res, a[i]);
-        return res;
+    float r[8];
+    for (int j = 0; j < 8; ++j) r[j] = a[j];
+    int i = 8;
+    for (; i < n - (n % 8); i += 8)
+        for (int j = 0; j < 8; ++j) r[j] = FADD(r[j], a[i + j]);
+    float res = FADD(FADD(FADD(r[0], r[1]), FADD(r[2], r[3])), FADD(FADD(r[4], r[5]), FADD(r[6], r[7])));
+    for (; i < n; ++i) res = FADD(res, a[i]);
+    return res;
+}
+__device__ float numpy_pairwise_sum(const float *a, int n) {
+    constexpr int kDepth = 32;
+    int start[kDepth], len[kDepth], phase[kDepth];
+    float left[kDepth];
+    int top = 0;
+    start[0] = 0;
+    len[0] = n;
+    phase[0] = 0;
+    float value = 0.f;
+    while (top >= 0) {
+        const int m = len[top];
+        if (m <= 128) {
+            value = numpy_pairwise_leaf(a + start[top], m);
+            --top;
+            continue;
+        }
+        const int n2 = m / 2 - (m / 2) % 8;
+        if (phase[top] == 0) {
+            phase[top] = 1;
+            start[top + 1] = start[top];
+            len[top + 1] = n2;
+            phase[top + 1] = 0;
+            ++top;
+        } else if (phase[top] == 1) {
+            phase[top] = 2;
+            left[top] = value;
+            start[top + 1] = start[top] + n2;
+            len[top + 1] = m - n2;
+            phase[top + 1] = 0;
+            ++top;
+        } else {
+            value = FADD(left[top], value);
+            --top;
+        }
     }
-    int n2 = n / 2;
-    n2 -= n2 % 8;
-    return FADD(numpy_pairwise_sum(a, n2), numpy_pairwise_sum(a + n2, n - n2));
+    return value;
 }
 
 struct RouteArgs {

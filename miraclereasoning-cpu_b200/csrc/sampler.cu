@@ -63,27 +63,66 @@ __device__ __forceinline__ double next_double(SamplerState &s) {
     return static_cast<double>(out >> 11) * (1.0 / 9007199254740992.0);
 }
 
-// NumPy's pairwise summation of float64 (identity start, blocks of 8 up to 128, halves above).
-__device__ double pairwise_sum(const double *a, int n) {
+// NumPy's pairwise summation of float64: identity start; up to 8 values in
+// order; up to 128 in eight running sums combined as ((r0+r1)+(r2+r3)) +
+// ((r4+r5)+(r6+r7)) plus the tail; above that the two halves (the first a
+// multiple of 8) summed apart and added.  Evaluated without recursion: an
+// explicit stack visits the halves in the same order (depth <= 32 covers 2^36).
+__device__ double pairwise_leaf(const double *a, int n) {
     if (n < 8) {
         double res = 0.0;
         for (int i = 0; i < n; ++i) res = __dadd_rn(res, a[i]);
         return res;
     }
-    if (n <= 128) {
-        double r[8];
-        for (int j = 0; j < 8; ++j) r[j] = a[j];
-        int i = 8;
-        for (; i < n - (n % 8); i += 8)
-            for (int j = 0; j < 8; ++j) r[j] = __dadd_rn(r[j], a[i + j]);
-        double res = __dadd_rn(__dadd_rn(__dadd_rn(r[0], r[1]), __dadd_rn(r[2], r[3])),
-                               __dadd_rn(__dadd_rn(r[4], r[5]), __dadd_rn(r[6], r[7])));
-        for (; i < n; ++i) res = __dadd_rn(res, a[i]);
-        return res;
+    double r[8];
+    for (int j = 0; j < 8; ++j) r[j] = a[j];
+    int i = 8;
+    for (; i < n - (n % 8); i += 8)
+        for (int j = 0; j < 8; ++j) r[j] = __dadd_rn(r[j], a[i + j]);
+    double res = __dadd_rn(__dadd_rn(__dadd_rn(r[0], r[1]), __dadd_rn(r[2], r[3])),
+                           __dadd_rn(__dadd_rn(r[4], r[5]), __dadd_rn(r[6], r[7])));
+    for (; i < n; ++i) res = __dadd_rn(res, a[i]);
+    return res;
+}
+__device__ double pairwise_sum(const double *a, int n) {
+    constexpr int kDepth = 32;
+    int start[kDepth], len[kDepth], phase[kDepth];
+    double left[kDepth];
+    int top = 0;
+    start[0] = 0;
+    len[0] = n;
+    phase[0] = 0;
+    double value = 0.0;  // the value of the frame just finished
+    while (top >= 0) {
+        const int m = len[top];
+        if (m <= 128) {
+            value = pairwise_leaf(a + start[top], m);
+            --top;
+        } else {
+            const int n2 = m / 2 - (m / 2) % 8;
+            if (phase[top] == 0) {  // the first half
+                phase[top] = 1;
+                start[top + 1] = start[top];
+                len[top + 1] = n2;
+                phase[top + 1] = 0;
+                ++top;
+                continue;
+            }
+            if (phase[top] == 1) {  // the second half, the first's value kept
+                phase[top] = 2;
+                left[top] = value;
+                start[top + 1] = start[top] + n2;
+                len[top + 1] = m - n2;
+                phase[top + 1] = 0;
+                ++top;
+                continue;
+            }
+            value = __dadd_rn(left[top], value);
+            --top;
+        }
+        // a finished frame hands its value to its parent (phase 1 or 2 there)
     }
-    int n2 = n / 2;
-    n2 -= n2 % 8;
-    return __dadd_rn(pairwise_sum(a, n2), pairwise_sum(a + n2, n - n2));
+    return value;
 }
 
 // Descending logits as ascending keys (ties keep their order: the sort is stable).
