@@ -25,6 +25,7 @@ constexpr int kThreads = 256;
 constexpr int kRows = 32;     // attention: query rows per CTA (tokens x group heads)
 constexpr int kKT = 32;       // attention: keys (or blocks) per tile
 constexpr int kMaxSlots = 32;  // kept blocks per query head the attention supports
+constexpr int kPT = kRows + 4;  // key-major score / weight rows: four rows' weights in one float4
 
 // x[t] = embedding row of ids[t], widened exactly.
 __global__ void k_embed(const int *ids, int T, const void *embed, int dt, int h, float *x) {
@@ -255,8 +256,8 @@ __global__ void __launch_bounds__(kThreads) k_attention(AttnArgs a) {
     float *q = sm;                        // [kRows][d + 4]
     float *kt = q + kRows * ks;           // [2][kKT][d + 4]
     float *vt = kt + 2 * kKT * ks;        // [2][kKT][d]; phase A: each token's own block mean key | value
-    float *s = vt + 2 * kKT * d;          // [kRows][kKT + 1]
-    float *mrow = s + kRows * (kKT + 1), *lrow = mrow + kRows, *corr = lrow + kRows;
+    float *st = vt + 2 * kKT * d;         // [kKT][kPT] scores, then weights, key-major
+    float *mrow = st + kKT * kPT, *lrow = mrow + kRows, *corr = lrow + kRows;  // corr: 16-byte aligned
     float *bscore = corr + kRows;         // [kRows][nb]
     float *ksc = bscore + static_cast<size_t>(kRows) * a.nb;  // [kRows][kMaxSlots] kept scores
     int *kid = reinterpret_cast<int *>(ksc + kRows * kMaxSlots);  // [kRows][kMaxSlots] kept blocks, ascending
@@ -373,27 +374,23 @@ __global__ void __launch_bounds__(kThreads) k_attention(AttnArgs a) {
         lrow[r] = l;
     }
     __syncthreads();
-    const int nblk = (kRows / 2) * dq;  // output blocks: 2 rows x 4 dims
-    float acc[2][8];
+    // the output: thread = (four rows 4 rq .., four dims 4 dq4 ..), accumulators in registers
+    const int rq = tid >> 5, dq4 = tid & 31;
+    const bool has_dims = 4 * dq4 < d;
+    float acc[4][4];
 #pragma unroll
-    for (int b = 0; b < 2; ++b) {
+    for (int x = 0; x < 4; ++x) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[b][e] = 0.f;
-        const int blk = tid + b * kThreads;
-        if (blk >= nblk) continue;
-        const int r0 = (blk / dq) * 2, j0 = (blk % dq) * 4;
+        for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
+        const int r = 4 * rq + x;
+        if (r >= R || !has_dims) continue;
+        const int tt = r / G, own = (p_first + tt) / a.block;
+        for (int i = 0; i < nkept[r]; ++i) {
+            const int bb = kid[r * kMaxSlots + i];
+            const float w = expf(__fsub_rn(ksc[r * kMaxSlots + i], mrow[r]));
+            const float *vs = bb == own ? cur_v + tt * d : a.v_mean + static_cast<size_t>(bb) * width + kh * d;
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
-            const int r = r0 + x;
-            if (r >= R) continue;
-            const int tt = r / G, own = (p_first + tt) / a.block;
-            for (int i = 0; i < nkept[r]; ++i) {
-                const int bb = kid[r * kMaxSlots + i];
-                const float w = expf(__fsub_rn(ksc[r * kMaxSlots + i], mrow[r]));
-                const float *vs = bb == own ? cur_v + tt * d : a.v_mean + static_cast<size_t>(bb) * width + kh * d;
-#pragma unroll
-                for (int y = 0; y < 4; ++y) acc[b][x * 4 + y] = fmaf(w, vs[j0 + y], acc[b][x * 4 + y]);
-            }
+            for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(w, vs[4 * dq4 + y], acc[x][y]);
         }
     }
     __syncthreads();  // phase A's means in vt are read; the window tiles take it over
@@ -421,13 +418,30 @@ __global__ void __launch_bounds__(kThreads) k_attention(AttnArgs a) {
         }
         __syncthreads();
         const float *ktb = kt + buf * kKT * ks, *vtb = vt + buf * kKT * d;
-        {
+        {  // scores of row sr against keys sk, sk + 8, sk + 16, sk + 24: one query load per four keys,
+           // each score in the token step's association (four chains, (a0 + a1) + (a2 + a3))
+            float c[4][4];
+#pragma unroll
+            for (int y = 0; y < 4; ++y)
+#pragma unroll
+                for (int z = 0; z < 4; ++z) c[y][z] = 0.f;
+            for (int j = 0; j < d; j += 4) {
+                const float4 q4 = *reinterpret_cast<const float4 *>(q + sr * ks + j);
+#pragma unroll
+                for (int y = 0; y < 4; ++y) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(ktb + (sk + 8 * y) * ks + j);
+                    c[y][0] = fmaf(q4.x, k4.x, c[y][0]);
+                    c[y][1] = fmaf(q4.y, k4.y, c[y][1]);
+                    c[y][2] = fmaf(q4.z, k4.z, c[y][2]);
+                    c[y][3] = fmaf(q4.w, k4.w, c[y][3]);
+                }
+            }
             const int p = p_first + sr / G;
 #pragma unroll
             for (int y = 0; y < 4; ++y) {
                 const int kk = sk + 8 * y, pos = kb + kk;
                 const bool live = sr < R && kk < nk && pos <= p && pos > p - a.window;
-                s[sr * (kKT + 1) + kk] = live ? score4(q + sr * ks, ktb + kk * ks, d, sqrt_d) : -INFINITY;
+                st[kk * kPT + sr] = live ? __fdiv_rn((c[y][0] + c[y][1]) + (c[y][2] + c[y][3]), sqrt_d) : -INFINITY;
             }
         }
         __syncthreads();
@@ -435,7 +449,7 @@ __global__ void __launch_bounds__(kThreads) k_attention(AttnArgs a) {
             float v[4], mt[4], pr[4], sum[4];
 #pragma unroll
             for (int x = 0; x < 4; ++x) {
-                v[x] = s[(warp + 8 * x) * (kKT + 1) + lane];
+                v[x] = st[lane * kPT + warp + 8 * x];
                 mt[x] = v[x];
             }
 #pragma unroll
@@ -458,7 +472,7 @@ __global__ void __launch_bounds__(kThreads) k_attention(AttnArgs a) {
 #pragma unroll
             for (int x = 0; x < 4; ++x) {
                 const int r = warp + 8 * x;
-                s[r * (kKT + 1) + lane] = pr[x];
+                st[lane * kPT + r] = pr[x];
                 if (lane == 0) {
                     const float m_old = mrow[r];
                     const float cf = m_old == -INFINITY ? 0.f : expf(__fsub_rn(m_old, mt[x]));
@@ -469,57 +483,47 @@ __global__ void __launch_bounds__(kThreads) k_attention(AttnArgs a) {
             }
         }
         __syncthreads();
-#pragma unroll
-        for (int b = 0; b < 2; ++b) {  // value mix: 2 rows x 4 dims per block
-            const int blk = tid + b * kThreads;
-            if (blk >= nblk) continue;
-            const int r0 = (blk / dq) * 2, j0 = (blk % dq) * 4;
-            if (r0 >= R) continue;
-            const float c0 = corr[r0], c1 = corr[r0 + 1];
+        if (has_dims && 4 * rq < R) {  // value mix: the four rows' weights of a key in one broadcast load
+            const float4 cr = *reinterpret_cast<const float4 *>(corr + 4 * rq);
 #pragma unroll
             for (int y = 0; y < 4; ++y) {
-                acc[b][y] *= c0;
-                acc[b][4 + y] *= c1;
+                acc[0][y] *= cr.x;
+                acc[1][y] *= cr.y;
+                acc[2][y] *= cr.z;
+                acc[3][y] *= cr.w;
             }
-            const float *s0 = s + r0 * (kKT + 1), *s1 = s0 + (kKT + 1);
             for (int kk = 0; kk < nk; ++kk) {
-                const float4 vv = *reinterpret_cast<const float4 *>(vtb + kk * d + j0);
-                const float w0 = s0[kk], w1 = s1[kk];
-                acc[b][0] = fmaf(w0, vv.x, acc[b][0]);
-                acc[b][1] = fmaf(w0, vv.y, acc[b][1]);
-                acc[b][2] = fmaf(w0, vv.z, acc[b][2]);
-                acc[b][3] = fmaf(w0, vv.w, acc[b][3]);
-                acc[b][4] = fmaf(w1, vv.x, acc[b][4]);
-                acc[b][5] = fmaf(w1, vv.y, acc[b][5]);
-                acc[b][6] = fmaf(w1, vv.z, acc[b][6]);
-                acc[b][7] = fmaf(w1, vv.w, acc[b][7]);
+                const float4 w4 = *reinterpret_cast<const float4 *>(st + kk * kPT + 4 * rq);
+                const float4 vv = *reinterpret_cast<const float4 *>(vtb + kk * d + 4 * dq4);
+                const float wx[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+                    acc[x][0] = fmaf(wx[x], vv.x, acc[x][0]);
+                    acc[x][1] = fmaf(wx[x], vv.y, acc[x][1]);
+                    acc[x][2] = fmaf(wx[x], vv.z, acc[x][2]);
+                    acc[x][3] = fmaf(wx[x], vv.w, acc[x][3]);
+                }
             }
         }
         __syncthreads();  // every reader of buffer buf is done before it is refilled
     }
+    if (!has_dims) return;
 #pragma unroll
-    for (int b = 0; b < 2; ++b) {
-        const int blk = tid + b * kThreads;
-        if (blk >= nblk) continue;
-        const int r0 = (blk / dq) * 2, j0 = (blk % dq) * 4;
+    for (int x = 0; x < 4; ++x) {
+        const int r = 4 * rq + x;
+        if (r >= R) continue;
+        const int tt = r / G, g = r - tt * G;
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
-            const int r = r0 + x;
-            if (r >= R) continue;
-            const int tt = r / G, g = r - tt * G;
-#pragma unroll
-            for (int y = 0; y < 4; ++y)
-                put_planes(a.planes, a.ps, static_cast<size_t>(t0 + tt) * a.ld + (kh * G + g) * d + j0 + y,
-                           __fdiv_rn(acc[b][x * 4 + y], lrow[r]));
-        }
+        for (int y = 0; y < 4; ++y)
+            put_planes(a.planes, a.ps, static_cast<size_t>(t0 + tt) * a.ld + (kh * G + g) * d + 4 * dq4 + y,
+                       __fdiv_rn(acc[x][y], lrow[r]));
     }
 }
 
 // Shared memory of k_attention for head dim d and nb blocks.
 inline size_t attention_smem(int d, int nb) {
     return sizeof(float) * (static_cast<size_t>(kRows) * (d + 4) + 2 * kKT * (d + 4) + 2 * static_cast<size_t>(kKT) * d +
-                            kRows * (kKT + 1) + 3 * kRows + static_cast<size_t>(kRows) * nb + 2 * kRows * kMaxSlots +
-                            kRows);
+                            kKT * kPT + 3 * kRows + static_cast<size_t>(kRows) * nb + 2 * kRows * kMaxSlots + kRows);
 }
 
 }  // namespace hp
