@@ -312,16 +312,27 @@ __device__ void stage(const float *x, int n, bool norm, const void *gain, int ga
 // The down projection's inputs: the act rows of the active slots (routed
 // 0 .. active-1, shared max_k ..), all loads of all rows in one pass.
 __device__ void stage_acts(const Args &a, int active, bool split, float *xs) {
-    const int slots_total = a.max_k + a.shared, n = a.cols, q = n / 4;
-    for (int i = threadIdx.x; i < slots_total * q; i += kConsumers) {
-        const int k = i / q, c = 4 * (i % q);
-        if (k >= active && k < a.max_k) continue;
-        const float4 v = __ldcg(reinterpret_cast<const float4 *>(a.acts + static_cast<size_t>(k) * n + c));
-        float *dst = xs + static_cast<size_t>(k) * n;
-        dst[plane_index(c, n, split)] = v.x;
-        dst[plane_index(c + 1, n, split)] = v.y;
-        dst[plane_index(c + 2, n, split)] = v.z;
-        dst[plane_index(c + 3, n, split)] = v.w;
+    const int slots_total = a.max_k + a.shared, n = a.cols, q = n / 4, total = slots_total * q;
+    constexpr int kBatch = 8;  // loads in flight per thread before the first store
+    for (int i0 = threadIdx.x; i0 < total; i0 += kBatch * kConsumers) {
+        float4 v[kBatch];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            const int i = i0 + b * kConsumers, k = i / q;
+            const bool live = i < total && !(k >= active && k < a.max_k);
+            v[b] = live ? __ldcg(reinterpret_cast<const float4 *>(a.acts + static_cast<size_t>(k) * n + 4 * (i % q)))
+                        : float4{};
+        }
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            const int i = i0 + b * kConsumers, k = i / q, c = 4 * (i % q);
+            if (i >= total || (k >= active && k < a.max_k)) continue;
+            float *dst = xs + static_cast<size_t>(k) * n;
+            dst[plane_index(c, n, split)] = v[b].x;
+            dst[plane_index(c + 1, n, split)] = v[b].y;
+            dst[plane_index(c + 2, n, split)] = v[b].z;
+            dst[plane_index(c + 3, n, split)] = v[b].w;
+        }
     }
 }
 
