@@ -45,6 +45,7 @@
 #include "common.cuh"
 #include "heavy.cuh"
 #include "prefill.cuh"
+#include "tcgen05.cuh"
 
 namespace mr {
 
@@ -725,8 +726,10 @@ struct HeavyBatch {
     int *ids = nullptr, *err = nullptr;
     float *x = nullptr, *qlat = nullptr, *kv = nullptr, *qh = nullptr, *sum_k = nullptr, *sum_v = nullptr,
           *rlog = nullptr, *weights = nullptr, *gu = nullptr, *rout = nullptr, *sgu = nullptr, *sout = nullptr,
-          *logits = nullptr;
+          *logits = nullptr, *bstate = nullptr;
+    bool window_tc = false;  // the window part of the attention on tcgen05 (head_dim 128)
     uint16_t *planes = nullptr, *gplanes = nullptr, *gsplanes = nullptr;
+    uint8_t *kv_planes = nullptr;  // window_tc: the key / value tiles of every 64-key block the chunk reaches
     int *chosen = nullptr, *active = nullptr, *row_of = nullptr, *token_of = nullptr, *tiles = nullptr,
         *tile_count = nullptr, *rows = nullptr;
     // per layer, kept with the engine: router rows, expert maps (gate | up pairs, down)
@@ -1549,6 +1552,10 @@ int batch_reserve(HeavyEngine &e, int tokens, bool all_logits) {
     if (!rc) rc = get(f4 * T * 2 * static_cast<size_t>(f) * std::max(1, e.shared), &b.sgu);
     if (!rc) rc = get(f4 * T * static_cast<size_t>(h) * std::max(1, e.shared), &b.sout);
     if (!rc) rc = get(f4 * (all ? T : 1) * static_cast<size_t>(e.vocab), &b.logits);
+    b.window_tc = e.d == hp::kWDim && hp::kWRows % (e.H / e.KVH) == 0;
+    if (!rc && b.window_tc) rc = get(f4 * T * static_cast<size_t>(e.H) * (e.d + 2), &b.bstate);
+    if (!rc && b.window_tc)
+        rc = get(hp::kTileBytes * e.KVH * static_cast<size_t>((T + e.window) / hp::kWKeys + 2), &b.kv_planes);
     // per layer: coarse | fine router rows as one matrix, the experts' weight maps
     const size_t router_rows = static_cast<size_t>(e.groups) + E;
     if (!rc) rc = get(u2 * router_rows * h * e.layers, &b.router_w);
@@ -1581,6 +1588,9 @@ int batch_reserve(HeavyEngine &e, int tokens, bool all_logits) {
     if (!rc)
         MR_CUDA_TRY(cudaFuncSetAttribute(hp::k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(hp::attention_smem(e.d, (e.context + e.block - 1) / e.block))));
+    if (!rc && b.window_tc)
+        MR_CUDA_TRY(cudaFuncSetAttribute(hp::k_window_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(hp::kWindowSmem)));
     if (rc) {
         batch_release(b);
         return rc;
@@ -1667,9 +1677,36 @@ int heavy_prefill(HeavyEngine *e, const int *ids, int T, int p0, bool all_logits
             aa.ps = ps;
             aa.ld = b.kmax;
             aa.kept_last = e->kept + li * H * slots_max;
+            aa.block_state = b.window_tc ? b.bstate : nullptr;  // the window part then runs on tcgen05
             const int QT = hp::kRows / G;
             hp::k_attention<<<dim3((T + QT - 1) / QT, KVH), hp::kThreads, hp::attention_smem(d, nb), s>>>(aa);
             MR_CUDA_TRY(cudaGetLastError());
+            if (b.window_tc) {
+                // the 64-key blocks from the first one a window of the chunk reaches to the chunk's end
+                const int block0 = std::max(0, p0 - e->window + 1) / hp::kWKeys;
+                const int nblocks = (p0 + T - 1) / hp::kWKeys - block0 + 1;
+                hp::k_kv_planes<<<nblocks * KVH, 256, 0, s>>>(e->k_ring[li], e->v_ring[li], KVH, block0, p0 + T,
+                                                              b.kv_planes);
+                MR_CUDA_TRY(cudaGetLastError());
+                hp::WindowArgs wa{};
+                wa.qh = b.qh;
+                wa.kv_planes = b.kv_planes;
+                wa.block0 = block0;
+                wa.block_state = b.bstate;
+                wa.T = T;
+                wa.p0 = p0;
+                wa.H = H;
+                wa.KVH = KVH;
+                wa.d = d;
+                wa.window = e->window;
+                wa.planes = b.planes;
+                wa.ps = ps;
+                wa.ld = b.kmax;
+                wa.err = b.err;
+                const int WT = hp::kWRows / G;
+                hp::k_window_tc<<<dim3((T + WT - 1) / WT, KVH), hp::kWThreads, hp::kWindowSmem, s>>>(wa);
+                MR_CUDA_TRY(cudaGetLastError());
+            }
             // x += s W_o attended
             const BatchSeg os = {Ly.o.w, h, 0};
             rc = batch_gemm(s, b.err, b.planes, ps, b.kmax, T, qd, &os, 1, b.x, h, true, loop_scale);

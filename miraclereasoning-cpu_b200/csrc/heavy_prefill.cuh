@@ -217,6 +217,8 @@ struct AttnArgs {
     size_t ps;
     int ld;
     int *kept_last;                // [H][slots_max]: the chunk's last token's kept blocks
+    float *block_state;            // or NULL: stop after the block part and leave each row's softmax
+                                   // state here ([T * H][d + 2]: weighted values, max, sum) for k_window_tc
 };
 
 // q . k / sqrt(d) with the token step's association (attn::tile_score): four
@@ -393,6 +395,23 @@ __global__ void __launch_bounds__(kThreads) k_attention(AttnArgs a) {
             for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(w, vs[4 * dq4 + y], acc[x][y]);
         }
     }
+    if (a.block_state) {  // the window runs on the tensor cores (k_window_tc), from this state
+        if (!has_dims) return;
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+            const int r = 4 * rq + x;
+            if (r >= R) continue;
+            const int tt = r / G, g = r - tt * G;
+            float *row = a.block_state + (static_cast<size_t>(t0 + tt) * a.H + kh * G + g) * (d + 2);
+#pragma unroll
+            for (int y = 0; y < 4; ++y) row[4 * dq4 + y] = acc[x][y];
+            if (dq4 == 0) {
+                row[d] = mrow[r];
+                row[d + 1] = lrow[r];
+            }
+        }
+        return;
+    }
     __syncthreads();  // phase A's means in vt are read; the window tiles take it over
     // B. the window (p - window, p] of every row
     const int lo = max(0, p_first - a.window + 1);
@@ -517,6 +536,319 @@ __global__ void __launch_bounds__(kThreads) k_attention(AttnArgs a) {
         for (int y = 0; y < 4; ++y)
             put_planes(a.planes, a.ps, static_cast<size_t>(t0 + tt) * a.ld + (kh * G + g) * d + 4 * dq4 + y,
                        __fdiv_rn(acc[x][y], lrow[r]));
+    }
+}
+
+// ---- the window part on the tensor cores ------------------------------------------------
+// CTA = 128 rows (128 / G tokens x the G query heads of KV head kh), two threads
+// per row (its TMEM lane, from warps w and w + 4: half the output dims each).  Per tile of 64 keys of the rows' windows:
+//   S = Q K^T   (M 128, N 64, K 128): Q and K as three BF16 parts each, the six
+//               products down to 2^-16 x 2^-8 (Qh Kh, Qh Km, Qm Kh, Qh Kl, Ql Kh, Qm Km)
+//   softmax     each thread its row: scale, window mask, running max / sum (online)
+//   O_t = P V   (M 128, N 128, K 64): P (into the key tile's space) and V^T, three parts each
+//   o = o * correction + O_t in registers.
+// Operands are written by the threads straight into the 128-byte-swizzled K-major
+// layout (tc::sw128_offset) and read by tcgen05.mma from shared memory; S and O_t
+// accumulate in TMEM.  The state starts from the block part's (k_attention with
+// block_state), so the result is the softmax over kept blocks and window together.
+struct WindowArgs {
+    const float *qh;               // [T][H * d] normalised, rotated queries
+    const uint8_t *kv_planes;      // k_kv_planes: per 64-key block from block0 and KV head, K then V^T tiles
+    int block0;                    // the first 64-key block held there
+    const float *block_state;      // [T * H][d + 2]
+    int T, p0, H, KVH, d, window;
+    uint16_t *planes;              // output: planes of the o projection's input [3][T][ld]
+    size_t ps;
+    int ld;
+    int *err;                      // a bounded wait gave up
+};
+constexpr int kWRows = 128, kWKeys = 64, kWThreads = 256, kWDim = 128;
+constexpr uint32_t kQPlane = 2 * 16384;  // 128 rows x 128 dims: two 64-wide atoms
+constexpr uint32_t kKPlane = 2 * 8192;   // 64 keys x 128 dims (the same space: P, 128 rows x 64 keys)
+constexpr uint32_t kVPlane = 16384;      // V^T: 128 dims x 64 keys
+constexpr size_t kWindowSmem = 1024 + 3 * kQPlane + 3 * kKPlane + 3 * kVPlane + 64;
+
+// Three BF16 parts of eight values (x = p0 + p1 + p2 exactly), each as 16 bytes.
+__device__ __forceinline__ void split8(const float (&v)[8], uint4 (&part)[3]) {
+    uint32_t w[3][4];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        uint16_t h[2][3];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const float x = v[i + e];
+            const uint16_t a0 = bf16_bits(x);
+            const float r1 = __fsub_rn(x, bf16_value(a0));
+            const uint16_t a1 = bf16_bits(r1);
+            const uint16_t a2 = bf16_bits(__fsub_rn(r1, bf16_value(a1)));
+            h[e][0] = a0;
+            h[e][1] = a1;
+            h[e][2] = a2;
+        }
+#pragma unroll
+        for (int pl = 0; pl < 3; ++pl) w[pl][i / 2] = static_cast<uint32_t>(h[0][pl]) | (static_cast<uint32_t>(h[1][pl]) << 16);
+    }
+#pragma unroll
+    for (int pl = 0; pl < 3; ++pl) part[pl] = make_uint4(w[pl][0], w[pl][1], w[pl][2], w[pl][3]);
+}
+
+// Key and value tiles in the window kernel's shared-memory layout, built once per
+// layer and loop for every 64-key block a chunk's windows reach: per (block,
+// KV head) the three parts of K (64 keys x 128 dims, two 64-dim atoms) and of
+// V^T (128 dims x 64 keys), 96 KB, copied by the window kernel as they are.
+// Keys past `keys` (the chunk's end) are zero.
+constexpr size_t kTileBytes = 3 * kKPlane + 3 * kVPlane;
+__host__ __device__ __forceinline__ size_t kv_tile_offset(int block, int KVH, int kh) {
+    return (static_cast<size_t>(block) * KVH + kh) * kTileBytes;
+}
+__global__ void __launch_bounds__(256) k_kv_planes(const float *k_rows, const float *v_rows, int KVH, int block0,
+                                                   int keys, uint8_t *planes) {
+    const int blk = block0 + static_cast<int>(blockIdx.x) / KVH, kh = blockIdx.x % KVH, tid = threadIdx.x;
+    const int width = KVH * kWDim, kb = blk * kWKeys;
+    uint8_t *tile = planes + kv_tile_offset(blockIdx.x / KVH, KVH, kh);
+    {  // K: thread = (key, 32 dims)
+        const int kk = tid >> 2, q4 = tid & 3, atom = q4 >> 1;
+        const bool live = kb + kk < keys;
+        const float *src = k_rows + static_cast<size_t>(kb + kk) * width + kh * kWDim + q4 * 32;
+        float4 x[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) x[c] = live ? __ldcg(reinterpret_cast<const float4 *>(src) + c) : float4{};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float v[8] = {x[2 * c].x, x[2 * c].y, x[2 * c].z, x[2 * c].w,
+                                x[2 * c + 1].x, x[2 * c + 1].y, x[2 * c + 1].z, x[2 * c + 1].w};
+            uint4 part[3];
+            split8(v, part);
+#pragma unroll
+            for (int pl = 0; pl < 3; ++pl)
+                *reinterpret_cast<uint4 *>(tile + pl * kKPlane + atom * 8192 +
+                                           tc::sw128_offset(kk, (q4 & 1) * 32 + c * 8)) = part[pl];
+        }
+    }
+    {  // V^T: thread = (dim j, 32 keys)
+        const int j = tid & 127, k0 = (tid >> 7) * 32;
+        float x[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            x[i] = kb + k0 + i < keys ? __ldcg(v_rows + static_cast<size_t>(kb + k0 + i) * width + kh * kWDim + j) : 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float v[8] = {x[8 * c], x[8 * c + 1], x[8 * c + 2], x[8 * c + 3],
+                                x[8 * c + 4], x[8 * c + 5], x[8 * c + 6], x[8 * c + 7]};
+            uint4 part[3];
+            split8(v, part);
+#pragma unroll
+            for (int pl = 0; pl < 3; ++pl)
+                *reinterpret_cast<uint4 *>(tile + 3 * kKPlane + pl * kVPlane + tc::sw128_offset(j, k0 + c * 8)) = part[pl];
+        }
+    }
+}
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     tc::saddr(dst)),
+                 "l"(src), "r"(bytes), "r"(tc::saddr(bar))
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(kWThreads, 1) k_window_tc(WindowArgs a) {
+    extern __shared__ uint8_t w_raw[];
+    uint8_t *qs = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(w_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *kp = qs + 3 * kQPlane;  // the key tile, then (after S) the weights P
+    uint8_t *vt = kp + 3 * kKPlane;
+    // [0] S done, [1] O done, [2] the key tile landed, [3] the value tile landed
+    uint64_t *bar = reinterpret_cast<uint64_t *>(vt + 3 * kVPlane);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 4);
+    const int G = a.H / a.KVH, QT = kWRows / G, kh = blockIdx.y, t0 = blockIdx.x * QT;
+    const int nt = min(QT, a.T - t0), R = nt * G;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // two threads per row (TMEM lane): warps w and w + 4; `half` picks the output dims and P chunks
+    const int r = (warp & 3) * 32 + lane, half = warp >> 2, tt = r / G, g = r - tt * G;
+    const bool live = r < R;
+    const int p = a.p0 + t0 + tt, p_first = a.p0 + t0, p_last = p_first + nt - 1;
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc::saddr(&bar[0])) : "memory");
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc::saddr(&bar[1])) : "memory");
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc::saddr(&bar[2])) : "memory");
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc::saddr(&bar[3])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {  // S: columns 0..63, O_t: 128..255
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(tc::saddr(tslot)) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    // the row's query (this thread: the 64-dim atom `half`) as three parts, all loads first
+    // (times 1/sqrt(d): the scores come out of the tensor cores scaled)
+    const size_t qrow = (static_cast<size_t>(t0 + tt) * a.H + kh * G + g) * kWDim;
+    {
+        const float inv_sqrt_d = __frcp_rn(__fsqrt_rn(static_cast<float>(kWDim)));
+        float4 x[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+            x[c] = live ? __ldg(reinterpret_cast<const float4 *>(a.qh + qrow + half * 64) + c) : float4{};
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            float v[8] = {x[2 * c].x, x[2 * c].y, x[2 * c].z, x[2 * c].w,
+                          x[2 * c + 1].x, x[2 * c + 1].y, x[2 * c + 1].z, x[2 * c + 1].w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = FMUL(v[i], inv_sqrt_d);
+            uint4 part[3];
+            split8(v, part);
+#pragma unroll
+            for (int pl = 0; pl < 3; ++pl)
+                *reinterpret_cast<uint4 *>(qs + pl * kQPlane + half * 16384 + tc::sw128_offset(r, c * 8)) = part[pl];
+        }
+    }
+    // the block part's state: weighted values (this thread's 64 dims), max, sum
+    constexpr int kHalf = kWDim / 2;
+    float o[kHalf];
+    float m = -INFINITY, l = 0.f;
+    {
+        const float *bs = a.block_state + (static_cast<size_t>(t0 + tt) * a.H + kh * G + g) * (kWDim + 2);
+#pragma unroll
+        for (int j = 0; j < kHalf; ++j) o[j] = live ? bs[half * kHalf + j] : 0.f;
+        if (live) {
+            m = bs[kWDim];
+            l = bs[kWDim + 1];
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tslot, lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int lo = max(0, p_first - a.window + 1);
+    bool ok = true;
+    int tile = 0;
+    for (int kb = (lo / kWKeys) * kWKeys; kb <= p_last && ok; kb += kWKeys, ++tile) {
+        const int nk = min(kWKeys, p_last + 1 - kb);
+        // this block's key / value tiles, as built by k_kv_planes (after every reader of the last tile's
+        // P and V^T is done: the barrier at the end of the previous iteration)
+        // (keys and values on their own barriers: the S products start while V^T still lands)
+        if (tid == 0) {
+            const uint8_t *src = a.kv_planes + kv_tile_offset(kb / kWKeys - a.block0, a.KVH, kh);
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::saddr(&bar[2])),
+                         "r"(static_cast<uint32_t>(3 * kKPlane))
+                         : "memory");
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::saddr(&bar[3])),
+                         "r"(static_cast<uint32_t>(3 * kVPlane))
+                         : "memory");
+            bulk_load(kp, src, 3 * kKPlane, &bar[2]);
+            bulk_load(vt, src + 3 * kKPlane, 3 * kVPlane, &bar[3]);
+        }
+        ok = __syncthreads_and(tc::wait(&bar[2], tile & 1, a.err));
+        if (!ok) break;
+        // the operands are visible to the tensor cores' (async) proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (tid == 0) {
+            const int combos[6][2] = {{0, 0}, {0, 1}, {1, 0}, {0, 2}, {2, 0}, {1, 1}};
+            const uint32_t qb = tc::saddr(qs), kbase = tc::saddr(kp);
+            bool first = true;
+#pragma unroll
+            for (int cmb = 0; cmb < 6; ++cmb)
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint64_t ad = tc::sw128_desc(qb + combos[cmb][0] * kQPlane + (ks >> 2) * 16384 + (ks & 3) * 32);
+                    const uint64_t bd = tc::sw128_desc(kbase + combos[cmb][1] * kKPlane + (ks >> 2) * 8192 + (ks & 3) * 32);
+                    tc::mma(tmem, ad, bd, tc::idesc(128, 64), !first);
+                    first = false;
+                }
+            tc::commit(&bar[0]);
+        }
+        ok = __syncthreads_and(tc::wait(&bar[0], tile & 1, a.err));
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        // softmax of this row over the tile (both threads of a row compute the same values)
+        float sc[kWKeys];
+        {
+            uint32_t u[32];
+            tc::tmem_ld32(lane_base, u);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) sc[k] = __uint_as_float(u[k]);
+            tc::tmem_ld32(lane_base + 32, u);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) sc[32 + k] = __uint_as_float(u[k]);
+        }
+        float mt = m;
+#pragma unroll
+        for (int k = 0; k < kWKeys; ++k) {
+            const int pos = kb + k;
+            const bool valid = live && k < nk && pos <= p && pos > p - a.window;
+            if (!valid) sc[k] = -INFINITY;
+            mt = fmaxf(mt, sc[k]);
+        }
+        const float corr = m == -INFINITY ? 0.f : expf(__fsub_rn(m, mt));
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < kWKeys; ++k) {
+            sc[k] = sc[k] == -INFINITY ? 0.f : expf(__fsub_rn(sc[k], mt));
+            sum += sc[k];
+        }
+        l = fmaf(l, corr, sum);
+        m = mt;
+        // P into the key tile's space, three parts: this thread its half of the row's chunks
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int cc = half * 4 + c;
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = sc[cc * 8 + i];
+            uint4 part[3];
+            split8(v, part);
+#pragma unroll
+            for (int pl = 0; pl < 3; ++pl)
+                *reinterpret_cast<uint4 *>(kp + pl * kKPlane + tc::sw128_offset(r, cc * 8)) = part[pl];
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        bool v_ok = true;
+        if (tid == 0 && (v_ok = tc::wait(&bar[3], tile & 1, a.err))) {  // the value tile, then P V^T
+            const int combos[6][2] = {{0, 0}, {0, 1}, {1, 0}, {0, 2}, {2, 0}, {1, 1}};
+            const uint32_t pb = tc::saddr(kp), vb = tc::saddr(vt);
+            bool first = true;
+#pragma unroll
+            for (int cmb = 0; cmb < 6; ++cmb)
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    const uint64_t ad = tc::sw128_desc(pb + combos[cmb][0] * kKPlane + ks * 32);
+                    const uint64_t bd = tc::sw128_desc(vb + combos[cmb][1] * kVPlane + ks * 32);
+                    tc::mma(tmem + 128, ad, bd, tc::idesc(128, 128), !first);
+                    first = false;
+                }
+            tc::commit(&bar[1]);
+        }
+        ok = __syncthreads_and(v_ok);
+        if (!ok) break;
+        ok = __syncthreads_and(tc::wait(&bar[1], tile & 1, a.err));
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+        for (int c = 0; c < kHalf; c += 32) {
+            uint32_t u[32];
+            tc::tmem_ld32(lane_base + 128 + half * kHalf + c, u);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) o[c + k] = fmaf(o[c + k], corr, __uint_as_float(u[k]));
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();  // every thread has its O_t and is done with P: the next tile may overwrite them
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    }
+    if (ok && live) {
+#pragma unroll
+        for (int j = 0; j < kHalf; ++j)
+            put_planes(a.planes, a.ps,
+                       static_cast<size_t>(t0 + tt) * a.ld + (kh * G + g) * kWDim + half * kHalf + j,
+                       __fdiv_rn(o[j], l));
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
     }
 }
 

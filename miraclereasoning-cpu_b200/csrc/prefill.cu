@@ -17,6 +17,7 @@
 #include <algorithm>
 
 #include "prefill.cuh"
+#include "tcgen05.cuh"
 
 namespace mr {
 namespace {
@@ -515,61 +516,17 @@ struct TcMaps {
     CUtensorMap b[3];  // W of each segment: {k, feature}
 };
 
-__device__ __forceinline__ uint64_t tc_now() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ uint32_t saddr(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-__device__ __forceinline__ bool tc_try_wait(uint64_t *bar, int parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(saddr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// bounded wait; false (and *err set) when it gives up or another wait already did
-__device__ bool tc_wait(uint64_t *bar, int parity, int *err) {
-    if (tc_try_wait(bar, parity)) return true;
-    const uint64_t start = tc_now();
-    for (unsigned spin = 0;; ++spin) {
-        if (tc_try_wait(bar, parity)) return true;
-        if ((spin & 255u) == 255u) {
-            if (*reinterpret_cast<volatile int *>(err)) return false;
-            if (tc_now() - start > kTcWaitNs) {
-                atomicExch(err, 1);
-                return false;
-            }
-        }
-    }
-}
-// K-major operand tile in shared memory, 128-byte swizzle: rows of 128 bytes,
-// 8-row groups 1024 bytes apart (stride byte offset), descriptor version 1
-// (sm100); the start address steps 32 bytes per K16 step inside the swizzle atom.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
-    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
-           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
-}
+__device__ __forceinline__ uint64_t tc_now() { return tc::now(); }
+using tc::saddr;
+using tc::sw128_desc;
+using tc::tmem_ld32;
+__device__ __forceinline__ bool tc_try_wait(uint64_t *bar, int parity) { return tc::try_wait(bar, parity); }
+__device__ __forceinline__ bool tc_wait(uint64_t *bar, int parity, int *err) { return tc::wait(bar, parity, err); }
 // kind::f16 instruction descriptor: D F32, A and B BF16, both K-major, N = BN, M = 128
 template <int BN>
 constexpr uint32_t tc_idesc() {
     return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
            (static_cast<uint32_t>(kTM >> 4) << 24);
-}
-
-// 32 consecutive TMEM columns of this thread's lane (32x32b shape), waited for.
-__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-        : "r"(addr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 template <int BN>
