@@ -108,3 +108,24 @@ def test_tcgen05_and_mma_sync_gemms_agree(backend):
         del model
     scale = float(np.abs(outs[1]).max())
     np.testing.assert_allclose(outs[0], outs[1], atol=2 * ATOL * max(1.0, scale), rtol=2 * RTOL)
+
+
+def test_batched_prompt_greedy_continuation_full_size(backend):
+    """The greedy ids after a batched full-size prompt are those after the same prompt
+    token by token (the batched GEMMs sum in another order: counted flips must be zero
+    on this workload; nano-1.7, 600 tokens, the local window wrapped, 24 greedy steps)."""
+    config = submodule("synthetic").config_for("nano17")
+    MiracleModel = submodule("model").MiracleModel
+    prompt = submodule("synthetic").prompt_ids(config.vocab_size, 600).tolist()
+    runs = []
+    for batched in (1, 0):
+        model = MiracleModel.synthetic(config, stored="BF16", backend=backend, context_length=1024)
+        submodule("_native").call("mr_model_set_batched_prefill", model._handle, batched, None)
+        logits, ids = model.prefill(prompt), []
+        for _ in range(24):
+            ids.append(int(np.argmax(logits)))
+            logits = model.decode(ids[-1])
+        runs.append(ids)
+        del model
+    flips = sum(a != b for a, b in zip(*runs))
+    assert flips == 0, runs
