@@ -772,11 +772,12 @@ struct HeavyEngine {
     // per (layer, loop), the router's block counter, and the launch numbers the
     // monotonic counters are compared against (both zeroed by heavy_reset)
     int sm_count = 0, attn_chunks = 0;
+    int smem_per_sm = 0, smem_reserved = 0;  // shared memory of an SM, and what each resident CTA costs besides
     // ring slots per stream::Mode (plain, swiglu, down): measured at 4 to 12 slots, bytes in
     // flight pay more than room for the next kernel's CTAs beside a smaller ring
     int stream_slots[3] = {12, 12, 8};
     float *attn_partial = nullptr;
-    unsigned long long *counters = nullptr;  // [KVH] ready, [KVH] done, [1] router blocks
+    unsigned long long *counters = nullptr;  // [KVH] ready, [KVH] window units done, [1] router blocks
     std::vector<float *> k_bsum, v_bsum;
     unsigned long long attn_seq = 0, route_seq = 0;
     unsigned long long wait_ns = kHeavyWaitNs;  // bounded waits (heavy_set_wait_limit)
@@ -1030,6 +1031,8 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
         int dev = 0;
         MR_CUDA_TRY(cudaGetDevice(&dev));
         MR_CUDA_TRY(cudaDeviceGetAttribute(&e->sm_count, cudaDevAttrMultiProcessorCount, dev));
+        MR_CUDA_TRY(cudaDeviceGetAttribute(&e->smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+        MR_CUDA_TRY(cudaDeviceGetAttribute(&e->smem_reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev));
         const int G = e->H / e->KVH;
         if (G > attn::kMaxG || e->d % 4 != 0 || e->d > attn::kMaxDim) {
             heavy_destroy(e);
@@ -1049,7 +1052,7 @@ int heavy_create(mr_model *m, const mr_model_config &c, cudaStream_t stream, con
             e->v_bsum.push_back(vs);
         }
         const size_t attn_smem =
-            attn::smem_bytes(e->latent, G, e->d, maxblocks, std::max(1, e->slots), static_cast<int>(units));
+            attn::smem_bytes(e->latent, G, e->d, maxblocks, std::max(1, e->slots), e->attn_chunks);
         MR_REQUIRE(static_cast<size_t>(G) * std::max(1, e->slots) * e->d <= static_cast<size_t>(attn::kChunk) * e->d,
                    "heavy-medium-2.0: %d kept blocks per query head exceed the attention tiles", e->slots);
         MR_CUDA_TRY(cudaFuncSetAttribute(attn::k_sparse_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1148,15 +1151,26 @@ namespace {
 
 // Launches k_stream for one dtype; the ring takes the shared memory the
 // launch's other regions leave.
-int launch_stream(HeavyEngine &e, stream::Args a) {
+// `beside`: the shared memory of the previous kernel's CTA.  When a ring of at
+// least kMinBeside slots still lets a CTA of this launch sit beside one of
+// those on an SM, the ring is cut to that size, so that this launch's CTAs
+// start streaming while the previous kernel runs (the o projection after the
+// attention: 7 slots instead of 12).
+constexpr int kMinBeside = 6;
+int launch_stream(HeavyEngine &e, stream::Args a, size_t beside = 0) {
     const int grid = e.sm_count;
     const size_t fixed = stream::fixed_smem(a, grid);
     const int slots = static_cast<int>((kStreamSmem - fixed) / stream::kSlotBytes);
     MR_REQUIRE(slots >= 2, "streaming GEMV: %zu bytes of inputs leave no room for the weight ring", fixed);
-    // a whole number of slots per consumer warp (see k_stream)
     a.probe = next_probe(e);
     a.wait_ns = e.wait_ns;
     a.slots = std::min({slots, stream::kMaxSlots, e.stream_slots[a.mode]});
+    if (beside) {
+        const long long room = static_cast<long long>(e.smem_per_sm) - 2LL * e.smem_reserved -
+                               static_cast<long long>(beside) - static_cast<long long>(fixed);
+        const int fit = room > 0 ? static_cast<int>(room / stream::kSlotBytes) : 0;
+        if (fit >= kMinBeside) a.slots = std::min(a.slots, fit);
+    }
     MR_REQUIRE(a.residual == 0 || a.nseg == 1, "streaming GEMV: a residual launch has one matrix");
     a.err = e.err;
     const size_t smem = fixed + static_cast<size_t>(a.slots) * stream::kSlotBytes;
@@ -1170,7 +1184,7 @@ int launch_stream(HeavyEngine &e, stream::Args a) {
 // y = W x (or y += scale W x) for matrices of one width and dtype, the input
 // RMSNorm'ed with `gain` when given.
 int stream_plain(HeavyEngine &e, std::initializer_list<GemvSeg> segs, const float *x, const void *gain,
-                 int gain_dtype, int residual, float scale) {
+                 int gain_dtype, int residual, float scale, size_t beside = 0) {
     stream::Args a{};
     a.mode = stream::kPlain;
     for (const GemvSeg &g : segs) {
@@ -1185,7 +1199,7 @@ int stream_plain(HeavyEngine &e, std::initializer_list<GemvSeg> segs, const floa
     a.eps = e.eps;
     a.residual = residual;
     a.scale = scale;
-    return launch_stream(e, a);
+    return launch_stream(e, a, beside);
 }
 
 int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
@@ -1202,7 +1216,7 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
     const float loop_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::sqrt((double)e->loops));
     const float shared_scale = static_cast<float>(static_cast<double>(e->residual_scale) / std::max(e->shared, 1));
     const size_t attn_smem =
-        attn::smem_bytes(e->latent, G, e->d, maxblocks, std::max(1, e->slots), e->attn_chunks + 1);
+        attn::smem_bytes(e->latent, G, e->d, maxblocks, std::max(1, e->slots), e->attn_chunks);
     if (int rc = launch(k_embed_row, (e->hidden + 255) / 256, 256, 0, s, e->embed, e->embed_dt, dtoken, token,
                         e->hidden, e->x))
         return rc;
@@ -1252,7 +1266,7 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             aa.kept = e->kept + li * e->H * std::max(1, e->slots);
             aa.partial = e->attn_partial;
             aa.ready = e->counters;
-            aa.done = e->counters + e->KVH;
+            aa.wdone = e->counters + e->KVH;
             aa.seq = ++e->attn_seq;
             aa.out = e->attn;
             aa.err = e->err;
@@ -1265,7 +1279,7 @@ int token_step(HeavyEngine *e, const int *dtoken, int token, int position) {
             if (int rc = stamp(*e)) return rc;
             // 3. x += s * W_o attended
             if (e->streamable) {
-                if (int rc = stream_plain(*e, {Ly.o}, e->attn, nullptr, 0, 1, loop_scale)) return rc;
+                if (int rc = stream_plain(*e, {Ly.o}, e->attn, nullptr, 0, 1, loop_scale, attn_smem)) return rc;
             } else {
                 GemvSeg o = Ly.o;
                 o.scale = loop_scale;
