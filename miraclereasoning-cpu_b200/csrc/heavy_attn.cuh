@@ -114,35 +114,47 @@ __device__ __forceinline__ void norm_rope(const float *src, float *dst, int dim,
 // n (<= kChunk) rows [row0, row0 + n) of a [*, width] float matrix, columns
 // [col, col + d): keys transposed into kT (column t of row j at j * kPad + t)
 // and, when vt is given, the same rows of `vsrc` row-major into vt (n x d).
-// Relative row `fresh_at` comes from kfresh / vfresh instead.  Every load is
-// issued before the first store.
+// Relative row `fresh_at` comes from kfresh / vfresh instead.  The loads
+// (Tile::load) and the stores (Tile::store) are separate calls, so that other
+// work can run while the loads are in flight.
+struct Tile {
+    static constexpr int kPer = kChunk * kMaxDim / 4 / kThreads;
+    float4 kv[kPer], vv[kPer];
+    __device__ __forceinline__ void load(const float *ksrc, const float *vsrc, size_t row0, int width, int col, int n,
+                                         int d, int fresh_at, const float *kfresh, const float *vfresh) {
+        const int q = d / 4, total = n * q;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int i = threadIdx.x + k * kThreads, t = i / q, c = i % q;
+            const size_t at = (row0 + t) * width + col;
+            kv[k] = i >= total    ? float4{}
+                    : t == fresh_at ? reinterpret_cast<const float4 *>(kfresh)[c]
+                                    : __ldcg(reinterpret_cast<const float4 *>(ksrc + at) + c);
+            vv[k] = (i >= total || !vsrc) ? float4{}
+                    : t == fresh_at       ? reinterpret_cast<const float4 *>(vfresh)[c]
+                                          : __ldcg(reinterpret_cast<const float4 *>(vsrc + at) + c);
+        }
+    }
+    __device__ __forceinline__ void store(float *kT, float *vt, int n, int d) const {
+        const int q = d / 4, total = n * q;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int i = threadIdx.x + k * kThreads, t = i / q, c = i % q;
+            if (i >= total) continue;
+            kT[(4 * c) * kPad + t] = kv[k].x;
+            kT[(4 * c + 1) * kPad + t] = kv[k].y;
+            kT[(4 * c + 2) * kPad + t] = kv[k].z;
+            kT[(4 * c + 3) * kPad + t] = kv[k].w;
+            if (vt) reinterpret_cast<float4 *>(vt + t * d)[c] = vv[k];
+        }
+    }
+};
 __device__ __forceinline__ void load_tile(float *kT, float *vt, const float *ksrc, const float *vsrc, size_t row0,
                                           int width, int col, int n, int d, int fresh_at, const float *kfresh,
                                           const float *vfresh) {
-    constexpr int kPer = kChunk * kMaxDim / 4 / kThreads;
-    const int q = d / 4, total = n * q;
-    float4 kv[kPer], vv[kPer];
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-        const int i = threadIdx.x + k * kThreads, t = i / q, c = i % q;
-        const size_t at = (row0 + t) * width + col;
-        kv[k] = i >= total    ? float4{}
-                : t == fresh_at ? reinterpret_cast<const float4 *>(kfresh)[c]
-                                : __ldcg(reinterpret_cast<const float4 *>(ksrc + at) + c);
-        vv[k] = (i >= total || !vt) ? float4{}
-                : t == fresh_at     ? reinterpret_cast<const float4 *>(vfresh)[c]
-                                    : __ldcg(reinterpret_cast<const float4 *>(vsrc + at) + c);
-    }
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-        const int i = threadIdx.x + k * kThreads, t = i / q, c = i % q;
-        if (i >= total) continue;
-        kT[(4 * c) * kPad + t] = kv[k].x;
-        kT[(4 * c + 1) * kPad + t] = kv[k].y;
-        kT[(4 * c + 2) * kPad + t] = kv[k].z;
-        kT[(4 * c + 3) * kPad + t] = kv[k].w;
-        if (vt) reinterpret_cast<float4 *>(vt + t * d)[c] = vv[k];
-    }
+    Tile tile;
+    tile.load(ksrc, vt ? vsrc : nullptr, row0, width, col, n, d, fresh_at, kfresh, vfresh);
+    tile.store(kT, vt, n, d);
 }
 
 // q . (column t of kT) / sqrt(d): one thread, columns in order, four FMA chains.
@@ -165,14 +177,17 @@ __device__ __forceinline__ void prefetch_rows(const float *first, size_t stride,
 }
 
 
-// q . k / sqrt(d) for one contiguous key row, tile_score's arithmetic.
+// q . k / sqrt(d) for one contiguous key row (both 16-byte aligned in shared
+// memory), tile_score's arithmetic; the loads run ahead of the four FMA chains.
 __device__ __forceinline__ float row_score(const float *qh, const float *k, int d) {
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 8
     for (int j = 0; j < d; j += 4) {
-        a0 = fmaf(qh[j], k[j], a0);
-        a1 = fmaf(qh[j + 1], k[j + 1], a1);
-        a2 = fmaf(qh[j + 2], k[j + 2], a2);
-        a3 = fmaf(qh[j + 3], k[j + 3], a3);
+        const float4 q4 = *reinterpret_cast<const float4 *>(qh + j), k4 = *reinterpret_cast<const float4 *>(k + j);
+        a0 = fmaf(q4.x, k4.x, a0);
+        a1 = fmaf(q4.y, k4.y, a1);
+        a2 = fmaf(q4.z, k4.z, a2);
+        a3 = fmaf(q4.w, k4.w, a3);
     }
     return __fdiv_rn((a0 + a1) + (a2 + a3), __fsqrt_rn(static_cast<float>(d)));
 }
@@ -224,6 +239,9 @@ __device__ void window_unit(const Args &a, const Smem &s, int kh, int u, int G) 
     const size_t lrow = static_cast<size_t>(a.latent_dim) * (a.kv_dtype == MR_DTYPE_F32 ? 4 : 2);
     // 1. the latent and the group's queries in one load round; this unit's rows
     //    of kv = W_kv_up latent (keys kh*d .., values width + kh*d ..)
+    //    (the window tile's loads, which need nothing of this token, go out first)
+    Tile tile;
+    tile.load(a.k_ring, a.v_ring, static_cast<size_t>(a.start + t0), width, kh * d, n, d, -1, nullptr, nullptr);
     for (int i = threadIdx.x; i < a.latent_dim; i += kThreads) s.lat[i] = __ldcg(a.latent + i);
     for (int i = threadIdx.x; i < G * d; i += kThreads) s.qs[i] = __ldcg(a.q + static_cast<size_t>(kh) * G * d + i);
     __syncthreads();
@@ -257,8 +275,7 @@ __device__ void window_unit(const Args &a, const Smem &s, int kh, int u, int G) 
     }
     // 2. the queries normalised and rotated; the window keys and values
     for (int g = warp; g < G; g += nwarps) norm_rope(s.qs + g * d, s.qs + g * d, d, a.split_half, a.position, a.inv_freq);
-    load_tile(s.kT, s.vt, a.k_ring, a.v_ring, static_cast<size_t>(a.start + t0), width, kh * d, n, d, -1, nullptr,
-              nullptr);
+    tile.store(s.kT, s.vt, n, d);
     __syncthreads();
     float *part = a.partial + (static_cast<size_t>(kh) * units + u) * G * (d + 2);
     for (int i = threadIdx.x; i < G * n; i += kThreads) {
@@ -470,12 +487,20 @@ __device__ void block_unit(const Args &a, const Smem &s, int kh, int G) {
         }
         l = warp_sum(l);
         __syncwarp();
+        // columns lane, lane + 32, ... (d <= kMaxDim); each column's sum in kept order
         const int *rows = s.row_s + g * (SM + 1);
-        for (int j = lane; j < d; j += 32) {
-            float acc = 0.f;
-            for (int e = 0; e < nk; ++e) acc = fmaf(w[e], s.vt[(g * SM + rows[e]) * d + j], acc);
-            s.bpart[g * (d + 2) + j] = fmaf(w[nk], s.vnew[j], acc);
+        constexpr int kCols = kMaxDim / 32;
+        float acc[kCols] = {};
+        for (int e = 0; e < nk; ++e) {
+            const float we = w[e];
+            const float *v = s.vt + (g * SM + rows[e]) * d;
+#pragma unroll
+            for (int q = 0; q < kCols; ++q)
+                if (lane + 32 * q < d) acc[q] = fmaf(we, v[lane + 32 * q], acc[q]);
         }
+#pragma unroll
+        for (int q = 0; q < kCols; ++q)
+            if (lane + 32 * q < d) s.bpart[g * (d + 2) + lane + 32 * q] = fmaf(w[nk], s.vnew[lane + 32 * q], acc[q]);
         if (lane == 0) {
             s.bpart[g * (d + 2) + d] = m;
             s.bpart[g * (d + 2) + d + 1] = l;
