@@ -775,7 +775,7 @@ struct HeavyEngine {
     int smem_per_sm = 0, smem_reserved = 0;  // shared memory of an SM, and what each resident CTA costs besides
     // ring slots per stream::Mode (plain, swiglu, down): measured at 4 to 12 slots, bytes in
     // flight pay more than room for the next kernel's CTAs beside a smaller ring
-    int stream_slots[3] = {12, 12, 8};
+    int stream_slots[3] = {12, 12, 16};
     float *attn_partial = nullptr;
     unsigned long long *counters = nullptr;  // [KVH] ready, [KVH] window units done, [1] router blocks
     std::vector<float *> k_bsum, v_bsum;
@@ -1160,7 +1160,8 @@ constexpr int kMinBeside = 6;
 int launch_stream(HeavyEngine &e, stream::Args a, size_t beside = 0) {
     const int grid = e.sm_count;
     const size_t fixed = stream::fixed_smem(a, grid);
-    const int slots = static_cast<int>((kStreamSmem - fixed) / stream::kSlotBytes);
+    a.slot_bytes = stream::slot_bytes(a);
+    const int slots = static_cast<int>((kStreamSmem - fixed) / a.slot_bytes);
     MR_REQUIRE(slots >= 2, "streaming GEMV: %zu bytes of inputs leave no room for the weight ring", fixed);
     a.probe = next_probe(e);
     a.wait_ns = e.wait_ns;
@@ -1168,12 +1169,12 @@ int launch_stream(HeavyEngine &e, stream::Args a, size_t beside = 0) {
     if (beside) {
         const long long room = static_cast<long long>(e.smem_per_sm) - 2LL * e.smem_reserved -
                                static_cast<long long>(beside) - static_cast<long long>(fixed);
-        const int fit = room > 0 ? static_cast<int>(room / stream::kSlotBytes) : 0;
+        const int fit = room > 0 ? static_cast<int>(room / a.slot_bytes) : 0;
         if (fit >= kMinBeside) a.slots = std::min(a.slots, fit);
     }
     MR_REQUIRE(a.residual == 0 || a.nseg == 1, "streaming GEMV: a residual launch has one matrix");
     a.err = e.err;
-    const size_t smem = fixed + static_cast<size_t>(a.slots) * stream::kSlotBytes;
+    const size_t smem = fixed + static_cast<size_t>(a.slots) * a.slot_bytes;
     switch (a.dtype) {
         case MR_DTYPE_BF16: return launch(stream::k_stream<MR_DTYPE_BF16>, grid, stream::kThreads, smem, e.stream, a);
         case MR_DTYPE_F16: return launch(stream::k_stream<MR_DTYPE_F16>, grid, stream::kThreads, smem, e.stream, a);

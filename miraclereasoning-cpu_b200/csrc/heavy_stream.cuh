@@ -34,8 +34,8 @@ namespace stream {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;  // + the producer warp
-constexpr int kSlotBytes = 16384;
-constexpr int kMaxSlots = 12;
+constexpr int kSlotBytes = 16384;  // the largest piece
+constexpr int kMaxSlots = 16;
 constexpr int kMaxSegs = 12;
 constexpr int kMaxPieceRows = 4;
 constexpr int kMaxPeers = 8;
@@ -51,7 +51,8 @@ struct Seg {
 };
 
 struct Args {
-    int mode, dtype, cols, slots;  // slots: ring slots of kSlotBytes
+    int mode, dtype, cols, slots;  // slots: ring slots of slot_bytes
+    int slot_bytes;                // one piece (<= kSlotBytes), a multiple of 128
     Seg seg[kMaxSegs];
     int nseg;                      // static segments (streamed before the dependency wait)
     // routed experts (kSwiglu / kDown): slots 0..active-1 = expert chosen[k]
@@ -137,10 +138,17 @@ __device__ __forceinline__ uint4 lds16(const void *p) {
     return v;
 }
 
-__device__ __forceinline__ int esize(int dtype) { return dtype == MR_DTYPE_F32 ? 4 : 2; }
-__device__ __forceinline__ int piece_rows(const Args &a) {
+__host__ __device__ __forceinline__ int esize(int dtype) { return dtype == MR_DTYPE_F32 ? 4 : 2; }
+__host__ __device__ __forceinline__ int piece_rows(const Args &a) {
     const int rb = a.cols * esize(a.dtype) * (a.mode == kSwiglu ? 2 : 1);
-    return max(1, min(kMaxPieceRows, kSlotBytes / rb));
+    const int p = kSlotBytes / rb;
+    return p < 1 ? 1 : p < kMaxPieceRows ? p : kMaxPieceRows;
+}
+// A ring slot holds one piece: its bytes rounded up to 128 (down projections of
+// 1408-wide BF16 rows: 4 x 2816 = 11264 bytes, so the ring holds more of them).
+inline int slot_bytes(const Args &a) {
+    const int bytes = piece_rows(a) * a.cols * esize(a.dtype) * (a.mode == kSwiglu ? 2 : 1);
+    return (bytes + 127) & ~127;
 }
 __device__ __forceinline__ int slice_lo(int rows, int c, int g) {
     return static_cast<int>(static_cast<long long>(rows) * c / g);
@@ -382,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(Args a) {
                 return;
             }
             const uint32_t bytes = static_cast<uint32_t>(p.nrows * row_bytes);
-            unsigned char *dst = ring + static_cast<size_t>(s) * kSlotBytes;
+            unsigned char *dst = ring + static_cast<size_t>(s) * a.slot_bytes;
             bar_expect(&full[s], bytes * pair);
             bulk(dst, p.w, bytes, &full[s], policy);
             if (pair == 2) bulk(dst + bytes, p.w2, bytes, &full[s], policy);
@@ -437,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(Args a) {
             ok = false;
             return;
         }
-        const unsigned char *slot = ring + static_cast<size_t>(s) * kSlotBytes;
+        const unsigned char *slot = ring + static_cast<size_t>(s) * a.slot_bytes;
         const float *x = a.mode == kDown ? xs + static_cast<size_t>(p.slot) * a.cols : xs;
         const float *xhi = x + a.cols / 2;
         float y[kMaxPieceRows];
