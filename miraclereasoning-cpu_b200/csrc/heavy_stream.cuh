@@ -23,10 +23,11 @@
 // tail (the ring is sized so that the next kernel's CTAs fit on the SM beside
 // this one's); routed experts follow once the routing is visible.
 //
-// Arithmetic per row is that of k_gemv / k_expert_*: lane l sums 16-byte
-// chunks l, l + 32, ... in order (each chunk an FMA chain over its 8 columns),
-// then a warp sum; the input's RMSNorm is staged by 256 threads exactly as
-// stage_input does.  So the outputs are bit-identical to those kernels.
+// Arithmetic per row: the same float32 products as k_gemv / k_expert_* (the
+// fallback for rows that are not whole 16-byte chunks), summed in another order
+// (rows_dot: lane l keeps one running sum per column of its chunks l, l + 32,
+// ..., folded pairwise, then a warp sum), which keeps the FMAs independent; the
+// input's RMSNorm is staged by 256 threads exactly as stage_input does.
 #pragma once
 
 namespace stream {
@@ -202,52 +203,80 @@ __device__ __forceinline__ void for_each_piece(const Args &a, bool dynamic, int 
     }
 }
 
-// One 16-byte chunk of weights against its 8 (4 for F32) inputs, as dot16.
+// One 16-byte chunk of weights widened to float: kChunkCols columns, in
+// column order (BF16 / F16: the low half of each 32-bit word first).
 template <int DT>
-__device__ __forceinline__ float chunk_dot(const uint4 &w, const float *xlo, const float *xhi, int c) {
-    if (DT == MR_DTYPE_F32) {
-        const float4 a = *reinterpret_cast<const float4 *>(xlo + 4 * c);
-        return __uint_as_float(w.x) * a.x + __uint_as_float(w.y) * a.y + __uint_as_float(w.z) * a.z +
-               __uint_as_float(w.w) * a.w;
-    }
-    const float4 a = *reinterpret_cast<const float4 *>(xlo + 4 * c), b = *reinterpret_cast<const float4 *>(xhi + 4 * c);
+constexpr int kChunkCols = DT == MR_DTYPE_F32 ? 4 : 8;
+template <int DT>
+__device__ __forceinline__ void widen(const uint4 &w, float (&v)[kChunkCols<DT>]) {
     const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-    float lo[4], hi[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        if (DT == MR_DTYPE_BF16) {
-            lo[i] = __uint_as_float(u[i] << 16);
-            hi[i] = __uint_as_float(u[i] & 0xffff0000u);
+        if (DT == MR_DTYPE_F32) {
+            v[i] = __uint_as_float(u[i]);
+        } else if (DT == MR_DTYPE_BF16) {
+            v[2 * i] = __uint_as_float(u[i] << 16);
+            v[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
         } else {
-            lo[i] = __half2float(__ushort_as_half(static_cast<uint16_t>(u[i] & 0xffffu)));
-            hi[i] = __half2float(__ushort_as_half(static_cast<uint16_t>(u[i] >> 16)));
+            v[2 * i] = __half2float(__ushort_as_half(static_cast<uint16_t>(u[i] & 0xffffu)));
+            v[2 * i + 1] = __half2float(__ushort_as_half(static_cast<uint16_t>(u[i] >> 16)));
         }
     }
-    float s = lo[0] * a.x;
-    s = fmaf(hi[0], a.y, s);
-    s = fmaf(lo[1], a.z, s);
-    s = fmaf(hi[1], a.w, s);
-    s = fmaf(lo[2], b.x, s);
-    s = fmaf(hi[2], b.y, s);
-    s = fmaf(lo[3], b.z, s);
-    s = fmaf(hi[3], b.w, s);
-    return s;
+}
+// The inputs of chunk c: columns 8c..8c+3 at xlo + 4c, 8c+4..8c+7 at xhi + 4c
+// (F32: 4c..4c+3 at xlo + 4c).
+template <int DT>
+__device__ __forceinline__ void chunk_x(const float *xlo, const float *xhi, int c, float (&v)[kChunkCols<DT>]) {
+    const float4 a = *reinterpret_cast<const float4 *>(xlo + 4 * c);
+    v[0] = a.x;
+    v[1] = a.y;
+    v[2] = a.z;
+    v[3] = a.w;
+    if (DT != MR_DTYPE_F32) {
+        const float4 b = *reinterpret_cast<const float4 *>(xhi + 4 * c);
+        v[4] = b.x;
+        v[5] = b.y;
+        v[6] = b.z;
+        v[7] = b.w;
+    }
+}
+// A row's running sums (one per column of a chunk) summed pairwise, then over the warp.
+template <int DT>
+__device__ __forceinline__ float fold(const float (&a)[kChunkCols<DT>]) {
+    float s = (a[0] + a[1]) + (a[2] + a[3]);
+    if (DT != MR_DTYPE_F32) s = s + ((a[4] + a[5]) + (a[6] + a[7]));
+    return warp_sum(s);
 }
 
-// Dot products of n (<= 4) consecutive rows of one slot with x; the rows'
-// sums are complete in every lane.
+// Dot products of n (<= kMaxPieceRows) consecutive rows of one slot with x.
+// Lane l takes the 16-byte chunks l, l + 32, ...; each row keeps one running
+// sum per column of a chunk, so a chunk's FMAs are independent of one another
+// (a single chain per row left the warps waiting on FMA latency with two warps
+// per scheduler); the sums fold pairwise at the end.  Every lane gets the sums.
 template <int DT>
 __device__ __forceinline__ void rows_dot(const char *slot, int n, int row_bytes, int nv, const float *xlo,
                                          const float *xhi, float (&y)[kMaxPieceRows]) {
+    constexpr int W = kChunkCols<DT>;
     const int lane = threadIdx.x & 31;
-    float acc[kMaxPieceRows] = {};
-    for (int c = lane; c < nv; c += 32) {
+    float acc[kMaxPieceRows][W];
 #pragma unroll
-        for (int r = 0; r < kMaxPieceRows; ++r)
-            if (r < n) acc[r] += chunk_dot<DT>(lds16(slot + r * row_bytes + 16 * c), xlo, xhi, c);
+    for (int r = 0; r < kMaxPieceRows; ++r)
+#pragma unroll
+        for (int k = 0; k < W; ++k) acc[r][k] = 0.f;
+    for (int c = lane; c < nv; c += 32) {
+        float x[W];
+        chunk_x<DT>(xlo, xhi, c, x);
+#pragma unroll
+        for (int r = 0; r < kMaxPieceRows; ++r) {
+            if (r >= n) break;
+            float w[W];
+            widen<DT>(lds16(slot + r * row_bytes + 16 * c), w);
+#pragma unroll
+            for (int k = 0; k < W; ++k) acc[r][k] = fmaf(w[k], x[k], acc[r][k]);
+        }
     }
 #pragma unroll
-    for (int r = 0; r < kMaxPieceRows; ++r) y[r] = warp_sum(acc[r]);
+    for (int r = 0; r < kMaxPieceRows; ++r) y[r] = fold<DT>(acc[r]);
 }
 
 // x (n floats) into the layout the dot products read: two planes for 16-bit
@@ -454,16 +483,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(Args a) {
                 const char *gp = reinterpret_cast<const char *>(slot) + r * row_bytes;
                 const char *base = gp;
                 float gu[kMaxPieceRows];
-                // gate row r and up row r share the x reads
+                // gate row r and up row r share the x reads (rows_dot's running sums)
                 const int off = p.nrows * row_bytes;
                 {
-                    float acc0 = 0.f, acc1 = 0.f;
+                    constexpr int W = kChunkCols<DT>;
+                    float ag[W], au[W];
+#pragma unroll
+                    for (int k = 0; k < W; ++k) ag[k] = au[k] = 0.f;
                     for (int c = lane; c < nv; c += 32) {
-                        acc0 += chunk_dot<DT>(lds16(base + 16 * c), x, xhi, c);
-                        acc1 += chunk_dot<DT>(lds16(base + off + 16 * c), x, xhi, c);
+                        float xv[W], wg[W], wu[W];
+                        chunk_x<DT>(x, xhi, c, xv);
+                        widen<DT>(lds16(base + 16 * c), wg);
+                        widen<DT>(lds16(base + off + 16 * c), wu);
+#pragma unroll
+                        for (int k = 0; k < W; ++k) {
+                            ag[k] = fmaf(wg[k], xv[k], ag[k]);
+                            au[k] = fmaf(wu[k], xv[k], au[k]);
+                        }
                     }
-                    gu[0] = warp_sum(acc0);
-                    gu[1] = warp_sum(acc1);
+                    gu[0] = fold<DT>(ag);
+                    gu[1] = fold<DT>(au);
                 }
                 if (lane == 0)
                     a.act_out[static_cast<size_t>(p.slot) * a.dyn_rows + p.row0 + r] =
