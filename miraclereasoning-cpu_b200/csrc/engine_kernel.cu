@@ -467,56 +467,63 @@ __device__ __forceinline__ int split_index(int j, int cols) { return (j >> 3) * 
 template <int DT>
 struct RowDot;
 
+// One 16-byte chunk of weights times its x values, added column by column to
+// running sums s[0 .. VEC-1] (independent FMAs: a chain per chunk left the
+// warps waiting on FMA latency); fold() sums them pairwise.
 template <>
 struct RowDot<MR_DTYPE_BF16> {
     static constexpr int VEC = 8;
-    __device__ static float chunk(const uint4 &w, const float4 a, const float4 b) {
-        float acc = __uint_as_float(w.x << 16) * a.x;
-        acc = fmaf(__uint_as_float(w.x & 0xffff0000u), a.y, acc);
-        acc = fmaf(__uint_as_float(w.y << 16), a.z, acc);
-        acc = fmaf(__uint_as_float(w.y & 0xffff0000u), a.w, acc);
-        acc = fmaf(__uint_as_float(w.z << 16), b.x, acc);
-        acc = fmaf(__uint_as_float(w.z & 0xffff0000u), b.y, acc);
-        acc = fmaf(__uint_as_float(w.w << 16), b.z, acc);
-        acc = fmaf(__uint_as_float(w.w & 0xffff0000u), b.w, acc);
-        return acc;
+    __device__ static void add(float (&s)[VEC], const uint4 &w, const float4 a, const float4 b) {
+        s[0] = fmaf(__uint_as_float(w.x << 16), a.x, s[0]);
+        s[1] = fmaf(__uint_as_float(w.x & 0xffff0000u), a.y, s[1]);
+        s[2] = fmaf(__uint_as_float(w.y << 16), a.z, s[2]);
+        s[3] = fmaf(__uint_as_float(w.y & 0xffff0000u), a.w, s[3]);
+        s[4] = fmaf(__uint_as_float(w.z << 16), b.x, s[4]);
+        s[5] = fmaf(__uint_as_float(w.z & 0xffff0000u), b.y, s[5]);
+        s[6] = fmaf(__uint_as_float(w.w << 16), b.z, s[6]);
+        s[7] = fmaf(__uint_as_float(w.w & 0xffff0000u), b.w, s[7]);
     }
 };
 
 template <>
 struct RowDot<MR_DTYPE_F16> {
     static constexpr int VEC = 8;
-    __device__ static float chunk(const uint4 &w, const float4 a, const float4 b) {
+    __device__ static void add(float (&s)[VEC], const uint4 &w, const float4 a, const float4 b) {
         const __half2 *h = reinterpret_cast<const __half2 *>(&w);
         const float2 p0 = __half22float2(h[0]), p1 = __half22float2(h[1]), p2 = __half22float2(h[2]),
                      p3 = __half22float2(h[3]);
-        float acc = p0.x * a.x;
-        acc = fmaf(p0.y, a.y, acc);
-        acc = fmaf(p1.x, a.z, acc);
-        acc = fmaf(p1.y, a.w, acc);
-        acc = fmaf(p2.x, b.x, acc);
-        acc = fmaf(p2.y, b.y, acc);
-        acc = fmaf(p3.x, b.z, acc);
-        acc = fmaf(p3.y, b.w, acc);
-        return acc;
+        s[0] = fmaf(p0.x, a.x, s[0]);
+        s[1] = fmaf(p0.y, a.y, s[1]);
+        s[2] = fmaf(p1.x, a.z, s[2]);
+        s[3] = fmaf(p1.y, a.w, s[3]);
+        s[4] = fmaf(p2.x, b.x, s[4]);
+        s[5] = fmaf(p2.y, b.y, s[5]);
+        s[6] = fmaf(p3.x, b.z, s[6]);
+        s[7] = fmaf(p3.y, b.w, s[7]);
     }
 };
 
 template <>
 struct RowDot<MR_DTYPE_F32> {
     static constexpr int VEC = 4;
-    __device__ static float chunk(const uint4 &w, const float4 a, const float4) {
-        float acc = __uint_as_float(w.x) * a.x;
-        acc = fmaf(__uint_as_float(w.y), a.y, acc);
-        acc = fmaf(__uint_as_float(w.z), a.z, acc);
-        acc = fmaf(__uint_as_float(w.w), a.w, acc);
-        return acc;
+    __device__ static void add(float (&s)[VEC], const uint4 &w, const float4 a, const float4) {
+        s[0] = fmaf(__uint_as_float(w.x), a.x, s[0]);
+        s[1] = fmaf(__uint_as_float(w.y), a.y, s[1]);
+        s[2] = fmaf(__uint_as_float(w.z), a.z, s[2]);
+        s[3] = fmaf(__uint_as_float(w.w), a.w, s[3]);
     }
 };
 
 template <int DT>
-__device__ __forceinline__ float xchunk(const uint4 &w, const XView &x, int c) {
-    return RowDot<DT>::chunk(w, x.L(c), DT == MR_DTYPE_F32 ? float4{} : x.H(c));
+__device__ __forceinline__ float fold(const float (&s)[RowDot<DT>::VEC]) {
+    float t = (s[0] + s[1]) + (s[2] + s[3]);
+    if constexpr (RowDot<DT>::VEC == 8) t = t + ((s[4] + s[5]) + (s[6] + s[7]));
+    return t;
+}
+
+template <int DT>
+__device__ __forceinline__ void xadd(float (&s)[RowDot<DT>::VEC], const uint4 &w, const XView &x, int c) {
+    RowDot<DT>::add(s, w, x.L(c), DT == MR_DTYPE_F32 ? float4{} : x.H(c));
 }
 
 // Weights read straight from global memory (non-bulk phases): bypass L1.
@@ -544,8 +551,11 @@ __device__ float row_partial(const char *rp, int cols, int first, int stride, in
     using D = RowDot<DT>;
     const int nv = cols / D::VEC;
     const size_t row_bytes = static_cast<size_t>(cols) * esize(DT);
-    // four independent accumulators: the chunks' FMA chains overlap
-    float acc = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    // a running sum per column of a chunk; four chunks' loads in flight at a time
+    float acc = 0.f;
+    float sums[D::VEC];
+#pragma unroll
+    for (int k = 0; k < D::VEC; ++k) sums[k] = 0.f;
     if (FROM_SMEM || (row_bytes & 15) == 0) {
         const uint4 *v = reinterpret_cast<const uint4 *>(rp);
         int c = first;
@@ -558,20 +568,20 @@ __device__ float row_partial(const char *rp, int cols, int first, int stride, in
                 w0 = ld_stream(v + c), w1 = ld_stream(v + c + stride), w2 = ld_stream(v + c + 2 * stride),
                 w3 = ld_stream(v + c + 3 * stride);
             }
-            acc += xchunk<DT>(w0, x, c);
-            acc1 += xchunk<DT>(w1, x, c + stride);
-            acc2 += xchunk<DT>(w2, x, c + 2 * stride);
-            acc3 += xchunk<DT>(w3, x, c + 3 * stride);
+            xadd<DT>(sums, w0, x, c);
+            xadd<DT>(sums, w1, x, c + stride);
+            xadd<DT>(sums, w2, x, c + 2 * stride);
+            xadd<DT>(sums, w3, x, c + 3 * stride);
         }
         if (c + stride < nv) {
             const uint4 w0 = FROM_SMEM ? ld_smem(v + c) : ld_stream(v + c);
             const uint4 w1 = FROM_SMEM ? ld_smem(v + c + stride) : ld_stream(v + c + stride);
-            acc1 += xchunk<DT>(w0, x, c);
-            acc2 += xchunk<DT>(w1, x, c + stride);
+            xadd<DT>(sums, w0, x, c);
+            xadd<DT>(sums, w1, x, c + stride);
             c += 2 * stride;
         }
-        for (; c < nv; c += stride) acc3 += xchunk<DT>(FROM_SMEM ? ld_smem(v + c) : ld_stream(v + c), x, c);
-        acc = (acc + acc1) + (acc2 + acc3);
+        for (; c < nv; c += stride) xadd<DT>(sums, FROM_SMEM ? ld_smem(v + c) : ld_stream(v + c), x, c);
+        acc = fold<DT>(sums);
         if (!FROM_SMEM && tail_lane >= 0)
             for (int j = nv * D::VEC + tail_lane; j < cols; j += 32) acc = fmaf(load_weight(rp, DT, j), x.plain[j], acc);
     } else if (tail_lane >= 0) {
@@ -595,28 +605,21 @@ __device__ float row_partial_any(int dtype, const char *rp, int cols, int first,
 template <int DT>
 __device__ __forceinline__ void rows4(const char *const (&rp)[4], int nr, int nv, int lane, const XView &x,
                                       float (&out)[4]) {
-    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
-    int c = lane;
-    for (; c + 32 < nv; c += 64) {
-        const float4 x0 = x.L(c), x1 = x.L(c + 32);
-        const float4 y0 = DT == MR_DTYPE_F32 ? float4{} : x.H(c), y1 = DT == MR_DTYPE_F32 ? float4{} : x.H(c + 32);
+    constexpr int V = RowDot<DT>::VEC;
+    float a[4][V];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            if (r < nr) {
-                const uint4 *v = reinterpret_cast<const uint4 *>(rp[r]);
-                a[r] += RowDot<DT>::chunk(ld_smem(v + c), x0, y0);
-                b[r] += RowDot<DT>::chunk(ld_smem(v + c + 32), x1, y1);
-            }
-        }
-    }
-    if (c < nv) {
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int k = 0; k < V; ++k) a[r][k] = 0.f;
+#pragma unroll 2
+    for (int c = lane; c < nv; c += 32) {
         const float4 x0 = x.L(c), y0 = DT == MR_DTYPE_F32 ? float4{} : x.H(c);
 #pragma unroll
         for (int r = 0; r < 4; ++r)
-            if (r < nr) a[r] += RowDot<DT>::chunk(ld_smem(reinterpret_cast<const uint4 *>(rp[r]) + c), x0, y0);
+            if (r < nr) RowDot<DT>::add(a[r], ld_smem(reinterpret_cast<const uint4 *>(rp[r]) + c), x0, y0);
     }
 #pragma unroll
-    for (int r = 0; r < 4; ++r) out[r] = a[r] + b[r];
+    for (int r = 0; r < 4; ++r) out[r] = fold<DT>(a[r]);
 }
 
 // y[i] = row_i . x for i < n (n <= kRowBatch); rows start at `base` with
