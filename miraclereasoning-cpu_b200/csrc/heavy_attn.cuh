@@ -37,6 +37,10 @@ constexpr int kChunk = 64;      // window keys per unit
 constexpr int kPad = kChunk + 1;  // transposed tile row: column t of key row j at j * kPad + t (no bank conflict)
 constexpr int kMaxG = 8;        // query heads per KV head
 constexpr int kMaxDim = 128;
+// registers per thread: at most 144, so that a streaming CTA of the next kernel (9 warps of
+// <= 96 registers) fits beside a unit on the SM's 64 K registers (7.654 against 7.666 ms per
+// heavy-medium-2.0 token)
+constexpr int kMaxRegs = 144;
 constexpr int kMergeBatch = 16;  // window units merged from registers in one load round (more: loaded as used)
 
 struct Args {
@@ -582,7 +586,7 @@ __device__ void block_unit(const Args &a, const Smem &s, int kh, int G) {
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) k_sparse_attention(Args a) {
+__global__ void __maxnreg__(kMaxRegs) k_sparse_attention(Args a) {
     pdl_trigger();
     extern __shared__ __align__(16) float sm[];
     const int units = a.chunks + 1;
